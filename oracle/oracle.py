@@ -1,0 +1,350 @@
+"""ctypes access to the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+Two libraries live under oracle/:
+
+* ``liboracle.so``          -- the C restatement of the reference algorithm
+                               (phonon_oracle.c + sleef_u10.c);
+* ``_ref/libphonon_ref.so`` -- the unmodified speech-mac sources compiled with
+                               the shims in oracle/shim (built only where the
+                               reference tree exists; the built file travels).
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's reference /
+cpu_baseline arm may import this module, and only as the checker.
+"""
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "liboracle.so"
+REF_SO = HERE / "_ref" / "libphonon_ref.so"
+
+F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+Q8_BYTES_PER_32 = 34
+LINEAR_SHAPES = {"qkv": (1536, 512), "out": (512, 512), "up": (2048, 512), "down": (512, 2048)}
+
+
+def build(ref_root=None):
+    """Compile liboracle.so and, when the reference tree exists, _ref/."""
+    cmd = f"make -s -C {HERE}"
+    if ref_root:
+        cmd += f" REF={ref_root}"
+    rc = os.system(cmd)
+    if rc != 0:
+        raise RuntimeError(f"oracle build failed: {cmd}")
+
+
+def _ptr(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class OracleLinear(C.Structure):
+    _fields_ = [("dtype", C.c_int), ("rows", C.c_size_t), ("cols", C.c_size_t), ("data", C.c_void_p)]
+
+
+class OracleLayer(C.Structure):
+    _fields_ = [("qkv", OracleLinear), ("out", OracleLinear), ("up", OracleLinear),
+                ("down", OracleLinear), ("norm1_w", C.c_void_p), ("norm1_b", C.c_void_p),
+                ("norm2_w", C.c_void_p), ("norm2_b", C.c_void_p)]
+
+
+class OracleCache(C.Structure):
+    _fields_ = [("n_layers", C.c_size_t), ("capacity", C.c_size_t), ("length", C.c_size_t),
+                ("keys", C.POINTER(C.c_float)), ("values", C.POINTER(C.c_float))]
+
+
+class Oracle:
+    """The C restatement."""
+
+    def __init__(self, path=ORACLE_SO):
+        if not Path(path).exists():
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle`")
+        L = self.lib = C.CDLL(str(path))
+        L.oracle_half_to_float.restype = C.c_float
+        L.oracle_half_to_float.argtypes = [C.c_uint16]
+        for name in ["oracle_q8_dot", "oracle_q8_matvec", "oracle_linear_batch",
+                     "oracle_layer_norm", "oracle_rms_norm", "oracle_erf_gelu",
+                     "oracle_rope_interleaved", "oracle_attention", "oracle_cache_init",
+                     "oracle_layer_step", "oracle_stack_step"]:
+            getattr(L, name).restype = C.c_int
+        L.oracle_q8_dot.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
+        L.oracle_q8_matvec.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p]
+        L.oracle_linear_batch.argtypes = [C.POINTER(OracleLinear), C.c_void_p, C.c_size_t,
+                                          C.c_void_p, C.c_void_p]
+        L.oracle_layer_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_float,
+                                        C.c_void_p]
+        L.oracle_rms_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_float, C.c_void_p]
+        L.oracle_erf_gelu.argtypes = [C.c_void_p, C.c_size_t]
+        L.oracle_rope_interleaved.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                              C.c_float]
+        L.oracle_attention.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t,
+                                       C.c_void_p]
+        L.oracle_cache_init.argtypes = [C.POINTER(OracleCache), C.c_size_t, C.c_size_t]
+        L.oracle_cache_destroy.argtypes = [C.POINTER(OracleCache)]
+        L.oracle_layer_step.argtypes = [C.POINTER(OracleLayer), C.POINTER(OracleCache), C.c_size_t,
+                                        C.c_size_t, C.c_void_p, C.c_float, C.c_void_p]
+        L.oracle_stack_step.argtypes = [C.POINTER(OracleLayer), C.c_size_t, C.POINTER(OracleCache),
+                                        C.c_size_t, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p]
+
+    # primitives -------------------------------------------------------------
+    def half_to_float(self, bits):
+        return self.lib.oracle_half_to_float(bits)
+
+    def q8_dot(self, blocks, x):
+        out = C.c_float()
+        ok = self.lib.oracle_q8_dot(_ptr(blocks), _ptr(x), x.size, C.byref(out))
+        return ok, out.value
+
+    def q8_matvec(self, blocks, x, rows, cols, out=None):
+        out = np.zeros(rows, np.float32) if out is None else out
+        ok = self.lib.oracle_q8_matvec(_ptr(blocks), _ptr(x), rows, cols, _ptr(out))
+        return ok, out
+
+    def linear(self, dtype, data, rows, cols, x, batch=1, bias=None):
+        lin = OracleLinear(dtype, rows, cols, data.ctypes.data)
+        out = np.zeros(batch * rows, np.float32)
+        ok = self.lib.oracle_linear_batch(C.byref(lin), _ptr(x), batch,
+                                          None if bias is None else _ptr(bias), _ptr(out))
+        return ok, out
+
+    def layer_norm(self, x, w, b, eps=1e-5):
+        out = np.zeros_like(x)
+        ok = self.lib.oracle_layer_norm(_ptr(x), _ptr(w), _ptr(b), x.size, eps, _ptr(out))
+        return ok, out
+
+    def rms_norm(self, x, w, eps=1e-5):
+        out = np.zeros_like(x)
+        ok = self.lib.oracle_rms_norm(_ptr(x), _ptr(w), x.size, eps, _ptr(out))
+        return ok, out
+
+    def erf_gelu(self, x):
+        y = np.array(x, np.float32, copy=True)
+        ok = self.lib.oracle_erf_gelu(_ptr(y), y.size)
+        return ok, y
+
+    def rope(self, x, heads, position, theta=10000.0):
+        y = np.array(x, np.float32, copy=True)
+        ok = self.lib.oracle_rope_interleaved(_ptr(y), y.size, heads, position, theta)
+        return ok, y
+
+    def attention(self, q, keys, values, count, stride):
+        out = np.zeros(64, np.float32)
+        ok = self.lib.oracle_attention(_ptr(q), _ptr(keys), _ptr(values), count, stride, _ptr(out))
+        return ok, out
+
+    # model ------------------------------------------------------------------
+    def model(self, weights, dtype=1):
+        return OracleModel(self, weights, dtype)
+
+
+class OracleModel:
+    """L-layer model over the restatement, one contiguous cache per stream."""
+
+    def __init__(self, oracle, weights, dtype=1):
+        self.o = oracle
+        self.weights = weights  # keep arrays alive
+        self.n_layers = len(weights)
+        self.layers = (OracleLayer * self.n_layers)()
+        for i, w in enumerate(weights):
+            lay = self.layers[i]
+            for name in ("qkv", "out", "up", "down"):
+                rows, cols = LINEAR_SHAPES[name]
+                setattr(lay, name, OracleLinear(dtype, rows, cols, w[name].ctypes.data))
+            lay.norm1_w, lay.norm1_b = w["norm1_w"].ctypes.data, w["norm1_b"].ctypes.data
+            lay.norm2_w, lay.norm2_b = w["norm2_w"].ctypes.data, w["norm2_b"].ctypes.data
+
+    def new_stream(self, capacity):
+        cache = OracleCache()
+        if not self.o.lib.oracle_cache_init(C.byref(cache), self.n_layers, capacity):
+            raise MemoryError("oracle cache")
+        return cache
+
+    def free_stream(self, cache):
+        self.o.lib.oracle_cache_destroy(C.byref(cache))
+
+    def step(self, cache, position, x, theta=10000.0, layer_outputs=False):
+        out = np.zeros(512, np.float32)
+        lo = np.zeros((self.n_layers, 512), np.float32) if layer_outputs else None
+        ok = self.o.lib.oracle_stack_step(self.layers, self.n_layers, C.byref(cache), position,
+                                          _ptr(np.ascontiguousarray(x, np.float32)), theta,
+                                          _ptr(out), None if lo is None else _ptr(lo))
+        return ok, out, lo
+
+    def layer_step(self, cache, layer, position, x, theta=10000.0):
+        out = np.zeros(512, np.float32)
+        ok = self.o.lib.oracle_layer_step(C.byref(self.layers[layer]), C.byref(cache), layer,
+                                          position, _ptr(np.ascontiguousarray(x, np.float32)),
+                                          theta, _ptr(out))
+        return ok, out
+
+    def kv(self, cache, layer, position):
+        n = cache.capacity * 512
+        base = layer * n + position * 512
+        keys = np.ctypeslib.as_array(cache.keys, shape=(cache.n_layers * n,))
+        vals = np.ctypeslib.as_array(cache.values, shape=(cache.n_layers * n,))
+        return keys[base:base + 512].copy(), vals[base:base + 512].copy()
+
+
+class PhononTensorView(C.Structure):
+    """src/phonon_pack.h:10-19 layout."""
+    _fields_ = [("dtype", C.c_int), ("rank", C.c_uint), ("shape", C.c_uint64 * 8),
+                ("data", C.c_void_p), ("byte_count", C.c_size_t), ("linear_data", C.c_void_p)]
+
+
+class Reference:
+    """The unmodified reference compiled under oracle/_ref."""
+
+    def __init__(self, path=REF_SO, blas_threads=1):
+        if not Path(path).exists():
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle ref`")
+        L = self.lib = C.CDLL(str(path))
+        L.ref_set_blas_threads.argtypes = [C.c_int]
+        L.ref_set_blas_threads(blas_threads)
+        L.ref_model_create.restype = C.c_void_p
+        L.ref_model_create.argtypes = [C.c_size_t, C.c_int, C.c_void_p, C.c_void_p]
+        L.ref_model_destroy.argtypes = [C.c_void_p]
+        L.ref_stream_create.restype = C.c_void_p
+        L.ref_stream_create.argtypes = [C.c_void_p, C.c_size_t]
+        L.ref_stream_destroy.argtypes = [C.c_void_p]
+        L.ref_stream_step.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_float,
+                                      C.c_void_p, C.c_void_p]
+        L.ref_layer_step.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p,
+                                     C.c_float, C.c_void_p]
+        L.ref_stream_commit.argtypes = [C.c_void_p, C.c_size_t]
+        L.ref_stream_prefill.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                         C.c_float, C.c_void_p]
+        L.ref_stream_kv.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_void_p]
+        L.ref_stream_fill.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_void_p]
+        L.ref_stream_length.restype = C.c_size_t
+        L.ref_stream_length.argtypes = [C.c_void_p]
+        L.phonon_q8_dot.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
+        L.phonon_q8_matvec.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p]
+        L.phonon_layer_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_float,
+                                        C.c_void_p]
+        L.phonon_rms_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_float, C.c_void_p]
+        L.phonon_erf_gelu.argtypes = [C.c_void_p, C.c_size_t]
+        L.phonon_rope_interleaved.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                              C.c_float]
+        L.phonon_attention_test.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t,
+                                            C.c_size_t, C.c_void_p]
+        L.phonon_prefill_attention_test.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p,
+                                                    C.c_size_t, C.c_void_p]
+        L.phonon_linear_batch.argtypes = [C.POINTER(PhononTensorView), C.c_void_p, C.c_size_t,
+                                          C.c_size_t, C.c_void_p, C.c_void_p, C.c_size_t]
+        L.phonon_math_sincos.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]
+        L.phonon_math_exp4.argtypes = [C.c_void_p]
+        L.phonon_math_silu.argtypes = [C.c_void_p, C.c_size_t]
+
+    def q8_dot(self, blocks, x):
+        out = C.c_float()
+        ok = self.lib.phonon_q8_dot(_ptr(blocks), _ptr(x), x.size, C.byref(out))
+        return ok, out.value
+
+    def q8_matvec(self, blocks, x, rows, cols, out=None):
+        out = np.zeros(rows, np.float32) if out is None else out
+        ok = self.lib.phonon_q8_matvec(_ptr(blocks), _ptr(x), rows, cols, _ptr(out))
+        return ok, out
+
+    def linear(self, dtype, data, rows, cols, x, batch=1, bias=None):
+        v = PhononTensorView()
+        v.dtype, v.rank = dtype, 2
+        v.shape[0], v.shape[1] = rows, cols
+        v.data = data.ctypes.data
+        v.byte_count = rows * cols * 2 if dtype == 2 else rows * cols // 32 * 34
+        out = np.zeros(batch * rows, np.float32)
+        ok = self.lib.phonon_linear_batch(C.byref(v), _ptr(x), rows, cols,
+                                          None if bias is None else _ptr(bias), _ptr(out), batch)
+        return ok, out
+
+    def layer_norm(self, x, w, b, eps=1e-5):
+        out = np.zeros_like(x)
+        ok = self.lib.phonon_layer_norm(_ptr(x), _ptr(w), _ptr(b), x.size, eps, _ptr(out))
+        return ok, out
+
+    def erf_gelu(self, x):
+        y = np.array(x, np.float32, copy=True)
+        ok = self.lib.phonon_erf_gelu(_ptr(y), y.size)
+        return ok, y
+
+    def rope(self, x, heads, position, theta=10000.0):
+        y = np.array(x, np.float32, copy=True)
+        ok = self.lib.phonon_rope_interleaved(_ptr(y), y.size, heads, position, theta)
+        return ok, y
+
+    def attention(self, q, keys, values, count, stride):
+        out = np.zeros(64, np.float32)
+        ok = self.lib.phonon_attention_test(_ptr(q), _ptr(keys), _ptr(values), count, stride,
+                                            _ptr(out))
+        return ok, out
+
+    def sincos(self, x):
+        c = np.zeros_like(x)
+        s = np.zeros_like(x)
+        self.lib.phonon_math_sincos(_ptr(x), x.size, _ptr(c), _ptr(s))
+        return c, s
+
+    def model(self, weights, dtype=1):
+        return RefModel(self, weights, dtype)
+
+
+class RefModel:
+    def __init__(self, ref, weights, dtype=1):
+        self.r = ref
+        self.weights = weights
+        self.n_layers = len(weights)
+        lin = (C.c_void_p * (4 * self.n_layers))()
+        nrm = (C.c_void_p * (4 * self.n_layers))()
+        for i, w in enumerate(weights):
+            for j, name in enumerate(("qkv", "out", "up", "down")):
+                lin[4 * i + j] = w[name].ctypes.data
+            for j, name in enumerate(("norm1_w", "norm1_b", "norm2_w", "norm2_b")):
+                nrm[4 * i + j] = w[name].ctypes.data
+        self.handle = ref.lib.ref_model_create(self.n_layers, dtype, lin, nrm)
+        if not self.handle:
+            raise RuntimeError("ref_model_create failed")
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            self.r.lib.ref_model_destroy(self.handle)
+            self.handle = None
+
+    def new_stream(self, capacity):
+        s = self.r.lib.ref_stream_create(self.handle, capacity)
+        if not s:
+            raise MemoryError("ref stream")
+        return s
+
+    def free_stream(self, s):
+        self.r.lib.ref_stream_destroy(s)
+
+    def step(self, stream, position, x, theta=10000.0, layer_outputs=False):
+        out = np.zeros(512, np.float32)
+        lo = np.zeros((self.n_layers, 512), np.float32) if layer_outputs else None
+        ok = self.r.lib.ref_stream_step(self.handle, stream, position,
+                                        _ptr(np.ascontiguousarray(x, np.float32)), theta,
+                                        _ptr(out), None if lo is None else _ptr(lo))
+        return ok, out, lo
+
+    def layer_step(self, stream, layer, position, x, theta=10000.0):
+        out = np.zeros(512, np.float32)
+        ok = self.r.lib.ref_layer_step(self.handle, stream, layer, position,
+                                       _ptr(np.ascontiguousarray(x, np.float32)), theta, _ptr(out))
+        return ok, out
+
+    def commit(self, stream, position):
+        return self.r.lib.ref_stream_commit(stream, position)
+
+    def kv(self, stream, layer, position):
+        k = np.zeros(512, np.float32)
+        v = np.zeros(512, np.float32)
+        ok = self.r.lib.ref_stream_kv(stream, layer, position, _ptr(k), _ptr(v))
+        assert ok
+        return k, v
+
+    def fill(self, stream, length, keys, values):
+        return self.r.lib.ref_stream_fill(stream, self.n_layers, length, _ptr(keys), _ptr(values))
+
+    def length(self, stream):
+        return self.r.lib.ref_stream_length(stream)

@@ -1,0 +1,70 @@
+/* CPU oracle for the Flow-transformer decode step: a plain-C restatement of
+ * the speech-mac reference algorithm (src/phonon_transformer.c, src/phonon_q8.c,
+ * src/phonon_pack.c) for any number of layers.
+ *
+ * TEST INFRASTRUCTURE ONLY. Only tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / reference arm of bench.py may load this library, and only as
+ * the checker. The CUDA product path never links or calls it.
+ *
+ * All entry points return 1 on success and 0 on failure, like the reference.
+ * Linear layers use a sequential fp32 dot product where the reference calls
+ * cblas_sgemm; every other routine follows the reference's operation order.
+ */
+#ifndef PHONON_ORACLE_H
+#define PHONON_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#define ORACLE_WIDTH 512
+#define ORACLE_HEADS 8
+#define ORACLE_HEAD_WIDTH 64
+#define ORACLE_FFN 2048
+#define ORACLE_MAX_POSITIONS 8192
+
+/* Linear storage kinds (reference PhononPackDType values). */
+#define ORACLE_Q8_0 1
+#define ORACLE_BF16 2
+
+typedef struct {
+    int dtype;
+    size_t rows, cols;
+    const void *data; /* Q8_0: rows*cols/32 34-byte blocks; BF16: rows*cols u16 */
+} OracleLinear;
+
+typedef struct {
+    OracleLinear qkv, out, up, down;
+    const uint16_t *norm1_w, *norm1_b, *norm2_w, *norm2_b; /* bf16 [512] */
+} OracleLayer;
+
+typedef struct {
+    size_t n_layers, capacity, length;
+    float *keys, *values; /* [layer][capacity][512], interleaved-RoPE order */
+} OracleCache;
+
+float oracle_half_to_float(uint16_t bits);
+int oracle_q8_dot(const void *blocks, const float *input, size_t elements, float *result);
+int oracle_q8_matvec(const void *weights, const float *input, size_t rows, size_t columns,
+                     float *output);
+int oracle_linear_batch(const OracleLinear *w, const float *input, size_t batch, const float *bias,
+                        float *output);
+int oracle_layer_norm(const float *input, const float *weight, const float *bias, size_t width,
+                      float epsilon, float *output);
+int oracle_rms_norm(const float *input, const float *weight, size_t width, float epsilon,
+                    float *output);
+int oracle_erf_gelu(float *values, size_t count);
+int oracle_rope_interleaved(float *values, size_t width, size_t heads, size_t position,
+                            float theta);
+int oracle_attention(const float query[64], const float *keys, const float *values, size_t count,
+                     size_t stride, float output[64]);
+
+int oracle_cache_init(OracleCache *cache, size_t n_layers, size_t capacity);
+void oracle_cache_destroy(OracleCache *cache);
+int oracle_layer_step(const OracleLayer *w, OracleCache *cache, size_t layer, size_t position,
+                      const float *input, float theta, float *output);
+/* Full step over n_layers; layer_outputs (optional) receives [n_layers][512]. */
+int oracle_stack_step(const OracleLayer *layers, size_t n_layers, OracleCache *cache,
+                      size_t position, const float *input, float theta, float *output,
+                      float *layer_outputs);
+
+#endif
