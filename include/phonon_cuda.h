@@ -1,0 +1,182 @@
+/* libphonon_cuda: B200 (sm_100a) Flow-transformer decode step behind a C ABI.
+ *
+ * This is the only boundary between host code and the GPU. It replaces the
+ * compute of speech-mac's src/phonon_transformer.c / src/phonon_q8.c; the C17
+ * drop-in (libphonon_transformer_cuda, include/phonon_transformer.h) keeps the
+ * reference prototypes and calls these entry points. Plain pointers and sizes
+ * only; every call returns a PhononCudaStatus and never throws.
+ *
+ * Model: d_model 512, 8 heads x 64, FFN 2048 (src/phonon_transformer.h:11-14),
+ * pre-LayerNorm blocks with interleaved RoPE (src/phonon_transformer.c:406-453),
+ * a runtime layer count (the reference fixes 9).
+ *
+ * KV cache: a device pool of fixed 16-position pages. A page holds the K and
+ * V rows of 16 consecutive positions for every layer; each stream owns a page
+ * table (position p lives in page table[p / 16], slot p % 16). Reading a
+ * stream's K/V back (phonon_cuda_kv_read) returns exactly the rows the
+ * reference would hold in its contiguous PhononKvCache.
+ *
+ * Threading: a context may be shared by threads; calls on one context are
+ * serialised internally. Contexts on different devices run independently.
+ */
+#ifndef PHONON_CUDA_H
+#define PHONON_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    PHONON_CUDA_OK = 0,
+    PHONON_CUDA_INVALID_ARGUMENT = 1, /* bad pointer, size, stream id or shape */
+    PHONON_CUDA_NON_FINITE = 2,       /* a non-finite input, weight or result */
+    PHONON_CUDA_OUT_OF_MEMORY = 3,    /* device or pinned host allocation failed */
+    PHONON_CUDA_POOL_EXHAUSTED = 4,   /* no free KV page */
+    PHONON_CUDA_CAPACITY = 5,         /* position >= stream capacity or 8192 */
+    PHONON_CUDA_BAD_POSITION = 6,     /* position != committed stream length */
+    PHONON_CUDA_CANCELLED = 7,        /* cancel poll returned nonzero */
+    PHONON_CUDA_DEVICE_ERROR = 8      /* CUDA runtime/driver error */
+} PhononCudaStatus;
+
+typedef enum { PHONON_CUDA_LINEAR_Q8_0 = 1, PHONON_CUDA_LINEAR_BF16 = 2 } PhononCudaLinearKind;
+typedef enum { PHONON_CUDA_KV_F32 = 0, PHONON_CUDA_KV_BF16 = 1 } PhononCudaKvType;
+
+#define PHONON_CUDA_WIDTH 512
+#define PHONON_CUDA_PAGE_POSITIONS 16
+#define PHONON_CUDA_MAX_POSITIONS 8192
+
+typedef struct {
+    int device;            /* CUDA ordinal */
+    uint32_t n_layers;     /* 1..64 */
+    uint32_t max_streams;  /* resident stream slots */
+    uint32_t max_batch;    /* streams per step call */
+    uint32_t pool_pages;   /* KV pool size in 16-position pages */
+    uint32_t kv_type;      /* PhononCudaKvType */
+    float theta;           /* RoPE base, 10000 in the reference */
+} PhononCudaConfig;
+
+/* One Flow layer, host memory, borrowed only while a call uploads it.
+ * Linears are Q8_0 blocks (34-byte PhononQ8Block, row-major) or bf16 per
+ * linear_kind: qkv [1536,512] (rows 0-511 Q, 512-1023 K, 1024-1535 V, RoPE
+ * interleaved), attention_out [512,512], mlp_in [2048,512], mlp_out [512,2048]
+ * (src/phonon_transformer.h:24-31). Norm vectors are bf16 [512]. */
+typedef struct {
+    const void *qkv, *attention_out, *mlp_in, *mlp_out;
+    const uint16_t *norm1_weight, *norm1_bias, *norm2_weight, *norm2_bias;
+    uint32_t linear_kind; /* PhononCudaLinearKind of the four projections */
+} PhononCudaLayer;
+
+typedef struct PhononCuda PhononCuda;
+typedef int (*PhononCudaCancelPoll)(void *context);
+
+/* Upload weights (repacked for the GEMV kernels) and allocate the KV pool and
+ * step scratch. Rejects non-finite scales or norm values (the reference
+ * rejects them on first use, src/phonon_pack.c:389-397, :320-325). */
+int phonon_cuda_create(const PhononCudaConfig *config, const PhononCudaLayer *layers,
+                       PhononCuda **out);
+void phonon_cuda_destroy(PhononCuda *ctx);
+/* Replace the weights of one layer in place (streams and KV are kept). */
+int phonon_cuda_set_layer(PhononCuda *ctx, uint32_t layer, const PhononCudaLayer *weights);
+/* Change the RoPE base for subsequent calls (the reference passes theta per call). */
+int phonon_cuda_set_theta(PhononCuda *ctx, float theta);
+
+/* Streams replace the reference's request-owned PhononKvCache
+ * (src/phonon_transformer.c:16-43): alloc ~ kv_cache_init, reset ~
+ * kv_cache_reset (pages return to the pool), free ~ kv_cache_destroy. */
+int phonon_cuda_stream_alloc(PhononCuda *ctx, uint32_t capacity, uint32_t *stream);
+int phonon_cuda_stream_reset(PhononCuda *ctx, uint32_t stream);
+int phonon_cuda_stream_free(PhononCuda *ctx, uint32_t stream);
+int phonon_cuda_stream_length(PhononCuda *ctx, uint32_t stream, uint32_t *length);
+/* Page ids backing positions [0, n_pages*16): the KV page table of a stream. */
+int phonon_cuda_stream_pages(PhononCuda *ctx, uint32_t stream, int32_t *pages, uint32_t max_pages,
+                             uint32_t *n_pages);
+uint32_t phonon_cuda_free_pages(PhononCuda *ctx);
+
+/* Batched decode step (phonon_flow_stack_step_cancel, src/phonon_transformer.c:455-482,
+ * for n streams at once). Host buffers x[n][512] in, y[n][512] out. Each
+ * streams[i] must be at positions[i] == its committed length. status[i] gets
+ * a PhononCudaStatus; a stream commits its position and has y[i] written only
+ * when status[i] == OK. cancel (optional) is polled before every layer and
+ * once after the last one; a nonzero poll resets every stream of the call and
+ * returns PHONON_CUDA_CANCELLED without writing y. */
+int phonon_cuda_step(PhononCuda *ctx, uint32_t n, const uint32_t *streams,
+                     const uint32_t *positions, const float *x, float *y, int32_t *status,
+                     PhononCudaCancelPoll cancel, void *cancel_context);
+
+/* Same step with device-resident activations x_dev/y_dev ([n][512] fp32),
+ * enqueued on the context's CUDA stream without waiting; commit happens at
+ * phonon_cuda_sync, which also returns per-stream status. Between the two
+ * calls no other call may use the context. */
+int phonon_cuda_step_device(PhononCuda *ctx, uint32_t n, const uint32_t *streams,
+                            const uint32_t *positions, const float *x_dev, float *y_dev);
+int phonon_cuda_sync(PhononCuda *ctx, int32_t *status);
+/* The context's CUDA stream (a cudaStream_t) for event timing. */
+void *phonon_cuda_cuda_stream(PhononCuda *ctx);
+
+/* One layer of one stream (phonon_flow_layer_step, src/phonon_transformer.c:406-453):
+ * appends K/V at `position`, attends over position+1 keys, does not commit. */
+int phonon_cuda_layer_step(PhononCuda *ctx, uint32_t stream, uint32_t layer, uint32_t position,
+                           const float *x, float *y);
+/* Commit `position` (phonon_kv_cache_commit_position, src/phonon_transformer.c:59-64). */
+int phonon_cuda_commit(PhononCuda *ctx, uint32_t stream, uint32_t position);
+
+/* Prefill (phonon_flow_stack_prefill_cancel, src/phonon_transformer.c:619-702):
+ * run `length` rows [length][512] through the stack as consecutive positions
+ * of an empty stream and commit them; last_output gets the last row's output.
+ * On failure or cancel the stream is reset and last_output is untouched. */
+int phonon_cuda_append(PhononCuda *ctx, uint32_t stream, const float *rows, uint32_t length,
+                       float *last_output, PhononCudaCancelPoll cancel, void *cancel_context);
+
+/* K/V rows of layers [layer_begin, layer_begin+layer_count) at positions
+ * [position, position+count), as [layer_count][count][512] fp32 in the
+ * reference's interleaved-RoPE order (phonon_kv_cache_append,
+ * src/phonon_transformer.c:45-57). Positions in pages the stream never
+ * allocated read as zeros; positions of an allocated page that were never
+ * written hold unspecified values (pages are not cleared on allocation).
+ * kv_write accepts only finite rows and allocates pages on first touch; it
+ * does not change the length. */
+int phonon_cuda_kv_read(PhononCuda *ctx, uint32_t stream, uint32_t layer_begin, uint32_t layer_count,
+                        uint32_t position, uint32_t count, float *keys, float *values);
+int phonon_cuda_kv_write(PhononCuda *ctx, uint32_t stream, uint32_t layer_begin,
+                         uint32_t layer_count, uint32_t position, uint32_t count,
+                         const float *keys, const float *values);
+/* Fill positions [0, length) of every layer with seeded pseudo-random K/V on
+ * the device and commit them: a synthetic context for decode benchmarks. */
+int phonon_cuda_stream_fill_synthetic(PhononCuda *ctx, uint32_t stream, uint32_t length,
+                                      uint64_t seed);
+
+/* ---- standalone linear (phonon_linear_batch / phonon_q8_matvec) ---- */
+typedef struct PhononCudaLinear PhononCudaLinear;
+/* Upload a [rows, cols] Q8_0 or bf16 matrix (cols % 32 == 0) to `device`. */
+int phonon_cuda_linear_create(int device, int kind, const void *data, size_t rows, size_t cols,
+                              PhononCudaLinear **out);
+void phonon_cuda_linear_destroy(PhononCudaLinear *linear);
+/* y[batch][rows] = x[batch][cols] W^T (+ bias), host buffers
+ * (src/phonon_transformer.c:253-313, src/phonon_q8.c:64-92). */
+int phonon_cuda_linear_apply(PhononCudaLinear *linear, const float *x, size_t batch,
+                             const float *bias, float *y);
+/* Same on device buffers, enqueued on `cuda_stream` (a cudaStream_t, may be 0). */
+int phonon_cuda_linear_apply_device(PhononCudaLinear *linear, const float *x_dev, size_t batch,
+                                    const float *bias_dev, float *y_dev, int32_t *status_dev,
+                                    void *cuda_stream);
+/* Bytes of the device copy (int8 plane + fp16 scales, or bf16). */
+size_t phonon_cuda_linear_bytes(const PhononCudaLinear *linear);
+
+/* ---- primitives on host buffers (src/phonon_transformer.c:66-251) ---- */
+int phonon_cuda_layer_norm(int device, const float *x, const float *w, const float *b,
+                           size_t width, float epsilon, float *out);
+int phonon_cuda_rms_norm(int device, const float *x, const float *w, size_t width, float epsilon,
+                         float *out);
+int phonon_cuda_erf_gelu(int device, float *values, size_t count);
+int phonon_cuda_rope_interleaved(int device, float *values, size_t width, size_t heads,
+                                 size_t position, float theta);
+
+const char *phonon_cuda_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,1380 @@
+// libphonon_cuda host runtime: contexts, KV page pool, step scheduling and
+// the C ABI declared in include/phonon_cuda.h.
+#include "phonon_cuda.h"
+#include "phonon_kernels.cuh"
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <vector>
+
+using namespace phonon;
+
+namespace {
+
+constexpr int kMaxLayers = 64;
+constexpr int kMaxDevices = 64;
+constexpr int kMaxPagesPerStream = PHONON_CUDA_MAX_POSITIONS / kPage;  // 512
+constexpr int kSplitTarget = 640;   // ~8 warps per split: fills 148 SMs several times over
+constexpr int kPrefillChunk = 256;  // rows per prefill pass
+
+#define CUDA_TRY(expr)                                                                       \
+    do {                                                                                     \
+        cudaError_t err_ = (expr);                                                           \
+        if (err_ != cudaSuccess) {                                                           \
+            std::fprintf(stderr, "phonon_cuda: %s failed: %s (%s:%d)\n", #expr,              \
+                         cudaGetErrorString(err_), __FILE__, __LINE__);                      \
+            return PHONON_CUDA_DEVICE_ERROR;                                                 \
+        }                                                                                    \
+    } while (0)
+
+// ------------------------------------------------------------ device linears
+struct DevLinear {
+    int kind = 0;
+    int rows = 0, cols = 0;
+    bool fast = false;  // lane-interleaved layout for the GEMV kernel
+    void* plane = nullptr;
+    __half* scales = nullptr;
+    size_t bytes = 0;
+};
+
+bool half_is_finite(uint16_t h) { return ((h >> 10) & 0x1f) != 0x1f; }
+
+bool bf16_is_finite(uint16_t b) { return ((b >> 7) & 0xff) != 0xff; }
+
+float bf16_host(uint16_t b) {
+    uint32_t u = static_cast<uint32_t>(b) << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+void free_linear(DevLinear& l) {
+    if (l.plane) cudaFree(l.plane);
+    if (l.scales) cudaFree(l.scales);
+    l = DevLinear{};
+}
+
+// Repack a host Q8_0 (34-byte blocks) or bf16 [rows, cols] matrix into the
+// device layout and upload it. The fast layout is described next to
+// GemvParams in phonon_kernels.cuh; other shapes keep natural row-major order.
+int upload_linear(int kind, const void* host, size_t rows, size_t cols, DevLinear* out) {
+    if (!host || !rows || !cols || rows > (1u << 24) || cols > (1u << 20)) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (kind == PHONON_CUDA_LINEAR_Q8_0 && cols % 32) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (kind != PHONON_CUDA_LINEAR_Q8_0 && kind != PHONON_CUDA_LINEAR_BF16) return PHONON_CUDA_INVALID_ARGUMENT;
+    DevLinear l;
+    l.kind = kind;
+    l.rows = static_cast<int>(rows);
+    l.cols = static_cast<int>(cols);
+    l.fast = cols % 512 == 0 && (cols == 512 || cols == 2048);
+    const size_t n = rows * cols;
+    auto logical = [&](size_t c) -> size_t {  // device column position -> logical column
+        if (!l.fast) return c;
+        const size_t chunk = c / 512, in = c % 512, lane = in / 16, j = (in % 16) / 4, e = in % 4;
+        return chunk * 512 + j * 128 + lane * 4 + e;
+    };
+    if (kind == PHONON_CUDA_LINEAR_Q8_0) {
+        const uint8_t* blocks = static_cast<const uint8_t*>(host);
+        std::vector<int8_t> q(n);
+        std::vector<uint16_t> s(n / 32);
+        for (size_t r = 0; r < rows; ++r) {
+            const uint8_t* row = blocks + r * (cols / 32) * 34;
+            for (size_t b = 0; b < cols / 32; ++b) {
+                const uint16_t h = static_cast<uint16_t>(row[b * 34] | (row[b * 34 + 1] << 8));
+                if (!half_is_finite(h)) return PHONON_CUDA_NON_FINITE;
+                size_t dst = b;
+                if (l.fast) {  // block c*16 + j*4 + g stored at c*16 + g*4 + j
+                    const size_t c = b / 16, k = b % 16, j = k / 4, g = k % 4;
+                    dst = c * 16 + g * 4 + j;
+                }
+                s[r * (cols / 32) + dst] = h;
+            }
+            for (size_t c = 0; c < cols; ++c) {
+                const size_t lc = logical(c);
+                q[r * cols + c] = static_cast<int8_t>(row[(lc / 32) * 34 + 2 + lc % 32]);
+            }
+        }
+        if (cudaMalloc(&l.plane, n) != cudaSuccess ||
+            cudaMalloc(reinterpret_cast<void**>(&l.scales), s.size() * 2) != cudaSuccess) {
+            free_linear(l);
+            return PHONON_CUDA_OUT_OF_MEMORY;
+        }
+        if (cudaMemcpy(l.plane, q.data(), n, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(l.scales, s.data(), s.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
+            free_linear(l);
+            return PHONON_CUDA_DEVICE_ERROR;
+        }
+        l.bytes = n + s.size() * 2;
+    } else {
+        const uint16_t* src = static_cast<const uint16_t*>(host);
+        std::vector<uint16_t> w(n);
+        for (size_t r = 0; r < rows; ++r)
+            for (size_t c = 0; c < cols; ++c) {
+                const uint16_t v = src[r * cols + logical(c)];
+                if (!bf16_is_finite(v)) return PHONON_CUDA_NON_FINITE;
+                w[r * cols + c] = v;
+            }
+        if (cudaMalloc(&l.plane, n * 2) != cudaSuccess) return PHONON_CUDA_OUT_OF_MEMORY;
+        if (cudaMemcpy(l.plane, w.data(), n * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
+            free_linear(l);
+            return PHONON_CUDA_DEVICE_ERROR;
+        }
+        l.bytes = n * 2;
+    }
+    *out = l;
+    return PHONON_CUDA_OK;
+}
+
+// ------------------------------------------------------------- GEMV launcher
+template <bool kQ8, int kChunks, int kBT, bool kLN, int kEpi>
+cudaError_t launch_gemv_t(const GemvParams& p, cudaStream_t s) {
+    auto kern = gemv_kernel<kQ8, kChunks, kBT, kLN, kEpi>;
+    constexpr int smem = kBT * kChunks * 512 * 4;
+    if constexpr (smem > 48 * 1024) {
+        // The opt-in shared memory size is a per-device function attribute.
+        static bool configured[kMaxDevices] = {};
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
+        if (!configured[dev]) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return e;
+            configured[dev] = true;
+        }
+    }
+    const int rows_per_cta = kGemvWarps * kRowsPerWarp;
+    kern<<<(p.rows + rows_per_cta - 1) / rows_per_cta, kGemvWarps * 32, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <bool kQ8, int kChunks, bool kLN, int kEpi>
+cudaError_t launch_gemv_bt(const GemvParams& p, cudaStream_t s) {
+    if (p.B <= 1) return launch_gemv_t<kQ8, kChunks, 1, kLN, kEpi>(p, s);
+    if (p.B <= 2) return launch_gemv_t<kQ8, kChunks, 2, kLN, kEpi>(p, s);
+    if (p.B <= 4) return launch_gemv_t<kQ8, kChunks, 4, kLN, kEpi>(p, s);
+    return launch_gemv_t<kQ8, kChunks, 8, kLN, kEpi>(p, s);
+}
+
+template <int kChunks, bool kLN, int kEpi>
+cudaError_t launch_gemv(bool q8, const GemvParams& p, cudaStream_t s) {
+    return q8 ? launch_gemv_bt<true, kChunks, kLN, kEpi>(p, s) : launch_gemv_bt<false, kChunks, kLN, kEpi>(p, s);
+}
+
+cudaError_t launch_linear(const DevLinear& l, const float* x, int B, const float* bias, float* y,
+                          int32_t* status, cudaStream_t s) {
+    const bool q8 = l.kind == PHONON_CUDA_LINEAR_Q8_0;
+    if (l.fast) {
+        GemvParams p{};
+        p.w = l.plane;
+        p.scales = l.scales;
+        p.rows = l.rows;
+        p.cols = l.cols;
+        p.x = x;
+        p.ldx = l.cols;
+        p.B = B;
+        p.bias = bias;
+        p.y = y;
+        p.ldy = l.rows;
+        p.status = status;
+        return l.cols == 512 ? launch_gemv<1, false, EPI_STORE>(q8, p, s) : launch_gemv<4, false, EPI_STORE>(q8, p, s);
+    }
+    const long long warps = static_cast<long long>(l.rows) * B;
+    const int threads = 256;
+    const long long blocks = (warps * 32 + threads - 1) / threads;
+    if (q8)
+        linear_generic_kernel<true><<<static_cast<unsigned>(blocks), threads, 0, s>>>(l.plane, l.scales, l.rows, l.cols, x, B, bias, y, status);
+    else
+        linear_generic_kernel<false><<<static_cast<unsigned>(blocks), threads, 0, s>>>(l.plane, nullptr, l.rows, l.cols, x, B, bias, y, status);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------- context
+struct StreamSlot {
+    bool used = false;
+    uint32_t capacity = 0, length = 0;
+    std::vector<int32_t> pages;
+};
+
+struct DevLayer {
+    DevLinear qkv, out, up, down;
+    float* norms = nullptr;  // fp32 [4][512]: norm1 w, norm1 b, norm2 w, norm2 b
+    bool q8 = true;
+};
+
+struct PhononCuda {
+    PhononCudaConfig cfg{};
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    std::vector<DevLayer> layers;
+    void* kv_pool = nullptr;
+    long long page_elems = 0;
+    int32_t* d_table = nullptr;
+    std::vector<int32_t> free_pages;
+    std::vector<StreamSlot> streams;
+    float* d_freq = nullptr;
+    int cap_rows = 0, max_splits = 0, meta_ints = 0;
+    float *d_x0 = nullptr, *d_x1 = nullptr, *d_y = nullptr, *d_q = nullptr, *d_a = nullptr,
+          *d_h = nullptr, *d_g = nullptr, *d_part = nullptr, *d_stage = nullptr;
+    int32_t *d_meta = nullptr, *d_status = nullptr;
+    int32_t* h_meta = nullptr;
+    float *h_x = nullptr, *h_y = nullptr, *h_stage = nullptr;
+    size_t stage_cap = 0;  // floats in d_stage / h_stage
+    int32_t* h_status = nullptr;
+    // pending phonon_cuda_step_device
+    bool pending = false;
+    std::vector<uint32_t> pending_streams;
+    std::vector<int32_t> pending_new_pages;
+};
+
+namespace {
+
+void free_layer(DevLayer& D) {
+    free_linear(D.qkv);
+    free_linear(D.out);
+    free_linear(D.up);
+    free_linear(D.down);
+    if (D.norms) cudaFree(D.norms);
+    D = DevLayer{};
+}
+
+// Upload one layer into `D` (freeing what it held only once the new copy is
+// complete, so a failed upload leaves the old weights in place).
+int load_layer(DevLayer* D, const PhononCudaLayer& w) {
+    if (!w.qkv || !w.attention_out || !w.mlp_in || !w.mlp_out || !w.norm1_weight || !w.norm1_bias ||
+        !w.norm2_weight || !w.norm2_bias ||
+        (w.linear_kind != PHONON_CUDA_LINEAR_Q8_0 && w.linear_kind != PHONON_CUDA_LINEAR_BF16))
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    float norms[4 * kWidth];
+    const uint16_t* src[4] = {w.norm1_weight, w.norm1_bias, w.norm2_weight, w.norm2_bias};
+    for (int k = 0; k < 4; ++k)
+        for (int i = 0; i < kWidth; ++i) {
+            if (!bf16_is_finite(src[k][i])) return PHONON_CUDA_NON_FINITE;
+            norms[k * kWidth + i] = bf16_host(src[k][i]);
+        }
+    DevLayer N;
+    N.q8 = w.linear_kind == PHONON_CUDA_LINEAR_Q8_0;
+    int st;
+    if ((st = upload_linear(w.linear_kind, w.qkv, 1536, 512, &N.qkv)) ||
+        (st = upload_linear(w.linear_kind, w.attention_out, 512, 512, &N.out)) ||
+        (st = upload_linear(w.linear_kind, w.mlp_in, 2048, 512, &N.up)) ||
+        (st = upload_linear(w.linear_kind, w.mlp_out, 512, 2048, &N.down))) {
+        free_layer(N);
+        return st;
+    }
+    if (cudaMalloc(&N.norms, sizeof(norms)) != cudaSuccess) {
+        free_layer(N);
+        return PHONON_CUDA_OUT_OF_MEMORY;
+    }
+    if (cudaMemcpy(N.norms, norms, sizeof(norms), cudaMemcpyHostToDevice) != cudaSuccess) {
+        free_layer(N);
+        return PHONON_CUDA_DEVICE_ERROR;
+    }
+    free_layer(*D);
+    *D = N;
+    return PHONON_CUDA_OK;
+}
+
+KvView kv_view(const PhononCuda* c) {
+    KvView kv;
+    kv.pool = c->kv_pool;
+    kv.page_elems = c->page_elems;
+    kv.bf16 = c->cfg.kv_type == PHONON_CUDA_KV_BF16;
+    kv.table = c->d_table;
+    kv.max_pages = kMaxPagesPerStream;
+    return kv;
+}
+
+bool valid_stream(const PhononCuda* c, uint32_t s) { return s < c->streams.size() && c->streams[s].used; }
+
+// Row batch for one enqueue: entry e is (stream slot, position); splits are
+// planned over the pages each entry attends.
+struct Batch {
+    int R = 0, S = 0, U = 0;
+    int32_t *d_slot, *d_pos, *d_first, *d_count, *d_updates;
+    Split* d_splits;
+};
+
+// Pages the caller allocated in this call, so that a failure can return them.
+struct PageUndo {
+    PhononCuda* c;
+    std::vector<std::pair<uint32_t, int32_t>> taken;  // (stream, page)
+    void rollback() {
+        for (auto it = taken.rbegin(); it != taken.rend(); ++it) {
+            c->streams[it->first].pages.pop_back();
+            c->free_pages.push_back(it->second);
+        }
+        taken.clear();
+    }
+};
+
+// Grow stream s to at least n pages; records page-table updates.
+int ensure_pages(PhononCuda* c, uint32_t s, uint32_t n, PageUndo& undo, std::vector<int32_t>& updates) {
+    StreamSlot& st = c->streams[s];
+    while (st.pages.size() < n) {
+        if (c->free_pages.empty()) return PHONON_CUDA_POOL_EXHAUSTED;
+        const int32_t page = c->free_pages.back();
+        c->free_pages.pop_back();
+        updates.push_back(static_cast<int32_t>(s));
+        updates.push_back(static_cast<int32_t>(st.pages.size()));
+        updates.push_back(page);
+        st.pages.push_back(page);
+        undo.taken.emplace_back(s, page);
+    }
+    return PHONON_CUDA_OK;
+}
+
+void release_pages(PhononCuda* c, uint32_t s) {
+    StreamSlot& st = c->streams[s];
+    for (auto it = st.pages.rbegin(); it != st.pages.rend(); ++it) c->free_pages.push_back(*it);
+    st.pages.clear();
+    st.length = 0;
+}
+
+// Pack metadata for entries (slot[e], pos[e]) into pinned memory, upload it
+// and apply page-table updates. Entry e attends over pos[e] + 1 keys.
+int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vector<int32_t>& pos,
+                 const std::vector<int32_t>& updates, Batch* out) {
+    const int R = static_cast<int>(slot.size());
+    long long total_pages = 0;
+    for (int e = 0; e < R; ++e) total_pages += pos[e] / kPage + 1;
+    const long long pps = std::max<long long>(1, (total_pages + kSplitTarget - 1) / kSplitTarget);
+    int32_t* m = c->h_meta;
+    int32_t *h_slot = m, *h_pos = m + R, *h_first = m + 2 * R, *h_count = m + 3 * R;
+    Split* h_splits = reinterpret_cast<Split*>(m + 4 * R);
+    int S = 0;
+    for (int e = 0; e < R; ++e) {
+        h_slot[e] = slot[e];
+        h_pos[e] = pos[e];
+        const int n_keys = pos[e] + 1, n_pages = pos[e] / kPage + 1;
+        h_first[e] = S;
+        int ns = 0;
+        for (int pb = 0; pb < n_pages; pb += static_cast<int>(pps), ++ns, ++S) {
+            if (S >= c->max_splits) return PHONON_CUDA_INVALID_ARGUMENT;
+            h_splits[S] = Split{e, pb, std::min<int>(static_cast<int>(pps), n_pages - pb), n_keys};
+        }
+        h_count[e] = ns;
+    }
+    const int U = static_cast<int>(updates.size() / 3);
+    int32_t* h_upd = m + 4 * R + 4 * S;
+    if (4 * R + 4 * S + 3 * U > c->meta_ints) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::memcpy(h_upd, updates.data(), updates.size() * 4);
+    const size_t bytes = static_cast<size_t>(4 * R + 4 * S + 3 * U) * 4;
+    CUDA_TRY(cudaMemcpyAsync(c->d_meta, c->h_meta, bytes, cudaMemcpyHostToDevice, c->stream));
+    Batch b;
+    b.R = R;
+    b.S = S;
+    b.U = U;
+    b.d_slot = c->d_meta;
+    b.d_pos = c->d_meta + R;
+    b.d_first = c->d_meta + 2 * R;
+    b.d_count = c->d_meta + 3 * R;
+    b.d_splits = reinterpret_cast<Split*>(c->d_meta + 4 * R);
+    b.d_updates = c->d_meta + 4 * R + 4 * S;
+    if (U > 0) {
+        page_update_kernel<<<(U + 127) / 128, 128, 0, c->stream>>>(c->d_table, kMaxPagesPerStream, b.d_updates, U);
+        CUDA_TRY(cudaGetLastError());
+    }
+    *out = b;
+    return PHONON_CUDA_OK;
+}
+
+// Enqueue layer `l` for the batch: in -> out (out != in).
+int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* out) {
+    const DevLayer& L = c->layers[l];
+    const bool q8 = L.q8;
+    cudaStream_t s = c->stream;
+    const KvView kv = kv_view(c);
+    GemvParams p{};
+    p.B = b.R;
+    p.status = c->d_status;
+    // 1. LN1 -> QKV -> RoPE -> q scratch + KV append
+    p.w = L.qkv.plane;
+    p.scales = L.qkv.scales;
+    p.rows = 1536;
+    p.cols = 512;
+    p.x = in;
+    p.ldx = kWidth;
+    p.ln_w = L.norms;
+    p.ln_b = L.norms + kWidth;
+    p.q = c->d_q;
+    p.slot = b.d_slot;
+    p.pos = b.d_pos;
+    p.freq = c->d_freq;
+    p.kv = kv;
+    p.layer = l;
+    CUDA_TRY((launch_gemv<1, true, EPI_QKV>(q8, p, s)));
+    // 2. split-K attention + combine
+    AttnParams ap{};
+    ap.q = c->d_q;
+    ap.slot = b.d_slot;
+    ap.splits = b.d_splits;
+    ap.n_splits = b.S;
+    ap.kv = kv;
+    ap.layer = l;
+    ap.part = c->d_part;
+    ap.status = c->d_status;
+    const long long warps = static_cast<long long>(b.S) * kHeads;
+    const unsigned grid = static_cast<unsigned>((warps + kAttnWarps - 1) / kAttnWarps);
+    if (kv.bf16) attn_partial_kernel<true><<<grid, kAttnWarps * 32, 0, s>>>(ap);
+    else attn_partial_kernel<false><<<grid, kAttnWarps * 32, 0, s>>>(ap);
+    CUDA_TRY(cudaGetLastError());
+    CombineParams cp{};
+    cp.part = c->d_part;
+    cp.first = b.d_first;
+    cp.count = b.d_count;
+    cp.B = b.R;
+    cp.out = c->d_a;
+    cp.status = c->d_status;
+    attn_combine_kernel<<<static_cast<unsigned>((static_cast<long long>(b.R) * kHeads + kAttnWarps - 1) / kAttnWarps),
+                          kAttnWarps * 32, 0, s>>>(cp);
+    CUDA_TRY(cudaGetLastError());
+    // 3. h = x + attn Wout^T
+    GemvParams po{};
+    po.B = b.R;
+    po.status = c->d_status;
+    po.w = L.out.plane;
+    po.scales = L.out.scales;
+    po.rows = 512;
+    po.cols = 512;
+    po.x = c->d_a;
+    po.ldx = kWidth;
+    po.res = in;
+    po.ldres = kWidth;
+    po.y = c->d_h;
+    po.ldy = kWidth;
+    CUDA_TRY((launch_gemv<1, false, EPI_RESID>(q8, po, s)));
+    // 4. g = GELU(LN2(h) Wup^T)
+    GemvParams pu{};
+    pu.B = b.R;
+    pu.status = c->d_status;
+    pu.w = L.up.plane;
+    pu.scales = L.up.scales;
+    pu.rows = kFfn;
+    pu.cols = 512;
+    pu.x = c->d_h;
+    pu.ldx = kWidth;
+    pu.ln_w = L.norms + 2 * kWidth;
+    pu.ln_b = L.norms + 3 * kWidth;
+    pu.y = c->d_g;
+    pu.ldy = kFfn;
+    CUDA_TRY((launch_gemv<1, true, EPI_GELU>(q8, pu, s)));
+    // 5. out = h + g Wdown^T
+    GemvParams pd{};
+    pd.B = b.R;
+    pd.status = c->d_status;
+    pd.w = L.down.plane;
+    pd.scales = L.down.scales;
+    pd.rows = 512;
+    pd.cols = kFfn;
+    pd.x = c->d_g;
+    pd.ldx = kFfn;
+    pd.res = c->d_h;
+    pd.ldres = kWidth;
+    pd.y = out;
+    pd.ldy = kWidth;
+    CUDA_TRY((launch_gemv<4, false, EPI_RESID>(q8, pd, s)));
+    return PHONON_CUDA_OK;
+}
+
+// Run layers [0, L) over the batch, reading `in` and leaving the result in
+// `final_out`. cancel (optional) is polled before each layer and once after;
+// `polls_per_layer` extra polls emulate the reference's in-layer schedule.
+int enqueue_stack(PhononCuda* c, const Batch& b, const float* in, float* final_out,
+                  PhononCudaCancelPoll cancel, void* cctx, const std::vector<int>* polls_per_layer,
+                  bool* cancelled) {
+    const int L = static_cast<int>(c->cfg.n_layers);
+    const float* cur = in;
+    for (int l = 0; l < L; ++l) {
+        if (cancel) {
+            const int polls = polls_per_layer ? (*polls_per_layer)[l] : 1;
+            for (int k = 0; k < polls; ++k)
+                if (cancel(cctx)) {
+                    *cancelled = true;
+                    return PHONON_CUDA_CANCELLED;
+                }
+        }
+        float* out = (l == L - 1) ? final_out : ((cur == c->d_x0) ? c->d_x1 : c->d_x0);
+        const int st = enqueue_layer(c, b, l, cur, out);
+        if (st != PHONON_CUDA_OK) return st;
+        cur = out;
+    }
+    if (cancel && cancel(cctx)) {
+        *cancelled = true;
+        return PHONON_CUDA_CANCELLED;
+    }
+    return PHONON_CUDA_OK;
+}
+
+int set_device(int device) {
+    CUDA_TRY(cudaSetDevice(device));
+    return PHONON_CUDA_OK;
+}
+
+void destroy_context(PhononCuda* c) {
+    if (!c) return;
+    cudaSetDevice(c->cfg.device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto& L : c->layers) free_layer(L);
+    void* dev[] = {c->kv_pool, c->d_table, c->d_freq, c->d_x0, c->d_x1, c->d_y, c->d_q, c->d_a,
+                   c->d_h, c->d_g, c->d_part, c->d_stage, c->d_meta, c->d_status};
+    for (void* p : dev)
+        if (p) cudaFree(p);
+    void* host[] = {c->h_meta, c->h_x, c->h_y, c->h_stage, c->h_status};
+    for (void* p : host)
+        if (p) cudaFreeHost(p);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+// RoPE inverse frequencies exactly as the reference builds them in fp32:
+// freq_i = 1 / powf(theta, (float)(2i) / (float)head_width)
+// (src/phonon_transformer.c:229-232).
+void rope_frequencies(float theta, size_t head_width, float* freq) {
+    for (size_t i = 0; i < head_width / 2; ++i) {
+        const float exponent = static_cast<float>(2 * i) / static_cast<float>(head_width);
+        freq[i] = 1.0f / powf(theta, exponent);
+    }
+}
+
+// Poll schedule of the reference prefill for one layer: layer start, after
+// LN1, one per (head, query block, 512-key block), after LN2
+// (src/phonon_transformer.c:497-509, :644-680).
+int prefill_polls_per_layer(size_t length) {
+    const size_t qb = length >= 768 ? 256 : (length >= 192 ? 64 : 32);
+    size_t attn = 0;
+    for (size_t start = 0; start < length; start += qb) {
+        const size_t rows = std::min(qb, length - start);
+        attn += (start + rows + 511) / 512;
+    }
+    return static_cast<int>(3 + 8 * attn);
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" {
+
+const char* phonon_cuda_status_string(int status) {
+    switch (status) {
+        case PHONON_CUDA_OK: return "ok";
+        case PHONON_CUDA_INVALID_ARGUMENT: return "invalid argument";
+        case PHONON_CUDA_NON_FINITE: return "non-finite value";
+        case PHONON_CUDA_OUT_OF_MEMORY: return "out of memory";
+        case PHONON_CUDA_POOL_EXHAUSTED: return "KV page pool exhausted";
+        case PHONON_CUDA_CAPACITY: return "stream capacity exceeded";
+        case PHONON_CUDA_BAD_POSITION: return "position is not the stream length";
+        case PHONON_CUDA_CANCELLED: return "cancelled";
+        case PHONON_CUDA_DEVICE_ERROR: return "CUDA error";
+        default: return "unknown status";
+    }
+}
+
+int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* layers, PhononCuda** out) {
+    if (!config || !layers || !out) return PHONON_CUDA_INVALID_ARGUMENT;
+    *out = nullptr;
+    const PhononCudaConfig& cfg = *config;
+    if (cfg.n_layers < 1 || cfg.n_layers > kMaxLayers || cfg.max_streams < 1 || cfg.max_batch < 1 ||
+        cfg.max_batch > 65536 || cfg.pool_pages < 1 || cfg.kv_type > PHONON_CUDA_KV_BF16 ||
+        !(cfg.theta > 0.0f) || !std::isfinite(cfg.theta))
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(cfg.device);
+    if (st) return st;
+    PhononCuda* c = new (std::nothrow) PhononCuda();
+    if (!c) return PHONON_CUDA_OUT_OF_MEMORY;
+    c->cfg = cfg;
+    auto fail = [&](int code) {
+        destroy_context(c);
+        return code;
+    };
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(PHONON_CUDA_DEVICE_ERROR);
+    c->layers.resize(cfg.n_layers);
+    for (uint32_t l = 0; l < cfg.n_layers; ++l)
+        if ((st = load_layer(&c->layers[l], layers[l]))) return fail(st);
+    float freq[32];
+    rope_frequencies(cfg.theta, kHeadDim, freq);
+    const size_t esize = cfg.kv_type == PHONON_CUDA_KV_BF16 ? 2 : 4;
+    c->page_elems = static_cast<long long>(cfg.n_layers) * 2 * kHeads * kPage * kHeadDim;
+    c->cap_rows = static_cast<int>(std::max<uint32_t>(cfg.max_batch, kPrefillChunk));
+    c->max_splits = kSplitTarget + c->cap_rows + 16;
+    const int U_max = c->cap_rows * 2 + kMaxPagesPerStream + 16;
+    c->meta_ints = 4 * c->cap_rows + 4 * c->max_splits + 3 * U_max;
+    const size_t rows = static_cast<size_t>(c->cap_rows);
+    bool ok = cudaMalloc(&c->kv_pool, static_cast<size_t>(cfg.pool_pages) * c->page_elems * esize) == cudaSuccess &&
+              cudaMalloc(&c->d_table, static_cast<size_t>(cfg.max_streams) * kMaxPagesPerStream * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_freq, sizeof(freq)) == cudaSuccess &&
+              cudaMalloc(&c->d_x0, rows * kWidth * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_x1, rows * kWidth * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_y, rows * kWidth * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_q, rows * kWidth * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_a, rows * kWidth * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_h, rows * kWidth * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_g, rows * kFfn * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_part, static_cast<size_t>(c->max_splits) * kHeads * kPartStride * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_meta, static_cast<size_t>(c->meta_ints) * 4) == cudaSuccess &&
+              cudaMalloc(&c->d_status, rows * 4) == cudaSuccess &&
+              cudaMallocHost(&c->h_meta, static_cast<size_t>(c->meta_ints) * 4) == cudaSuccess &&
+              cudaMallocHost(&c->h_x, rows * kWidth * 4) == cudaSuccess &&
+              cudaMallocHost(&c->h_y, rows * kWidth * 4) == cudaSuccess &&
+              cudaMallocHost(&c->h_status, rows * 4) == cudaSuccess;
+    if (!ok) return fail(PHONON_CUDA_OUT_OF_MEMORY);
+    if (cudaMemcpy(c->d_freq, freq, sizeof(freq), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(c->d_table, 0, static_cast<size_t>(cfg.max_streams) * kMaxPagesPerStream * 4) != cudaSuccess)
+        return fail(PHONON_CUDA_DEVICE_ERROR);
+    c->free_pages.reserve(cfg.pool_pages);
+    for (int32_t p = static_cast<int32_t>(cfg.pool_pages) - 1; p >= 0; --p) c->free_pages.push_back(p);
+    c->streams.resize(cfg.max_streams);
+    *out = c;
+    return PHONON_CUDA_OK;
+}
+
+void phonon_cuda_destroy(PhononCuda* ctx) { destroy_context(ctx); }
+
+int phonon_cuda_set_theta(PhononCuda* c, float theta) {
+    if (!c || !(theta > 0.0f) || !std::isfinite(theta)) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (theta == c->cfg.theta) return PHONON_CUDA_OK;
+    int st = set_device(c->cfg.device);
+    if (st) return st;
+    float freq[32];
+    rope_frequencies(theta, kHeadDim, freq);
+    CUDA_TRY(cudaMemcpyAsync(c->d_freq, freq, sizeof(freq), cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    c->cfg.theta = theta;
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_set_layer(PhononCuda* c, uint32_t layer, const PhononCudaLayer* weights) {
+    if (!c || !weights) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending || layer >= c->cfg.n_layers) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(c->cfg.device);
+    if (st) return st;
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return PHONON_CUDA_DEVICE_ERROR;
+    return load_layer(&c->layers[layer], *weights);
+}
+
+int phonon_cuda_stream_alloc(PhononCuda* c, uint32_t capacity, uint32_t* stream) {
+    if (!c || !stream || capacity == 0) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (capacity > PHONON_CUDA_MAX_POSITIONS) return PHONON_CUDA_CAPACITY;
+    std::lock_guard<std::mutex> g(c->mu);
+    for (uint32_t s = 0; s < c->streams.size(); ++s)
+        if (!c->streams[s].used) {
+            c->streams[s].used = true;
+            c->streams[s].capacity = capacity;
+            c->streams[s].length = 0;
+            c->streams[s].pages.clear();
+            *stream = s;
+            return PHONON_CUDA_OK;
+        }
+    return PHONON_CUDA_CAPACITY;
+}
+
+int phonon_cuda_stream_reset(PhononCuda* c, uint32_t stream) {
+    if (!c) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (!valid_stream(c, stream)) return PHONON_CUDA_INVALID_ARGUMENT;
+    release_pages(c, stream);
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_stream_free(PhononCuda* c, uint32_t stream) {
+    if (!c) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (!valid_stream(c, stream)) return PHONON_CUDA_INVALID_ARGUMENT;
+    release_pages(c, stream);
+    c->streams[stream].used = false;
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_stream_length(PhononCuda* c, uint32_t stream, uint32_t* length) {
+    if (!c || !length) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (!valid_stream(c, stream)) return PHONON_CUDA_INVALID_ARGUMENT;
+    *length = c->streams[stream].length;
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_stream_pages(PhononCuda* c, uint32_t stream, int32_t* pages, uint32_t max_pages, uint32_t* n_pages) {
+    if (!c || !n_pages) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (!valid_stream(c, stream)) return PHONON_CUDA_INVALID_ARGUMENT;
+    const auto& v = c->streams[stream].pages;
+    *n_pages = static_cast<uint32_t>(v.size());
+    if (pages)
+        for (uint32_t i = 0; i < std::min<uint32_t>(max_pages, *n_pages); ++i) pages[i] = v[i];
+    return PHONON_CUDA_OK;
+}
+
+uint32_t phonon_cuda_free_pages(PhononCuda* c) {
+    if (!c) return 0;
+    std::lock_guard<std::mutex> g(c->mu);
+    return static_cast<uint32_t>(c->free_pages.size());
+}
+
+void* phonon_cuda_cuda_stream(PhononCuda* c) { return c ? c->stream : nullptr; }
+
+}  // extern "C"
+
+namespace {
+
+// Validate a decode batch and allocate the pages it writes. On success the
+// entries are in slot/pos and `undo` holds the new pages.
+int prepare_decode(PhononCuda* c, uint32_t n, const uint32_t* streams, const uint32_t* positions,
+                   std::vector<int32_t>& slot, std::vector<int32_t>& pos, std::vector<int32_t>& updates,
+                   PageUndo& undo, bool require_length) {
+    if (n < 1 || n > c->cfg.max_batch || !streams || !positions) return PHONON_CUDA_INVALID_ARGUMENT;
+    slot.resize(n);
+    pos.resize(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t s = streams[i];
+        if (!valid_stream(c, s)) return PHONON_CUDA_INVALID_ARGUMENT;
+        for (uint32_t j = 0; j < i; ++j)
+            if (streams[j] == s) return PHONON_CUDA_INVALID_ARGUMENT;
+        const StreamSlot& st = c->streams[s];
+        if (positions[i] >= st.capacity || positions[i] >= PHONON_CUDA_MAX_POSITIONS) return PHONON_CUDA_CAPACITY;
+        if (require_length && positions[i] != st.length) return PHONON_CUDA_BAD_POSITION;
+        slot[i] = static_cast<int32_t>(s);
+        pos[i] = static_cast<int32_t>(positions[i]);
+    }
+    for (uint32_t i = 0; i < n; ++i) {
+        const int st = ensure_pages(c, streams[i], positions[i] / kPage + 1, undo, updates);
+        if (st != PHONON_CUDA_OK) {
+            undo.rollback();
+            return st;
+        }
+    }
+    return PHONON_CUDA_OK;
+}
+
+int finish_sync(PhononCuda* c, uint32_t n) {
+    CUDA_TRY(cudaMemcpyAsync(c->h_status, c->d_status, n * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return PHONON_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int phonon_cuda_step(PhononCuda* c, uint32_t n, const uint32_t* streams, const uint32_t* positions,
+                     const float* x, float* y, int32_t* status, PhononCudaCancelPoll cancel, void* cctx) {
+    if (!c || !x || !y || !status) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(c->cfg.device);
+    if (st) return st;
+    std::vector<int32_t> slot, pos, updates;
+    PageUndo undo{c, {}};
+    if ((st = prepare_decode(c, n, streams, positions, slot, pos, updates, undo, true))) return st;
+    Batch b;
+    if ((st = upload_batch(c, slot, pos, updates, &b))) {
+        undo.rollback();
+        return st;
+    }
+    std::memcpy(c->h_x, x, static_cast<size_t>(n) * kWidth * 4);
+    cudaMemcpyAsync(c->d_x0, c->h_x, static_cast<size_t>(n) * kWidth * 4, cudaMemcpyHostToDevice, c->stream);
+    cudaMemsetAsync(c->d_status, 0, n * 4, c->stream);
+    bool cancelled = false;
+    st = enqueue_stack(c, b, c->d_x0, c->d_y, cancel, cctx, nullptr, &cancelled);
+    if (st == PHONON_CUDA_OK)
+        cudaMemcpyAsync(c->h_y, c->d_y, static_cast<size_t>(n) * kWidth * 4, cudaMemcpyDeviceToHost, c->stream);
+    const int sync = finish_sync(c, n);
+    if (cancelled) {
+        for (uint32_t i = 0; i < n; ++i) release_pages(c, streams[i]);
+        return PHONON_CUDA_CANCELLED;
+    }
+    if (st) return st;
+    if (sync) return sync;
+    for (uint32_t i = 0; i < n; ++i) {
+        status[i] = c->h_status[i] ? c->h_status[i] : PHONON_CUDA_OK;
+        if (status[i] == PHONON_CUDA_OK) {
+            c->streams[streams[i]].length++;
+            std::memcpy(y + static_cast<size_t>(i) * kWidth, c->h_y + static_cast<size_t>(i) * kWidth, kWidth * 4);
+        }
+    }
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_step_device(PhononCuda* c, uint32_t n, const uint32_t* streams, const uint32_t* positions,
+                            const float* x_dev, float* y_dev) {
+    if (!c || !x_dev || !y_dev) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(c->cfg.device);
+    if (st) return st;
+    std::vector<int32_t> slot, pos, updates;
+    PageUndo undo{c, {}};
+    if ((st = prepare_decode(c, n, streams, positions, slot, pos, updates, undo, true))) return st;
+    Batch b;
+    if ((st = upload_batch(c, slot, pos, updates, &b))) {
+        undo.rollback();
+        return st;
+    }
+    cudaMemsetAsync(c->d_status, 0, n * 4, c->stream);
+    bool cancelled = false;
+    if ((st = enqueue_stack(c, b, x_dev, y_dev, nullptr, nullptr, nullptr, &cancelled))) return st;
+    c->pending = true;
+    c->pending_streams.assign(streams, streams + n);
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_sync(PhononCuda* c, int32_t* status) {
+    if (!c) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (!c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(c->cfg.device);
+    if (st) return st;
+    const uint32_t n = static_cast<uint32_t>(c->pending_streams.size());
+    c->pending = false;
+    if ((st = finish_sync(c, n))) return st;
+    for (uint32_t i = 0; i < n; ++i) {
+        const int32_t s = c->h_status[i] ? c->h_status[i] : PHONON_CUDA_OK;
+        if (status) status[i] = s;
+        if (s == PHONON_CUDA_OK) c->streams[c->pending_streams[i]].length++;
+    }
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_layer_step(PhononCuda* c, uint32_t stream, uint32_t layer, uint32_t position, const float* x,
+                           float* y) {
+    if (!c || !x || !y) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending || layer >= c->cfg.n_layers) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(c->cfg.device);
+    if (st) return st;
+    std::vector<int32_t> slot, pos, updates;
+    PageUndo undo{c, {}};
+    if ((st = prepare_decode(c, 1, &stream, &position, slot, pos, updates, undo, true))) return st;
+    Batch b;
+    if ((st = upload_batch(c, slot, pos, updates, &b))) {
+        undo.rollback();
+        return st;
+    }
+    std::memcpy(c->h_x, x, kWidth * 4);
+    cudaMemcpyAsync(c->d_x0, c->h_x, kWidth * 4, cudaMemcpyHostToDevice, c->stream);
+    cudaMemsetAsync(c->d_status, 0, 4, c->stream);
+    if ((st = enqueue_layer(c, b, static_cast<int>(layer), c->d_x0, c->d_y))) return st;
+    cudaMemcpyAsync(c->h_y, c->d_y, kWidth * 4, cudaMemcpyDeviceToHost, c->stream);
+    if ((st = finish_sync(c, 1))) return st;
+    if (c->h_status[0]) return c->h_status[0];
+    std::memcpy(y, c->h_y, kWidth * 4);
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_commit(PhononCuda* c, uint32_t stream, uint32_t position) {
+    if (!c) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (!valid_stream(c, stream)) return PHONON_CUDA_INVALID_ARGUMENT;
+    StreamSlot& s = c->streams[stream];
+    if (position != s.length) return PHONON_CUDA_BAD_POSITION;
+    if (position >= s.capacity) return PHONON_CUDA_CAPACITY;
+    s.length++;
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_append(PhononCuda* c, uint32_t stream, const float* rows, uint32_t length, float* last_output,
+                       PhononCudaCancelPoll cancel, void* cctx) {
+    if (!c || !rows || !last_output || length == 0) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending || !valid_stream(c, stream)) return PHONON_CUDA_INVALID_ARGUMENT;
+    StreamSlot& ss = c->streams[stream];
+    if (ss.length != 0) return PHONON_CUDA_BAD_POSITION;
+    if (length > ss.capacity || length > PHONON_CUDA_MAX_POSITIONS) return PHONON_CUDA_CAPACITY;
+    int st = set_device(c->cfg.device);
+    if (st) return st;
+    std::vector<int32_t> updates;
+    PageUndo undo{c, {}};
+    if ((st = ensure_pages(c, stream, (length - 1) / kPage + 1, undo, updates))) {
+        undo.rollback();
+        return st;
+    }
+    // Emulated reference poll schedule: the full per-layer count on the first
+    // pass over the layers, one poll per layer afterwards.
+    std::vector<int> first_polls(c->cfg.n_layers, prefill_polls_per_layer(length));
+    std::vector<int> later_polls(c->cfg.n_layers, 1);
+    const int chunk = c->cap_rows;
+    int result = PHONON_CUDA_OK;
+    bool cancelled = false, bad = false;
+    for (uint32_t p0 = 0; p0 < length && result == PHONON_CUDA_OK; p0 += chunk) {
+        const int R = static_cast<int>(std::min<uint32_t>(chunk, length - p0));
+        std::vector<int32_t> slot(R, static_cast<int32_t>(stream)), pos(R);
+        for (int e = 0; e < R; ++e) pos[e] = static_cast<int32_t>(p0 + e);
+        Batch b;
+        result = upload_batch(c, slot, pos, p0 == 0 ? updates : std::vector<int32_t>{}, &b);
+        if (result != PHONON_CUDA_OK) break;
+        std::memcpy(c->h_x, rows + static_cast<size_t>(p0) * kWidth, static_cast<size_t>(R) * kWidth * 4);
+        cudaMemcpyAsync(c->d_x0, c->h_x, static_cast<size_t>(R) * kWidth * 4, cudaMemcpyHostToDevice, c->stream);
+        cudaMemsetAsync(c->d_status, 0, R * 4, c->stream);
+        result = enqueue_stack(c, b, c->d_x0, c->d_y, cancel, cctx, p0 == 0 ? &first_polls : &later_polls, &cancelled);
+        if (result == PHONON_CUDA_OK && p0 + R == length)
+            cudaMemcpyAsync(c->h_y, c->d_y + static_cast<size_t>(R - 1) * kWidth, kWidth * 4, cudaMemcpyDeviceToHost,
+                            c->stream);
+        const int sync = finish_sync(c, R);
+        if (result == PHONON_CUDA_OK && sync) result = sync;
+        for (int e = 0; e < R && result == PHONON_CUDA_OK; ++e)
+            if (c->h_status[e]) bad = true;
+        if (bad) result = PHONON_CUDA_NON_FINITE;
+    }
+    if (result != PHONON_CUDA_OK) {
+        release_pages(c, stream);
+        return cancelled ? PHONON_CUDA_CANCELLED : result;
+    }
+    ss.length = length;
+    std::memcpy(last_output, c->h_y, kWidth * 4);
+    return PHONON_CUDA_OK;
+}
+
+// Grow the pinned/device staging rows for KV transfers to hold n floats.
+static int reserve_stage(PhononCuda* c, size_t n) {
+    if (n <= c->stage_cap) return PHONON_CUDA_OK;
+    if (c->d_stage) cudaFree(c->d_stage);
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    c->d_stage = nullptr;
+    c->h_stage = nullptr;
+    c->stage_cap = 0;
+    if (cudaMalloc(&c->d_stage, n * 4) != cudaSuccess || cudaMallocHost(&c->h_stage, n * 4) != cudaSuccess)
+        return PHONON_CUDA_OUT_OF_MEMORY;
+    c->stage_cap = n;
+    return PHONON_CUDA_OK;
+}
+
+static int check_kv_range(PhononCuda* c, uint32_t stream, uint32_t layer_begin, uint32_t layer_count,
+                          uint32_t position, uint32_t count) {
+    if (c->pending || !valid_stream(c, stream) || layer_count == 0 || count == 0 ||
+        layer_begin >= c->cfg.n_layers || layer_count > c->cfg.n_layers - layer_begin)
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    if (position >= c->streams[stream].capacity || count > c->streams[stream].capacity - position)
+        return PHONON_CUDA_CAPACITY;
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_kv_write(PhononCuda* c, uint32_t stream, uint32_t layer_begin, uint32_t layer_count,
+                         uint32_t position, uint32_t count, const float* keys, const float* values) {
+    if (!c || !keys || !values) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    int st = check_kv_range(c, stream, layer_begin, layer_count, position, count);
+    if (st) return st;
+    const size_t n = static_cast<size_t>(layer_count) * count * kWidth;
+    for (size_t i = 0; i < n; ++i)
+        if (!std::isfinite(keys[i]) || !std::isfinite(values[i])) return PHONON_CUDA_NON_FINITE;
+    if ((st = set_device(c->cfg.device)) || (st = reserve_stage(c, 2 * n))) return st;
+    std::vector<int32_t> updates;
+    PageUndo undo{c, {}};
+    if ((st = ensure_pages(c, stream, (position + count - 1) / kPage + 1, undo, updates))) {
+        undo.rollback();
+        return st;
+    }
+    if (!updates.empty()) {
+        Batch b;
+        std::vector<int32_t> slot{static_cast<int32_t>(stream)}, pos{static_cast<int32_t>(position)};
+        if ((st = upload_batch(c, slot, pos, updates, &b))) {
+            undo.rollback();
+            return st;
+        }
+    }
+    std::memcpy(c->h_stage, keys, n * 4);
+    std::memcpy(c->h_stage + n, values, n * 4);
+    CUDA_TRY(cudaMemcpyAsync(c->d_stage, c->h_stage, 2 * n * 4, cudaMemcpyHostToDevice, c->stream));
+    kv_rows_kernel<<<static_cast<unsigned>(std::min<size_t>((2 * n + 255) / 256, 4096)), 256, 0, c->stream>>>(
+        kv_view(c), static_cast<int>(stream), static_cast<int>(layer_begin), static_cast<int>(layer_count),
+        static_cast<int>(position), static_cast<int>(count), c->d_stage, 1);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_kv_read(PhononCuda* c, uint32_t stream, uint32_t layer_begin, uint32_t layer_count,
+                        uint32_t position, uint32_t count, float* keys, float* values) {
+    if (!c || !keys || !values) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    int st = check_kv_range(c, stream, layer_begin, layer_count, position, count);
+    if (st) return st;
+    const size_t n = static_cast<size_t>(layer_count) * count * kWidth;
+    const uint32_t allocated = static_cast<uint32_t>(c->streams[stream].pages.size()) * kPage;
+    const uint32_t readable = position >= allocated ? 0 : std::min(count, allocated - position);
+    if (readable < count) {  // never-allocated positions read as zeros
+        for (uint32_t l = 0; l < layer_count; ++l) {
+            std::memset(keys + (static_cast<size_t>(l) * count + readable) * kWidth, 0, (count - readable) * kWidth * 4);
+            std::memset(values + (static_cast<size_t>(l) * count + readable) * kWidth, 0, (count - readable) * kWidth * 4);
+        }
+    }
+    if (readable == 0) return PHONON_CUDA_OK;
+    if ((st = set_device(c->cfg.device)) || (st = reserve_stage(c, 2 * n))) return st;
+    kv_rows_kernel<<<static_cast<unsigned>(std::min<size_t>((2 * n + 255) / 256, 4096)), 256, 0, c->stream>>>(
+        kv_view(c), static_cast<int>(stream), static_cast<int>(layer_begin), static_cast<int>(layer_count),
+        static_cast<int>(position), static_cast<int>(readable), c->d_stage, 0);
+    CUDA_TRY(cudaGetLastError());
+    const size_t nr = static_cast<size_t>(layer_count) * readable * kWidth;
+    CUDA_TRY(cudaMemcpyAsync(c->h_stage, c->d_stage, 2 * nr * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    for (uint32_t l = 0; l < layer_count; ++l) {
+        std::memcpy(keys + static_cast<size_t>(l) * count * kWidth, c->h_stage + static_cast<size_t>(l) * readable * kWidth,
+                    static_cast<size_t>(readable) * kWidth * 4);
+        std::memcpy(values + static_cast<size_t>(l) * count * kWidth,
+                    c->h_stage + nr + static_cast<size_t>(l) * readable * kWidth, static_cast<size_t>(readable) * kWidth * 4);
+    }
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_stream_fill_synthetic(PhononCuda* c, uint32_t stream, uint32_t length, uint64_t seed) {
+    if (!c || length == 0) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending || !valid_stream(c, stream)) return PHONON_CUDA_INVALID_ARGUMENT;
+    StreamSlot& ss = c->streams[stream];
+    if (ss.length != 0) return PHONON_CUDA_BAD_POSITION;
+    if (length > ss.capacity) return PHONON_CUDA_CAPACITY;
+    int st = set_device(c->cfg.device);
+    if (st) return st;
+    std::vector<int32_t> updates;
+    PageUndo undo{c, {}};
+    if ((st = ensure_pages(c, stream, (length - 1) / kPage + 1, undo, updates))) {
+        undo.rollback();
+        return st;
+    }
+    Batch b;
+    std::vector<int32_t> slot{static_cast<int32_t>(stream)}, pos{0};
+    if ((st = upload_batch(c, slot, pos, updates, &b))) {
+        undo.rollback();
+        return st;
+    }
+    kv_fill_kernel<<<296, 256, 0, c->stream>>>(kv_view(c), static_cast<int>(stream), static_cast<int>(c->cfg.n_layers),
+                                               static_cast<int>(length), seed);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    ss.length = length;
+    return PHONON_CUDA_OK;
+}
+
+}  // extern "C"
+
+// ============================================================ linear handles
+struct PhononCudaLinear {
+    int device = 0;
+    DevLinear lin;
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    size_t cap = 0;
+    float *d_x = nullptr, *d_y = nullptr, *d_bias = nullptr;
+    int32_t* d_status = nullptr;
+};
+
+extern "C" {
+
+int phonon_cuda_linear_create(int device, int kind, const void* data, size_t rows, size_t cols,
+                              PhononCudaLinear** out) {
+    if (!out) return PHONON_CUDA_INVALID_ARGUMENT;
+    *out = nullptr;
+    int st = set_device(device);
+    if (st) return st;
+    PhononCudaLinear* l = new (std::nothrow) PhononCudaLinear();
+    if (!l) return PHONON_CUDA_OUT_OF_MEMORY;
+    l->device = device;
+    if ((st = upload_linear(kind, data, rows, cols, &l->lin))) {
+        delete l;
+        return st;
+    }
+    if (cudaStreamCreateWithFlags(&l->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&l->d_bias, rows * 4) != cudaSuccess || cudaMalloc(&l->d_status, 4 * 4096) != cudaSuccess) {
+        phonon_cuda_linear_destroy(l);
+        return PHONON_CUDA_OUT_OF_MEMORY;
+    }
+    *out = l;
+    return PHONON_CUDA_OK;
+}
+
+void phonon_cuda_linear_destroy(PhononCudaLinear* l) {
+    if (!l) return;
+    cudaSetDevice(l->device);
+    if (l->stream) cudaStreamSynchronize(l->stream);
+    free_linear(l->lin);
+    void* dev[] = {l->d_x, l->d_y, l->d_bias, l->d_status};
+    for (void* p : dev)
+        if (p) cudaFree(p);
+    if (l->stream) cudaStreamDestroy(l->stream);
+    delete l;
+}
+
+size_t phonon_cuda_linear_bytes(const PhononCudaLinear* l) { return l ? l->lin.bytes : 0; }
+
+int phonon_cuda_linear_apply(PhononCudaLinear* l, const float* x, size_t batch, const float* bias, float* y) {
+    if (!l || !x || !y || batch == 0 || batch > 4096) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(l->mu);
+    int st = set_device(l->device);
+    if (st) return st;
+    const size_t rows = l->lin.rows, cols = l->lin.cols;
+    if (batch > l->cap) {
+        if (l->d_x) cudaFree(l->d_x);
+        if (l->d_y) cudaFree(l->d_y);
+        l->d_x = l->d_y = nullptr;
+        l->cap = 0;
+        if (cudaMalloc(&l->d_x, batch * cols * 4) != cudaSuccess || cudaMalloc(&l->d_y, batch * rows * 4) != cudaSuccess)
+            return PHONON_CUDA_OUT_OF_MEMORY;
+        l->cap = batch;
+    }
+    CUDA_TRY(cudaMemcpyAsync(l->d_x, x, batch * cols * 4, cudaMemcpyHostToDevice, l->stream));
+    if (bias) CUDA_TRY(cudaMemcpyAsync(l->d_bias, bias, rows * 4, cudaMemcpyHostToDevice, l->stream));
+    CUDA_TRY(cudaMemsetAsync(l->d_status, 0, batch * 4, l->stream));
+    CUDA_TRY(launch_linear(l->lin, l->d_x, static_cast<int>(batch), bias ? l->d_bias : nullptr, l->d_y, l->d_status,
+                           l->stream));
+    std::vector<int32_t> status(batch);
+    CUDA_TRY(cudaMemcpyAsync(y, l->d_y, batch * rows * 4, cudaMemcpyDeviceToHost, l->stream));
+    CUDA_TRY(cudaMemcpyAsync(status.data(), l->d_status, batch * 4, cudaMemcpyDeviceToHost, l->stream));
+    CUDA_TRY(cudaStreamSynchronize(l->stream));
+    for (size_t b = 0; b < batch; ++b)
+        if (status[b]) return PHONON_CUDA_NON_FINITE;
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_linear_apply_device(PhononCudaLinear* l, const float* x_dev, size_t batch, const float* bias_dev,
+                                    float* y_dev, int32_t* status_dev, void* cuda_stream) {
+    if (!l || !x_dev || !y_dev || batch == 0 || batch > 65536) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(l->device);
+    if (st) return st;
+    CUDA_TRY(launch_linear(l->lin, x_dev, static_cast<int>(batch), bias_dev, y_dev, status_dev,
+                           static_cast<cudaStream_t>(cuda_stream)));
+    return PHONON_CUDA_OK;
+}
+
+}  // extern "C"
+
+// ============================================================== primitives
+namespace {
+
+__global__ void layernorm_any_kernel(const float* x, const float* w, const float* b, float* out, int width,
+                                     float eps, int32_t* status) {
+    // Widths other than 512: one thread, double mean and variance like the
+    // reference (src/phonon_transformer.c:158-177), fp32 affine step.
+    if (threadIdx.x != 0) return;
+    double sum = 0.0;
+    for (int i = 0; i < width; ++i) {
+        if (!isfinite(x[i]) || !isfinite(w[i]) || !isfinite(b[i])) {
+            *status = kStatusNonFinite;
+            return;
+        }
+        sum += x[i];
+    }
+    const double mean = sum / static_cast<double>(width);
+    double squares = 0.0;
+    for (int i = 0; i < width; ++i) {
+        const double centered = static_cast<double>(x[i]) - mean;
+        squares = __dadd_rn(squares, __dmul_rn(centered, centered));
+    }
+    const float variance = __double2float_rn(squares / static_cast<double>(width));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
+    for (int i = 0; i < width; ++i) {
+        const float v = __fadd_rn(__fmul_rn(__fmul_rn(__double2float_rn(static_cast<double>(x[i]) - mean), scale), w[i]), b[i]);
+        if (!isfinite(v)) *status = kStatusNonFinite;
+        out[i] = v;
+    }
+}
+
+__global__ void layernorm512_eps_kernel(const float* x, const float* w, const float* b, float* out, float eps,
+                                        int32_t* status) {
+    if (!warp_layernorm512(x, w, b, out, eps) && threadIdx.x == 0) *status = kStatusNonFinite;
+}
+
+// x * scale * w, scale = 1/sqrtf(mean(x^2) + eps) with a double sum of squares
+// (src/phonon_transformer.c:66-85). One thread: the reference order exactly.
+__global__ void rmsnorm_kernel(const float* x, const float* w, float* out, int width, float eps, int32_t* status) {
+    if (threadIdx.x != 0) return;
+    double squares = 0.0;
+    for (int i = 0; i < width; ++i) {
+        if (!isfinite(x[i]) || !isfinite(w[i])) {
+            *status = kStatusNonFinite;
+            return;
+        }
+        squares = __dadd_rn(squares, __dmul_rn(static_cast<double>(x[i]), static_cast<double>(x[i])));
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(squares / static_cast<double>(width)), eps)));
+    if (!isfinite(scale)) {
+        *status = kStatusNonFinite;
+        return;
+    }
+    for (int i = 0; i < width; ++i) {
+        const float v = __fmul_rn(__fmul_rn(x[i], scale), w[i]);
+        if (!isfinite(v)) *status = kStatusNonFinite;
+        out[i] = v;
+    }
+}
+
+// Elements in full groups of four use the polynomial erf; the count % 4 tail
+// uses erf evaluated in double (the reference calls libm erff there).
+__global__ void gelu_kernel(float* v, long long count, int32_t* status) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    const float x = v[i];
+    if (!isfinite(x)) {
+        *status = kStatusNonFinite;
+        return;
+    }
+    float y;
+    if (i < count - count % 4) {
+        y = gelu_erf(x);
+    } else {
+        const float scaled = __fmul_rn(x, 0.7071067811865475244f);
+        const float e = __double2float_rn(erf(static_cast<double>(scaled)));
+        y = __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, e));
+    }
+    if (!isfinite(y)) *status = kStatusNonFinite;
+    v[i] = y;
+}
+
+__global__ void rope_kernel(float* v, int width, int heads, int position, const float* freq, int32_t* status) {
+    const int head_width = width / heads;
+    const int pairs = width / 2;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= pairs) return;
+    const int h = i / (head_width / 2), k = i % (head_width / 2);
+    float a = v[h * head_width + 2 * k], b = v[h * head_width + 2 * k + 1];
+    if (!isfinite(a) || !isfinite(b)) {
+        *status = kStatusNonFinite;
+        return;
+    }
+    rope_pair(a, b, position, freq[k]);
+    if (!isfinite(a) || !isfinite(b)) *status = kStatusNonFinite;
+    v[h * head_width + 2 * k] = a;
+    v[h * head_width + 2 * k + 1] = b;
+}
+
+// Per-device scratch for the primitive calls.
+struct PrimExec {
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    size_t cap = 0;  // floats per buffer
+    float *d_a = nullptr, *d_b = nullptr, *d_c = nullptr, *d_d = nullptr;
+    int32_t* d_status = nullptr;
+};
+
+PrimExec* prim_exec(int device) {
+    static std::mutex table_mu;
+    static std::vector<PrimExec*> table;
+    std::lock_guard<std::mutex> g(table_mu);
+    if (device < 0 || device > 1024) return nullptr;
+    if (table.size() <= static_cast<size_t>(device)) table.resize(device + 1, nullptr);
+    if (!table[device]) table[device] = new PrimExec();
+    return table[device];
+}
+
+int prim_reserve(PrimExec* e, size_t n) {
+    if (!e->stream && cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return PHONON_CUDA_DEVICE_ERROR;
+    if (!e->d_status && cudaMalloc(&e->d_status, 4) != cudaSuccess) return PHONON_CUDA_OUT_OF_MEMORY;
+    if (n <= e->cap) return PHONON_CUDA_OK;
+    float** bufs[] = {&e->d_a, &e->d_b, &e->d_c, &e->d_d};
+    for (float** b : bufs) {
+        if (*b) cudaFree(*b);
+        *b = nullptr;
+    }
+    e->cap = 0;
+    for (float** b : bufs)
+        if (cudaMalloc(b, n * 4) != cudaSuccess) return PHONON_CUDA_OUT_OF_MEMORY;
+    e->cap = n;
+    return PHONON_CUDA_OK;
+}
+
+int prim_finish(PrimExec* e) {
+    int32_t status = 0;
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaMemcpyAsync(&status, e->d_status, 4, cudaMemcpyDeviceToHost, e->stream));
+    CUDA_TRY(cudaStreamSynchronize(e->stream));
+    return status ? PHONON_CUDA_NON_FINITE : PHONON_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int phonon_cuda_layer_norm(int device, const float* x, const float* w, const float* b, size_t width, float eps,
+                           float* out) {
+    if (!x || !w || !b || !out || width == 0 || width > (1u << 24) || !(eps > 0.0f) || !std::isfinite(eps))
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(device);
+    if (st) return st;
+    PrimExec* e = prim_exec(device);
+    if (!e) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(e->mu);
+    if ((st = prim_reserve(e, width))) return st;
+    CUDA_TRY(cudaMemcpyAsync(e->d_a, x, width * 4, cudaMemcpyHostToDevice, e->stream));
+    CUDA_TRY(cudaMemcpyAsync(e->d_b, w, width * 4, cudaMemcpyHostToDevice, e->stream));
+    CUDA_TRY(cudaMemcpyAsync(e->d_c, b, width * 4, cudaMemcpyHostToDevice, e->stream));
+    CUDA_TRY(cudaMemsetAsync(e->d_status, 0, 4, e->stream));
+    if (width == 512)
+        layernorm512_eps_kernel<<<1, 32, 0, e->stream>>>(e->d_a, e->d_b, e->d_c, e->d_d, eps, e->d_status);
+    else
+        layernorm_any_kernel<<<1, 32, 0, e->stream>>>(e->d_a, e->d_b, e->d_c, e->d_d, static_cast<int>(width), eps,
+                                                      e->d_status);
+    if ((st = prim_finish(e))) return st;
+    CUDA_TRY(cudaMemcpy(out, e->d_d, width * 4, cudaMemcpyDeviceToHost));
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_rms_norm(int device, const float* x, const float* w, size_t width, float eps, float* out) {
+    if (!x || !w || !out || width == 0 || width > (1u << 24) || !(eps > 0.0f) || !std::isfinite(eps))
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(device);
+    if (st) return st;
+    PrimExec* e = prim_exec(device);
+    if (!e) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(e->mu);
+    if ((st = prim_reserve(e, width))) return st;
+    CUDA_TRY(cudaMemcpyAsync(e->d_a, x, width * 4, cudaMemcpyHostToDevice, e->stream));
+    CUDA_TRY(cudaMemcpyAsync(e->d_b, w, width * 4, cudaMemcpyHostToDevice, e->stream));
+    CUDA_TRY(cudaMemsetAsync(e->d_status, 0, 4, e->stream));
+    rmsnorm_kernel<<<1, 32, 0, e->stream>>>(e->d_a, e->d_b, e->d_d, static_cast<int>(width), eps, e->d_status);
+    if ((st = prim_finish(e))) return st;
+    CUDA_TRY(cudaMemcpy(out, e->d_d, width * 4, cudaMemcpyDeviceToHost));
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_erf_gelu(int device, float* values, size_t count) {
+    if (count == 0) return PHONON_CUDA_OK;
+    if (!values || count > (1u << 28)) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(device);
+    if (st) return st;
+    PrimExec* e = prim_exec(device);
+    if (!e) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(e->mu);
+    if ((st = prim_reserve(e, count))) return st;
+    CUDA_TRY(cudaMemcpyAsync(e->d_a, values, count * 4, cudaMemcpyHostToDevice, e->stream));
+    CUDA_TRY(cudaMemsetAsync(e->d_status, 0, 4, e->stream));
+    gelu_kernel<<<static_cast<unsigned>((count + 255) / 256), 256, 0, e->stream>>>(e->d_a, static_cast<long long>(count),
+                                                                                   e->d_status);
+    if ((st = prim_finish(e))) return st;
+    CUDA_TRY(cudaMemcpy(values, e->d_a, count * 4, cudaMemcpyDeviceToHost));
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_rope_interleaved(int device, float* values, size_t width, size_t heads, size_t position, float theta) {
+    if (!values || !width || !heads || width % heads || (width / heads) % 2 || !(theta > 0.0f) ||
+        !std::isfinite(theta) || width > (1u << 24) || position > (1u << 30))
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(device);
+    if (st) return st;
+    PrimExec* e = prim_exec(device);
+    if (!e) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(e->mu);
+    if ((st = prim_reserve(e, width))) return st;
+    std::vector<float> freq(width / heads / 2);
+    rope_frequencies(theta, width / heads, freq.data());
+    CUDA_TRY(cudaMemcpyAsync(e->d_a, values, width * 4, cudaMemcpyHostToDevice, e->stream));
+    CUDA_TRY(cudaMemcpyAsync(e->d_b, freq.data(), freq.size() * 4, cudaMemcpyHostToDevice, e->stream));
+    CUDA_TRY(cudaMemsetAsync(e->d_status, 0, 4, e->stream));
+    rope_kernel<<<static_cast<unsigned>((width / 2 + 255) / 256), 256, 0, e->stream>>>(
+        e->d_a, static_cast<int>(width), static_cast<int>(heads), static_cast<int>(position), e->d_b, e->d_status);
+    if ((st = prim_finish(e))) return st;
+    CUDA_TRY(cudaMemcpy(values, e->d_a, width * 4, cudaMemcpyDeviceToHost));
+    return PHONON_CUDA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,686 @@
+// Device code of libphonon_cuda (sm_100a).
+//
+// Kernels of one Flow layer step, in launch order:
+//   gemv_kernel<LN, EPI_QKV>   LN1 -> [q|k|v] = xn Wqkv^T -> RoPE(q,k) -> q to scratch,
+//                              k/v appended to the stream's KV page
+//   attn_partial_kernel        split-K flash-decode over 16-position pages
+//   attn_combine_kernel        merge the splits of each (stream, head)
+//   gemv_kernel<-, EPI_RESID>  h = x + attn Wout^T
+//   gemv_kernel<LN, EPI_GELU>  g = GELU(LN2(h) Wup^T)
+//   gemv_kernel<-, EPI_RESID>  x' = h + g Wdown^T
+//
+// Numerics follow speech-mac src/phonon_transformer.c. LayerNorm reproduces
+// the reference's Welford cascade bit for bit; RoPE uses the reference's fp32
+// frequencies and phases; GELU uses the same A&S erf polynomial. Linear and
+// attention reductions run in a GPU order (fp32 accumulate).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace phonon {
+
+constexpr int kWidth = 512;
+constexpr int kHeads = 8;
+constexpr int kHeadDim = 64;
+constexpr int kFfn = 2048;
+constexpr int kPage = 16;
+constexpr int kGemvWarps = 8;      // warps per GEMV CTA
+constexpr int kRowsPerWarp = 2;    // a RoPE pair (2i, 2i+1) stays in one warp
+constexpr int kAttnWarps = 4;      // warps per attention CTA
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kStatusNonFinite = 2;  // PHONON_CUDA_NON_FINITE
+
+enum Epilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_GELU = 2, EPI_QKV = 3 };
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) {
+    return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return static_cast<uint16_t>(u >> 16);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+    return v;
+}
+
+__device__ __forceinline__ void flag_nonfinite(int32_t* status, int b) {
+    if (status) atomicOr(status + b, kStatusNonFinite);
+}
+
+// ------------------------------------------------------------------ LayerNorm
+// Merge `add` samples (a_mean, a_m2) into (mean, m2) holding n samples, in the
+// reference's unfused order: mean += c*delta; m2 += a_m2 + delta*delta*c*n
+// (src/phonon_transformer.c:90-98).
+__device__ __forceinline__ void ln_merge(float n, float add, float a_mean, float a_m2, float& mean,
+                                         float& m2) {
+    float total = __fadd_rn(n, add);
+    float c = total != 0.0f ? __fdiv_rn(add, total) : 0.0f;
+    float delta = __fsub_rn(a_mean, mean);
+    mean = __fadd_rn(mean, __fmul_rn(c, delta));
+    m2 = __fadd_rn(m2, __fadd_rn(a_m2, __fmul_rn(__fmul_rn(__fmul_rn(delta, delta), c), n)));
+}
+
+// One warp normalises one 512-wide row: out = ((x - mean) * rstd) * w + b with
+// the moments of the reference's moments_512 (src/phonon_transformer.c:99-151)
+// and its affine step (:178-183). Lane (chunk*4 + l) runs the 16-step Welford
+// of elements chunk*64 + j*4 + l; every lane then replays the chunk cascade
+// and the four-lane merge identically. Returns false (on every lane) if an
+// input, weight, bias or output is non-finite.
+__device__ __forceinline__ bool warp_layernorm512(const float* __restrict__ x,
+                                                  const float* __restrict__ w,
+                                                  const float* __restrict__ b,
+                                                  float* __restrict__ out,
+                                                  float eps = 1e-5f) {
+    const int lane = threadIdx.x & 31;
+    const int chunk = lane >> 2, sub = lane & 3;
+    bool ok = true;
+    float mean = 0.0f, m2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        float v = x[chunk * 64 + j * 4 + sub];
+        ok &= isfinite(v);
+        float delta = __fsub_rn(v, mean);
+        mean = __fadd_rn(mean, __fmul_rn(delta, __fdiv_rn(1.0f, static_cast<float>(j + 1))));
+        m2 = __fadd_rn(m2, __fmul_rn(delta, __fsub_rn(v, mean)));
+    }
+    float s1[3][4], s2[3][4], cnt[3] = {0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int l = 0; l < 3; ++l)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) s1[l][k] = s2[l][k] = 0.0f;
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float fm = __shfl_sync(kFull, mean, ch * 4 + k);
+            float fq = __shfl_sync(kFull, m2, ch * 4 + k);
+            ln_merge(cnt[0], 16.0f, fm, fq, s1[0][k], s2[0][k]);
+        }
+        cnt[0] += 16.0f;
+        int carry = ch + 1;
+#pragma unroll
+        for (int level = 1; level < 3; ++level) {
+            if ((carry & 1) != 0) break;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                ln_merge(cnt[level], cnt[level - 1], s1[level - 1][k], s2[level - 1][k],
+                         s1[level][k], s2[level][k]);
+                s1[level - 1][k] = s2[level - 1][k] = 0.0f;
+            }
+            cnt[level] += cnt[level - 1];
+            cnt[level - 1] = 0.0f;
+            carry >>= 1;
+        }
+    }
+#pragma unroll
+    for (int level = 1; level < 3; ++level) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ln_merge(cnt[0], cnt[level], s1[level][k], s2[level][k], s1[0][k], s2[0][k]);
+        cnt[0] += cnt[level];
+    }
+    float mu = 0.0f, q = 0.0f, n = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float total = n + 128.0f;
+        float c = __fdiv_rn(128.0f, total);
+        float delta = __fsub_rn(s1[0][k], mu);
+        mu = __fmaf_rn(c, delta, mu);
+        q = __fadd_rn(q, __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), c), n, s2[0][k]));
+        n = total;
+    }
+    const float var = __fdiv_rn(q, 512.0f);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    const double dmu = static_cast<double>(mu);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const int i = lane + 32 * k;
+        const float wi = w[i], bi = b[i];
+        ok &= isfinite(wi) && isfinite(bi);
+        float centered = __double2float_rn(__dsub_rn(static_cast<double>(x[i]), dmu));
+        float y = __fadd_rn(__fmul_rn(__fmul_rn(centered, scale), wi), bi);
+        ok &= isfinite(y);
+        out[i] = y;
+    }
+    return __all_sync(kFull, ok);
+}
+
+// ----------------------------------------------------------------------- GELU
+// 0.5*x*(1+erf(x/sqrt2)) with the A&S 7.1.26 erf in the reference's fused
+// order (src/phonon_transformer.c:190-200, :209-211). exp(-x^2) is evaluated
+// in double and rounded once, which is the correctly rounded fp32 exp.
+__device__ __forceinline__ float gelu_erf(float v) {
+    const float x = __fmul_rn(v, 0.7071067811865475244f);
+    const float t = __fdiv_rn(1.0f, __fmaf_rn(0.3275911f, fabsf(x), 1.0f));
+    float r = __fmaf_rn(1.061405429f, t, -1.453152027f);
+    r = __fmaf_rn(r, t, 1.421413741f);
+    r = __fmaf_rn(r, t, -0.284496736f);
+    r = __fmaf_rn(r, t, 0.254829592f);
+    const float sq = __fmul_rn(x, x);
+    const float neg_exp = -__double2float_rn(exp(-static_cast<double>(sq)));
+    const float e = copysignf(__fmaf_rn(__fmul_rn(t, neg_exp), r, 1.0f), x);
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, e));
+}
+
+// ---------------------------------------------------------------------- RoPE
+// Rotate pair (a, b) = (x[2i], x[2i+1]) by position * freq[i]; phases in
+// fp32 like the reference (src/phonon_transformer.c:229-244), cos/sin
+// evaluated in double and rounded once.
+__device__ __forceinline__ void rope_pair(float& a, float& b, int position, float freq) {
+    const float phase = __fmul_rn(static_cast<float>(position), freq);
+    double sd, cd;
+    sincos(static_cast<double>(phase), &sd, &cd);
+    const float c = __double2float_rn(cd), s = __double2float_rn(sd);
+    const float ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    const float rb = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    a = ra;
+    b = rb;
+}
+
+// ----------------------------------------------------------------- KV pages
+// A page stores 16 positions of every layer as [layer][k|v][head][slot][dim].
+struct KvView {
+    void* pool;
+    long long page_elems;   // elements per page: n_layers * 2 * 8 * 16 * 64
+    int bf16;               // 1: bf16 elements, 0: fp32
+    const int32_t* table;   // [stream slot][max_pages]
+    int max_pages;
+};
+
+__device__ __forceinline__ long long kv_offset(const KvView& kv, int page, int layer, int which,
+                                               int head, int slot) {
+    return static_cast<long long>(page) * kv.page_elems +
+           ((static_cast<long long>(layer * 2 + which) * kHeads + head) * kPage + slot) * kHeadDim;
+}
+
+__device__ __forceinline__ void kv_store2(const KvView& kv, long long off, float a, float b) {
+    if (kv.bf16) {
+        uint32_t packed = static_cast<uint32_t>(f32_to_bf16(a)) |
+                          (static_cast<uint32_t>(f32_to_bf16(b)) << 16);
+        *reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(kv.pool) + off) = packed;
+    } else {
+        *reinterpret_cast<float2*>(static_cast<float*>(kv.pool) + off) = make_float2(a, b);
+    }
+}
+
+// --------------------------------------------------------------------- GEMV
+// Device weight layout ("lane-interleaved", cols a multiple of 512): in row r,
+// the 16 bytes at r*cols + c*512 + lane*16 hold the int8 weights of logical
+// columns c*512 + j*128 + lane*4 + e (byte j*4 + e), so one 16-byte load per
+// lane feeds four float4 reads of x from shared memory without bank
+// conflicts. Q8_0 scales: r*(cols/32) + c*16 + g*4 + j holds the binary16
+// scale of block c*16 + j*4 + g, so lane l reads its four scales
+// (g = l/8) as one 8-byte load. bf16 weights use the same column order.
+struct GemvParams {
+    const void* w;            // int8 plane (Q8_0) or bf16 plane
+    const __half* scales;     // Q8_0 only
+    int rows, cols;
+    const float* x;           // [B][ldx]
+    int ldx, B;
+    const float* ln_w;        // LN prologue (fp32 [512]) when kLN
+    const float* ln_b;
+    const float* bias;        // EPI_STORE, optional
+    float* y;                 // output [B][ldy]
+    int ldy;
+    const float* res;         // EPI_RESID residual [B][ldres]
+    int ldres;
+    // EPI_QKV
+    float* q;                 // [B][512]
+    const int32_t* slot;      // [B] stream slot
+    const int32_t* pos;       // [B] position
+    const float* freq;        // [32] RoPE frequencies
+    KvView kv;
+    int layer;
+    int32_t* status;          // [B]
+};
+
+template <bool kQ8, int kChunks, int kBT, bool kLN, int kEpi>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
+    extern __shared__ __align__(16) float xs[];  // [kBT][kChunks * 512]
+    __shared__ int ln_bad[kBT];
+    constexpr int cols = kChunks * 512;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = (blockIdx.x * kGemvWarps + warp) * kRowsPerWarp;
+    const bool active = row0 < p.rows;
+
+    // Weights for this warp's two rows live in registers for the whole call.
+    uint4 wq[kRowsPerWarp][kChunks][kQ8 ? 1 : 2];
+    float sc[kRowsPerWarp][kChunks][4];
+    if (active) {
+#pragma unroll
+        for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+            const int r = min(row0 + rr, p.rows - 1);
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) {
+                if constexpr (kQ8) {
+                    const uint8_t* base = static_cast<const uint8_t*>(p.w) +
+                                          static_cast<size_t>(r) * cols + c * 512 + lane * 16;
+                    wq[rr][c][0] = __ldg(reinterpret_cast<const uint4*>(base));
+                    const __half* sb = p.scales + static_cast<size_t>(r) * (cols / 32) + c * 16 +
+                                       (lane >> 3) * 4;
+                    uint2 raw = __ldg(reinterpret_cast<const uint2*>(sb));
+                    __half2 h01 = *reinterpret_cast<__half2*>(&raw.x);
+                    __half2 h23 = *reinterpret_cast<__half2*>(&raw.y);
+                    sc[rr][c][0] = __low2float(h01);
+                    sc[rr][c][1] = __high2float(h01);
+                    sc[rr][c][2] = __low2float(h23);
+                    sc[rr][c][3] = __high2float(h23);
+                } else {
+                    const uint16_t* base = static_cast<const uint16_t*>(p.w) +
+                                           static_cast<size_t>(r) * cols + c * 512 + lane * 16;
+                    wq[rr][c][0] = __ldg(reinterpret_cast<const uint4*>(base));
+                    wq[rr][c][1] = __ldg(reinterpret_cast<const uint4*>(base + 8));
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) sc[rr][c][j] = 1.0f;
+                }
+            }
+        }
+    }
+
+    for (int b0 = 0; b0 < p.B; b0 += kBT) {
+        const int nb = min(kBT, p.B - b0);
+        __syncthreads();
+        if constexpr (kLN) {
+            for (int r = warp; r < nb; r += kGemvWarps) {
+                bool ok = warp_layernorm512(p.x + static_cast<size_t>(b0 + r) * p.ldx, p.ln_w,
+                                            p.ln_b, xs + r * cols);
+                if (lane == 0) ln_bad[r] = ok ? 0 : 1;
+            }
+        } else {
+            const int n4 = nb * cols / 4;
+            for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+                const int e = i * 4, r = e / cols, cc = e % cols;
+                *reinterpret_cast<float4*>(xs + e) =
+                    *reinterpret_cast<const float4*>(p.x + static_cast<size_t>(b0 + r) * p.ldx + cc);
+            }
+        }
+        __syncthreads();
+        if constexpr (kLN) {
+            if (blockIdx.x == 0 && threadIdx.x < nb && ln_bad[threadIdx.x])
+                flag_nonfinite(p.status, b0 + threadIdx.x);
+        }
+        if (!active) continue;
+
+        float acc[kRowsPerWarp][kBT];
+#pragma unroll
+        for (int rr = 0; rr < kRowsPerWarp; ++rr)
+#pragma unroll
+            for (int bb = 0; bb < kBT; ++bb) acc[rr][bb] = 0.0f;
+
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+            float wf[kRowsPerWarp][16];
+#pragma unroll
+            for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+                if constexpr (kQ8) {
+                    const uint32_t words[4] = {wq[rr][c][0].x, wq[rr][c][0].y, wq[rr][c][0].z,
+                                               wq[rr][c][0].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            wf[rr][j * 4 + e] = static_cast<float>(
+                                static_cast<int8_t>((words[j] >> (8 * e)) & 0xffu));
+                } else {
+                    const uint32_t words[8] = {wq[rr][c][0].x, wq[rr][c][0].y, wq[rr][c][0].z,
+                                               wq[rr][c][0].w, wq[rr][c][1].x, wq[rr][c][1].y,
+                                               wq[rr][c][1].z, wq[rr][c][1].w};
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        wf[rr][2 * k] = __uint_as_float(words[k] << 16);
+                        wf[rr][2 * k + 1] = __uint_as_float(words[k] & 0xffff0000u);
+                    }
+                }
+            }
+#pragma unroll
+            for (int bb = 0; bb < kBT; ++bb) {
+                if (bb < nb) {
+                    const float* xr = xs + bb * cols + c * 512 + lane * 4;
+                    float4 xv[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) xv[j] = *reinterpret_cast<const float4*>(xr + j * 128);
+#pragma unroll
+                    for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            float part = wf[rr][j * 4 + 0] * xv[j].x;
+                            part = fmaf(wf[rr][j * 4 + 1], xv[j].y, part);
+                            part = fmaf(wf[rr][j * 4 + 2], xv[j].z, part);
+                            part = fmaf(wf[rr][j * 4 + 3], xv[j].w, part);
+                            acc[rr][bb] = fmaf(sc[rr][c][j], part, acc[rr][bb]);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int rr = 0; rr < kRowsPerWarp; ++rr)
+#pragma unroll
+            for (int bb = 0; bb < kBT; ++bb) acc[rr][bb] = warp_sum(acc[rr][bb]);
+
+        // Lane bb finishes stream b0+bb for both rows of the pair.
+#pragma unroll
+        for (int bb = 0; bb < kBT; ++bb) {
+            if (lane != bb || bb >= nb) continue;
+            const int b = b0 + bb;
+            float v0 = acc[0][bb], v1 = acc[1][bb];
+            const int r0 = row0, r1 = row0 + 1;
+            const bool has1 = r1 < p.rows;
+            if constexpr (kEpi == EPI_QKV) {
+                const int region = r0 >> 9;          // 0 = q, 1 = k, 2 = v
+                const int within = r0 & 511;
+                const int pos = p.pos[b];
+                if (region < 2) rope_pair(v0, v1, pos, p.freq[(within & 63) >> 1]);
+                if (!isfinite(v0) || !isfinite(v1)) flag_nonfinite(p.status, b);
+                if (region == 0) {
+                    *reinterpret_cast<float2*>(p.q + static_cast<size_t>(b) * kWidth + within) =
+                        make_float2(v0, v1);
+                } else {
+                    const int page = p.kv.table[static_cast<size_t>(p.slot[b]) * p.kv.max_pages + pos / kPage];
+                    const long long off = kv_offset(p.kv, page, p.layer, region - 1, within >> 6,
+                                                    pos % kPage) + (within & 63);
+                    kv_store2(p.kv, off, v0, v1);
+                }
+            } else {
+                float out[2] = {v0, v1};
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    if (rr == 1 && !has1) break;
+                    const int r = row0 + rr;
+                    float v = out[rr];
+                    if constexpr (kEpi == EPI_RESID) v = __fadd_rn(p.res[static_cast<size_t>(b) * p.ldres + r], v);
+                    if constexpr (kEpi == EPI_GELU) {
+                        if (!isfinite(v)) flag_nonfinite(p.status, b);
+                        v = gelu_erf(v);
+                    }
+                    if constexpr (kEpi == EPI_STORE) {
+                        if (p.bias) v = __fadd_rn(v, p.bias[r]);
+                    }
+                    if (!isfinite(v)) flag_nonfinite(p.status, b);
+                    p.y[static_cast<size_t>(b) * p.ldy + r] = v;
+                }
+            }
+        }
+    }
+}
+
+// Any-shape linear (cols % 32 == 0 for Q8_0, any cols for bf16), natural
+// row-major layout: one warp per (stream, row). Used for shapes outside the
+// four Flow projections (e.g. the reference's small test matrices).
+template <bool kQ8>
+__global__ void linear_generic_kernel(const void* __restrict__ w, const __half* __restrict__ scales,
+                                      int rows, int cols, const float* __restrict__ x, int B,
+                                      const float* __restrict__ bias, float* __restrict__ y,
+                                      int32_t* status) {
+    const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (gw >= static_cast<long long>(rows) * B) return;
+    const int b = static_cast<int>(gw / rows), r = static_cast<int>(gw % rows);
+    const float* xr = x + static_cast<size_t>(b) * cols;
+    float acc = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+        float wv;
+        if constexpr (kQ8) {
+            const int8_t q = static_cast<const int8_t*>(w)[static_cast<size_t>(r) * cols + c];
+            wv = __fmul_rn(__half2float(scales[static_cast<size_t>(r) * (cols / 32) + c / 32]),
+                           static_cast<float>(q));
+        } else {
+            wv = bf16_to_f32(static_cast<const uint16_t*>(w)[static_cast<size_t>(r) * cols + c]);
+        }
+        acc = fmaf(xr[c], wv, acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+        if (bias) acc = __fadd_rn(acc, bias[r]);
+        if (!isfinite(acc)) flag_nonfinite(status, b);
+        y[static_cast<size_t>(b) * rows + r] = acc;
+    }
+}
+
+// ---------------------------------------------------------------- attention
+// Split descriptor: stream index b in the batch, first page, page count and
+// the number of valid keys of that stream (position + 1).
+struct Split {
+    int b, page_begin, page_count, n_keys;
+};
+
+struct AttnParams {
+    const float* q;        // [B][512] RoPE'd queries
+    const int32_t* slot;   // [B]
+    const Split* splits;   // [S]
+    int n_splits;
+    KvView kv;
+    int layer;
+    float* part;           // [S][8][66]: max, sum, acc[64]
+    int32_t* status;
+};
+
+constexpr int kPartStride = 2 + kHeadDim;
+
+// One warp per (split, head). Lane l scores key (l & 15) of the current page
+// over dims (l >> 4)*32 .. +31, so the two halves of a 64-dim dot meet with a
+// single shuffle; for P.V lane l owns output dims 2l, 2l+1. Online softmax:
+// running max m, sum s, accumulator a; exp(-inf) = 0 for masked keys.
+template <bool kBf16>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_partial_kernel(AttnParams p) {
+    const int lane = threadIdx.x & 31;
+    const long long item = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (item >= static_cast<long long>(p.n_splits) * kHeads) return;
+    const int s_idx = static_cast<int>(item >> 3), head = static_cast<int>(item & 7);
+    const Split sp = p.splits[s_idx];
+    const int half = lane >> 4, key_lane = lane & 15;
+    const int slot = p.slot[sp.b];
+    float qh[32];
+    {
+        const float4* qs = reinterpret_cast<const float4*>(p.q + static_cast<size_t>(sp.b) * kWidth +
+                                                           head * kHeadDim + half * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float4 v = qs[i];
+            qh[4 * i] = v.x;
+            qh[4 * i + 1] = v.y;
+            qh[4 * i + 2] = v.z;
+            qh[4 * i + 3] = v.w;
+        }
+    }
+    float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f;
+    bool finite_ok = true;
+    const int32_t* table = p.kv.table + static_cast<size_t>(slot) * p.kv.max_pages;
+    for (int pg = sp.page_begin; pg < sp.page_begin + sp.page_count; ++pg) {
+        const int page = table[pg];
+        const long long kbase = kv_offset(p.kv, page, p.layer, 0, head, 0);
+        const long long vbase = kv_offset(p.kv, page, p.layer, 1, head, 0);
+        const int key = pg * kPage + key_lane;
+        const bool valid = key < sp.n_keys;
+        float dot = 0.0f;
+        if constexpr (kBf16) {
+            const uint4* kr = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.kv.pool) +
+                                                             kbase + key_lane * kHeadDim + half * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint4 v = kr[i];
+                const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    dot = fmaf(qh[8 * i + 2 * k], __uint_as_float(words[k] << 16), dot);
+                    dot = fmaf(qh[8 * i + 2 * k + 1], __uint_as_float(words[k] & 0xffff0000u), dot);
+                }
+            }
+        } else {
+            const float4* kr = reinterpret_cast<const float4*>(static_cast<const float*>(p.kv.pool) +
+                                                               kbase + key_lane * kHeadDim + half * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float4 v = kr[i];
+                dot = fmaf(qh[4 * i], v.x, dot);
+                dot = fmaf(qh[4 * i + 1], v.y, dot);
+                dot = fmaf(qh[4 * i + 2], v.z, dot);
+                dot = fmaf(qh[4 * i + 3], v.w, dot);
+            }
+        }
+        dot += __shfl_xor_sync(kFull, dot, 16);
+        float score = dot * 0.125f;
+        if (valid) finite_ok &= isfinite(score);
+        score = valid ? score : -INFINITY;
+        float pm = score;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, o));
+        const float m_new = fmaxf(m, pm);
+        const float alpha = m == -INFINITY ? 0.0f : expf(m - m_new);
+        const float pr = valid ? expf(score - m_new) : 0.0f;
+        float ps = pr;
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
+        l = fmaf(l, alpha, ps);
+        a0 *= alpha;
+        a1 *= alpha;
+        const int n_valid = min(kPage, sp.n_keys - pg * kPage);
+#pragma unroll
+        for (int j = 0; j < kPage; ++j) {
+            const float pj = __shfl_sync(kFull, pr, j);
+            if (j < n_valid) {
+                float v0, v1;
+                if constexpr (kBf16) {
+                    uint32_t w2 = *reinterpret_cast<const uint32_t*>(
+                        static_cast<const uint16_t*>(p.kv.pool) + vbase + j * kHeadDim + 2 * lane);
+                    v0 = __uint_as_float(w2 << 16);
+                    v1 = __uint_as_float(w2 & 0xffff0000u);
+                } else {
+                    float2 w2 = *reinterpret_cast<const float2*>(static_cast<const float*>(p.kv.pool) +
+                                                                 vbase + j * kHeadDim + 2 * lane);
+                    v0 = w2.x;
+                    v1 = w2.y;
+                }
+                a0 = fmaf(pj, v0, a0);
+                a1 = fmaf(pj, v1, a1);
+            }
+        }
+        m = m_new;
+    }
+    float* out = p.part + (static_cast<size_t>(s_idx) * kHeads + head) * kPartStride;
+    *reinterpret_cast<float2*>(out + 2 + 2 * lane) = make_float2(a0, a1);
+    if (lane == 0) {
+        out[0] = m;
+        out[1] = l;
+    }
+    if (!__all_sync(kFull, finite_ok) && lane == 0) flag_nonfinite(p.status, sp.b);
+}
+
+struct CombineParams {
+    const float* part;        // [S][8][66]
+    const int32_t* first;     // [B] first split of stream b
+    const int32_t* count;     // [B] splits of stream b
+    int B;
+    float* out;               // [B][512]
+    int32_t* status;
+};
+
+// One warp per (stream, head): out = sum_s e^(m_s-M) a_s / sum_s e^(m_s-M) l_s.
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_combine_kernel(CombineParams p) {
+    const int lane = threadIdx.x & 31;
+    const long long item = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (item >= static_cast<long long>(p.B) * kHeads) return;
+    const int b = static_cast<int>(item >> 3), head = static_cast<int>(item & 7);
+    const int first = p.first[b], n = p.count[b];
+    float mx = -INFINITY;
+    for (int s = 0; s < n; ++s) mx = fmaxf(mx, p.part[(static_cast<size_t>(first + s) * kHeads + head) * kPartStride]);
+    float total = 0.0f, a0 = 0.0f, a1 = 0.0f;
+    for (int s = 0; s < n; ++s) {
+        const float* pp = p.part + (static_cast<size_t>(first + s) * kHeads + head) * kPartStride;
+        const float w = pp[0] == -INFINITY ? 0.0f : expf(pp[0] - mx);
+        total = fmaf(w, pp[1], total);
+        float2 av = *reinterpret_cast<const float2*>(pp + 2 + 2 * lane);
+        a0 = fmaf(w, av.x, a0);
+        a1 = fmaf(w, av.y, a1);
+    }
+    bool ok = total > 0.0f && isfinite(total);
+    const float inv = __fdiv_rn(1.0f, total);
+    const float o0 = __fmul_rn(a0, inv), o1 = __fmul_rn(a1, inv);
+    ok &= isfinite(o0) && isfinite(o1);
+    *reinterpret_cast<float2*>(p.out + static_cast<size_t>(b) * kWidth + head * kHeadDim + 2 * lane) =
+        make_float2(o0, o1);
+    if (!__all_sync(kFull, ok) && lane == 0) flag_nonfinite(p.status, b);
+}
+
+// ------------------------------------------------------------- small kernels
+// Apply page-table updates: (slot, index, page) triples.
+__global__ void page_update_kernel(int32_t* table, int max_pages, const int32_t* updates, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) table[static_cast<size_t>(updates[3 * i]) * max_pages + updates[3 * i + 1]] = updates[3 * i + 2];
+}
+
+// Copy K/V rows between a staging buffer and the pages of one stream.
+// Staging layout: keys [layer_count][count][512] then values, fp32.
+// dir 0: pages -> staging, 1: staging -> pages.
+__global__ void kv_rows_kernel(KvView kv, int slot, int layer_begin, int layer_count, int position, int count,
+                               float* stage, int dir) {
+    const long long n = static_cast<long long>(layer_count) * count * kWidth;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < 2 * n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int which = static_cast<int>(i / n);
+        const long long r = i % n;
+        const int l = static_cast<int>(r / (static_cast<long long>(count) * kWidth));
+        const int p = position + static_cast<int>((r / kWidth) % count);
+        const int d = static_cast<int>(r % kWidth);
+        const int page = kv.table[static_cast<size_t>(slot) * kv.max_pages + p / kPage];
+        const long long off = kv_offset(kv, page, layer_begin + l, which, d >> 6, p % kPage) + (d & 63);
+        if (dir == 0) {
+            stage[i] = kv.bf16 ? bf16_to_f32(static_cast<const uint16_t*>(kv.pool)[off])
+                               : static_cast<const float*>(kv.pool)[off];
+        } else {
+            const float v = stage[i];
+            if (kv.bf16) static_cast<uint16_t*>(kv.pool)[off] = f32_to_bf16(v);
+            else static_cast<float*>(kv.pool)[off] = v;
+        }
+    }
+}
+
+// Seeded pseudo-random K/V (roughly N(0,1): sum of four uniforms, centred and
+// scaled) for positions [0, length) of every layer of one stream.
+__device__ __forceinline__ uint32_t hash32(uint64_t x) {
+    x ^= x >> 33;
+    x *= 0xff51afd7ed558ccdull;
+    x ^= x >> 33;
+    x *= 0xc4ceb9fe1a85ec53ull;
+    x ^= x >> 33;
+    return static_cast<uint32_t>(x);
+}
+
+__global__ void kv_fill_kernel(KvView kv, int slot, int n_layers, int length, uint64_t seed) {
+    const long long per_pos = static_cast<long long>(n_layers) * 2 * kWidth;
+    const long long total = per_pos * length;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int position = static_cast<int>(i / per_pos);
+        const long long r = i % per_pos;
+        const int layer = static_cast<int>(r / (2 * kWidth));
+        const int which = static_cast<int>((r / kWidth) & 1);
+        const int d = static_cast<int>(r % kWidth);
+        const uint32_t h = hash32(seed * 0x9E3779B97F4A7C15ull + static_cast<uint64_t>(i));
+        const float u = (static_cast<float>(h & 0xffff) + static_cast<float>(h >> 16)) * (1.0f / 65536.0f);
+        const float v = (u - 1.0f) * 2.449f;  // ~unit variance
+        const int page = kv.table[static_cast<size_t>(slot) * kv.max_pages + position / kPage];
+        const long long off = kv_offset(kv, page, layer, which, d >> 6, position % kPage) + (d & 63);
+        if (kv.bf16) static_cast<uint16_t*>(kv.pool)[off] = f32_to_bf16(v);
+        else static_cast<float*>(kv.pool)[off] = v;
+    }
+}
+
+// ------------------------------------------------ standalone primitive kernels
+__global__ void layernorm_rows_kernel(const float* x, const float* w, const float* b, float* out,
+                                      int rows, int32_t* status) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    if (!warp_layernorm512(x + static_cast<size_t>(row) * kWidth, w, b, out + static_cast<size_t>(row) * kWidth) &&
+        (threadIdx.x & 31) == 0)
+        flag_nonfinite(status, 0);
+}
+
+}  // namespace phonon

@@ -1,0 +1,291 @@
+"""ctypes bindings of libphonon_cuda (include/phonon_cuda.h).
+
+Thin Python mirror of the C ABI for tests and the benchmark. The library is
+loaded from the package directory; a missing library raises instead of
+falling back to anything else.
+"""
+import ctypes as C
+
+import numpy as np
+
+from ._libs import load_cuda
+
+OK, INVALID, NON_FINITE, OOM, POOL_EXHAUSTED, CAPACITY, BAD_POSITION, CANCELLED, DEVICE_ERROR = range(9)
+Q8_0, BF16 = 1, 2
+KV_F32, KV_BF16 = 0, 1
+WIDTH = 512
+PAGE = 16
+
+CANCEL_FN = C.CFUNCTYPE(C.c_int, C.c_void_p)
+
+
+class Config(C.Structure):
+    _fields_ = [("device", C.c_int), ("n_layers", C.c_uint32), ("max_streams", C.c_uint32),
+                ("max_batch", C.c_uint32), ("pool_pages", C.c_uint32), ("kv_type", C.c_uint32),
+                ("theta", C.c_float)]
+
+
+class Layer(C.Structure):
+    _fields_ = [("qkv", C.c_void_p), ("attention_out", C.c_void_p), ("mlp_in", C.c_void_p),
+                ("mlp_out", C.c_void_p), ("norm1_weight", C.c_void_p), ("norm1_bias", C.c_void_p),
+                ("norm2_weight", C.c_void_p), ("norm2_bias", C.c_void_p),
+                ("linear_kind", C.c_uint32)]
+
+
+class CudaError(RuntimeError):
+    def __init__(self, status, what):
+        self.status = status
+        super().__init__(f"{what}: {lib().phonon_cuda_status_string(status).decode()} ({status})")
+
+
+_typed = None
+
+
+def lib():
+    global _typed
+    L = load_cuda()
+    if _typed is L:
+        return L
+    P, U32, I32, SZ, F = C.c_void_p, C.c_uint32, C.c_int32, C.c_size_t, C.c_float
+    sig = {
+        "phonon_cuda_create": [C.POINTER(Config), C.POINTER(Layer), C.POINTER(P)],
+        "phonon_cuda_set_layer": [P, U32, C.POINTER(Layer)],
+        "phonon_cuda_set_theta": [P, F],
+        "phonon_cuda_stream_alloc": [P, U32, C.POINTER(U32)],
+        "phonon_cuda_stream_reset": [P, U32],
+        "phonon_cuda_stream_free": [P, U32],
+        "phonon_cuda_stream_length": [P, U32, C.POINTER(U32)],
+        "phonon_cuda_stream_pages": [P, U32, P, U32, C.POINTER(U32)],
+        "phonon_cuda_step": [P, U32, P, P, P, P, P, CANCEL_FN, P],
+        "phonon_cuda_step_device": [P, U32, P, P, P, P],
+        "phonon_cuda_sync": [P, P],
+        "phonon_cuda_layer_step": [P, U32, U32, U32, P, P],
+        "phonon_cuda_commit": [P, U32, U32],
+        "phonon_cuda_append": [P, U32, P, U32, P, CANCEL_FN, P],
+        "phonon_cuda_kv_read": [P, U32, U32, U32, U32, U32, P, P],
+        "phonon_cuda_kv_write": [P, U32, U32, U32, U32, U32, P, P],
+        "phonon_cuda_stream_fill_synthetic": [P, U32, U32, C.c_uint64],
+        "phonon_cuda_linear_create": [C.c_int, C.c_int, P, SZ, SZ, C.POINTER(P)],
+        "phonon_cuda_linear_apply": [P, P, SZ, P, P],
+        "phonon_cuda_linear_apply_device": [P, P, SZ, P, P, P, P],
+        "phonon_cuda_layer_norm": [C.c_int, P, P, P, SZ, F, P],
+        "phonon_cuda_rms_norm": [C.c_int, P, P, SZ, F, P],
+        "phonon_cuda_erf_gelu": [C.c_int, P, SZ],
+        "phonon_cuda_rope_interleaved": [C.c_int, P, SZ, SZ, SZ, F],
+    }
+    for name, args in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = C.c_int
+    L.phonon_cuda_destroy.argtypes = [P]
+    L.phonon_cuda_destroy.restype = None
+    L.phonon_cuda_linear_destroy.argtypes = [P]
+    L.phonon_cuda_linear_destroy.restype = None
+    L.phonon_cuda_linear_bytes.argtypes = [P]
+    L.phonon_cuda_linear_bytes.restype = SZ
+    L.phonon_cuda_free_pages.argtypes = [P]
+    L.phonon_cuda_free_pages.restype = U32
+    L.phonon_cuda_cuda_stream.argtypes = [P]
+    L.phonon_cuda_cuda_stream.restype = P
+    L.phonon_cuda_status_string.argtypes = [C.c_int]
+    L.phonon_cuda_status_string.restype = C.c_char_p
+    _typed = L
+    return L
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def check(status, what):
+    if status != OK:
+        raise CudaError(status, what)
+
+
+def rel_err(a, ref, floor=1e-2):
+    """max_i |a_i - ref_i| / max(|ref_i|, floor * max_j |ref_j|)."""
+    a = np.asarray(a, np.float64)
+    ref = np.asarray(ref, np.float64)
+    den = np.maximum(np.abs(ref), floor * np.abs(ref).max())
+    return float(np.max(np.abs(a - ref) / den))
+
+
+def layer_struct(w, kind=Q8_0):
+    return Layer(w["qkv"].ctypes.data, w["out"].ctypes.data, w["up"].ctypes.data,
+                 w["down"].ctypes.data, w["norm1_w"].ctypes.data, w["norm1_b"].ctypes.data,
+                 w["norm2_w"].ctypes.data, w["norm2_b"].ctypes.data, kind)
+
+
+class Context:
+    """One libphonon_cuda context (weights + KV page pool) on one device."""
+
+    def __init__(self, weights, device=0, max_streams=64, max_batch=64, pool_pages=1024,
+                 kv_type=KV_F32, theta=10000.0, kind=Q8_0):
+        self.L = lib()
+        self.n_layers = len(weights)
+        layers = (Layer * self.n_layers)(*[layer_struct(w, kind) for w in weights])
+        cfg = Config(device, self.n_layers, max_streams, max_batch, pool_pages, kv_type, theta)
+        h = C.c_void_p()
+        check(self.L.phonon_cuda_create(C.byref(cfg), layers, C.byref(h)), "phonon_cuda_create")
+        self.h = h
+        self.device = device
+        self.kv_type = kv_type
+
+    def close(self):
+        if self.h:
+            self.L.phonon_cuda_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # streams ----------------------------------------------------------------
+    def stream_alloc(self, capacity):
+        s = C.c_uint32()
+        check(self.L.phonon_cuda_stream_alloc(self.h, capacity, C.byref(s)), "stream_alloc")
+        return s.value
+
+    def stream_free(self, s):
+        check(self.L.phonon_cuda_stream_free(self.h, s), "stream_free")
+
+    def stream_reset(self, s):
+        check(self.L.phonon_cuda_stream_reset(self.h, s), "stream_reset")
+
+    def length(self, s):
+        n = C.c_uint32()
+        check(self.L.phonon_cuda_stream_length(self.h, s, C.byref(n)), "stream_length")
+        return n.value
+
+    def pages(self, s):
+        n = C.c_uint32()
+        check(self.L.phonon_cuda_stream_pages(self.h, s, None, 0, C.byref(n)), "stream_pages")
+        out = np.zeros(max(n.value, 1), np.int32)
+        check(self.L.phonon_cuda_stream_pages(self.h, s, _p(out), n.value, C.byref(n)), "stream_pages")
+        return out[:n.value]
+
+    def free_pages(self):
+        return self.L.phonon_cuda_free_pages(self.h)
+
+    def fill_synthetic(self, s, length, seed):
+        check(self.L.phonon_cuda_stream_fill_synthetic(self.h, s, length, seed), "fill_synthetic")
+
+    # compute ----------------------------------------------------------------
+    def step(self, streams, positions, x, cancel=None, raise_on_status=True):
+        n = len(streams)
+        st = np.ascontiguousarray(streams, np.uint32)
+        pos = np.ascontiguousarray(positions, np.uint32)
+        x = np.ascontiguousarray(x, np.float32).reshape(n, WIDTH)
+        y = np.zeros((n, WIDTH), np.float32)
+        status = np.zeros(n, np.int32)
+        cb = CANCEL_FN(cancel) if cancel else CANCEL_FN()
+        rc = self.L.phonon_cuda_step(self.h, n, _p(st), _p(pos), _p(x), _p(y), _p(status), cb, None)
+        check(rc, "phonon_cuda_step")
+        if raise_on_status and status.any():
+            raise CudaError(int(status[status != 0][0]), "phonon_cuda_step stream status")
+        return y if raise_on_status else (y, status)
+
+    def step_device(self, streams, positions, x_ptr, y_ptr):
+        n = len(streams)
+        st = np.ascontiguousarray(streams, np.uint32)
+        pos = np.ascontiguousarray(positions, np.uint32)
+        check(self.L.phonon_cuda_step_device(self.h, n, _p(st), _p(pos), C.c_void_p(x_ptr),
+                                             C.c_void_p(y_ptr)), "phonon_cuda_step_device")
+
+    def sync(self, n):
+        status = np.zeros(n, np.int32)
+        check(self.L.phonon_cuda_sync(self.h, _p(status)), "phonon_cuda_sync")
+        return status
+
+    def cuda_stream(self):
+        return self.L.phonon_cuda_cuda_stream(self.h)
+
+    def layer_step(self, s, layer, position, x):
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros(WIDTH, np.float32)
+        check(self.L.phonon_cuda_layer_step(self.h, s, layer, position, _p(x), _p(y)), "layer_step")
+        return y
+
+    def commit(self, s, position):
+        check(self.L.phonon_cuda_commit(self.h, s, position), "commit")
+
+    def append(self, s, rows, cancel=None):
+        rows = np.ascontiguousarray(rows, np.float32)
+        out = np.zeros(WIDTH, np.float32)
+        cb = CANCEL_FN(cancel) if cancel else CANCEL_FN()
+        check(self.L.phonon_cuda_append(self.h, s, _p(rows), rows.shape[0], _p(out), cb, None), "append")
+        return out
+
+    def kv_read(self, s, position, count=1, layer_begin=0, layer_count=None):
+        lc = self.n_layers - layer_begin if layer_count is None else layer_count
+        k = np.zeros((lc, count, WIDTH), np.float32)
+        v = np.zeros((lc, count, WIDTH), np.float32)
+        check(self.L.phonon_cuda_kv_read(self.h, s, layer_begin, lc, position, count, _p(k), _p(v)),
+              "kv_read")
+        return k, v
+
+    def kv_write(self, s, position, keys, values, layer_begin=0):
+        keys = np.ascontiguousarray(keys, np.float32)
+        values = np.ascontiguousarray(values, np.float32)
+        lc, count = keys.shape[0], keys.shape[1]
+        check(self.L.phonon_cuda_kv_write(self.h, s, layer_begin, lc, position, count, _p(keys),
+                                          _p(values)), "kv_write")
+
+
+class Linear:
+    """A device copy of one Q8_0 / bf16 matrix (phonon_cuda_linear_*)."""
+
+    def __init__(self, data, rows, cols, kind=Q8_0, device=0):
+        self.L = lib()
+        self.data = np.ascontiguousarray(data)
+        h = C.c_void_p()
+        check(self.L.phonon_cuda_linear_create(device, kind, _p(self.data), rows, cols, C.byref(h)),
+              "linear_create")
+        self.h, self.rows, self.cols = h, rows, cols
+
+    def bytes(self):
+        return self.L.phonon_cuda_linear_bytes(self.h)
+
+    def __call__(self, x, bias=None):
+        x = np.ascontiguousarray(x, np.float32)
+        batch = x.size // self.cols
+        y = np.zeros((batch, self.rows), np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        check(self.L.phonon_cuda_linear_apply(self.h, _p(x), batch, _p(b), _p(y)), "linear_apply")
+        return y
+
+    def apply_device(self, x_ptr, batch, y_ptr, stream_ptr=0, bias_ptr=None, status_ptr=None):
+        check(self.L.phonon_cuda_linear_apply_device(self.h, C.c_void_p(x_ptr), batch,
+                                                     C.c_void_p(bias_ptr), C.c_void_p(y_ptr),
+                                                     C.c_void_p(status_ptr), C.c_void_p(stream_ptr)),
+              "linear_apply_device")
+
+    def close(self):
+        if self.h:
+            self.L.phonon_cuda_linear_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def layer_norm(x, w, b, eps=1e-5, device=0):
+    x, w, b = (np.ascontiguousarray(a, np.float32) for a in (x, w, b))
+    out = np.zeros_like(x)
+    rc = lib().phonon_cuda_layer_norm(device, _p(x), _p(w), _p(b), x.size, eps, _p(out))
+    return rc, out
+
+
+def erf_gelu(x, device=0):
+    y = np.array(x, np.float32, copy=True)
+    return lib().phonon_cuda_erf_gelu(device, _p(y), y.size), y
+
+
+def rope(x, heads, position, theta=10000.0, device=0):
+    y = np.array(x, np.float32, copy=True)
+    return lib().phonon_cuda_rope_interleaved(device, _p(y), y.size, heads, position, theta), y
