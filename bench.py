@@ -1,0 +1,556 @@
+"""Benchmark of the B200 Flow-transformer decode step (speech-mac configs).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Headline (one JSON line on rank 0): configs[3] -- 512 concurrent streams,
+12 layers, contexts U[64,2048] (seed 2), Poisson arrivals and departures
+(mean 1 per step, seed 2), bf16 KV in 16-position pages, streams sharded by
+request over N GPUs (no collective on the data path; torch.distributed only
+synchronises the timing). `value` is decode frames/s of the whole job with
+inputs resident in HBM; `e2e` is the same workload through phonon_cuda_step
+with host buffers (H2D of x and D2H of y inside every timed step).
+
+Also reported at N=1: configs[0] (one stream, 128-position prefix + 125
+steps, L2 flushed between steps) and configs[1] (Q8 matvec GB/s of weight
+bytes, cold HBM and hot L2), plus the reference's C path timed on the host
+cores (cpu_baseline).
+
+`--impl reference` times the reference's own CPU path (oracle/_ref, the
+unmodified speech-mac C compiled with the oracle shims) on the same workload
+and prints the same line with "impl": "reference".
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "speech-mac_b200"))
+sys.path.insert(0, str(ROOT))
+
+N_LAYERS = 12
+STREAMS = 512
+METRIC = "decode frames/s (configs[3]: 512 streams, bf16 KV, 12 layers)"
+UNIT = "frames/s"
+L2_BYTES = 126 * 2**20
+HBM_FALLBACK_GBS = 6650.0
+
+
+def measured_hbm_gbs():
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+# ------------------------------------------------------------------ workload
+class ServingSim:
+    """configs[3] arrival process, identical on every rank.
+
+    Start: 512 streams with prefix lengths U[64, 2048]. Each step: D ~
+    Poisson(1) random active streams finish, then A ~ Poisson(1) new streams
+    arrive with prefix U[64, 2048]; every active stream decodes one position.
+    Streams go to the rank holding the fewest KV pages (ties: lowest rank)."""
+
+    def __init__(self, world, seed=2, streams=STREAMS):
+        self.rng = np.random.default_rng(seed)
+        max_active = streams + streams // 2
+        self.world = world
+        self.max_active = max_active
+        self.next_id = 0
+        self.active = {}  # id -> [rank, position]
+        self.pages = [0] * world
+        for _ in range(streams):
+            self._arrive()
+
+    def _arrive(self):
+        prefix = int(self.rng.integers(64, 2049))
+        rank = min(range(self.world), key=lambda r: (self.pages[r], r))
+        sid = self.next_id
+        self.next_id += 1
+        self.active[sid] = [rank, prefix]
+        self.pages[rank] += prefix // 16 + 1
+        return sid
+
+    def churn(self):
+        """Advance one step of arrivals/departures; returns (left, arrived)."""
+        left, arrived = [], []
+        for _ in range(int(self.rng.poisson(1.0))):
+            if len(self.active) <= 1:
+                break
+            ids = sorted(self.active)
+            sid = ids[int(self.rng.integers(0, len(ids)))]
+            rank, pos = self.active.pop(sid)
+            self.pages[rank] -= pos // 16 + 1
+            left.append(sid)
+        for _ in range(int(self.rng.poisson(1.0))):
+            if len(self.active) < self.max_active:
+                arrived.append(self._arrive())
+        return left, arrived
+
+    def advance(self):
+        for v in self.active.values():
+            v[1] += 1
+            if v[1] % 16 == 0:
+                self.pages[v[0]] += 1
+
+
+class RankServer:
+    """This rank's share of the serving simulation on one libphonon_cuda context."""
+
+    def __init__(self, rt, weights, rank, world, device, total_steps, streams):
+        self.rt = rt
+        self.rank = rank
+        self.sim = ServingSim(world, streams=streams)
+        per_rank = (self.sim.max_active + world - 1) // world + 8
+        cap_positions = 2048 + total_steps + 32
+        pool = per_rank * (cap_positions // 16 + 1)
+        self.ctx = rt.Context(weights, device=device, max_streams=per_rank, max_batch=per_rank,
+                              pool_pages=pool, kv_type=rt.KV_BF16)
+        self.capacity = cap_positions
+        self.slot = {}
+        for sid, (r, pos) in self.sim.active.items():
+            if r == rank:
+                self._admit(sid, pos)
+
+    def _admit(self, sid, prefix):
+        s = self.ctx.stream_alloc(self.capacity)
+        self.ctx.fill_synthetic(s, prefix, 1000003 * sid + 17)
+        self.slot[sid] = s
+
+    def churn(self):
+        left, arrived = self.sim.churn()
+        for sid in left:
+            if sid in self.slot:
+                self.ctx.stream_free(self.slot.pop(sid))
+        for sid in arrived:
+            r, pos = self.sim.active[sid]
+            if r == self.rank:
+                self._admit(sid, pos)
+
+    def batch(self):
+        ids = sorted(sid for sid in self.slot)
+        return [self.slot[i] for i in ids], [self.sim.active[i][1] for i in ids]
+
+
+# -------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during a region
+    (a reader thread collects lines while the region runs)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+        self.first = threading.Event()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.lines.append(line)
+                self.first.set()
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            self.first.wait(timeout=10)
+            self.skip = len(self.lines)  # samples taken before the region starts
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.reader.join(timeout=10)
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines[getattr(self, "skip", 0):]:
+            f = [x.strip() for x in line.split(",")]
+            try:
+                sm.append(float(f[0]))
+                mx = max(mx, float(f[1]))
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(names, f[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- GPU arm
+def run_ours(args):
+    import torch
+
+    from phonon_b200 import runtime as rt
+    from phonon_b200 import synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} needs {args.gpus} ranks (torchrun), got {world}")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def reduce(x, op):
+        if not dist:
+            return x
+        t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    weights = synth.flow_weights(N_LAYERS, seed=0)
+    total_steps = 2 * (args.warmup + args.steps) + 8
+    server = RankServer(rt, weights, rank, world, local, total_steps, args.streams)
+    ctx = server.ctx
+    stream = torch.cuda.ExternalStream(ctx.cuda_stream())
+    max_b = server.sim.max_active + 8
+    x_dev = torch.randn(max_b, 512, device="cuda", dtype=torch.float32)
+    y_dev = torch.empty(max_b, 512, device="cuda", dtype=torch.float32)
+
+    def device_step():
+        server.churn()
+        streams, pos = server.batch()
+        ctx.step_device(streams, pos, x_dev.data_ptr(), y_dev.data_ptr())
+        status = ctx.sync(len(streams))
+        if status.any():
+            raise RuntimeError(f"non-finite status in {int((status != 0).sum())} streams")
+        server.sim.advance()
+        return len(streams)
+
+    host_x = synth.Generator(99 + rank).normal(max_b * 512).reshape(max_b, 512)
+    h2d = d2h = 0
+
+    def host_step():
+        nonlocal h2d, d2h
+        server.churn()
+        streams, pos = server.batch()
+        n = len(streams)
+        y = ctx.step(streams, pos, host_x[:n])
+        h2d += n * 512 * 4
+        d2h += y.nbytes + n * 4
+        server.sim.advance()
+        return n
+
+    def timed(fn, steps, profile=False):
+        barrier()
+        if profile:
+            ctx.profile(True)
+        l0 = ctx.launch_count()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        frames = 0
+        with ClockSampler(local) as clocks:
+            start.record(stream)
+            for _ in range(steps):
+                frames += fn()
+            end.record(stream)
+            end.synchronize()
+        barrier()
+        ms = start.elapsed_time(end)
+        prof = ctx.profile_read() if profile else None
+        if profile:
+            ctx.profile(False)
+        return frames, ms, ctx.launch_count() - l0, prof, clocks.summary()
+
+    for _ in range(args.warmup):
+        device_step()
+    frames, ms, launches, prof, clocks = timed(device_step, args.steps, profile=True)
+    tot_frames = reduce(frames, dist.ReduceOp.SUM if dist else None)
+    max_ms = reduce(ms, dist.ReduceOp.MAX if dist else None)
+    for _ in range(args.warmup):
+        host_step()
+    h2d = d2h = 0
+    e_frames, e_ms, _, _, _ = timed(host_step, args.steps)
+    e_tot = reduce(e_frames, dist.ReduceOp.SUM if dist else None)
+    e_max = reduce(e_ms, dist.ReduceOp.MAX if dist else None)
+
+    extras = {}
+    if world == 1 and not args.quick:
+        extras["single_stream"] = bench_single_stream(rt, synth, weights, torch)
+        extras["q8_matvec"] = bench_q8_matvec(rt, synth, torch, args.matvec_reps)
+
+    if rank == 0:
+        peak, peak_kind = measured_hbm_gbs()
+        dom = max(prof, key=lambda k: prof[k]["ms"])
+        d = prof[dom]
+        achieved = d["bytes"] / (d["ms"] * 1e-3) / 1e9
+        all_bytes = sum(v["bytes"] for v in prof.values())
+        line = {
+            "metric": METRIC, "value": round(tot_frames / (max_ms * 1e-3), 1), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "configs[3]" if args.streams == STREAMS else f"configs[3] shape, {args.streams} streams",
+                       "streams": args.streams, "layers": N_LAYERS,
+                       "context": "prefix U[64,2048] seed 2, synthetic K/V",
+                       "arrivals": "Poisson(1) arrivals and departures per step, seed 2",
+                       "kv": "bf16, 16-position pages", "weights": "Q8_0 int8 + fp16 scales, seed 0",
+                       "parallelism": f"request sharding x{world}",
+                       "l2": "per-step KV reads (~13 GB at N=1) far exceed the 126 MB L2"},
+            "roofline": {"bound": "hbm", "kernel": dom,
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "traffic": None,
+                         "algorithmic_bytes_per_launch": round(d["bytes"] / max(d["launches"], 1)),
+                         "avg_launch_us": round(d["ms"] * 1e3 / max(d["launches"], 1), 2),
+                         "step_achieved_gbs": round(all_bytes / (max_ms * 1e-3) / 1e9, 1),
+                         "kernels": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
+                                         "gbs": round(v["bytes"] / max(v["ms"], 1e-9) * 1e-6, 1)}
+                                     for k, v in prof.items() if v["launches"]}},
+            "e2e": {"value": round(e_tot / (e_max * 1e-3), 1), "unit": UNIT,
+                    "h2d_bytes_per_step": int(h2d / args.steps),
+                    "d2h_bytes_per_step": int(d2h / args.steps)},
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        line.update(extras)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def l2_flush(torch, buf):
+    buf.add_(1.0)
+
+
+def bench_single_stream(rt, synth, weights, torch):
+    """128-position prefix then 125 decode steps of one stream,
+    fp32 KV; the L2 is flushed (256 MB write) before every timed step."""
+    ctx = rt.Context(weights, max_streams=2, max_batch=1, pool_pages=32, kv_type=rt.KV_F32)
+    s = ctx.stream_alloc(256)
+    g = synth.stream_generator(0, 0)
+    ctx.append(s, np.stack([g.normal(512) for _ in range(128)]))
+    xs = torch.tensor(np.stack([g.normal(512) for _ in range(125)]), device="cuda")
+    y = torch.empty(512, device="cuda")
+    stream = torch.cuda.ExternalStream(ctx.cuda_stream())
+    flush = torch.zeros(64 * 2**20, device="cuda")  # 256 MB
+    times = []
+    for i in range(125):
+        l2_flush(torch, flush)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ctx.step_device([s], [128 + i], xs[i].data_ptr(), y.data_ptr())
+        b.record(stream)
+        ctx.sync(1)
+        times.append(a.elapsed_time(b))
+    ctx.close()
+    total = sum(times)
+    return {"workload": "configs[0]", "frames_per_s": round(125 / (total * 1e-3), 1),
+            "ms_per_step_median": round(statistics.median(times), 4),
+            "l2": "flushed before each step"}
+
+
+def bench_q8_matvec(rt, synth, torch, reps):
+    """the four projection shapes, per-row scales, batch 1/8/64;
+    GB/s of weight bytes. cold: L2 flushed before every launch; hot: back to
+    back on an L2-resident copy."""
+    g = synth.Generator(1)
+    flush = torch.zeros(64 * 2**20, device="cuda")
+    out = {}
+    stream = torch.cuda.current_stream()
+    for name, (rows, cols) in {"qkv": (1536, 512), "out": (512, 512), "up": (2048, 512),
+                               "down": (512, 2048)}.items():
+        lin = rt.Linear(g.q8_linear(rows, cols, synth.SCALE_PER_ROW), rows, cols)
+        wbytes = lin.bytes()
+        for batch in (1, 8, 64):
+            x = torch.randn(batch, cols, device="cuda")
+            y = torch.empty(batch, rows, device="cuda")
+            cold = []
+            for _ in range(reps):
+                l2_flush(torch, flush)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                lin.apply_device(x.data_ptr(), batch, y.data_ptr(), stream.cuda_stream)
+                b.record(stream)
+                b.synchronize()
+                cold.append(a.elapsed_time(b))
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for _ in range(20):
+                lin.apply_device(x.data_ptr(), batch, y.data_ptr(), stream.cuda_stream)
+            a.record(stream)
+            for _ in range(reps):
+                lin.apply_device(x.data_ptr(), batch, y.data_ptr(), stream.cuda_stream)
+            b.record(stream)
+            b.synchronize()
+            hot = a.elapsed_time(b) / reps
+            med = statistics.median(cold)
+            out[f"{name}_b{batch}"] = {"cold_gbs": round(wbytes / (med * 1e-3) / 1e9, 1),
+                                       "hot_gbs": round(wbytes / (hot * 1e-3) / 1e9, 1),
+                                       "cold_us": round(med * 1e3, 2), "hot_us": round(hot * 1e3, 2)}
+        lin.close()
+    return {"workload": "configs[1]", "reps": reps, "weight_bytes": "rows*cols*34/32", **out}
+
+
+# --------------------------------------------------------------- CPU baseline
+def cpu_threads():
+    return max(1, len(os.sched_getaffinity(0)))
+
+
+class RefRunner:
+    """The reference (oracle/_ref) on the configs[3] shape: one host thread
+    per stream, contexts U[64,2048] (seed 2) filled with seeded K/V rows,
+    prepared fp32 linears, OpenBLAS single-threaded per call."""
+
+    def __init__(self, threads):
+        from oracle.oracle import REF_SO, Reference
+        from phonon_b200 import synth
+        if not REF_SO.exists():
+            raise FileNotFoundError("oracle/_ref/libphonon_ref.so is not built")
+        self.synth = synth
+        self.threads = threads
+        ref = Reference(blas_threads=1)
+        self.model = ref.model(synth.flow_weights(N_LAYERS, seed=0), prepare=True)
+        rng = np.random.default_rng(2)
+        self.lens = [int(x) for x in rng.integers(64, 2049, threads)]
+        self.cap = max(self.lens) + 2048
+        kv = rng.standard_normal((N_LAYERS, max(self.lens), 512), dtype=np.float32)
+        self.streams = []
+        for t in range(threads):
+            s = self.model.new_stream(self.cap)
+            keys = np.ascontiguousarray(kv[:, :self.lens[t]])
+            self.model.fill(s, self.lens[t], keys, keys)
+            self.streams.append(s)
+        self.pos = list(self.lens)
+        self.x = [synth.stream_generator(5, t).normal(512) for t in range(threads)]
+
+    def run(self, seconds):
+        frames = [0] * self.threads
+        stop = threading.Event()
+
+        def work(t):
+            while not stop.is_set() and self.pos[t] < self.cap:
+                ok, _, _ = self.model.step(self.streams[t], self.pos[t], self.x[t])
+                if not ok:
+                    raise RuntimeError("reference step failed")
+                self.pos[t] += 1
+                frames[t] += 1
+
+        workers = [threading.Thread(target=work, args=(t,)) for t in range(self.threads)]
+        t0 = time.perf_counter()
+        for w in workers:
+            w.start()
+        time.sleep(seconds)
+        stop.set()
+        for w in workers:
+            w.join()
+        return sum(frames), time.perf_counter() - t0
+
+    def close(self):
+        for s in self.streams:
+            self.model.free_stream(s)
+
+
+def cpu_threads():
+    return max(1, min(64, len(os.sched_getaffinity(0))))
+
+
+def cpu_baseline(seconds):
+    threads = cpu_threads()
+    r = RefRunner(threads)
+    r.run(1.0)
+    frames, dt = r.run(seconds)
+    r.close()
+    return {"value": round(frames / dt, 2), "unit": UNIT, "cores": threads, "kind": "reference",
+            "sample": f"{threads} streams (one per host thread), contexts U[64,2048] seed 2 "
+                      f"(mean {int(np.mean(r.lens))}), 12 layers, fp32 KV, {frames} frames in "
+                      f"{dt:.1f} s, OpenBLAS 1 thread per call"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = cpu_threads()
+    per_step = max(0.25, args.cpu_seconds / max(args.steps, 1))
+    try:
+        r = RefRunner(threads)
+    except FileNotFoundError as e:
+        print(json.dumps({"impl": "reference", "unavailable": str(e)}))
+        return
+    for _ in range(args.warmup):
+        r.run(per_step / 2)
+    t_frames, t_time = 0, 0.0
+    for _ in range(args.steps):
+        f, dt = r.run(per_step)
+        t_frames += f
+        t_time += dt
+    r.close()
+    value = round(t_frames / t_time, 2)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_time * 1e3 / args.steps, 2), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "configs[3]", "streams": threads, "layers": N_LAYERS,
+                       "context": "prefix U[64,2048] seed 2",
+                       "kv": "fp32 (the reference has no bf16 KV)",
+                       "parallelism": f"{threads} host threads"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": f"each step: {threads} threads each decode their own "
+                                       f"stream for {per_step:.2f} s"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--quick", action="store_true", help="skip the configs[0]/[1] extras")
+    ap.add_argument("--streams", type=int, default=STREAMS,
+                    help="concurrent streams at start (512 = configs[3]; smaller for profiling)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--matvec-reps", type=int, default=2000)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -174,6 +174,26 @@ int phonon_cuda_erf_gelu(int device, float *values, size_t count);
 int phonon_cuda_rope_interleaved(int device, float *values, size_t width, size_t heads,
                                  size_t position, float theta);
 
+/* ---- live kernel profiling (CUDA events on the context's stream) ---- */
+typedef enum {
+    PHONON_CUDA_K_QKV = 0,       /* LN1 + QKV GEMV + RoPE + KV append */
+    PHONON_CUDA_K_ATTENTION = 1, /* split-K paged flash-decode */
+    PHONON_CUDA_K_COMBINE = 2,   /* split merge */
+    PHONON_CUDA_K_OUT = 3,       /* out projection + residual */
+    PHONON_CUDA_K_UP = 4,        /* LN2 + FFN up + GELU */
+    PHONON_CUDA_K_DOWN = 5,      /* FFN down + residual */
+    PHONON_CUDA_K_OTHER = 6,     /* page-table updates, KV fills */
+    PHONON_CUDA_K_COUNT = 7
+} PhononCudaKernelClass;
+/* Enable (1) or disable (0) per-launch event timing; enabling clears the
+ * totals. While enabled, every step accumulates per class: device time (ms),
+ * algorithmic bytes (weights + K/V rows + activations each launch must move)
+ * and launch counts. Arrays have PHONON_CUDA_K_COUNT entries. */
+int phonon_cuda_profile_enable(PhononCuda *ctx, int enable);
+int phonon_cuda_profile_read(PhononCuda *ctx, double *ms, double *bytes, uint64_t *launches);
+/* Kernels this context has launched since creation. */
+uint64_t phonon_cuda_launch_count(PhononCuda *ctx);
+
 const char *phonon_cuda_status_string(int status);
 
 #ifdef __cplusplus

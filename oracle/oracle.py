@@ -52,7 +52,8 @@ class OracleLayer(C.Structure):
 
 class OracleCache(C.Structure):
     _fields_ = [("n_layers", C.c_size_t), ("capacity", C.c_size_t), ("length", C.c_size_t),
-                ("keys", C.POINTER(C.c_float)), ("values", C.POINTER(C.c_float))]
+                ("keys", C.POINTER(C.c_float)), ("values", C.POINTER(C.c_float)),
+                ("kv_bf16", C.c_int)]
 
 
 class Oracle:
@@ -155,11 +156,20 @@ class OracleModel:
             lay.norm1_w, lay.norm1_b = w["norm1_w"].ctypes.data, w["norm1_b"].ctypes.data
             lay.norm2_w, lay.norm2_b = w["norm2_w"].ctypes.data, w["norm2_b"].ctypes.data
 
-    def new_stream(self, capacity):
+    def new_stream(self, capacity, kv_bf16=False):
         cache = OracleCache()
         if not self.o.lib.oracle_cache_init(C.byref(cache), self.n_layers, capacity):
             raise MemoryError("oracle cache")
+        cache.kv_bf16 = 1 if kv_bf16 else 0
         return cache
+
+    def set_kv(self, cache, layer, position, key, value):
+        n = cache.capacity * 512
+        base = layer * n + position * 512
+        keys = np.ctypeslib.as_array(cache.keys, shape=(cache.n_layers * n,))
+        vals = np.ctypeslib.as_array(cache.values, shape=(cache.n_layers * n,))
+        keys[base:base + 512] = key
+        vals[base:base + 512] = value
 
     def free_stream(self, cache):
         self.o.lib.oracle_cache_destroy(C.byref(cache))
@@ -205,6 +215,7 @@ class Reference:
         L.ref_model_create.restype = C.c_void_p
         L.ref_model_create.argtypes = [C.c_size_t, C.c_int, C.c_void_p, C.c_void_p]
         L.ref_model_destroy.argtypes = [C.c_void_p]
+        L.ref_model_prepare.argtypes = [C.c_void_p]
         L.ref_stream_create.restype = C.c_void_p
         L.ref_stream_create.argtypes = [C.c_void_p, C.c_size_t]
         L.ref_stream_destroy.argtypes = [C.c_void_p]
@@ -285,8 +296,11 @@ class Reference:
         self.lib.phonon_math_sincos(_ptr(x), x.size, _ptr(c), _ptr(s))
         return c, s
 
-    def model(self, weights, dtype=1):
-        return RefModel(self, weights, dtype)
+    def model(self, weights, dtype=1, prepare=False):
+        m = RefModel(self, weights, dtype)
+        if prepare and not self.lib.ref_model_prepare(m.handle):
+            raise RuntimeError("ref_model_prepare failed")
+        return m
 
 
 class RefModel:

@@ -43,6 +43,17 @@ static float bf16_to_float(uint16_t bits) {
     return f;
 }
 
+/* Round to the nearest bf16 (ties to even), returned widened to fp32. */
+static float round_bf16(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    u &= 0xffff0000u;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
 static int bf16_vector(const uint16_t *bits, float *out, size_t count) {
     if (!bits)
         return 0;
@@ -511,6 +522,11 @@ int oracle_layer_step(const OracleLayer *w, OracleCache *cache, size_t layer, si
     size_t base = layer * cache->capacity * 512;
     memcpy(cache->keys + base + position * 512, k, 512 * sizeof(float));
     memcpy(cache->values + base + position * 512, v, 512 * sizeof(float));
+    if (cache->kv_bf16) /* bf16 KV pages (benchmark configs[3]): one rounding on append */
+        for (size_t i = 0; i < 512; i++) {
+            cache->keys[base + position * 512 + i] = round_bf16(k[i]);
+            cache->values[base + position * 512 + i] = round_bf16(v[i]);
+        }
     for (size_t h = 0; h < 8; h++)
         if (!oracle_attention(q + h * 64, cache->keys + base + h * 64,
                               cache->values + base + h * 64, position + 1, 512,

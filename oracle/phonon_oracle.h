@@ -40,6 +40,7 @@ typedef struct {
 typedef struct {
     size_t n_layers, capacity, length;
     float *keys, *values; /* [layer][capacity][512], interleaved-RoPE order */
+    int kv_bf16;          /* 1: K/V rows are rounded to bf16 (nearest-even) on append */
 } OracleCache;
 
 float oracle_half_to_float(uint16_t bits);

@@ -88,7 +88,31 @@ RefModel *ref_model_create(size_t n_layers, int dtype, const void *const *linear
     return m;
 }
 
+/* Materialise every linear to fp32 once, as phonon_pack_prepare_linears does
+ * for an engine (src/phonon_pack.c:413-448, called from src/speech.c:30-61),
+ * so that timed steps do not re-expand Q8 weights per call. */
+int ref_model_prepare(RefModel *m) {
+    if (!m)
+        return 0;
+    for (size_t l = 0; l < m->n_layers; l++)
+        for (size_t i = 0; i < 4; i++) {
+            PhononTensorView *v = &m->views[l][i];
+            if (v->linear_data)
+                continue;
+            float *expanded = NULL;
+            if (!phonon_tensor_expand_linear(v, &expanded))
+                return 0;
+            v->linear_data = expanded;
+        }
+    return 1;
+}
+
 void ref_model_destroy(RefModel *m) {
+    if (!m)
+        return;
+    for (size_t l = 0; l < m->n_layers; l++)
+        for (size_t i = 0; i < 4; i++)
+            free((void *)m->views[l][i].linear_data);
     free(m);
 }
 

@@ -230,6 +230,19 @@ struct PhononCuda {
     float *h_x = nullptr, *h_y = nullptr, *h_stage = nullptr;
     size_t stage_cap = 0;  // floats in d_stage / h_stage
     int32_t* h_status = nullptr;
+    // launch accounting and live profiling
+    uint64_t launches = 0;
+    bool prof_on = false;
+    struct ProfRec {
+        int cls;
+        cudaEvent_t a, b;
+        double bytes;
+    };
+    std::vector<ProfRec> prof_pending;
+    std::vector<cudaEvent_t> prof_events;  // free list
+    double prof_ms[PHONON_CUDA_K_COUNT] = {};
+    double prof_bytes[PHONON_CUDA_K_COUNT] = {};
+    uint64_t prof_launches[PHONON_CUDA_K_COUNT] = {};
     // pending phonon_cuda_step_device
     bool pending = false;
     std::vector<uint32_t> pending_streams;
@@ -296,10 +309,61 @@ KvView kv_view(const PhononCuda* c) {
 
 bool valid_stream(const PhononCuda* c, uint32_t s) { return s < c->streams.size() && c->streams[s].used; }
 
+cudaEvent_t prof_event(PhononCuda* c) {
+    if (!c->prof_events.empty()) {
+        cudaEvent_t e = c->prof_events.back();
+        c->prof_events.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Bracket one kernel launch: count it and, when profiling, time it.
+struct LaunchScope {
+    PhononCuda* c;
+    int cls;
+    double bytes;
+    cudaEvent_t a = nullptr;
+    LaunchScope(PhononCuda* c_, int cls_, double bytes_) : c(c_), cls(cls_), bytes(bytes_) {
+        c->launches++;
+        if (c->prof_on) {
+            a = prof_event(c);
+            cudaEventRecord(a, c->stream);
+        }
+    }
+    ~LaunchScope() {
+        if (!a) return;
+        cudaEvent_t b = prof_event(c);
+        cudaEventRecord(b, c->stream);
+        c->prof_pending.push_back({cls, a, b, bytes});
+    }
+};
+
+// Fold finished launch timings into the totals (after a stream sync).
+void prof_collect(PhononCuda* c) {
+    for (auto& r : c->prof_pending) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+            c->prof_ms[r.cls] += ms;
+            c->prof_bytes[r.cls] += r.bytes;
+            c->prof_launches[r.cls] += 1;
+        }
+        c->prof_events.push_back(r.a);
+        c->prof_events.push_back(r.b);
+    }
+    c->prof_pending.clear();
+}
+
+// Device bytes of one linear's weights (int8 plane + fp16 scales, or bf16).
+double linear_bytes(const DevLinear& l) { return static_cast<double>(l.bytes); }
+
 // Row batch for one enqueue: entry e is (stream slot, position); splits are
 // planned over the pages each entry attends.
 struct Batch {
     int R = 0, S = 0, U = 0;
+    double keys = 0;  // sum over entries of (position + 1)
     int32_t *d_slot, *d_pos, *d_first, *d_count, *d_updates;
     Split* d_splits;
 };
@@ -374,6 +438,7 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     b.R = R;
     b.S = S;
     b.U = U;
+    for (int e = 0; e < R; ++e) b.keys += pos[e] + 1;
     b.d_slot = c->d_meta;
     b.d_pos = c->d_meta + R;
     b.d_first = c->d_meta + 2 * R;
@@ -381,6 +446,7 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     b.d_splits = reinterpret_cast<Split*>(c->d_meta + 4 * R);
     b.d_updates = c->d_meta + 4 * R + 4 * S;
     if (U > 0) {
+        LaunchScope ls(c, PHONON_CUDA_K_OTHER, U * 12.0);
         page_update_kernel<<<(U + 127) / 128, 128, 0, c->stream>>>(c->d_table, kMaxPagesPerStream, b.d_updates, U);
         CUDA_TRY(cudaGetLastError());
     }
@@ -412,7 +478,12 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     p.freq = c->d_freq;
     p.kv = kv;
     p.layer = l;
-    CUDA_TRY((launch_gemv<1, true, EPI_QKV>(q8, p, s)));
+    const double act = 4.0 * b.R;  // bytes per activation element across the batch
+    const double esize = kv.bf16 ? 2.0 : 4.0;
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_QKV, linear_bytes(L.qkv) + act * (kWidth + kWidth) + b.R * 2.0 * kWidth * esize);
+        CUDA_TRY((launch_gemv<1, true, EPI_QKV>(q8, p, s)));
+    }
     // 2. split-K attention + combine
     AttnParams ap{};
     ap.q = c->d_q;
@@ -425,9 +496,13 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     ap.status = c->d_status;
     const long long warps = static_cast<long long>(b.S) * kHeads;
     const unsigned grid = static_cast<unsigned>((warps + kAttnWarps - 1) / kAttnWarps);
-    if (kv.bf16) attn_partial_kernel<true><<<grid, kAttnWarps * 32, 0, s>>>(ap);
-    else attn_partial_kernel<false><<<grid, kAttnWarps * 32, 0, s>>>(ap);
-    CUDA_TRY(cudaGetLastError());
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_ATTENTION,
+                       b.keys * 2.0 * kWidth * esize + act * kWidth + b.S * kHeads * kPartStride * 4.0);
+        if (kv.bf16) attn_partial_kernel<true><<<grid, kAttnWarps * 32, 0, s>>>(ap);
+        else attn_partial_kernel<false><<<grid, kAttnWarps * 32, 0, s>>>(ap);
+        CUDA_TRY(cudaGetLastError());
+    }
     CombineParams cp{};
     cp.part = c->d_part;
     cp.first = b.d_first;
@@ -435,9 +510,12 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     cp.B = b.R;
     cp.out = c->d_a;
     cp.status = c->d_status;
-    attn_combine_kernel<<<static_cast<unsigned>((static_cast<long long>(b.R) * kHeads + kAttnWarps - 1) / kAttnWarps),
-                          kAttnWarps * 32, 0, s>>>(cp);
-    CUDA_TRY(cudaGetLastError());
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_COMBINE, b.S * kHeads * kPartStride * 4.0 + act * kWidth);
+        attn_combine_kernel<<<static_cast<unsigned>((static_cast<long long>(b.R) * kHeads + kAttnWarps - 1) / kAttnWarps),
+                              kAttnWarps * 32, 0, s>>>(cp);
+        CUDA_TRY(cudaGetLastError());
+    }
     // 3. h = x + attn Wout^T
     GemvParams po{};
     po.B = b.R;
@@ -452,7 +530,10 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     po.ldres = kWidth;
     po.y = c->d_h;
     po.ldy = kWidth;
-    CUDA_TRY((launch_gemv<1, false, EPI_RESID>(q8, po, s)));
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_OUT, linear_bytes(L.out) + act * 3 * kWidth);
+        CUDA_TRY((launch_gemv<1, false, EPI_RESID>(q8, po, s)));
+    }
     // 4. g = GELU(LN2(h) Wup^T)
     GemvParams pu{};
     pu.B = b.R;
@@ -467,7 +548,10 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     pu.ln_b = L.norms + 3 * kWidth;
     pu.y = c->d_g;
     pu.ldy = kFfn;
-    CUDA_TRY((launch_gemv<1, true, EPI_GELU>(q8, pu, s)));
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_UP, linear_bytes(L.up) + act * (kWidth + kFfn));
+        CUDA_TRY((launch_gemv<1, true, EPI_GELU>(q8, pu, s)));
+    }
     // 5. out = h + g Wdown^T
     GemvParams pd{};
     pd.B = b.R;
@@ -482,7 +566,10 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     pd.ldres = kWidth;
     pd.y = out;
     pd.ldy = kWidth;
-    CUDA_TRY((launch_gemv<4, false, EPI_RESID>(q8, pd, s)));
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_DOWN, linear_bytes(L.down) + act * (kFfn + 2 * kWidth));
+        CUDA_TRY((launch_gemv<4, false, EPI_RESID>(q8, pd, s)));
+    }
     return PHONON_CUDA_OK;
 }
 
@@ -525,6 +612,11 @@ void destroy_context(PhononCuda* c) {
     cudaSetDevice(c->cfg.device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (auto& L : c->layers) free_layer(L);
+    for (auto& r : c->prof_pending) {
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
     void* dev[] = {c->kv_pool, c->d_table, c->d_freq, c->d_x0, c->d_x1, c->d_y, c->d_q, c->d_a,
                    c->d_h, c->d_g, c->d_part, c->d_stage, c->d_meta, c->d_status};
     for (void* p : dev)
@@ -724,6 +816,36 @@ uint32_t phonon_cuda_free_pages(PhononCuda* c) {
 
 void* phonon_cuda_cuda_stream(PhononCuda* c) { return c ? c->stream : nullptr; }
 
+int phonon_cuda_profile_enable(PhononCuda* c, int enable) {
+    if (!c) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    c->prof_on = enable != 0;
+    if (c->prof_on)
+        for (int k = 0; k < PHONON_CUDA_K_COUNT; ++k) {
+            c->prof_ms[k] = c->prof_bytes[k] = 0.0;
+            c->prof_launches[k] = 0;
+        }
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_profile_read(PhononCuda* c, double* ms, double* bytes, uint64_t* launches) {
+    if (!c) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    for (int k = 0; k < PHONON_CUDA_K_COUNT; ++k) {
+        if (ms) ms[k] = c->prof_ms[k];
+        if (bytes) bytes[k] = c->prof_bytes[k];
+        if (launches) launches[k] = c->prof_launches[k];
+    }
+    return PHONON_CUDA_OK;
+}
+
+uint64_t phonon_cuda_launch_count(PhononCuda* c) {
+    if (!c) return 0;
+    std::lock_guard<std::mutex> g(c->mu);
+    return c->launches;
+}
+
 }  // extern "C"
 
 namespace {
@@ -760,6 +882,7 @@ int prepare_decode(PhononCuda* c, uint32_t n, const uint32_t* streams, const uin
 int finish_sync(PhononCuda* c, uint32_t n) {
     CUDA_TRY(cudaMemcpyAsync(c->h_status, c->d_status, n * 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
+    prof_collect(c);
     return PHONON_CUDA_OK;
 }
 
@@ -1048,10 +1171,15 @@ int phonon_cuda_stream_fill_synthetic(PhononCuda* c, uint32_t stream, uint32_t l
         undo.rollback();
         return st;
     }
-    kv_fill_kernel<<<296, 256, 0, c->stream>>>(kv_view(c), static_cast<int>(stream), static_cast<int>(c->cfg.n_layers),
-                                               static_cast<int>(length), seed);
-    CUDA_TRY(cudaGetLastError());
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_OTHER, static_cast<double>(length) * c->page_elems / kPage *
+                                                   (c->cfg.kv_type == PHONON_CUDA_KV_BF16 ? 2 : 4));
+        kv_fill_kernel<<<296, 256, 0, c->stream>>>(kv_view(c), static_cast<int>(stream),
+                                                   static_cast<int>(c->cfg.n_layers), static_cast<int>(length), seed);
+        CUDA_TRY(cudaGetLastError());
+    }
     CUDA_TRY(cudaStreamSynchronize(c->stream));
+    prof_collect(c);
     ss.length = length;
     return PHONON_CUDA_OK;
 }

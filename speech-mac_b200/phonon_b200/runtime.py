@@ -10,6 +10,7 @@ import numpy as np
 
 from ._libs import load_cuda
 
+KERNEL_CLASSES = ("qkv", "attention", "combine", "out", "up", "down", "other")
 OK, INVALID, NON_FINITE, OOM, POOL_EXHAUSTED, CAPACITY, BAD_POSITION, CANCELLED, DEVICE_ERROR = range(9)
 Q8_0, BF16 = 1, 2
 KV_F32, KV_BF16 = 0, 1
@@ -72,6 +73,8 @@ def lib():
         "phonon_cuda_rms_norm": [C.c_int, P, P, SZ, F, P],
         "phonon_cuda_erf_gelu": [C.c_int, P, SZ],
         "phonon_cuda_rope_interleaved": [C.c_int, P, SZ, SZ, SZ, F],
+        "phonon_cuda_profile_enable": [P, C.c_int],
+        "phonon_cuda_profile_read": [P, P, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -87,6 +90,8 @@ def lib():
     L.phonon_cuda_free_pages.restype = U32
     L.phonon_cuda_cuda_stream.argtypes = [P]
     L.phonon_cuda_cuda_stream.restype = P
+    L.phonon_cuda_launch_count.argtypes = [P]
+    L.phonon_cuda_launch_count.restype = C.c_uint64
     L.phonon_cuda_status_string.argtypes = [C.c_int]
     L.phonon_cuda_status_string.restype = C.c_char_p
     _typed = L
@@ -201,6 +206,20 @@ class Context:
 
     def cuda_stream(self):
         return self.L.phonon_cuda_cuda_stream(self.h)
+
+    def profile(self, enable=True):
+        check(self.L.phonon_cuda_profile_enable(self.h, 1 if enable else 0), "profile_enable")
+
+    def profile_read(self):
+        n = len(KERNEL_CLASSES)
+        ms, by = np.zeros(n, np.float64), np.zeros(n, np.float64)
+        la = np.zeros(n, np.uint64)
+        check(self.L.phonon_cuda_profile_read(self.h, _p(ms), _p(by), _p(la)), "profile_read")
+        return {k: {"ms": float(ms[i]), "bytes": float(by[i]), "launches": int(la[i])}
+                for i, k in enumerate(KERNEL_CLASSES)}
+
+    def launch_count(self):
+        return int(self.L.phonon_cuda_launch_count(self.h))
 
     def layer_step(self, s, layer, position, x):
         x = np.ascontiguousarray(x, np.float32)
