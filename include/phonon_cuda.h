@@ -174,6 +174,16 @@ int phonon_cuda_erf_gelu(int device, float *values, size_t count);
 int phonon_cuda_rope_interleaved(int device, float *values, size_t width, size_t heads,
                                  size_t position, float theta);
 
+/* ---- tensor-core contraction (diagnostic) ----
+ * D[m][n] = sum_k A[m][k] * B[n][k] in exact int32 on the tcgen05 kernel the
+ * batched step uses for its projections (A = int8 weight rows, B = int8 digit
+ * rows). Host buffers; K must be a multiple of 128. Has no counterpart in the
+ * reference, which never accumulates integers (src/phonon_q8.c:46-57 sums
+ * fp32 partials); it exists so the integer accumulation can be checked
+ * bit-exactly against a CPU integer product. */
+int phonon_cuda_i8_gemm(int device, const int8_t *a, const int8_t *b, size_t m, size_t n, size_t k,
+                        int32_t *d);
+
 /* ---- live kernel profiling (CUDA events on the context's stream) ---- */
 typedef enum {
     PHONON_CUDA_K_QKV = 0,       /* LN1 + QKV GEMV + RoPE + KV append */

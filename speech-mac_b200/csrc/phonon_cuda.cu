@@ -1,6 +1,7 @@
 // libphonon_cuda host runtime: contexts, KV page pool, step scheduling and
 // the C ABI declared in include/phonon_cuda.h.
 #include "phonon_cuda.h"
+#include "phonon_gemm.cuh"
 #include "phonon_kernels.cuh"
 
 #include <cuda_fp16.h>
@@ -24,6 +25,7 @@ constexpr int kMaxDevices = 64;
 constexpr int kMaxPagesPerStream = PHONON_CUDA_MAX_POSITIONS / kPage;  // 512
 constexpr int kSplitTarget = 640;   // ~8 warps per split: fills 148 SMs several times over
 constexpr int kPrefillChunk = 256;  // rows per prefill pass
+constexpr int kTensorMinBatch = 32;  // streams from which projections run on tcgen05
 
 #define CUDA_TRY(expr)                                                                       \
     do {                                                                                     \
@@ -43,7 +45,43 @@ struct DevLinear {
     void* plane = nullptr;
     __half* scales = nullptr;
     size_t bytes = 0;
+    // Tensor-core copy: Q8_0 whose 32-blocks share one scale per row.
+    bool tensor = false;
+    int8_t* nat = nullptr;       // natural row-major int8 [rows][cols]
+    float* row_scale = nullptr;  // [rows]
+    CUtensorMap tmap;            // 128-byte x 128-row SWIZZLE_128B boxes over `nat`
 };
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D int8 map [rows][cols] (cols bytes per row) with 128 x 128 boxes.
+bool make_i8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn || cols % kGemmKTile || reinterpret_cast<uintptr_t>(base) % 16) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols};
+    const cuuint32_t box[2] = {kGemmKTile, 128};
+    const cuuint32_t estride[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estride,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 bool half_is_finite(uint16_t h) { return ((h >> 10) & 0x1f) != 0x1f; }
 
@@ -59,6 +97,8 @@ float bf16_host(uint16_t b) {
 void free_linear(DevLinear& l) {
     if (l.plane) cudaFree(l.plane);
     if (l.scales) cudaFree(l.scales);
+    if (l.nat) cudaFree(l.nat);
+    if (l.row_scale) cudaFree(l.row_scale);
     l = DevLinear{};
 }
 
@@ -101,10 +141,38 @@ int upload_linear(int kind, const void* host, size_t rows, size_t cols, DevLinea
                 q[r * cols + c] = static_cast<int8_t>(row[(lc / 32) * 34 + 2 + lc % 32]);
             }
         }
+        // Tensor-core eligibility: every 32-block of a row has the same scale.
+        bool uniform = cols % kGemmKTile == 0;
+        std::vector<int8_t> nat;
+        std::vector<float> rs;
+        if (uniform) {
+            nat.resize(n);
+            rs.resize(rows);
+            for (size_t r = 0; r < rows && uniform; ++r) {
+                const uint8_t* row = blocks + r * (cols / 32) * 34;
+                const uint16_t h0 = static_cast<uint16_t>(row[0] | (row[1] << 8));
+                for (size_t b = 0; b < cols / 32; ++b) {
+                    if (static_cast<uint16_t>(row[b * 34] | (row[b * 34 + 1] << 8)) != h0) uniform = false;
+                    std::memcpy(&nat[r * cols + b * 32], row + b * 34 + 2, 32);
+                }
+                __half_raw hr;
+                hr.x = h0;
+                rs[r] = __half2float(__half(hr));
+            }
+        }
         if (cudaMalloc(&l.plane, n) != cudaSuccess ||
-            cudaMalloc(reinterpret_cast<void**>(&l.scales), s.size() * 2) != cudaSuccess) {
+            cudaMalloc(reinterpret_cast<void**>(&l.scales), s.size() * 2) != cudaSuccess ||
+            (uniform && (cudaMalloc(&l.nat, n) != cudaSuccess || cudaMalloc(&l.row_scale, rows * 4) != cudaSuccess))) {
             free_linear(l);
             return PHONON_CUDA_OUT_OF_MEMORY;
+        }
+        if (uniform) {
+            if (cudaMemcpy(l.nat, nat.data(), n, cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemcpy(l.row_scale, rs.data(), rows * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+                free_linear(l);
+                return PHONON_CUDA_DEVICE_ERROR;
+            }
+            l.tensor = make_i8_map(&l.tmap, l.nat, rows, cols);
         }
         if (cudaMemcpy(l.plane, q.data(), n, cudaMemcpyHostToDevice) != cudaSuccess ||
             cudaMemcpy(l.scales, s.data(), s.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
@@ -196,6 +264,31 @@ cudaError_t launch_linear(const DevLinear& l, const float* x, int B, const float
     return cudaGetLastError();
 }
 
+template <int kEpi>
+cudaError_t launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, int rows, int n_digit_rows, const GemmParams& p,
+                        cudaStream_t s) {
+    static bool configured[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(i8_gemm_kernel<kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    dim3 grid((rows + kGemmM - 1) / kGemmM, (n_digit_rows + kGemmN - 1) / kGemmN);
+    i8_gemm_kernel<kEpi><<<grid, kGemmThreads, kGemmSmem, s>>>(tw, tx, p);
+    return cudaGetLastError();
+}
+
+template <int kCols, bool kLN>
+cudaError_t launch_digits(const float* x, int ldx, const float* ln_w, const float* ln_b, int B, int Bpad,
+                          int8_t* digits, int32_t* exps, int32_t* status, cudaStream_t s) {
+    digits_kernel<kCols, kLN><<<(Bpad + 7) / 8, 256, 0, s>>>(x, ldx, ln_w, ln_b, B, Bpad, digits, exps, status);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------- context
@@ -226,6 +319,11 @@ struct PhononCuda {
     float *d_x0 = nullptr, *d_x1 = nullptr, *d_y = nullptr, *d_q = nullptr, *d_a = nullptr,
           *d_h = nullptr, *d_g = nullptr, *d_part = nullptr, *d_stage = nullptr;
     int32_t *d_meta = nullptr, *d_status = nullptr;
+    // tensor-core path: digit rows of the current batch and their exponents
+    int8_t *d_dig512 = nullptr, *d_dig2048 = nullptr;
+    int32_t *d_exps = nullptr, *d_err = nullptr;
+    CUtensorMap tm_dig512, tm_dig2048;
+    bool tensor_ok = false;
     int32_t* h_meta = nullptr;
     float *h_x = nullptr, *h_y = nullptr, *h_stage = nullptr;
     size_t stage_cap = 0;  // floats in d_stage / h_stage
@@ -455,36 +553,13 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
 }
 
 // Enqueue layer `l` for the batch: in -> out (out != in).
-int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* out) {
-    const DevLayer& L = c->layers[l];
-    const bool q8 = L.q8;
+int enqueue_attention(PhononCuda* c, const Batch& b, int l);
+
+int enqueue_attention(PhononCuda* c, const Batch& b, int l) {
     cudaStream_t s = c->stream;
     const KvView kv = kv_view(c);
-    GemvParams p{};
-    p.B = b.R;
-    p.status = c->d_status;
-    // 1. LN1 -> QKV -> RoPE -> q scratch + KV append
-    p.w = L.qkv.plane;
-    p.scales = L.qkv.scales;
-    p.rows = 1536;
-    p.cols = 512;
-    p.x = in;
-    p.ldx = kWidth;
-    p.ln_w = L.norms;
-    p.ln_b = L.norms + kWidth;
-    p.q = c->d_q;
-    p.slot = b.d_slot;
-    p.pos = b.d_pos;
-    p.freq = c->d_freq;
-    p.kv = kv;
-    p.layer = l;
-    const double act = 4.0 * b.R;  // bytes per activation element across the batch
+    const double act = 4.0 * b.R;
     const double esize = kv.bf16 ? 2.0 : 4.0;
-    {
-        LaunchScope ls(c, PHONON_CUDA_K_QKV, linear_bytes(L.qkv) + act * (kWidth + kWidth) + b.R * 2.0 * kWidth * esize);
-        CUDA_TRY((launch_gemv<1, true, EPI_QKV>(q8, p, s)));
-    }
-    // 2. split-K attention + combine
     AttnParams ap{};
     ap.q = c->d_q;
     ap.slot = b.d_slot;
@@ -515,6 +590,134 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
         attn_combine_kernel<<<static_cast<unsigned>((static_cast<long long>(b.R) * kHeads + kAttnWarps - 1) / kAttnWarps),
                               kAttnWarps * 32, 0, s>>>(cp);
         CUDA_TRY(cudaGetLastError());
+    }
+    return PHONON_CUDA_OK;
+}
+
+// The same layer with the four projections on tcgen05 (digit-sliced int8).
+int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, float* out) {
+    const DevLayer& L = c->layers[l];
+    cudaStream_t s = c->stream;
+    const KvView kv = kv_view(c);
+    const int B = b.R, Bpad = (b.R + 31) / 32 * 32, nd = kDigits * Bpad;
+    const double act = 4.0 * B, esize = kv.bf16 ? 2.0 : 4.0, dig = kDigits * Bpad;
+    GemmParams g{};
+    g.B = B;
+    g.exps = c->d_exps;
+    g.status = c->d_status;
+    g.error = c->d_err;
+    // 1. LN1 + digits, QKV + RoPE + KV append
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_QKV, act * kWidth + dig * 512);
+        CUDA_TRY((launch_digits<512, true>(in, kWidth, L.norms, L.norms + kWidth, B, Bpad, c->d_dig512, c->d_exps,
+                                           c->d_status, s)));
+    }
+    g.rows = 1536;
+    g.K = 512;
+    g.row_scale = L.qkv.row_scale;
+    g.q = c->d_q;
+    g.slot = b.d_slot;
+    g.pos = b.d_pos;
+    g.freq = c->d_freq;
+    g.kv = kv;
+    g.layer = l;
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_QKV, 1536.0 * 512 + dig * 512 + act * kWidth + B * 2.0 * kWidth * esize);
+        CUDA_TRY(launch_gemm<GEPI_QKV>(L.qkv.tmap, c->tm_dig512, 1536, nd, g, s));
+    }
+    // 2. attention
+    int st = enqueue_attention(c, b, l);
+    if (st) return st;
+    // 3. h = x + attn Wout^T
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_OUT, act * kWidth + dig * 512);
+        CUDA_TRY((launch_digits<512, false>(c->d_a, kWidth, nullptr, nullptr, B, Bpad, c->d_dig512, c->d_exps,
+                                            c->d_status, s)));
+    }
+    GemmParams go = g;
+    go.rows = 512;
+    go.K = 512;
+    go.row_scale = L.out.row_scale;
+    go.res = in;
+    go.ldres = kWidth;
+    go.y = c->d_h;
+    go.ldy = kWidth;
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_OUT, 512.0 * 512 + dig * 512 + act * 2 * kWidth);
+        CUDA_TRY(launch_gemm<GEPI_RESID>(L.out.tmap, c->tm_dig512, 512, nd, go, s));
+    }
+    // 4. g = GELU(LN2(h) Wup^T)
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_UP, act * kWidth + dig * 512);
+        CUDA_TRY((launch_digits<512, true>(c->d_h, kWidth, L.norms + 2 * kWidth, L.norms + 3 * kWidth, B, Bpad,
+                                           c->d_dig512, c->d_exps, c->d_status, s)));
+    }
+    GemmParams gu = g;
+    gu.rows = kFfn;
+    gu.K = 512;
+    gu.row_scale = L.up.row_scale;
+    gu.y = c->d_g;
+    gu.ldy = kFfn;
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_UP, 2048.0 * 512 + dig * 512 + act * kFfn);
+        CUDA_TRY(launch_gemm<GEPI_GELU>(L.up.tmap, c->tm_dig512, kFfn, nd, gu, s));
+    }
+    // 5. out = h + g Wdown^T
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_DOWN, act * kFfn + dig * 2048);
+        CUDA_TRY((launch_digits<2048, false>(c->d_g, kFfn, nullptr, nullptr, B, Bpad, c->d_dig2048, c->d_exps,
+                                             c->d_status, s)));
+    }
+    GemmParams gd = g;
+    gd.rows = 512;
+    gd.K = kFfn;
+    gd.row_scale = L.down.row_scale;
+    gd.res = c->d_h;
+    gd.ldres = kWidth;
+    gd.y = out;
+    gd.ldy = kWidth;
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_DOWN, 512.0 * 2048 + dig * 2048 + act * 2 * kWidth);
+        CUDA_TRY(launch_gemm<GEPI_RESID>(L.down.tmap, c->tm_dig2048, 512, nd, gd, s));
+    }
+    return PHONON_CUDA_OK;
+}
+
+int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* out) {
+    const DevLayer& L = c->layers[l];
+    if (c->tensor_ok && b.R >= kTensorMinBatch && L.qkv.tensor && L.out.tensor && L.up.tensor && L.down.tensor)
+        return enqueue_layer_tensor(c, b, l, in, out);
+    const bool q8 = L.q8;
+    cudaStream_t s = c->stream;
+    const KvView kv = kv_view(c);
+    GemvParams p{};
+    p.B = b.R;
+    p.status = c->d_status;
+    // 1. LN1 -> QKV -> RoPE -> q scratch + KV append
+    p.w = L.qkv.plane;
+    p.scales = L.qkv.scales;
+    p.rows = 1536;
+    p.cols = 512;
+    p.x = in;
+    p.ldx = kWidth;
+    p.ln_w = L.norms;
+    p.ln_b = L.norms + kWidth;
+    p.q = c->d_q;
+    p.slot = b.d_slot;
+    p.pos = b.d_pos;
+    p.freq = c->d_freq;
+    p.kv = kv;
+    p.layer = l;
+    const double act = 4.0 * b.R;  // bytes per activation element across the batch
+    const double esize = kv.bf16 ? 2.0 : 4.0;
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_QKV, linear_bytes(L.qkv) + act * (kWidth + kWidth) + b.R * 2.0 * kWidth * esize);
+        CUDA_TRY((launch_gemv<1, true, EPI_QKV>(q8, p, s)));
+    }
+    // 2. split-K attention + combine
+    {
+        int st = enqueue_attention(c, b, l);
+        if (st) return st;
     }
     // 3. h = x + attn Wout^T
     GemvParams po{};
@@ -618,7 +821,8 @@ void destroy_context(PhononCuda* c) {
     }
     for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
     void* dev[] = {c->kv_pool, c->d_table, c->d_freq, c->d_x0, c->d_x1, c->d_y, c->d_q, c->d_a,
-                   c->d_h, c->d_g, c->d_part, c->d_stage, c->d_meta, c->d_status};
+                   c->d_h, c->d_g, c->d_part, c->d_stage, c->d_meta, c->d_status,
+                   c->d_dig512, c->d_dig2048, c->d_exps, c->d_err};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_meta, c->h_x, c->h_y, c->h_stage, c->h_status};
@@ -718,7 +922,14 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
               cudaMallocHost(&c->h_x, rows * kWidth * 4) == cudaSuccess &&
               cudaMallocHost(&c->h_y, rows * kWidth * 4) == cudaSuccess &&
               cudaMallocHost(&c->h_status, rows * 4) == cudaSuccess;
+    const size_t rows_pad = (rows + 31) / 32 * 32;
+    ok = ok && cudaMalloc(&c->d_dig512, rows_pad * kDigits * 512) == cudaSuccess &&
+         cudaMalloc(&c->d_dig2048, rows_pad * kDigits * 2048) == cudaSuccess &&
+         cudaMalloc(&c->d_exps, rows_pad * 4) == cudaSuccess && cudaMalloc(&c->d_err, 4) == cudaSuccess;
     if (!ok) return fail(PHONON_CUDA_OUT_OF_MEMORY);
+    if (cudaMemset(c->d_err, 0, 4) != cudaSuccess) return fail(PHONON_CUDA_DEVICE_ERROR);
+    c->tensor_ok = make_i8_map(&c->tm_dig512, c->d_dig512, rows_pad * kDigits, 512) &&
+                   make_i8_map(&c->tm_dig2048, c->d_dig2048, rows_pad * kDigits, 2048);
     if (cudaMemcpy(c->d_freq, freq, sizeof(freq), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemset(c->d_table, 0, static_cast<size_t>(cfg.max_streams) * kMaxPagesPerStream * 4) != cudaSuccess)
         return fail(PHONON_CUDA_DEVICE_ERROR);
@@ -881,8 +1092,16 @@ int prepare_decode(PhononCuda* c, uint32_t n, const uint32_t* streams, const uin
 
 int finish_sync(PhononCuda* c, uint32_t n) {
     CUDA_TRY(cudaMemcpyAsync(c->h_status, c->d_status, n * 4, cudaMemcpyDeviceToHost, c->stream));
+    int32_t err = 0;
+    CUDA_TRY(cudaMemcpyAsync(&err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     prof_collect(c);
+    if (err) {  // a tensor-core tile gave up waiting: report, then clear for the next call
+        cudaMemsetAsync(c->d_err, 0, 4, c->stream);
+        cudaStreamSynchronize(c->stream);
+        std::fprintf(stderr, "phonon_cuda: tensor-core tile wait expired\n");
+        return PHONON_CUDA_DEVICE_ERROR;
+    }
     return PHONON_CUDA_OK;
 }
 
@@ -1185,6 +1404,50 @@ int phonon_cuda_stream_fill_synthetic(PhononCuda* c, uint32_t stream, uint32_t l
 }
 
 }  // extern "C"
+
+// ========================================================= raw int8 GEMM
+extern "C" int phonon_cuda_i8_gemm(int device, const int8_t* a, const int8_t* b, size_t m, size_t n, size_t k,
+                                   int32_t* d) {
+    if (!a || !b || !d || !m || !n || !k || k % kGemmKTile || m > (1u << 20) || n > (1u << 20) || k > (1u << 16))
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(device);
+    if (st) return st;
+    int8_t *da = nullptr, *db = nullptr;
+    int32_t *dd = nullptr, *derr = nullptr;
+    cudaStream_t s = nullptr;
+    auto cleanup = [&](int code) {
+        if (s) cudaStreamSynchronize(s);
+        if (da) cudaFree(da);
+        if (db) cudaFree(db);
+        if (dd) cudaFree(dd);
+        if (derr) cudaFree(derr);
+        if (s) cudaStreamDestroy(s);
+        return code;
+    };
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess || cudaMalloc(&da, m * k) != cudaSuccess ||
+        cudaMalloc(&db, n * k) != cudaSuccess || cudaMalloc(&dd, m * n * 4) != cudaSuccess ||
+        cudaMalloc(&derr, 4) != cudaSuccess)
+        return cleanup(PHONON_CUDA_OUT_OF_MEMORY);
+    CUtensorMap ta, tb;
+    if (!make_i8_map(&ta, da, m, k) || !make_i8_map(&tb, db, n, k)) return cleanup(PHONON_CUDA_DEVICE_ERROR);
+    if (cudaMemcpy(da, a, m * k, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(db, b, n * k, cudaMemcpyHostToDevice) != cudaSuccess || cudaMemset(derr, 0, 4) != cudaSuccess)
+        return cleanup(PHONON_CUDA_DEVICE_ERROR);
+    GemmParams p{};
+    p.rows = static_cast<int>(m);
+    p.K = static_cast<int>(k);
+    p.raw = dd;
+    p.n_total = static_cast<int>(n);
+    p.error = derr;
+    if (launch_gemm<GEPI_RAW>(ta, tb, static_cast<int>(m), static_cast<int>(n), p, s) != cudaSuccess)
+        return cleanup(PHONON_CUDA_DEVICE_ERROR);
+    int32_t err = 0;
+    if (cudaMemcpyAsync(&err, derr, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
+        return cleanup(PHONON_CUDA_DEVICE_ERROR);
+    if (err) return cleanup(PHONON_CUDA_DEVICE_ERROR);
+    if (cudaMemcpy(d, dd, m * n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return cleanup(PHONON_CUDA_DEVICE_ERROR);
+    return cleanup(PHONON_CUDA_OK);
+}
 
 // ============================================================ linear handles
 struct PhononCudaLinear {

@@ -1,0 +1,387 @@
+// Batched projections on the 5th-generation tensor cores (sm_100a tcgen05).
+//
+// y[b][r] = s_r * sum_k x[b][k] * q[r][k] for B streams at once, with the
+// weight rows r as the MMA M dimension and the streams as N.
+//
+// Activations become exact int8 data by digit slicing: each stream row x_b
+// gets an exponent e_b (max|x_b| < 2^(e_b-1)) and four signed base-128
+// digits d_j in [-64, 64] with x_b ~= 2^e_b * sum_j d_j * 2^(-7(j+1)); the
+// residual is below 2^(e_b-29). Digit row 4b+j is operand B. One int8 MMA
+// chain then yields D[r][4b+j] = sum_k q[r][k] * d_j[b][k] exactly in int32
+// (|D| <= 2048 * 64 * 127 < 2^24, so it is also exact in fp32), and the
+// epilogue recombines y = s_r * sum_j D[r][4b+j] * 2^(e_b - 7(j+1)).
+//
+// Kernel shape: one CTA per 128-row x 32-stream tile (M = 128, N = 128 digit
+// rows), 6 warps: warp 0 issues TMA tile loads (no multicast), warp 1 owns
+// the TMEM accumulator and issues tcgen05.mma, warps 2-5 drain TMEM in the
+// epilogue. K is staged in 128-byte tiles (SWIZZLE_128B) through a 4-deep
+// mbarrier ring. Every mbarrier wait is bounded: on expiry the CTA raises the
+// context's error flag, skips its remaining work and still frees its TMEM.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "phonon_kernels.cuh"
+
+namespace phonon {
+
+constexpr int kGemmM = 128;       // weight rows per tile (MMA M)
+constexpr int kGemmN = 128;       // digit rows per tile (MMA N) = 32 streams x 4 slices
+constexpr int kGemmKTile = 128;   // bytes of K per stage
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;
+constexpr int kGemmStreamsPerTile = kGemmN / 4;
+constexpr int kDigits = 4;
+constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmM + kGemmN) * kGemmKTile + 256;
+constexpr long long kWaitBudgetCycles = 4ll << 30;  // ~2 s at 1.9 GHz
+
+enum GemmEpilogue : int { GEPI_RAW = 0, GEPI_RESID = 1, GEPI_GELU = 2, GEPI_QKV = 3 };
+
+struct GemmParams {
+    int rows;              // weight rows (M)
+    int K;                 // bytes per row
+    int B;                 // streams
+    const float* row_scale;  // [rows] weight row scales
+    const int32_t* exps;   // [B] e_b of the digit rows
+    // outputs, as in GemvParams
+    float* y;
+    int ldy;
+    const float* res;
+    int ldres;
+    float* q;
+    const int32_t* slot;
+    const int32_t* pos;
+    const float* freq;
+    KvView kv;
+    int layer;
+    int32_t* status;
+    int32_t* raw;          // GEPI_RAW: D as [rows][n_total] int32
+    int n_total;
+    int32_t* error;        // set when a bounded wait expires
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait: returns false (and raises *error) when the budget runs out or
+// another role of this CTA already failed.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* error,
+                                          volatile int* cta_failed) {
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*cta_failed) return false;
+        if (clock64() - start > kWaitBudgetCycles) {
+            *cta_failed = 1;
+            if (error) atomicExch(error, 1);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+// K-major operand tile in SWIZZLE_128B form: 8-row atoms of 8 x 16 bytes,
+// atoms 1024 bytes apart (stride byte offset 64 x 16), descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
+    uint64_t d = (static_cast<uint64_t>(addr) >> 4) & 0x3FFFull;
+    d |= static_cast<uint64_t>(1) << 16;                 // leading byte offset (unused when swizzled)
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;         // stride byte offset
+    d |= static_cast<uint64_t>(1) << 46;                 // descriptor version (sm_100)
+    d |= static_cast<uint64_t>(2) << 61;                 // SWIZZLE_128B
+    return d;
+}
+
+// kind::i8 instruction descriptor: s32 accumulator, signed A and B, both
+// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float pow2f(int e) {  // exact 2^e for normal exponents
+    return __int_as_float((127 + e) << 23);
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    i8_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                   GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;                                           // [stages][128 rows][128 B]
+    uint8_t* sB = smem + kGemmStages * kGemmM * kGemmKTile;       // [stages][128 rows][128 B]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kGemmStages * kGemmN * kGemmKTile);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kGemmStages + 1);
+    volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const uint32_t full0 = smem_addr(bars), empty0 = full0 + 8 * kGemmStages, accum = full0 + 16 * kGemmStages;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m_tile = blockIdx.x, n_tile = blockIdx.y;
+    const int nk = p.K / kGemmKTile;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGemmStages; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, 1);
+        }
+        mbar_init(accum, 1);
+        *failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                     "r"(kGemmN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // TMA producer: weight tile rows [m_tile*128, +128), digit rows [n_tile*128, +128).
+        for (int kt = 0; kt < nk; ++kt) {
+            const int s = kt % kGemmStages;
+            if (kt >= kGemmStages &&
+                !mbar_wait(empty0 + 8 * s, ((kt / kGemmStages) - 1) & 1, p.error, failed))
+                break;
+            mbar_expect_tx(full0 + 8 * s, (kGemmM + kGemmN) * kGemmKTile);
+            tma_load_2d(smem_addr(sA + s * kGemmM * kGemmKTile), &tm_w, kt * kGemmKTile, m_tile * kGemmM,
+                        full0 + 8 * s);
+            tma_load_2d(smem_addr(sB + s * kGemmN * kGemmKTile), &tm_x, kt * kGemmKTile, n_tile * kGemmN,
+                        full0 + 8 * s);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer: four K=32 steps per 128-byte stage.
+        constexpr uint32_t idesc = umma_idesc_i8(kGemmM, kGemmN);
+        bool ok = true;
+        for (int kt = 0; kt < nk; ++kt) {
+            const int s = kt % kGemmStages;
+            if (!mbar_wait(full0 + 8 * s, (kt / kGemmStages) & 1, p.error, failed)) {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a0 = smem_addr(sA + s * kGemmM * kGemmKTile);
+            const uint32_t b0 = smem_addr(sB + s * kGemmN * kGemmKTile);
+#pragma unroll
+            for (int kk = 0; kk < kGemmKTile / 32; ++kk)
+                umma_i8(tmem, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
+                        (kt | kk) != 0);
+            umma_commit(empty0 + 8 * s);
+        }
+        if (ok) umma_commit(accum);
+    } else if (warp >= 2) {
+        // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows.
+        const int quarter = warp & 3;
+        const int r = m_tile * kGemmM + quarter * 32 + lane;
+        const bool have = __all_sync(kFull, mbar_wait(accum, 0, p.error, failed));
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (have) {
+            const float scale = (kEpi == GEPI_RAW || r >= p.rows) ? 1.0f : p.row_scale[r];
+#pragma unroll 1
+            for (int c0 = 0; c0 < kGemmN; c0 += 32) {
+                uint32_t d[32];
+                tmem_load32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c0, d);
+                if constexpr (kEpi == GEPI_RAW) {
+                    if (r < p.rows)
+                        for (int i = 0; i < 32; ++i) {
+                            const int n = n_tile * kGemmN + c0 + i;
+                            if (n < p.n_total) p.raw[static_cast<size_t>(r) * p.n_total + n] = static_cast<int32_t>(d[i]);
+                        }
+                    continue;
+                }
+                // 8 streams per 32 columns: recombine the four digit slices.
+#pragma unroll
+                for (int t = 0; t < 8; ++t) {
+                    const int b = n_tile * kGemmStreamsPerTile + (c0 >> 2) + t;
+                    const bool live = b < p.B;
+                    const int e = live ? p.exps[b] : 0;
+                    float v = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < kDigits; ++j)
+                        v = fmaf(static_cast<float>(static_cast<int32_t>(d[4 * t + j])), pow2f(e - 7 * (j + 1)), v);
+                    v *= scale;
+                    if constexpr (kEpi == GEPI_QKV) {
+                        // rows r (even lane) and r+1 (odd lane) form a RoPE pair
+                        const float other = __shfl_xor_sync(kFull, v, 1);
+                        if (!live || r >= p.rows) continue;
+                        const int region = r >> 9, within = r & 511;
+                        const int position = p.pos[b];
+                        float a = (lane & 1) ? other : v, bb = (lane & 1) ? v : other;
+                        if (region < 2) rope_pair(a, bb, position, p.freq[(within & 63) >> 1]);
+                        const float mine = (lane & 1) ? bb : a;
+                        if (!isfinite(mine)) flag_nonfinite(p.status, b);
+                        if (region == 0) {
+                            p.q[static_cast<size_t>(b) * kWidth + within] = mine;
+                        } else {
+                            const int page = p.kv.table[static_cast<size_t>(p.slot[b]) * p.kv.max_pages + position / kPage];
+                            const long long off = kv_offset(p.kv, page, p.layer, region - 1, within >> 6,
+                                                            position % kPage) + (within & 63);
+                            if (p.kv.bf16) static_cast<uint16_t*>(p.kv.pool)[off] = f32_to_bf16(mine);
+                            else static_cast<float*>(p.kv.pool)[off] = mine;
+                        }
+                    } else {
+                        if (!live || r >= p.rows) continue;
+                        if constexpr (kEpi == GEPI_RESID) v = __fadd_rn(p.res[static_cast<size_t>(b) * p.ldres + r], v);
+                        if constexpr (kEpi == GEPI_GELU) {
+                            if (!isfinite(v)) flag_nonfinite(p.status, b);
+                            v = gelu_erf(v);
+                        }
+                        if (!isfinite(v)) flag_nonfinite(p.status, b);
+                        p.y[static_cast<size_t>(b) * p.ldy + r] = v;
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmN) : "memory");
+    }
+}
+
+// Digit slicing (see the header comment). One warp per stream row of width
+// kCols; with kLN the row is first layer-normalised exactly as in
+// warp_layernorm512. Writes digit rows 4b..4b+3 and e_b; rows of streams
+// B..Bpad-1 are zeroed so that padded tiles multiply zeros.
+template <int kCols, bool kLN>
+__global__ void __launch_bounds__(256) digits_kernel(const float* __restrict__ x, int ldx, const float* ln_w,
+                                                     const float* ln_b, int B, int Bpad, int8_t* __restrict__ digits,
+                                                     int32_t* __restrict__ exps, int32_t* status) {
+    __shared__ __align__(16) float row[8][kLN ? kCols : 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x * 8 + warp;
+    if (b >= Bpad) return;
+    constexpr int per_lane = kCols / 32;
+    if (b >= B) {
+        for (int j = 0; j < kDigits; ++j)
+            for (int i = lane * 16; i < kCols; i += 32 * 16)
+                *reinterpret_cast<int4*>(digits + (static_cast<size_t>(4 * b + j)) * kCols + i) = make_int4(0, 0, 0, 0);
+        if (lane == 0) exps[b] = 0;
+        return;
+    }
+    const float* src = x + static_cast<size_t>(b) * ldx;
+    if constexpr (kLN) {
+        const bool ok = warp_layernorm512(src, ln_w, ln_b, row[warp]);
+        if (!ok && lane == 0) flag_nonfinite(status, b);
+        __syncwarp();
+        src = row[warp];
+    }
+    // lane owns columns lane*4 + 128*i .. +3 (i < per_lane/4): float4 reads
+    float v[per_lane];
+#pragma unroll
+    for (int i = 0; i < per_lane / 4; ++i) {
+        const float4 f = *reinterpret_cast<const float4*>(src + i * 128 + lane * 4);
+        v[4 * i] = f.x;
+        v[4 * i + 1] = f.y;
+        v[4 * i + 2] = f.z;
+        v[4 * i + 3] = f.w;
+    }
+    float mx = 0.0f;
+    bool finite_ok = true;
+#pragma unroll
+    for (int i = 0; i < per_lane; ++i) {
+        finite_ok &= isfinite(v[i]);
+        mx = fmaxf(mx, fabsf(v[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    if (!__all_sync(kFull, finite_ok)) {
+        if (lane == 0) flag_nonfinite(status, b);
+        mx = 0.0f;
+    }
+    int e = 0;
+    frexpf(mx, &e);  // mx < 2^e
+    e += 1;          // |x| * 2^-e < 1/2
+    if (e < -90) {   // rows below 2^-91: digits of zero (keeps every 2^(e-28) normal)
+        mx = 0.0f;
+        e = 0;
+    }
+    const float down = pow2f(-e);
+    uint32_t packed[kDigits][per_lane / 4];
+#pragma unroll
+    for (int i = 0; i < per_lane / 4; ++i)
+#pragma unroll
+        for (int j = 0; j < kDigits; ++j) packed[j][i] = 0;
+#pragma unroll
+    for (int i = 0; i < per_lane; ++i) {
+        float r = (finite_ok && mx > 0.0f) ? v[i] * down : 0.0f;  // exact scaling by a power of two
+#pragma unroll
+        for (int j = 0; j < kDigits; ++j) {
+            r *= 128.0f;
+            const float dj = rintf(r);
+            r -= dj;  // exact: the fractional part of r
+            packed[j][i / 4] |= (static_cast<uint32_t>(static_cast<int32_t>(dj)) & 0xffu) << (8 * (i % 4));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kDigits; ++j)
+#pragma unroll
+        for (int i = 0; i < per_lane / 4; ++i)
+            *reinterpret_cast<uint32_t*>(digits + static_cast<size_t>(4 * b + j) * kCols + i * 128 + lane * 4) =
+                packed[j][i];
+    if (lane == 0) exps[b] = e;
+}
+
+}  // namespace phonon

@@ -308,3 +308,18 @@ def erf_gelu(x, device=0):
 def rope(x, heads, position, theta=10000.0, device=0):
     y = np.array(x, np.float32, copy=True)
     return lib().phonon_cuda_rope_interleaved(device, _p(y), y.size, heads, position, theta), y
+
+
+def i8_gemm(a, b, device=0):
+    """D[m][n] = sum_k a[m][k] b[n][k] (int8 in, exact int32 out) on tcgen05."""
+    a = np.ascontiguousarray(a, np.int8)
+    b = np.ascontiguousarray(b, np.int8)
+    m, k = a.shape
+    n = b.shape[0]
+    d = np.zeros((m, n), np.int32)
+    L = lib()
+    L.phonon_cuda_i8_gemm.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t,
+                                      C.c_size_t, C.c_void_p]
+    L.phonon_cuda_i8_gemm.restype = C.c_int
+    check(L.phonon_cuda_i8_gemm(device, _p(a), _p(b), m, n, k, _p(d)), "i8_gemm")
+    return d
