@@ -1,6 +1,7 @@
 // libphonon_cuda host runtime: contexts, KV page pool, step scheduling and
 // the C ABI declared in include/phonon_cuda.h.
 #include "phonon_cuda.h"
+#include "phonon_attention.cuh"
 #include "phonon_gemm.cuh"
 #include "phonon_kernels.cuh"
 
@@ -70,17 +71,25 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// 2-D int8 map [rows][cols] (cols bytes per row) with 128 x 128 boxes.
-bool make_i8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+// 2-D tiled map over [rows][cols] elements, rows `pitch` bytes apart,
+// boxes of box_cols x box_rows, SWIZZLE_128B.
+bool make_map_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t rows, uint64_t cols,
+                 uint64_t pitch, uint32_t box_cols, uint32_t box_rows) {
     EncodeTiledFn fn = encode_tiled();
-    if (!fn || cols % kGemmKTile || reinterpret_cast<uintptr_t>(base) % 16) return false;
+    if (!fn || pitch % 16 || reinterpret_cast<uintptr_t>(base) % 16) return false;
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols};
-    const cuuint32_t box[2] = {kGemmKTile, 128};
+    const cuuint64_t strides[1] = {pitch};
+    const cuuint32_t box[2] = {box_cols, box_rows};
     const cuuint32_t estride[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estride,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    return fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// int8 [rows][cols] (cols bytes per row) in 128-byte x 128-row boxes.
+bool make_i8_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+    if (cols % kGemmKTile) return false;
+    return make_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, rows, cols, cols, kGemmKTile, 128);
 }
 
 bool half_is_finite(uint16_t h) { return ((h >> 10) & 0x1f) != 0x1f; }
@@ -282,6 +291,24 @@ cudaError_t launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, int rows, 
     return cudaGetLastError();
 }
 
+template <bool kBf16>
+cudaError_t launch_attn_tma(const CUtensorMap& tm, const AttnParams& p, int n_layers, int32_t* err, int n_splits,
+                            cudaStream_t s) {
+    static bool configured[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(attn_tma_kernel<kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 AttnTma<kBf16>::kSmem);
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    attn_tma_kernel<kBf16><<<n_splits, kAttnTmaThreads, AttnTma<kBf16>::kSmem, s>>>(tm, p, n_layers, err);
+    return cudaGetLastError();
+}
+
 template <int kCols, bool kLN>
 cudaError_t launch_digits(const float* x, int ldx, const float* ln_w, const float* ln_b, int B, int Bpad,
                           int8_t* digits, int32_t* exps, int32_t* status, cudaStream_t s) {
@@ -316,6 +343,7 @@ struct PhononCuda {
     std::vector<StreamSlot> streams;
     float* d_freq = nullptr;
     int cap_rows = 0, max_splits = 0, meta_ints = 0;
+    float2* d_rope = nullptr;
     float *d_x0 = nullptr, *d_x1 = nullptr, *d_y = nullptr, *d_q = nullptr, *d_a = nullptr,
           *d_h = nullptr, *d_g = nullptr, *d_part = nullptr, *d_stage = nullptr;
     int32_t *d_meta = nullptr, *d_status = nullptr;
@@ -324,6 +352,9 @@ struct PhononCuda {
     int32_t *d_exps = nullptr, *d_err = nullptr;
     CUtensorMap tm_dig512, tm_dig2048;
     bool tensor_ok = false;
+    // KV pool as rows of 64 head dims for TMA page staging
+    CUtensorMap tm_kv;
+    bool attn_tma = false;
     int32_t* h_meta = nullptr;
     float *h_x = nullptr, *h_y = nullptr, *h_stage = nullptr;
     size_t stage_cap = 0;  // floats in d_stage / h_stage
@@ -462,6 +493,7 @@ double linear_bytes(const DevLinear& l) { return static_cast<double>(l.bytes); }
 struct Batch {
     int R = 0, S = 0, U = 0;
     double keys = 0;  // sum over entries of (position + 1)
+    float2* d_rope = nullptr;  // [R][32] (cos, sin) of this batch's positions
     int32_t *d_slot, *d_pos, *d_first, *d_count, *d_updates;
     Split* d_splits;
 };
@@ -543,6 +575,12 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     b.d_count = c->d_meta + 3 * R;
     b.d_splits = reinterpret_cast<Split*>(c->d_meta + 4 * R);
     b.d_updates = c->d_meta + 4 * R + 4 * S;
+    b.d_rope = c->d_rope;
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_OTHER, R * 32 * 12.0);
+        rope_table_kernel<<<(R * 32 + 255) / 256, 256, 0, c->stream>>>(b.d_pos, c->d_freq, R, b.d_rope);
+        CUDA_TRY(cudaGetLastError());
+    }
     if (U > 0) {
         LaunchScope ls(c, PHONON_CUDA_K_OTHER, U * 12.0);
         page_update_kernel<<<(U + 127) / 128, 128, 0, c->stream>>>(c->d_table, kMaxPagesPerStream, b.d_updates, U);
@@ -574,9 +612,14 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l) {
     {
         LaunchScope ls(c, PHONON_CUDA_K_ATTENTION,
                        b.keys * 2.0 * kWidth * esize + act * kWidth + b.S * kHeads * kPartStride * 4.0);
-        if (kv.bf16) attn_partial_kernel<true><<<grid, kAttnWarps * 32, 0, s>>>(ap);
-        else attn_partial_kernel<false><<<grid, kAttnWarps * 32, 0, s>>>(ap);
-        CUDA_TRY(cudaGetLastError());
+        if (c->attn_tma) {
+            CUDA_TRY(kv.bf16 ? launch_attn_tma<true>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.S, s)
+                             : launch_attn_tma<false>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.S, s));
+        } else {
+            if (kv.bf16) attn_partial_kernel<true><<<grid, kAttnWarps * 32, 0, s>>>(ap);
+            else attn_partial_kernel<false><<<grid, kAttnWarps * 32, 0, s>>>(ap);
+            CUDA_TRY(cudaGetLastError());
+        }
     }
     CombineParams cp{};
     cp.part = c->d_part;
@@ -618,7 +661,7 @@ int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, 
     g.q = c->d_q;
     g.slot = b.d_slot;
     g.pos = b.d_pos;
-    g.freq = c->d_freq;
+    g.rope = b.d_rope;
     g.kv = kv;
     g.layer = l;
     {
@@ -705,7 +748,7 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     p.q = c->d_q;
     p.slot = b.d_slot;
     p.pos = b.d_pos;
-    p.freq = c->d_freq;
+    p.rope = b.d_rope;
     p.kv = kv;
     p.layer = l;
     const double act = 4.0 * b.R;  // bytes per activation element across the batch
@@ -822,7 +865,7 @@ void destroy_context(PhononCuda* c) {
     for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
     void* dev[] = {c->kv_pool, c->d_table, c->d_freq, c->d_x0, c->d_x1, c->d_y, c->d_q, c->d_a,
                    c->d_h, c->d_g, c->d_part, c->d_stage, c->d_meta, c->d_status,
-                   c->d_dig512, c->d_dig2048, c->d_exps, c->d_err};
+                   c->d_dig512, c->d_dig2048, c->d_exps, c->d_err, c->d_rope};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_meta, c->h_x, c->h_y, c->h_stage, c->h_status};
@@ -925,11 +968,21 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
     const size_t rows_pad = (rows + 31) / 32 * 32;
     ok = ok && cudaMalloc(&c->d_dig512, rows_pad * kDigits * 512) == cudaSuccess &&
          cudaMalloc(&c->d_dig2048, rows_pad * kDigits * 2048) == cudaSuccess &&
-         cudaMalloc(&c->d_exps, rows_pad * 4) == cudaSuccess && cudaMalloc(&c->d_err, 4) == cudaSuccess;
+         cudaMalloc(&c->d_exps, rows_pad * 4) == cudaSuccess && cudaMalloc(&c->d_err, 4) == cudaSuccess &&
+         cudaMalloc(&c->d_rope, rows * 32 * sizeof(float2)) == cudaSuccess;
     if (!ok) return fail(PHONON_CUDA_OUT_OF_MEMORY);
     if (cudaMemset(c->d_err, 0, 4) != cudaSuccess) return fail(PHONON_CUDA_DEVICE_ERROR);
     c->tensor_ok = make_i8_map(&c->tm_dig512, c->d_dig512, rows_pad * kDigits, 512) &&
                    make_i8_map(&c->tm_dig2048, c->d_dig2048, rows_pad * kDigits, 2048);
+    {
+        // Row r of the pool = 64 dims of (page, layer, k|v, head, slot); a
+        // page-layer K block is rows [(page*L + layer)*256, +128).
+        const uint64_t kv_rows = static_cast<uint64_t>(cfg.pool_pages) * cfg.n_layers * 256;
+        const bool bf16 = cfg.kv_type == PHONON_CUDA_KV_BF16;
+        c->attn_tma = kv_rows < (1ull << 31) &&
+                      make_map_2d(&c->tm_kv, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                  c->kv_pool, kv_rows, kHeadDim, kHeadDim * esize, bf16 ? 64 : 32, 128);
+    }
     if (cudaMemcpy(c->d_freq, freq, sizeof(freq), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemset(c->d_table, 0, static_cast<size_t>(cfg.max_streams) * kMaxPagesPerStream * 4) != cudaSuccess)
         return fail(PHONON_CUDA_DEVICE_ERROR);

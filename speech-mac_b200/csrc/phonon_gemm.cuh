@@ -53,7 +53,7 @@ struct GemmParams {
     float* q;
     const int32_t* slot;
     const int32_t* pos;
-    const float* freq;
+    const float2* rope;    // [B][32] per-step (cos, sin)
     KvView kv;
     int layer;
     int32_t* status;
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const int region = r >> 9, within = r & 511;
                         const int position = p.pos[b];
                         float a = (lane & 1) ? other : v, bb = (lane & 1) ? v : other;
-                        if (region < 2) rope_pair(a, bb, position, p.freq[(within & 63) >> 1]);
+                        if (region < 2) rope_apply(a, bb, p.rope[b * 32 + ((within & 63) >> 1)]);
                         const float mine = (lane & 1) ? bb : a;
                         if (!isfinite(mine)) flag_nonfinite(p.status, b);
                         if (region == 0) {

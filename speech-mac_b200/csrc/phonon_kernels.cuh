@@ -184,6 +184,25 @@ __device__ __forceinline__ void rope_pair(float& a, float& b, int position, floa
     b = rb;
 }
 
+// Rotate with a precomputed (cos, sin) of the pair's phase.
+__device__ __forceinline__ void rope_apply(float& a, float& b, float2 cs) {
+    const float ra = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+    const float rb = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+    a = ra;
+    b = rb;
+}
+
+// Per-step RoPE table: cs[e][i] = (cos, sin) of pos[e] * freq[i] for the
+// 32 frequencies of a 64-wide head; every layer of the step reuses it.
+__global__ void rope_table_kernel(const int32_t* pos, const float* freq, int R, float2* cs) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= R * 32) return;
+    const float phase = __fmul_rn(static_cast<float>(pos[t >> 5]), freq[t & 31]);
+    double sd, cd;
+    sincos(static_cast<double>(phase), &sd, &cd);
+    cs[t] = make_float2(__double2float_rn(cd), __double2float_rn(sd));
+}
+
 // ----------------------------------------------------------------- KV pages
 // A page stores 16 positions of every layer as [layer][k|v][head][slot][dim].
 struct KvView {
@@ -235,7 +254,7 @@ struct GemvParams {
     float* q;                 // [B][512]
     const int32_t* slot;      // [B] stream slot
     const int32_t* pos;       // [B] position
-    const float* freq;        // [32] RoPE frequencies
+    const float2* rope;       // [B][32] per-step (cos, sin)
     KvView kv;
     int layer;
     int32_t* status;          // [B]
@@ -377,7 +396,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
                 const int region = r0 >> 9;          // 0 = q, 1 = k, 2 = v
                 const int within = r0 & 511;
                 const int pos = p.pos[b];
-                if (region < 2) rope_pair(v0, v1, pos, p.freq[(within & 63) >> 1]);
+                if (region < 2) rope_apply(v0, v1, p.rope[b * 32 + ((within & 63) >> 1)]);
                 if (!isfinite(v0) || !isfinite(v1)) flag_nonfinite(p.status, b);
                 if (region == 0) {
                     *reinterpret_cast<float2*>(p.q + static_cast<size_t>(b) * kWidth + within) =
