@@ -63,8 +63,9 @@ class ServingSim:
     arrive with prefix U[64, 2048]; every active stream decodes one position.
     Streams go to the rank holding the fewest KV pages (ties: lowest rank)."""
 
-    def __init__(self, world, seed=2, streams=STREAMS):
+    def __init__(self, world, seed=2, streams=STREAMS, prefix_max=2048):
         self.rng = np.random.default_rng(seed)
+        self.prefix_max = prefix_max
         max_active = streams + streams // 2
         self.world = world
         self.max_active = max_active
@@ -75,7 +76,7 @@ class ServingSim:
             self._arrive()
 
     def _arrive(self):
-        prefix = int(self.rng.integers(64, 2049))
+        prefix = int(self.rng.integers(64, self.prefix_max + 1))
         rank = min(range(self.world), key=lambda r: (self.pages[r], r))
         sid = self.next_id
         self.next_id += 1
@@ -109,12 +110,12 @@ class ServingSim:
 class RankServer:
     """This rank's share of the serving simulation on one libphonon_cuda context."""
 
-    def __init__(self, rt, weights, rank, world, device, total_steps, streams):
+    def __init__(self, rt, weights, rank, world, device, total_steps, streams, prefix_max=2048):
         self.rt = rt
         self.rank = rank
-        self.sim = ServingSim(world, streams=streams)
+        self.sim = ServingSim(world, streams=streams, prefix_max=prefix_max)
         per_rank = (self.sim.max_active + world - 1) // world + 8
-        cap_positions = 2048 + total_steps + 32
+        cap_positions = prefix_max + total_steps + 32
         pool = per_rank * (cap_positions // 16 + 1)
         self.ctx = rt.Context(weights, device=device, max_streams=per_rank, max_batch=per_rank,
                               pool_pages=pool, kv_type=rt.KV_BF16)
@@ -240,7 +241,7 @@ def run_ours(args):
 
     weights = synth.flow_weights(N_LAYERS, seed=0)
     total_steps = 2 * (args.warmup + args.steps) + 8
-    server = RankServer(rt, weights, rank, world, local, total_steps, args.streams)
+    server = RankServer(rt, weights, rank, world, local, total_steps, args.streams, args.prefix_max)
     ctx = server.ctx
     stream = torch.cuda.ExternalStream(ctx.cuda_stream())
     max_b = server.sim.max_active + 8
@@ -326,7 +327,8 @@ def run_ours(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "configs[3]" if args.streams == STREAMS else f"configs[3] shape, {args.streams} streams",
+            "config": {"workload": "configs[3]" if (args.streams, args.prefix_max) == (STREAMS, 2048)
+                       else f"configs[3] shape, {args.streams} streams, prefix <= {args.prefix_max}",
                        "streams": args.streams, "layers": N_LAYERS,
                        "context": "prefix U[64,2048] seed 2, synthetic K/V",
                        "arrivals": "Poisson(1) arrivals and departures per step, seed 2",
@@ -550,6 +552,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--quick", action="store_true", help="skip the configs[0]/[1] extras")
+    ap.add_argument("--prefix-max", type=int, default=2048,
+                    help="upper end of the prefix distribution (2048 = configs[3]; smaller for profiling)")
     ap.add_argument("--streams", type=int, default=STREAMS,
                     help="concurrent streams at start (512 = configs[3]; smaller for profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
