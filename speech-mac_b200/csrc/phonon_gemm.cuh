@@ -30,11 +30,18 @@ namespace phonon {
 constexpr int kGemmM = 128;       // weight rows per tile (MMA M)
 constexpr int kGemmN = 128;       // digit rows per tile (MMA N) = 32 streams x 4 slices
 constexpr int kGemmKTile = 128;   // bytes of K per stage
-constexpr int kGemmStages = 4;
+constexpr int kGemmStages = 3;
 constexpr int kGemmThreads = 192;
 constexpr int kGemmStreamsPerTile = kGemmN / 4;
 constexpr int kDigits = 4;
-constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmM + kGemmN) * kGemmKTile + 256;
+// Per-tile stream data staged by the epilogue warps (exponents, pages, RoPE).
+struct GemmTileMeta {
+    int32_t exp[kGemmN / 4];
+    int32_t pos[kGemmN / 4];
+    int32_t page[kGemmN / 4];
+    float2 cs[kGemmN / 4][32];
+};
+constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmM + kGemmN) * kGemmKTile + 256 + static_cast<int>(sizeof(GemmTileMeta));
 constexpr long long kWaitBudgetCycles = 4ll << 30;  // ~2 s at 1.9 GHz
 
 enum GemmEpilogue : int { GEPI_RAW = 0, GEPI_RESID = 1, GEPI_GELU = 2, GEPI_QKV = 3 };
@@ -161,7 +168,7 @@ __device__ __forceinline__ float pow2f(int e) {  // exact 2^e for normal exponen
 }
 
 template <int kEpi>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, 2)
     i8_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    GemmParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -171,6 +178,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kGemmStages * kGemmN * kGemmKTile);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kGemmStages + 1);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    GemmTileMeta* meta = reinterpret_cast<GemmTileMeta*>(smem + kGemmStages * (kGemmM + kGemmN) * kGemmKTile + 256);
     const uint32_t full0 = smem_addr(bars), empty0 = full0 + 8 * kGemmStages, accum = full0 + 16 * kGemmStages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -231,13 +239,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (ok) umma_commit(accum);
     } else if (warp >= 2) {
         // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows.
+        // While the MMAs run, stage this tile's per-stream data in shared
+        // memory and prefetch the residual, so that draining the accumulator
+        // issues no dependent global loads.
         const int quarter = warp & 3;
         const int r = m_tile * kGemmM + quarter * 32 + lane;
+        const int et = threadIdx.x - 64;  // 0..127 over the epilogue warps
+        const int b0 = n_tile * kGemmStreamsPerTile;
+        if constexpr (kEpi != GEPI_RAW) {
+            if (et < kGemmStreamsPerTile) {
+                const int b = b0 + et;
+                const bool live = b < p.B;
+                meta->exp[et] = live ? p.exps[b] : 0;
+                if constexpr (kEpi == GEPI_QKV) {
+                    const int position = live ? p.pos[b] : 0;
+                    meta->pos[et] = position;
+                    meta->page[et] = live ? p.kv.table[static_cast<size_t>(p.slot[b]) * p.kv.max_pages + position / kPage] : 0;
+                }
+            }
+            if constexpr (kEpi == GEPI_QKV) {
+                for (int i = et; i < kGemmStreamsPerTile * 32; i += 128) {
+                    const int b = b0 + i / 32;
+                    meta->cs[i / 32][i % 32] = b < p.B ? p.rope[b * 32 + (i % 32)] : make_float2(1.0f, 0.0f);
+                }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+        float res[kGemmStreamsPerTile];
+        if constexpr (kEpi == GEPI_RESID) {
+#pragma unroll
+            for (int t = 0; t < kGemmStreamsPerTile; ++t)
+                res[t] = (b0 + t < p.B && r < p.rows) ? p.res[static_cast<size_t>(b0 + t) * p.ldres + r] : 0.0f;
+        }
+        const float scale = (kEpi == GEPI_RAW || r >= p.rows) ? 1.0f : p.row_scale[r];
         const bool have = __all_sync(kFull, mbar_wait(accum, 0, p.error, failed));
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (have) {
-            const float scale = (kEpi == GEPI_RAW || r >= p.rows) ? 1.0f : p.row_scale[r];
-#pragma unroll 1
+#pragma unroll
             for (int c0 = 0; c0 < kGemmN; c0 += 32) {
                 uint32_t d[32];
                 tmem_load32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c0, d);
@@ -252,9 +290,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // 8 streams per 32 columns: recombine the four digit slices.
 #pragma unroll
                 for (int t = 0; t < 8; ++t) {
-                    const int b = n_tile * kGemmStreamsPerTile + (c0 >> 2) + t;
+                    const int tt = (c0 >> 2) + t;  // stream within the tile
+                    const int b = b0 + tt;
                     const bool live = b < p.B;
-                    const int e = live ? p.exps[b] : 0;
+                    const int e = meta->exp[tt];
                     float v = 0.0f;
 #pragma unroll
                     for (int j = 0; j < kDigits; ++j)
@@ -265,23 +304,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const float other = __shfl_xor_sync(kFull, v, 1);
                         if (!live || r >= p.rows) continue;
                         const int region = r >> 9, within = r & 511;
-                        const int position = p.pos[b];
                         float a = (lane & 1) ? other : v, bb = (lane & 1) ? v : other;
-                        if (region < 2) rope_apply(a, bb, p.rope[b * 32 + ((within & 63) >> 1)]);
+                        if (region < 2) rope_apply(a, bb, meta->cs[tt][(within & 63) >> 1]);
                         const float mine = (lane & 1) ? bb : a;
                         if (!isfinite(mine)) flag_nonfinite(p.status, b);
                         if (region == 0) {
                             p.q[static_cast<size_t>(b) * kWidth + within] = mine;
                         } else {
-                            const int page = p.kv.table[static_cast<size_t>(p.slot[b]) * p.kv.max_pages + position / kPage];
-                            const long long off = kv_offset(p.kv, page, p.layer, region - 1, within >> 6,
+                            const int position = meta->pos[tt];
+                            const long long off = kv_offset(p.kv, meta->page[tt], p.layer, region - 1, within >> 6,
                                                             position % kPage) + (within & 63);
                             if (p.kv.bf16) static_cast<uint16_t*>(p.kv.pool)[off] = f32_to_bf16(mine);
                             else static_cast<float*>(p.kv.pool)[off] = mine;
                         }
                     } else {
                         if (!live || r >= p.rows) continue;
-                        if constexpr (kEpi == GEPI_RESID) v = __fadd_rn(p.res[static_cast<size_t>(b) * p.ldres + r], v);
+                        if constexpr (kEpi == GEPI_RESID) v = __fadd_rn(res[tt], v);
                         if constexpr (kEpi == GEPI_GELU) {
                             if (!isfinite(v)) flag_nonfinite(p.status, b);
                             v = gelu_erf(v);
