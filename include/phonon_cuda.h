@@ -162,6 +162,29 @@ int phonon_cuda_linear_apply(PhononCudaLinear *linear, const float *x, size_t ba
 int phonon_cuda_linear_apply_device(PhononCudaLinear *linear, const float *x_dev, size_t batch,
                                     const float *bias_dev, float *y_dev, int32_t *status_dev,
                                     void *cuda_stream);
+/* Allocation-free variant of phonon_cuda_linear_apply_device, for callers
+ * that may not allocate device memory once they are running: a host thread
+ * inside a real-time audio callback, code that runs while a CUDA graph is
+ * being captured, or an engine whose device memory budget was fixed at start
+ * up. It has no counterpart in the reference (the reference's linears are
+ * host SGEMMs, src/phonon_transformer.c:253-313).
+ *
+ * It runs the tensor-core path: the batch is digit-sliced into a scratch
+ * array that the library owns as a file-scope device array (sized for
+ * PHONON_CUDA_NOALLOC_MAX_BATCH streams of up to 2048 columns, about 513 KB,
+ * held by every device that loads the library until exit), then contracted
+ * by the int8 tcgen05 kernel. No cudaMalloc, cudaFree or other allocating
+ * routine is called. Requirements: the linear has Q8_0 weights whose
+ * 32-blocks share one scale per row and 512 or 2048 columns; batch <=
+ * PHONON_CUDA_NOALLOC_MAX_BATCH (else PHONON_CUDA_CAPACITY). The first call
+ * on a device looks up the scratch address on that device; make that first
+ * call before any stream capture. Every call shares the one scratch array:
+ * calls that overlap on the GPU (different streams or threads without
+ * ordering) race and corrupt each other's results. */
+#define PHONON_CUDA_NOALLOC_MAX_BATCH 64
+int phonon_cuda_linear_apply_device_noalloc(PhononCudaLinear *linear, const float *x_dev,
+                                            size_t batch, const float *bias_dev, float *y_dev,
+                                            int32_t *status_dev, void *cuda_stream);
 /* Bytes of the device copy (int8 plane + fp16 scales, or bf16). */
 size_t phonon_cuda_linear_bytes(const PhononCudaLinear *linear);
 

@@ -1580,6 +1580,98 @@ int phonon_cuda_linear_apply(PhononCudaLinear* l, const float* x, size_t batch, 
     return PHONON_CUDA_OK;
 }
 
+}  // extern "C"
+
+// ------------------------------------------- allocation-free tensor linear
+// Scratch of phonon_cuda_linear_apply_device_noalloc: digit rows of up to
+// PHONON_CUDA_NOALLOC_MAX_BATCH streams x 2048 columns, their exponents and
+// the tile error flag. Host code must not use these names as addresses: the
+// device address comes from cudaGetSymbolAddress on each device.
+constexpr int kNoallocRows = kDigits * PHONON_CUDA_NOALLOC_MAX_BATCH;
+static __device__ __align__(256) int8_t g_noalloc_digits[kNoallocRows * 2048];
+static __device__ __align__(256) int32_t g_noalloc_exps[PHONON_CUDA_NOALLOC_MAX_BATCH];
+static __device__ __align__(256) int32_t g_noalloc_error[1];
+
+namespace {
+
+struct NoallocScratch {
+    bool ready = false;
+    int8_t* digits = nullptr;
+    int32_t* exps = nullptr;
+    int32_t* error = nullptr;
+    CUtensorMap map512, map2048;
+};
+
+// One-time set-up per device (the device must be current): resolve the
+// scratch addresses and describe the digit rows for TMA. Idempotent.
+int noalloc_scratch(int device, NoallocScratch** out) {
+    static std::mutex mu;
+    static NoallocScratch table[kMaxDevices];
+    if (device < 0 || device >= kMaxDevices) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(mu);
+    NoallocScratch& t = table[device];
+    if (!t.ready) {
+        void* d = nullptr;
+        void* e = nullptr;
+        void* f = nullptr;
+        if (cudaGetSymbolAddress(&d, g_noalloc_digits) != cudaSuccess ||
+            cudaGetSymbolAddress(&e, g_noalloc_exps) != cudaSuccess ||
+            cudaGetSymbolAddress(&f, g_noalloc_error) != cudaSuccess)
+            return PHONON_CUDA_DEVICE_ERROR;
+        t.digits = static_cast<int8_t*>(d);
+        t.exps = static_cast<int32_t*>(e);
+        t.error = static_cast<int32_t*>(f);
+        if (!make_i8_map(&t.map512, t.digits, kNoallocRows, 512) ||
+            !make_i8_map(&t.map2048, t.digits, kNoallocRows, 2048))
+            return PHONON_CUDA_DEVICE_ERROR;
+        t.ready = true;
+    }
+    *out = &t;
+    return PHONON_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int phonon_cuda_linear_apply_device_noalloc(PhononCudaLinear* l, const float* x_dev, size_t batch,
+                                            const float* bias_dev, float* y_dev, int32_t* status_dev,
+                                            void* cuda_stream) {
+    if (!l || !x_dev || !y_dev || batch == 0) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (batch > PHONON_CUDA_NOALLOC_MAX_BATCH) {
+        std::fprintf(stderr, "phonon_cuda_linear_apply_device_noalloc: batch %zu exceeds the scratch limit of %d\n",
+                     batch, PHONON_CUDA_NOALLOC_MAX_BATCH);
+        return PHONON_CUDA_CAPACITY;
+    }
+    const DevLinear& w = l->lin;
+    if (!w.tensor || (w.cols != 512 && w.cols != 2048)) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(l->device);
+    if (st) return st;
+    NoallocScratch* sc = nullptr;
+    if ((st = noalloc_scratch(l->device, &sc))) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+    const int B = static_cast<int>(batch), Bpad = (B + 31) / 32 * 32;
+    // The scratch keeps the previous call's contents: clear the error flag.
+    CUDA_TRY(cudaMemsetAsync(sc->error, 0, sizeof(int32_t), s));
+    if (w.cols == 512)
+        CUDA_TRY((launch_digits<512, false>(x_dev, 512, nullptr, nullptr, B, Bpad, sc->digits, sc->exps, status_dev, s)));
+    else
+        CUDA_TRY((launch_digits<2048, false>(x_dev, 2048, nullptr, nullptr, B, Bpad, sc->digits, sc->exps, status_dev, s)));
+    GemmParams p{};
+    p.rows = w.rows;
+    p.K = w.cols;
+    p.B = B;
+    p.row_scale = w.row_scale;
+    p.exps = sc->exps;
+    p.y = y_dev;
+    p.ldy = w.rows;
+    p.status = status_dev;
+    p.error = sc->error;
+    p.bias = bias_dev;
+    CUDA_TRY(launch_gemm<GEPI_STORE>(w.tmap, w.cols == 512 ? sc->map512 : sc->map2048, w.rows, kDigits * Bpad, p, s));
+    return PHONON_CUDA_OK;
+}
+
 int phonon_cuda_linear_apply_device(PhononCudaLinear* l, const float* x_dev, size_t batch, const float* bias_dev,
                                     float* y_dev, int32_t* status_dev, void* cuda_stream) {
     if (!l || !x_dev || !y_dev || batch == 0 || batch > 65536) return PHONON_CUDA_INVALID_ARGUMENT;

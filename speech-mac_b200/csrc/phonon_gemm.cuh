@@ -44,7 +44,7 @@ struct GemmTileMeta {
 constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmM + kGemmN) * kGemmKTile + 256 + static_cast<int>(sizeof(GemmTileMeta));
 constexpr long long kWaitBudgetCycles = 4ll << 30;  // ~2 s at 1.9 GHz
 
-enum GemmEpilogue : int { GEPI_RAW = 0, GEPI_RESID = 1, GEPI_GELU = 2, GEPI_QKV = 3 };
+enum GemmEpilogue : int { GEPI_RAW = 0, GEPI_RESID = 1, GEPI_GELU = 2, GEPI_QKV = 3, GEPI_STORE = 4 };
 
 struct GemmParams {
     int rows;              // weight rows (M)
@@ -67,6 +67,7 @@ struct GemmParams {
     int32_t* raw;          // GEPI_RAW: D as [rows][n_total] int32
     int n_total;
     int32_t* error;        // set when a bounded wait expires
+    const float* bias;     // GEPI_STORE: optional [rows]
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -320,6 +321,9 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
                     } else {
                         if (!live || r >= p.rows) continue;
                         if constexpr (kEpi == GEPI_RESID) v = __fadd_rn(res[tt], v);
+                        if constexpr (kEpi == GEPI_STORE) {
+                            if (p.bias) v = __fadd_rn(v, p.bias[r]);
+                        }
                         if constexpr (kEpi == GEPI_GELU) {
                             if (!isfinite(v)) flag_nonfinite(p.status, b);
                             v = gelu_erf(v);
