@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
+    pdl_wait();  // q, the page table and the metadata come from earlier kernels
 
     if (warp == kAttnHeadsPerCta) {
         if (lane == 0) {
@@ -173,6 +174,7 @@ __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * s);
     }
+    pdl_trigger();
     float* out = p.part + (static_cast<size_t>(blockIdx.x) * kHeads + head) * kPartStride;
     *reinterpret_cast<float2*>(out + 2 + 2 * lane) = make_float2(a0, a1);
     if (lane == 0) {

@@ -15,6 +15,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <utility>
 #include <vector>
 
 using namespace phonon;
@@ -37,6 +38,23 @@ constexpr int kTensorMinBatch = 32;  // streams from which projections run on tc
             return PHONON_CUDA_DEVICE_ERROR;                                                 \
         }                                                                                    \
     } while (0)
+
+// Launch with programmatic dependent launch allowed: the kernel may begin
+// while the previous kernel of the stream drains (see pdl_wait/pdl_trigger).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------ device linears
 struct DevLinear {
@@ -228,8 +246,7 @@ cudaError_t launch_gemv_t(const GemvParams& p, cudaStream_t s) {
         }
     }
     const int rows_per_cta = kGemvWarps * kRowsPerWarp;
-    kern<<<(p.rows + rows_per_cta - 1) / rows_per_cta, kGemvWarps * 32, smem, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3((p.rows + rows_per_cta - 1) / rows_per_cta), dim3(kGemvWarps * 32), smem, s, p);
 }
 
 template <bool kQ8, int kChunks, bool kLN, int kEpi>
@@ -287,8 +304,7 @@ cudaError_t launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, int rows, 
         configured[dev] = true;
     }
     dim3 grid((rows + kGemmM - 1) / kGemmM, (n_digit_rows + kGemmN - 1) / kGemmN);
-    i8_gemm_kernel<kEpi><<<grid, kGemmThreads, kGemmSmem, s>>>(tw, tx, p);
-    return cudaGetLastError();
+    return launch_pdl(i8_gemm_kernel<kEpi>, grid, dim3(kGemmThreads), kGemmSmem, s, tw, tx, p);
 }
 
 template <bool kBf16>
@@ -305,15 +321,15 @@ cudaError_t launch_attn_tma(const CUtensorMap& tm, const AttnParams& p, int n_la
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    attn_tma_kernel<kBf16><<<n_splits, kAttnTmaThreads, AttnTma<kBf16>::kSmem, s>>>(tm, p, n_layers, err);
-    return cudaGetLastError();
+    return launch_pdl(attn_tma_kernel<kBf16>, dim3(n_splits), dim3(kAttnTmaThreads), AttnTma<kBf16>::kSmem, s, tm, p,
+                      n_layers, err);
 }
 
 template <int kCols, bool kLN>
 cudaError_t launch_digits(const float* x, int ldx, const float* ln_w, const float* ln_b, int B, int Bpad,
                           int8_t* digits, int32_t* exps, int32_t* status, cudaStream_t s) {
-    digits_kernel<kCols, kLN><<<(Bpad + 7) / 8, 256, 0, s>>>(x, ldx, ln_w, ln_b, B, Bpad, digits, exps, status);
-    return cudaGetLastError();
+    return launch_pdl(digits_kernel<kCols, kLN>, dim3((Bpad + 7) / 8), dim3(256), 0, s, x, ldx, ln_w, ln_b, B, Bpad,
+                      digits, exps, status);
 }
 
 }  // namespace
@@ -578,13 +594,13 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     b.d_rope = c->d_rope;
     {
         LaunchScope ls(c, PHONON_CUDA_K_OTHER, R * 32 * 12.0);
-        rope_table_kernel<<<(R * 32 + 255) / 256, 256, 0, c->stream>>>(b.d_pos, c->d_freq, R, b.d_rope);
-        CUDA_TRY(cudaGetLastError());
+        CUDA_TRY(launch_pdl(rope_table_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, c->stream,
+                            static_cast<const int32_t*>(b.d_pos), static_cast<const float*>(c->d_freq), R, b.d_rope));
     }
     if (U > 0) {
         LaunchScope ls(c, PHONON_CUDA_K_OTHER, U * 12.0);
-        page_update_kernel<<<(U + 127) / 128, 128, 0, c->stream>>>(c->d_table, kMaxPagesPerStream, b.d_updates, U);
-        CUDA_TRY(cudaGetLastError());
+        CUDA_TRY(launch_pdl(page_update_kernel, dim3((U + 127) / 128), dim3(128), 0, c->stream, c->d_table,
+                            kMaxPagesPerStream, static_cast<const int32_t*>(b.d_updates), U));
     }
     *out = b;
     return PHONON_CUDA_OK;
@@ -616,9 +632,8 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l) {
             CUDA_TRY(kv.bf16 ? launch_attn_tma<true>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.S, s)
                              : launch_attn_tma<false>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.S, s));
         } else {
-            if (kv.bf16) attn_partial_kernel<true><<<grid, kAttnWarps * 32, 0, s>>>(ap);
-            else attn_partial_kernel<false><<<grid, kAttnWarps * 32, 0, s>>>(ap);
-            CUDA_TRY(cudaGetLastError());
+            CUDA_TRY(kv.bf16 ? launch_pdl(attn_partial_kernel<true>, dim3(grid), dim3(kAttnWarps * 32), 0, s, ap)
+                             : launch_pdl(attn_partial_kernel<false>, dim3(grid), dim3(kAttnWarps * 32), 0, s, ap));
         }
     }
     CombineParams cp{};
@@ -630,9 +645,9 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l) {
     cp.status = c->d_status;
     {
         LaunchScope ls(c, PHONON_CUDA_K_COMBINE, b.S * kHeads * kPartStride * 4.0 + act * kWidth);
-        attn_combine_kernel<<<static_cast<unsigned>((static_cast<long long>(b.R) * kHeads + kAttnWarps - 1) / kAttnWarps),
-                              kAttnWarps * 32, 0, s>>>(cp);
-        CUDA_TRY(cudaGetLastError());
+        CUDA_TRY(launch_pdl(attn_combine_kernel,
+                            dim3(static_cast<unsigned>((static_cast<long long>(b.R) * kHeads + kAttnWarps - 1) / kAttnWarps)),
+                            dim3(kAttnWarps * 32), 0, s, cp));
     }
     return PHONON_CUDA_OK;
 }

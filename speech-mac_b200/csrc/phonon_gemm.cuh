@@ -207,14 +207,23 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 
     if (warp == 0 && lane == 0) {
         // TMA producer: weight tile rows [m_tile*128, +128), digit rows [n_tile*128, +128).
+        // Weight tiles of the first stages do not depend on the previous
+        // kernel: issue them before waiting for it.
+        const int pre = nk < kGemmStages ? nk : kGemmStages;
+        for (int kt = 0; kt < pre; ++kt) {
+            mbar_expect_tx(full0 + 8 * kt, (kGemmM + kGemmN) * kGemmKTile);
+            tma_load_2d(smem_addr(sA + kt * kGemmM * kGemmKTile), &tm_w, kt * kGemmKTile, m_tile * kGemmM,
+                        full0 + 8 * kt);
+        }
+        pdl_wait();
         for (int kt = 0; kt < nk; ++kt) {
             const int s = kt % kGemmStages;
-            if (kt >= kGemmStages &&
-                !mbar_wait(empty0 + 8 * s, ((kt / kGemmStages) - 1) & 1, p.error, failed))
-                break;
-            mbar_expect_tx(full0 + 8 * s, (kGemmM + kGemmN) * kGemmKTile);
-            tma_load_2d(smem_addr(sA + s * kGemmM * kGemmKTile), &tm_w, kt * kGemmKTile, m_tile * kGemmM,
-                        full0 + 8 * s);
+            if (kt >= pre) {
+                if (!mbar_wait(empty0 + 8 * s, ((kt / kGemmStages) - 1) & 1, p.error, failed)) break;
+                mbar_expect_tx(full0 + 8 * s, (kGemmM + kGemmN) * kGemmKTile);
+                tma_load_2d(smem_addr(sA + s * kGemmM * kGemmKTile), &tm_w, kt * kGemmKTile, m_tile * kGemmM,
+                            full0 + 8 * s);
+            }
             tma_load_2d(smem_addr(sB + s * kGemmN * kGemmKTile), &tm_x, kt * kGemmKTile, n_tile * kGemmN,
                         full0 + 8 * s);
         }
@@ -247,6 +256,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         const int r = m_tile * kGemmM + quarter * 32 + lane;
         const int et = threadIdx.x - 64;  // 0..127 over the epilogue warps
         const int b0 = n_tile * kGemmStreamsPerTile;
+        pdl_wait();  // exponents, residuals and positions come from earlier kernels
         if constexpr (kEpi != GEPI_RAW) {
             if (et < kGemmStreamsPerTile) {
                 const int b = b0 + et;
@@ -275,6 +285,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         const float scale = (kEpi == GEPI_RAW || r >= p.rows) ? 1.0f : p.row_scale[r];
         const bool have = __all_sync(kFull, mbar_wait(accum, 0, p.error, failed));
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        pdl_trigger();
         if (have) {
 #pragma unroll
             for (int c0 = 0; c0 < kGemmN; c0 += 32) {
@@ -353,6 +364,8 @@ __global__ void __launch_bounds__(256) digits_kernel(const float* __restrict__ x
                                                      int32_t* __restrict__ exps, int32_t* status) {
     __shared__ __align__(16) float row[8][kLN ? kCols : 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.x * 8 + warp;
     if (b >= Bpad) return;
     constexpr int per_lane = kCols / 32;

@@ -34,6 +34,14 @@ constexpr int kStatusNonFinite = 2;  // PHONON_CUDA_NON_FINITE
 
 enum Epilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_GELU = 2, EPI_QKV = 3 };
 
+// Programmatic dependent launch: kernels of a step are launched so that the
+// next one may start while this one drains. pdl_wait() blocks until the
+// previous kernel of the stream has completed and its writes are visible
+// (call it before touching anything it produced); pdl_trigger() lets the
+// next kernel begin launching. Both are no-ops without the launch attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float bf16_to_f32(uint16_t b) {
     return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }
@@ -195,6 +203,8 @@ __device__ __forceinline__ void rope_apply(float& a, float& b, float2 cs) {
 // Per-step RoPE table: cs[e][i] = (cos, sin) of pos[e] * freq[i] for the
 // 32 frequencies of a 64-wide head; every layer of the step reuses it.
 __global__ void rope_table_kernel(const int32_t* pos, const float* freq, int R, float2* cs) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= R * 32) return;
     const float phase = __fmul_rn(static_cast<float>(pos[t >> 5]), freq[t & 31]);
@@ -303,6 +313,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
         }
     }
 
+    pdl_wait();  // weights above are independent of the previous kernel
     for (int b0 = 0; b0 < p.B; b0 += kBT) {
         const int nb = min(kBT, p.B - b0);
         __syncthreads();
@@ -384,6 +395,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
 #pragma unroll
             for (int bb = 0; bb < kBT; ++bb) acc[rr][bb] = warp_sum(acc[rr][bb]);
 
+        if (b0 + kBT >= p.B) pdl_trigger();
         // Lane bb finishes stream b0+bb for both rows of the pair.
 #pragma unroll
         for (int bb = 0; bb < kBT; ++bb) {
@@ -490,6 +502,7 @@ constexpr int kPartStride = 2 + kHeadDim;
 template <bool kBf16>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_partial_kernel(AttnParams p) {
     const int lane = threadIdx.x & 31;
+    pdl_wait();
     const long long item = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     if (item >= static_cast<long long>(p.n_splits) * kHeads) return;
     const int s_idx = static_cast<int>(item >> 3), head = static_cast<int>(item & 7);
@@ -604,6 +617,8 @@ struct CombineParams {
 // One warp per (stream, head): out = sum_s e^(m_s-M) a_s / sum_s e^(m_s-M) l_s.
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_combine_kernel(CombineParams p) {
     const int lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_trigger();
     const long long item = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     if (item >= static_cast<long long>(p.B) * kHeads) return;
     const int b = static_cast<int>(item >> 3), head = static_cast<int>(item & 7);
@@ -631,6 +646,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_combine_kernel(CombinePa
 // ------------------------------------------------------------- small kernels
 // Apply page-table updates: (slot, index, page) triples.
 __global__ void page_update_kernel(int32_t* table, int max_pages, const int32_t* updates, int n) {
+    pdl_wait();
+    pdl_trigger();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) table[static_cast<size_t>(updates[3 * i]) * max_pages + updates[3 * i + 1]] = updates[3 * i + 2];
 }
