@@ -223,6 +223,8 @@ def run_ours(args):
     if world > 1:
         import datetime
 
+        os.environ["NCCL_DEBUG"] = "WARN"  # rank 0 prints exactly one line on stdout
+
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
