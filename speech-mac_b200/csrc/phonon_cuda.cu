@@ -607,9 +607,11 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
 }
 
 // Enqueue layer `l` for the batch: in -> out (out != in).
-int enqueue_attention(PhononCuda* c, const Batch& b, int l);
+int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out = false);
 
-int enqueue_attention(PhononCuda* c, const Batch& b, int l) {
+// Split-K attention then the split merge. With digits_out the merge writes
+// the digit rows of the attention output (tensor-core path) instead of fp32.
+int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out) {
     cudaStream_t s = c->stream;
     const KvView kv = kv_view(c);
     const double act = 4.0 * b.R;
@@ -643,6 +645,12 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l) {
     cp.B = b.R;
     cp.out = c->d_a;
     cp.status = c->d_status;
+    if (digits_out) {
+        const int Bpad = (b.R + 31) / 32 * 32;
+        LaunchScope ls(c, PHONON_CUDA_K_COMBINE, b.S * kHeads * kPartStride * 4.0 + kDigits * Bpad * 512.0);
+        CUDA_TRY(launch_pdl(attn_combine_digits_kernel, dim3(Bpad), dim3(256), 0, s, cp, Bpad, c->d_dig512, c->d_exps));
+        return PHONON_CUDA_OK;
+    }
     {
         LaunchScope ls(c, PHONON_CUDA_K_COMBINE, b.S * kHeads * kPartStride * 4.0 + act * kWidth);
         CUDA_TRY(launch_pdl(attn_combine_kernel,
@@ -683,15 +691,10 @@ int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, 
         LaunchScope ls(c, PHONON_CUDA_K_QKV, 1536.0 * 512 + dig * 512 + act * kWidth + B * 2.0 * kWidth * esize);
         CUDA_TRY(launch_gemm<GEPI_QKV>(L.qkv.tmap, c->tm_dig512, 1536, nd, g, s));
     }
-    // 2. attention
-    int st = enqueue_attention(c, b, l);
+    // 2. attention; the combine writes the digit rows of the attention output
+    int st = enqueue_attention(c, b, l, true);
     if (st) return st;
     // 3. h = x + attn Wout^T
-    {
-        LaunchScope ls(c, PHONON_CUDA_K_OUT, act * kWidth + dig * 512);
-        CUDA_TRY((launch_digits<512, false>(c->d_a, kWidth, nullptr, nullptr, B, Bpad, c->d_dig512, c->d_exps,
-                                            c->d_status, s)));
-    }
     GemmParams go = g;
     go.rows = 512;
     go.K = 512;

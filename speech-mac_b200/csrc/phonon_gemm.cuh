@@ -354,6 +354,85 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     }
 }
 
+// Exponent e of a row whose largest magnitude is mx: |x| * 2^-e < 1/2.
+// Rows below 2^-91 get e = 0 and all-zero digits (keeps every 2^(e-28) a
+// normal float).
+__device__ __forceinline__ int digit_exponent(float mx, bool& zero) {
+    int e = 0;
+    frexpf(mx, &e);
+    e += 1;
+    zero = !(mx > 0.0f) || e < -90;
+    return zero ? 0 : e;
+}
+
+// Four base-128 digits of r = x * 2^-e (|r| < 1/2), packed little-endian.
+__device__ __forceinline__ uint32_t slice_digits(float r) {
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < kDigits; ++j) {
+        r *= 128.0f;
+        const float dj = rintf(r);
+        r -= dj;  // exact: the fractional part of r
+        packed |= (static_cast<uint32_t>(static_cast<int32_t>(dj)) & 0xffu) << (8 * j);
+    }
+    return packed;
+}
+
+// Attention combine fused with digit slicing (tensor-core path): one CTA per
+// stream (8 warps = 8 heads) merges the head's splits like attn_combine_kernel,
+// then the CTA takes the row maximum over all 512 outputs and writes the
+// stream's four digit rows and exponent. CTAs for padded streams write zeros.
+__global__ void __launch_bounds__(256) attn_combine_digits_kernel(CombineParams p, int Bpad, int8_t* __restrict__ digits,
+                                                                  int32_t* __restrict__ exps) {
+    __shared__ float head_max[kHeads];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x, head = warp;
+    pdl_wait();
+    pdl_trigger();
+    int8_t* drow = digits + static_cast<size_t>(4 * b) * kWidth + head * kHeadDim + 2 * lane;
+    if (b >= p.B) {
+#pragma unroll
+        for (int j = 0; j < kDigits; ++j) *reinterpret_cast<uint16_t*>(drow + j * kWidth) = 0;
+        if (threadIdx.x == 0) exps[b] = 0;
+        return;
+    }
+    const int first = p.first[b], n = p.count[b];
+    float mx = -INFINITY;
+    for (int s = 0; s < n; ++s) mx = fmaxf(mx, p.part[(static_cast<size_t>(first + s) * kHeads + head) * kPartStride]);
+    float total = 0.0f, a0 = 0.0f, a1 = 0.0f;
+    for (int s = 0; s < n; ++s) {
+        const float* pp = p.part + (static_cast<size_t>(first + s) * kHeads + head) * kPartStride;
+        const float w = pp[0] == -INFINITY ? 0.0f : expf(pp[0] - mx);
+        total = fmaf(w, pp[1], total);
+        const float2 av = *reinterpret_cast<const float2*>(pp + 2 + 2 * lane);
+        a0 = fmaf(w, av.x, a0);
+        a1 = fmaf(w, av.y, a1);
+    }
+    bool ok = total > 0.0f && isfinite(total);
+    const float inv = __fdiv_rn(1.0f, total);
+    const float o0 = __fmul_rn(a0, inv), o1 = __fmul_rn(a1, inv);
+    ok &= isfinite(o0) && isfinite(o1);
+    if (!__all_sync(kFull, ok) && lane == 0) flag_nonfinite(p.status, b);
+    float m = ok ? fmaxf(fabsf(o0), fabsf(o1)) : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+    if (lane == 0) head_max[head] = m;
+    __syncthreads();
+    float row_max = 0.0f;
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) row_max = fmaxf(row_max, head_max[h]);
+    bool zero;
+    const int e = digit_exponent(row_max, zero);
+    const float down = pow2f(-e);
+    const uint32_t d0 = (zero || !ok) ? 0u : slice_digits(o0 * down);
+    const uint32_t d1 = (zero || !ok) ? 0u : slice_digits(o1 * down);
+#pragma unroll
+    for (int j = 0; j < kDigits; ++j)
+        *reinterpret_cast<uint16_t*>(drow + j * kWidth) =
+            static_cast<uint16_t>(((d0 >> (8 * j)) & 0xffu) | (((d1 >> (8 * j)) & 0xffu) << 8));
+    if (threadIdx.x == 0) exps[b] = e;
+}
+
 // Digit slicing (see the header comment). One warp per stream row of width
 // kCols; with kLN the row is first layer-normalised exactly as in
 // warp_layernorm512. Writes digit rows 4b..4b+3 and e_b; rows of streams
@@ -406,13 +485,8 @@ __global__ void __launch_bounds__(256) digits_kernel(const float* __restrict__ x
         if (lane == 0) flag_nonfinite(status, b);
         mx = 0.0f;
     }
-    int e = 0;
-    frexpf(mx, &e);  // mx < 2^e
-    e += 1;          // |x| * 2^-e < 1/2
-    if (e < -90) {   // rows below 2^-91: digits of zero (keeps every 2^(e-28) normal)
-        mx = 0.0f;
-        e = 0;
-    }
+    bool zero;
+    const int e = digit_exponent(mx, zero);
     const float down = pow2f(-e);
     uint32_t packed[kDigits][per_lane / 4];
 #pragma unroll
@@ -421,14 +495,10 @@ __global__ void __launch_bounds__(256) digits_kernel(const float* __restrict__ x
         for (int j = 0; j < kDigits; ++j) packed[j][i] = 0;
 #pragma unroll
     for (int i = 0; i < per_lane; ++i) {
-        float r = (finite_ok && mx > 0.0f) ? v[i] * down : 0.0f;  // exact scaling by a power of two
+        // exact scaling by a power of two, then the four digits
+        const uint32_t d = (finite_ok && !zero) ? slice_digits(v[i] * down) : 0u;
 #pragma unroll
-        for (int j = 0; j < kDigits; ++j) {
-            r *= 128.0f;
-            const float dj = rintf(r);
-            r -= dj;  // exact: the fractional part of r
-            packed[j][i / 4] |= (static_cast<uint32_t>(static_cast<int32_t>(dj)) & 0xffu) << (8 * (i % 4));
-        }
+        for (int j = 0; j < kDigits; ++j) packed[j][i / 4] |= ((d >> (8 * j)) & 0xffu) << (8 * (i % 4));
     }
 #pragma unroll
     for (int j = 0; j < kDigits; ++j)

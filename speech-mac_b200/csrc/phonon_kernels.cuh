@@ -69,8 +69,10 @@ __device__ __forceinline__ void flag_nonfinite(int32_t* status, int b) {
 // (src/phonon_transformer.c:90-98).
 __device__ __forceinline__ void ln_merge(float n, float add, float a_mean, float a_m2, float& mean,
                                          float& m2) {
-    float total = __fadd_rn(n, add);
-    float c = total != 0.0f ? __fdiv_rn(add, total) : 0.0f;
+    // n and add are compile-time constants once the callers' loops unroll,
+    // so this IEEE division (and its rounding) happens at compile time.
+    float total = n + add;
+    float c = total != 0.0f ? add / total : 0.0f;
     float delta = __fsub_rn(a_mean, mean);
     mean = __fadd_rn(mean, __fmul_rn(c, delta));
     m2 = __fadd_rn(m2, __fadd_rn(a_m2, __fmul_rn(__fmul_rn(__fmul_rn(delta, delta), c), n)));
@@ -96,7 +98,7 @@ __device__ __forceinline__ bool warp_layernorm512(const float* __restrict__ x,
         float v = x[chunk * 64 + j * 4 + sub];
         ok &= isfinite(v);
         float delta = __fsub_rn(v, mean);
-        mean = __fadd_rn(mean, __fmul_rn(delta, __fdiv_rn(1.0f, static_cast<float>(j + 1))));
+        mean = __fadd_rn(mean, __fmul_rn(delta, 1.0f / static_cast<float>(j + 1)));  // folded at compile time
         m2 = __fadd_rn(m2, __fmul_rn(delta, __fsub_rn(v, mean)));
     }
     float s1[3][4], s2[3][4], cnt[3] = {0.0f, 0.0f, 0.0f};
@@ -138,7 +140,7 @@ __device__ __forceinline__ bool warp_layernorm512(const float* __restrict__ x,
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         float total = n + 128.0f;
-        float c = __fdiv_rn(128.0f, total);
+        float c = 128.0f / total;  // 1, 1/2, 1/3, 1/4: folded at compile time
         float delta = __fsub_rn(s1[0][k], mu);
         mu = __fmaf_rn(c, delta, mu);
         q = __fadd_rn(q, __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), c), n, s2[0][k]));
