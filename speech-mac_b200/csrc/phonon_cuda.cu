@@ -375,6 +375,19 @@ struct PhononCuda {
     float *h_x = nullptr, *h_y = nullptr, *h_stage = nullptr;
     size_t stage_cap = 0;  // floats in d_stage / h_stage
     int32_t* h_status = nullptr;
+    // Replay of repeated step shapes: the step's kernels are captured into a
+    // CUDA graph the second time the same (R, S, input, output) shape comes
+    // in a row and replayed while it repeats (a batch-1 decode keeps its
+    // split count for 16 positions).
+    struct StepShape {
+        int R = -1, S = -1;
+        const void* in = nullptr;
+        const void* out = nullptr;
+        bool operator==(const StepShape& o) const { return R == o.R && S == o.S && in == o.in && out == o.out; }
+    };
+    StepShape last_shape, graph_shape;
+    cudaGraphExec_t graph_exec = nullptr;
+    uint64_t graph_kernels = 0;
     // launch accounting and live profiling
     uint64_t launches = 0;
     bool prof_on = false;
@@ -840,9 +853,72 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
 // Run layers [0, L) over the batch, reading `in` and leaving the result in
 // `final_out`. cancel (optional) is polled before each layer and once after;
 // `polls_per_layer` extra polls emulate the reference's in-layer schedule.
+void drop_graph(PhononCuda* c) {
+    if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
+    c->graph_exec = nullptr;
+    c->graph_shape = PhononCuda::StepShape{};
+    c->last_shape = PhononCuda::StepShape{};
+}
+
+int enqueue_layers_direct(PhononCuda* c, const Batch& b, const float* in, float* final_out) {
+    const int L = static_cast<int>(c->cfg.n_layers);
+    const float* cur = in;
+    for (int l = 0; l < L; ++l) {
+        float* out = (l == L - 1) ? final_out : ((cur == c->d_x0) ? c->d_x1 : c->d_x0);
+        const int st = enqueue_layer(c, b, l, cur, out);
+        if (st != PHONON_CUDA_OK) return st;
+        cur = out;
+    }
+    return PHONON_CUDA_OK;
+}
+
+// All layers of an uncancellable, unprofiled step, through the step graph
+// when the shape repeats; any capture problem falls back to direct launches.
+int enqueue_layers_graphed(PhononCuda* c, const Batch& b, const float* in, float* final_out) {
+    PhononCuda::StepShape shape;
+    shape.R = b.R;
+    shape.S = b.S;
+    shape.in = in;
+    shape.out = final_out;
+    if (c->graph_exec && c->graph_shape == shape) {
+        CUDA_TRY(cudaGraphLaunch(c->graph_exec, c->stream));
+        c->launches += c->graph_kernels;
+        return PHONON_CUDA_OK;
+    }
+    if (!(c->last_shape == shape)) {
+        c->last_shape = shape;
+        return enqueue_layers_direct(c, b, in, final_out);
+    }
+    cudaGraph_t g = nullptr;
+    const uint64_t before = c->launches;
+    if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return enqueue_layers_direct(c, b, in, final_out);
+    }
+    const int st = enqueue_layers_direct(c, b, in, final_out);
+    const cudaError_t end = cudaStreamEndCapture(c->stream, &g);
+    cudaGraphExec_t exec = nullptr;
+    if (st != PHONON_CUDA_OK || end != cudaSuccess || !g || cudaGraphInstantiate(&exec, g, 0) != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        c->launches = before;
+        return enqueue_layers_direct(c, b, in, final_out);
+    }
+    cudaGraphDestroy(g);
+    if (c->graph_exec) cudaGraphExecDestroy(c->graph_exec);
+    c->graph_exec = exec;
+    c->graph_shape = shape;
+    c->graph_kernels = c->launches - before;
+    c->launches = before;
+    CUDA_TRY(cudaGraphLaunch(c->graph_exec, c->stream));
+    c->launches += c->graph_kernels;
+    return PHONON_CUDA_OK;
+}
+
 int enqueue_stack(PhononCuda* c, const Batch& b, const float* in, float* final_out,
                   PhononCudaCancelPoll cancel, void* cctx, const std::vector<int>* polls_per_layer,
                   bool* cancelled) {
+    if (!cancel && !c->prof_on) return enqueue_layers_graphed(c, b, in, final_out);
     const int L = static_cast<int>(c->cfg.n_layers);
     const float* cur = in;
     for (int l = 0; l < L; ++l) {
@@ -875,6 +951,7 @@ void destroy_context(PhononCuda* c) {
     if (!c) return;
     cudaSetDevice(c->cfg.device);
     if (c->stream) cudaStreamSynchronize(c->stream);
+    drop_graph(c);
     for (auto& L : c->layers) free_layer(L);
     for (auto& r : c->prof_pending) {
         cudaEventDestroy(r.a);
@@ -1035,6 +1112,7 @@ int phonon_cuda_set_layer(PhononCuda* c, uint32_t layer, const PhononCudaLayer* 
     int st = set_device(c->cfg.device);
     if (st) return st;
     if (cudaStreamSynchronize(c->stream) != cudaSuccess) return PHONON_CUDA_DEVICE_ERROR;
+    drop_graph(c);  // captured kernels hold the old weight pointers
     return load_layer(&c->layers[layer], *weights);
 }
 
