@@ -216,7 +216,8 @@ typedef enum {
     PHONON_CUDA_K_UP = 4,        /* LN2 + FFN up + GELU */
     PHONON_CUDA_K_DOWN = 5,      /* FFN down + residual */
     PHONON_CUDA_K_OTHER = 6,     /* page-table updates, KV fills */
-    PHONON_CUDA_K_COUNT = 7
+    PHONON_CUDA_K_FUSED = 7,     /* whole step in one persistent launch (small batches) */
+    PHONON_CUDA_K_COUNT = 8
 } PhononCudaKernelClass;
 /* Enable (1) or disable (0) per-launch event timing; enabling clears the
  * totals. While enabled, every step accumulates per class: device time (ms),
@@ -226,6 +227,22 @@ int phonon_cuda_profile_enable(PhononCuda *ctx, int enable);
 int phonon_cuda_profile_read(PhononCuda *ctx, double *ms, double *bytes, uint64_t *launches);
 /* Kernels this context has launched since creation. */
 uint64_t phonon_cuda_launch_count(PhononCuda *ctx);
+
+/* ---- step paths by batch size ----
+ * A decode step (phonon_cuda_step / phonon_cuda_step_device without a cancel
+ * poll) of at most fused_max_batch streams runs as ONE persistent launch
+ * that keeps a CTA on every SM for all layers; larger batches run one launch
+ * per stage, with the projections on the tensor cores from tensor_min_batch
+ * streams up. Defaults: PHONON_CUDA_FUSED_MAX_BATCH and 32. fused_max_batch
+ * = 0 disables the persistent step; values above PHONON_CUDA_FUSED_MAX_BATCH
+ * or tensor_min_batch = 0 are PHONON_CUDA_INVALID_ARGUMENT. All paths give
+ * the same results within the tolerances of the reference's tests (the
+ * persistent and per-stage GEMV paths bit for bit). The persistent step needs
+ * Q8_0 weights, cooperative launch and enough shared memory for the batch
+ * (bf16 KV: up to 64 streams; fp32 KV: up to 48); otherwise the per-stage
+ * path runs. */
+#define PHONON_CUDA_FUSED_MAX_BATCH 64
+int phonon_cuda_set_batch_paths(PhononCuda *ctx, uint32_t fused_max_batch, uint32_t tensor_min_batch);
 
 const char *phonon_cuda_status_string(int status);
 

@@ -4,6 +4,7 @@
 #include "phonon_attention.cuh"
 #include "phonon_gemm.cuh"
 #include "phonon_kernels.cuh"
+#include "phonon_persist.cuh"
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -28,6 +29,7 @@ constexpr int kMaxPagesPerStream = PHONON_CUDA_MAX_POSITIONS / kPage;  // 512
 constexpr int kSplitTarget = 640;   // ~8 warps per split: fills 148 SMs several times over
 constexpr int kPrefillChunk = 256;  // rows per prefill pass
 constexpr int kTensorMinBatch = 32;  // streams from which projections run on tcgen05
+constexpr int kMaxSms = 1024;        // bound on the SM count (persistent split table)
 
 #define CUDA_TRY(expr)                                                                       \
     do {                                                                                     \
@@ -371,6 +373,14 @@ struct PhononCuda {
     // KV pool as rows of 64 head dims for TMA page staging
     CUtensorMap tm_kv;
     bool attn_tma = false;
+    // Whole-step persistent kernel (batches up to fused_max streams)
+    int sms = 0, smem_optin = 0;
+    bool persist_ok = false;         // device and weights allow it
+    uint32_t fused_max = kPersistMaxBatch;
+    uint32_t tensor_min = kTensorMinBatch;
+    PersistLayer* d_players = nullptr;  // [n_layers]
+    unsigned* d_bar = nullptr;
+    unsigned bar_epoch = 0;
     int32_t* h_meta = nullptr;
     float *h_x = nullptr, *h_y = nullptr, *h_stage = nullptr;
     size_t stage_cap = 0;  // floats in d_stage / h_stage
@@ -521,9 +531,11 @@ double linear_bytes(const DevLinear& l) { return static_cast<double>(l.bytes); }
 // planned over the pages each entry attends.
 struct Batch {
     int R = 0, S = 0, U = 0;
+    bool persist = false;  // whole step in step_persist_kernel
     double keys = 0;  // sum over entries of (position + 1)
     float2* d_rope = nullptr;  // [R][32] (cos, sin) of this batch's positions
     int32_t *d_slot, *d_pos, *d_first, *d_count, *d_updates;
+    int32_t* d_cta_split = nullptr;  // persistent path: [sms + 1]
     Split* d_splits;
 };
 
@@ -563,14 +575,51 @@ void release_pages(PhononCuda* c, uint32_t s) {
     st.length = 0;
 }
 
+// Shared-memory plan of step_persist_kernel for R streams on G SMs: the
+// union of the stage-B page ring and the activation rows of a group, then
+// the two weight buffers (QKV|up and out|down rows of one CTA), then the
+// mbarriers and flags. False when it exceeds the per-CTA opt-in limit.
+struct PersistShape {
+    int n_groups = 0, smem = 0, off_x = 0, off_w0 = 0, off_w1 = 0, off_norm = 0, off_bar = 0;
+};
+
+bool persist_shape(int R, int G, int smem_limit, bool bf16, PersistShape* out) {
+    PersistShape sh;
+    sh.n_groups = (R + kPersistGroup - 1) / kPersistGroup;
+    const int nct = G / sh.n_groups;
+    if (R < 1 || nct < 1) return false;
+    const int ring = bf16 ? PersistAttn<true>::kBytes : PersistAttn<false>::kBytes;
+    const int x_bytes = std::max(ring, kPersistGroup * kFfn * 4);
+    const int w0 = std::max(persist_cta_rows(PM_QKV, nct) * persist_row_bytes(PM_QKV),
+                            persist_cta_rows(PM_UP, nct) * persist_row_bytes(PM_UP));
+    const int w1 = std::max(persist_cta_rows(PM_OUT, nct) * persist_row_bytes(PM_OUT),
+                            persist_cta_rows(PM_DOWN, nct) * persist_row_bytes(PM_DOWN));
+    sh.off_x = 0;
+    sh.off_w0 = x_bytes;
+    sh.off_w1 = sh.off_w0 + w0;
+    sh.off_norm = sh.off_w1 + w1;
+    sh.off_bar = sh.off_norm + kPersistNormBytes;
+    sh.smem = sh.off_bar + 128 + 1024;  // barriers and flags; 1024-byte alignment slack
+    *out = sh;
+    return sh.smem <= smem_limit;
+}
+
+// The whole step of this batch runs as one persistent launch.
+bool use_persist(const PhononCuda* c, int R, bool cancel) {
+    if (!c->persist_ok || cancel || R < 1 || static_cast<uint32_t>(R) > c->fused_max) return false;
+    PersistShape sh;
+    return persist_shape(R, c->sms, c->smem_optin, c->cfg.kv_type == PHONON_CUDA_KV_BF16, &sh);
+}
+
 // Pack metadata for entries (slot[e], pos[e]) into pinned memory, upload it
-// and apply page-table updates. Entry e attends over pos[e] + 1 keys.
+// and apply page-table updates. Entry e attends over pos[e] + 1 keys. With
+// device_prep false the RoPE table and the page updates are left to the
+// persistent kernel.
 int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vector<int32_t>& pos,
-                 const std::vector<int32_t>& updates, Batch* out) {
+                 const std::vector<int32_t>& updates, Batch* out, bool device_prep = true) {
     const int R = static_cast<int>(slot.size());
     long long total_pages = 0;
     for (int e = 0; e < R; ++e) total_pages += pos[e] / kPage + 1;
-    const long long pps = std::max<long long>(1, (total_pages + kSplitTarget - 1) / kSplitTarget);
     int32_t* m = c->h_meta;
     int32_t *h_slot = m, *h_pos = m + R, *h_first = m + 2 * R, *h_count = m + 3 * R;
     Split* h_splits = reinterpret_cast<Split*>(m + 4 * R);
@@ -578,20 +627,63 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     for (int e = 0; e < R; ++e) {
         h_slot[e] = slot[e];
         h_pos[e] = pos[e];
-        const int n_keys = pos[e] + 1, n_pages = pos[e] / kPage + 1;
-        h_first[e] = S;
-        int ns = 0;
-        for (int pb = 0; pb < n_pages; pb += static_cast<int>(pps), ++ns, ++S) {
-            if (S >= c->max_splits) return PHONON_CUDA_INVALID_ARGUMENT;
-            h_splits[S] = Split{e, pb, std::min<int>(static_cast<int>(pps), n_pages - pb), n_keys};
+        h_first[e] = 0;
+        h_count[e] = 0;
+    }
+    // Batches above PHONON_CUDA_FUSED_MAX_BATCH: runs of pps pages per split,
+    // one CTA each. Smaller batches (any path, so that the persistent and
+    // per-stage steps merge the same splits): the pages of all entries in
+    // (entry, page) order cut into at most one balanced chunk per SM (>=
+    // kPersistMinChunk pages); a chunk is one split per entry segment it
+    // covers, and chunk k's splits are [cta_split[k], cta_split[k+1]).
+    const bool chunked = R <= PHONON_CUDA_FUSED_MAX_BATCH && c->sms > 0;
+    const int G = chunked ? c->sms : 0;
+    std::vector<int32_t> cta_split;
+    if (!chunked) {
+        const long long pps = std::max<long long>(1, (total_pages + kSplitTarget - 1) / kSplitTarget);
+        for (int e = 0; e < R; ++e) {
+            const int n_keys = pos[e] + 1, n_pages = pos[e] / kPage + 1;
+            h_first[e] = S;
+            int ns = 0;
+            for (int pb = 0; pb < n_pages; pb += static_cast<int>(pps), ++ns, ++S) {
+                if (S >= c->max_splits) return PHONON_CUDA_INVALID_ARGUMENT;
+                h_splits[S] = Split{e, pb, std::min<int>(static_cast<int>(pps), n_pages - pb), n_keys};
+            }
+            h_count[e] = ns;
         }
-        h_count[e] = ns;
+    } else {
+        const long long chunks =
+            std::max<long long>(1, std::min<long long>(G, total_pages / kPersistMinChunk));
+        cta_split.assign(static_cast<size_t>(G) + 1, 0);
+        long long done = 0;  // pages before entry e
+        int e = 0, pb = 0;   // cursor: page pb of entry e
+        for (long long k = 0; k < chunks; ++k) {
+            cta_split[k] = S;
+            long long left = (k + 1) * total_pages / chunks - (done + pb);  // pages of chunk k
+            while (left > 0) {
+                const int n_pages = pos[e] / kPage + 1;
+                const int take = static_cast<int>(std::min<long long>(left, n_pages - pb));
+                if (S >= c->max_splits) return PHONON_CUDA_INVALID_ARGUMENT;
+                if (h_count[e] == 0) h_first[e] = S;
+                h_splits[S++] = Split{e, pb, take, pos[e] + 1};
+                h_count[e]++;
+                pb += take;
+                left -= take;
+                if (pb == n_pages) {
+                    done += n_pages;
+                    ++e;
+                    pb = 0;
+                }
+            }
+        }
+        for (long long k = chunks; k <= G; ++k) cta_split[k] = S;
     }
     const int U = static_cast<int>(updates.size() / 3);
     int32_t* h_upd = m + 4 * R + 4 * S;
-    if (4 * R + 4 * S + 3 * U > c->meta_ints) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (4 * R + 4 * S + 3 * U + G + 1 > c->meta_ints) return PHONON_CUDA_INVALID_ARGUMENT;
     std::memcpy(h_upd, updates.data(), updates.size() * 4);
-    const size_t bytes = static_cast<size_t>(4 * R + 4 * S + 3 * U) * 4;
+    if (chunked) std::memcpy(h_upd + 3 * U, cta_split.data(), cta_split.size() * 4);
+    const size_t bytes = static_cast<size_t>(4 * R + 4 * S + 3 * U + (chunked ? G + 1 : 0)) * 4;
     CUDA_TRY(cudaMemcpyAsync(c->d_meta, c->h_meta, bytes, cudaMemcpyHostToDevice, c->stream));
     Batch b;
     b.R = R;
@@ -604,7 +696,13 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     b.d_count = c->d_meta + 3 * R;
     b.d_splits = reinterpret_cast<Split*>(c->d_meta + 4 * R);
     b.d_updates = c->d_meta + 4 * R + 4 * S;
+    b.d_cta_split = b.d_updates + 3 * U;
     b.d_rope = c->d_rope;
+    b.persist = !device_prep;
+    if (!device_prep) {
+        *out = b;
+        return PHONON_CUDA_OK;
+    }
     {
         LaunchScope ls(c, PHONON_CUDA_K_OTHER, R * 32 * 12.0);
         CUDA_TRY(launch_pdl(rope_table_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, c->stream,
@@ -759,7 +857,7 @@ int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, 
 
 int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* out) {
     const DevLayer& L = c->layers[l];
-    if (c->tensor_ok && b.R >= kTensorMinBatch && L.qkv.tensor && L.out.tensor && L.up.tensor && L.down.tensor)
+    if (c->tensor_ok && b.R >= static_cast<int>(c->tensor_min) && L.qkv.tensor && L.out.tensor && L.up.tensor && L.down.tensor)
         return enqueue_layer_tensor(c, b, l, in, out);
     const bool q8 = L.q8;
     cudaStream_t s = c->stream;
@@ -915,9 +1013,78 @@ int enqueue_layers_graphed(PhononCuda* c, const Batch& b, const float* in, float
     return PHONON_CUDA_OK;
 }
 
+template <bool kBf16>
+cudaError_t launch_persist_t(PhononCuda* c, const PersistParams& pp, int smem) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(c->sms));
+    cfg.blockDim = dim3(kPersistThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = c->stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;  // all CTAs resident: the grid barriers rely on it
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, step_persist_kernel<kBf16>, c->tm_kv, pp);
+}
+
+// Every layer of the batch in one step_persist_kernel launch.
+int enqueue_persist(PhononCuda* c, const Batch& b, const float* in, float* final_out) {
+    const bool bf16 = c->cfg.kv_type == PHONON_CUDA_KV_BF16;
+    PersistShape sh;
+    if (!persist_shape(b.R, c->sms, c->smem_optin, bf16, &sh)) return PHONON_CUDA_INVALID_ARGUMENT;
+    const int L = static_cast<int>(c->cfg.n_layers);
+    PersistParams pp{};
+    pp.layers = c->d_players;
+    pp.n_layers = L;
+    pp.R = b.R;
+    pp.S = b.S;
+    pp.U = b.U;
+    pp.n_groups = sh.n_groups;
+    pp.in = in;
+    pp.out = final_out;
+    pp.xbuf0 = in == c->d_x1 ? c->d_x0 : c->d_x1;
+    pp.xbuf1 = in == c->d_x1 ? c->d_x1 : c->d_x0;
+    pp.h = c->d_h;
+    pp.g = c->d_g;
+    pp.q = c->d_q;
+    pp.part = c->d_part;
+    pp.status = c->d_status;
+    pp.error = c->d_err;
+    pp.barrier = c->d_bar;
+    pp.barrier_base = c->bar_epoch;
+    pp.slot = b.d_slot;
+    pp.pos = b.d_pos;
+    pp.first = b.d_first;
+    pp.count = b.d_count;
+    pp.updates = b.d_updates;
+    pp.splits = b.d_splits;
+    pp.cta_split = b.d_cta_split;
+    pp.freq = c->d_freq;
+    pp.rope = c->d_rope;
+    pp.kv = kv_view(c);
+    pp.off_x = sh.off_x;
+    pp.off_w0 = sh.off_w0;
+    pp.off_w1 = sh.off_w1;
+    pp.off_norm = sh.off_norm;
+    pp.off_bar = sh.off_bar;
+    double weights = 0.0;
+    for (const DevLayer& D : c->layers)
+        weights += linear_bytes(D.qkv) + linear_bytes(D.out) + linear_bytes(D.up) + linear_bytes(D.down);
+    const double esize = bf16 ? 2.0 : 4.0;
+    const double bytes = weights + L * (b.keys + b.R) * 2.0 * kWidth * esize + b.R * 2.0 * kWidth * 4.0;
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_FUSED, bytes);
+        CUDA_TRY(bf16 ? launch_persist_t<true>(c, pp, sh.smem) : launch_persist_t<false>(c, pp, sh.smem));
+    }
+    c->bar_epoch += static_cast<unsigned>(c->sms) * static_cast<unsigned>(1 + 5 * L);
+    return PHONON_CUDA_OK;
+}
+
 int enqueue_stack(PhononCuda* c, const Batch& b, const float* in, float* final_out,
                   PhononCudaCancelPoll cancel, void* cctx, const std::vector<int>* polls_per_layer,
                   bool* cancelled) {
+    if (b.persist) return enqueue_persist(c, b, in, final_out);
     if (!cancel && !c->prof_on) return enqueue_layers_graphed(c, b, in, final_out);
     const int L = static_cast<int>(c->cfg.n_layers);
     const float* cur = in;
@@ -947,6 +1114,40 @@ int set_device(int device) {
     return PHONON_CUDA_OK;
 }
 
+// Upload the per-layer weight pointers of step_persist_kernel and decide
+// whether it can run: Q8_0 weights in the GEMV layout, TMA page staging,
+// cooperative launch, and one resident CTA per SM at the largest plan.
+int refresh_persist(PhononCuda* c) {
+    std::vector<PersistLayer> pl(c->layers.size());
+    bool ok = c->attn_tma && c->sms > 0;
+    for (size_t l = 0; l < c->layers.size(); ++l) {
+        const DevLayer& D = c->layers[l];
+        const DevLinear* lin[4] = {&D.qkv, &D.out, &D.up, &D.down};
+        for (int m = 0; m < 4; ++m) {
+            ok = ok && D.q8 && lin[m]->fast && lin[m]->plane && lin[m]->scales;
+            pl[l].plane[m] = static_cast<const uint8_t*>(lin[m]->plane);
+            pl[l].scales[m] = lin[m]->scales;
+        }
+        pl[l].norms = D.norms;
+    }
+    CUDA_TRY(cudaMemcpy(c->d_players, pl.data(), sizeof(PersistLayer) * pl.size(), cudaMemcpyHostToDevice));
+    int coop = 0;
+    CUDA_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->cfg.device));
+    ok = ok && coop;
+    if (ok) {
+        const bool bf16 = c->cfg.kv_type == PHONON_CUDA_KV_BF16;
+        const void* fn = bf16 ? reinterpret_cast<const void*>(step_persist_kernel<true>)
+                              : reinterpret_cast<const void*>(step_persist_kernel<false>);
+        int resident = 0;
+        ok = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, c->smem_optin) == cudaSuccess &&
+             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, fn, kPersistThreads, c->smem_optin) == cudaSuccess &&
+             resident >= 1;
+        cudaGetLastError();
+    }
+    c->persist_ok = ok;
+    return PHONON_CUDA_OK;
+}
+
 void destroy_context(PhononCuda* c) {
     if (!c) return;
     cudaSetDevice(c->cfg.device);
@@ -960,7 +1161,8 @@ void destroy_context(PhononCuda* c) {
     for (cudaEvent_t e : c->prof_events) cudaEventDestroy(e);
     void* dev[] = {c->kv_pool, c->d_table, c->d_freq, c->d_x0, c->d_x1, c->d_y, c->d_q, c->d_a,
                    c->d_h, c->d_g, c->d_part, c->d_stage, c->d_meta, c->d_status,
-                   c->d_dig512, c->d_dig2048, c->d_exps, c->d_err, c->d_rope};
+                   c->d_dig512, c->d_dig2048, c->d_exps, c->d_err, c->d_rope,
+                   c->d_players, c->d_bar};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_meta, c->h_x, c->h_y, c->h_stage, c->h_status};
@@ -1041,7 +1243,7 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
     c->cap_rows = static_cast<int>(std::max<uint32_t>(cfg.max_batch, kPrefillChunk));
     c->max_splits = kSplitTarget + c->cap_rows + 16;
     const int U_max = c->cap_rows * 2 + kMaxPagesPerStream + 16;
-    c->meta_ints = 4 * c->cap_rows + 4 * c->max_splits + 3 * U_max;
+    c->meta_ints = 4 * c->cap_rows + 4 * c->max_splits + 3 * U_max + kMaxSms + 1;
     const size_t rows = static_cast<size_t>(c->cap_rows);
     bool ok = cudaMalloc(&c->kv_pool, static_cast<size_t>(cfg.pool_pages) * c->page_elems * esize) == cudaSuccess &&
               cudaMalloc(&c->d_table, static_cast<size_t>(cfg.max_streams) * kMaxPagesPerStream * 4) == cudaSuccess &&
@@ -1078,6 +1280,12 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
                       make_map_2d(&c->tm_kv, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                                   c->kv_pool, kv_rows, kHeadDim, kHeadDim * esize, bf16 ? 64 : 32, 128);
     }
+    if (cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, cfg.device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&c->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, cfg.device) != cudaSuccess ||
+        cudaMalloc(&c->d_players, sizeof(PersistLayer) * cfg.n_layers) != cudaSuccess ||
+        cudaMalloc(&c->d_bar, 4) != cudaSuccess || cudaMemset(c->d_bar, 0, 4) != cudaSuccess || c->sms > kMaxSms)
+        return fail(PHONON_CUDA_OUT_OF_MEMORY);
+    if ((st = refresh_persist(c))) return fail(st);
     if (cudaMemcpy(c->d_freq, freq, sizeof(freq), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemset(c->d_table, 0, static_cast<size_t>(cfg.max_streams) * kMaxPagesPerStream * 4) != cudaSuccess)
         return fail(PHONON_CUDA_DEVICE_ERROR);
@@ -1113,7 +1321,8 @@ int phonon_cuda_set_layer(PhononCuda* c, uint32_t layer, const PhononCudaLayer* 
     if (st) return st;
     if (cudaStreamSynchronize(c->stream) != cudaSuccess) return PHONON_CUDA_DEVICE_ERROR;
     drop_graph(c);  // captured kernels hold the old weight pointers
-    return load_layer(&c->layers[layer], *weights);
+    if ((st = load_layer(&c->layers[layer], *weights))) return st;
+    return refresh_persist(c);
 }
 
 int phonon_cuda_stream_alloc(PhononCuda* c, uint32_t capacity, uint32_t* stream) {
@@ -1206,6 +1415,16 @@ uint64_t phonon_cuda_launch_count(PhononCuda* c) {
     return c->launches;
 }
 
+int phonon_cuda_set_batch_paths(PhononCuda* c, uint32_t fused_max_batch, uint32_t tensor_min_batch) {
+    if (!c || fused_max_batch > PHONON_CUDA_FUSED_MAX_BATCH || tensor_min_batch < 1) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    c->fused_max = fused_max_batch;
+    c->tensor_min = tensor_min_batch;
+    drop_graph(c);  // a captured step holds the old path choice
+    return PHONON_CUDA_OK;
+}
+
 }  // extern "C"
 
 namespace {
@@ -1245,10 +1464,12 @@ int finish_sync(PhononCuda* c, uint32_t n) {
     CUDA_TRY(cudaMemcpyAsync(&err, c->d_err, 4, cudaMemcpyDeviceToHost, c->stream));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     prof_collect(c);
-    if (err) {  // a tensor-core tile gave up waiting: report, then clear for the next call
+    if (err) {  // a bounded device wait expired: report, then clear for the next call
         cudaMemsetAsync(c->d_err, 0, 4, c->stream);
+        if (c->d_bar) cudaMemsetAsync(c->d_bar, 0, 4, c->stream);
+        c->bar_epoch = 0;
         cudaStreamSynchronize(c->stream);
-        std::fprintf(stderr, "phonon_cuda: tensor-core tile wait expired\n");
+        std::fprintf(stderr, "phonon_cuda: a device wait expired\n");
         return PHONON_CUDA_DEVICE_ERROR;
     }
     return PHONON_CUDA_OK;
@@ -1269,7 +1490,7 @@ int phonon_cuda_step(PhononCuda* c, uint32_t n, const uint32_t* streams, const u
     PageUndo undo{c, {}};
     if ((st = prepare_decode(c, n, streams, positions, slot, pos, updates, undo, true))) return st;
     Batch b;
-    if ((st = upload_batch(c, slot, pos, updates, &b))) {
+    if ((st = upload_batch(c, slot, pos, updates, &b, !use_persist(c, static_cast<int>(n), cancel != nullptr)))) {
         undo.rollback();
         return st;
     }
@@ -1308,7 +1529,7 @@ int phonon_cuda_step_device(PhononCuda* c, uint32_t n, const uint32_t* streams, 
     PageUndo undo{c, {}};
     if ((st = prepare_decode(c, n, streams, positions, slot, pos, updates, undo, true))) return st;
     Batch b;
-    if ((st = upload_batch(c, slot, pos, updates, &b))) {
+    if ((st = upload_batch(c, slot, pos, updates, &b, !use_persist(c, static_cast<int>(n), false)))) {
         undo.rollback();
         return st;
     }

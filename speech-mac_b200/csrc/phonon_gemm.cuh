@@ -397,16 +397,14 @@ __global__ void __launch_bounds__(256) attn_combine_digits_kernel(CombineParams 
         return;
     }
     const int first = p.first[b], n = p.count[b];
-    float mx = -INFINITY;
-    for (int s = 0; s < n; ++s) mx = fmaxf(mx, p.part[(static_cast<size_t>(first + s) * kHeads + head) * kPartStride]);
-    float total = 0.0f, a0 = 0.0f, a1 = 0.0f;
+    float M = -INFINITY, total = 0.0f, a0 = 0.0f, a1 = 0.0f;
     for (int s = 0; s < n; ++s) {
         const float* pp = p.part + (static_cast<size_t>(first + s) * kHeads + head) * kPartStride;
-        const float w = pp[0] == -INFINITY ? 0.0f : expf(pp[0] - mx);
-        total = fmaf(w, pp[1], total);
+        const MergeWeights w = merge_weights(M, pp[0]);
+        total = merge_fold(total, w, pp[1]);
         const float2 av = *reinterpret_cast<const float2*>(pp + 2 + 2 * lane);
-        a0 = fmaf(w, av.x, a0);
-        a1 = fmaf(w, av.y, a1);
+        a0 = merge_fold(a0, w, av.x);
+        a1 = merge_fold(a1, w, av.y);
     }
     bool ok = total > 0.0f && isfinite(total);
     const float inv = __fdiv_rn(1.0f, total);

@@ -19,6 +19,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace phonon {
 
 constexpr int kWidth = 512;
@@ -64,97 +66,143 @@ __device__ __forceinline__ void flag_nonfinite(int32_t* status, int b) {
 }
 
 // ------------------------------------------------------------------ LayerNorm
-// Merge `add` samples (a_mean, a_m2) into (mean, m2) holding n samples, in the
+// Merge ADD samples (a_mean, a_m2) into (mean, m2) holding N samples, in the
 // reference's unfused order: mean += c*delta; m2 += a_m2 + delta*delta*c*n
-// (src/phonon_transformer.c:90-98).
-__device__ __forceinline__ void ln_merge(float n, float add, float a_mean, float a_m2, float& mean,
-                                         float& m2) {
-    // n and add are compile-time constants once the callers' loops unroll,
-    // so this IEEE division (and its rounding) happens at compile time.
-    float total = n + add;
-    float c = total != 0.0f ? add / total : 0.0f;
-    float delta = __fsub_rn(a_mean, mean);
+// with c = ADD / (N + ADD) (src/phonon_transformer.c:90-98). N and ADD are
+// template constants, so c is a compile-time constant (the reference's
+// cascade only ever divides by these counts).
+template <int N, int ADD>
+__device__ __forceinline__ void ln_merge(float a_mean, float a_m2, float& mean, float& m2) {
+    constexpr float n = static_cast<float>(N);
+    constexpr float c = (N + ADD) != 0 ? static_cast<float>(ADD) / static_cast<float>(N + ADD) : 0.0f;
+    const float delta = __fsub_rn(a_mean, mean);
     mean = __fadd_rn(mean, __fmul_rn(c, delta));
     m2 = __fadd_rn(m2, __fadd_rn(a_m2, __fmul_rn(__fmul_rn(__fmul_rn(delta, delta), c), n)));
 }
 
+// Moments of one 512-wide row held by a warp, lane (chunk*4 + l) holding
+// elements chunk*64 + j*4 + l (j = 0..15), as the reference's moments_512
+// (src/phonon_transformer.c:99-151): a 16-step Welford per lane; then every
+// lane replays, for each of the four lanes l of a chunk, the cascade that
+// folds the 8 chunk results (16 samples each) through three levels of a
+// binary counter, and finally merges the four lanes. The schedule below is
+// that cascade unrolled. Returns the mean and 1/sqrt(var + eps).
+__device__ __forceinline__ void ln_moments512(const float (&v)[16], float eps, float& mu_out, float& scale_out) {
+    constexpr float kRecip[16] = {1.0f / 1,  1.0f / 2,  1.0f / 3,  1.0f / 4,  1.0f / 5,  1.0f / 6,
+                                  1.0f / 7,  1.0f / 8,  1.0f / 9,  1.0f / 10, 1.0f / 11, 1.0f / 12,
+                                  1.0f / 13, 1.0f / 14, 1.0f / 15, 1.0f / 16};
+    float mean = 0.0f, m2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const float delta = __fsub_rn(v[j], mean);
+        mean = __fadd_rn(mean, __fmul_rn(delta, kRecip[j]));
+        m2 = __fadd_rn(m2, __fmul_rn(delta, __fsub_rn(v[j], mean)));
+    }
+    float l0m[4], l0q[4], l1m[4], l1q[4], l2m[4], l2q[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) l0m[k] = l0q[k] = l1m[k] = l1q[k] = l2m[k] = l2q[k] = 0.0f;
+    auto chunk_into_l0 = [&](int ch, auto first) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float fm = __shfl_sync(kFull, mean, ch * 4 + k);
+            const float fq = __shfl_sync(kFull, m2, ch * 4 + k);
+            if constexpr (decltype(first)::value) ln_merge<0, 16>(fm, fq, l0m[k], l0q[k]);
+            else ln_merge<16, 16>(fm, fq, l0m[k], l0q[k]);
+        }
+    };
+    using First = std::true_type;
+    using Second = std::false_type;
+    // chunks 0, 1 -> level 1 (32 samples)
+    chunk_into_l0(0, First{});
+    chunk_into_l0(1, Second{});
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        ln_merge<0, 32>(l0m[k], l0q[k], l1m[k], l1q[k]);
+        l0m[k] = l0q[k] = 0.0f;
+    }
+    // chunks 2, 3 -> level 1 (64) -> level 2
+    chunk_into_l0(2, First{});
+    chunk_into_l0(3, Second{});
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        ln_merge<32, 32>(l0m[k], l0q[k], l1m[k], l1q[k]);
+        l0m[k] = l0q[k] = 0.0f;
+        ln_merge<0, 64>(l1m[k], l1q[k], l2m[k], l2q[k]);
+        l1m[k] = l1q[k] = 0.0f;
+    }
+    // chunks 4, 5 -> level 1 (32)
+    chunk_into_l0(4, First{});
+    chunk_into_l0(5, Second{});
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        ln_merge<0, 32>(l0m[k], l0q[k], l1m[k], l1q[k]);
+        l0m[k] = l0q[k] = 0.0f;
+    }
+    // chunks 6, 7 -> level 1 (64) -> level 2 (128)
+    chunk_into_l0(6, First{});
+    chunk_into_l0(7, Second{});
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        ln_merge<32, 32>(l0m[k], l0q[k], l1m[k], l1q[k]);
+        l0m[k] = l0q[k] = 0.0f;
+        ln_merge<64, 64>(l1m[k], l1q[k], l2m[k], l2q[k]);
+        l1m[k] = l1q[k] = 0.0f;
+        // final fold of the (now empty) levels into level 0
+        ln_merge<0, 0>(l1m[k], l1q[k], l0m[k], l0q[k]);
+        ln_merge<0, 128>(l2m[k], l2q[k], l0m[k], l0q[k]);
+    }
+    // four-lane merge, 128 samples each: c = 1, 1/2, 1/3, 1/4
+    float mu = 0.0f, q = 0.0f;
+    constexpr float kC[4] = {128.0f / 128.0f, 128.0f / 256.0f, 128.0f / 384.0f, 128.0f / 512.0f};
+    constexpr float kN[4] = {0.0f, 128.0f, 256.0f, 384.0f};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float delta = __fsub_rn(l0m[k], mu);
+        mu = __fmaf_rn(kC[k], delta, mu);
+        q = __fadd_rn(q, __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), kC[k]), kN[k], l0q[k]));
+    }
+    const float var = __fmul_rn(q, 1.0f / 512.0f);  // == q / 512 exactly (power of two)
+    mu_out = mu;
+    scale_out = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+}
+
 // One warp normalises one 512-wide row: out = ((x - mean) * rstd) * w + b with
-// the moments of the reference's moments_512 (src/phonon_transformer.c:99-151)
-// and its affine step (:178-183). Lane (chunk*4 + l) runs the 16-step Welford
-// of elements chunk*64 + j*4 + l; every lane then replays the chunk cascade
-// and the four-lane merge identically. Returns false (on every lane) if an
-// input, weight, bias or output is non-finite.
+// the moments of ln_moments512 and the reference's affine step
+// (src/phonon_transformer.c:178-183). x is read once; each lane applies the
+// affine step to the elements it holds. Returns false (on every lane) if an
+// input, weight, bias or output is non-finite. kL2: read x through L2 only
+// (rows that other CTAs of a running kernel wrote).
+template <bool kL2 = false>
+__device__ __forceinline__ float ln_load(const float* p) {
+    if constexpr (kL2) return __ldcg(p);
+    return *p;
+}
+
+template <bool kL2 = false>
 __device__ __forceinline__ bool warp_layernorm512(const float* __restrict__ x,
                                                   const float* __restrict__ w,
                                                   const float* __restrict__ b,
                                                   float* __restrict__ out,
                                                   float eps = 1e-5f) {
     const int lane = threadIdx.x & 31;
-    const int chunk = lane >> 2, sub = lane & 3;
+    const int base = (lane >> 2) * 64 + (lane & 3);
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = ln_load<kL2>(x + base + j * 4);
     bool ok = true;
-    float mean = 0.0f, m2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) ok &= isfinite(v[j]);
+    float mu, scale;
+    ln_moments512(v, eps, mu, scale);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        float v = x[chunk * 64 + j * 4 + sub];
-        ok &= isfinite(v);
-        float delta = __fsub_rn(v, mean);
-        mean = __fadd_rn(mean, __fmul_rn(delta, 1.0f / static_cast<float>(j + 1)));  // folded at compile time
-        m2 = __fadd_rn(m2, __fmul_rn(delta, __fsub_rn(v, mean)));
-    }
-    float s1[3][4], s2[3][4], cnt[3] = {0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int l = 0; l < 3; ++l)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) s1[l][k] = s2[l][k] = 0.0f;
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            float fm = __shfl_sync(kFull, mean, ch * 4 + k);
-            float fq = __shfl_sync(kFull, m2, ch * 4 + k);
-            ln_merge(cnt[0], 16.0f, fm, fq, s1[0][k], s2[0][k]);
-        }
-        cnt[0] += 16.0f;
-        int carry = ch + 1;
-#pragma unroll
-        for (int level = 1; level < 3; ++level) {
-            if ((carry & 1) != 0) break;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                ln_merge(cnt[level], cnt[level - 1], s1[level - 1][k], s2[level - 1][k],
-                         s1[level][k], s2[level][k]);
-                s1[level - 1][k] = s2[level - 1][k] = 0.0f;
-            }
-            cnt[level] += cnt[level - 1];
-            cnt[level - 1] = 0.0f;
-            carry >>= 1;
-        }
-    }
-#pragma unroll
-    for (int level = 1; level < 3; ++level) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) ln_merge(cnt[0], cnt[level], s1[level][k], s2[level][k], s1[0][k], s2[0][k]);
-        cnt[0] += cnt[level];
-    }
-    float mu = 0.0f, q = 0.0f, n = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        float total = n + 128.0f;
-        float c = 128.0f / total;  // 1, 1/2, 1/3, 1/4: folded at compile time
-        float delta = __fsub_rn(s1[0][k], mu);
-        mu = __fmaf_rn(c, delta, mu);
-        q = __fadd_rn(q, __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), c), n, s2[0][k]));
-        n = total;
-    }
-    const float var = __fdiv_rn(q, 512.0f);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-    const double dmu = static_cast<double>(mu);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-        const int i = lane + 32 * k;
+        const int i = base + j * 4;
         const float wi = w[i], bi = b[i];
         ok &= isfinite(wi) && isfinite(bi);
-        float centered = __double2float_rn(__dsub_rn(static_cast<double>(x[i]), dmu));
+        // The reference centres in double and rounds once to float; for fp32
+        // operands that equals the fp32 subtraction bit for bit (binary64 has
+        // 53 >= 2*24 + 2 bits, so rounding twice is innocuous for +, -).
+        const float centered = __fsub_rn(v[j], mu);
         float y = __fadd_rn(__fmul_rn(__fmul_rn(centered, scale), wi), bi);
         ok &= isfinite(y);
         out[i] = y;
@@ -616,7 +664,26 @@ struct CombineParams {
     int32_t* status;
 };
 
-// One warp per (stream, head): out = sum_s e^(m_s-M) a_s / sum_s e^(m_s-M) l_s.
+// Split merge, one step: fold the partial (pm, pl, pa) of the next split (in
+// page order) into the running (M, S, A): M' = max(M, pm), S' = S e^(M-M') +
+// pl e^(pm-M'), A' = A e^(M-M') + pa e^(pm-M'); the merged head output is
+// A / S. All merge paths (per-stage, tensor-core and persistent) use it.
+struct MergeWeights {
+    float alpha, beta;
+};
+
+__device__ __forceinline__ MergeWeights merge_weights(float& M, float pm) {
+    const float M2 = fmaxf(M, pm);
+    MergeWeights w;
+    w.alpha = M == -INFINITY ? 0.0f : expf(M - M2);
+    w.beta = pm == -INFINITY ? 0.0f : expf(pm - M2);
+    M = M2;
+    return w;
+}
+
+__device__ __forceinline__ float merge_fold(float acc, MergeWeights w, float v) { return fmaf(acc, w.alpha, w.beta * v); }
+
+// One warp per (stream, head): merge the stream's splits in page order.
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_combine_kernel(CombineParams p) {
     const int lane = threadIdx.x & 31;
     pdl_wait();
@@ -625,16 +692,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_combine_kernel(CombinePa
     if (item >= static_cast<long long>(p.B) * kHeads) return;
     const int b = static_cast<int>(item >> 3), head = static_cast<int>(item & 7);
     const int first = p.first[b], n = p.count[b];
-    float mx = -INFINITY;
-    for (int s = 0; s < n; ++s) mx = fmaxf(mx, p.part[(static_cast<size_t>(first + s) * kHeads + head) * kPartStride]);
-    float total = 0.0f, a0 = 0.0f, a1 = 0.0f;
+    float M = -INFINITY, total = 0.0f, a0 = 0.0f, a1 = 0.0f;
     for (int s = 0; s < n; ++s) {
         const float* pp = p.part + (static_cast<size_t>(first + s) * kHeads + head) * kPartStride;
-        const float w = pp[0] == -INFINITY ? 0.0f : expf(pp[0] - mx);
-        total = fmaf(w, pp[1], total);
-        float2 av = *reinterpret_cast<const float2*>(pp + 2 + 2 * lane);
-        a0 = fmaf(w, av.x, a0);
-        a1 = fmaf(w, av.y, a1);
+        const MergeWeights w = merge_weights(M, pp[0]);
+        total = merge_fold(total, w, pp[1]);
+        const float2 av = *reinterpret_cast<const float2*>(pp + 2 + 2 * lane);
+        a0 = merge_fold(a0, w, av.x);
+        a1 = merge_fold(a1, w, av.y);
     }
     bool ok = total > 0.0f && isfinite(total);
     const float inv = __fdiv_rn(1.0f, total);

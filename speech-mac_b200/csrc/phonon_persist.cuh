@@ -1,0 +1,681 @@
+// Whole-step persistent kernel for small batches (sm_100a).
+//
+// A decode step of a few streams is a chain of dependent, latency-bound
+// stages: at one launch per stage the step costs several launch latencies
+// per layer. Here one cooperative launch runs every layer of the step (the
+// loop of phonon_flow_stack_step, speech-mac src/phonon_transformer.c:455-489).
+// One CTA per SM stays resident; CTAs meet at grid barriers between the
+// stages of a layer:
+//
+//   A  LN1 + QKV + RoPE + KV append   (src/phonon_transformer.c:414-431)
+//   B  paged attention over balanced page chunks, one chunk per CTA, TMA
+//      page staging as in attn_tma_kernel; writes per-split partials
+//      (flow_attention, :340-404)
+//   C  split merge + out projection + residual (:432-443)
+//   D  LN2 + FFN up + GELU             (:444-447)
+//   E  FFN down + residual             (:448-452)
+//
+// Work split: CTAs form ceil(R/8) groups. A group owns 8 streams (one per
+// compute warp for the LayerNorms, which each CTA of the group computes for
+// itself) and divides the rows of every projection, in RoPE pairs, among
+// its CTAs. Warp 8 is a copy warp: it stages the CTA's weight rows (and the
+// LayerNorm vectors) of the next projections in shared memory with bulk
+// async copies (two buffers: QKV and up share one, out and down the other,
+// each refilled as soon as the stage that read it has passed its barrier),
+// stages the GELU rows for stage E, and in stage B it is the TMA producer of
+// the page ring. Row dot products and their epilogues use gemv_kernel's
+// per-lane arithmetic and summation order; the attention partials use
+// attn_tma_kernel's.
+//
+// Every wait (grid barrier, mbarrier) is bounded: on expiry it raises the
+// context's error flag; once raised, every wait in the grid returns at once,
+// the kernel runs to its end without issuing new copies, and the copy warp
+// waits (bounded) for the copies it has in flight before the CTA exits.
+#pragma once
+
+#include "phonon_attention.cuh"
+
+namespace phonon {
+
+// Stage timestamps for profiling builds (-DPHONON_PERSIST_TRACE): thread 0
+// of every CTA writes %globaltimer at marked points into
+// g_persist_trace[(cta * 65 + layer) * 16 + slot]. Empty otherwise.
+#ifdef PHONON_PERSIST_TRACE
+__device__ unsigned long long* g_persist_trace;
+#define PERSIST_MARK(layer, slot)                                                                   \
+    do {                                                                                             \
+        if (threadIdx.x == 0 && g_persist_trace) {                                                   \
+            unsigned long long t_;                                                                   \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                   \
+            g_persist_trace[(static_cast<size_t>(blockIdx.x) * 65 + (layer)) * 16 + (slot)] = t_;    \
+        }                                                                                            \
+    } while (0)
+#else
+#define PERSIST_MARK(layer, slot) \
+    do {                          \
+    } while (0)
+#endif
+
+constexpr int kPersistWarps = 8;                          // compute warps
+constexpr int kPersistThreads = 32 * (kPersistWarps + 1);  // + copy warp
+constexpr int kPersistGroup = 8;                          // streams per CTA group
+constexpr int kPersistMaxBatch = 64;
+constexpr int kPersistMinChunk = 4;                       // pages per attention chunk, at least
+constexpr int kPersistNormBytes = 2 * kWidth * 4;         // LayerNorm weight + bias, fp32
+constexpr long long kDrainBudgetCycles = 1ll << 28;       // ~0.14 s
+
+template <bool kBf16>
+struct PersistAttn {
+    static constexpr int kStages = kBf16 ? 3 : 2;
+    static constexpr int kStageBytes = AttnTma<kBf16>::kStageBytes;
+    static constexpr int kBytes = kStages * kStageBytes;
+};
+
+enum PersistMat : int { PM_QKV = 0, PM_OUT = 1, PM_UP = 2, PM_DOWN = 3 };
+
+__host__ __device__ constexpr int persist_rows(int m) { return m == PM_QKV ? 1536 : (m == PM_UP ? 2048 : 512); }
+__host__ __device__ constexpr int persist_cols(int m) { return m == PM_DOWN ? 2048 : 512; }
+// Shared-memory bytes per weight row: int8 plane + binary16 block scales.
+__host__ __device__ constexpr int persist_row_bytes(int m) { return persist_cols(m) + persist_cols(m) / 16; }
+// Rows of matrix m held by one CTA of a group of nct CTAs (at most).
+__host__ __device__ constexpr int persist_cta_rows(int m, int nct) {
+    return 2 * ((persist_rows(m) / 2 + nct - 1) / nct);
+}
+
+struct PersistLayer {
+    const uint8_t* plane[4];   // qkv, out, up, down: lane-interleaved int8 rows
+    const __half* scales[4];   // their Q8_0 block scales
+    const float* norms;        // fp32 [4][512]: norm1 w, b, norm2 w, b
+};
+
+struct PersistParams {
+    const PersistLayer* layers;
+    int n_layers, R, S, U, n_groups;
+    const float* in;           // [R][512]
+    float* out;                // [R][512]
+    float *xbuf0, *xbuf1, *h, *g, *q, *part;
+    int32_t* status;           // [R]
+    int32_t* error;            // context error flag
+    unsigned* barrier;         // grid barrier counter (monotonic across launches)
+    unsigned barrier_base;     // its value when this launch starts
+    const int32_t *slot, *pos, *first, *count, *updates;
+    const Split* splits;       // in (stream, page) order
+    const int32_t* cta_split;  // [gridDim.x + 1]: CTA c runs splits [cta_split[c], cta_split[c+1])
+    const float* freq;         // [32] RoPE inverse frequencies
+    float2* rope;              // [R][32] (cos, sin), written in stage 0
+    KvView kv;                 // kv.table is written in stage 0 (page updates)
+    int off_x, off_w0, off_w1, off_norm, off_bar;  // shared-memory offsets from the 1024-aligned base
+};
+
+struct RowSlice {
+    int row0, n_pairs;
+};
+
+__device__ __forceinline__ RowSlice persist_slice(int m, int grank, int nct) {
+    const int pairs = persist_rows(m) / 2;
+    const int per = (pairs + nct - 1) / nct;
+    const int p0 = grank * per;
+    return RowSlice{2 * p0, max(0, min(per, pairs - p0))};
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Drain wait of the copy warp: bounded, and independent of the failure flag.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - start > kDrainBudgetCycles) return;
+}
+
+// Grid barrier. Every CTA adds one to the counter (release); the k-th
+// barrier of a launch completes when it reaches base + k * gridDim.x
+// (wrap-safe compare, acquire). The failure flags are polled every 64 spins.
+__device__ __forceinline__ void grid_sync(const PersistParams& p, unsigned& epoch, volatile int* failed) {
+    __syncthreads();
+    epoch += gridDim.x;
+    if (threadIdx.x == 0) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        atomicAdd(p.barrier, 1u);
+        const unsigned target = p.barrier_base + epoch;
+        const long long start = clock64();
+        for (unsigned spin = 1; static_cast<int>(ld_acquire_gpu(p.barrier) - target) < 0; ++spin) {
+            if ((spin & 63) != 0) continue;
+            if (*failed || *reinterpret_cast<volatile int32_t*>(p.error)) {
+                *failed = 1;
+                break;
+            }
+            if (clock64() - start > kWaitBudgetCycles) {
+                *failed = 1;
+                atomicExch(p.error, 1);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// Stage rows rs of matrix m of layer L into `buf` (plane bytes, then
+// scales); with norm_dst, also the LayerNorm vectors `norm` (w then b).
+__device__ __forceinline__ void fill_weights(uint8_t* buf, uint32_t bar, const PersistLayer& L, int m, RowSlice rs,
+                                             uint8_t* norm_dst, const float* norm) {
+    const int cols = persist_cols(m);
+    const uint32_t wbytes = static_cast<uint32_t>(rs.n_pairs) * 2 * cols;
+    const uint32_t sbytes = static_cast<uint32_t>(rs.n_pairs) * 2 * (cols / 32) * 2;
+    mbar_expect_tx(bar, wbytes + sbytes + (norm_dst ? kPersistNormBytes : 0));
+    if (wbytes) {
+        bulk_load(smem_addr(buf), L.plane[m] + static_cast<size_t>(rs.row0) * cols, wbytes, bar);
+        bulk_load(smem_addr(buf + wbytes), L.scales[m] + static_cast<size_t>(rs.row0) * (cols / 32), sbytes, bar);
+    }
+    if (norm_dst) bulk_load(smem_addr(norm_dst), norm, kPersistNormBytes, bar);
+}
+
+// Sum over the warp of 16 per-lane values v[rr][bb] (rr < 2, bb < 8) by
+// recursive halving: at each of the five levels (xor 16, 8, 4, 2, 1) a lane
+// keeps half of its values and adds the partner's copy of them. The additions
+// are those of a butterfly warp_sum of each value (same pairs, same levels),
+// so the sums are the same to the bit; lane l ends with value (l >> 4, (l >> 1) & 7).
+__device__ __forceinline__ float warp_reduce16(const float (&v)[2][kPersistGroup]) {
+    const int lane = threadIdx.x & 31;
+    float a[8], b[4], c[2];
+    const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float keep = u16 ? v[1][i] : v[0][i], send = u16 ? v[0][i] : v[1][i];
+        a[i] = keep + __shfl_xor_sync(kFull, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float keep = u8 ? a[i + 4] : a[i], send = u8 ? a[i] : a[i + 4];
+        b[i] = keep + __shfl_xor_sync(kFull, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float keep = u4 ? b[i + 2] : b[i], send = u4 ? b[i] : b[i + 2];
+        c[i] = keep + __shfl_xor_sync(kFull, send, 4);
+    }
+    const float keep = u2 ? c[1] : c[0], send = u2 ? c[0] : c[1];
+    const float d = keep + __shfl_xor_sync(kFull, send, 2);
+    return d + __shfl_xor_sync(kFull, d, 1);
+}
+
+// The CTA's row pairs of one projection against the group's streams: weights
+// (rows rs.row0 ..) and activations xs[nb][cols] in shared memory. Lane j < nb
+// finishes stream b0 + j; its epilogue operands (residual pair, RoPE angles,
+// KV page) are loaded before the dot products so their latency overlaps them.
+template <int kChunks, int kEpi>
+__device__ __forceinline__ void persist_gemv(const PersistParams& p, int layer, const uint8_t* wb, RowSlice rs,
+                                             const float* xs, int b0, int nb, const float* res, float* y, int ldy) {
+    constexpr int cols = kChunks * 512;
+    const __half* wsc = reinterpret_cast<const __half*>(wb + static_cast<size_t>(rs.n_pairs) * 2 * cols);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int eb = b0 + min(lane, nb - 1);  // this lane's epilogue stream (clamped for idle lanes)
+    for (int t = warp; t < rs.n_pairs; t += kPersistWarps) {
+        const int r0 = rs.row0 + 2 * t;
+        float2 pre = make_float2(0.0f, 0.0f);
+        int page = 0;
+        if constexpr (kEpi == EPI_RESID) pre = __ldcg(reinterpret_cast<const float2*>(res + static_cast<size_t>(eb) * kWidth + r0));
+        if constexpr (kEpi == EPI_QKV) {
+            const int region = r0 >> 9;
+            if (region < 2) pre = __ldcg(p.rope + eb * 32 + ((r0 & 63) >> 1));
+            if (region > 0)
+                page = __ldcg(p.kv.table + static_cast<size_t>(p.slot[eb]) * p.kv.max_pages + p.pos[eb] / kPage);
+        }
+        float acc[2][kPersistGroup];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+            for (int bb = 0; bb < kPersistGroup; ++bb) acc[rr][bb] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+            float wf[2][16], sc[2][4];
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const int lr = 2 * t + rr;
+                const uint4 wq = *reinterpret_cast<const uint4*>(wb + static_cast<size_t>(lr) * cols + c * 512 + lane * 16);
+                const uint2 raw = *reinterpret_cast<const uint2*>(wsc + static_cast<size_t>(lr) * (cols / 32) + c * 16 +
+                                                                  (lane >> 3) * 4);
+                const __half2 h01 = *reinterpret_cast<const __half2*>(&raw.x);
+                const __half2 h23 = *reinterpret_cast<const __half2*>(&raw.y);
+                sc[rr][0] = __low2float(h01);
+                sc[rr][1] = __high2float(h01);
+                sc[rr][2] = __low2float(h23);
+                sc[rr][3] = __high2float(h23);
+                const uint32_t words[4] = {wq.x, wq.y, wq.z, wq.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        wf[rr][j * 4 + e] = static_cast<float>(static_cast<int8_t>((words[j] >> (8 * e)) & 0xffu));
+            }
+#pragma unroll
+            for (int bb = 0; bb < kPersistGroup; ++bb) {
+                if (bb < nb) {
+                    const float* xr = xs + bb * cols + c * 512 + lane * 4;
+                    float4 xv[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) xv[j] = *reinterpret_cast<const float4*>(xr + j * 128);
+#pragma unroll
+                    for (int rr = 0; rr < 2; ++rr) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            float part = wf[rr][j * 4 + 0] * xv[j].x;
+                            part = fmaf(wf[rr][j * 4 + 1], xv[j].y, part);
+                            part = fmaf(wf[rr][j * 4 + 2], xv[j].z, part);
+                            part = fmaf(wf[rr][j * 4 + 3], xv[j].w, part);
+                            acc[rr][bb] = fmaf(sc[rr][j], part, acc[rr][bb]);
+                        }
+                    }
+                }
+            }
+        }
+        const float red = warp_reduce16(acc);
+        float v0 = __shfl_sync(kFull, red, 2 * (lane & 7));       // (row r0, stream lane)
+        float v1 = __shfl_sync(kFull, red, 16 + 2 * (lane & 7));  // (row r0 + 1, stream lane)
+        if (lane >= nb) continue;
+        const int b = b0 + lane;
+        if constexpr (kEpi == EPI_QKV) {
+            const int region = r0 >> 9;  // 0 = q, 1 = k, 2 = v
+            const int within = r0 & 511;
+            if (region < 2) rope_apply(v0, v1, pre);
+            if (!isfinite(v0) || !isfinite(v1)) flag_nonfinite(p.status, b);
+            if (region == 0) {
+                *reinterpret_cast<float2*>(p.q + static_cast<size_t>(b) * kWidth + within) = make_float2(v0, v1);
+            } else {
+                const int pos = p.pos[b];
+                const long long off = kv_offset(p.kv, page, layer, region - 1, within >> 6, pos % kPage) + (within & 63);
+                kv_store2(p.kv, off, v0, v1);
+            }
+        } else {
+            if constexpr (kEpi == EPI_RESID) {
+                v0 = __fadd_rn(pre.x, v0);
+                v1 = __fadd_rn(pre.y, v1);
+            }
+            if constexpr (kEpi == EPI_GELU) {
+                if (!isfinite(v0) || !isfinite(v1)) flag_nonfinite(p.status, b);
+                v0 = gelu_erf(v0);
+                v1 = gelu_erf(v1);
+            }
+            if (!isfinite(v0) || !isfinite(v1)) flag_nonfinite(p.status, b);
+            *reinterpret_cast<float2*>(y + static_cast<size_t>(b) * ldy + r0) = make_float2(v0, v1);
+        }
+    }
+}
+
+// Stage B: the CTA's chunk of pages, as splits [cta_split[c], cta_split[c+1])
+// (one split per stream segment). The copy warp is the TMA producer of the
+// page ring; warp h consumes head h and writes the split's partial
+// (max, sum, acc[64]). The ring counter runs on across splits and layers
+// (identical in all roles).
+template <bool kBf16>
+__device__ __forceinline__ void persist_attention(const CUtensorMap* tm, const PersistParams& p, int layer,
+                                                  uint8_t* stages, uint32_t full0, uint32_t empty0, uint32_t& ring,
+                                                  int* last_issue, volatile int* failed) {
+    using A = PersistAttn<kBf16>;
+    using T = AttnTma<kBf16>;
+    constexpr int kSt = A::kStages;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int s_begin = p.cta_split[blockIdx.x], s_end = p.cta_split[blockIdx.x + 1];
+    if (warp == kPersistWarps) {
+        uint32_t n = ring;
+        if (lane == 0) fence_proxy_async_global();  // KV appended in stage A
+        for (int s = s_begin; s < s_end; ++s) {
+            const Split sp = p.splits[s];
+            const int32_t* table = p.kv.table + static_cast<size_t>(p.slot[sp.b]) * p.kv.max_pages;
+            for (int i = 0; i < sp.page_count; ++i, ++n) {
+                if (lane != 0 || *failed) continue;
+                const int st = static_cast<int>(n % kSt);
+                if (n >= static_cast<uint32_t>(kSt) && !mbar_wait(empty0 + 8 * st, ((n / kSt) - 1) & 1, p.error, failed))
+                    continue;
+                const int page = __ldcg(table + sp.page_begin + i);
+                const int row0 = (page * p.n_layers + layer) * 256;  // K block; V block follows
+                uint8_t* stage = stages + st * A::kStageBytes;
+                mbar_expect_tx(full0 + 8 * st, A::kStageBytes);
+#pragma unroll
+                for (int bx = 0; bx < T::kBoxes; ++bx) {
+                    tma_load_2d(smem_addr(stage + bx * T::kBoxBytes), tm, bx * T::kBoxCols, row0, full0 + 8 * st);
+                    tma_load_2d(smem_addr(stage + T::kBlockBytes + bx * T::kBoxBytes), tm, bx * T::kBoxCols, row0 + 128,
+                                full0 + 8 * st);
+                }
+                last_issue[st] = static_cast<int>(n);
+            }
+        }
+        __syncwarp();
+        ring = n;
+        return;
+    }
+
+    const int head = warp, half = lane >> 4, key_lane = lane & 15;
+    const int krow = head * kPage + key_lane;
+    uint32_t n = ring;
+    for (int s = s_begin; s < s_end; ++s) {
+        const Split sp = p.splits[s];
+        float qh[32];
+        {
+            const float4* qs = reinterpret_cast<const float4*>(p.q + static_cast<size_t>(sp.b) * kWidth +
+                                                               head * kHeadDim + half * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float4 v = __ldcg(qs + i);
+                qh[4 * i] = v.x;
+                qh[4 * i + 1] = v.y;
+                qh[4 * i + 2] = v.z;
+                qh[4 * i + 3] = v.w;
+            }
+        }
+        float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f;
+        bool finite_ok = true;
+        for (int i = 0; i < sp.page_count; ++i, ++n) {
+            const int st = static_cast<int>(n % kSt);
+            const bool got = __all_sync(kFull, mbar_wait(full0 + 8 * st, (n / kSt) & 1, p.error, failed));
+            if (got) {
+                const uint8_t* sK = stages + st * A::kStageBytes;
+                const uint8_t* sV = sK + T::kBlockBytes;
+                const int pg = sp.page_begin + i;
+                const bool valid = pg * kPage + key_lane < sp.n_keys;
+                float dot = 0.0f;
+                if constexpr (kBf16) {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(sw128(sK, krow, half * 4 + c));
+                        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            dot = fmaf(qh[8 * c + 2 * k], __uint_as_float(w[k] << 16), dot);
+                            dot = fmaf(qh[8 * c + 2 * k + 1], __uint_as_float(w[k] & 0xffff0000u), dot);
+                        }
+                    }
+                } else {
+                    const uint8_t* box = sK + half * T::kBoxBytes;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const float4 v = *reinterpret_cast<const float4*>(sw128(box, krow, c));
+                        dot = fmaf(qh[4 * c], v.x, dot);
+                        dot = fmaf(qh[4 * c + 1], v.y, dot);
+                        dot = fmaf(qh[4 * c + 2], v.z, dot);
+                        dot = fmaf(qh[4 * c + 3], v.w, dot);
+                    }
+                }
+                dot += __shfl_xor_sync(kFull, dot, 16);
+                float score = dot * 0.125f;
+                if (valid) finite_ok &= isfinite(score);
+                score = valid ? score : -INFINITY;
+                float pm = score;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, o));
+                const float m_new = fmaxf(m, pm);
+                const float alpha = m == -INFINITY ? 0.0f : expf(m - m_new);
+                const float pr = valid ? expf(score - m_new) : 0.0f;
+                float ps = pr;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
+                l = fmaf(l, alpha, ps);
+                a0 *= alpha;
+                a1 *= alpha;
+                const int n_valid = min(kPage, sp.n_keys - pg * kPage);
+#pragma unroll
+                for (int j = 0; j < kPage; ++j) {
+                    const float pj = __shfl_sync(kFull, pr, j);
+                    if (j < n_valid) {
+                        const int vrow = head * kPage + j;
+                        float v0, v1;
+                        if constexpr (kBf16) {
+                            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(sw128(sV, vrow, lane >> 2) + (lane & 3) * 4);
+                            v0 = __uint_as_float(w2 << 16);
+                            v1 = __uint_as_float(w2 & 0xffff0000u);
+                        } else {
+                            const uint8_t* box = sV + (lane >> 4) * T::kBoxBytes;
+                            const float2 w2 =
+                                *reinterpret_cast<const float2*>(sw128(box, vrow, (lane & 15) >> 1) + (lane & 1) * 8);
+                            v0 = w2.x;
+                            v1 = w2.y;
+                        }
+                        a0 = fmaf(pj, v0, a0);
+                        a1 = fmaf(pj, v1, a1);
+                    }
+                }
+                m = m_new;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty0 + 8 * st);
+        }
+        float* out = p.part + (static_cast<size_t>(s) * kHeads + head) * kPartStride;
+        *reinterpret_cast<float2*>(out + 2 + 2 * lane) = make_float2(a0, a1);
+        if (lane == 0) {
+            out[0] = m;
+            out[1] = l;
+        }
+        if (!__all_sync(kFull, finite_ok) && lane == 0) flag_nonfinite(p.status, sp.b);
+    }
+    ring = n;
+}
+
+// Stage C prologue: merge the splits of every (stream, head) of the group
+// into the attention output rows xs[nb][512] (merge_weights / merge_fold, in
+// page order). Four threads per (stream, head), 16 dims each; partials are
+// read four splits at a time.
+__device__ __forceinline__ void persist_merge(const PersistParams& p, float* xs, int b0, int nb) {
+    const int t = threadIdx.x, item = t >> 2, quarter = t & 3;
+    if (item >= nb * kHeads) return;
+    const int bb = item >> 3, head = item & 7, b = b0 + bb;
+    const int first = p.first[b], cnt = p.count[b];
+    float M = -INFINITY, S = 0.0f, acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+    for (int k0 = 0; k0 < cnt; k0 += 4) {
+        float pm[4], pl[4];
+        float2 pa[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int k = min(k0 + u, cnt - 1);
+            const float* pp = p.part + (static_cast<size_t>(first + k) * kHeads + head) * kPartStride;
+            pm[u] = __ldcg(pp);
+            pl[u] = __ldcg(pp + 1);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) pa[u][i] = __ldcg(reinterpret_cast<const float2*>(pp + 2 + quarter * 16) + i);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (k0 + u >= cnt) break;
+            const MergeWeights w = merge_weights(M, pm[u]);
+            S = merge_fold(S, w, pl[u]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                acc[2 * i] = merge_fold(acc[2 * i], w, pa[u][i].x);
+                acc[2 * i + 1] = merge_fold(acc[2 * i + 1], w, pa[u][i].y);
+            }
+        }
+    }
+    bool ok = S > 0.0f && isfinite(S);
+    const float inv = __fdiv_rn(1.0f, S);
+    float* dst = xs + bb * kWidth + head * kHeadDim + quarter * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float o = __fmul_rn(acc[i], inv);
+        ok &= isfinite(o);
+        dst[i] = o;
+    }
+    if (!ok) flag_nonfinite(p.status, b);
+}
+
+template <bool kBf16>
+__global__ void __launch_bounds__(kPersistThreads, 1)
+    step_persist_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ PersistParams p) {
+    constexpr int kSt = PersistAttn<kBf16>::kStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* xs = reinterpret_cast<float*>(smem + p.off_x);
+    uint8_t* stages = smem + p.off_x;  // stage B only; xs in the other stages
+    uint8_t* wb[2] = {smem + p.off_w0, smem + p.off_w1};
+    uint8_t* norm_s = smem + p.off_norm;
+    const float* ln_w = reinterpret_cast<const float*>(norm_s);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
+    const uint32_t full0 = smem_addr(bars), empty0 = full0 + 8 * kSt, wfull0 = full0 + 16 * kSt,
+                   xfull = wfull0 + 16;
+    volatile int* failed = reinterpret_cast<volatile int*>(bars + 2 * kSt + 3);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool copy_lane = warp == kPersistWarps && lane == 0;
+    const int gi = blockIdx.x % p.n_groups, grank = blockIdx.x / p.n_groups;
+    const int nct = (static_cast<int>(gridDim.x) - gi + p.n_groups - 1) / p.n_groups;
+    const int b0 = gi * kPersistGroup, nb = min(kPersistGroup, p.R - b0);
+    const RowSlice rs[4] = {persist_slice(PM_QKV, grank, nct), persist_slice(PM_OUT, grank, nct),
+                            persist_slice(PM_UP, grank, nct), persist_slice(PM_DOWN, grank, nct)};
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kSt; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, kPersistWarps);
+        }
+        mbar_init(wfull0, 1);
+        mbar_init(wfull0 + 8, 1);
+        mbar_init(xfull, 1);
+        *failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    uint32_t fills[2] = {0, 0};      // weight fills per buffer (same count in every thread)
+    uint32_t issued[2] = {0, 0};     // fills the copy lane actually issued
+    uint32_t xfills = 0, xissued = 0;
+    int last_issue[kSt];             // copy lane: newest page-ring index per stage
+#pragma unroll
+    for (int s = 0; s < kSt; ++s) last_issue[s] = -1;
+    uint32_t ring = 0;
+    unsigned epoch = 0;
+    // Buffer 0 holds QKV or up rows and the LayerNorm vectors in front of them.
+    auto fill = [&](int k, int layer, int m) {
+        if (warp == kPersistWarps) {
+            if (lane == 0 && !*failed) {
+                const PersistLayer L = p.layers[layer];
+                const float* norm = m == PM_QKV ? L.norms : (m == PM_UP ? L.norms + 2 * kWidth : nullptr);
+                fill_weights(wb[k], wfull0 + 8 * k, L, m, rs[m], norm ? norm_s : nullptr, norm);
+                ++issued[k];
+            }
+            __syncwarp();
+        }
+        ++fills[k];
+    };
+    auto wait_fill = [&](int k) { mbar_wait(wfull0 + 8 * k, (fills[k] - 1) & 1, p.error, failed); };
+
+    fill(0, 0, PM_QKV);
+    fill(1, 0, PM_OUT);
+
+    // Stage 0: page-table updates and the step's RoPE table.
+    {
+        const int tid = blockIdx.x * blockDim.x + threadIdx.x, nt = gridDim.x * blockDim.x;
+        if (blockIdx.x == 0)
+            for (int i = threadIdx.x; i < p.U; i += blockDim.x)
+                const_cast<int32_t*>(p.kv.table)[static_cast<size_t>(p.updates[3 * i]) * p.kv.max_pages +
+                                                 p.updates[3 * i + 1]] = p.updates[3 * i + 2];
+        for (int t = tid; t < p.R * 32; t += nt) {
+            const float phase = __fmul_rn(static_cast<float>(p.pos[t >> 5]), p.freq[t & 31]);
+            double sd, cd;
+            sincos(static_cast<double>(phase), &sd, &cd);
+            p.rope[t] = make_float2(__double2float_rn(cd), __double2float_rn(sd));
+        }
+    }
+    grid_sync(p, epoch, failed);
+    PERSIST_MARK(64, 0);
+
+    for (int l = 0; l < p.n_layers; ++l) {
+        const float* cur = l == 0 ? p.in : (((l - 1) & 1) ? p.xbuf1 : p.xbuf0);
+        float* next = l == p.n_layers - 1 ? p.out : ((l & 1) ? p.xbuf1 : p.xbuf0);
+        if (l > 0) fill(1, l, PM_OUT);
+
+        // A: LN1 -> QKV -> RoPE -> q, KV append
+        if (warp < kPersistWarps) wait_fill(0);
+        if (warp < nb) {
+            const bool ok = warp_layernorm512<true>(cur + static_cast<size_t>(b0 + warp) * kWidth, ln_w, ln_w + kWidth,
+                                                    xs + warp * kWidth);
+            if (!ok && lane == 0 && grank == 0) flag_nonfinite(p.status, b0 + warp);
+        }
+        __syncthreads();
+        PERSIST_MARK(l, 1);
+        if (warp < kPersistWarps) persist_gemv<1, EPI_QKV>(p, l, wb[0], rs[PM_QKV], xs, b0, nb, nullptr, nullptr, 0);
+        fence_proxy_async_global();  // KV stores before stage B's TMA reads
+        PERSIST_MARK(l, 2);
+        grid_sync(p, epoch, failed);
+        PERSIST_MARK(l, 3);
+
+        // B: attention partials
+        fill(0, l, PM_UP);
+        persist_attention<kBf16>(&tm_kv, p, l, stages, full0, empty0, ring, last_issue, failed);
+        PERSIST_MARK(l, 4);
+        grid_sync(p, epoch, failed);
+        PERSIST_MARK(l, 5);
+
+        // C: merge the splits, h = x + attn Wout^T
+        if (warp < kPersistWarps) persist_merge(p, xs, b0, nb);
+        __syncthreads();
+        PERSIST_MARK(l, 6);
+        if (warp < kPersistWarps) {
+            wait_fill(1);
+            persist_gemv<1, EPI_RESID>(p, l, wb[1], rs[PM_OUT], xs, b0, nb, cur, p.h, kWidth);
+        }
+        PERSIST_MARK(l, 7);
+        grid_sync(p, epoch, failed);
+        PERSIST_MARK(l, 8);
+
+        // D: g = GELU(LN2(h) Wup^T)
+        fill(1, l, PM_DOWN);
+        if (warp < kPersistWarps) wait_fill(0);
+        if (warp < nb) {
+            const bool ok = warp_layernorm512<true>(p.h + static_cast<size_t>(b0 + warp) * kWidth, ln_w, ln_w + kWidth,
+                                                    xs + warp * kWidth);
+            if (!ok && lane == 0 && grank == 0) flag_nonfinite(p.status, b0 + warp);
+        }
+        __syncthreads();
+        PERSIST_MARK(l, 9);
+        if (warp < kPersistWarps) persist_gemv<1, EPI_GELU>(p, l, wb[0], rs[PM_UP], xs, b0, nb, nullptr, p.g, kFfn);
+        fence_proxy_async_global();  // GELU rows before stage E's bulk copy
+        PERSIST_MARK(l, 10);
+        grid_sync(p, epoch, failed);
+        PERSIST_MARK(l, 11);
+
+        // E: x' = h + g Wdown^T; the copy warp stages the group's GELU rows
+        if (warp == kPersistWarps) {
+            if (lane == 0 && !*failed) {
+                fence_proxy_async_global();
+                const uint32_t bytes = static_cast<uint32_t>(nb) * kFfn * 4;
+                mbar_expect_tx(xfull, bytes);
+                bulk_load(smem_addr(xs), p.g + static_cast<size_t>(b0) * kFfn, bytes, xfull);
+                ++xissued;
+            }
+            __syncwarp();
+        }
+        ++xfills;
+        if (l + 1 < p.n_layers) fill(0, l + 1, PM_QKV);
+        if (warp < kPersistWarps) {
+            mbar_wait(xfull, (xfills - 1) & 1, p.error, failed);
+            wait_fill(1);
+            PERSIST_MARK(l, 12);
+            persist_gemv<4, EPI_RESID>(p, l, wb[1], rs[PM_DOWN], xs, b0, nb, p.h, next, kWidth);
+        }
+        PERSIST_MARK(l, 13);
+        grid_sync(p, epoch, failed);
+        PERSIST_MARK(l, 14);
+    }
+
+    // Copies still in flight (only after a failure) land before the CTA exits.
+    if (copy_lane) {
+        for (int s = 0; s < kSt; ++s)
+            if (last_issue[s] >= 0) mbar_drain(full0 + 8 * s, (static_cast<uint32_t>(last_issue[s]) / kSt) & 1);
+        for (int k = 0; k < 2; ++k)
+            if (issued[k] > 0) mbar_drain(wfull0 + 8 * k, (issued[k] - 1) & 1);
+        if (xissued > 0) mbar_drain(xfull, (xissued - 1) & 1);
+    }
+}
+
+}  // namespace phonon

@@ -10,10 +10,11 @@ import numpy as np
 
 from ._libs import load_cuda
 
-KERNEL_CLASSES = ("qkv", "attention", "combine", "out", "up", "down", "other")
+KERNEL_CLASSES = ("qkv", "attention", "combine", "out", "up", "down", "other", "fused")
 OK, INVALID, NON_FINITE, OOM, POOL_EXHAUSTED, CAPACITY, BAD_POSITION, CANCELLED, DEVICE_ERROR = range(9)
 Q8_0, BF16 = 1, 2
 KV_F32, KV_BF16 = 0, 1
+FUSED_MAX_BATCH = 64  # PHONON_CUDA_FUSED_MAX_BATCH
 WIDTH = 512
 PAGE = 16
 
@@ -75,6 +76,7 @@ def lib():
         "phonon_cuda_rope_interleaved": [C.c_int, P, SZ, SZ, SZ, F],
         "phonon_cuda_profile_enable": [P, C.c_int],
         "phonon_cuda_profile_read": [P, P, P, P],
+        "phonon_cuda_set_batch_paths": [P, U32, U32],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -220,6 +222,11 @@ class Context:
 
     def launch_count(self):
         return int(self.L.phonon_cuda_launch_count(self.h))
+
+    def set_batch_paths(self, fused_max_batch, tensor_min_batch=32):
+        """Batch sizes routed to the persistent whole-step launch (<= fused_max_batch)
+        and to the tensor-core projections (>= tensor_min_batch)."""
+        check(self.L.phonon_cuda_set_batch_paths(self.h, fused_max_batch, tensor_min_batch), "set_batch_paths")
 
     def layer_step(self, s, layer, position, x):
         x = np.ascontiguousarray(x, np.float32)
