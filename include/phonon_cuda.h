@@ -230,19 +230,21 @@ uint64_t phonon_cuda_launch_count(PhononCuda *ctx);
 
 /* ---- step paths by batch size ----
  * A decode step (phonon_cuda_step / phonon_cuda_step_device without a cancel
- * poll) of at most fused_max_batch streams runs as ONE persistent launch
- * that keeps a CTA on every SM for all layers; larger batches run one launch
- * per stage, with the projections on the tensor cores from tensor_min_batch
- * streams up. Defaults: PHONON_CUDA_FUSED_MAX_BATCH and 32. fused_max_batch
- * = 0 disables the persistent step; values above PHONON_CUDA_FUSED_MAX_BATCH
- * or tensor_min_batch = 0 are PHONON_CUDA_INVALID_ARGUMENT. All paths give
- * the same results within the tolerances of the reference's tests (the
- * persistent and per-stage GEMV paths bit for bit). The persistent step needs
- * Q8_0 weights, cooperative launch and enough shared memory for the batch
- * (bf16 KV: up to 64 streams; fp32 KV: up to 48); otherwise the per-stage
- * path runs. */
+ * poll) of fused_min_batch..fused_max_batch streams runs as ONE persistent
+ * launch that keeps a CTA on every SM for all layers; other batches run one
+ * launch per stage, with the projections on the tensor cores from
+ * tensor_min_batch streams up. Defaults: 8, PHONON_CUDA_FUSED_MAX_BATCH, 32
+ * (a few streams are as fast one launch per stage). fused_min_batch >
+ * fused_max_batch disables the persistent step; fused_min_batch = 0,
+ * fused_max_batch > PHONON_CUDA_FUSED_MAX_BATCH or tensor_min_batch = 0 are
+ * PHONON_CUDA_INVALID_ARGUMENT. The persistent and per-stage GEMV paths give
+ * the same results bit for bit (the tensor-core path within the tolerances
+ * of the reference's tests). The persistent step needs Q8_0 weights,
+ * cooperative launch and enough shared memory for the batch; otherwise the
+ * per-stage path runs. */
 #define PHONON_CUDA_FUSED_MAX_BATCH 64
-int phonon_cuda_set_batch_paths(PhononCuda *ctx, uint32_t fused_max_batch, uint32_t tensor_min_batch);
+int phonon_cuda_set_batch_paths(PhononCuda *ctx, uint32_t fused_min_batch, uint32_t fused_max_batch,
+                                uint32_t tensor_min_batch);
 
 const char *phonon_cuda_status_string(int status);
 

@@ -30,6 +30,7 @@ constexpr int kSplitTarget = 640;   // ~8 warps per split: fills 148 SMs several
 constexpr int kPrefillChunk = 256;  // rows per prefill pass
 constexpr int kTensorMinBatch = 32;  // streams from which projections run on tcgen05
 constexpr int kMaxSms = 1024;        // bound on the SM count (persistent split table)
+constexpr int kFusedMinBatch = 8;    // smaller batches are as fast or faster one launch per stage
 
 #define CUDA_TRY(expr)                                                                       \
     do {                                                                                     \
@@ -376,7 +377,7 @@ struct PhononCuda {
     // Whole-step persistent kernel (batches up to fused_max streams)
     int sms = 0, smem_optin = 0;
     bool persist_ok = false;         // device and weights allow it
-    uint32_t fused_max = kPersistMaxBatch;
+    uint32_t fused_min = kFusedMinBatch, fused_max = kPersistMaxBatch;
     uint32_t tensor_min = kTensorMinBatch;
     PersistLayer* d_players = nullptr;  // [n_layers]
     unsigned* d_bar = nullptr;
@@ -580,7 +581,7 @@ void release_pages(PhononCuda* c, uint32_t s) {
 // the two weight buffers (QKV|up and out|down rows of one CTA), then the
 // mbarriers and flags. False when it exceeds the per-CTA opt-in limit.
 struct PersistShape {
-    int n_groups = 0, smem = 0, off_x = 0, off_w0 = 0, off_w1 = 0, off_norm = 0, off_bar = 0;
+    int n_groups = 0, smem = 0, off_x = 0, off_w0 = 0, off_w1 = 0, off_norm = 0, off_bar = 0, ring = 0;
 };
 
 bool persist_shape(int R, int G, int smem_limit, bool bf16, PersistShape* out) {
@@ -588,12 +589,17 @@ bool persist_shape(int R, int G, int smem_limit, bool bf16, PersistShape* out) {
     sh.n_groups = (R + kPersistGroup - 1) / kPersistGroup;
     const int nct = G / sh.n_groups;
     if (R < 1 || nct < 1) return false;
-    const int ring = bf16 ? PersistAttn<true>::kBytes : PersistAttn<false>::kBytes;
-    const int x_bytes = std::max(ring, kPersistGroup * kFfn * 4);
     const int w0 = std::max(persist_cta_rows(PM_QKV, nct) * persist_row_bytes(PM_QKV),
                             persist_cta_rows(PM_UP, nct) * persist_row_bytes(PM_UP));
     const int w1 = std::max(persist_cta_rows(PM_OUT, nct) * persist_row_bytes(PM_OUT),
                             persist_cta_rows(PM_DOWN, nct) * persist_row_bytes(PM_DOWN));
+    // The page ring takes what is left, between 2 and kPersistMaxRing stages;
+    // the same region holds the GELU rows of a group in stage E.
+    const int stage = bf16 ? PersistAttn<true>::kStageBytes : PersistAttn<false>::kStageBytes;
+    const int left = smem_limit - (w0 + w1 + kPersistNormBytes + 128 + 1024);
+    sh.ring = std::min(kPersistMaxRing, left / stage);
+    const int x_bytes = std::max(sh.ring * stage, kPersistGroup * kFfn * 4);
+    if (sh.ring < 2 || x_bytes > left) return false;
     sh.off_x = 0;
     sh.off_w0 = x_bytes;
     sh.off_w1 = sh.off_w0 + w0;
@@ -606,7 +612,8 @@ bool persist_shape(int R, int G, int smem_limit, bool bf16, PersistShape* out) {
 
 // The whole step of this batch runs as one persistent launch.
 bool use_persist(const PhononCuda* c, int R, bool cancel) {
-    if (!c->persist_ok || cancel || R < 1 || static_cast<uint32_t>(R) > c->fused_max) return false;
+    if (!c->persist_ok || cancel || static_cast<uint32_t>(R) < c->fused_min || static_cast<uint32_t>(R) > c->fused_max)
+        return false;
     PersistShape sh;
     return persist_shape(R, c->sms, c->smem_optin, c->cfg.kv_type == PHONON_CUDA_KV_BF16, &sh);
 }
@@ -1068,6 +1075,7 @@ int enqueue_persist(PhononCuda* c, const Batch& b, const float* in, float* final
     pp.off_w1 = sh.off_w1;
     pp.off_norm = sh.off_norm;
     pp.off_bar = sh.off_bar;
+    pp.ring = sh.ring;
     double weights = 0.0;
     for (const DevLayer& D : c->layers)
         weights += linear_bytes(D.qkv) + linear_bytes(D.out) + linear_bytes(D.up) + linear_bytes(D.down);
@@ -1415,10 +1423,13 @@ uint64_t phonon_cuda_launch_count(PhononCuda* c) {
     return c->launches;
 }
 
-int phonon_cuda_set_batch_paths(PhononCuda* c, uint32_t fused_max_batch, uint32_t tensor_min_batch) {
-    if (!c || fused_max_batch > PHONON_CUDA_FUSED_MAX_BATCH || tensor_min_batch < 1) return PHONON_CUDA_INVALID_ARGUMENT;
+int phonon_cuda_set_batch_paths(PhononCuda* c, uint32_t fused_min_batch, uint32_t fused_max_batch,
+                                uint32_t tensor_min_batch) {
+    if (!c || fused_min_batch < 1 || fused_max_batch > PHONON_CUDA_FUSED_MAX_BATCH || tensor_min_batch < 1)
+        return PHONON_CUDA_INVALID_ARGUMENT;
     std::lock_guard<std::mutex> g(c->mu);
     if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    c->fused_min = fused_min_batch;
     c->fused_max = fused_max_batch;
     c->tensor_min = tensor_min_batch;
     drop_graph(c);  // a captured step holds the old path choice

@@ -64,11 +64,13 @@ constexpr int kPersistMinChunk = 4;                       // pages per attention
 constexpr int kPersistNormBytes = 2 * kWidth * 4;         // LayerNorm weight + bias, fp32
 constexpr long long kDrainBudgetCycles = 1ll << 28;       // ~0.14 s
 
+// Page ring of stage B: one stage = the K and V blocks of one page; the
+// number of stages (2..kPersistMaxRing) is what shared memory leaves after
+// the weight buffers, chosen per launch.
+constexpr int kPersistMaxRing = 6;
 template <bool kBf16>
 struct PersistAttn {
-    static constexpr int kStages = kBf16 ? 3 : 2;
     static constexpr int kStageBytes = AttnTma<kBf16>::kStageBytes;
-    static constexpr int kBytes = kStages * kStageBytes;
 };
 
 enum PersistMat : int { PM_QKV = 0, PM_OUT = 1, PM_UP = 2, PM_DOWN = 3 };
@@ -77,9 +79,10 @@ __host__ __device__ constexpr int persist_rows(int m) { return m == PM_QKV ? 153
 __host__ __device__ constexpr int persist_cols(int m) { return m == PM_DOWN ? 2048 : 512; }
 // Shared-memory bytes per weight row: int8 plane + binary16 block scales.
 __host__ __device__ constexpr int persist_row_bytes(int m) { return persist_cols(m) + persist_cols(m) / 16; }
-// Rows of matrix m held by one CTA of a group of nct CTAs (at most).
+// Rows of matrix m held by one CTA of a group of nct CTAs (at most); rows go
+// in quads (two RoPE pairs), the unit of one warp task.
 __host__ __device__ constexpr int persist_cta_rows(int m, int nct) {
-    return 2 * ((persist_rows(m) / 2 + nct - 1) / nct);
+    return 4 * ((persist_rows(m) / 4 + nct - 1) / nct);
 }
 
 struct PersistLayer {
@@ -105,17 +108,18 @@ struct PersistParams {
     float2* rope;              // [R][32] (cos, sin), written in stage 0
     KvView kv;                 // kv.table is written in stage 0 (page updates)
     int off_x, off_w0, off_w1, off_norm, off_bar;  // shared-memory offsets from the 1024-aligned base
+    int ring;                  // stage-B ring stages (2..kPersistMaxRing)
 };
 
 struct RowSlice {
-    int row0, n_pairs;
+    int row0, n_quads;
 };
 
 __device__ __forceinline__ RowSlice persist_slice(int m, int grank, int nct) {
-    const int pairs = persist_rows(m) / 2;
-    const int per = (pairs + nct - 1) / nct;
-    const int p0 = grank * per;
-    return RowSlice{2 * p0, max(0, min(per, pairs - p0))};
+    const int quads = persist_rows(m) / 4;
+    const int per = (quads + nct - 1) / nct;
+    const int q0 = grank * per;
+    return RowSlice{4 * q0, max(0, min(per, quads - q0))};
 }
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -171,8 +175,8 @@ __device__ __forceinline__ void grid_sync(const PersistParams& p, unsigned& epoc
 __device__ __forceinline__ void fill_weights(uint8_t* buf, uint32_t bar, const PersistLayer& L, int m, RowSlice rs,
                                              uint8_t* norm_dst, const float* norm) {
     const int cols = persist_cols(m);
-    const uint32_t wbytes = static_cast<uint32_t>(rs.n_pairs) * 2 * cols;
-    const uint32_t sbytes = static_cast<uint32_t>(rs.n_pairs) * 2 * (cols / 32) * 2;
+    const uint32_t wbytes = static_cast<uint32_t>(rs.n_quads) * 4 * cols;
+    const uint32_t sbytes = static_cast<uint32_t>(rs.n_quads) * 4 * (cols / 32) * 2;
     mbar_expect_tx(bar, wbytes + sbytes + (norm_dst ? kPersistNormBytes : 0));
     if (wbytes) {
         bulk_load(smem_addr(buf), L.plane[m] + static_cast<size_t>(rs.row0) * cols, wbytes, bar);
@@ -181,68 +185,77 @@ __device__ __forceinline__ void fill_weights(uint8_t* buf, uint32_t bar, const P
     if (norm_dst) bulk_load(smem_addr(norm_dst), norm, kPersistNormBytes, bar);
 }
 
-// Sum over the warp of 16 per-lane values v[rr][bb] (rr < 2, bb < 8) by
+// Sum over the warp of 32 per-lane values v[rr][bb] (rr < 4, bb < 8) by
 // recursive halving: at each of the five levels (xor 16, 8, 4, 2, 1) a lane
 // keeps half of its values and adds the partner's copy of them. The additions
 // are those of a butterfly warp_sum of each value (same pairs, same levels),
-// so the sums are the same to the bit; lane l ends with value (l >> 4, (l >> 1) & 7).
-__device__ __forceinline__ float warp_reduce16(const float (&v)[2][kPersistGroup]) {
+// so the sums are the same to the bit; lane l ends with value (l >> 3, l & 7).
+__device__ __forceinline__ float warp_reduce32(const float (&v)[4][kPersistGroup]) {
     const int lane = threadIdx.x & 31;
-    float a[8], b[4], c[2];
+    float a[16], b[8], c[4], d[2];
     const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float keep = u16 ? v[1][i] : v[0][i], send = u16 ? v[0][i] : v[1][i];
-        a[i] = keep + __shfl_xor_sync(kFull, send, 16);
+    for (int i = 0; i < 16; ++i) {  // value index i (+16): rr = i >> 3 (+2), bb = i & 7
+        const float lo = v[i >> 3][i & 7], hi = v[2 + (i >> 3)][i & 7];
+        a[i] = (u16 ? hi : lo) + __shfl_xor_sync(kFull, u16 ? lo : hi, 16);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float keep = u8 ? a[i + 4] : a[i], send = u8 ? a[i] : a[i + 4];
-        b[i] = keep + __shfl_xor_sync(kFull, send, 8);
-    }
+    for (int i = 0; i < 8; ++i) b[i] = (u8 ? a[i + 8] : a[i]) + __shfl_xor_sync(kFull, u8 ? a[i] : a[i + 8], 8);
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const float keep = u4 ? b[i + 2] : b[i], send = u4 ? b[i] : b[i + 2];
-        c[i] = keep + __shfl_xor_sync(kFull, send, 4);
-    }
-    const float keep = u2 ? c[1] : c[0], send = u2 ? c[0] : c[1];
-    const float d = keep + __shfl_xor_sync(kFull, send, 2);
-    return d + __shfl_xor_sync(kFull, d, 1);
+    for (int i = 0; i < 4; ++i) c[i] = (u4 ? b[i + 4] : b[i]) + __shfl_xor_sync(kFull, u4 ? b[i] : b[i + 4], 4);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) d[i] = (u2 ? c[i + 2] : c[i]) + __shfl_xor_sync(kFull, u2 ? c[i] : c[i + 2], 2);
+    const bool u1 = lane & 1;
+    return (u1 ? d[1] : d[0]) + __shfl_xor_sync(kFull, u1 ? d[0] : d[1], 1);
 }
 
-// The CTA's row pairs of one projection against the group's streams: weights
-// (rows rs.row0 ..) and activations xs[nb][cols] in shared memory. Lane j < nb
-// finishes stream b0 + j; its epilogue operands (residual pair, RoPE angles,
-// KV page) are loaded before the dot products so their latency overlaps them.
+// Four signed int8 weights of a word as exact floats: each byte, offset by
+// 128, is placed in the mantissa of 2^23 and the offset subtracted again.
+__device__ __forceinline__ void i8x4_to_float(uint32_t word, float* f) {
+    const uint32_t u = word ^ 0x80808080u;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+        f[e] = __uint_as_float(__byte_perm(u, 0x4B000000u, e | (4 << 4) | (5 << 8) | (7 << 12))) - 8388736.0f;
+}
+
+// The CTA's row quads of one projection against the group's streams: weights
+// (rows rs.row0 ..) and activations xs[nb][cols] in shared memory. After the
+// reduction lane l holds row r0 + (l >> 3) of stream b0 + (l & 7) and runs
+// its epilogue (for RoPE the even row of a pair rotates both); the epilogue
+// operands are loaded before the dot products so their latency overlaps them.
 template <int kChunks, int kEpi>
 __device__ __forceinline__ void persist_gemv(const PersistParams& p, int layer, const uint8_t* wb, RowSlice rs,
                                              const float* xs, int b0, int nb, const float* res, float* y, int ldy) {
     constexpr int cols = kChunks * 512;
-    const __half* wsc = reinterpret_cast<const __half*>(wb + static_cast<size_t>(rs.n_pairs) * 2 * cols);
+    const __half* wsc = reinterpret_cast<const __half*>(wb + static_cast<size_t>(rs.n_quads) * 4 * cols);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int eb = b0 + min(lane, nb - 1);  // this lane's epilogue stream (clamped for idle lanes)
-    for (int t = warp; t < rs.n_pairs; t += kPersistWarps) {
-        const int r0 = rs.row0 + 2 * t;
-        float2 pre = make_float2(0.0f, 0.0f);
+    const int my_rr = lane >> 3, my_bb = lane & 7;
+    const bool my_live = my_bb < nb;
+    const int eb = b0 + min(my_bb, nb - 1);  // this lane's epilogue stream (clamped for idle lanes)
+    for (int t = warp; t < rs.n_quads; t += kPersistWarps) {
+        const int r0 = rs.row0 + 4 * t;
+        const int my_r = r0 + my_rr;
+        float pre = 0.0f;
+        float2 cs = make_float2(1.0f, 0.0f);
         int page = 0;
-        if constexpr (kEpi == EPI_RESID) pre = __ldcg(reinterpret_cast<const float2*>(res + static_cast<size_t>(eb) * kWidth + r0));
+        if constexpr (kEpi == EPI_RESID) pre = __ldcg(res + static_cast<size_t>(eb) * kWidth + my_r);
         if constexpr (kEpi == EPI_QKV) {
             const int region = r0 >> 9;
-            if (region < 2) pre = __ldcg(p.rope + eb * 32 + ((r0 & 63) >> 1));
+            if (region < 2) cs = __ldcg(p.rope + eb * 32 + ((my_r & 63) >> 1));
             if (region > 0)
                 page = __ldcg(p.kv.table + static_cast<size_t>(p.slot[eb]) * p.kv.max_pages + p.pos[eb] / kPage);
         }
-        float acc[2][kPersistGroup];
+        float acc[4][kPersistGroup];
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr)
+        for (int rr = 0; rr < 4; ++rr)
 #pragma unroll
             for (int bb = 0; bb < kPersistGroup; ++bb) acc[rr][bb] = 0.0f;
-#pragma unroll
+#pragma unroll 1
         for (int c = 0; c < kChunks; ++c) {
-            float wf[2][16], sc[2][4];
+            float wf[4][16], sc[4][4];
 #pragma unroll
-            for (int rr = 0; rr < 2; ++rr) {
-                const int lr = 2 * t + rr;
+            for (int rr = 0; rr < 4; ++rr) {
+                const int lr = 4 * t + rr;
                 const uint4 wq = *reinterpret_cast<const uint4*>(wb + static_cast<size_t>(lr) * cols + c * 512 + lane * 16);
                 const uint2 raw = *reinterpret_cast<const uint2*>(wsc + static_cast<size_t>(lr) * (cols / 32) + c * 16 +
                                                                   (lane >> 3) * 4);
@@ -252,12 +265,10 @@ __device__ __forceinline__ void persist_gemv(const PersistParams& p, int layer, 
                 sc[rr][1] = __high2float(h01);
                 sc[rr][2] = __low2float(h23);
                 sc[rr][3] = __high2float(h23);
-                const uint32_t words[4] = {wq.x, wq.y, wq.z, wq.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        wf[rr][j * 4 + e] = static_cast<float>(static_cast<int8_t>((words[j] >> (8 * e)) & 0xffu));
+                i8x4_to_float(wq.x, wf[rr] + 0);
+                i8x4_to_float(wq.y, wf[rr] + 4);
+                i8x4_to_float(wq.z, wf[rr] + 8);
+                i8x4_to_float(wq.w, wf[rr] + 12);
             }
 #pragma unroll
             for (int bb = 0; bb < kPersistGroup; ++bb) {
@@ -267,7 +278,7 @@ __device__ __forceinline__ void persist_gemv(const PersistParams& p, int layer, 
 #pragma unroll
                     for (int j = 0; j < 4; ++j) xv[j] = *reinterpret_cast<const float4*>(xr + j * 128);
 #pragma unroll
-                    for (int rr = 0; rr < 2; ++rr) {
+                    for (int rr = 0; rr < 4; ++rr) {
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             float part = wf[rr][j * 4 + 0] * xv[j].x;
@@ -280,15 +291,15 @@ __device__ __forceinline__ void persist_gemv(const PersistParams& p, int layer, 
                 }
             }
         }
-        const float red = warp_reduce16(acc);
-        float v0 = __shfl_sync(kFull, red, 2 * (lane & 7));       // (row r0, stream lane)
-        float v1 = __shfl_sync(kFull, red, 16 + 2 * (lane & 7));  // (row r0 + 1, stream lane)
-        if (lane >= nb) continue;
-        const int b = b0 + lane;
+        float v = warp_reduce32(acc);  // (row r0 + my_rr, stream b0 + my_bb)
+        const int b = b0 + my_bb;
         if constexpr (kEpi == EPI_QKV) {
+            const float partner = __shfl_xor_sync(kFull, v, 8);  // the other row of this lane's RoPE pair
+            if (!my_live || (my_rr & 1)) continue;
             const int region = r0 >> 9;  // 0 = q, 1 = k, 2 = v
-            const int within = r0 & 511;
-            if (region < 2) rope_apply(v0, v1, pre);
+            const int within = my_r & 511;
+            float v0 = v, v1 = partner;
+            if (region < 2) rope_apply(v0, v1, cs);
             if (!isfinite(v0) || !isfinite(v1)) flag_nonfinite(p.status, b);
             if (region == 0) {
                 *reinterpret_cast<float2*>(p.q + static_cast<size_t>(b) * kWidth + within) = make_float2(v0, v1);
@@ -298,17 +309,14 @@ __device__ __forceinline__ void persist_gemv(const PersistParams& p, int layer, 
                 kv_store2(p.kv, off, v0, v1);
             }
         } else {
-            if constexpr (kEpi == EPI_RESID) {
-                v0 = __fadd_rn(pre.x, v0);
-                v1 = __fadd_rn(pre.y, v1);
-            }
+            if (!my_live) continue;
+            if constexpr (kEpi == EPI_RESID) v = __fadd_rn(pre, v);
             if constexpr (kEpi == EPI_GELU) {
-                if (!isfinite(v0) || !isfinite(v1)) flag_nonfinite(p.status, b);
-                v0 = gelu_erf(v0);
-                v1 = gelu_erf(v1);
+                if (!isfinite(v)) flag_nonfinite(p.status, b);
+                v = gelu_erf(v);
             }
-            if (!isfinite(v0) || !isfinite(v1)) flag_nonfinite(p.status, b);
-            *reinterpret_cast<float2*>(y + static_cast<size_t>(b) * ldy + r0) = make_float2(v0, v1);
+            if (!isfinite(v)) flag_nonfinite(p.status, b);
+            y[static_cast<size_t>(b) * ldy + my_r] = v;
         }
     }
 }
@@ -324,7 +332,7 @@ __device__ __forceinline__ void persist_attention(const CUtensorMap* tm, const P
                                                   int* last_issue, volatile int* failed) {
     using A = PersistAttn<kBf16>;
     using T = AttnTma<kBf16>;
-    constexpr int kSt = A::kStages;
+    const uint32_t kSt = static_cast<uint32_t>(p.ring);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int s_begin = p.cta_split[blockIdx.x], s_end = p.cta_split[blockIdx.x + 1];
     if (warp == kPersistWarps) {
@@ -336,8 +344,7 @@ __device__ __forceinline__ void persist_attention(const CUtensorMap* tm, const P
             for (int i = 0; i < sp.page_count; ++i, ++n) {
                 if (lane != 0 || *failed) continue;
                 const int st = static_cast<int>(n % kSt);
-                if (n >= static_cast<uint32_t>(kSt) && !mbar_wait(empty0 + 8 * st, ((n / kSt) - 1) & 1, p.error, failed))
-                    continue;
+                if (n >= kSt && !mbar_wait(empty0 + 8 * st, ((n / kSt) - 1) & 1, p.error, failed)) continue;
                 const int page = __ldcg(table + sp.page_begin + i);
                 const int row0 = (page * p.n_layers + layer) * 256;  // K block; V block follows
                 uint8_t* stage = stages + st * A::kStageBytes;
@@ -512,7 +519,7 @@ __device__ __forceinline__ void persist_merge(const PersistParams& p, float* xs,
 template <bool kBf16>
 __global__ void __launch_bounds__(kPersistThreads, 1)
     step_persist_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ PersistParams p) {
-    constexpr int kSt = PersistAttn<kBf16>::kStages;
+    constexpr int kSt = kPersistMaxRing;  // mbarrier slots; p.ring of them are used
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* xs = reinterpret_cast<float*>(smem + p.off_x);
@@ -534,7 +541,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
                             persist_slice(PM_UP, grank, nct), persist_slice(PM_DOWN, grank, nct)};
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kSt; ++s) {
+        for (int s = 0; s < p.ring; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, kPersistWarps);
         }
@@ -670,8 +677,9 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
 
     // Copies still in flight (only after a failure) land before the CTA exits.
     if (copy_lane) {
-        for (int s = 0; s < kSt; ++s)
-            if (last_issue[s] >= 0) mbar_drain(full0 + 8 * s, (static_cast<uint32_t>(last_issue[s]) / kSt) & 1);
+        for (int s = 0; s < p.ring; ++s)
+            if (last_issue[s] >= 0)
+                mbar_drain(full0 + 8 * s, (static_cast<uint32_t>(last_issue[s]) / static_cast<uint32_t>(p.ring)) & 1);
         for (int k = 0; k < 2; ++k)
             if (issued[k] > 0) mbar_drain(wfull0 + 8 * k, (issued[k] - 1) & 1);
         if (xissued > 0) mbar_drain(xfull, (xissued - 1) & 1);

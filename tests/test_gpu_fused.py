@@ -22,9 +22,9 @@ NO_TENSOR = 1 << 20
 def _pair(weights, kv_type):
     kw = dict(max_streams=72, max_batch=64, pool_pages=2048, kv_type=kv_type)
     fused = rt.Context(weights, **kw)
-    fused.set_batch_paths(rt.FUSED_MAX_BATCH, NO_TENSOR)
+    fused.set_batch_paths(1, rt.FUSED_MAX_BATCH, NO_TENSOR)
     staged = rt.Context(weights, **kw)
-    staged.set_batch_paths(0, NO_TENSOR)
+    staged.set_batch_paths(rt.FUSED_MAX_BATCH + 1, rt.FUSED_MAX_BATCH, NO_TENSOR)
     return fused, staged
 
 
