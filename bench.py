@@ -314,6 +314,8 @@ def run_ours(args):
     if world == 1 and not args.quick:
         extras["single_stream"] = bench_single_stream(rt, synth, weights, torch)
         extras["q8_matvec"] = bench_q8_matvec(rt, synth, torch, args.matvec_reps)
+        extras["config2"] = bench_config2(rt, weights, torch)
+        extras["config4"] = bench_config4(rt, weights, torch)
 
     if rank == 0:
         peak, peak_kind = measured_hbm_gbs()
@@ -398,18 +400,141 @@ def bench_single_stream(rt, synth, weights, torch):
             "l2": "flushed before each step"}
 
 
+WEIGHT_BYTES_PER_LAYER = 3_342_336  # Q8_0 qkv + out + up + down (34-byte blocks of 32)
+
+
+def decode_run(rt, weights, torch, lengths, steps, kv_type, profile_every=0):
+    """Decode `steps` frames of len(lengths) streams whose caches start with
+    lengths[i] synthetic positions, every stream in every step (device
+    buffers, one sync per step, as a serving loop). Returns frames/s, ms per
+    step and the step's algorithmic HBM bytes per second (weights + K/V read
+    + K/V appended)."""
+    R = len(lengths)
+    esize = 2 if kv_type == rt.KV_BF16 else 4
+    pages = sum((int(n) + steps + 15) // 16 + 1 for n in lengths)
+    ctx = rt.Context(weights, max_streams=R + 1, max_batch=R, pool_pages=pages + 8, kv_type=kv_type)
+    ss = [ctx.stream_alloc(int(n) + steps + 1) for n in lengths]
+    for i, (s, n) in enumerate(zip(ss, lengths)):
+        ctx.fill_synthetic(s, int(n), 500 + i)
+    x = torch.randn(R, 512, device="cuda")
+    y = torch.empty(R, 512, device="cuda")
+    stream = torch.cuda.ExternalStream(ctx.cuda_stream())
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    step_bytes = 0.0
+    for k in range(steps):
+        pos = [int(n) + k for n in lengths]
+        ctx.step_device(ss, pos, x.data_ptr(), y.data_ptr())
+        if ctx.sync(R).any():
+            raise RuntimeError("non-finite step")
+        keys = sum(p + 1 for p in pos)
+        step_bytes += N_LAYERS * (WEIGHT_BYTES_PER_LAYER + (keys + R) * 2 * 512 * esize)
+    b.record(stream)
+    b.synchronize()
+    ms = a.elapsed_time(b)
+    ctx.close()
+    return {"frames_per_s": round(R * steps / (ms * 1e-3), 1), "ms_per_step": round(ms / steps, 4),
+            "step_gbs": round(step_bytes / (ms * 1e-3) / 1e9, 1)}
+
+
+def attention_gbs(rt, weights, torch, lengths, steps, kv_type):
+    """Attention-only HBM GB/s: the same decode on the per-stage launches with
+    per-launch CUDA events (the persistent step has no separate attention
+    launch)."""
+    R = len(lengths)
+    pages = sum((int(n) + steps + 15) // 16 + 1 for n in lengths)
+    ctx = rt.Context(weights, max_streams=R + 1, max_batch=R, pool_pages=pages + 8, kv_type=kv_type)
+    ctx.set_batch_paths(rt.FUSED_MAX_BATCH + 1, rt.FUSED_MAX_BATCH, 32)
+    ss = [ctx.stream_alloc(int(n) + steps + 1) for n in lengths]
+    for i, (s, n) in enumerate(zip(ss, lengths)):
+        ctx.fill_synthetic(s, int(n), 500 + i)
+    x = torch.randn(R, 512, device="cuda")
+    y = torch.empty(R, 512, device="cuda")
+    ctx.profile(True)
+    for k in range(steps):
+        ctx.step_device(ss, [int(n) + k for n in lengths], x.data_ptr(), y.data_ptr())
+        ctx.sync(R)
+    prof = ctx.profile_read()
+    ctx.close()
+    att = prof["attention"]
+    return round(att["bytes"] / (att["ms"] * 1e-3) / 1e9, 1)
+
+
+def bench_config2(rt, weights, torch):
+    """64 streams, prefixes U[32,512] (seed 1), 250 decode steps,
+    fp32 KV pages (synthetic K/V for the prefixes)."""
+    lengths = np.random.default_rng(1).integers(32, 513, size=64)
+    r = decode_run(rt, weights, torch, lengths, 250, rt.KV_F32)
+    return {"workload": "configs[2]", **r, "bytes": "weights + K/V read + K/V append per step"}
+
+
+def bench_config4(rt, weights, torch):
+    """8 streams, 256-position prefixes, 4096 decode steps (up to
+    4352 positions), fp32 KV; whole-step GB/s over the run and attention-only
+    GB/s on a late window (contexts ~4000)."""
+    r = decode_run(rt, weights, torch, [256] * 8, 4096, rt.KV_F32)
+    att = attention_gbs(rt, weights, torch, [4000] * 8, 40, rt.KV_F32)
+    return {"workload": "configs[4]", **r, "attention_gbs_at_4000": att}
+
+
+def q8_stream_gbs(torch, lins, rows, cols, batch, wbytes, launches):
+    """Back-to-back matvecs captured in one CUDA graph (launch overhead out of
+    the way, consecutive launches overlapped by programmatic dependent
+    launch). Launch i reads lins[i % len(lins)]: with many device copies of
+    the matrix, together several times the 126 MB L2, every launch streams
+    its weights from HBM; with one copy they stay L2-resident. Returns
+    weight GB/s and microseconds per launch."""
+    copies = len(lins)
+    x = torch.randn(batch, cols, device="cuda")
+    y = torch.empty(batch, rows, device="cuda")
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        for lin in lins[:2]:  # first launches configure the kernels outside the capture
+            lin.apply_device(x.data_ptr(), batch, y.data_ptr(), side.cuda_stream)
+    side.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side, capture_error_mode="relaxed"):
+        for i in range(launches):
+            lins[i % copies].apply_device(x.data_ptr(), batch, y.data_ptr(), side.cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    a.record(cur)
+    for _ in range(3):
+        graph.replay()
+    b.record(cur)
+    b.synchronize()
+    per_launch = a.elapsed_time(b) / (3 * launches)
+    del graph
+    return round(wbytes / (per_launch * 1e-3) / 1e9, 1), round(per_launch * 1e3, 3)
+
+
 def bench_q8_matvec(rt, synth, torch, reps):
     """configs[1]: the four projection shapes, per-row scales, batch 1/8/64;
-    GB/s of weight bytes. cold: L2 flushed before every launch; hot: back to
-    back on an L2-resident copy."""
+    GB/s of weight bytes. cold: L2 flushed before every single launch
+    (latency of one call); hot: back to back on an L2-resident copy;
+    stream_hbm / stream_l2: launches back to back in a CUDA graph over
+    rotating HBM-cold copies / one L2-resident copy (throughput, see
+    q8_stream_gbs)."""
     g = synth.Generator(1)
     flush = torch.zeros(64 * 2**20, device="cuda")
     out = {}
     stream = torch.cuda.current_stream()
     for name, (rows, cols) in {"qkv": (1536, 512), "out": (512, 512), "up": (2048, 512),
                                "down": (512, 2048)}.items():
-        lin = rt.Linear(g.q8_linear(rows, cols, synth.SCALE_PER_ROW), rows, cols)
+        data = g.q8_linear(rows, cols, synth.SCALE_PER_ROW)
+        lin = rt.Linear(data, rows, cols)
         wbytes = lin.bytes()
+        copies = -(-4 * 126 * 2**20 // wbytes)  # 4x L2
+        rot = [lin] + [rt.Linear(data, rows, cols) for _ in range(copies - 1)]
+        for batch in (1, 8):
+            hbm, hbm_us = q8_stream_gbs(torch, rot, rows, cols, batch, wbytes, copies)
+            l2, l2_us = q8_stream_gbs(torch, [lin], rows, cols, batch, wbytes, 512)
+            out[f"{name}_b{batch}_stream"] = {"stream_hbm_gbs": hbm, "stream_hbm_us": hbm_us,
+                                              "stream_l2_gbs": l2, "stream_l2_us": l2_us, "copies": copies}
+        for extra in rot[1:]:
+            extra.close()
         for batch in (1, 8, 64):
             x = torch.randn(batch, cols, device="cuda")
             y = torch.empty(batch, rows, device="cuda")
