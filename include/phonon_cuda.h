@@ -233,18 +233,22 @@ uint64_t phonon_cuda_launch_count(PhononCuda *ctx);
  * poll) of fused_min_batch..fused_max_batch streams runs as ONE persistent
  * launch that keeps a CTA on every SM for all layers; other batches run one
  * launch per stage, with the projections on the tensor cores from
- * tensor_min_batch streams up. Defaults: 8, PHONON_CUDA_FUSED_MAX_BATCH, 32
- * (a few streams are as fast one launch per stage). fused_min_batch >
- * fused_max_batch disables the persistent step; fused_min_batch = 0,
- * fused_max_batch > PHONON_CUDA_FUSED_MAX_BATCH or tensor_min_batch = 0 are
- * PHONON_CUDA_INVALID_ARGUMENT. The persistent and per-stage GEMV paths give
- * the same results bit for bit (the tensor-core path within the tolerances
- * of the reference's tests). The persistent step needs Q8_0 weights,
- * cooperative launch and enough shared memory for the batch; otherwise the
- * per-stage path runs. */
+ * tensor_min_batch streams up, and from split_min_batch streams up as two
+ * half batches on two CUDA streams, so that one half's attention overlaps
+ * the other half's projections. Defaults: 8, PHONON_CUDA_FUSED_MAX_BATCH, 32,
+ * 384 (a few streams are as fast one launch per stage; halves gain from a
+ * few hundred streams; the second lane exists when max_batch >= 96). A step
+ * on two lanes gives the same results as on one, bit for bit. fused_min_batch > fused_max_batch disables the
+ * persistent step; fused_min_batch = 0, fused_max_batch >
+ * PHONON_CUDA_FUSED_MAX_BATCH, tensor_min_batch = 0 or split_min_batch < 2
+ * are PHONON_CUDA_INVALID_ARGUMENT. The persistent and per-stage GEMV paths
+ * give the same results bit for bit (the tensor-core path within the
+ * tolerances of the reference's tests). The persistent step needs Q8_0
+ * weights, cooperative launch and enough shared memory for the batch;
+ * otherwise the per-stage path runs. */
 #define PHONON_CUDA_FUSED_MAX_BATCH 64
 int phonon_cuda_set_batch_paths(PhononCuda *ctx, uint32_t fused_min_batch, uint32_t fused_max_batch,
-                                uint32_t tensor_min_batch);
+                                uint32_t tensor_min_batch, uint32_t split_min_batch);
 
 const char *phonon_cuda_status_string(int status);
 

@@ -31,6 +31,8 @@ constexpr int kPrefillChunk = 256;  // rows per prefill pass
 constexpr int kTensorMinBatch = 32;  // streams from which projections run on tcgen05
 constexpr int kMaxSms = 1024;        // bound on the SM count (persistent split table)
 constexpr int kFusedMinBatch = 8;    // smaller batches are as fast or faster one launch per stage
+constexpr int kSplitMinBatch = 384;  // from here a step runs as two concurrent half batches
+constexpr int kLaneSplitTarget = 320;  // splits per step on two lanes: each half's attention leaves SMs to the other
 
 #define CUDA_TRY(expr)                                                                       \
     do {                                                                                     \
@@ -350,6 +352,20 @@ struct DevLayer {
     bool q8 = true;
 };
 
+// Per-step scratch and stream of one lane. A large batch can be split over
+// two lanes that run concurrently (one half's attention overlaps the other
+// half's projections); lane 0 uses the context's main stream and buffers.
+struct Lane {
+    cudaStream_t stream = nullptr;
+    float *x0 = nullptr, *x1 = nullptr, *q = nullptr, *a = nullptr, *h = nullptr, *g = nullptr, *part = nullptr;
+    int32_t *meta = nullptr, *h_meta = nullptr;
+    int8_t *dig512 = nullptr, *dig2048 = nullptr;
+    int32_t* exps = nullptr;
+    CUtensorMap tm_dig512, tm_dig2048;
+    float2* rope = nullptr;
+    cudaEvent_t ready = nullptr;  // recorded when the lane's share of a step is enqueued
+};
+
 struct PhononCuda {
     PhononCudaConfig cfg{};
     std::mutex mu;
@@ -374,10 +390,14 @@ struct PhononCuda {
     // KV pool as rows of 64 head dims for TMA page staging
     CUtensorMap tm_kv;
     bool attn_tma = false;
+    Lane lanes[2];
+    bool lane1_ok = false;  // second lane allocated
     // Whole-step persistent kernel (batches up to fused_max streams)
     int sms = 0, smem_optin = 0;
     bool persist_ok = false;         // device and weights allow it
     uint32_t fused_min = kFusedMinBatch, fused_max = kPersistMaxBatch;
+    uint32_t split_min = kSplitMinBatch;  // batches from which a step runs on two lanes
+    cudaEvent_t fork = nullptr, join = nullptr;
     uint32_t tensor_min = kTensorMinBatch;
     PersistLayer* d_players = nullptr;  // [n_layers]
     unsigned* d_bar = nullptr;
@@ -494,18 +514,20 @@ struct LaunchScope {
     PhononCuda* c;
     int cls;
     double bytes;
+    cudaStream_t s;
     cudaEvent_t a = nullptr;
-    LaunchScope(PhononCuda* c_, int cls_, double bytes_) : c(c_), cls(cls_), bytes(bytes_) {
+    LaunchScope(PhononCuda* c_, int cls_, double bytes_, cudaStream_t s_ = nullptr)
+        : c(c_), cls(cls_), bytes(bytes_), s(s_ ? s_ : c_->stream) {
         c->launches++;
         if (c->prof_on) {
             a = prof_event(c);
-            cudaEventRecord(a, c->stream);
+            cudaEventRecord(a, s);
         }
     }
     ~LaunchScope() {
         if (!a) return;
         cudaEvent_t b = prof_event(c);
-        cudaEventRecord(b, c->stream);
+        cudaEventRecord(b, s);
         c->prof_pending.push_back({cls, a, b, bytes});
     }
 };
@@ -533,6 +555,9 @@ double linear_bytes(const DevLinear& l) { return static_cast<double>(l.bytes); }
 struct Batch {
     int R = 0, S = 0, U = 0;
     bool persist = false;  // whole step in step_persist_kernel
+    bool split = false;    // one lane's share of a step split over two lanes
+    Lane* lane = nullptr;
+    int32_t* d_status = nullptr;  // status words of this batch's entries
     double keys = 0;  // sum over entries of (position + 1)
     float2* d_rope = nullptr;  // [R][32] (cos, sin) of this batch's positions
     int32_t *d_slot, *d_pos, *d_first, *d_count, *d_updates;
@@ -623,11 +648,14 @@ bool use_persist(const PhononCuda* c, int R, bool cancel) {
 // device_prep false the RoPE table and the page updates are left to the
 // persistent kernel.
 int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vector<int32_t>& pos,
-                 const std::vector<int32_t>& updates, Batch* out, bool device_prep = true) {
+                 const std::vector<int32_t>& updates, Batch* out, bool device_prep = true, Lane* lane = nullptr,
+                 int32_t* status = nullptr, long long plan_pps = 0) {
+    if (!lane) lane = &c->lanes[0];
+    if (!status) status = c->d_status;
     const int R = static_cast<int>(slot.size());
     long long total_pages = 0;
     for (int e = 0; e < R; ++e) total_pages += pos[e] / kPage + 1;
-    int32_t* m = c->h_meta;
+    int32_t* m = lane->h_meta;
     int32_t *h_slot = m, *h_pos = m + R, *h_first = m + 2 * R, *h_count = m + 3 * R;
     Split* h_splits = reinterpret_cast<Split*>(m + 4 * R);
     int S = 0;
@@ -643,11 +671,14 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     // (entry, page) order cut into at most one balanced chunk per SM (>=
     // kPersistMinChunk pages); a chunk is one split per entry segment it
     // covers, and chunk k's splits are [cta_split[k], cta_split[k+1]).
-    const bool chunked = R <= PHONON_CUDA_FUSED_MAX_BATCH && c->sms > 0;
+    // plan_pps > 0: pages per split fixed by the caller (a half batch keeps
+    // the split plan of its whole step).
+    const bool chunked = plan_pps == 0 && R <= PHONON_CUDA_FUSED_MAX_BATCH && c->sms > 0;
     const int G = chunked ? c->sms : 0;
     std::vector<int32_t> cta_split;
     if (!chunked) {
-        const long long pps = std::max<long long>(1, (total_pages + kSplitTarget - 1) / kSplitTarget);
+        const long long pps =
+            plan_pps > 0 ? plan_pps : std::max<long long>(1, (total_pages + kSplitTarget - 1) / kSplitTarget);
         for (int e = 0; e < R; ++e) {
             const int n_keys = pos[e] + 1, n_pages = pos[e] / kPage + 1;
             h_first[e] = S;
@@ -691,33 +722,35 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     std::memcpy(h_upd, updates.data(), updates.size() * 4);
     if (chunked) std::memcpy(h_upd + 3 * U, cta_split.data(), cta_split.size() * 4);
     const size_t bytes = static_cast<size_t>(4 * R + 4 * S + 3 * U + (chunked ? G + 1 : 0)) * 4;
-    CUDA_TRY(cudaMemcpyAsync(c->d_meta, c->h_meta, bytes, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(lane->meta, lane->h_meta, bytes, cudaMemcpyHostToDevice, lane->stream));
     Batch b;
+    b.lane = lane;
+    b.d_status = status;
     b.R = R;
     b.S = S;
     b.U = U;
     for (int e = 0; e < R; ++e) b.keys += pos[e] + 1;
-    b.d_slot = c->d_meta;
-    b.d_pos = c->d_meta + R;
-    b.d_first = c->d_meta + 2 * R;
-    b.d_count = c->d_meta + 3 * R;
-    b.d_splits = reinterpret_cast<Split*>(c->d_meta + 4 * R);
-    b.d_updates = c->d_meta + 4 * R + 4 * S;
+    b.d_slot = lane->meta;
+    b.d_pos = lane->meta + R;
+    b.d_first = lane->meta + 2 * R;
+    b.d_count = lane->meta + 3 * R;
+    b.d_splits = reinterpret_cast<Split*>(lane->meta + 4 * R);
+    b.d_updates = lane->meta + 4 * R + 4 * S;
     b.d_cta_split = b.d_updates + 3 * U;
-    b.d_rope = c->d_rope;
+    b.d_rope = lane->rope;
     b.persist = !device_prep;
     if (!device_prep) {
         *out = b;
         return PHONON_CUDA_OK;
     }
     {
-        LaunchScope ls(c, PHONON_CUDA_K_OTHER, R * 32 * 12.0);
-        CUDA_TRY(launch_pdl(rope_table_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, c->stream,
+        LaunchScope ls(c, PHONON_CUDA_K_OTHER, R * 32 * 12.0, b.lane->stream);
+        CUDA_TRY(launch_pdl(rope_table_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, lane->stream,
                             static_cast<const int32_t*>(b.d_pos), static_cast<const float*>(c->d_freq), R, b.d_rope));
     }
     if (U > 0) {
-        LaunchScope ls(c, PHONON_CUDA_K_OTHER, U * 12.0);
-        CUDA_TRY(launch_pdl(page_update_kernel, dim3((U + 127) / 128), dim3(128), 0, c->stream, c->d_table,
+        LaunchScope ls(c, PHONON_CUDA_K_OTHER, U * 12.0, b.lane->stream);
+        CUDA_TRY(launch_pdl(page_update_kernel, dim3((U + 127) / 128), dim3(128), 0, lane->stream, c->d_table,
                             kMaxPagesPerStream, static_cast<const int32_t*>(b.d_updates), U));
     }
     *out = b;
@@ -730,24 +763,24 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out = fa
 // Split-K attention then the split merge. With digits_out the merge writes
 // the digit rows of the attention output (tensor-core path) instead of fp32.
 int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out) {
-    cudaStream_t s = c->stream;
+    cudaStream_t s = b.lane->stream;
     const KvView kv = kv_view(c);
     const double act = 4.0 * b.R;
     const double esize = kv.bf16 ? 2.0 : 4.0;
     AttnParams ap{};
-    ap.q = c->d_q;
+    ap.q = b.lane->q;
     ap.slot = b.d_slot;
     ap.splits = b.d_splits;
     ap.n_splits = b.S;
     ap.kv = kv;
     ap.layer = l;
-    ap.part = c->d_part;
-    ap.status = c->d_status;
+    ap.part = b.lane->part;
+    ap.status = b.d_status;
     const long long warps = static_cast<long long>(b.S) * kHeads;
     const unsigned grid = static_cast<unsigned>((warps + kAttnWarps - 1) / kAttnWarps);
     {
         LaunchScope ls(c, PHONON_CUDA_K_ATTENTION,
-                       b.keys * 2.0 * kWidth * esize + act * kWidth + b.S * kHeads * kPartStride * 4.0);
+                       b.keys * 2.0 * kWidth * esize + act * kWidth + b.S * kHeads * kPartStride * 4.0, b.lane->stream);
         if (c->attn_tma) {
             CUDA_TRY(kv.bf16 ? launch_attn_tma<true>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.S, s)
                              : launch_attn_tma<false>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.S, s));
@@ -757,20 +790,20 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out) {
         }
     }
     CombineParams cp{};
-    cp.part = c->d_part;
+    cp.part = b.lane->part;
     cp.first = b.d_first;
     cp.count = b.d_count;
     cp.B = b.R;
-    cp.out = c->d_a;
-    cp.status = c->d_status;
+    cp.out = b.lane->a;
+    cp.status = b.d_status;
     if (digits_out) {
         const int Bpad = (b.R + 31) / 32 * 32;
-        LaunchScope ls(c, PHONON_CUDA_K_COMBINE, b.S * kHeads * kPartStride * 4.0 + kDigits * Bpad * 512.0);
-        CUDA_TRY(launch_pdl(attn_combine_digits_kernel, dim3(Bpad), dim3(256), 0, s, cp, Bpad, c->d_dig512, c->d_exps));
+        LaunchScope ls(c, PHONON_CUDA_K_COMBINE, b.S * kHeads * kPartStride * 4.0 + kDigits * Bpad * 512.0, b.lane->stream);
+        CUDA_TRY(launch_pdl(attn_combine_digits_kernel, dim3(Bpad), dim3(256), 0, s, cp, Bpad, b.lane->dig512, b.lane->exps));
         return PHONON_CUDA_OK;
     }
     {
-        LaunchScope ls(c, PHONON_CUDA_K_COMBINE, b.S * kHeads * kPartStride * 4.0 + act * kWidth);
+        LaunchScope ls(c, PHONON_CUDA_K_COMBINE, b.S * kHeads * kPartStride * 4.0 + act * kWidth, b.lane->stream);
         CUDA_TRY(launch_pdl(attn_combine_kernel,
                             dim3(static_cast<unsigned>((static_cast<long long>(b.R) * kHeads + kAttnWarps - 1) / kAttnWarps)),
                             dim3(kAttnWarps * 32), 0, s, cp));
@@ -781,33 +814,33 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out) {
 // The same layer with the four projections on tcgen05 (digit-sliced int8).
 int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, float* out) {
     const DevLayer& L = c->layers[l];
-    cudaStream_t s = c->stream;
+    cudaStream_t s = b.lane->stream;
     const KvView kv = kv_view(c);
     const int B = b.R, Bpad = (b.R + 31) / 32 * 32, nd = kDigits * Bpad;
     const double act = 4.0 * B, esize = kv.bf16 ? 2.0 : 4.0, dig = kDigits * Bpad;
     GemmParams g{};
     g.B = B;
-    g.exps = c->d_exps;
-    g.status = c->d_status;
+    g.exps = b.lane->exps;
+    g.status = b.d_status;
     g.error = c->d_err;
     // 1. LN1 + digits, QKV + RoPE + KV append
     {
-        LaunchScope ls(c, PHONON_CUDA_K_QKV, act * kWidth + dig * 512);
-        CUDA_TRY((launch_digits<512, true>(in, kWidth, L.norms, L.norms + kWidth, B, Bpad, c->d_dig512, c->d_exps,
-                                           c->d_status, s)));
+        LaunchScope ls(c, PHONON_CUDA_K_QKV, act * kWidth + dig * 512, b.lane->stream);
+        CUDA_TRY((launch_digits<512, true>(in, kWidth, L.norms, L.norms + kWidth, B, Bpad, b.lane->dig512, b.lane->exps,
+                                           b.d_status, s)));
     }
     g.rows = 1536;
     g.K = 512;
     g.row_scale = L.qkv.row_scale;
-    g.q = c->d_q;
+    g.q = b.lane->q;
     g.slot = b.d_slot;
     g.pos = b.d_pos;
     g.rope = b.d_rope;
     g.kv = kv;
     g.layer = l;
     {
-        LaunchScope ls(c, PHONON_CUDA_K_QKV, 1536.0 * 512 + dig * 512 + act * kWidth + B * 2.0 * kWidth * esize);
-        CUDA_TRY(launch_gemm<GEPI_QKV>(L.qkv.tmap, c->tm_dig512, 1536, nd, g, s));
+        LaunchScope ls(c, PHONON_CUDA_K_QKV, 1536.0 * 512 + dig * 512 + act * kWidth + B * 2.0 * kWidth * esize, b.lane->stream);
+        CUDA_TRY(launch_gemm<GEPI_QKV>(L.qkv.tmap, b.lane->tm_dig512, 1536, nd, g, s));
     }
     // 2. attention; the combine writes the digit rows of the attention output
     int st = enqueue_attention(c, b, l, true);
@@ -819,45 +852,45 @@ int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, 
     go.row_scale = L.out.row_scale;
     go.res = in;
     go.ldres = kWidth;
-    go.y = c->d_h;
+    go.y = b.lane->h;
     go.ldy = kWidth;
     {
-        LaunchScope ls(c, PHONON_CUDA_K_OUT, 512.0 * 512 + dig * 512 + act * 2 * kWidth);
-        CUDA_TRY(launch_gemm<GEPI_RESID>(L.out.tmap, c->tm_dig512, 512, nd, go, s));
+        LaunchScope ls(c, PHONON_CUDA_K_OUT, 512.0 * 512 + dig * 512 + act * 2 * kWidth, b.lane->stream);
+        CUDA_TRY(launch_gemm<GEPI_RESID>(L.out.tmap, b.lane->tm_dig512, 512, nd, go, s));
     }
     // 4. g = GELU(LN2(h) Wup^T)
     {
-        LaunchScope ls(c, PHONON_CUDA_K_UP, act * kWidth + dig * 512);
-        CUDA_TRY((launch_digits<512, true>(c->d_h, kWidth, L.norms + 2 * kWidth, L.norms + 3 * kWidth, B, Bpad,
-                                           c->d_dig512, c->d_exps, c->d_status, s)));
+        LaunchScope ls(c, PHONON_CUDA_K_UP, act * kWidth + dig * 512, b.lane->stream);
+        CUDA_TRY((launch_digits<512, true>(b.lane->h, kWidth, L.norms + 2 * kWidth, L.norms + 3 * kWidth, B, Bpad,
+                                           b.lane->dig512, b.lane->exps, b.d_status, s)));
     }
     GemmParams gu = g;
     gu.rows = kFfn;
     gu.K = 512;
     gu.row_scale = L.up.row_scale;
-    gu.y = c->d_g;
+    gu.y = b.lane->g;
     gu.ldy = kFfn;
     {
-        LaunchScope ls(c, PHONON_CUDA_K_UP, 2048.0 * 512 + dig * 512 + act * kFfn);
-        CUDA_TRY(launch_gemm<GEPI_GELU>(L.up.tmap, c->tm_dig512, kFfn, nd, gu, s));
+        LaunchScope ls(c, PHONON_CUDA_K_UP, 2048.0 * 512 + dig * 512 + act * kFfn, b.lane->stream);
+        CUDA_TRY(launch_gemm<GEPI_GELU>(L.up.tmap, b.lane->tm_dig512, kFfn, nd, gu, s));
     }
     // 5. out = h + g Wdown^T
     {
-        LaunchScope ls(c, PHONON_CUDA_K_DOWN, act * kFfn + dig * 2048);
-        CUDA_TRY((launch_digits<2048, false>(c->d_g, kFfn, nullptr, nullptr, B, Bpad, c->d_dig2048, c->d_exps,
-                                             c->d_status, s)));
+        LaunchScope ls(c, PHONON_CUDA_K_DOWN, act * kFfn + dig * 2048, b.lane->stream);
+        CUDA_TRY((launch_digits<2048, false>(b.lane->g, kFfn, nullptr, nullptr, B, Bpad, b.lane->dig2048, b.lane->exps,
+                                             b.d_status, s)));
     }
     GemmParams gd = g;
     gd.rows = 512;
     gd.K = kFfn;
     gd.row_scale = L.down.row_scale;
-    gd.res = c->d_h;
+    gd.res = b.lane->h;
     gd.ldres = kWidth;
     gd.y = out;
     gd.ldy = kWidth;
     {
-        LaunchScope ls(c, PHONON_CUDA_K_DOWN, 512.0 * 2048 + dig * 2048 + act * 2 * kWidth);
-        CUDA_TRY(launch_gemm<GEPI_RESID>(L.down.tmap, c->tm_dig2048, 512, nd, gd, s));
+        LaunchScope ls(c, PHONON_CUDA_K_DOWN, 512.0 * 2048 + dig * 2048 + act * 2 * kWidth, b.lane->stream);
+        CUDA_TRY(launch_gemm<GEPI_RESID>(L.down.tmap, b.lane->tm_dig2048, 512, nd, gd, s));
     }
     return PHONON_CUDA_OK;
 }
@@ -867,11 +900,11 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     if (c->tensor_ok && b.R >= static_cast<int>(c->tensor_min) && L.qkv.tensor && L.out.tensor && L.up.tensor && L.down.tensor)
         return enqueue_layer_tensor(c, b, l, in, out);
     const bool q8 = L.q8;
-    cudaStream_t s = c->stream;
+    cudaStream_t s = b.lane->stream;
     const KvView kv = kv_view(c);
     GemvParams p{};
     p.B = b.R;
-    p.status = c->d_status;
+    p.status = b.d_status;
     // 1. LN1 -> QKV -> RoPE -> q scratch + KV append
     p.w = L.qkv.plane;
     p.scales = L.qkv.scales;
@@ -881,7 +914,7 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     p.ldx = kWidth;
     p.ln_w = L.norms;
     p.ln_b = L.norms + kWidth;
-    p.q = c->d_q;
+    p.q = b.lane->q;
     p.slot = b.d_slot;
     p.pos = b.d_pos;
     p.rope = b.d_rope;
@@ -890,7 +923,7 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     const double act = 4.0 * b.R;  // bytes per activation element across the batch
     const double esize = kv.bf16 ? 2.0 : 4.0;
     {
-        LaunchScope ls(c, PHONON_CUDA_K_QKV, linear_bytes(L.qkv) + act * (kWidth + kWidth) + b.R * 2.0 * kWidth * esize);
+        LaunchScope ls(c, PHONON_CUDA_K_QKV, linear_bytes(L.qkv) + act * (kWidth + kWidth) + b.R * 2.0 * kWidth * esize, b.lane->stream);
         CUDA_TRY((launch_gemv<1, true, EPI_QKV>(q8, p, s)));
     }
     // 2. split-K attention + combine
@@ -901,55 +934,55 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     // 3. h = x + attn Wout^T
     GemvParams po{};
     po.B = b.R;
-    po.status = c->d_status;
+    po.status = b.d_status;
     po.w = L.out.plane;
     po.scales = L.out.scales;
     po.rows = 512;
     po.cols = 512;
-    po.x = c->d_a;
+    po.x = b.lane->a;
     po.ldx = kWidth;
     po.res = in;
     po.ldres = kWidth;
-    po.y = c->d_h;
+    po.y = b.lane->h;
     po.ldy = kWidth;
     {
-        LaunchScope ls(c, PHONON_CUDA_K_OUT, linear_bytes(L.out) + act * 3 * kWidth);
+        LaunchScope ls(c, PHONON_CUDA_K_OUT, linear_bytes(L.out) + act * 3 * kWidth, b.lane->stream);
         CUDA_TRY((launch_gemv<1, false, EPI_RESID>(q8, po, s)));
     }
     // 4. g = GELU(LN2(h) Wup^T)
     GemvParams pu{};
     pu.B = b.R;
-    pu.status = c->d_status;
+    pu.status = b.d_status;
     pu.w = L.up.plane;
     pu.scales = L.up.scales;
     pu.rows = kFfn;
     pu.cols = 512;
-    pu.x = c->d_h;
+    pu.x = b.lane->h;
     pu.ldx = kWidth;
     pu.ln_w = L.norms + 2 * kWidth;
     pu.ln_b = L.norms + 3 * kWidth;
-    pu.y = c->d_g;
+    pu.y = b.lane->g;
     pu.ldy = kFfn;
     {
-        LaunchScope ls(c, PHONON_CUDA_K_UP, linear_bytes(L.up) + act * (kWidth + kFfn));
+        LaunchScope ls(c, PHONON_CUDA_K_UP, linear_bytes(L.up) + act * (kWidth + kFfn), b.lane->stream);
         CUDA_TRY((launch_gemv<1, true, EPI_GELU>(q8, pu, s)));
     }
     // 5. out = h + g Wdown^T
     GemvParams pd{};
     pd.B = b.R;
-    pd.status = c->d_status;
+    pd.status = b.d_status;
     pd.w = L.down.plane;
     pd.scales = L.down.scales;
     pd.rows = 512;
     pd.cols = kFfn;
-    pd.x = c->d_g;
+    pd.x = b.lane->g;
     pd.ldx = kFfn;
-    pd.res = c->d_h;
+    pd.res = b.lane->h;
     pd.ldres = kWidth;
     pd.y = out;
     pd.ldy = kWidth;
     {
-        LaunchScope ls(c, PHONON_CUDA_K_DOWN, linear_bytes(L.down) + act * (kFfn + 2 * kWidth));
+        LaunchScope ls(c, PHONON_CUDA_K_DOWN, linear_bytes(L.down) + act * (kFfn + 2 * kWidth), b.lane->stream);
         CUDA_TRY((launch_gemv<4, false, EPI_RESID>(q8, pd, s)));
     }
     return PHONON_CUDA_OK;
@@ -969,7 +1002,7 @@ int enqueue_layers_direct(PhononCuda* c, const Batch& b, const float* in, float*
     const int L = static_cast<int>(c->cfg.n_layers);
     const float* cur = in;
     for (int l = 0; l < L; ++l) {
-        float* out = (l == L - 1) ? final_out : ((cur == c->d_x0) ? c->d_x1 : c->d_x0);
+        float* out = (l == L - 1) ? final_out : ((cur == b.lane->x0) ? b.lane->x1 : b.lane->x0);
         const int st = enqueue_layer(c, b, l, cur, out);
         if (st != PHONON_CUDA_OK) return st;
         cur = out;
@@ -1050,13 +1083,13 @@ int enqueue_persist(PhononCuda* c, const Batch& b, const float* in, float* final
     pp.n_groups = sh.n_groups;
     pp.in = in;
     pp.out = final_out;
-    pp.xbuf0 = in == c->d_x1 ? c->d_x0 : c->d_x1;
-    pp.xbuf1 = in == c->d_x1 ? c->d_x1 : c->d_x0;
-    pp.h = c->d_h;
-    pp.g = c->d_g;
-    pp.q = c->d_q;
-    pp.part = c->d_part;
-    pp.status = c->d_status;
+    pp.xbuf0 = in == b.lane->x1 ? b.lane->x0 : b.lane->x1;
+    pp.xbuf1 = in == b.lane->x1 ? b.lane->x1 : b.lane->x0;
+    pp.h = b.lane->h;
+    pp.g = b.lane->g;
+    pp.q = b.lane->q;
+    pp.part = b.lane->part;
+    pp.status = b.d_status;
     pp.error = c->d_err;
     pp.barrier = c->d_bar;
     pp.barrier_base = c->bar_epoch;
@@ -1068,7 +1101,7 @@ int enqueue_persist(PhononCuda* c, const Batch& b, const float* in, float* final
     pp.splits = b.d_splits;
     pp.cta_split = b.d_cta_split;
     pp.freq = c->d_freq;
-    pp.rope = c->d_rope;
+    pp.rope = b.lane->rope;
     pp.kv = kv_view(c);
     pp.off_x = sh.off_x;
     pp.off_w0 = sh.off_w0;
@@ -1082,7 +1115,7 @@ int enqueue_persist(PhononCuda* c, const Batch& b, const float* in, float* final
     const double esize = bf16 ? 2.0 : 4.0;
     const double bytes = weights + L * (b.keys + b.R) * 2.0 * kWidth * esize + b.R * 2.0 * kWidth * 4.0;
     {
-        LaunchScope ls(c, PHONON_CUDA_K_FUSED, bytes);
+        LaunchScope ls(c, PHONON_CUDA_K_FUSED, bytes, b.lane->stream);
         CUDA_TRY(bf16 ? launch_persist_t<true>(c, pp, sh.smem) : launch_persist_t<false>(c, pp, sh.smem));
     }
     c->bar_epoch += static_cast<unsigned>(c->sms) * static_cast<unsigned>(1 + 5 * L);
@@ -1093,7 +1126,8 @@ int enqueue_stack(PhononCuda* c, const Batch& b, const float* in, float* final_o
                   PhononCudaCancelPoll cancel, void* cctx, const std::vector<int>* polls_per_layer,
                   bool* cancelled) {
     if (b.persist) return enqueue_persist(c, b, in, final_out);
-    if (!cancel && !c->prof_on) return enqueue_layers_graphed(c, b, in, final_out);
+    if (!cancel && !c->prof_on && !b.split) return enqueue_layers_graphed(c, b, in, final_out);
+    if (!cancel) return enqueue_layers_direct(c, b, in, final_out);
     const int L = static_cast<int>(c->cfg.n_layers);
     const float* cur = in;
     for (int l = 0; l < L; ++l) {
@@ -1105,7 +1139,7 @@ int enqueue_stack(PhononCuda* c, const Batch& b, const float* in, float* final_o
                     return PHONON_CUDA_CANCELLED;
                 }
         }
-        float* out = (l == L - 1) ? final_out : ((cur == c->d_x0) ? c->d_x1 : c->d_x0);
+        float* out = (l == L - 1) ? final_out : ((cur == b.lane->x0) ? b.lane->x1 : b.lane->x0);
         const int st = enqueue_layer(c, b, l, cur, out);
         if (st != PHONON_CUDA_OK) return st;
         cur = out;
@@ -1119,6 +1153,45 @@ int enqueue_stack(PhononCuda* c, const Batch& b, const float* in, float* final_o
 
 int set_device(int device) {
     CUDA_TRY(cudaSetDevice(device));
+    return PHONON_CUDA_OK;
+}
+
+// A decode step of entries (slot, pos) from `in` to `out` (device rows).
+// Small batches within the fused window run as one persistent launch;
+// batches of at least split_min entries run as two half batches on two
+// lanes, so that one half's attention (HBM-bound) overlaps the other half's
+// projections (latency-bound); everything else runs one launch per stage.
+// Page-table updates are applied by the first lane before the second starts.
+int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::vector<int32_t>& pos,
+                   const std::vector<int32_t>& updates, const float* in, float* out, PhononCudaCancelPoll cancel,
+                   void* cctx, bool* cancelled) {
+    const int n = static_cast<int>(slot.size());
+    const bool persist = use_persist(c, n, cancel != nullptr);
+    int st;
+    if (persist || cancel || !c->lane1_ok || static_cast<uint32_t>(n) < c->split_min) {
+        Batch b;
+        if ((st = upload_batch(c, slot, pos, updates, &b, !persist))) return st;
+        return enqueue_stack(c, b, in, out, cancel, cctx, nullptr, cancelled);
+    }
+    const int n0 = n / 2;
+    Lane& L1 = c->lanes[1];
+    long long total_pages = 0;  // the whole step's split plan, for both halves
+    for (int e = 0; e < n; ++e) total_pages += pos[e] / kPage + 1;
+    const long long pps = std::max<long long>(1, (total_pages + kLaneSplitTarget - 1) / kLaneSplitTarget);
+    const std::vector<int32_t> s0(slot.begin(), slot.begin() + n0), p0(pos.begin(), pos.begin() + n0);
+    const std::vector<int32_t> s1(slot.begin() + n0, slot.end()), p1(pos.begin() + n0, pos.end());
+    Batch b0, b1;
+    if ((st = upload_batch(c, s0, p0, updates, &b0, true, &c->lanes[0], c->d_status, pps))) return st;
+    CUDA_TRY(cudaEventRecord(c->fork, c->stream));  // page updates and everything before this step
+    CUDA_TRY(cudaStreamWaitEvent(L1.stream, c->fork, 0));
+    if ((st = upload_batch(c, s1, p1, {}, &b1, true, &L1, c->d_status + n0, pps))) return st;
+    b0.split = b1.split = true;
+    if ((st = enqueue_stack(c, b0, in, out, nullptr, nullptr, nullptr, cancelled))) return st;
+    if ((st = enqueue_stack(c, b1, in + static_cast<size_t>(n0) * kWidth, out + static_cast<size_t>(n0) * kWidth,
+                            nullptr, nullptr, nullptr, cancelled)))
+        return st;
+    CUDA_TRY(cudaEventRecord(c->join, L1.stream));
+    CUDA_TRY(cudaStreamWaitEvent(c->stream, c->join, 0));
     return PHONON_CUDA_OK;
 }
 
@@ -1176,6 +1249,17 @@ void destroy_context(PhononCuda* c) {
     void* host[] = {c->h_meta, c->h_x, c->h_y, c->h_stage, c->h_status};
     for (void* p : host)
         if (p) cudaFreeHost(p);
+    {
+        Lane& L1 = c->lanes[1];
+        if (L1.stream) cudaStreamSynchronize(L1.stream);
+        void* dev1[] = {L1.x0, L1.x1, L1.q, L1.a, L1.h, L1.g, L1.part, L1.meta, L1.dig512, L1.dig2048, L1.exps, L1.rope};
+        for (void* p : dev1)
+            if (p) cudaFree(p);
+        if (L1.h_meta) cudaFreeHost(L1.h_meta);
+        if (L1.stream) cudaStreamDestroy(L1.stream);
+        if (c->fork) cudaEventDestroy(c->fork);
+        if (c->join) cudaEventDestroy(c->join);
+    }
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -1279,6 +1363,47 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
     if (cudaMemset(c->d_err, 0, 4) != cudaSuccess) return fail(PHONON_CUDA_DEVICE_ERROR);
     c->tensor_ok = make_i8_map(&c->tm_dig512, c->d_dig512, rows_pad * kDigits, 512) &&
                    make_i8_map(&c->tm_dig2048, c->d_dig2048, rows_pad * kDigits, 2048);
+    {
+        Lane& L0 = c->lanes[0];
+        L0.stream = c->stream;
+        L0.x0 = c->d_x0;
+        L0.x1 = c->d_x1;
+        L0.q = c->d_q;
+        L0.a = c->d_a;
+        L0.h = c->d_h;
+        L0.g = c->d_g;
+        L0.part = c->d_part;
+        L0.meta = c->d_meta;
+        L0.h_meta = c->h_meta;
+        L0.dig512 = c->d_dig512;
+        L0.dig2048 = c->d_dig2048;
+        L0.exps = c->d_exps;
+        L0.tm_dig512 = c->tm_dig512;
+        L0.tm_dig2048 = c->tm_dig2048;
+        L0.rope = c->d_rope;
+        if (cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming) != cudaSuccess)
+            return fail(PHONON_CUDA_DEVICE_ERROR);
+        // A second lane only when a step can hold two half batches.
+        if (cfg.max_batch >= 96) {
+            Lane& L1 = c->lanes[1];
+            const bool ok1 =
+                cudaStreamCreateWithFlags(&L1.stream, cudaStreamNonBlocking) == cudaSuccess &&
+                cudaMalloc(&L1.x0, rows * kWidth * 4) == cudaSuccess && cudaMalloc(&L1.x1, rows * kWidth * 4) == cudaSuccess &&
+                cudaMalloc(&L1.q, rows * kWidth * 4) == cudaSuccess && cudaMalloc(&L1.a, rows * kWidth * 4) == cudaSuccess &&
+                cudaMalloc(&L1.h, rows * kWidth * 4) == cudaSuccess && cudaMalloc(&L1.g, rows * kFfn * 4) == cudaSuccess &&
+                cudaMalloc(&L1.part, static_cast<size_t>(c->max_splits) * kHeads * kPartStride * 4) == cudaSuccess &&
+                cudaMalloc(&L1.meta, static_cast<size_t>(c->meta_ints) * 4) == cudaSuccess &&
+                cudaMallocHost(&L1.h_meta, static_cast<size_t>(c->meta_ints) * 4) == cudaSuccess &&
+                cudaMalloc(&L1.dig512, rows_pad * kDigits * 512) == cudaSuccess &&
+                cudaMalloc(&L1.dig2048, rows_pad * kDigits * 2048) == cudaSuccess &&
+                cudaMalloc(&L1.exps, rows_pad * 4) == cudaSuccess &&
+                cudaMalloc(&L1.rope, rows * 32 * sizeof(float2)) == cudaSuccess;
+            if (!ok1) return fail(PHONON_CUDA_OUT_OF_MEMORY);
+            c->lane1_ok = c->tensor_ok && make_i8_map(&L1.tm_dig512, L1.dig512, rows_pad * kDigits, 512) &&
+                          make_i8_map(&L1.tm_dig2048, L1.dig2048, rows_pad * kDigits, 2048);
+        }
+    }
     {
         // Row r of the pool = 64 dims of (page, layer, k|v, head, slot); a
         // page-layer K block is rows [(page*L + layer)*256, +128).
@@ -1424,13 +1549,15 @@ uint64_t phonon_cuda_launch_count(PhononCuda* c) {
 }
 
 int phonon_cuda_set_batch_paths(PhononCuda* c, uint32_t fused_min_batch, uint32_t fused_max_batch,
-                                uint32_t tensor_min_batch) {
-    if (!c || fused_min_batch < 1 || fused_max_batch > PHONON_CUDA_FUSED_MAX_BATCH || tensor_min_batch < 1)
+                                uint32_t tensor_min_batch, uint32_t split_min_batch) {
+    if (!c || fused_min_batch < 1 || fused_max_batch > PHONON_CUDA_FUSED_MAX_BATCH || tensor_min_batch < 1 ||
+        split_min_batch < 2)
         return PHONON_CUDA_INVALID_ARGUMENT;
     std::lock_guard<std::mutex> g(c->mu);
     if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
     c->fused_min = fused_min_batch;
     c->fused_max = fused_max_batch;
+    c->split_min = split_min_batch;
     c->tensor_min = tensor_min_batch;
     drop_graph(c);  // a captured step holds the old path choice
     return PHONON_CUDA_OK;
@@ -1500,16 +1627,12 @@ int phonon_cuda_step(PhononCuda* c, uint32_t n, const uint32_t* streams, const u
     std::vector<int32_t> slot, pos, updates;
     PageUndo undo{c, {}};
     if ((st = prepare_decode(c, n, streams, positions, slot, pos, updates, undo, true))) return st;
-    Batch b;
-    if ((st = upload_batch(c, slot, pos, updates, &b, !use_persist(c, static_cast<int>(n), cancel != nullptr)))) {
-        undo.rollback();
-        return st;
-    }
     std::memcpy(c->h_x, x, static_cast<size_t>(n) * kWidth * 4);
     cudaMemcpyAsync(c->d_x0, c->h_x, static_cast<size_t>(n) * kWidth * 4, cudaMemcpyHostToDevice, c->stream);
     cudaMemsetAsync(c->d_status, 0, n * 4, c->stream);
     bool cancelled = false;
-    st = enqueue_stack(c, b, c->d_x0, c->d_y, cancel, cctx, nullptr, &cancelled);
+    st = enqueue_decode(c, slot, pos, updates, c->d_x0, c->d_y, cancel, cctx, &cancelled);
+    if (st && st != PHONON_CUDA_CANCELLED && !cancelled) undo.rollback();
     if (st == PHONON_CUDA_OK)
         cudaMemcpyAsync(c->h_y, c->d_y, static_cast<size_t>(n) * kWidth * 4, cudaMemcpyDeviceToHost, c->stream);
     const int sync = finish_sync(c, n);
@@ -1539,14 +1662,12 @@ int phonon_cuda_step_device(PhononCuda* c, uint32_t n, const uint32_t* streams, 
     std::vector<int32_t> slot, pos, updates;
     PageUndo undo{c, {}};
     if ((st = prepare_decode(c, n, streams, positions, slot, pos, updates, undo, true))) return st;
-    Batch b;
-    if ((st = upload_batch(c, slot, pos, updates, &b, !use_persist(c, static_cast<int>(n), false)))) {
+    cudaMemsetAsync(c->d_status, 0, n * 4, c->stream);
+    bool cancelled = false;
+    if ((st = enqueue_decode(c, slot, pos, updates, x_dev, y_dev, nullptr, nullptr, &cancelled))) {
         undo.rollback();
         return st;
     }
-    cudaMemsetAsync(c->d_status, 0, n * 4, c->stream);
-    bool cancelled = false;
-    if ((st = enqueue_stack(c, b, x_dev, y_dev, nullptr, nullptr, nullptr, &cancelled))) return st;
     c->pending = true;
     c->pending_streams.assign(streams, streams + n);
     return PHONON_CUDA_OK;

@@ -76,7 +76,7 @@ def lib():
         "phonon_cuda_rope_interleaved": [C.c_int, P, SZ, SZ, SZ, F],
         "phonon_cuda_profile_enable": [P, C.c_int],
         "phonon_cuda_profile_read": [P, P, P, P],
-        "phonon_cuda_set_batch_paths": [P, U32, U32, U32],
+        "phonon_cuda_set_batch_paths": [P, U32, U32, U32, U32],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -223,12 +223,14 @@ class Context:
     def launch_count(self):
         return int(self.L.phonon_cuda_launch_count(self.h))
 
-    def set_batch_paths(self, fused_min_batch=8, fused_max_batch=FUSED_MAX_BATCH, tensor_min_batch=32):
+    def set_batch_paths(self, fused_min_batch=8, fused_max_batch=FUSED_MAX_BATCH, tensor_min_batch=32,
+                        split_min_batch=384):
         """Batch sizes routed to the persistent whole-step launch
-        (fused_min_batch..fused_max_batch) and to the tensor-core projections
-        (>= tensor_min_batch); a minimum above the maximum disables the former."""
-        check(self.L.phonon_cuda_set_batch_paths(self.h, fused_min_batch, fused_max_batch, tensor_min_batch),
-              "set_batch_paths")
+        (fused_min_batch..fused_max_batch; a minimum above the maximum
+        disables it), to the tensor-core projections (>= tensor_min_batch) and
+        to two concurrent half batches (>= split_min_batch)."""
+        check(self.L.phonon_cuda_set_batch_paths(self.h, fused_min_batch, fused_max_batch, tensor_min_batch,
+                                                 split_min_batch), "set_batch_paths")
 
     def layer_step(self, s, layer, position, x):
         x = np.ascontiguousarray(x, np.float32)
