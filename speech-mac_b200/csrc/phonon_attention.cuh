@@ -1,11 +1,13 @@
 // Split-K paged flash-decode with TMA page staging (sm_100a).
 //
-// One CTA per split (a run of pages of one stream), all 8 heads: warp 8 is a
-// producer that, for every page of the split, looks the page up in the
-// stream's page table and TMA-loads the page's K block and V block of this
-// layer ([8 heads][16 slots][64 dims], 16 KB each in bf16) into a ring of
-// shared-memory stages; warps 0-7 (one per head) consume each stage with the
-// online softmax of attn_partial_kernel and release it. Tiles are loaded with
+// One CTA per balanced chunk of pages (its splits [cta_split[c],
+// cta_split[c+1]), one split per stream segment; or one split per CTA when
+// there is no chunk table), all 8 heads: warp 8 is a producer that, for every
+// page, looks the page up in the stream's page table and TMA-loads the page's
+// K block and V block of this layer ([8 heads][16 slots][64 dims], 16 KB each
+// in bf16) into a ring of shared-memory stages that runs on across the
+// chunk's splits; warps 0-7 (one per head) consume each stage with the online
+// softmax of attn_partial_kernel, release it, and write one partial per split. Tiles are loaded with
 // SWIZZLE_128B (16-byte chunk index XOR row % 8), so the per-key row reads of
 // the consumers are bank-conflict free. fp32 pages use two 128-byte column
 // boxes per block. No multicast; every wait is bounded.
@@ -49,8 +51,6 @@ __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_
     volatile int* failed = reinterpret_cast<volatile int*>(bars + 2 * T::kStages);
     const uint32_t full0 = smem_addr(bars), empty0 = full0 + 8 * T::kStages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const Split sp = p.splits[blockIdx.x];
-    const int slot = p.slot[sp.b];
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < T::kStages; ++s) {
@@ -62,22 +62,32 @@ __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_
     }
     __syncthreads();
     pdl_wait();  // q, the page table and the metadata come from earlier kernels
+    // This CTA's splits: a balanced chunk of pages (cta_split) or one split.
+    // The step's metadata is read only after the wait: nothing of it may be
+    // read while earlier launches of the stream can still be in flight.
+    const int s_begin = p.cta_split ? __ldcg(p.cta_split + blockIdx.x) : static_cast<int>(blockIdx.x);
+    const int s_end = p.cta_split ? __ldcg(p.cta_split + blockIdx.x + 1) : static_cast<int>(blockIdx.x) + 1;
 
     if (warp == kAttnHeadsPerCta) {
         if (lane == 0) {
-            const int32_t* table = p.kv.table + static_cast<size_t>(slot) * p.kv.max_pages;
-            for (int i = 0; i < sp.page_count; ++i) {
-                const int s = i % T::kStages;
-                if (i >= T::kStages && !mbar_wait(empty0 + 8 * s, ((i / T::kStages) - 1) & 1, error, failed)) break;
-                const int page = table[sp.page_begin + i];
-                const int row0 = (page * n_layers + p.layer) * 256;  // K block; V block follows
-                uint8_t* stage = smem + s * T::kStageBytes;
-                mbar_expect_tx(full0 + 8 * s, T::kStageBytes);
+            // Ring index n runs on across the CTA's splits: stage n % kStages, use n / kStages.
+            int n = 0;
+            for (int s = s_begin; s < s_end && !*failed; ++s) {
+                const Split sp = p.splits[s];
+                const int32_t* table = p.kv.table + static_cast<size_t>(p.slot[sp.b]) * p.kv.max_pages;
+                for (int i = 0; i < sp.page_count; ++i, ++n) {
+                    const int st = n % T::kStages;
+                    if (n >= T::kStages && !mbar_wait(empty0 + 8 * st, ((n / T::kStages) - 1) & 1, error, failed)) break;
+                    const int page = table[sp.page_begin + i];
+                    const int row0 = (page * n_layers + p.layer) * 256;  // K block; V block follows
+                    uint8_t* stage = smem + st * T::kStageBytes;
+                    mbar_expect_tx(full0 + 8 * st, T::kStageBytes);
 #pragma unroll
-                for (int bx = 0; bx < T::kBoxes; ++bx) {
-                    tma_load_2d(smem_addr(stage + bx * T::kBoxBytes), &tm_kv, bx * T::kBoxCols, row0, full0 + 8 * s);
-                    tma_load_2d(smem_addr(stage + T::kBlockBytes + bx * T::kBoxBytes), &tm_kv, bx * T::kBoxCols,
-                                row0 + 128, full0 + 8 * s);
+                    for (int bx = 0; bx < T::kBoxes; ++bx) {
+                        tma_load_2d(smem_addr(stage + bx * T::kBoxBytes), &tm_kv, bx * T::kBoxCols, row0, full0 + 8 * st);
+                        tma_load_2d(smem_addr(stage + T::kBlockBytes + bx * T::kBoxBytes), &tm_kv, bx * T::kBoxCols,
+                                    row0 + 128, full0 + 8 * st);
+                    }
                 }
             }
         }
@@ -86,102 +96,110 @@ __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_
 
     // Consumer: head = warp. Lane l scores key (l & 15) over dims (l >> 4)*32..+31.
     const int head = warp, half = lane >> 4, key_lane = lane & 15;
-    float qh[32];
-    {
-        const float4* qs = reinterpret_cast<const float4*>(p.q + static_cast<size_t>(sp.b) * kWidth + head * kHeadDim +
-                                                           half * 32);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 v = qs[i];
-            qh[4 * i] = v.x;
-            qh[4 * i + 1] = v.y;
-            qh[4 * i + 2] = v.z;
-            qh[4 * i + 3] = v.w;
-        }
-    }
-    float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f;
-    bool finite_ok = true;
     const int krow = head * kPage + key_lane;
-    for (int i = 0; i < sp.page_count; ++i) {
-        const int s = i % T::kStages;
-        if (!__all_sync(kFull, mbar_wait(full0 + 8 * s, (i / T::kStages) & 1, error, failed))) break;
-        const uint8_t* sK = smem + s * T::kStageBytes;
-        const uint8_t* sV = sK + T::kBlockBytes;
-        const int pg = sp.page_begin + i;
-        const bool valid = pg * kPage + key_lane < sp.n_keys;
-        float dot = 0.0f;
-        if constexpr (kBf16) {
+    int n = 0;
+    for (int s = s_begin; s < s_end; ++s) {
+        const Split sp = p.splits[s];
+        float qh[32];
+        {
+            const float4* qs = reinterpret_cast<const float4*>(p.q + static_cast<size_t>(sp.b) * kWidth + head * kHeadDim +
+                                                               half * 32);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const uint4 v = *reinterpret_cast<const uint4*>(sw128(sK, krow, half * 4 + c));
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    dot = fmaf(qh[8 * c + 2 * k], __uint_as_float(w[k] << 16), dot);
-                    dot = fmaf(qh[8 * c + 2 * k + 1], __uint_as_float(w[k] & 0xffff0000u), dot);
-                }
-            }
-        } else {
-            const uint8_t* box = sK + half * T::kBoxBytes;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const float4 v = *reinterpret_cast<const float4*>(sw128(box, krow, c));
-                dot = fmaf(qh[4 * c], v.x, dot);
-                dot = fmaf(qh[4 * c + 1], v.y, dot);
-                dot = fmaf(qh[4 * c + 2], v.z, dot);
-                dot = fmaf(qh[4 * c + 3], v.w, dot);
+            for (int i = 0; i < 8; ++i) {
+                const float4 v = qs[i];
+                qh[4 * i] = v.x;
+                qh[4 * i + 1] = v.y;
+                qh[4 * i + 2] = v.z;
+                qh[4 * i + 3] = v.w;
             }
         }
-        dot += __shfl_xor_sync(kFull, dot, 16);
-        float score = dot * 0.125f;
-        if (valid) finite_ok &= isfinite(score);
-        score = valid ? score : -INFINITY;
-        float pm = score;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, o));
-        const float m_new = fmaxf(m, pm);
-        const float alpha = m == -INFINITY ? 0.0f : expf(m - m_new);
-        const float pr = valid ? expf(score - m_new) : 0.0f;
-        float ps = pr;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
-        l = fmaf(l, alpha, ps);
-        a0 *= alpha;
-        a1 *= alpha;
-        const int n_valid = min(kPage, sp.n_keys - pg * kPage);
-#pragma unroll
-        for (int j = 0; j < kPage; ++j) {
-            const float pj = __shfl_sync(kFull, pr, j);
-            if (j < n_valid) {
-                const int vrow = head * kPage + j;
-                float v0, v1;
-                if constexpr (kBf16) {
-                    const uint32_t w2 =
-                        *reinterpret_cast<const uint32_t*>(sw128(sV, vrow, lane >> 2) + (lane & 3) * 4);
-                    v0 = __uint_as_float(w2 << 16);
-                    v1 = __uint_as_float(w2 & 0xffff0000u);
-                } else {
-                    const uint8_t* box = sV + (lane >> 4) * T::kBoxBytes;
-                    const float2 w2 = *reinterpret_cast<const float2*>(sw128(box, vrow, (lane & 15) >> 1) + (lane & 1) * 8);
-                    v0 = w2.x;
-                    v1 = w2.y;
-                }
-                a0 = fmaf(pj, v0, a0);
-                a1 = fmaf(pj, v1, a1);
+        float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f;
+        bool finite_ok = true;
+        for (int i = 0; i < sp.page_count; ++i, ++n) {
+            const int st = n % T::kStages;
+            if (!__all_sync(kFull, mbar_wait(full0 + 8 * st, (n / T::kStages) & 1, error, failed))) {
+                s = s_end;  // give up: the error flag is raised
+                break;
             }
+            const uint8_t* sK = smem + st * T::kStageBytes;
+            const uint8_t* sV = sK + T::kBlockBytes;
+            const int pg = sp.page_begin + i;
+            const bool valid = pg * kPage + key_lane < sp.n_keys;
+            float dot = 0.0f;
+            if constexpr (kBf16) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(sw128(sK, krow, half * 4 + c));
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        dot = fmaf(qh[8 * c + 2 * k], __uint_as_float(w[k] << 16), dot);
+                        dot = fmaf(qh[8 * c + 2 * k + 1], __uint_as_float(w[k] & 0xffff0000u), dot);
+                    }
+                }
+            } else {
+                const uint8_t* box = sK + half * T::kBoxBytes;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float4 v = *reinterpret_cast<const float4*>(sw128(box, krow, c));
+                    dot = fmaf(qh[4 * c], v.x, dot);
+                    dot = fmaf(qh[4 * c + 1], v.y, dot);
+                    dot = fmaf(qh[4 * c + 2], v.z, dot);
+                    dot = fmaf(qh[4 * c + 3], v.w, dot);
+                }
+            }
+            dot += __shfl_xor_sync(kFull, dot, 16);
+            float score = dot * 0.125f;
+            if (valid) finite_ok &= isfinite(score);
+            score = valid ? score : -INFINITY;
+            float pm = score;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, o));
+            const float m_new = fmaxf(m, pm);
+            const float alpha = m == -INFINITY ? 0.0f : expf(m - m_new);
+            const float pr = valid ? expf(score - m_new) : 0.0f;
+            float ps = pr;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
+            l = fmaf(l, alpha, ps);
+            a0 *= alpha;
+            a1 *= alpha;
+            const int n_valid = min(kPage, sp.n_keys - pg * kPage);
+#pragma unroll
+            for (int j = 0; j < kPage; ++j) {
+                const float pj = __shfl_sync(kFull, pr, j);
+                if (j < n_valid) {
+                    const int vrow = head * kPage + j;
+                    float v0, v1;
+                    if constexpr (kBf16) {
+                        const uint32_t w2 =
+                            *reinterpret_cast<const uint32_t*>(sw128(sV, vrow, lane >> 2) + (lane & 3) * 4);
+                        v0 = __uint_as_float(w2 << 16);
+                        v1 = __uint_as_float(w2 & 0xffff0000u);
+                    } else {
+                        const uint8_t* box = sV + (lane >> 4) * T::kBoxBytes;
+                        const float2 w2 = *reinterpret_cast<const float2*>(sw128(box, vrow, (lane & 15) >> 1) + (lane & 1) * 8);
+                        v0 = w2.x;
+                        v1 = w2.y;
+                    }
+                    a0 = fmaf(pj, v0, a0);
+                    a1 = fmaf(pj, v1, a1);
+                }
+            }
+            m = m_new;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty0 + 8 * st);
         }
-        m = m_new;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty0 + 8 * s);
+        if (s >= s_end) break;  // a wait gave up
+        if (s == s_end - 1) pdl_trigger();
+        float* out = p.part + (static_cast<size_t>(s) * kHeads + head) * kPartStride;
+        *reinterpret_cast<float2*>(out + 2 + 2 * lane) = make_float2(a0, a1);
+        if (lane == 0) {
+            out[0] = m;
+            out[1] = l;
+        }
+        if (!__all_sync(kFull, finite_ok) && lane == 0) flag_nonfinite(p.status, sp.b);
     }
-    pdl_trigger();
-    float* out = p.part + (static_cast<size_t>(blockIdx.x) * kHeads + head) * kPartStride;
-    *reinterpret_cast<float2*>(out + 2 + 2 * lane) = make_float2(a0, a1);
-    if (lane == 0) {
-        out[0] = m;
-        out[1] = l;
-    }
-    if (!__all_sync(kFull, finite_ok) && lane == 0) flag_nonfinite(p.status, sp.b);
 }
 
 }  // namespace phonon

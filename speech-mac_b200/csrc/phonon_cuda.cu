@@ -26,13 +26,11 @@ namespace {
 constexpr int kMaxLayers = 64;
 constexpr int kMaxDevices = 64;
 constexpr int kMaxPagesPerStream = PHONON_CUDA_MAX_POSITIONS / kPage;  // 512
-constexpr int kSplitTarget = 640;   // ~8 warps per split: fills 148 SMs several times over
 constexpr int kPrefillChunk = 256;  // rows per prefill pass
 constexpr int kTensorMinBatch = 32;  // streams from which projections run on tcgen05
 constexpr int kMaxSms = 1024;        // bound on the SM count (persistent split table)
 constexpr int kFusedMinBatch = 8;    // smaller batches are as fast or faster one launch per stage
-constexpr int kSplitMinBatch = 384;  // from here a step runs as two concurrent half batches
-constexpr int kLaneSplitTarget = 320;  // splits per step on two lanes: each half's attention leaves SMs to the other
+constexpr int kSplitMinBatch = 192;  // from here a step runs as two concurrent half batches
 
 #define CUDA_TRY(expr)                                                                       \
     do {                                                                                     \
@@ -407,14 +405,18 @@ struct PhononCuda {
     size_t stage_cap = 0;  // floats in d_stage / h_stage
     int32_t* h_status = nullptr;
     // Replay of repeated step shapes: the step's kernels are captured into a
-    // CUDA graph the second time the same (R, S, input, output) shape comes
+    // CUDA graph the second time the same StepShape comes
     // in a row and replayed while it repeats (a batch-1 decode keeps its
     // split count for 16 positions).
+    // Everything the captured launches depend on besides the metadata
+    // contents: batch and split counts, attention grid, buffers.
     struct StepShape {
-        int R = -1, S = -1;
+        int R = -1, S = -1, chunks = -1;
         const void* in = nullptr;
         const void* out = nullptr;
-        bool operator==(const StepShape& o) const { return R == o.R && S == o.S && in == o.in && out == o.out; }
+        bool operator==(const StepShape& o) const {
+            return R == o.R && S == o.S && chunks == o.chunks && in == o.in && out == o.out;
+        }
     };
     StepShape last_shape, graph_shape;
     cudaGraphExec_t graph_exec = nullptr;
@@ -561,7 +563,8 @@ struct Batch {
     double keys = 0;  // sum over entries of (position + 1)
     float2* d_rope = nullptr;  // [R][32] (cos, sin) of this batch's positions
     int32_t *d_slot, *d_pos, *d_first, *d_count, *d_updates;
-    int32_t* d_cta_split = nullptr;  // persistent path: [sms + 1]
+    int32_t* d_cta_split = nullptr;  // split range of each attention CTA (chunk)
+    int n_chunks = 0;
     Split* d_splits;
 };
 
@@ -649,7 +652,7 @@ bool use_persist(const PhononCuda* c, int R, bool cancel) {
 // persistent kernel.
 int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vector<int32_t>& pos,
                  const std::vector<int32_t>& updates, Batch* out, bool device_prep = true, Lane* lane = nullptr,
-                 int32_t* status = nullptr, long long plan_pps = 0) {
+                 int32_t* status = nullptr, int plan_chunks = 0) {
     if (!lane) lane = &c->lanes[0];
     if (!status) status = c->d_status;
     const int R = static_cast<int>(slot.size());
@@ -671,28 +674,17 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     // (entry, page) order cut into at most one balanced chunk per SM (>=
     // kPersistMinChunk pages); a chunk is one split per entry segment it
     // covers, and chunk k's splits are [cta_split[k], cta_split[k+1]).
-    // plan_pps > 0: pages per split fixed by the caller (a half batch keeps
-    // the split plan of its whole step).
-    const bool chunked = plan_pps == 0 && R <= PHONON_CUDA_FUSED_MAX_BATCH && c->sms > 0;
-    const int G = chunked ? c->sms : 0;
-    std::vector<int32_t> cta_split;
-    if (!chunked) {
-        const long long pps =
-            plan_pps > 0 ? plan_pps : std::max<long long>(1, (total_pages + kSplitTarget - 1) / kSplitTarget);
-        for (int e = 0; e < R; ++e) {
-            const int n_keys = pos[e] + 1, n_pages = pos[e] / kPage + 1;
-            h_first[e] = S;
-            int ns = 0;
-            for (int pb = 0; pb < n_pages; pb += static_cast<int>(pps), ++ns, ++S) {
-                if (S >= c->max_splits) return PHONON_CUDA_INVALID_ARGUMENT;
-                h_splits[S] = Split{e, pb, std::min<int>(static_cast<int>(pps), n_pages - pb), n_keys};
-            }
-            h_count[e] = ns;
-        }
-    } else {
-        const long long chunks =
-            std::max<long long>(1, std::min<long long>(G, total_pages / kPersistMinChunk));
-        cta_split.assign(static_cast<size_t>(G) + 1, 0);
+    // Split plan: the pages of all entries in (entry, page) order are cut
+    // into at most `chunks` balanced chunks of at least kPersistMinChunk
+    // pages; a chunk is one split per entry segment it covers, so every
+    // entry's splits are consecutive and in page order, and chunk k's splits
+    // are [cta_split[k], cta_split[k+1]). One chunk per CTA: per SM up to 64
+    // entries (the persistent kernel's grid), two per SM above.
+    const int chunks_max = plan_chunks > 0 ? plan_chunks : (R <= PHONON_CUDA_FUSED_MAX_BATCH ? 1 : 2) * c->sms;
+    const long long chunks = std::max<long long>(1, std::min<long long>(chunks_max, total_pages / kPersistMinChunk));
+    const int G = std::max<int>(chunks_max, c->sms);  // table entries: at least one per SM of a persistent grid
+    std::vector<int32_t> cta_split(static_cast<size_t>(G) + 1, 0);
+    {
         long long done = 0;  // pages before entry e
         int e = 0, pb = 0;   // cursor: page pb of entry e
         for (long long k = 0; k < chunks; ++k) {
@@ -716,12 +708,17 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
         }
         for (long long k = chunks; k <= G; ++k) cta_split[k] = S;
     }
+    // Metadata layout: slot, pos, first, count [R each], splits [4S], the
+    // chunk table [G+1], page updates [3U]. Everything a step's kernels read
+    // sits at offsets fixed by (R, S, G), which a replayed step graph keeps;
+    // only the page updates (applied outside the graph) come after.
     const int U = static_cast<int>(updates.size() / 3);
-    int32_t* h_upd = m + 4 * R + 4 * S;
-    if (4 * R + 4 * S + 3 * U + G + 1 > c->meta_ints) return PHONON_CUDA_INVALID_ARGUMENT;
+    int32_t* h_cta = m + 4 * R + 4 * S;
+    int32_t* h_upd = h_cta + G + 1;
+    if (4 * R + 4 * S + G + 1 + 3 * U > c->meta_ints) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::memcpy(h_cta, cta_split.data(), cta_split.size() * 4);
     std::memcpy(h_upd, updates.data(), updates.size() * 4);
-    if (chunked) std::memcpy(h_upd + 3 * U, cta_split.data(), cta_split.size() * 4);
-    const size_t bytes = static_cast<size_t>(4 * R + 4 * S + 3 * U + (chunked ? G + 1 : 0)) * 4;
+    const size_t bytes = static_cast<size_t>(4 * R + 4 * S + G + 1 + 3 * U) * 4;
     CUDA_TRY(cudaMemcpyAsync(lane->meta, lane->h_meta, bytes, cudaMemcpyHostToDevice, lane->stream));
     Batch b;
     b.lane = lane;
@@ -735,8 +732,9 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     b.d_first = lane->meta + 2 * R;
     b.d_count = lane->meta + 3 * R;
     b.d_splits = reinterpret_cast<Split*>(lane->meta + 4 * R);
-    b.d_updates = lane->meta + 4 * R + 4 * S;
-    b.d_cta_split = b.d_updates + 3 * U;
+    b.d_cta_split = lane->meta + 4 * R + 4 * S;
+    b.d_updates = b.d_cta_split + G + 1;
+    b.n_chunks = static_cast<int>(chunks);
     b.d_rope = lane->rope;
     b.persist = !device_prep;
     if (!device_prep) {
@@ -771,6 +769,7 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out) {
     ap.q = b.lane->q;
     ap.slot = b.d_slot;
     ap.splits = b.d_splits;
+    ap.cta_split = b.d_cta_split;
     ap.n_splits = b.S;
     ap.kv = kv;
     ap.layer = l;
@@ -782,8 +781,8 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out) {
         LaunchScope ls(c, PHONON_CUDA_K_ATTENTION,
                        b.keys * 2.0 * kWidth * esize + act * kWidth + b.S * kHeads * kPartStride * 4.0, b.lane->stream);
         if (c->attn_tma) {
-            CUDA_TRY(kv.bf16 ? launch_attn_tma<true>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.S, s)
-                             : launch_attn_tma<false>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.S, s));
+            CUDA_TRY(kv.bf16 ? launch_attn_tma<true>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.n_chunks, s)
+                             : launch_attn_tma<false>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.n_chunks, s));
         } else {
             CUDA_TRY(kv.bf16 ? launch_pdl(attn_partial_kernel<true>, dim3(grid), dim3(kAttnWarps * 32), 0, s, ap)
                              : launch_pdl(attn_partial_kernel<false>, dim3(grid), dim3(kAttnWarps * 32), 0, s, ap));
@@ -1016,6 +1015,7 @@ int enqueue_layers_graphed(PhononCuda* c, const Batch& b, const float* in, float
     PhononCuda::StepShape shape;
     shape.R = b.R;
     shape.S = b.S;
+    shape.chunks = b.n_chunks;
     shape.in = in;
     shape.out = final_out;
     if (c->graph_exec && c->graph_shape == shape) {
@@ -1175,16 +1175,14 @@ int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::v
     }
     const int n0 = n / 2;
     Lane& L1 = c->lanes[1];
-    long long total_pages = 0;  // the whole step's split plan, for both halves
-    for (int e = 0; e < n; ++e) total_pages += pos[e] / kPage + 1;
-    const long long pps = std::max<long long>(1, (total_pages + kLaneSplitTarget - 1) / kLaneSplitTarget);
+    const int chunks = c->sms;  // one attention CTA per SM per half: each half's attention leaves SMs to the other
     const std::vector<int32_t> s0(slot.begin(), slot.begin() + n0), p0(pos.begin(), pos.begin() + n0);
     const std::vector<int32_t> s1(slot.begin() + n0, slot.end()), p1(pos.begin() + n0, pos.end());
     Batch b0, b1;
-    if ((st = upload_batch(c, s0, p0, updates, &b0, true, &c->lanes[0], c->d_status, pps))) return st;
+    if ((st = upload_batch(c, s0, p0, updates, &b0, true, &c->lanes[0], c->d_status, chunks))) return st;
     CUDA_TRY(cudaEventRecord(c->fork, c->stream));  // page updates and everything before this step
     CUDA_TRY(cudaStreamWaitEvent(L1.stream, c->fork, 0));
-    if ((st = upload_batch(c, s1, p1, {}, &b1, true, &L1, c->d_status + n0, pps))) return st;
+    if ((st = upload_batch(c, s1, p1, {}, &b1, true, &L1, c->d_status + n0, chunks))) return st;
     b0.split = b1.split = true;
     if ((st = enqueue_stack(c, b0, in, out, nullptr, nullptr, nullptr, cancelled))) return st;
     if ((st = enqueue_stack(c, b1, in + static_cast<size_t>(n0) * kWidth, out + static_cast<size_t>(n0) * kWidth,
@@ -1333,9 +1331,9 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
     const size_t esize = cfg.kv_type == PHONON_CUDA_KV_BF16 ? 2 : 4;
     c->page_elems = static_cast<long long>(cfg.n_layers) * 2 * kHeads * kPage * kHeadDim;
     c->cap_rows = static_cast<int>(std::max<uint32_t>(cfg.max_batch, kPrefillChunk));
-    c->max_splits = kSplitTarget + c->cap_rows + 16;
+    c->max_splits = 2 * kMaxSms + c->cap_rows + 16;  // at most one split per (chunk, entry) boundary
     const int U_max = c->cap_rows * 2 + kMaxPagesPerStream + 16;
-    c->meta_ints = 4 * c->cap_rows + 4 * c->max_splits + 3 * U_max + kMaxSms + 1;
+    c->meta_ints = 4 * c->cap_rows + 4 * c->max_splits + 3 * U_max + 2 * kMaxSms + 1;
     const size_t rows = static_cast<size_t>(c->cap_rows);
     bool ok = cudaMalloc(&c->kv_pool, static_cast<size_t>(cfg.pool_pages) * c->page_elems * esize) == cudaSuccess &&
               cudaMalloc(&c->d_table, static_cast<size_t>(cfg.max_streams) * kMaxPagesPerStream * 4) == cudaSuccess &&

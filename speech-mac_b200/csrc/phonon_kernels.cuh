@@ -536,6 +536,7 @@ struct AttnParams {
     const float* q;        // [B][512] RoPE'd queries
     const int32_t* slot;   // [B]
     const Split* splits;   // [S]
+    const int32_t* cta_split;  // TMA kernel: [grid + 1] split range of each CTA, or null (one split per CTA)
     int n_splits;
     KvView kv;
     int layer;
