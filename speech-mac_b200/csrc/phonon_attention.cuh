@@ -41,6 +41,127 @@ __device__ __forceinline__ const uint8_t* sw128(const uint8_t* box, int row, int
     return box + row * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
+// A consumer lane's byte offsets into a stage's K and V blocks, swizzle
+// included. The swizzle of row r depends on r & 7 only, and the rows a lane
+// reads are head*16 + key (K) and head*16 + j (V, j < 16): the offsets are
+// fixed per lane, and V row j + 8 is V row j plus 8 rows of 128 bytes.
+template <bool kBf16>
+struct AttnLane {
+    int k_off[kBf16 ? 4 : 8];  // the lane's 16-byte chunks of its key row
+    int v_off[8];              // the lane's two dims in V rows head*16 + j, j < 8
+};
+
+template <bool kBf16>
+__device__ __forceinline__ AttnLane<kBf16> attn_lane(int head, int lane) {
+    using T = AttnTma<kBf16>;
+    AttnLane<kBf16> a;
+    const int half = lane >> 4, krow = head * kPage + (lane & 15);
+#pragma unroll
+    for (int c = 0; c < (kBf16 ? 4 : 8); ++c) {
+        if constexpr (kBf16) a.k_off[c] = krow * 128 + (((half * 4 + c) ^ (krow & 7)) << 4);
+        else a.k_off[c] = half * T::kBoxBytes + krow * 128 + ((c ^ (krow & 7)) << 4);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int vrow = head * kPage + j;
+        if constexpr (kBf16) a.v_off[j] = vrow * 128 + (((lane >> 2) ^ (vrow & 7)) << 4) + (lane & 3) * 4;
+        else a.v_off[j] = (lane >> 4) * T::kBoxBytes + vrow * 128 + ((((lane & 15) >> 1) ^ (vrow & 7)) << 4) + (lane & 1) * 8;
+    }
+    return a;
+}
+
+// One page of one head (the warp's) into the online softmax state (m, l,
+// a0, a1): lane l scores key (l & 15) over dims (l >> 4)*32 .. +31, the two
+// halves meet with one shuffle, and for P.V lane l owns output dims 2l,
+// 2l+1. Keys key0 + k with key0 + k >= n_keys are masked (exp(-inf) = 0).
+// Shared by attn_tma_kernel and the persistent step kernel.
+template <bool kBf16>
+__device__ __forceinline__ void attn_page(const uint8_t* sK, const uint8_t* sV, const AttnLane<kBf16>& ad,
+                                          const float (&qh)[32], int key0, int n_keys, float& m, float& l, float& a0,
+                                          float& a1, bool& finite_ok) {
+    const int lane = threadIdx.x & 31;
+    const bool valid = key0 + (lane & 15) < n_keys;
+    float dot = 0.0f;
+    if constexpr (kBf16) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 v = *reinterpret_cast<const uint4*>(sK + ad.k_off[c]);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                dot = fmaf(qh[8 * c + 2 * k], __uint_as_float(w[k] << 16), dot);
+                dot = fmaf(qh[8 * c + 2 * k + 1], __uint_as_float(w[k] & 0xffff0000u), dot);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float4 v = *reinterpret_cast<const float4*>(sK + ad.k_off[c]);
+            dot = fmaf(qh[4 * c], v.x, dot);
+            dot = fmaf(qh[4 * c + 1], v.y, dot);
+            dot = fmaf(qh[4 * c + 2], v.z, dot);
+            dot = fmaf(qh[4 * c + 3], v.w, dot);
+        }
+    }
+    dot += __shfl_xor_sync(kFull, dot, 16);
+    float score = dot * 0.125f;
+    if (valid) finite_ok &= isfinite(score);
+    score = valid ? score : -INFINITY;
+    float pm = score;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, o));
+    const float m_new = fmaxf(m, pm);
+    const float alpha = m == -INFINITY ? 0.0f : expf(m - m_new);
+    const float pr = valid ? expf(score - m_new) : 0.0f;
+    float ps = pr;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
+    l = fmaf(l, alpha, ps);
+    a0 *= alpha;
+    a1 *= alpha;
+    const int n_valid = min(kPage, n_keys - key0);
+    if (n_valid == kPage) {  // full page: no per-key guard
+#pragma unroll
+        for (int j = 0; j < kPage; ++j) {
+            const float pj = __shfl_sync(kFull, pr, j);
+            const uint8_t* vp = sV + ad.v_off[j & 7] + (j >> 3) * 1024;
+            float v0, v1;
+            if constexpr (kBf16) {
+                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vp);
+                v0 = __uint_as_float(w2 << 16);
+                v1 = __uint_as_float(w2 & 0xffff0000u);
+            } else {
+                const float2 w2 = *reinterpret_cast<const float2*>(vp);
+                v0 = w2.x;
+                v1 = w2.y;
+            }
+            a0 = fmaf(pj, v0, a0);
+            a1 = fmaf(pj, v1, a1);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kPage; ++j) {
+            const float pj = __shfl_sync(kFull, pr, j);
+            if (j < n_valid) {
+                const uint8_t* vp = sV + ad.v_off[j & 7] + (j >> 3) * 1024;
+                float v0, v1;
+                if constexpr (kBf16) {
+                    const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vp);
+                    v0 = __uint_as_float(w2 << 16);
+                    v1 = __uint_as_float(w2 & 0xffff0000u);
+                } else {
+                    const float2 w2 = *reinterpret_cast<const float2*>(vp);
+                    v0 = w2.x;
+                    v1 = w2.y;
+                }
+                a0 = fmaf(pj, v0, a0);
+                a1 = fmaf(pj, v1, a1);
+            }
+        }
+    }
+    m = m_new;
+}
+
 template <bool kBf16>
 __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_constant__ CUtensorMap tm_kv,
                                                                    AttnParams p, int n_layers, int32_t* error) {
@@ -94,9 +215,9 @@ __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_
         return;
     }
 
-    // Consumer: head = warp. Lane l scores key (l & 15) over dims (l >> 4)*32..+31.
-    const int head = warp, half = lane >> 4, key_lane = lane & 15;
-    const int krow = head * kPage + key_lane;
+    // Consumer: head = warp (attn_page).
+    const int head = warp, half = lane >> 4;
+    const AttnLane<kBf16> ad = attn_lane<kBf16>(head, lane);
     int n = 0;
     for (int s = s_begin; s < s_end; ++s) {
         const Split sp = p.splits[s];
@@ -122,71 +243,8 @@ __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_
                 break;
             }
             const uint8_t* sK = smem + st * T::kStageBytes;
-            const uint8_t* sV = sK + T::kBlockBytes;
-            const int pg = sp.page_begin + i;
-            const bool valid = pg * kPage + key_lane < sp.n_keys;
-            float dot = 0.0f;
-            if constexpr (kBf16) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(sw128(sK, krow, half * 4 + c));
-                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        dot = fmaf(qh[8 * c + 2 * k], __uint_as_float(w[k] << 16), dot);
-                        dot = fmaf(qh[8 * c + 2 * k + 1], __uint_as_float(w[k] & 0xffff0000u), dot);
-                    }
-                }
-            } else {
-                const uint8_t* box = sK + half * T::kBoxBytes;
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const float4 v = *reinterpret_cast<const float4*>(sw128(box, krow, c));
-                    dot = fmaf(qh[4 * c], v.x, dot);
-                    dot = fmaf(qh[4 * c + 1], v.y, dot);
-                    dot = fmaf(qh[4 * c + 2], v.z, dot);
-                    dot = fmaf(qh[4 * c + 3], v.w, dot);
-                }
-            }
-            dot += __shfl_xor_sync(kFull, dot, 16);
-            float score = dot * 0.125f;
-            if (valid) finite_ok &= isfinite(score);
-            score = valid ? score : -INFINITY;
-            float pm = score;
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, o));
-            const float m_new = fmaxf(m, pm);
-            const float alpha = m == -INFINITY ? 0.0f : expf(m - m_new);
-            const float pr = valid ? expf(score - m_new) : 0.0f;
-            float ps = pr;
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
-            l = fmaf(l, alpha, ps);
-            a0 *= alpha;
-            a1 *= alpha;
-            const int n_valid = min(kPage, sp.n_keys - pg * kPage);
-#pragma unroll
-            for (int j = 0; j < kPage; ++j) {
-                const float pj = __shfl_sync(kFull, pr, j);
-                if (j < n_valid) {
-                    const int vrow = head * kPage + j;
-                    float v0, v1;
-                    if constexpr (kBf16) {
-                        const uint32_t w2 =
-                            *reinterpret_cast<const uint32_t*>(sw128(sV, vrow, lane >> 2) + (lane & 3) * 4);
-                        v0 = __uint_as_float(w2 << 16);
-                        v1 = __uint_as_float(w2 & 0xffff0000u);
-                    } else {
-                        const uint8_t* box = sV + (lane >> 4) * T::kBoxBytes;
-                        const float2 w2 = *reinterpret_cast<const float2*>(sw128(box, vrow, (lane & 15) >> 1) + (lane & 1) * 8);
-                        v0 = w2.x;
-                        v1 = w2.y;
-                    }
-                    a0 = fmaf(pj, v0, a0);
-                    a1 = fmaf(pj, v1, a1);
-                }
-            }
-            m = m_new;
+            attn_page<kBf16>(sK, sK + T::kBlockBytes, ad, qh, (sp.page_begin + i) * kPage, sp.n_keys, m, l, a0, a1,
+                             finite_ok);
             __syncwarp();
             if (lane == 0) mbar_arrive(empty0 + 8 * st);
         }

@@ -98,6 +98,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // another role of this CTA already failed.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* error,
                                           volatile int* cta_failed) {
+    if (mbar_try_wait(bar, parity)) return true;  // the common case: no clock read
     const long long start = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (*cta_failed) return false;

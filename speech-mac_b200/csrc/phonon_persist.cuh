@@ -363,8 +363,8 @@ __device__ __forceinline__ void persist_attention(const CUtensorMap* tm, const P
         return;
     }
 
-    const int head = warp, half = lane >> 4, key_lane = lane & 15;
-    const int krow = head * kPage + key_lane;
+    const int head = warp, half = lane >> 4;
+    const AttnLane<kBf16> ad = attn_lane<kBf16>(head, lane);
     uint32_t n = ring;
     for (int s = s_begin; s < s_end; ++s) {
         const Split sp = p.splits[s];
@@ -388,71 +388,8 @@ __device__ __forceinline__ void persist_attention(const CUtensorMap* tm, const P
             const bool got = __all_sync(kFull, mbar_wait(full0 + 8 * st, (n / kSt) & 1, p.error, failed));
             if (got) {
                 const uint8_t* sK = stages + st * A::kStageBytes;
-                const uint8_t* sV = sK + T::kBlockBytes;
-                const int pg = sp.page_begin + i;
-                const bool valid = pg * kPage + key_lane < sp.n_keys;
-                float dot = 0.0f;
-                if constexpr (kBf16) {
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const uint4 v = *reinterpret_cast<const uint4*>(sw128(sK, krow, half * 4 + c));
-                        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            dot = fmaf(qh[8 * c + 2 * k], __uint_as_float(w[k] << 16), dot);
-                            dot = fmaf(qh[8 * c + 2 * k + 1], __uint_as_float(w[k] & 0xffff0000u), dot);
-                        }
-                    }
-                } else {
-                    const uint8_t* box = sK + half * T::kBoxBytes;
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const float4 v = *reinterpret_cast<const float4*>(sw128(box, krow, c));
-                        dot = fmaf(qh[4 * c], v.x, dot);
-                        dot = fmaf(qh[4 * c + 1], v.y, dot);
-                        dot = fmaf(qh[4 * c + 2], v.z, dot);
-                        dot = fmaf(qh[4 * c + 3], v.w, dot);
-                    }
-                }
-                dot += __shfl_xor_sync(kFull, dot, 16);
-                float score = dot * 0.125f;
-                if (valid) finite_ok &= isfinite(score);
-                score = valid ? score : -INFINITY;
-                float pm = score;
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, o));
-                const float m_new = fmaxf(m, pm);
-                const float alpha = m == -INFINITY ? 0.0f : expf(m - m_new);
-                const float pr = valid ? expf(score - m_new) : 0.0f;
-                float ps = pr;
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
-                l = fmaf(l, alpha, ps);
-                a0 *= alpha;
-                a1 *= alpha;
-                const int n_valid = min(kPage, sp.n_keys - pg * kPage);
-#pragma unroll
-                for (int j = 0; j < kPage; ++j) {
-                    const float pj = __shfl_sync(kFull, pr, j);
-                    if (j < n_valid) {
-                        const int vrow = head * kPage + j;
-                        float v0, v1;
-                        if constexpr (kBf16) {
-                            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(sw128(sV, vrow, lane >> 2) + (lane & 3) * 4);
-                            v0 = __uint_as_float(w2 << 16);
-                            v1 = __uint_as_float(w2 & 0xffff0000u);
-                        } else {
-                            const uint8_t* box = sV + (lane >> 4) * T::kBoxBytes;
-                            const float2 w2 =
-                                *reinterpret_cast<const float2*>(sw128(box, vrow, (lane & 15) >> 1) + (lane & 1) * 8);
-                            v0 = w2.x;
-                            v1 = w2.y;
-                        }
-                        a0 = fmaf(pj, v0, a0);
-                        a1 = fmaf(pj, v1, a1);
-                    }
-                }
-                m = m_new;
+                attn_page<kBf16>(sK, sK + T::kBlockBytes, ad, qh, (sp.page_begin + i) * kPage, sp.n_keys, m, l, a0,
+                                 a1, finite_ok);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(empty0 + 8 * st);
