@@ -42,9 +42,9 @@ UNIT = "frames/s"
 L2_BYTES = 126 * 2**20
 HBM_FALLBACK_GBS = 6650.0
 # DRAM bytes (read + write) per algorithmic byte of the attention kernel, from
-# one ncu capture of the same kernel on a 16-stream case; scaled by each
-# launch's algorithmic bytes to give `traffic` (profiles/attn_tma_kernel_configs3_16streams.md).
-ATTN_DRAM_PER_ALGO_BYTE = 1.013
+# one ncu capture of the same kernel on the configs[3] shape at 128 streams;
+# scaled by each launch's algorithmic bytes to give `traffic`.
+ATTN_DRAM_PER_ALGO_BYTE = 1.027
 
 
 def measured_hbm_gbs():
