@@ -207,6 +207,18 @@ int phonon_cuda_rope_interleaved(int device, float *values, size_t width, size_t
 int phonon_cuda_i8_gemm(int device, const int8_t *a, const int8_t *b, size_t m, size_t n, size_t k,
                         int32_t *d);
 
+/* ---- bounded device waits (diagnostic) ----
+ * Every spin-wait in the library's kernels (mbarrier waits of the tensor-core
+ * and attention kernels, grid barriers of the persistent step) gives up after
+ * a budget of about two seconds, raises the context's error flag and lets
+ * the kernel finish; the call then returns PHONON_CUDA_DEVICE_ERROR and the
+ * context stays usable. This entry point runs those wait routines with a
+ * budget of budget_us microseconds on something nothing completes: kind 0,
+ * an mbarrier; kind 1, a grid barrier that one CTA never reaches. It returns
+ * PHONON_CUDA_DEVICE_ERROR when the wait expired and reported it (the
+ * expected outcome), and the wall time of the kernel in *elapsed_ns. */
+int phonon_cuda_wait_expiry_probe(int device, int kind, uint32_t budget_us, uint64_t *elapsed_ns);
+
 /* ---- live kernel profiling (CUDA events on the context's stream) ---- */
 typedef enum {
     PHONON_CUDA_K_QKV = 0,       /* LN1 + QKV GEMV + RoPE + KV append */

@@ -1546,6 +1546,41 @@ uint64_t phonon_cuda_launch_count(PhononCuda* c) {
     return c->launches;
 }
 
+int phonon_cuda_wait_expiry_probe(int device, int kind, uint32_t budget_us, uint64_t* elapsed_ns) {
+    if ((kind != 0 && kind != 1) || budget_us == 0 || budget_us > 1000000) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(device);
+    if (st) return st;
+    int32_t* d_err = nullptr;
+    unsigned* d_ctr = nullptr;
+    cudaEvent_t a = nullptr, b = nullptr;
+    int clock_khz = 0;
+    int result = PHONON_CUDA_DEVICE_ERROR;
+    if (cudaMalloc(&d_err, 4) == cudaSuccess && cudaMalloc(&d_ctr, 4) == cudaSuccess &&
+        cudaMemset(d_err, 0, 4) == cudaSuccess && cudaMemset(d_ctr, 0, 4) == cudaSuccess &&
+        cudaEventCreate(&a) == cudaSuccess && cudaEventCreate(&b) == cudaSuccess &&
+        cudaDeviceGetAttribute(&clock_khz, cudaDevAttrClockRate, device) == cudaSuccess) {
+        const long long budget = static_cast<long long>(budget_us) * clock_khz / 1000;
+        // Two CTAs of one warp each fit on any device at once, which the
+        // grid barrier needs (the counter target is 2 arrivals).
+        cudaEventRecord(a);
+        wait_expiry_kernel<<<2, 32>>>(kind, budget, d_err, d_ctr);
+        cudaEventRecord(b);
+        int32_t err = 0;
+        float ms = 0.0f;
+        if (cudaGetLastError() == cudaSuccess && cudaEventSynchronize(b) == cudaSuccess &&
+            cudaMemcpy(&err, d_err, 4, cudaMemcpyDeviceToHost) == cudaSuccess &&
+            cudaEventElapsedTime(&ms, a, b) == cudaSuccess) {
+            if (elapsed_ns) *elapsed_ns = static_cast<uint64_t>(ms * 1e6);
+            result = err ? PHONON_CUDA_DEVICE_ERROR : PHONON_CUDA_OK;
+        }
+    }
+    if (a) cudaEventDestroy(a);
+    if (b) cudaEventDestroy(b);
+    if (d_err) cudaFree(d_err);
+    if (d_ctr) cudaFree(d_ctr);
+    return result;
+}
+
 int phonon_cuda_set_batch_paths(PhononCuda* c, uint32_t fused_min_batch, uint32_t fused_max_batch,
                                 uint32_t tensor_min_batch, uint32_t split_min_batch) {
     if (!c || fused_min_batch < 1 || fused_max_batch > PHONON_CUDA_FUSED_MAX_BATCH || tensor_min_batch < 1 ||

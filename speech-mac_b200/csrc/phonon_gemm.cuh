@@ -94,21 +94,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
-// Bounded wait: returns false (and raises *error) when the budget runs out or
-// another role of this CTA already failed.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* error,
-                                          volatile int* cta_failed) {
+// Bounded wait: returns false (and raises *error) when `budget` clock cycles
+// run out or another role of this CTA already failed.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, int32_t* error,
+                                              volatile int* cta_failed, long long budget) {
     if (mbar_try_wait(bar, parity)) return true;  // the common case: no clock read
     const long long start = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (*cta_failed) return false;
-        if (clock64() - start > kWaitBudgetCycles) {
+        if (clock64() - start > budget) {
             *cta_failed = 1;
             if (error) atomicExch(error, 1);
             return false;
         }
     }
     return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* error,
+                                          volatile int* cta_failed) {
+    return mbar_wait_for(bar, parity, error, cta_failed, kWaitBudgetCycles);
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {

@@ -146,7 +146,8 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
 // Grid barrier. Every CTA adds one to the counter (release); the k-th
 // barrier of a launch completes when it reaches base + k * gridDim.x
 // (wrap-safe compare, acquire). The failure flags are polled every 64 spins.
-__device__ __forceinline__ void grid_sync(const PersistParams& p, unsigned& epoch, volatile int* failed) {
+__device__ __forceinline__ void grid_sync_for(const PersistParams& p, unsigned& epoch, volatile int* failed,
+                                              long long budget) {
     __syncthreads();
     epoch += gridDim.x;
     if (threadIdx.x == 0) {
@@ -160,7 +161,7 @@ __device__ __forceinline__ void grid_sync(const PersistParams& p, unsigned& epoc
                 *failed = 1;
                 break;
             }
-            if (clock64() - start > kWaitBudgetCycles) {
+            if (clock64() - start > budget) {
                 *failed = 1;
                 atomicExch(p.error, 1);
                 break;
@@ -168,6 +169,36 @@ __device__ __forceinline__ void grid_sync(const PersistParams& p, unsigned& epoc
         }
     }
     __syncthreads();
+}
+
+__device__ __forceinline__ void grid_sync(const PersistParams& p, unsigned& epoch, volatile int* failed) {
+    grid_sync_for(p, epoch, failed, kWaitBudgetCycles);
+}
+
+// Expiry of the bounded waits, for tests: kind 0 waits on an mbarrier that
+// nothing completes; kind 1 is a grid barrier that CTA 1 never reaches. Each
+// wait gives up after `budget` cycles, raises *error and the kernel returns.
+__global__ void wait_expiry_kernel(int kind, long long budget, int32_t* error, unsigned* counter) {
+    __shared__ uint64_t bar;
+    __shared__ int failed;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_addr(&bar), 1);
+        failed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (kind == 0) {
+        if (blockIdx.x == 0 && threadIdx.x == 0)
+            mbar_wait_for(smem_addr(&bar), 0, error, reinterpret_cast<volatile int*>(&failed), budget);
+        return;
+    }
+    if (blockIdx.x != 0) return;  // CTA 1 never arrives
+    PersistParams p{};
+    p.error = error;
+    p.barrier = counter;
+    p.barrier_base = 0;
+    unsigned epoch = 0;
+    grid_sync_for(p, epoch, reinterpret_cast<volatile int*>(&failed), budget);
 }
 
 // Stage rows rs of matrix m of layer L into `buf` (plane bytes, then

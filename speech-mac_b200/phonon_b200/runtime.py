@@ -77,6 +77,7 @@ def lib():
         "phonon_cuda_profile_enable": [P, C.c_int],
         "phonon_cuda_profile_read": [P, P, P, P],
         "phonon_cuda_set_batch_paths": [P, U32, U32, U32, U32],
+        "phonon_cuda_wait_expiry_probe": [C.c_int, C.c_int, U32, C.POINTER(C.c_uint64)],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -107,6 +108,14 @@ def _p(a):
 def check(status, what):
     if status != OK:
         raise CudaError(status, what)
+
+
+def wait_expiry_probe(kind, budget_us, device=0):
+    """Run a bounded device wait on something nothing completes (kind 0: an
+    mbarrier, 1: a grid barrier); returns (status, elapsed seconds)."""
+    ns = C.c_uint64(0)
+    st = lib().phonon_cuda_wait_expiry_probe(device, kind, budget_us, C.byref(ns))
+    return st, ns.value * 1e-9
 
 
 def rel_err(a, ref, floor=1e-2):
