@@ -621,13 +621,14 @@ bool persist_shape(int R, int G, int smem_limit, bool bf16, PersistShape* out) {
                             persist_cta_rows(PM_UP, nct) * persist_row_bytes(PM_UP));
     const int w1 = std::max(persist_cta_rows(PM_OUT, nct) * persist_row_bytes(PM_OUT),
                             persist_cta_rows(PM_DOWN, nct) * persist_row_bytes(PM_DOWN));
-    // The page ring takes what is left, between 2 and kPersistMaxRing stages;
-    // the same region holds the GELU rows of a group in stage E.
+    // Stage B's page ring spans the activation region (the GELU rows of a
+    // group in stage E) and both weight buffers, which hold nothing in flight
+    // then: up to kPersistMaxRing stages, at least 2.
     const int stage = bf16 ? PersistAttn<true>::kStageBytes : PersistAttn<false>::kStageBytes;
     const int left = smem_limit - (w0 + w1 + kPersistNormBytes + 128 + 1024);
-    sh.ring = std::min(kPersistMaxRing, left / stage);
-    const int x_bytes = std::max(sh.ring * stage, kPersistGroup * kFfn * 4);
-    if (sh.ring < 2 || x_bytes > left) return false;
+    const int x_bytes = std::min(left, std::max(kPersistGroup * kFfn * 4, kPersistMaxRing * stage - w0 - w1));
+    sh.ring = std::min(kPersistMaxRing, (x_bytes + w0 + w1) / stage);
+    if (sh.ring < 2 || x_bytes < kPersistGroup * kFfn * 4) return false;
     sh.off_x = 0;
     sh.off_w0 = x_bytes;
     sh.off_w1 = sh.off_w0 + w0;

@@ -20,10 +20,11 @@
 // itself) and divides the rows of every projection, in RoPE pairs, among
 // its CTAs. Warp 8 is a copy warp: it stages the CTA's weight rows (and the
 // LayerNorm vectors) of the next projections in shared memory with bulk
-// async copies (two buffers: QKV and up share one, out and down the other,
-// each refilled as soon as the stage that read it has passed its barrier),
-// stages the GELU rows for stage E, and in stage B it is the TMA producer of
-// the page ring. Row dot products and their epilogues use gemv_kernel's
+// async copies (two buffers: QKV and up share one, out and down the other;
+// QKV rows are staged during stage E, out and up rows at the start of stage
+// C, down rows at the start of stage D), stages the GELU rows for stage E,
+// and in stage B it is the TMA producer of the page ring, which then spans
+// the activation region and both weight buffers. Row dot products and their epilogues use gemv_kernel's
 // per-lane arithmetic and summation order; the attention partials use
 // attn_tma_kernel's.
 //
@@ -545,7 +546,6 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     auto wait_fill = [&](int k) { mbar_wait(wfull0 + 8 * k, (fills[k] - 1) & 1, p.error, failed); };
 
     fill(0, 0, PM_QKV);
-    fill(1, 0, PM_OUT);
 
     // Stage 0: page-table updates and the step's RoPE table.
     {
@@ -567,7 +567,6 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
     for (int l = 0; l < p.n_layers; ++l) {
         const float* cur = l == 0 ? p.in : (((l - 1) & 1) ? p.xbuf1 : p.xbuf0);
         float* next = l == p.n_layers - 1 ? p.out : ((l & 1) ? p.xbuf1 : p.xbuf0);
-        if (l > 0) fill(1, l, PM_OUT);
 
         // A: LN1 -> QKV -> RoPE -> q, KV append
         if (warp < kPersistWarps) wait_fill(0);
@@ -584,14 +583,17 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         grid_sync(p, epoch, failed);
         PERSIST_MARK(l, 3);
 
-        // B: attention partials
-        fill(0, l, PM_UP);
+        // B: attention partials. No weight copy is in flight now, so the
+        // page ring may span both weight buffers as well.
         persist_attention<kBf16>(&tm_kv, p, l, stages, full0, empty0, ring, last_issue, failed);
         PERSIST_MARK(l, 4);
         grid_sync(p, epoch, failed);
         PERSIST_MARK(l, 5);
 
-        // C: merge the splits, h = x + attn Wout^T
+        // C: merge the splits, h = x + attn Wout^T (the out rows arrive while
+        // the merge runs; the up rows are needed in D)
+        fill(1, l, PM_OUT);
+        fill(0, l, PM_UP);
         if (warp < kPersistWarps) persist_merge(p, xs, b0, nb);
         __syncthreads();
         PERSIST_MARK(l, 6);
