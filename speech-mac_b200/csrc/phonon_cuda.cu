@@ -231,9 +231,9 @@ int upload_linear(int kind, const void* host, size_t rows, size_t cols, DevLinea
 }
 
 // ------------------------------------------------------------- GEMV launcher
-template <bool kQ8, int kChunks, int kBT, bool kLN, int kEpi>
+template <bool kQ8, int kChunks, int kBT, int kSrc, int kEpi>
 cudaError_t launch_gemv_t(const GemvParams& p, cudaStream_t s) {
-    auto kern = gemv_kernel<kQ8, kChunks, kBT, kLN, kEpi>;
+    auto kern = gemv_kernel<kQ8, kChunks, kBT, kSrc, kEpi>;
     constexpr int smem = kBT * kChunks * 512 * 4;
     if constexpr (smem > 48 * 1024) {
         // The opt-in shared memory size is a per-device function attribute.
@@ -252,17 +252,17 @@ cudaError_t launch_gemv_t(const GemvParams& p, cudaStream_t s) {
     return launch_pdl(kern, dim3((p.rows + rows_per_cta - 1) / rows_per_cta), dim3(kGemvWarps * 32), smem, s, p);
 }
 
-template <bool kQ8, int kChunks, bool kLN, int kEpi>
+template <bool kQ8, int kChunks, int kSrc, int kEpi>
 cudaError_t launch_gemv_bt(const GemvParams& p, cudaStream_t s) {
-    if (p.B <= 1) return launch_gemv_t<kQ8, kChunks, 1, kLN, kEpi>(p, s);
-    if (p.B <= 2) return launch_gemv_t<kQ8, kChunks, 2, kLN, kEpi>(p, s);
-    if (p.B <= 4) return launch_gemv_t<kQ8, kChunks, 4, kLN, kEpi>(p, s);
-    return launch_gemv_t<kQ8, kChunks, 8, kLN, kEpi>(p, s);
+    if (p.B <= 1) return launch_gemv_t<kQ8, kChunks, 1, kSrc, kEpi>(p, s);
+    if (p.B <= 2) return launch_gemv_t<kQ8, kChunks, 2, kSrc, kEpi>(p, s);
+    if (p.B <= 4) return launch_gemv_t<kQ8, kChunks, 4, kSrc, kEpi>(p, s);
+    return launch_gemv_t<kQ8, kChunks, 8, kSrc, kEpi>(p, s);
 }
 
-template <int kChunks, bool kLN, int kEpi>
+template <int kChunks, int kSrc, int kEpi>
 cudaError_t launch_gemv(bool q8, const GemvParams& p, cudaStream_t s) {
-    return q8 ? launch_gemv_bt<true, kChunks, kLN, kEpi>(p, s) : launch_gemv_bt<false, kChunks, kLN, kEpi>(p, s);
+    return q8 ? launch_gemv_bt<true, kChunks, kSrc, kEpi>(p, s) : launch_gemv_bt<false, kChunks, kSrc, kEpi>(p, s);
 }
 
 cudaError_t launch_linear(const DevLinear& l, const float* x, int B, const float* bias, float* y,
@@ -281,7 +281,7 @@ cudaError_t launch_linear(const DevLinear& l, const float* x, int B, const float
         p.y = y;
         p.ldy = l.rows;
         p.status = status;
-        return l.cols == 512 ? launch_gemv<1, false, EPI_STORE>(q8, p, s) : launch_gemv<4, false, EPI_STORE>(q8, p, s);
+        return l.cols == 512 ? launch_gemv<1, SRC_X, EPI_STORE>(q8, p, s) : launch_gemv<4, SRC_X, EPI_STORE>(q8, p, s);
     }
     const long long warps = static_cast<long long>(l.rows) * B;
     const int threads = 256;
@@ -743,25 +743,23 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
         return PHONON_CUDA_OK;
     }
     {
-        LaunchScope ls(c, PHONON_CUDA_K_OTHER, R * 32 * 12.0, b.lane->stream);
-        CUDA_TRY(launch_pdl(rope_table_kernel, dim3((R * 32 + 255) / 256), dim3(256), 0, lane->stream,
-                            static_cast<const int32_t*>(b.d_pos), static_cast<const float*>(c->d_freq), R, b.d_rope));
-    }
-    if (U > 0) {
-        LaunchScope ls(c, PHONON_CUDA_K_OTHER, U * 12.0, b.lane->stream);
-        CUDA_TRY(launch_pdl(page_update_kernel, dim3((U + 127) / 128), dim3(128), 0, lane->stream, c->d_table,
-                            kMaxPagesPerStream, static_cast<const int32_t*>(b.d_updates), U));
+        LaunchScope ls(c, PHONON_CUDA_K_OTHER, R * 32 * 12.0 + U * 12.0, b.lane->stream);
+        const int threads = std::max(R * 32, U);
+        CUDA_TRY(launch_pdl(step_prep_kernel, dim3((threads + 255) / 256), dim3(256), 0, lane->stream,
+                            static_cast<const int32_t*>(b.d_pos), static_cast<const float*>(c->d_freq), R, b.d_rope,
+                            c->d_table, kMaxPagesPerStream, static_cast<const int32_t*>(b.d_updates), U));
     }
     *out = b;
     return PHONON_CUDA_OK;
 }
 
 // Enqueue layer `l` for the batch: in -> out (out != in).
-int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out = false);
+int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out = false, bool no_merge = false);
 
 // Split-K attention then the split merge. With digits_out the merge writes
-// the digit rows of the attention output (tensor-core path) instead of fp32.
-int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out) {
+// the digit rows of the attention output (tensor-core path) instead of fp32;
+// with no_merge the consumer merges the partials itself.
+int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out, bool no_merge) {
     cudaStream_t s = b.lane->stream;
     const KvView kv = kv_view(c);
     const double act = 4.0 * b.R;
@@ -789,6 +787,7 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out) {
                              : launch_pdl(attn_partial_kernel<false>, dim3(grid), dim3(kAttnWarps * 32), 0, s, ap));
         }
     }
+    if (no_merge) return PHONON_CUDA_OK;
     CombineParams cp{};
     cp.part = b.lane->part;
     cp.first = b.d_first;
@@ -924,14 +923,14 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     const double esize = kv.bf16 ? 2.0 : 4.0;
     {
         LaunchScope ls(c, PHONON_CUDA_K_QKV, linear_bytes(L.qkv) + act * (kWidth + kWidth) + b.R * 2.0 * kWidth * esize, b.lane->stream);
-        CUDA_TRY((launch_gemv<1, true, EPI_QKV>(q8, p, s)));
+        CUDA_TRY((launch_gemv<1, SRC_LN, EPI_QKV>(q8, p, s)));
     }
-    // 2. split-K attention + combine
+    // 2. split-K attention (the out projection merges the splits)
     {
-        int st = enqueue_attention(c, b, l);
+        int st = enqueue_attention(c, b, l, false, true);
         if (st) return st;
     }
-    // 3. h = x + attn Wout^T
+    // 3. h = x + attn Wout^T, attn merged from the split partials
     GemvParams po{};
     po.B = b.R;
     po.status = b.d_status;
@@ -939,7 +938,9 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     po.scales = L.out.scales;
     po.rows = 512;
     po.cols = 512;
-    po.x = b.lane->a;
+    po.part = b.lane->part;
+    po.first = b.d_first;
+    po.count = b.d_count;
     po.ldx = kWidth;
     po.res = in;
     po.ldres = kWidth;
@@ -947,7 +948,7 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     po.ldy = kWidth;
     {
         LaunchScope ls(c, PHONON_CUDA_K_OUT, linear_bytes(L.out) + act * 3 * kWidth, b.lane->stream);
-        CUDA_TRY((launch_gemv<1, false, EPI_RESID>(q8, po, s)));
+        CUDA_TRY((launch_gemv<1, SRC_MERGE, EPI_RESID>(q8, po, s)));
     }
     // 4. g = GELU(LN2(h) Wup^T)
     GemvParams pu{};
@@ -965,7 +966,7 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     pu.ldy = kFfn;
     {
         LaunchScope ls(c, PHONON_CUDA_K_UP, linear_bytes(L.up) + act * (kWidth + kFfn), b.lane->stream);
-        CUDA_TRY((launch_gemv<1, true, EPI_GELU>(q8, pu, s)));
+        CUDA_TRY((launch_gemv<1, SRC_LN, EPI_GELU>(q8, pu, s)));
     }
     // 5. out = h + g Wdown^T
     GemvParams pd{};
@@ -983,7 +984,7 @@ int enqueue_layer(PhononCuda* c, const Batch& b, int l, const float* in, float* 
     pd.ldy = kWidth;
     {
         LaunchScope ls(c, PHONON_CUDA_K_DOWN, linear_bytes(L.down) + act * (kFfn + 2 * kWidth), b.lane->stream);
-        CUDA_TRY((launch_gemv<4, false, EPI_RESID>(q8, pd, s)));
+        CUDA_TRY((launch_gemv<4, SRC_X, EPI_RESID>(q8, pd, s)));
     }
     return PHONON_CUDA_OK;
 }

@@ -3,9 +3,9 @@
 // Kernels of one Flow layer step, in launch order:
 //   gemv_kernel<LN, EPI_QKV>   LN1 -> [q|k|v] = xn Wqkv^T -> RoPE(q,k) -> q to scratch,
 //                              k/v appended to the stream's KV page
-//   attn_partial_kernel        split-K flash-decode over 16-position pages
-//   attn_combine_kernel        merge the splits of each (stream, head)
-//   gemv_kernel<-, EPI_RESID>  h = x + attn Wout^T
+//   attn_tma_kernel            split-K flash-decode over 16-position pages
+//   gemv_kernel<MERGE, RESID>  merge the splits of each (stream, head), then
+//                              h = x + attn Wout^T
 //   gemv_kernel<LN, EPI_GELU>  g = GELU(LN2(h) Wup^T)
 //   gemv_kernel<-, EPI_RESID>  x' = h + g Wdown^T
 //
@@ -35,6 +35,9 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kStatusNonFinite = 2;  // PHONON_CUDA_NON_FINITE
 
 enum Epilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_GELU = 2, EPI_QKV = 3 };
+// Where a GEMV's activation rows come from: x as is, LayerNorm(x), or the
+// merge of the step's attention split partials (the attention output).
+enum GemvSource : int { SRC_X = 0, SRC_LN = 1, SRC_MERGE = 2 };
 
 // Programmatic dependent launch: kernels of a step are launched so that the
 // next one may start while this one drains. pdl_wait() blocks until the
@@ -250,12 +253,16 @@ __device__ __forceinline__ void rope_apply(float& a, float& b, float2 cs) {
     b = rb;
 }
 
-// Per-step RoPE table: cs[e][i] = (cos, sin) of pos[e] * freq[i] for the
-// 32 frequencies of a 64-wide head; every layer of the step reuses it.
-__global__ void rope_table_kernel(const int32_t* pos, const float* freq, int R, float2* cs) {
+// Start of a step: apply the page-table updates ((slot, index, page)
+// triples) and build the step's RoPE table, cs[e][i] = (cos, sin) of
+// pos[e] * freq[i] for the 32 frequencies of a 64-wide head (every layer of
+// the step reuses it).
+__global__ void step_prep_kernel(const int32_t* pos, const float* freq, int R, float2* cs, int32_t* table,
+                                 int max_pages, const int32_t* updates, int U) {
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < U) table[static_cast<size_t>(updates[3 * t]) * max_pages + updates[3 * t + 1]] = updates[3 * t + 2];
     if (t >= R * 32) return;
     const float phase = __fmul_rn(static_cast<float>(pos[t >> 5]), freq[t & 31]);
     double sd, cd;
@@ -289,6 +296,29 @@ __device__ __forceinline__ void kv_store2(const KvView& kv, long long off, float
     }
 }
 
+// Attention split partials: per (split, head) the running max, the sum of
+// exponentials and the 64 accumulated output dims.
+constexpr int kPartStride = 2 + kHeadDim;
+
+// Split merge, one step: fold the partial (pm, pl, pa) of the next split (in
+// page order) into the running (M, S, A): M' = max(M, pm), S' = S e^(M-M') +
+// pl e^(pm-M'), A' = A e^(M-M') + pa e^(pm-M'); the merged head output is
+// A / S. All merge paths (per-stage, tensor-core and persistent) use it.
+struct MergeWeights {
+    float alpha, beta;
+};
+
+__device__ __forceinline__ MergeWeights merge_weights(float& M, float pm) {
+    const float M2 = fmaxf(M, pm);
+    MergeWeights w;
+    w.alpha = M == -INFINITY ? 0.0f : expf(M - M2);
+    w.beta = pm == -INFINITY ? 0.0f : expf(pm - M2);
+    M = M2;
+    return w;
+}
+
+__device__ __forceinline__ float merge_fold(float acc, MergeWeights w, float v) { return fmaf(acc, w.alpha, w.beta * v); }
+
 // --------------------------------------------------------------------- GEMV
 // Device weight layout ("lane-interleaved", cols a multiple of 512): in row r,
 // the 16 bytes at r*cols + c*512 + lane*16 hold the int8 weights of logical
@@ -303,8 +333,11 @@ struct GemvParams {
     int rows, cols;
     const float* x;           // [B][ldx]
     int ldx, B;
-    const float* ln_w;        // LN prologue (fp32 [512]) when kLN
+    const float* ln_w;        // SRC_LN: LayerNorm weight and bias (fp32 [512])
     const float* ln_b;
+    const float* part;        // SRC_MERGE: split partials [S][8][66] ...
+    const int32_t* first;     // ... and each stream's first split and split count
+    const int32_t* count;
     const float* bias;        // EPI_STORE, optional
     float* y;                 // output [B][ldy]
     int ldy;
@@ -320,8 +353,9 @@ struct GemvParams {
     int32_t* status;          // [B]
 };
 
-template <bool kQ8, int kChunks, int kBT, bool kLN, int kEpi>
+template <bool kQ8, int kChunks, int kBT, int kSrc, int kEpi>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
+    constexpr bool kLN = kSrc == SRC_LN;
     extern __shared__ __align__(16) float xs[];  // [kBT][kChunks * 512]
     __shared__ int ln_bad[kBT];
     constexpr int cols = kChunks * 512;
@@ -372,6 +406,28 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
                 bool ok = warp_layernorm512(p.x + static_cast<size_t>(b0 + r) * p.ldx, p.ln_w,
                                             p.ln_b, xs + r * cols);
                 if (lane == 0) ln_bad[r] = ok ? 0 : 1;
+            }
+        } else if constexpr (kSrc == SRC_MERGE) {
+            // Warp h merges head h of every stream of the tile (the
+            // arithmetic of attn_combine_kernel).
+            const int head = warp, lane_ = threadIdx.x & 31;
+            for (int r = 0; r < nb; ++r) {
+                const int b = b0 + r, first = p.first[b], n = p.count[b];
+                float M = -INFINITY, total = 0.0f, a0 = 0.0f, a1 = 0.0f;
+                for (int s = 0; s < n; ++s) {
+                    const float* pp = p.part + (static_cast<size_t>(first + s) * kHeads + head) * kPartStride;
+                    const MergeWeights w = merge_weights(M, pp[0]);
+                    total = merge_fold(total, w, pp[1]);
+                    const float2 av = *reinterpret_cast<const float2*>(pp + 2 + 2 * lane_);
+                    a0 = merge_fold(a0, w, av.x);
+                    a1 = merge_fold(a1, w, av.y);
+                }
+                bool ok = total > 0.0f && isfinite(total);
+                const float inv = __fdiv_rn(1.0f, total);
+                const float o0 = __fmul_rn(a0, inv), o1 = __fmul_rn(a1, inv);
+                ok &= isfinite(o0) && isfinite(o1);
+                *reinterpret_cast<float2*>(xs + r * cols + head * kHeadDim + 2 * lane_) = make_float2(o0, o1);
+                if (!__all_sync(kFull, ok) && lane_ == 0 && blockIdx.x == 0) flag_nonfinite(p.status, b);
             }
         } else {
             const int n4 = nb * cols / 4;
@@ -544,7 +600,6 @@ struct AttnParams {
     int32_t* status;
 };
 
-constexpr int kPartStride = 2 + kHeadDim;
 
 // One warp per (split, head). Lane l scores key (l & 15) of the current page
 // over dims (l >> 4)*32 .. +31, so the two halves of a 64-dim dot meet with a
@@ -665,25 +720,6 @@ struct CombineParams {
     int32_t* status;
 };
 
-// Split merge, one step: fold the partial (pm, pl, pa) of the next split (in
-// page order) into the running (M, S, A): M' = max(M, pm), S' = S e^(M-M') +
-// pl e^(pm-M'), A' = A e^(M-M') + pa e^(pm-M'); the merged head output is
-// A / S. All merge paths (per-stage, tensor-core and persistent) use it.
-struct MergeWeights {
-    float alpha, beta;
-};
-
-__device__ __forceinline__ MergeWeights merge_weights(float& M, float pm) {
-    const float M2 = fmaxf(M, pm);
-    MergeWeights w;
-    w.alpha = M == -INFINITY ? 0.0f : expf(M - M2);
-    w.beta = pm == -INFINITY ? 0.0f : expf(pm - M2);
-    M = M2;
-    return w;
-}
-
-__device__ __forceinline__ float merge_fold(float acc, MergeWeights w, float v) { return fmaf(acc, w.alpha, w.beta * v); }
-
 // One warp per (stream, head): merge the stream's splits in page order.
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_combine_kernel(CombineParams p) {
     const int lane = threadIdx.x & 31;
@@ -712,14 +748,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_combine_kernel(CombinePa
 }
 
 // ------------------------------------------------------------- small kernels
-// Apply page-table updates: (slot, index, page) triples.
-__global__ void page_update_kernel(int32_t* table, int max_pages, const int32_t* updates, int n) {
-    pdl_wait();
-    pdl_trigger();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) table[static_cast<size_t>(updates[3 * i]) * max_pages + updates[3 * i + 1]] = updates[3 * i + 2];
-}
-
 // Copy K/V rows between a staging buffer and the pages of one stream.
 // Staging layout: keys [layer_count][count][512] then values, fp32.
 // dir 0: pages -> staging, 1: staging -> pages.
