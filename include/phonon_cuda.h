@@ -248,9 +248,11 @@ uint64_t phonon_cuda_launch_count(PhononCuda *ctx);
  * tensor_min_batch streams up, and from split_min_batch streams up as two
  * half batches on two CUDA streams, so that one half's attention overlaps
  * the other half's projections. Defaults: 8, PHONON_CUDA_FUSED_MAX_BATCH, 32,
- * 384 (a few streams are as fast one launch per stage; halves gain from a
+ * 320 (a few streams are as fast one launch per stage; halves gain from a
  * few hundred streams; the second lane exists when max_batch >= 96). A step
- * on two lanes gives the same results as on one, bit for bit. fused_min_batch > fused_max_batch disables the
+ * on two lanes gives the results of one lane up to rounding: each half
+ * plans its attention splits on its own, so partial sums merge in another
+ * order. fused_min_batch > fused_max_batch disables the
  * persistent step; fused_min_batch = 0, fused_max_batch >
  * PHONON_CUDA_FUSED_MAX_BATCH, tensor_min_batch = 0 or split_min_batch < 2
  * are PHONON_CUDA_INVALID_ARGUMENT. The persistent and per-stage GEMV paths

@@ -1,16 +1,24 @@
 // Split-K paged flash-decode with TMA page staging (sm_100a).
 //
-// One CTA per balanced chunk of pages (its splits [cta_split[c],
-// cta_split[c+1]), one split per stream segment; or one split per CTA when
-// there is no chunk table), all 8 heads: warp 8 is a producer that, for every
-// page, looks the page up in the stream's page table and TMA-loads the page's
-// K block and V block of this layer ([8 heads][16 slots][64 dims], 16 KB each
-// in bf16) into a ring of shared-memory stages that runs on across the
-// chunk's splits; warps 0-7 (one per head) consume each stage with the online
-// softmax of attn_partial_kernel, release it, and write one partial per split. Tiles are loaded with
-// SWIZZLE_128B (16-byte chunk index XOR row % 8), so the per-key row reads of
-// the consumers are bank-conflict free. fp32 pages use two 128-byte column
-// boxes per block. No multicast; every wait is bounded.
+// The step's pages, in (stream, page) order, are cut into chunks (large
+// first, small last: guided self-scheduling) and each chunk into one split
+// per stream segment it covers. A CTA runs its own chunk c = blockIdx.x
+// first, then takes chunks by ticket from an atomic counter until they run
+// out, so that CTAs whose memory traffic is slower (or that start late
+// because the SM is busy) take fewer pages and the launch ends together.
+// Warp 8 is the producer: for every page it TMA-loads the page's K block and
+// V block of this layer ([8 heads][16 slots][64 dims], 16 KB each in bf16)
+// into a ring of shared-memory stages that runs on across splits and
+// chunks, tagging each stage with its chunk; page ids come from the step's
+// flat list (split order, uploaded with the step's plan), 32 per coalesced
+// load, and a chunk's ticket is drawn while the previous chunk's pages go
+// out. After the last chunk it sends an end tag through the ring. Warps 0-7
+// (one per head) consume each stage with the online softmax of
+// attn_partial_kernel, release it, and write one partial per split. K/V
+// loads carry an L2 evict-first hint. Tiles are loaded with SWIZZLE_128B
+// (16-byte chunk index XOR row % 8), so the per-key row reads of the
+// consumers are bank-conflict free. fp32 pages use two 128-byte column boxes
+// per block. No multicast; every wait is bounded.
 #pragma once
 
 #include "phonon_gemm.cuh"
@@ -163,13 +171,14 @@ __device__ __forceinline__ void attn_page(const uint8_t* sK, const uint8_t* sV, 
 }
 
 template <bool kBf16>
-__global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_constant__ CUtensorMap tm_kv,
+__global__ void __launch_bounds__(kAttnTmaThreads, 2) attn_tma_kernel(const __grid_constant__ CUtensorMap tm_kv,
                                                                    AttnParams p, int n_layers, int32_t* error) {
     using T = AttnTma<kBf16>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + T::kStages * T::kStageBytes);
     volatile int* failed = reinterpret_cast<volatile int*>(bars + 2 * T::kStages);
+    volatile int* stage_chunk = failed + 1;  // [kStages]: chunk of the stage's page; -1: no more chunks
     const uint32_t full0 = smem_addr(bars), empty0 = full0 + 8 * T::kStages;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -182,34 +191,73 @@ __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    pdl_wait();  // q, the page table and the metadata come from earlier kernels
-    // This CTA's splits: a balanced chunk of pages (cta_split) or one split.
-    // The step's metadata is read only after the wait: nothing of it may be
-    // read while earlier launches of the stream can still be in flight.
-    const int s_begin = p.cta_split ? __ldcg(p.cta_split + blockIdx.x) : static_cast<int>(blockIdx.x);
-    const int s_end = p.cta_split ? __ldcg(p.cta_split + blockIdx.x + 1) : static_cast<int>(blockIdx.x) + 1;
+    pdl_wait();  // q, the appended K/V, the plan and the ticket counter come from earlier work
+    const int n_chunks = __ldcg(p.plan + 1);
+    const int32_t* cta_split = p.plan + __ldcg(p.plan + 2);
+    const int32_t* cta_page = p.plan + __ldcg(p.plan + 3);
+    const int32_t* ids = p.plan + __ldcg(p.plan + 4);
 
     if (warp == kAttnHeadsPerCta) {
-        if (lane == 0) {
-            // Ring index n runs on across the CTA's splits: stage n % kStages, use n / kStages.
-            int n = 0;
-            for (int s = s_begin; s < s_end && !*failed; ++s) {
-                const Split sp = p.splits[s];
-                const int32_t* table = p.kv.table + static_cast<size_t>(p.slot[sp.b]) * p.kv.max_pages;
-                for (int i = 0; i < sp.page_count; ++i, ++n) {
-                    const int st = n % T::kStages;
-                    if (n >= T::kStages && !mbar_wait(empty0 + 8 * st, ((n / T::kStages) - 1) & 1, error, failed)) break;
-                    const int page = table[sp.page_begin + i];
-                    const int row0 = (page * n_layers + p.layer) * 256;  // K block; V block follows
-                    uint8_t* stage = smem + st * T::kStageBytes;
-                    mbar_expect_tx(full0 + 8 * st, T::kStageBytes);
+        // Ring index n runs on across splits and chunks: stage n % kStages,
+        // use n / kStages. Lane j holds the id of page n0 + j of the chunk;
+        // lane 0 issues.
+        const uint64_t policy = l2_evict_first_policy();
+        int n = 0;
+        bool stop = false;
+        int c = blockIdx.x;
+        int f0 = 0, np = 0;
+        if (c < n_chunks) {
+            f0 = __ldcg(cta_page + c);
+            np = __ldcg(cta_page + c + 1) - f0;
+        }
+        int id = lane < np ? __ldcg(ids + f0 + lane) : 0;
+        while (c < n_chunks && !stop) {
+            // the next chunk: ticket and bounds, in flight while this chunk's pages go out
+            int ticket = 0;
+            if (lane == 0) ticket = atomicAdd(p.chunk_ctr, 1);
+            const int c_next = static_cast<int>(gridDim.x) + __shfl_sync(kFull, ticket, 0);
+            int f0n = 0, npn = 0;
+            if (c_next < n_chunks) {
+                f0n = __ldcg(cta_page + c_next);
+                npn = __ldcg(cta_page + c_next + 1) - f0n;
+            }
+            for (int n0 = 0; n0 < np && !stop; n0 += 32) {
+                if (n0 > 0) id = n0 + lane < np ? __ldcg(ids + f0 + n0 + lane) : 0;
+                const int cnt = min(32, np - n0);
+                for (int j = 0; j < cnt; ++j, ++n) {
+                    const int page = __shfl_sync(kFull, id, j);
+                    if (lane == 0) {
+                        const int st = n % T::kStages;
+                        if (n < T::kStages || mbar_wait(empty0 + 8 * st, ((n / T::kStages) - 1) & 1, error, failed)) {
+                            const int row0 = (page * n_layers + p.layer) * 256;  // K block; V block follows
+                            uint8_t* stage = smem + st * T::kStageBytes;
+                            stage_chunk[st] = c;
+                            mbar_expect_tx(full0 + 8 * st, T::kStageBytes);
 #pragma unroll
-                    for (int bx = 0; bx < T::kBoxes; ++bx) {
-                        tma_load_2d(smem_addr(stage + bx * T::kBoxBytes), &tm_kv, bx * T::kBoxCols, row0, full0 + 8 * st);
-                        tma_load_2d(smem_addr(stage + T::kBlockBytes + bx * T::kBoxBytes), &tm_kv, bx * T::kBoxCols,
-                                    row0 + 128, full0 + 8 * st);
+                            for (int bx = 0; bx < T::kBoxes; ++bx) {
+                                tma_load_2d_hint(smem_addr(stage + bx * T::kBoxBytes), &tm_kv, bx * T::kBoxCols,
+                                                 row0, full0 + 8 * st, policy);
+                                tma_load_2d_hint(smem_addr(stage + T::kBlockBytes + bx * T::kBoxBytes), &tm_kv,
+                                                 bx * T::kBoxCols, row0 + 128, full0 + 8 * st, policy);
+                            }
+                        }
                     }
+                    // one decision for the whole warp (a wait that gave up sets *failed)
+                    stop = __any_sync(kFull, *failed != 0);
+                    if (stop) break;
                 }
+            }
+            c = c_next;
+            f0 = f0n;
+            np = npn;
+            id = c < n_chunks && lane < np ? __ldcg(ids + f0 + lane) : 0;
+        }
+        if (!stop && lane == 0) {
+            pdl_trigger();  // everything left of this CTA is in the ring
+            const int st = n % T::kStages;
+            if (n < T::kStages || mbar_wait(empty0 + 8 * st, ((n / T::kStages) - 1) & 1, error, failed)) {
+                stage_chunk[st] = -1;  // end tag: completes the stage's phase without data
+                mbar_arrive(full0 + 8 * st);
             }
         }
         return;
@@ -219,44 +267,53 @@ __global__ void __launch_bounds__(kAttnTmaThreads) attn_tma_kernel(const __grid_
     const int head = warp, half = lane >> 4;
     const AttnLane<kBf16> ad = attn_lane<kBf16>(head, lane);
     int n = 0;
-    for (int s = s_begin; s < s_end; ++s) {
-        const Split sp = p.splits[s];
-        float qh[32];
-        {
-            const float4* qs = reinterpret_cast<const float4*>(p.q + static_cast<size_t>(sp.b) * kWidth + head * kHeadDim +
-                                                               half * 32);
+    bool ok = true;
+    while (ok) {
+        const int st0 = n % T::kStages;
+        if (!__all_sync(kFull, mbar_wait(full0 + 8 * st0, (n / T::kStages) & 1, error, failed))) break;
+        const int c = stage_chunk[st0];
+        if (c < 0) break;
+        const int s_begin = __ldcg(cta_split + c), s_end = __ldcg(cta_split + c + 1);
+        bool landed = true;  // stage n has been waited for
+        for (int s = s_begin; s < s_end && ok; ++s) {
+            const Split sp = p.splits[s];
+            float qh[32];
+            {
+                const float4* qs = reinterpret_cast<const float4*>(p.q + static_cast<size_t>(sp.b) * kWidth +
+                                                                   head * kHeadDim + half * 32);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float4 v = qs[i];
-                qh[4 * i] = v.x;
-                qh[4 * i + 1] = v.y;
-                qh[4 * i + 2] = v.z;
-                qh[4 * i + 3] = v.w;
+                for (int i = 0; i < 8; ++i) {
+                    const float4 v = qs[i];
+                    qh[4 * i] = v.x;
+                    qh[4 * i + 1] = v.y;
+                    qh[4 * i + 2] = v.z;
+                    qh[4 * i + 3] = v.w;
+                }
             }
-        }
-        float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f;
-        bool finite_ok = true;
-        for (int i = 0; i < sp.page_count; ++i, ++n) {
-            const int st = n % T::kStages;
-            if (!__all_sync(kFull, mbar_wait(full0 + 8 * st, (n / T::kStages) & 1, error, failed))) {
-                s = s_end;  // give up: the error flag is raised
-                break;
+            float m = -INFINITY, l = 0.0f, a0 = 0.0f, a1 = 0.0f;
+            bool finite_ok = true;
+            for (int i = 0; i < sp.page_count; ++i, ++n) {
+                const int st = n % T::kStages;
+                if (!landed && !__all_sync(kFull, mbar_wait(full0 + 8 * st, (n / T::kStages) & 1, error, failed))) {
+                    ok = false;  // give up: the error flag is raised
+                    break;
+                }
+                landed = false;
+                const uint8_t* sK = smem + st * T::kStageBytes;
+                attn_page<kBf16>(sK, sK + T::kBlockBytes, ad, qh, (sp.page_begin + i) * kPage, sp.n_keys, m, l, a0,
+                                 a1, finite_ok);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty0 + 8 * st);
             }
-            const uint8_t* sK = smem + st * T::kStageBytes;
-            attn_page<kBf16>(sK, sK + T::kBlockBytes, ad, qh, (sp.page_begin + i) * kPage, sp.n_keys, m, l, a0, a1,
-                             finite_ok);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(empty0 + 8 * st);
+            if (!ok) break;
+            float* out = p.part + (static_cast<size_t>(s) * kHeads + head) * kPartStride;
+            *reinterpret_cast<float2*>(out + 2 + 2 * lane) = make_float2(a0, a1);
+            if (lane == 0) {
+                out[0] = m;
+                out[1] = l;
+            }
+            if (!__all_sync(kFull, finite_ok) && lane == 0) flag_nonfinite(p.status, sp.b);
         }
-        if (s >= s_end) break;  // a wait gave up
-        if (s == s_end - 1) pdl_trigger();
-        float* out = p.part + (static_cast<size_t>(s) * kHeads + head) * kPartStride;
-        *reinterpret_cast<float2*>(out + 2 + 2 * lane) = make_float2(a0, a1);
-        if (lane == 0) {
-            out[0] = m;
-            out[1] = l;
-        }
-        if (!__all_sync(kFull, finite_ok) && lane == 0) flag_nonfinite(p.status, sp.b);
     }
 }
 

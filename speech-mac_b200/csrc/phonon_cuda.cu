@@ -30,7 +30,11 @@ constexpr int kPrefillChunk = 256;  // rows per prefill pass
 constexpr int kTensorMinBatch = 32;  // streams from which projections run on tcgen05
 constexpr int kMaxSms = 1024;        // bound on the SM count (persistent split table)
 constexpr int kFusedMinBatch = 8;    // smaller batches are as fast or faster one launch per stage
-constexpr int kSplitMinBatch = 192;  // from here a step runs as two concurrent half batches
+constexpr int kPlanHeader = 8;       // ints of the step plan header in the metadata
+constexpr int kGuide = 2;            // guided chunks: remaining pages / (kGuide * attention CTAs)
+constexpr int kTicketMinChunk = 8;   // pages per guided chunk, at least
+constexpr int kMaxChunks = 8192;     // chunks per plan, at most
+constexpr int kSplitMinBatch = 320;  // from here a step runs as two concurrent half batches
 
 #define CUDA_TRY(expr)                                                                       \
     do {                                                                                     \
@@ -331,8 +335,15 @@ cudaError_t launch_attn_tma(const CUtensorMap& tm, const AttnParams& p, int n_la
 template <int kCols, bool kLN>
 cudaError_t launch_digits(const float* x, int ldx, const float* ln_w, const float* ln_b, int B, int Bpad,
                           int8_t* digits, int32_t* exps, int32_t* status, cudaStream_t s) {
-    return launch_pdl(digits_kernel<kCols, kLN>, dim3((Bpad + 7) / 8), dim3(256), 0, s, x, ldx, ln_w, ln_b, B, Bpad,
-                      digits, exps, status);
+    if constexpr (kLN) {
+        static_assert(kCols == kWidth, "LayerNorm rows are 512 wide");
+        return launch_pdl(ln_digits_kernel, dim3((Bpad + 7) / 8), dim3(256), 0, s, x, ldx, ln_w, ln_b, B, Bpad,
+                          digits, exps, status);
+    } else {
+        constexpr int rows_per_cta = 256 / (kCols / 8);
+        return launch_pdl(digits_kernel<kCols>, dim3((Bpad + rows_per_cta - 1) / rows_per_cta), dim3(256), 0, s, x,
+                          ldx, B, Bpad, digits, exps, status);
+    }
 }
 
 }  // namespace
@@ -362,6 +373,10 @@ struct Lane {
     CUtensorMap tm_dig512, tm_dig2048;
     float2* rope = nullptr;
     cudaEvent_t ready = nullptr;  // recorded when the lane's share of a step is enqueued
+    int32_t* chunk_ctr = nullptr;  // [n_layers] attention chunk tickets, zeroed at step start
+    std::vector<long long> h_cuts;  // host scratch of the split planner: chunk boundaries
+    std::vector<int32_t> h_pages;   //   page ids in split order
+    std::vector<int32_t> h_first_split;  //   first split of each chunk
 };
 
 struct PhononCuda {
@@ -563,8 +578,10 @@ struct Batch {
     double keys = 0;  // sum over entries of (position + 1)
     float2* d_rope = nullptr;  // [R][32] (cos, sin) of this batch's positions
     int32_t *d_slot, *d_pos, *d_first, *d_count, *d_updates;
-    int32_t* d_cta_split = nullptr;  // split range of each attention CTA (chunk)
+    int32_t* d_plan = nullptr;       // plan header (splits, chunks, table offsets)
+    int32_t* d_cta_split = nullptr;  // split range of each chunk (chunk k = persistent CTA k)
     int n_chunks = 0;
+    int attn_grid = 0;  // attention CTAs (chunks beyond the first attn_grid go by ticket)
     Split* d_splits;
 };
 
@@ -653,7 +670,7 @@ bool use_persist(const PhononCuda* c, int R, bool cancel) {
 // persistent kernel.
 int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vector<int32_t>& pos,
                  const std::vector<int32_t>& updates, Batch* out, bool device_prep = true, Lane* lane = nullptr,
-                 int32_t* status = nullptr, int plan_chunks = 0) {
+                 int32_t* status = nullptr, int plan_grid = 0) {
     if (!lane) lane = &c->lanes[0];
     if (!status) status = c->d_status;
     const int R = static_cast<int>(slot.size());
@@ -661,7 +678,6 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     for (int e = 0; e < R; ++e) total_pages += pos[e] / kPage + 1;
     int32_t* m = lane->h_meta;
     int32_t *h_slot = m, *h_pos = m + R, *h_first = m + 2 * R, *h_count = m + 3 * R;
-    Split* h_splits = reinterpret_cast<Split*>(m + 4 * R);
     int S = 0;
     for (int e = 0; e < R; ++e) {
         h_slot[e] = slot[e];
@@ -669,34 +685,66 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
         h_first[e] = 0;
         h_count[e] = 0;
     }
-    // Batches above PHONON_CUDA_FUSED_MAX_BATCH: runs of pps pages per split,
-    // one CTA each. Smaller batches (any path, so that the persistent and
-    // per-stage steps merge the same splits): the pages of all entries in
-    // (entry, page) order cut into at most one balanced chunk per SM (>=
-    // kPersistMinChunk pages); a chunk is one split per entry segment it
-    // covers, and chunk k's splits are [cta_split[k], cta_split[k+1]).
-    // Split plan: the pages of all entries in (entry, page) order are cut
-    // into at most `chunks` balanced chunks of at least kPersistMinChunk
-    // pages; a chunk is one split per entry segment it covers, so every
-    // entry's splits are consecutive and in page order, and chunk k's splits
-    // are [cta_split[k], cta_split[k+1]). One chunk per CTA: per SM up to 64
-    // entries (the persistent kernel's grid), two per SM above.
-    const int chunks_max = plan_chunks > 0 ? plan_chunks : (R <= PHONON_CUDA_FUSED_MAX_BATCH ? 1 : 2) * c->sms;
-    const long long chunks = std::max<long long>(1, std::min<long long>(chunks_max, total_pages / kPersistMinChunk));
-    const int G = std::max<int>(chunks_max, c->sms);  // table entries: at least one per SM of a persistent grid
-    std::vector<int32_t> cta_split(static_cast<size_t>(G) + 1, 0);
+    // Split plan: the pages of all entries, in (entry, page) order, are cut
+    // into chunks, and a chunk is one split per entry segment it covers, so
+    // every entry's splits are consecutive and in page order; chunk k's
+    // splits are [cta_split[k], cta_split[k+1]). Batches within the
+    // persistent window (on any path, so that the persistent and per-stage
+    // steps merge the same splits), and each half of a batch split over two
+    // lanes (plan_grid: a static chunk per CTA leaves the SMs a CTA finishes
+    // early with to the other lane's projections): at most `grid` balanced
+    // chunks of at least kPersistMinChunk pages, chunk k run by CTA k. Other
+    // batches: guided self-scheduling over two attention CTAs per SM, chunk
+    // sizes ceil(remaining / (kGuide * grid)) pages, at least
+    // kTicketMinChunk, the first `grid` chunks run by CTA k and the rest
+    // taken by ticket.
+    const bool guided = R > PHONON_CUDA_FUSED_MAX_BATCH && plan_grid == 0;
+    const int grid = plan_grid > 0 ? plan_grid : (guided ? 2 : 1) * c->sms;
+    std::vector<long long>& cuts = lane->h_cuts;
+    cuts.clear();
+    cuts.push_back(0);
+    if (!guided) {
+        const long long chunks = std::max<long long>(1, std::min<long long>(grid, total_pages / kPersistMinChunk));
+        for (long long k = 1; k <= chunks; ++k) cuts.push_back(k * total_pages / chunks);
+    } else {
+        long long done = 0;
+        const long long div = static_cast<long long>(kGuide) * grid;
+        while (done < total_pages) {
+            long long size = std::max<long long>((total_pages - done + div - 1) / div, kTicketMinChunk);
+            if (static_cast<int>(cuts.size()) >= kMaxChunks) size = total_pages - done;  // the last one takes the rest
+            done = std::min(total_pages, done + size);
+            cuts.push_back(done);
+        }
+    }
+    const int C = static_cast<int>(cuts.size()) - 1;
+    const int G = std::max(C, c->sms);  // chunk table entries: at least one per CTA of a persistent grid
+    // Metadata layout: slot, pos, first, count [R each], the plan header [8]
+    // (splits S, chunks C, offsets from the header of cta_split [G+1],
+    // cta_page [G+1] and the page ids [P] in split order), splits [4S], the
+    // two chunk tables, the page ids, then page updates [3U]. The kernels of
+    // a step read S, C and the tables through the header, so a replayed step
+    // graph depends on R alone; the page updates are applied outside graphs.
+    int32_t* hdr = m + 4 * R;
+    Split* h_splits = reinterpret_cast<Split*>(hdr + kPlanHeader);
+    const long long split_cap = c->max_splits;
+    std::vector<int32_t>& flat = lane->h_pages;
+    flat.clear();
     {
         long long done = 0;  // pages before entry e
         int e = 0, pb = 0;   // cursor: page pb of entry e
-        for (long long k = 0; k < chunks; ++k) {
-            cta_split[k] = S;
-            long long left = (k + 1) * total_pages / chunks - (done + pb);  // pages of chunk k
+        std::vector<int32_t>& first_split = lane->h_first_split;
+        first_split.resize(static_cast<size_t>(G) + 1);
+        for (int k = 0; k < C; ++k) {
+            first_split[k] = S;
+            long long left = cuts[k + 1] - (done + pb);  // pages of chunk k
             while (left > 0) {
                 const int n_pages = pos[e] / kPage + 1;
                 const int take = static_cast<int>(std::min<long long>(left, n_pages - pb));
-                if (S >= c->max_splits) return PHONON_CUDA_INVALID_ARGUMENT;
+                const std::vector<int32_t>& pages = c->streams[slot[e]].pages;
+                if (S >= split_cap || static_cast<int>(pages.size()) < pb + take) return PHONON_CUDA_INVALID_ARGUMENT;
                 if (h_count[e] == 0) h_first[e] = S;
                 h_splits[S++] = Split{e, pb, take, pos[e] + 1};
+                flat.insert(flat.end(), pages.begin() + pb, pages.begin() + pb + take);
                 h_count[e]++;
                 pb += take;
                 left -= take;
@@ -707,19 +755,27 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
                 }
             }
         }
-        for (long long k = chunks; k <= G; ++k) cta_split[k] = S;
+        for (int k = C; k <= G; ++k) first_split[k] = S;
     }
-    // Metadata layout: slot, pos, first, count [R each], splits [4S], the
-    // chunk table [G+1], page updates [3U]. Everything a step's kernels read
-    // sits at offsets fixed by (R, S, G), which a replayed step graph keeps;
-    // only the page updates (applied outside the graph) come after.
     const int U = static_cast<int>(updates.size() / 3);
-    int32_t* h_cta = m + 4 * R + 4 * S;
-    int32_t* h_upd = h_cta + G + 1;
-    if (4 * R + 4 * S + G + 1 + 3 * U > c->meta_ints) return PHONON_CUDA_INVALID_ARGUMENT;
-    std::memcpy(h_cta, cta_split.data(), cta_split.size() * 4);
-    std::memcpy(h_upd, updates.data(), updates.size() * 4);
-    const size_t bytes = static_cast<size_t>(4 * R + 4 * S + G + 1 + 3 * U) * 4;
+    const long long P = static_cast<long long>(flat.size());
+    const long long off_split_table = kPlanHeader + 4ll * S;
+    const long long off_page_table = off_split_table + G + 1;
+    const long long off_ids = off_page_table + G + 1;
+    const long long ints = 4ll * R + off_ids + P + 3ll * U;
+    if (ints > c->meta_ints) return PHONON_CUDA_INVALID_ARGUMENT;
+    hdr[0] = S;
+    hdr[1] = C;
+    hdr[2] = static_cast<int32_t>(off_split_table);
+    hdr[3] = static_cast<int32_t>(off_page_table);
+    hdr[4] = static_cast<int32_t>(off_ids);
+    hdr[5] = hdr[6] = hdr[7] = 0;
+    std::memcpy(hdr + off_split_table, lane->h_first_split.data(), static_cast<size_t>(G + 1) * 4);
+    int32_t* h_cta_page = hdr + off_page_table;
+    for (int k = 0; k <= G; ++k) h_cta_page[k] = static_cast<int32_t>(cuts[std::min(k, C)]);
+    std::memcpy(hdr + off_ids, flat.data(), flat.size() * 4);
+    std::memcpy(hdr + off_ids + P, updates.data(), updates.size() * 4);
+    const size_t bytes = static_cast<size_t>(ints) * 4;
     CUDA_TRY(cudaMemcpyAsync(lane->meta, lane->h_meta, bytes, cudaMemcpyHostToDevice, lane->stream));
     Batch b;
     b.lane = lane;
@@ -732,10 +788,12 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     b.d_pos = lane->meta + R;
     b.d_first = lane->meta + 2 * R;
     b.d_count = lane->meta + 3 * R;
-    b.d_splits = reinterpret_cast<Split*>(lane->meta + 4 * R);
-    b.d_cta_split = lane->meta + 4 * R + 4 * S;
-    b.d_updates = b.d_cta_split + G + 1;
-    b.n_chunks = static_cast<int>(chunks);
+    b.d_plan = lane->meta + 4 * R;
+    b.d_splits = reinterpret_cast<Split*>(b.d_plan + kPlanHeader);
+    b.d_cta_split = b.d_plan + off_split_table;
+    b.d_updates = b.d_plan + off_ids + P;
+    b.n_chunks = C;
+    b.attn_grid = guided ? grid : C;
     b.d_rope = lane->rope;
     b.persist = !device_prep;
     if (!device_prep) {
@@ -744,10 +802,12 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     }
     {
         LaunchScope ls(c, PHONON_CUDA_K_OTHER, R * 32 * 12.0 + U * 12.0, b.lane->stream);
-        const int threads = std::max(R * 32, U);
+        const int n_ctr = static_cast<int>(c->cfg.n_layers);
+        const int threads = std::max({R * 32, U, n_ctr});
         CUDA_TRY(launch_pdl(step_prep_kernel, dim3((threads + 255) / 256), dim3(256), 0, lane->stream,
                             static_cast<const int32_t*>(b.d_pos), static_cast<const float*>(c->d_freq), R, b.d_rope,
-                            c->d_table, kMaxPagesPerStream, static_cast<const int32_t*>(b.d_updates), U));
+                            c->d_table, kMaxPagesPerStream, static_cast<const int32_t*>(b.d_updates), U,
+                            lane->chunk_ctr, n_ctr));
     }
     *out = b;
     return PHONON_CUDA_OK;
@@ -768,7 +828,8 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out, boo
     ap.q = b.lane->q;
     ap.slot = b.d_slot;
     ap.splits = b.d_splits;
-    ap.cta_split = b.d_cta_split;
+    ap.plan = b.d_plan;
+    ap.chunk_ctr = b.lane->chunk_ctr + l;
     ap.n_splits = b.S;
     ap.kv = kv;
     ap.layer = l;
@@ -780,8 +841,8 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out, boo
         LaunchScope ls(c, PHONON_CUDA_K_ATTENTION,
                        b.keys * 2.0 * kWidth * esize + act * kWidth + b.S * kHeads * kPartStride * 4.0, b.lane->stream);
         if (c->attn_tma) {
-            CUDA_TRY(kv.bf16 ? launch_attn_tma<true>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.n_chunks, s)
-                             : launch_attn_tma<false>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.n_chunks, s));
+            CUDA_TRY(kv.bf16 ? launch_attn_tma<true>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.attn_grid, s)
+                             : launch_attn_tma<false>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.attn_grid, s));
         } else {
             CUDA_TRY(kv.bf16 ? launch_pdl(attn_partial_kernel<true>, dim3(grid), dim3(kAttnWarps * 32), 0, s, ap)
                              : launch_pdl(attn_partial_kernel<false>, dim3(grid), dim3(kAttnWarps * 32), 0, s, ap));
@@ -1016,8 +1077,10 @@ int enqueue_layers_direct(PhononCuda* c, const Batch& b, const float* in, float*
 int enqueue_layers_graphed(PhononCuda* c, const Batch& b, const float* in, float* final_out) {
     PhononCuda::StepShape shape;
     shape.R = b.R;
-    shape.S = b.S;
-    shape.chunks = b.n_chunks;
+    // Kernels read S and the chunk tables through the plan header; the TMA
+    // attention grid is fixed except for small (static) plans.
+    shape.S = c->attn_tma ? 0 : b.S;
+    shape.chunks = b.attn_grid;
     shape.in = in;
     shape.out = final_out;
     if (c->graph_exec && c->graph_shape == shape) {
@@ -1177,14 +1240,14 @@ int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::v
     }
     const int n0 = n / 2;
     Lane& L1 = c->lanes[1];
-    const int chunks = c->sms;  // one attention CTA per SM per half: each half's attention leaves SMs to the other
+    const int grid = c->sms;  // one attention CTA per SM per half: each half's attention leaves SMs to the other
     const std::vector<int32_t> s0(slot.begin(), slot.begin() + n0), p0(pos.begin(), pos.begin() + n0);
     const std::vector<int32_t> s1(slot.begin() + n0, slot.end()), p1(pos.begin() + n0, pos.end());
     Batch b0, b1;
-    if ((st = upload_batch(c, s0, p0, updates, &b0, true, &c->lanes[0], c->d_status, chunks))) return st;
+    if ((st = upload_batch(c, s0, p0, updates, &b0, true, &c->lanes[0], c->d_status, grid))) return st;
     CUDA_TRY(cudaEventRecord(c->fork, c->stream));  // page updates and everything before this step
     CUDA_TRY(cudaStreamWaitEvent(L1.stream, c->fork, 0));
-    if ((st = upload_batch(c, s1, p1, {}, &b1, true, &L1, c->d_status + n0, chunks))) return st;
+    if ((st = upload_batch(c, s1, p1, {}, &b1, true, &L1, c->d_status + n0, grid))) return st;
     b0.split = b1.split = true;
     if ((st = enqueue_stack(c, b0, in, out, nullptr, nullptr, nullptr, cancelled))) return st;
     if ((st = enqueue_stack(c, b1, in + static_cast<size_t>(n0) * kWidth, out + static_cast<size_t>(n0) * kWidth,
@@ -1252,7 +1315,8 @@ void destroy_context(PhononCuda* c) {
     {
         Lane& L1 = c->lanes[1];
         if (L1.stream) cudaStreamSynchronize(L1.stream);
-        void* dev1[] = {L1.x0, L1.x1, L1.q, L1.a, L1.h, L1.g, L1.part, L1.meta, L1.dig512, L1.dig2048, L1.exps, L1.rope};
+        void* dev1[] = {L1.x0, L1.x1, L1.q, L1.a, L1.h, L1.g, L1.part, L1.meta, L1.dig512, L1.dig2048, L1.exps, L1.rope,
+                        L1.chunk_ctr, c->lanes[0].chunk_ctr};
         for (void* p : dev1)
             if (p) cudaFree(p);
         if (L1.h_meta) cudaFreeHost(L1.h_meta);
@@ -1333,9 +1397,13 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
     const size_t esize = cfg.kv_type == PHONON_CUDA_KV_BF16 ? 2 : 4;
     c->page_elems = static_cast<long long>(cfg.n_layers) * 2 * kHeads * kPage * kHeadDim;
     c->cap_rows = static_cast<int>(std::max<uint32_t>(cfg.max_batch, kPrefillChunk));
-    c->max_splits = 2 * kMaxSms + c->cap_rows + 16;  // at most one split per (chunk, entry) boundary
+    c->max_splits = kMaxChunks + c->cap_rows + 16;  // at most one split per (chunk, entry) boundary
     const int U_max = c->cap_rows * 2 + kMaxPagesPerStream + 16;
-    c->meta_ints = 4 * c->cap_rows + 4 * c->max_splits + 3 * U_max + 2 * kMaxSms + 1;
+    // page ids of a batch: every page of its streams, at most the pool
+    const long long batch_pages = std::min<long long>(static_cast<long long>(c->cap_rows) * kMaxPagesPerStream,
+                                                      cfg.pool_pages);
+    c->meta_ints = static_cast<int>(4 * c->cap_rows + kPlanHeader + 4 * c->max_splits +
+                                    2 * (std::max(kMaxChunks, kMaxSms) + 1) + batch_pages + 3 * U_max);
     const size_t rows = static_cast<size_t>(c->cap_rows);
     bool ok = cudaMalloc(&c->kv_pool, static_cast<size_t>(cfg.pool_pages) * c->page_elems * esize) == cudaSuccess &&
               cudaMalloc(&c->d_table, static_cast<size_t>(cfg.max_streams) * kMaxPagesPerStream * 4) == cudaSuccess &&
@@ -1381,6 +1449,9 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
         L0.tm_dig512 = c->tm_dig512;
         L0.tm_dig2048 = c->tm_dig2048;
         L0.rope = c->d_rope;
+        const size_t ctr_bytes = static_cast<size_t>(cfg.n_layers) * 4;
+        if (cudaMalloc(&L0.chunk_ctr, ctr_bytes) != cudaSuccess || cudaMemset(L0.chunk_ctr, 0, ctr_bytes) != cudaSuccess)
+            return fail(PHONON_CUDA_OUT_OF_MEMORY);
         if (cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming) != cudaSuccess)
             return fail(PHONON_CUDA_DEVICE_ERROR);
@@ -1398,7 +1469,9 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
                 cudaMalloc(&L1.dig512, rows_pad * kDigits * 512) == cudaSuccess &&
                 cudaMalloc(&L1.dig2048, rows_pad * kDigits * 2048) == cudaSuccess &&
                 cudaMalloc(&L1.exps, rows_pad * 4) == cudaSuccess &&
-                cudaMalloc(&L1.rope, rows * 32 * sizeof(float2)) == cudaSuccess;
+                cudaMalloc(&L1.rope, rows * 32 * sizeof(float2)) == cudaSuccess &&
+                cudaMalloc(&L1.chunk_ctr, ctr_bytes) == cudaSuccess &&
+                cudaMemset(L1.chunk_ctr, 0, ctr_bytes) == cudaSuccess;
             if (!ok1) return fail(PHONON_CUDA_OUT_OF_MEMORY);
             c->lane1_ok = c->tensor_ok && make_i8_map(&L1.tm_dig512, L1.dig512, rows_pad * kDigits, 512) &&
                           make_i8_map(&L1.tm_dig2048, L1.dig2048, rows_pad * kDigits, 2048);

@@ -12,10 +12,10 @@
 // epilogue recombines y = s_r * sum_j D[r][4b+j] * 2^(e_b - 7(j+1)).
 //
 // Kernel shape: one CTA per 128-row x 32-stream tile (M = 128, N = 128 digit
-// rows), 6 warps: warp 0 issues TMA tile loads (no multicast), warp 1 owns
-// the TMEM accumulator and issues tcgen05.mma, warps 2-5 drain TMEM in the
-// epilogue. K is staged in 128-byte tiles (SWIZZLE_128B) through a 4-deep
-// mbarrier ring. Every mbarrier wait is bounded: on expiry the CTA raises the
+// rows), 10 warps: warp 0 issues TMA tile loads (no multicast), warp 1 owns
+// the TMEM accumulator and issues tcgen05.mma, warps 2-9 drain TMEM in the
+// epilogue (two warps per 32-lane quarter, each half of the columns). K is
+// staged in 128-byte tiles (SWIZZLE_128B) through a 3-deep mbarrier ring. Every mbarrier wait is bounded: on expiry the CTA raises the
 // context's error flag, skips its remaining work and still frees its TMEM.
 #pragma once
 
@@ -31,7 +31,8 @@ constexpr int kGemmM = 128;       // weight rows per tile (MMA M)
 constexpr int kGemmN = 128;       // digit rows per tile (MMA N) = 32 streams x 4 slices
 constexpr int kGemmKTile = 128;   // bytes of K per stage
 constexpr int kGemmStages = 3;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;  // producer, MMA issuer, 8 epilogue warps
+constexpr int kGemmEpiThreads = kGemmThreads - 64;
 constexpr int kGemmStreamsPerTile = kGemmN / 4;
 constexpr int kDigits = 4;
 // Per-tile stream data staged by the epilogue warps (exponents, pages, RoPE).
@@ -45,6 +46,29 @@ constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmM + kGemmN) * kGemmKTile + 
 constexpr long long kWaitBudgetCycles = 4ll << 30;  // ~2 s at 1.9 GHz
 
 enum GemmEpilogue : int { GEPI_RAW = 0, GEPI_RESID = 1, GEPI_GELU = 2, GEPI_QKV = 3, GEPI_STORE = 4 };
+
+// Phase timestamps for profiling builds (-DPHONON_GEMM_TRACE): one thread per
+// role writes %globaltimer into g_gemm_trace[(cta * 8) + slot] for launches
+// whose epilogue kind equals g_gemm_trace_kind (the last such launch wins;
+// CTAs past kGemmTraceCtas write nothing). Empty otherwise.
+#ifdef PHONON_GEMM_TRACE
+constexpr unsigned kGemmTraceCtas = 4096;
+__device__ unsigned long long* g_gemm_trace;
+__device__ int g_gemm_trace_kind;
+#define GEMM_MARK(slot)                                                                  \
+    do {                                                                                \
+        const unsigned cta_ = blockIdx.y * gridDim.x + blockIdx.x;                      \
+        if (g_gemm_trace && g_gemm_trace_kind == kEpi && cta_ < kGemmTraceCtas) {       \
+            unsigned long long t_;                                                      \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                      \
+            g_gemm_trace[static_cast<size_t>(cta_) * 8 + (slot)] = t_;                  \
+        }                                                                               \
+    } while (0)
+#else
+#define GEMM_MARK(slot) \
+    do {                \
+    } while (0)
+#endif
 
 struct GemmParams {
     int rows;              // weight rows (M)
@@ -120,6 +144,23 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+// L2 policy for data read once per step (K/V pages): evict first, so that
+// the stream does not push weights, metadata and activations out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "l"(policy)
         : "memory");
 }
 
@@ -210,6 +251,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) GEMM_MARK(0);  // set up (barriers, TMEM)
 
     if (warp == 0 && lane == 0) {
         // TMA producer: weight tile rows [m_tile*128, +128), digit rows [n_tile*128, +128).
@@ -222,6 +264,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
                         full0 + 8 * kt);
         }
         pdl_wait();
+        GEMM_MARK(1);  // previous launch complete
         for (int kt = 0; kt < nk; ++kt) {
             const int s = kt % kGemmStages;
             if (kt >= pre) {
@@ -243,6 +286,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
                 ok = false;
                 break;
             }
+            if (kt == 0) GEMM_MARK(2);  // first stage landed
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t a0 = smem_addr(sA + s * kGemmM * kGemmKTile);
             const uint32_t b0 = smem_addr(sB + s * kGemmN * kGemmKTile);
@@ -253,14 +297,19 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
             umma_commit(empty0 + 8 * s);
         }
         if (ok) umma_commit(accum);
+        GEMM_MARK(3);  // all MMAs issued
     } else if (warp >= 2) {
-        // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows.
-        // While the MMAs run, stage this tile's per-stream data in shared
-        // memory and prefetch the residual, so that draining the accumulator
-        // issues no dependent global loads.
+        // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = weight rows;
+        // warps 2-5 drain accumulator columns 0-63 (streams 0-15 of the
+        // tile), warps 6-9 columns 64-127 (streams 16-31). While the MMAs
+        // run, stage this tile's per-stream data in shared memory and
+        // prefetch the residual, so that draining the accumulator issues no
+        // dependent global loads.
+        constexpr int kHalf = kGemmStreamsPerTile / 2;
         const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int r = m_tile * kGemmM + quarter * 32 + lane;
-        const int et = threadIdx.x - 64;  // 0..127 over the epilogue warps
+        const int et = threadIdx.x - 64;  // 0..255 over the epilogue warps
         const int b0 = n_tile * kGemmStreamsPerTile;
         pdl_wait();  // exponents, residuals and positions come from earlier kernels
         if constexpr (kEpi != GEPI_RAW) {
@@ -275,26 +324,40 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
                 }
             }
             if constexpr (kEpi == GEPI_QKV) {
-                for (int i = et; i < kGemmStreamsPerTile * 32; i += 128) {
+                constexpr int kPer = kGemmStreamsPerTile * 32 / kGemmEpiThreads;
+                float2 cs[kPer];
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) {  // independent loads, then the stores
+                    const int i = et + k * kGemmEpiThreads;
                     const int b = b0 + i / 32;
-                    meta->cs[i / 32][i % 32] = b < p.B ? p.rope[b * 32 + (i % 32)] : make_float2(1.0f, 0.0f);
+                    cs[k] = b < p.B ? p.rope[b * 32 + (i % 32)] : make_float2(1.0f, 0.0f);
+                }
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) {
+                    const int i = et + k * kGemmEpiThreads;
+                    meta->cs[i / 32][i % 32] = cs[k];
                 }
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync 1, %0;" ::"n"(kGemmEpiThreads) : "memory");
         }
-        float res[kGemmStreamsPerTile];
+        float res[kHalf];
         if constexpr (kEpi == GEPI_RESID) {
 #pragma unroll
-            for (int t = 0; t < kGemmStreamsPerTile; ++t)
-                res[t] = (b0 + t < p.B && r < p.rows) ? p.res[static_cast<size_t>(b0 + t) * p.ldres + r] : 0.0f;
+            for (int t = 0; t < kHalf; ++t) {
+                const int b = b0 + half * kHalf + t;
+                res[t] = (b < p.B && r < p.rows) ? p.res[static_cast<size_t>(b) * p.ldres + r] : 0.0f;
+            }
         }
         const float scale = (kEpi == GEPI_RAW || r >= p.rows) ? 1.0f : p.row_scale[r];
+        if (et == 0) GEMM_MARK(4);  // epilogue staged, waiting for the accumulator
         const bool have = __all_sync(kFull, mbar_wait(accum, 0, p.error, failed));
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (et == 0) GEMM_MARK(5);  // accumulator ready
         pdl_trigger();
         if (have) {
 #pragma unroll
-            for (int c0 = 0; c0 < kGemmN; c0 += 32) {
+            for (int h = 0; h < 2; ++h) {
+                const int c0 = half * (kGemmN / 2) + h * 32;
                 uint32_t d[32];
                 tmem_load32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c0, d);
                 if constexpr (kEpi == GEPI_RAW) {
@@ -303,61 +366,80 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
                             const int n = n_tile * kGemmN + c0 + i;
                             if (n < p.n_total) p.raw[static_cast<size_t>(r) * p.n_total + n] = static_cast<int32_t>(d[i]);
                         }
-                    continue;
-                }
-                // 8 streams per 32 columns: recombine the four digit slices.
+                } else {
+                    // 8 streams per 32 columns: recombine the four digit slices.
+                    // Values of padded streams and rows are computed (from zero
+                    // digits) and not stored, keeping the 8 chains branch-free.
+                    float v[8];
 #pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const int tt = (c0 >> 2) + t;  // stream within the tile
-                    const int b = b0 + tt;
-                    const bool live = b < p.B;
-                    const int e = meta->exp[tt];
-                    float v = 0.0f;
+                    for (int t = 0; t < 8; ++t) {
+                        const int e = meta->exp[(c0 >> 2) + t];
+                        float acc = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < kDigits; ++j)
-                        v = fmaf(static_cast<float>(static_cast<int32_t>(d[4 * t + j])), pow2f(e - 7 * (j + 1)), v);
-                    v *= scale;
+                        for (int j = 0; j < kDigits; ++j)
+                            acc = fmaf(static_cast<float>(static_cast<int32_t>(d[4 * t + j])), pow2f(e - 7 * (j + 1)), acc);
+                        v[t] = acc * scale;
+                    }
                     if constexpr (kEpi == GEPI_QKV) {
-                        // rows r (even lane) and r+1 (odd lane) form a RoPE pair
-                        const float other = __shfl_xor_sync(kFull, v, 1);
-                        if (!live || r >= p.rows) continue;
                         const int region = r >> 9, within = r & 511;
-                        float a = (lane & 1) ? other : v, bb = (lane & 1) ? v : other;
-                        if (region < 2) rope_apply(a, bb, meta->cs[tt][(within & 63) >> 1]);
-                        const float mine = (lane & 1) ? bb : a;
-                        if (!isfinite(mine)) flag_nonfinite(p.status, b);
-                        if (region == 0) {
-                            p.q[static_cast<size_t>(b) * kWidth + within] = mine;
-                        } else {
-                            const int position = meta->pos[tt];
-                            const long long off = kv_offset(p.kv, meta->page[tt], p.layer, region - 1, within >> 6,
-                                                            position % kPage) + (within & 63);
-                            if (p.kv.bf16) static_cast<uint16_t*>(p.kv.pool)[off] = f32_to_bf16(mine);
-                            else static_cast<float*>(p.kv.pool)[off] = mine;
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) {
+                            // rows r (even lane) and r+1 (odd lane) form a RoPE pair
+                            const int tt = (c0 >> 2) + t;
+                            const float other = __shfl_xor_sync(kFull, v[t], 1);
+                            float a = (lane & 1) ? other : v[t], bb = (lane & 1) ? v[t] : other;
+                            if (region < 2) rope_apply(a, bb, meta->cs[tt][(within & 63) >> 1]);
+                            v[t] = (lane & 1) ? bb : a;
+                        }
+                        if (r < p.rows) {
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) {
+                                const int tt = (c0 >> 2) + t;
+                                const int b = b0 + tt;
+                                if (b >= p.B) break;
+                                if (!isfinite(v[t])) flag_nonfinite(p.status, b);
+                                if (region == 0) {
+                                    p.q[static_cast<size_t>(b) * kWidth + within] = v[t];
+                                } else {
+                                    const long long off = kv_offset(p.kv, meta->page[tt], p.layer, region - 1, within >> 6,
+                                                                    meta->pos[tt] % kPage) + (within & 63);
+                                    if (p.kv.bf16) static_cast<uint16_t*>(p.kv.pool)[off] = f32_to_bf16(v[t]);
+                                    else static_cast<float*>(p.kv.pool)[off] = v[t];
+                                }
+                            }
                         }
                     } else {
-                        if (!live || r >= p.rows) continue;
-                        if constexpr (kEpi == GEPI_RESID) v = __fadd_rn(res[tt], v);
-                        if constexpr (kEpi == GEPI_STORE) {
-                            if (p.bias) v = __fadd_rn(v, p.bias[r]);
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) {
+                            if constexpr (kEpi == GEPI_RESID) v[t] = __fadd_rn(res[h * 8 + t], v[t]);
+                            if constexpr (kEpi == GEPI_STORE) {
+                                if (p.bias && r < p.rows) v[t] = __fadd_rn(v[t], p.bias[r]);
+                            }
+                            if constexpr (kEpi == GEPI_GELU) v[t] = gelu_erf(v[t]);
                         }
-                        if constexpr (kEpi == GEPI_GELU) {
-                            if (!isfinite(v)) flag_nonfinite(p.status, b);
-                            v = gelu_erf(v);
+                        if (r < p.rows) {
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) {
+                                const int b = b0 + (c0 >> 2) + t;
+                                if (b >= p.B) break;
+                                // GELU keeps non-finite inputs non-finite, so the check after it also covers them
+                                if (!isfinite(v[t])) flag_nonfinite(p.status, b);
+                                p.y[static_cast<size_t>(b) * p.ldy + r] = v[t];
+                            }
                         }
-                        if (!isfinite(v)) flag_nonfinite(p.status, b);
-                        p.y[static_cast<size_t>(b) * p.ldy + r] = v;
                     }
                 }
             }
         }
     }
+    if (threadIdx.x == 64) GEMM_MARK(6);  // first epilogue warp done
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmN) : "memory");
     }
+    if (threadIdx.x == 0) GEMM_MARK(7);  // CTA end
 }
 
 // Exponent e of a row whose largest magnitude is mx: |x| * 2^-e < 1/2.
@@ -384,10 +466,78 @@ __device__ __forceinline__ uint32_t slice_digits(float r) {
     return packed;
 }
 
-// Attention combine fused with digit slicing (tensor-core path): one CTA per
-// stream (8 warps = 8 heads) merges the head's splits like attn_combine_kernel,
-// then the CTA takes the row maximum over all 512 outputs and writes the
-// stream's four digit rows and exponent. CTAs for padded streams write zeros.
+// One head's share of the split merge of a stream (warp = head): the
+// stream's splits folded in page order like attn_combine_kernel; lane l holds
+// output dims 2l, 2l+1. ok: finite, with a positive sum. Loads go to L2 (the
+// partials may have been written by other SMs).
+struct HeadMerge {
+    float o0, o1;
+    bool ok;
+};
+
+__device__ __forceinline__ HeadMerge merge_head(const float* part, int first, int n, int head, int lane) {
+    constexpr int kBatch = 8;  // splits whose loads are in flight together
+    float M = -INFINITY, total = 0.0f, a0 = 0.0f, a1 = 0.0f;
+    for (int s0 = 0; s0 < n; s0 += kBatch) {
+        float pm[kBatch], pl[kBatch];
+        float2 av[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            if (s0 + j < n) {
+                const float* pp = part + (static_cast<size_t>(first + s0 + j) * kHeads + head) * kPartStride;
+                pm[j] = __ldcg(pp);
+                pl[j] = __ldcg(pp + 1);
+                av[j] = __ldcg(reinterpret_cast<const float2*>(pp + 2 + 2 * lane));
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            if (s0 + j < n) {
+                const MergeWeights w = merge_weights(M, pm[j]);
+                total = merge_fold(total, w, pl[j]);
+                a0 = merge_fold(a0, w, av[j].x);
+                a1 = merge_fold(a1, w, av[j].y);
+            }
+        }
+    }
+    HeadMerge h;
+    h.ok = total > 0.0f && isfinite(total);
+    const float inv = __fdiv_rn(1.0f, total);
+    h.o0 = __fmul_rn(a0, inv);
+    h.o1 = __fmul_rn(a1, inv);
+    h.ok &= isfinite(h.o0) && isfinite(h.o1);
+    return h;
+}
+
+// Largest output magnitude of the head over the warp (0 for lanes not ok).
+__device__ __forceinline__ float head_abs_max(const HeadMerge& h) {
+    float m = h.ok ? fmaxf(fabsf(h.o0), fabsf(h.o1)) : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+    return m;
+}
+
+// The head's two dims per lane of the stream's four digit rows (drow points
+// at row 4b, dim head*64 + 2*lane), for a row whose largest magnitude is
+// row_max; returns the row exponent e_b.
+__device__ __forceinline__ int write_head_digits(const HeadMerge& h, float row_max, int8_t* drow) {
+    bool zero;
+    const int e = digit_exponent(row_max, zero);
+    const float down = pow2f(-e);
+    const uint32_t d0 = (zero || !h.ok) ? 0u : slice_digits(h.o0 * down);
+    const uint32_t d1 = (zero || !h.ok) ? 0u : slice_digits(h.o1 * down);
+#pragma unroll
+    for (int j = 0; j < kDigits; ++j)
+        *reinterpret_cast<uint16_t*>(drow + j * kWidth) =
+            static_cast<uint16_t>(((d0 >> (8 * j)) & 0xffu) | (((d1 >> (8 * j)) & 0xffu) << 8));
+    return e;
+}
+
+// Attention combine fused with digit slicing (tensor-core path when attention
+// runs without the TMA page ring): one CTA per stream (8 warps = 8 heads)
+// merges the head's splits like attn_combine_kernel, then the CTA takes the
+// row maximum over all 512 outputs and writes the stream's four digit rows
+// and exponent. CTAs for padded streams write zeros.
 __global__ void __launch_bounds__(256) attn_combine_digits_kernel(CombineParams p, int Bpad, int8_t* __restrict__ digits,
                                                                   int32_t* __restrict__ exps) {
     __shared__ float head_max[kHeads];
@@ -402,50 +552,27 @@ __global__ void __launch_bounds__(256) attn_combine_digits_kernel(CombineParams 
         if (threadIdx.x == 0) exps[b] = 0;
         return;
     }
-    const int first = p.first[b], n = p.count[b];
-    float M = -INFINITY, total = 0.0f, a0 = 0.0f, a1 = 0.0f;
-    for (int s = 0; s < n; ++s) {
-        const float* pp = p.part + (static_cast<size_t>(first + s) * kHeads + head) * kPartStride;
-        const MergeWeights w = merge_weights(M, pp[0]);
-        total = merge_fold(total, w, pp[1]);
-        const float2 av = *reinterpret_cast<const float2*>(pp + 2 + 2 * lane);
-        a0 = merge_fold(a0, w, av.x);
-        a1 = merge_fold(a1, w, av.y);
-    }
-    bool ok = total > 0.0f && isfinite(total);
-    const float inv = __fdiv_rn(1.0f, total);
-    const float o0 = __fmul_rn(a0, inv), o1 = __fmul_rn(a1, inv);
-    ok &= isfinite(o0) && isfinite(o1);
-    if (!__all_sync(kFull, ok) && lane == 0) flag_nonfinite(p.status, b);
-    float m = ok ? fmaxf(fabsf(o0), fabsf(o1)) : 0.0f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+    const HeadMerge h = merge_head(p.part, p.first[b], p.count[b], head, lane);
+    if (!__all_sync(kFull, h.ok) && lane == 0) flag_nonfinite(p.status, b);
+    const float m = head_abs_max(h);
     if (lane == 0) head_max[head] = m;
     __syncthreads();
     float row_max = 0.0f;
 #pragma unroll
-    for (int h = 0; h < kHeads; ++h) row_max = fmaxf(row_max, head_max[h]);
-    bool zero;
-    const int e = digit_exponent(row_max, zero);
-    const float down = pow2f(-e);
-    const uint32_t d0 = (zero || !ok) ? 0u : slice_digits(o0 * down);
-    const uint32_t d1 = (zero || !ok) ? 0u : slice_digits(o1 * down);
-#pragma unroll
-    for (int j = 0; j < kDigits; ++j)
-        *reinterpret_cast<uint16_t*>(drow + j * kWidth) =
-            static_cast<uint16_t>(((d0 >> (8 * j)) & 0xffu) | (((d1 >> (8 * j)) & 0xffu) << 8));
+    for (int hh = 0; hh < kHeads; ++hh) row_max = fmaxf(row_max, head_max[hh]);
+    const int e = write_head_digits(h, row_max, drow);
     if (threadIdx.x == 0) exps[b] = e;
 }
 
-// Digit slicing (see the header comment). One warp per stream row of width
-// kCols; with kLN the row is first layer-normalised exactly as in
-// warp_layernorm512. Writes digit rows 4b..4b+3 and e_b; rows of streams
-// B..Bpad-1 are zeroed so that padded tiles multiply zeros.
-template <int kCols, bool kLN>
-__global__ void __launch_bounds__(256) digits_kernel(const float* __restrict__ x, int ldx, const float* ln_w,
-                                                     const float* ln_b, int B, int Bpad, int8_t* __restrict__ digits,
-                                                     int32_t* __restrict__ exps, int32_t* status) {
-    __shared__ __align__(16) float row[8][kLN ? kCols : 1];
+// LayerNorm then digit slicing (see the header comment), one warp per stream
+// row of 512: the row is layer-normalised exactly as in warp_layernorm512,
+// then sliced. Writes digit rows 4b..4b+3 and e_b; rows of streams B..Bpad-1
+// are zeroed so that padded tiles multiply zeros.
+__global__ void __launch_bounds__(256) ln_digits_kernel(const float* __restrict__ x, int ldx, const float* ln_w,
+                                                        const float* ln_b, int B, int Bpad, int8_t* __restrict__ digits,
+                                                        int32_t* __restrict__ exps, int32_t* status) {
+    constexpr int kCols = kWidth;
+    __shared__ __align__(16) float row[8][kCols];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
     pdl_trigger();
@@ -459,13 +586,10 @@ __global__ void __launch_bounds__(256) digits_kernel(const float* __restrict__ x
         if (lane == 0) exps[b] = 0;
         return;
     }
-    const float* src = x + static_cast<size_t>(b) * ldx;
-    if constexpr (kLN) {
-        const bool ok = warp_layernorm512(src, ln_w, ln_b, row[warp]);
-        if (!ok && lane == 0) flag_nonfinite(status, b);
-        __syncwarp();
-        src = row[warp];
-    }
+    const bool ok = warp_layernorm512(x + static_cast<size_t>(b) * ldx, ln_w, ln_b, row[warp]);
+    if (!ok && lane == 0) flag_nonfinite(status, b);
+    __syncwarp();
+    const float* src = row[warp];
     // lane owns columns lane*4 + 128*i .. +3 (i < per_lane/4): float4 reads
     float v[per_lane];
 #pragma unroll
@@ -511,6 +635,86 @@ __global__ void __launch_bounds__(256) digits_kernel(const float* __restrict__ x
             *reinterpret_cast<uint32_t*>(digits + static_cast<size_t>(4 * b + j) * kCols + i * 128 + lane * 4) =
                 packed[j][i];
     if (lane == 0) exps[b] = e;
+}
+
+// Digit slicing of rows of width kCols (no LayerNorm): kCols/8 threads per
+// stream row, 8 consecutive columns each, the row maximum reduced across the
+// row's warps through shared memory. A row holding a non-finite value is
+// flagged and gets all-zero digits and e_b = 0, as do the padded rows
+// B..Bpad-1.
+template <int kCols>
+__global__ void __launch_bounds__(256) digits_kernel(const float* __restrict__ x, int ldx, int B, int Bpad,
+                                                     int8_t* __restrict__ digits, int32_t* __restrict__ exps,
+                                                     int32_t* status) {
+    constexpr int kRowThreads = kCols / 8;
+    constexpr int kRows = 256 / kRowThreads;  // stream rows per CTA
+    constexpr int kRowWarps = kRowThreads / 32;
+    static_assert(kRowWarps >= 1 && kRows * kRowThreads == 256, "kCols must be 256..2048");
+    __shared__ float warp_max[8];
+    __shared__ int warp_bad[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rt = threadIdx.x % kRowThreads;
+    const int b = blockIdx.x * kRows + threadIdx.x / kRowThreads;
+    pdl_wait();
+    pdl_trigger();
+    float v[8];
+    if (b < B) {
+        const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * ldx + rt * 8);
+        const float4 f0 = src[0], f1 = src[1];
+        v[0] = f0.x, v[1] = f0.y, v[2] = f0.z, v[3] = f0.w;
+        v[4] = f1.x, v[5] = f1.y, v[6] = f1.z, v[7] = f1.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    float mx = 0.0f;
+    bool finite_ok = true;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        finite_ok &= isfinite(v[i]);
+        mx = fmaxf(mx, fabsf(v[i]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    finite_ok = __all_sync(kFull, finite_ok);
+    if (lane == 0) {
+        warp_max[warp] = mx;
+        warp_bad[warp] = !finite_ok;
+    }
+    __syncthreads();
+    const int w0 = (threadIdx.x / kRowThreads) * kRowWarps;
+    bool bad = false;
+#pragma unroll
+    for (int w = 0; w < kRowWarps; ++w) {
+        mx = fmaxf(mx, warp_max[w0 + w]);
+        bad |= warp_bad[w0 + w] != 0;
+    }
+    if (b >= Bpad) return;
+    if (bad) {
+        if (rt == 0) flag_nonfinite(status, b);
+        mx = 0.0f;
+    }
+    bool zero;
+    const int e = digit_exponent(mx, zero);
+    const float down = pow2f(-e);
+    uint32_t lo[kDigits], hi[kDigits];
+#pragma unroll
+    for (int j = 0; j < kDigits; ++j) lo[j] = hi[j] = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        // exact scaling by a power of two, then the four digits
+        const uint32_t d = zero ? 0u : slice_digits(v[i] * down);
+#pragma unroll
+        for (int j = 0; j < kDigits; ++j) {
+            const uint32_t byte = ((d >> (8 * j)) & 0xffu) << (8 * (i % 4));
+            if (i < 4) lo[j] |= byte;
+            else hi[j] |= byte;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kDigits; ++j)
+        *reinterpret_cast<uint2*>(digits + static_cast<size_t>(4 * b + j) * kCols + rt * 8) = make_uint2(lo[j], hi[j]);
+    if (rt == 0) exps[b] = e;
 }
 
 }  // namespace phonon

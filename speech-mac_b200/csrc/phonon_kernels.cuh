@@ -258,10 +258,11 @@ __device__ __forceinline__ void rope_apply(float& a, float& b, float2 cs) {
 // pos[e] * freq[i] for the 32 frequencies of a 64-wide head (every layer of
 // the step reuses it).
 __global__ void step_prep_kernel(const int32_t* pos, const float* freq, int R, float2* cs, int32_t* table,
-                                 int max_pages, const int32_t* updates, int U) {
+                                 int max_pages, const int32_t* updates, int U, int32_t* counters, int n_counters) {
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n_counters) counters[t] = 0;
     if (t < U) table[static_cast<size_t>(updates[3 * t]) * max_pages + updates[3 * t + 1]] = updates[3 * t + 2];
     if (t >= R * 32) return;
     const float phase = __fmul_rn(static_cast<float>(pos[t >> 5]), freq[t & 31]);
@@ -592,7 +593,12 @@ struct AttnParams {
     const float* q;        // [B][512] RoPE'd queries
     const int32_t* slot;   // [B]
     const Split* splits;   // [S]
-    const int32_t* cta_split;  // TMA kernel: [grid + 1] split range of each CTA, or null (one split per CTA)
+    // TMA kernel: the step's plan header, [0] splits, [1] chunks C, then the
+    // offsets (in ints, from the header) of [2] cta_split and [3] cta_page
+    // (first split and first page of each chunk, at least C + 1 entries) and
+    // [4] the page ids of all splits in split order
+    const int32_t* plan;
+    int32_t* chunk_ctr;    // TMA kernel: chunk tickets of this launch (zeroed at step start)
     int n_splits;
     KvView kv;
     int layer;

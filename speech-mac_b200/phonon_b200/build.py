@@ -33,7 +33,7 @@ def _stale(target, sources):
 
 def build_cuda(force=False):
     out = PKG / "libphonon_cuda.so"
-    srcs = [CSRC / "phonon_cuda.cu", CSRC / "phonon_kernels.cuh", INCLUDE / "phonon_cuda.h"]
+    srcs = [CSRC / "phonon_cuda.cu", *sorted(CSRC.glob("*.cuh")), INCLUDE / "phonon_cuda.h"]
     if force or _stale(out, srcs):
         _run([NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-Wall", f"-I{INCLUDE}", "-shared", "-o", str(out),
