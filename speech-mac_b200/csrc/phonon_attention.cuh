@@ -11,8 +11,10 @@
 // into a ring of shared-memory stages that runs on across splits and
 // chunks, tagging each stage with its chunk; page ids come from the step's
 // flat list (split order, uploaded with the step's plan), 32 per coalesced
-// load, and a chunk's ticket is drawn while the previous chunk's pages go
-// out. After the last chunk it sends an end tag through the ring. Warps 0-7
+// load; the next chunk's ticket is drawn while the current chunk's last
+// pages go out, and the first chunk's pages that hold only earlier positions
+// are requested before the kernel waits for its predecessor. After the last
+// chunk it sends an end tag through the ring. Warps 0-7
 // (one per head) consume each stage with the online softmax of
 // attn_partial_kernel, release it, and write one partial per split. K/V
 // loads carry an L2 evict-first hint. Tiles are loaded with SWIZZLE_128B
@@ -34,9 +36,11 @@ struct AttnTma {
     static constexpr int kBoxes = kBf16 ? 1 : 2;            // 128-byte column boxes per block
     static constexpr int kBoxBytes = 128 * 128;             // 128 rows x 128 bytes
     static constexpr int kBlockBytes = kBoxes * kBoxBytes;  // K (or V) of one page, all heads
-    static constexpr int kStageBytes = 2 * kBlockBytes;
+    static constexpr int kStageBytes = 2 * kBlockBytes;     // a page's K and V
     static constexpr int kStages = 3;
-    static constexpr int kSmem = 1024 + kStages * kStageBytes + 64;
+    // + barriers (2 per stage), the failure flag and the stage tags
+    static constexpr int kSmem = 1024 + kStages * kStageBytes + 128;
+    static_assert(2 * kStages * 8 + 4 + 4 * kStages <= 128, "ring bookkeeping exceeds its shared memory");
     static constexpr int kBoxCols = kBf16 ? 64 : 32;        // elements per 128-byte box row
 };
 
@@ -79,17 +83,23 @@ __device__ __forceinline__ AttnLane<kBf16> attn_lane(int head, int lane) {
 }
 
 // One page of one head (the warp's) into the online softmax state (m, l,
-// a0, a1): lane l scores key (l & 15) over dims (l >> 4)*32 .. +31, the two
-// halves meet with one shuffle, and for P.V lane l owns output dims 2l,
-// 2l+1. Keys key0 + k with key0 + k >= n_keys are masked (exp(-inf) = 0).
-// Shared by attn_tma_kernel and the persistent step kernel.
+// a0, a1), in two halves so that a ring can release the K block before the
+// V block is read. attn_page_k: lane l scores key (l & 15) over dims
+// (l >> 4)*32 .. +31, the two halves meet with one shuffle; keys key0 + k
+// with key0 + k >= n_keys are masked (exp(-inf) = 0); the running max, sum
+// and rescaled accumulators are updated and the key's probability pr (lane
+// l: key l & 15) returned. attn_page_v: P.V, lane l owns output dims 2l,
+// 2l+1. attn_page = both, for a ring holding K and V together; shared with
+// the persistent step kernel.
 template <bool kBf16>
-__device__ __forceinline__ void attn_page(const uint8_t* sK, const uint8_t* sV, const AttnLane<kBf16>& ad,
-                                          const float (&qh)[32], int key0, int n_keys, float& m, float& l, float& a0,
-                                          float& a1, bool& finite_ok) {
+__device__ __forceinline__ float attn_page_k(const uint8_t* sK, const AttnLane<kBf16>& ad, const float (&qh)[32],
+                                             int key0, int n_keys, float& m, float& l, float& a0, float& a1,
+                                             bool& finite_ok) {
     const int lane = threadIdx.x & 31;
     const bool valid = key0 + (lane & 15) < n_keys;
-    float dot = 0.0f;
+    // four independent partial dots (a quarter of the lane's 32 dims each),
+    // summed pairwise: a short dependency chain per page
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if constexpr (kBf16) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -97,20 +107,21 @@ __device__ __forceinline__ void attn_page(const uint8_t* sK, const uint8_t* sV, 
             const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                dot = fmaf(qh[8 * c + 2 * k], __uint_as_float(w[k] << 16), dot);
-                dot = fmaf(qh[8 * c + 2 * k + 1], __uint_as_float(w[k] & 0xffff0000u), dot);
+                d[c] = fmaf(qh[8 * c + 2 * k], __uint_as_float(w[k] << 16), d[c]);
+                d[c] = fmaf(qh[8 * c + 2 * k + 1], __uint_as_float(w[k] & 0xffff0000u), d[c]);
             }
         }
     } else {
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
             const float4 v = *reinterpret_cast<const float4*>(sK + ad.k_off[c]);
-            dot = fmaf(qh[4 * c], v.x, dot);
-            dot = fmaf(qh[4 * c + 1], v.y, dot);
-            dot = fmaf(qh[4 * c + 2], v.z, dot);
-            dot = fmaf(qh[4 * c + 3], v.w, dot);
+            d[c >> 1] = fmaf(qh[4 * c], v.x, d[c >> 1]);
+            d[c >> 1] = fmaf(qh[4 * c + 1], v.y, d[c >> 1]);
+            d[c >> 1] = fmaf(qh[4 * c + 2], v.z, d[c >> 1]);
+            d[c >> 1] = fmaf(qh[4 * c + 3], v.w, d[c >> 1]);
         }
     }
+    float dot = (d[0] + d[1]) + (d[2] + d[3]);
     dot += __shfl_xor_sync(kFull, dot, 16);
     float score = dot * 0.125f;
     if (valid) finite_ok &= isfinite(score);
@@ -127,47 +138,64 @@ __device__ __forceinline__ void attn_page(const uint8_t* sK, const uint8_t* sV, 
     l = fmaf(l, alpha, ps);
     a0 *= alpha;
     a1 *= alpha;
+    m = m_new;
+    return pr;
+}
+
+template <bool kBf16>
+__device__ __forceinline__ float2 attn_v_pair(const uint8_t* vp) {
+    if constexpr (kBf16) {
+        const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vp);
+        return make_float2(__uint_as_float(w2 << 16), __uint_as_float(w2 & 0xffff0000u));
+    } else {
+        return *reinterpret_cast<const float2*>(vp);
+    }
+}
+
+// P.V of one page: even and odd keys in two independent chains, added to
+// the (rescaled) accumulators at the end.
+template <bool kBf16>
+__device__ __forceinline__ void attn_page_v(const uint8_t* sV, const AttnLane<kBf16>& ad, float pr, int key0,
+                                            int n_keys, float& a0, float& a1) {
     const int n_valid = min(kPage, n_keys - key0);
+    float e0 = 0.0f, e1 = 0.0f, o0 = 0.0f, o1 = 0.0f;
     if (n_valid == kPage) {  // full page: no per-key guard
 #pragma unroll
-        for (int j = 0; j < kPage; ++j) {
-            const float pj = __shfl_sync(kFull, pr, j);
-            const uint8_t* vp = sV + ad.v_off[j & 7] + (j >> 3) * 1024;
-            float v0, v1;
-            if constexpr (kBf16) {
-                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vp);
-                v0 = __uint_as_float(w2 << 16);
-                v1 = __uint_as_float(w2 & 0xffff0000u);
-            } else {
-                const float2 w2 = *reinterpret_cast<const float2*>(vp);
-                v0 = w2.x;
-                v1 = w2.y;
-            }
-            a0 = fmaf(pj, v0, a0);
-            a1 = fmaf(pj, v1, a1);
+        for (int j = 0; j < kPage; j += 2) {
+            const float pe = __shfl_sync(kFull, pr, j), po = __shfl_sync(kFull, pr, j + 1);
+            const float2 ve = attn_v_pair<kBf16>(sV + ad.v_off[j & 7] + (j >> 3) * 1024);
+            const float2 vo = attn_v_pair<kBf16>(sV + ad.v_off[(j + 1) & 7] + ((j + 1) >> 3) * 1024);
+            e0 = fmaf(pe, ve.x, e0);
+            e1 = fmaf(pe, ve.y, e1);
+            o0 = fmaf(po, vo.x, o0);
+            o1 = fmaf(po, vo.y, o1);
         }
     } else {
 #pragma unroll
-        for (int j = 0; j < kPage; ++j) {
-            const float pj = __shfl_sync(kFull, pr, j);
+        for (int j = 0; j < kPage; j += 2) {
+            const float pe = __shfl_sync(kFull, pr, j), po = __shfl_sync(kFull, pr, j + 1);
             if (j < n_valid) {
-                const uint8_t* vp = sV + ad.v_off[j & 7] + (j >> 3) * 1024;
-                float v0, v1;
-                if constexpr (kBf16) {
-                    const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vp);
-                    v0 = __uint_as_float(w2 << 16);
-                    v1 = __uint_as_float(w2 & 0xffff0000u);
-                } else {
-                    const float2 w2 = *reinterpret_cast<const float2*>(vp);
-                    v0 = w2.x;
-                    v1 = w2.y;
-                }
-                a0 = fmaf(pj, v0, a0);
-                a1 = fmaf(pj, v1, a1);
+                const float2 ve = attn_v_pair<kBf16>(sV + ad.v_off[j & 7] + (j >> 3) * 1024);
+                e0 = fmaf(pe, ve.x, e0);
+                e1 = fmaf(pe, ve.y, e1);
+            }
+            if (j + 1 < n_valid) {
+                const float2 vo = attn_v_pair<kBf16>(sV + ad.v_off[(j + 1) & 7] + ((j + 1) >> 3) * 1024);
+                o0 = fmaf(po, vo.x, o0);
+                o1 = fmaf(po, vo.y, o1);
             }
         }
     }
-    m = m_new;
+    a0 += e0 + o0;
+    a1 += e1 + o1;
+}
+
+template <bool kBf16>
+__device__ __forceinline__ void attn_page(const uint8_t* sK, const uint8_t* sV, const AttnLane<kBf16>& ad,
+                                          const float (&qh)[32], int key0, int n_keys, float& m, float& l, float& a0,
+                                          float& a1, bool& finite_ok) {
+    const float pr = attn_page_k<kBf16>(sK, ad, qh, key0, n_keys, m, l, a0, a1, finite_ok);
+    attn_page_v<kBf16>(sV, ad, pr, key0, n_keys, a0, a1);
 }
 
 template <bool kBf16>
@@ -191,7 +219,11 @@ __global__ void __launch_bounds__(kAttnTmaThreads, 2) attn_tma_kernel(const __gr
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    pdl_wait();  // q, the appended K/V, the plan and the ticket counter come from earlier work
+    // The plan (header, chunk tables, page ids) is host data uploaded before
+    // the step's first kernel, so it may be read before the wait; so may the
+    // K/V of every page but a stream's last one (the page this layer's QKV
+    // launch appends to, marked ~page in the id list): the producer starts
+    // its first chunk's ring before the wait.
     const int n_chunks = __ldcg(p.plan + 1);
     const int32_t* cta_split = p.plan + __ldcg(p.plan + 2);
     const int32_t* cta_page = p.plan + __ldcg(p.plan + 3);
@@ -199,58 +231,68 @@ __global__ void __launch_bounds__(kAttnTmaThreads, 2) attn_tma_kernel(const __gr
 
     if (warp == kAttnHeadsPerCta) {
         // Ring index n runs on across splits and chunks: stage n % kStages,
-        // use n / kStages. Lane j holds the id of page n0 + j of the chunk;
-        // lane 0 issues.
+        // use n / kStages. Lane j holds the id of page i0 + j of the chunk;
+        // lane 0 issues. The next chunk's ticket is drawn when this chunk
+        // has kTicketLead pages left to issue, so that near the end no CTA
+        // holds a chunk it has not started.
+        constexpr int kTicketLead = 4;
         const uint64_t policy = l2_evict_first_policy();
         int n = 0;
-        bool stop = false;
+        bool stop = false, waited = false;
         int c = blockIdx.x;
         int f0 = 0, np = 0;
         if (c < n_chunks) {
             f0 = __ldcg(cta_page + c);
             np = __ldcg(cta_page + c + 1) - f0;
         }
-        int id = lane < np ? __ldcg(ids + f0 + lane) : 0;
         while (c < n_chunks && !stop) {
-            // the next chunk: ticket and bounds, in flight while this chunk's pages go out
-            int ticket = 0;
-            if (lane == 0) ticket = atomicAdd(p.chunk_ctr, 1);
-            const int c_next = static_cast<int>(gridDim.x) + __shfl_sync(kFull, ticket, 0);
-            int f0n = 0, npn = 0;
-            if (c_next < n_chunks) {
-                f0n = __ldcg(cta_page + c_next);
-                npn = __ldcg(cta_page + c_next + 1) - f0n;
-            }
-            for (int n0 = 0; n0 < np && !stop; n0 += 32) {
-                if (n0 > 0) id = n0 + lane < np ? __ldcg(ids + f0 + n0 + lane) : 0;
-                const int cnt = min(32, np - n0);
-                for (int j = 0; j < cnt; ++j, ++n) {
-                    const int page = __shfl_sync(kFull, id, j);
-                    if (lane == 0) {
-                        const int st = n % T::kStages;
-                        if (n < T::kStages || mbar_wait(empty0 + 8 * st, ((n / T::kStages) - 1) & 1, error, failed)) {
-                            const int row0 = (page * n_layers + p.layer) * 256;  // K block; V block follows
-                            uint8_t* stage = smem + st * T::kStageBytes;
-                            stage_chunk[st] = c;
-                            mbar_expect_tx(full0 + 8 * st, T::kStageBytes);
+            int c_next = n_chunks, f0n = 0, npn = 0;
+            const int draw_at = max(0, np - kTicketLead);
+            int id = 0;
+            for (int i = 0; i < np; ++i, ++n) {
+                if ((i & 31) == 0) id = i + lane < np ? __ldcg(ids + f0 + i + lane) : 0;
+                if (i == draw_at) {
+                    if (!waited) {
+                        pdl_wait();  // the ticket counter is zeroed by the step's prep kernel
+                        waited = true;
+                    }
+                    int ticket = 0;
+                    if (lane == 0) ticket = atomicAdd(p.chunk_ctr, 1);
+                    c_next = static_cast<int>(gridDim.x) + __shfl_sync(kFull, ticket, 0);
+                    if (c_next < n_chunks) {
+                        f0n = __ldcg(cta_page + c_next);
+                        npn = __ldcg(cta_page + c_next + 1) - f0n;
+                    }
+                }
+                const int raw = __shfl_sync(kFull, id, i & 31);
+                if (raw < 0 && !waited) {
+                    pdl_wait();  // a stream's last page: this layer's K/V row is being appended
+                    waited = true;
+                }
+                const int page = raw < 0 ? ~raw : raw;
+                if (lane == 0) {
+                    const int st = n % T::kStages;
+                    if (n < T::kStages || mbar_wait(empty0 + 8 * st, ((n / T::kStages) - 1) & 1, error, failed)) {
+                        const int row0 = (page * n_layers + p.layer) * 256;  // K block; V block follows
+                        uint8_t* stage = smem + st * T::kStageBytes;
+                        stage_chunk[st] = c;
+                        mbar_expect_tx(full0 + 8 * st, T::kStageBytes);
 #pragma unroll
-                            for (int bx = 0; bx < T::kBoxes; ++bx) {
-                                tma_load_2d_hint(smem_addr(stage + bx * T::kBoxBytes), &tm_kv, bx * T::kBoxCols,
-                                                 row0, full0 + 8 * st, policy);
-                                tma_load_2d_hint(smem_addr(stage + T::kBlockBytes + bx * T::kBoxBytes), &tm_kv,
-                                                 bx * T::kBoxCols, row0 + 128, full0 + 8 * st, policy);
-                            }
+                        for (int bx = 0; bx < T::kBoxes; ++bx) {
+                            tma_load_2d_hint(smem_addr(stage + bx * T::kBoxBytes), &tm_kv, bx * T::kBoxCols, row0,
+                                             full0 + 8 * st, policy);
+                            tma_load_2d_hint(smem_addr(stage + T::kBlockBytes + bx * T::kBoxBytes), &tm_kv,
+                                             bx * T::kBoxCols, row0 + 128, full0 + 8 * st, policy);
                         }
                     }
-                    // one decision for the whole warp (a wait that gave up sets *failed)
-                    stop = __any_sync(kFull, *failed != 0);
-                    if (stop) break;
                 }
+                // one decision for the whole warp (a wait that gave up sets *failed)
+                stop = __any_sync(kFull, *failed != 0);
+                if (stop) break;
             }
             c = c_next;
             f0 = f0n;
             np = npn;
-            id = c < n_chunks && lane < np ? __ldcg(ids + f0 + lane) : 0;
         }
         if (!stop && lane == 0) {
             pdl_trigger();  // everything left of this CTA is in the ring
@@ -263,6 +305,7 @@ __global__ void __launch_bounds__(kAttnTmaThreads, 2) attn_tma_kernel(const __gr
         return;
     }
 
+    pdl_wait();  // q and the appended K/V rows come from earlier launches
     // Consumer: head = warp (attn_page).
     const int head = warp, half = lane >> 4;
     const AttnLane<kBf16> ad = attn_lane<kBf16>(head, lane);
@@ -274,7 +317,7 @@ __global__ void __launch_bounds__(kAttnTmaThreads, 2) attn_tma_kernel(const __gr
         const int c = stage_chunk[st0];
         if (c < 0) break;
         const int s_begin = __ldcg(cta_split + c), s_end = __ldcg(cta_split + c + 1);
-        bool landed = true;  // stage n has been waited for
+        bool landed = true;  // stage n (the chunk's first K block) has been waited for
         for (int s = s_begin; s < s_end && ok; ++s) {
             const Split sp = p.splits[s];
             float qh[32];

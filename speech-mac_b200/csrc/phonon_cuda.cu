@@ -389,6 +389,7 @@ struct PhononCuda {
     int32_t* d_table = nullptr;
     std::vector<int32_t> free_pages;
     std::vector<StreamSlot> streams;
+    std::vector<int32_t> h_fresh_page;  // split planner scratch per stream slot (INT32_MAX between calls)
     float* d_freq = nullptr;
     int cap_rows = 0, max_splits = 0, meta_ints = 0;
     float2* d_rope = nullptr;
@@ -720,7 +721,8 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     const int G = std::max(C, c->sms);  // chunk table entries: at least one per CTA of a persistent grid
     // Metadata layout: slot, pos, first, count [R each], the plan header [8]
     // (splits S, chunks C, offsets from the header of cta_split [G+1],
-    // cta_page [G+1] and the page ids [P] in split order), splits [4S], the
+    // cta_page [G+1] and the page ids [P] in split order, a stream's last
+    // page as ~id), splits [4S], the
     // two chunk tables, the page ids, then page updates [3U]. The kernels of
     // a step read S, C and the tables through the header, so a replayed step
     // graph depends on R alone; the page updates are applied outside graphs.
@@ -729,6 +731,15 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     const long long split_cap = c->max_splits;
     std::vector<int32_t>& flat = lane->h_pages;
     flat.clear();
+    // first page of each stream that this batch appends to (its lowest position)
+    for (int e = 0; e < R; ++e) c->h_fresh_page[slot[e]] = std::min(c->h_fresh_page[slot[e]], pos[e] / kPage);
+    struct FreshReset {  // back to INT32_MAX on every way out
+        PhononCuda* c;
+        const std::vector<int32_t>& slot;
+        ~FreshReset() {
+            for (int32_t sl : slot) c->h_fresh_page[sl] = INT32_MAX;
+        }
+    } fresh_reset{c, slot};
     {
         long long done = 0;  // pages before entry e
         int e = 0, pb = 0;   // cursor: page pb of entry e
@@ -745,6 +756,9 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
                 if (h_count[e] == 0) h_first[e] = S;
                 h_splits[S++] = Split{e, pb, take, pos[e] + 1};
                 flat.insert(flat.end(), pages.begin() + pb, pages.begin() + pb + take);
+                // pages this launch appends to (from the stream's lowest position in the batch on) as ~id
+                const int fresh = std::max(pb, c->h_fresh_page[slot[e]]);
+                for (int q = fresh; q < pb + take; ++q) flat[flat.size() - (pb + take - q)] = ~pages[q];
                 h_count[e]++;
                 pb += take;
                 left -= take;
@@ -1498,6 +1512,7 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
     c->free_pages.reserve(cfg.pool_pages);
     for (int32_t p = static_cast<int32_t>(cfg.pool_pages) - 1; p >= 0; --p) c->free_pages.push_back(p);
     c->streams.resize(cfg.max_streams);
+    c->h_fresh_page.assign(cfg.max_streams, INT32_MAX);
     *out = c;
     return PHONON_CUDA_OK;
 }

@@ -596,7 +596,8 @@ struct AttnParams {
     // TMA kernel: the step's plan header, [0] splits, [1] chunks C, then the
     // offsets (in ints, from the header) of [2] cta_split and [3] cta_page
     // (first split and first page of each chunk, at least C + 1 entries) and
-    // [4] the page ids of all splits in split order
+    // [4] the page ids of all splits in split order (a stream's last page,
+    // which the step appends to, stored as ~id)
     const int32_t* plan;
     int32_t* chunk_ctr;    // TMA kernel: chunk tickets of this launch (zeroed at step start)
     int n_splits;
