@@ -44,7 +44,7 @@ HBM_FALLBACK_GBS = 6650.0
 # DRAM bytes (read + write) per algorithmic byte of the attention kernel, from
 # one ncu capture of the same kernel on the configs[3] shape at 128 streams;
 # scaled by each launch's algorithmic bytes to give `traffic`.
-ATTN_DRAM_PER_ALGO_BYTE = 1.027
+ATTN_DRAM_PER_ALGO_BYTE = 1.024
 
 
 def measured_hbm_gbs():
