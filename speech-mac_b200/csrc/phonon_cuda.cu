@@ -1740,6 +1740,17 @@ int finish_sync(PhononCuda* c, uint32_t n) {
 
 extern "C" {
 
+// Host memory the driver has page-locked (cudaHostAlloc, cudaHostRegister):
+// DMA can read it directly, without a staging copy.
+static bool is_pinned_host(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
 int phonon_cuda_step(PhononCuda* c, uint32_t n, const uint32_t* streams, const uint32_t* positions,
                      const float* x, float* y, int32_t* status, PhononCudaCancelPoll cancel, void* cctx) {
     if (!c || !x || !y || !status) return PHONON_CUDA_INVALID_ARGUMENT;
@@ -1750,8 +1761,13 @@ int phonon_cuda_step(PhononCuda* c, uint32_t n, const uint32_t* streams, const u
     std::vector<int32_t> slot, pos, updates;
     PageUndo undo{c, {}};
     if ((st = prepare_decode(c, n, streams, positions, slot, pos, updates, undo, true))) return st;
-    std::memcpy(c->h_x, x, static_cast<size_t>(n) * kWidth * 4);
-    cudaMemcpyAsync(c->d_x0, c->h_x, static_cast<size_t>(n) * kWidth * 4, cudaMemcpyHostToDevice, c->stream);
+    const size_t x_bytes = static_cast<size_t>(n) * kWidth * 4;
+    if (is_pinned_host(x)) {
+        CUDA_TRY(cudaMemcpyAsync(c->d_x0, x, x_bytes, cudaMemcpyHostToDevice, c->stream));
+    } else {
+        std::memcpy(c->h_x, x, x_bytes);
+        CUDA_TRY(cudaMemcpyAsync(c->d_x0, c->h_x, x_bytes, cudaMemcpyHostToDevice, c->stream));
+    }
     cudaMemsetAsync(c->d_status, 0, n * 4, c->stream);
     bool cancelled = false;
     st = enqueue_decode(c, slot, pos, updates, c->d_x0, c->d_y, cancel, cctx, &cancelled);

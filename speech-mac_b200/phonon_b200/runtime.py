@@ -189,12 +189,22 @@ class Context:
         check(self.L.phonon_cuda_stream_fill_synthetic(self.h, s, length, seed), "fill_synthetic")
 
     # compute ----------------------------------------------------------------
-    def step(self, streams, positions, x, cancel=None, raise_on_status=True):
+    def step(self, streams, positions, x, cancel=None, raise_on_status=True, out=None):
+        """One decode step through host buffers (phonon_cuda_step). `out`, if
+        given, is a float32 C-contiguous [n][512] array that receives y (rows
+        of failed streams are left as they were); x or out in page-locked
+        memory (e.g. torch pin_memory tensors' numpy views) are copied by DMA
+        directly."""
         n = len(streams)
         st = np.ascontiguousarray(streams, np.uint32)
         pos = np.ascontiguousarray(positions, np.uint32)
         x = np.ascontiguousarray(x, np.float32).reshape(n, WIDTH)
-        y = np.zeros((n, WIDTH), np.float32)
+        if out is None:
+            y = np.zeros((n, WIDTH), np.float32)
+        else:
+            y = out
+            if y.dtype != np.float32 or y.shape != (n, WIDTH) or not y.flags.c_contiguous:
+                raise ValueError("out must be a C-contiguous float32 array of shape (n, 512)")
         status = np.zeros(n, np.int32)
         cb = CANCEL_FN(cancel) if cancel else CANCEL_FN()
         rc = self.L.phonon_cuda_step(self.h, n, _p(st), _p(pos), _p(x), _p(y), _p(status), cb, None)

@@ -31,6 +31,29 @@ def test_nonfinite_input_fails_only_that_stream(ctx):
     ctx.stream_free(b)
 
 
+def test_pinned_host_buffers(ctx):
+    """Page-locked x goes to the device by DMA without the staging copy, and
+    an `out` buffer receives y: results equal those of plain numpy buffers,
+    and a failed stream's row of `out` is left as it was."""
+    import torch
+    g = synth.Generator(11)
+    x = g.normal(3 * 512).reshape(3, 512).astype(np.float32)
+    x[2, 5] = np.inf
+    pinned_x = torch.from_numpy(x).pin_memory().numpy()
+    pinned_y = torch.full((3, 512), 7.0).pin_memory().numpy()
+    a = [ctx.stream_alloc(32) for _ in range(3)]
+    b = [ctx.stream_alloc(32) for _ in range(3)]
+    for pos in range(3):
+        y_ref, st_ref = ctx.step(b, [pos, pos, 0], x, raise_on_status=False)
+        y, st = ctx.step(a, [pos, pos, 0], pinned_x, raise_on_status=False, out=pinned_y)
+        assert y is pinned_y
+        assert list(st) == list(st_ref) == [rt.OK, rt.OK, rt.NON_FINITE]
+        assert np.array_equal(pinned_y[:2], y_ref[:2])
+        assert np.all(pinned_y[2] == 7.0)
+    for s in a + b:
+        ctx.stream_free(s)
+
+
 def test_argument_checks(ctx):
     a = ctx.stream_alloc(4)
     x = np.zeros((2, 512), np.float32)
