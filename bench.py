@@ -454,7 +454,7 @@ def attention_gbs(rt, weights, torch, lengths, steps, kv_type):
     R = len(lengths)
     pages = sum((int(n) + steps + 15) // 16 + 1 for n in lengths)
     ctx = rt.Context(weights, max_streams=R + 1, max_batch=R, pool_pages=pages + 8, kv_type=kv_type)
-    ctx.set_batch_paths(rt.FUSED_MAX_BATCH + 1, rt.FUSED_MAX_BATCH, 32)
+    ctx.set_batch_paths(rt.FUSED_MAX_BATCH + 1, rt.FUSED_MAX_BATCH, 4)
     ss = [ctx.stream_alloc(int(n) + steps + 1) for n in lengths]
     for i, (s, n) in enumerate(zip(ss, lengths)):
         ctx.fill_synthetic(s, int(n), 500 + i)

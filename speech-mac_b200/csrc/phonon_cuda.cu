@@ -27,9 +27,14 @@ constexpr int kMaxLayers = 64;
 constexpr int kMaxDevices = 64;
 constexpr int kMaxPagesPerStream = PHONON_CUDA_MAX_POSITIONS / kPage;  // 512
 constexpr int kPrefillChunk = 256;  // rows per prefill pass
-constexpr int kTensorMinBatch = 32;  // streams from which projections run on tcgen05
+// Batch paths by measurement (bf16 K/V, contexts 1000, µs per step; per-stage
+// GEMV / per-stage tcgen05 / persistent): 1 stream 374 / 526 / 451, 2: 550 /
+// 531 / 481, 3: 634 / 548 / 532, 4: 793 / 570 / 628, 8: 1164 / 627 / 794,
+// 16: 1683 / 624 / 730, 64: 4741 / 885 / 1106.
+constexpr int kTensorMinBatch = 4;   // streams from which projections run on tcgen05
 constexpr int kMaxSms = 1024;        // bound on the SM count (persistent split table)
-constexpr int kFusedMinBatch = 8;    // smaller batches are as fast or faster one launch per stage
+constexpr int kFusedMinBatch = 2;    // default window of the persistent step
+constexpr int kFusedMaxBatch = 3;
 constexpr int kPlanHeader = 8;       // ints of the step plan header in the metadata
 constexpr int kGuide = 2;            // guided chunks: remaining pages / (kGuide * attention CTAs)
 constexpr int kTicketMinChunk = 8;   // pages per guided chunk, at least
@@ -409,7 +414,7 @@ struct PhononCuda {
     // Whole-step persistent kernel (batches up to fused_max streams)
     int sms = 0, smem_optin = 0;
     bool persist_ok = false;         // device and weights allow it
-    uint32_t fused_min = kFusedMinBatch, fused_max = kPersistMaxBatch;
+    uint32_t fused_min = kFusedMinBatch, fused_max = kFusedMaxBatch;
     uint32_t split_min = kSplitMinBatch;  // batches from which a step runs on two lanes
     cudaEvent_t fork = nullptr, join = nullptr;
     uint32_t tensor_min = kTensorMinBatch;

@@ -242,7 +242,7 @@ class Context:
     def launch_count(self):
         return int(self.L.phonon_cuda_launch_count(self.h))
 
-    def set_batch_paths(self, fused_min_batch=8, fused_max_batch=FUSED_MAX_BATCH, tensor_min_batch=32,
+    def set_batch_paths(self, fused_min_batch=2, fused_max_batch=3, tensor_min_batch=4,
                         split_min_batch=320):
         """Batch sizes routed to the persistent whole-step launch
         (fused_min_batch..fused_max_batch; a minimum above the maximum

@@ -77,7 +77,26 @@ def test_config0_prefix_and_decode(ctx12, oracle, weights12):
     om.free_stream(oc)
 
 
-def test_batched_staggered_streams(ctx12, oracle, weights12):
+NEVER = 1 << 20
+# (fused window, tensor-core minimum): the defaults (GEMV for 1 stream, the
+# persistent step for 2-3, tensor-core projections from 4), every batch in the
+# persistent step, every batch on the per-stage GEMVs
+PATHS = {"default": None, "persistent": (1, rt.FUSED_MAX_BATCH, NEVER), "gemv": (NEVER, rt.FUSED_MAX_BATCH, NEVER)}
+
+
+@pytest.mark.parametrize("paths", list(PATHS))
+def test_batched_staggered_streams(ctx12, oracle, weights12, paths):
+    """Batches growing from 1 to 12 streams (staggered starts) on each batch
+    path, against the oracle stream by stream."""
+    if PATHS[paths]:
+        ctx12.set_batch_paths(*PATHS[paths])
+    try:
+        _staggered(ctx12, oracle, weights12)
+    finally:
+        ctx12.set_batch_paths()
+
+
+def _staggered(ctx12, oracle, weights12):
     om = oracle.model(weights12)
     n = 12
     streams = [ctx12.stream_alloc(96) for _ in range(n)]
