@@ -1268,10 +1268,22 @@ int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::v
     CUDA_TRY(cudaStreamWaitEvent(L1.stream, c->fork, 0));
     if ((st = upload_batch(c, s1, p1, {}, &b1, true, &L1, c->d_status + n0, grid))) return st;
     b0.split = b1.split = true;
-    if ((st = enqueue_stack(c, b0, in, out, nullptr, nullptr, nullptr, cancelled))) return st;
-    if ((st = enqueue_stack(c, b1, in + static_cast<size_t>(n0) * kWidth, out + static_cast<size_t>(n0) * kWidth,
-                            nullptr, nullptr, nullptr, cancelled)))
-        return st;
+    // The halves' launches are issued layer by layer, alternating, so that
+    // the second half starts as soon as the first (issuing all of one half
+    // first delays the other by the host time of ~100 launches).
+    {
+        const int L = static_cast<int>(c->cfg.n_layers);
+        const float* cur[2] = {in, in + static_cast<size_t>(n0) * kWidth};
+        float* fin[2] = {out, out + static_cast<size_t>(n0) * kWidth};
+        const Batch* bs[2] = {&b0, &b1};
+        for (int l = 0; l < L; ++l)
+            for (int k = 0; k < 2; ++k) {
+                const Batch& b = *bs[k];
+                float* o = (l == L - 1) ? fin[k] : ((cur[k] == b.lane->x0) ? b.lane->x1 : b.lane->x0);
+                if ((st = enqueue_layer(c, b, l, cur[k], o))) return st;
+                cur[k] = o;
+            }
+    }
     CUDA_TRY(cudaEventRecord(c->join, L1.stream));
     CUDA_TRY(cudaStreamWaitEvent(c->stream, c->join, 0));
     return PHONON_CUDA_OK;
