@@ -190,6 +190,74 @@ __device__ __forceinline__ void attn_page_v(const uint8_t* sV, const AttnLane<kB
     a1 += e1 + o1;
 }
 
+// A bf16 page's share of one consumer lane in registers: its four 16-byte K
+// chunks and its two dims of V for the 16 keys. attn_tma_kernel loads these
+// and releases the ring stage before the math, so a stage is held only for
+// the shared-memory loads. The math (attn_page_regs) is attn_page_k +
+// attn_page_v operation for operation, on register data.
+struct PageRegsBf16 {
+    uint4 k[4];
+    uint32_t v[kPage];
+};
+
+__device__ __forceinline__ void load_page_bf16(const uint8_t* sK, const uint8_t* sV, const AttnLane<true>& ad,
+                                               PageRegsBf16& r) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) r.k[c] = *reinterpret_cast<const uint4*>(sK + ad.k_off[c]);
+#pragma unroll
+    for (int j = 0; j < kPage; ++j) r.v[j] = *reinterpret_cast<const uint32_t*>(sV + ad.v_off[j & 7] + (j >> 3) * 1024);
+}
+
+__device__ __forceinline__ void attn_page_regs(const PageRegsBf16& r, const float (&qh)[32], int key0, int n_keys,
+                                               float& m, float& l, float& a0, float& a1, bool& finite_ok) {
+    const int lane = threadIdx.x & 31;
+    const bool valid = key0 + (lane & 15) < n_keys;
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t w[4] = {r.k[c].x, r.k[c].y, r.k[c].z, r.k[c].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            d[c] = fmaf(qh[8 * c + 2 * k], __uint_as_float(w[k] << 16), d[c]);
+            d[c] = fmaf(qh[8 * c + 2 * k + 1], __uint_as_float(w[k] & 0xffff0000u), d[c]);
+        }
+    }
+    float dot = (d[0] + d[1]) + (d[2] + d[3]);
+    dot += __shfl_xor_sync(kFull, dot, 16);
+    float score = dot * 0.125f;
+    if (valid) finite_ok &= isfinite(score);
+    score = valid ? score : -INFINITY;
+    float pm = score;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) pm = fmaxf(pm, __shfl_xor_sync(kFull, pm, o));
+    const float m_new = fmaxf(m, pm);
+    const float alpha = m == -INFINITY ? 0.0f : expf(m - m_new);
+    const float pr = valid ? expf(score - m_new) : 0.0f;
+    float ps = pr;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
+    l = fmaf(l, alpha, ps);
+    a0 *= alpha;
+    a1 *= alpha;
+    m = m_new;
+    const int n_valid = min(kPage, n_keys - key0);
+    float e0 = 0.0f, e1 = 0.0f, o0 = 0.0f, o1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kPage; j += 2) {
+        const float pe = __shfl_sync(kFull, pr, j), po = __shfl_sync(kFull, pr, j + 1);
+        if (j < n_valid) {  // keys past the stream's end may hold anything
+            e0 = fmaf(pe, __uint_as_float(r.v[j] << 16), e0);
+            e1 = fmaf(pe, __uint_as_float(r.v[j] & 0xffff0000u), e1);
+        }
+        if (j + 1 < n_valid) {
+            o0 = fmaf(po, __uint_as_float(r.v[j + 1] << 16), o0);
+            o1 = fmaf(po, __uint_as_float(r.v[j + 1] & 0xffff0000u), o1);
+        }
+    }
+    a0 += e0 + o0;
+    a1 += e1 + o1;
+}
+
 template <bool kBf16>
 __device__ __forceinline__ void attn_page(const uint8_t* sK, const uint8_t* sV, const AttnLane<kBf16>& ad,
                                           const float (&qh)[32], int key0, int n_keys, float& m, float& l, float& a0,
@@ -200,7 +268,7 @@ __device__ __forceinline__ void attn_page(const uint8_t* sK, const uint8_t* sV, 
 
 template <bool kBf16>
 __global__ void __launch_bounds__(kAttnTmaThreads, 2) attn_tma_kernel(const __grid_constant__ CUtensorMap tm_kv,
-                                                                   AttnParams p, int n_layers, int32_t* error) {
+                                                                   AttnParams p, int32_t* error) {
     using T = AttnTma<kBf16>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -273,7 +341,7 @@ __global__ void __launch_bounds__(kAttnTmaThreads, 2) attn_tma_kernel(const __gr
                 if (lane == 0) {
                     const int st = n % T::kStages;
                     if (n < T::kStages || mbar_wait(empty0 + 8 * st, ((n / T::kStages) - 1) & 1, error, failed)) {
-                        const int row0 = (page * n_layers + p.layer) * 256;  // K block; V block follows
+                        const int row0 = (p.layer * p.kv.pool_pages + page) * 256;  // K block; V block follows
                         uint8_t* stage = smem + st * T::kStageBytes;
                         stage_chunk[st] = c;
                         mbar_expect_tx(full0 + 8 * st, T::kStageBytes);
@@ -343,10 +411,19 @@ __global__ void __launch_bounds__(kAttnTmaThreads, 2) attn_tma_kernel(const __gr
                 }
                 landed = false;
                 const uint8_t* sK = smem + st * T::kStageBytes;
-                attn_page<kBf16>(sK, sK + T::kBlockBytes, ad, qh, (sp.page_begin + i) * kPage, sp.n_keys, m, l, a0,
-                                 a1, finite_ok);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty0 + 8 * st);
+                if constexpr (kBf16) {
+                    // the lane's share into registers, the stage back to the producer, then the math
+                    PageRegsBf16 pr;
+                    load_page_bf16(sK, sK + T::kBlockBytes, ad, pr);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty0 + 8 * st);
+                    attn_page_regs(pr, qh, (sp.page_begin + i) * kPage, sp.n_keys, m, l, a0, a1, finite_ok);
+                } else {
+                    attn_page<kBf16>(sK, sK + T::kBlockBytes, ad, qh, (sp.page_begin + i) * kPage, sp.n_keys, m, l,
+                                     a0, a1, finite_ok);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty0 + 8 * st);
+                }
             }
             if (!ok) break;
             float* out = p.part + (static_cast<size_t>(s) * kHeads + head) * kPartStride;

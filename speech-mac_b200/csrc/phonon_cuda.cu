@@ -320,8 +320,7 @@ cudaError_t launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, int rows, 
 }
 
 template <bool kBf16>
-cudaError_t launch_attn_tma(const CUtensorMap& tm, const AttnParams& p, int n_layers, int32_t* err, int n_splits,
-                            cudaStream_t s) {
+cudaError_t launch_attn_tma(const CUtensorMap& tm, const AttnParams& p, int32_t* err, int n_ctas, cudaStream_t s) {
     static bool configured[kMaxDevices] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -333,8 +332,7 @@ cudaError_t launch_attn_tma(const CUtensorMap& tm, const AttnParams& p, int n_la
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    return launch_pdl(attn_tma_kernel<kBf16>, dim3(n_splits), dim3(kAttnTmaThreads), AttnTma<kBf16>::kSmem, s, tm, p,
-                      n_layers, err);
+    return launch_pdl(attn_tma_kernel<kBf16>, dim3(n_ctas), dim3(kAttnTmaThreads), AttnTma<kBf16>::kSmem, s, tm, p, err);
 }
 
 template <int kCols, bool kLN>
@@ -512,7 +510,7 @@ int load_layer(DevLayer* D, const PhononCudaLayer& w) {
 KvView kv_view(const PhononCuda* c) {
     KvView kv;
     kv.pool = c->kv_pool;
-    kv.page_elems = c->page_elems;
+    kv.pool_pages = static_cast<int>(c->cfg.pool_pages);
     kv.bf16 = c->cfg.kv_type == PHONON_CUDA_KV_BF16;
     kv.table = c->d_table;
     kv.max_pages = kMaxPagesPerStream;
@@ -860,8 +858,8 @@ int enqueue_attention(PhononCuda* c, const Batch& b, int l, bool digits_out, boo
         LaunchScope ls(c, PHONON_CUDA_K_ATTENTION,
                        b.keys * 2.0 * kWidth * esize + act * kWidth + b.S * kHeads * kPartStride * 4.0, b.lane->stream);
         if (c->attn_tma) {
-            CUDA_TRY(kv.bf16 ? launch_attn_tma<true>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.attn_grid, s)
-                             : launch_attn_tma<false>(c->tm_kv, ap, c->cfg.n_layers, c->d_err, b.attn_grid, s));
+            CUDA_TRY(kv.bf16 ? launch_attn_tma<true>(c->tm_kv, ap, c->d_err, b.attn_grid, s)
+                             : launch_attn_tma<false>(c->tm_kv, ap, c->d_err, b.attn_grid, s));
         } else {
             CUDA_TRY(kv.bf16 ? launch_pdl(attn_partial_kernel<true>, dim3(grid), dim3(kAttnWarps * 32), 0, s, ap)
                              : launch_pdl(attn_partial_kernel<false>, dim3(grid), dim3(kAttnWarps * 32), 0, s, ap));
@@ -1509,8 +1507,8 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
         }
     }
     {
-        // Row r of the pool = 64 dims of (page, layer, k|v, head, slot); a
-        // page-layer K block is rows [(page*L + layer)*256, +128).
+        // Row r of the pool = 64 dims of (layer, page, k|v, head, slot); a
+        // layer-page K block is rows [(layer*pool_pages + page)*256, +128).
         const uint64_t kv_rows = static_cast<uint64_t>(cfg.pool_pages) * cfg.n_layers * 256;
         const bool bf16 = cfg.kv_type == PHONON_CUDA_KV_BF16;
         c->attn_tma = kv_rows < (1ull << 31) &&

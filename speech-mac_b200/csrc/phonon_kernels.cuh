@@ -272,10 +272,14 @@ __global__ void step_prep_kernel(const int32_t* pos, const float* freq, int R, f
 }
 
 // ----------------------------------------------------------------- KV pages
-// A page stores 16 positions of every layer as [layer][k|v][head][slot][dim].
+// A page holds 16 positions of every layer. The pool is layer-major:
+// [layer][page][k|v][head][slot][dim], so the K/V blocks one layer's
+// attention reads are the pool's pages in a contiguous range of memory (a
+// page-major pool, [page][layer][...], spaces them n_layers blocks apart,
+// and a bare TMA page ring measured ~7 % less DRAM bandwidth on that stride).
 struct KvView {
     void* pool;
-    long long page_elems;   // elements per page: n_layers * 2 * 8 * 16 * 64
+    int pool_pages;         // pages per layer
     int bf16;               // 1: bf16 elements, 0: fp32
     const int32_t* table;   // [stream slot][max_pages]
     int max_pages;
@@ -283,8 +287,8 @@ struct KvView {
 
 __device__ __forceinline__ long long kv_offset(const KvView& kv, int page, int layer, int which,
                                                int head, int slot) {
-    return static_cast<long long>(page) * kv.page_elems +
-           ((static_cast<long long>(layer * 2 + which) * kHeads + head) * kPage + slot) * kHeadDim;
+    return ((static_cast<long long>(layer) * kv.pool_pages + page) * 2 + which) * (kHeads * kPage * kHeadDim) +
+           (head * kPage + slot) * kHeadDim;
 }
 
 __device__ __forceinline__ void kv_store2(const KvView& kv, long long off, float a, float b) {

@@ -378,7 +378,7 @@ __device__ __forceinline__ void persist_attention(const CUtensorMap* tm, const P
                 const int st = static_cast<int>(n % kSt);
                 if (n >= kSt && !mbar_wait(empty0 + 8 * st, ((n / kSt) - 1) & 1, p.error, failed)) continue;
                 const int page = __ldcg(table + sp.page_begin + i);
-                const int row0 = (page * p.n_layers + layer) * 256;  // K block; V block follows
+                const int row0 = (layer * p.kv.pool_pages + page) * 256;  // K block; V block follows
                 uint8_t* stage = stages + st * A::kStageBytes;
                 mbar_expect_tx(full0 + 8 * st, A::kStageBytes);
 #pragma unroll
