@@ -44,6 +44,9 @@ struct AttnTma {
     static constexpr int kBoxCols = kBf16 ? 64 : 32;        // elements per 128-byte box row
 };
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
 
 // Address of 16-byte chunk `chunk` of row `row` in a SWIZZLE_128B box.
 __device__ __forceinline__ const uint8_t* sw128(const uint8_t* box, int row, int chunk) {
