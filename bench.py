@@ -384,6 +384,7 @@ def bench_single_stream(rt, synth, weights, torch):
     """128-position prefix then 125 decode steps of one stream,
     fp32 KV; the L2 is flushed (256 MB write) before every timed step."""
     ctx = rt.Context(weights, max_streams=2, max_batch=1, pool_pages=32, kv_type=rt.KV_F32)
+    cluster = ctx.set_cluster_step(rt.MAX_POSITIONS)
     s = ctx.stream_alloc(256)
     g = synth.stream_generator(0, 0)
     ctx.append(s, np.stack([g.normal(512) for _ in range(128)]))
@@ -405,8 +406,15 @@ def bench_single_stream(rt, synth, weights, torch):
         times.append(a.elapsed_time(b))
     ctx.close()
     total = sum(times)
+    # algorithmic HBM bytes: weights, K/V rows read (positions 0..P) and appended, per layer and step
+    kv_row = 2 * 512 * 4
+    bytes_ = sum(N_LAYERS * (WEIGHT_BYTES_PER_LAYER + (128 + i + 1) * kv_row + kv_row) for i in range(125))
+    gbs = bytes_ / (total * 1e-3) / 1e9
+    peak, peak_kind = measured_hbm_gbs()
     return {"workload": "configs[0]", "frames_per_s": round(125 / (total * 1e-3), 1),
             "ms_per_step_median": round(statistics.median(times), 4),
+            "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 4), "peak_source": peak_kind,
+            "path": "16-CTA cluster step" if cluster else "per-stage GEMV step",
             "l2": "flushed before each step"}
 
 
@@ -575,10 +583,6 @@ def bench_q8_matvec(rt, synth, torch, reps):
 
 
 # --------------------------------------------------------------- CPU baseline
-def cpu_threads():
-    return max(1, len(os.sched_getaffinity(0)))
-
-
 class RefRunner:
     """The reference (oracle/_ref) on the configs[3] shape: one host thread
     per stream, contexts U[64,2048] (seed 2) filled with seeded K/V rows,

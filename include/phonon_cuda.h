@@ -267,6 +267,22 @@ uint64_t phonon_cuda_launch_count(PhononCuda *ctx);
 int phonon_cuda_set_batch_paths(PhononCuda *ctx, uint32_t fused_min_batch, uint32_t fused_max_batch,
                                 uint32_t tensor_min_batch, uint32_t split_min_batch);
 
+/* ---- single-stream step on one thread-block cluster ----
+ * A decode step of ONE stream (phonon_cuda_step / phonon_cuda_step_device
+ * without a cancel poll) at a position below max_position runs as one launch
+ * of a 16-CTA cluster: the CTAs pass activations through distributed shared
+ * memory and meet at hardware cluster barriers, with no kernel boundary or
+ * grid-wide barrier between the ~60 dependent stages of the step. Replaces
+ * phonon_flow_stack_step_cancel (src/phonon_transformer.c:455-482) for the
+ * reference engine's one-request-per-thread decode loop (src/speech.c:170).
+ * max_position 0 sends every batch through the paths of
+ * phonon_cuda_set_batch_paths; the default is PHONON_CUDA_MAX_POSITIONS.
+ * *available (optional) receives 1 when the context can run the path (Q8_0
+ * weights, TMA K/V staging, a 16-CTA cluster resident on the device).
+ * Projections and appended K/V rows equal the other paths' bit for bit; the
+ * attention merges its partial sums in another order (within rounding). */
+int phonon_cuda_set_cluster_step(PhononCuda *ctx, uint32_t max_position, int *available);
+
 const char *phonon_cuda_status_string(int status);
 
 #ifdef __cplusplus

@@ -4,6 +4,7 @@
 #include "phonon_attention.cuh"
 #include "phonon_gemm.cuh"
 #include "phonon_kernels.cuh"
+#include "phonon_cluster.cuh"
 #include "phonon_persist.cuh"
 
 #include <cuda_fp16.h>
@@ -407,6 +408,12 @@ struct PhononCuda {
     // KV pool as rows of 64 head dims for TMA page staging
     CUtensorMap tm_kv;
     bool attn_tma = false;
+    // Single-stream steps on one 16-CTA cluster (step_cluster_kernel): one
+    // head's K/V blocks of a page as 16-row boxes; steps of one stream at a
+    // position below cluster_max_pos take that path when cluster_ok.
+    CUtensorMap tm_kv16;
+    bool cluster_ok = false;
+    uint32_t cluster_max_pos = PHONON_CUDA_MAX_POSITIONS;
     Lane lanes[2];
     bool lane1_ok = false;  // second lane allocated
     // Whole-step persistent kernel (batches up to fused_max streams)
@@ -1204,6 +1211,83 @@ int enqueue_persist(PhononCuda* c, const Batch& b, const float* in, float* final
     return PHONON_CUDA_OK;
 }
 
+template <bool kBf16>
+cudaLaunchConfig_t cluster_config(cudaStream_t s, cudaLaunchAttribute* at) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(kClusterCtas);
+    cfg.blockDim = dim3(kClThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(ClShape<kBf16>::kSmem);
+    cfg.stream = s;
+    at[0].id = cudaLaunchAttributeClusterDimension;  // the whole grid is one cluster
+    at[0].val.clusterDim.x = kClusterCtas;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+// Opt the cluster kernel into its shared memory and a 16-CTA cluster, and
+// check that such a cluster can be resident on this device.
+template <bool kBf16>
+bool cluster_launchable() {
+    const void* fn = reinterpret_cast<const void*>(step_cluster_kernel<kBf16>);
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ClShape<kBf16>::kSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    cudaLaunchAttribute at[1];
+    cudaLaunchConfig_t cfg = cluster_config<kBf16>(nullptr, at);
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, step_cluster_kernel<kBf16>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return clusters >= 1;
+}
+
+// A single-stream decode step (entry (slot, pos), page-table updates
+// `updates`) as one launch of step_cluster_kernel.
+bool use_cluster(const PhononCuda* c, int n, const std::vector<int32_t>& pos, const std::vector<int32_t>& updates,
+                 bool cancel) {
+    return c->cluster_ok && n == 1 && !cancel && static_cast<uint32_t>(pos[0]) < c->cluster_max_pos &&
+           updates.size() <= 3u * kClMaxUpdates;
+}
+
+int enqueue_cluster(PhononCuda* c, int32_t slot, int32_t pos, const std::vector<int32_t>& updates, const float* in,
+                    float* out) {
+    const bool bf16 = c->cfg.kv_type == PHONON_CUDA_KV_BF16;
+    ClusterParams cp{};
+    cp.layers = c->d_players;
+    cp.n_layers = static_cast<int>(c->cfg.n_layers);
+    cp.in = in;
+    cp.out = out;
+    cp.status = c->d_status;
+    cp.error = c->d_err;
+    cp.slot = slot;
+    cp.pos = pos;
+    cp.n_updates = static_cast<int>(updates.size() / 3);
+    for (size_t i = 0; i < updates.size(); ++i) cp.updates[i] = updates[i];
+    cp.freq = c->d_freq;
+    cp.kv = kv_view(c);
+    double weights = 0.0;
+    for (const DevLayer& D : c->layers)
+        weights += linear_bytes(D.qkv) + linear_bytes(D.out) + linear_bytes(D.up) + linear_bytes(D.down);
+    const double esize = bf16 ? 2.0 : 4.0;
+    const double bytes = weights + cp.n_layers * (pos + 2.0) * 2.0 * kWidth * esize + 2.0 * kWidth * 4.0;
+    LaunchScope ls(c, PHONON_CUDA_K_FUSED, bytes, c->stream);
+    cudaLaunchAttribute at[1];
+    if (bf16) {
+        cudaLaunchConfig_t cfg = cluster_config<true>(c->stream, at);
+        CUDA_TRY(cudaLaunchKernelEx(&cfg, step_cluster_kernel<true>, c->tm_kv16, cp));
+    } else {
+        cudaLaunchConfig_t cfg = cluster_config<false>(c->stream, at);
+        CUDA_TRY(cudaLaunchKernelEx(&cfg, step_cluster_kernel<false>, c->tm_kv16, cp));
+    }
+    return PHONON_CUDA_OK;
+}
+
 int enqueue_stack(PhononCuda* c, const Batch& b, const float* in, float* final_out,
                   PhononCudaCancelPoll cancel, void* cctx, const std::vector<int>* polls_per_layer,
                   bool* cancelled) {
@@ -1248,6 +1332,7 @@ int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::v
                    const std::vector<int32_t>& updates, const float* in, float* out, PhononCudaCancelPoll cancel,
                    void* cctx, bool* cancelled) {
     const int n = static_cast<int>(slot.size());
+    if (use_cluster(c, n, pos, updates, cancel != nullptr)) return enqueue_cluster(c, slot[0], pos[0], updates, in, out);
     const bool persist = use_persist(c, n, cancel != nullptr);
     int st;
     if (persist || cancel || !c->lane1_ok || static_cast<uint32_t>(n) < c->split_min) {
@@ -1318,6 +1403,15 @@ int refresh_persist(PhononCuda* c) {
         cudaGetLastError();
     }
     c->persist_ok = ok;
+    // The single-stream cluster step needs the same weights (Q8_0 in the
+    // GEMV layout), the 16-row K/V boxes and a resident 16-CTA cluster.
+    bool cl = c->attn_tma && !c->layers.empty();
+    for (const DevLayer& D : c->layers) {
+        const DevLinear* lin[4] = {&D.qkv, &D.out, &D.up, &D.down};
+        for (int m = 0; m < 4; ++m) cl = cl && D.q8 && lin[m]->fast && lin[m]->plane && lin[m]->scales;
+    }
+    if (cl) cl = c->cfg.kv_type == PHONON_CUDA_KV_BF16 ? cluster_launchable<true>() : cluster_launchable<false>();
+    c->cluster_ok = cl;
     return PHONON_CUDA_OK;
 }
 
@@ -1513,7 +1607,9 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
         const bool bf16 = cfg.kv_type == PHONON_CUDA_KV_BF16;
         c->attn_tma = kv_rows < (1ull << 31) &&
                       make_map_2d(&c->tm_kv, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                                  c->kv_pool, kv_rows, kHeadDim, kHeadDim * esize, bf16 ? 64 : 32, 128);
+                                  c->kv_pool, kv_rows, kHeadDim, kHeadDim * esize, bf16 ? 64 : 32, 128) &&
+                      make_map_2d(&c->tm_kv16, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                  c->kv_pool, kv_rows, kHeadDim, kHeadDim * esize, bf16 ? 64 : 32, kPage);
     }
     if (cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, cfg.device) != cudaSuccess ||
         cudaDeviceGetAttribute(&c->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, cfg.device) != cudaSuccess ||
@@ -1698,6 +1794,24 @@ int phonon_cuda_set_batch_paths(PhononCuda* c, uint32_t fused_min_batch, uint32_
     c->split_min = split_min_batch;
     c->tensor_min = tensor_min_batch;
     drop_graph(c);  // a captured step holds the old path choice
+    return PHONON_CUDA_OK;
+}
+
+#ifdef PHONON_CLUSTER_TRACE
+// Profiling builds only: the cluster step's phase timestamps of the last launch.
+int phonon_cuda_debug_cluster_trace(unsigned long long* out) {
+    return cudaMemcpyFromSymbol(out, g_cluster_trace, sizeof(g_cluster_trace)) == cudaSuccess ? PHONON_CUDA_OK
+                                                                                             : PHONON_CUDA_DEVICE_ERROR;
+}
+#endif
+
+int phonon_cuda_set_cluster_step(PhononCuda* c, uint32_t max_position, int* available) {
+    if (!c) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    c->cluster_max_pos = max_position;
+    if (available) *available = c->cluster_ok ? 1 : 0;
+    drop_graph(c);
     return PHONON_CUDA_OK;
 }
 

@@ -15,6 +15,7 @@ OK, INVALID, NON_FINITE, OOM, POOL_EXHAUSTED, CAPACITY, BAD_POSITION, CANCELLED,
 Q8_0, BF16 = 1, 2
 KV_F32, KV_BF16 = 0, 1
 FUSED_MAX_BATCH = 64  # PHONON_CUDA_FUSED_MAX_BATCH
+MAX_POSITIONS = 8192  # PHONON_CUDA_MAX_POSITIONS
 WIDTH = 512
 PAGE = 16
 
@@ -77,6 +78,7 @@ def lib():
         "phonon_cuda_profile_enable": [P, C.c_int],
         "phonon_cuda_profile_read": [P, P, P, P],
         "phonon_cuda_set_batch_paths": [P, U32, U32, U32, U32],
+        "phonon_cuda_set_cluster_step": [P, U32, C.POINTER(C.c_int)],
         "phonon_cuda_wait_expiry_probe": [C.c_int, C.c_int, U32, C.POINTER(C.c_uint64)],
     }
     for name, args in sig.items():
@@ -250,6 +252,14 @@ class Context:
         to two concurrent half batches (>= split_min_batch)."""
         check(self.L.phonon_cuda_set_batch_paths(self.h, fused_min_batch, fused_max_batch, tensor_min_batch,
                                                  split_min_batch), "set_batch_paths")
+
+    def set_cluster_step(self, max_position=8192):
+        """Single-stream steps at positions below max_position run on one
+        16-CTA cluster (0 disables it). Returns whether the context can run
+        that path at all."""
+        available = C.c_int(0)
+        check(self.L.phonon_cuda_set_cluster_step(self.h, max_position, C.byref(available)), "set_cluster_step")
+        return bool(available.value)
 
     def layer_step(self, s, layer, position, x):
         x = np.ascontiguousarray(x, np.float32)

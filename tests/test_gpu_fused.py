@@ -25,6 +25,8 @@ def _pair(weights, kv_type):
     fused.set_batch_paths(1, rt.FUSED_MAX_BATCH, NO_TENSOR)
     staged = rt.Context(weights, **kw)
     staged.set_batch_paths(rt.FUSED_MAX_BATCH + 1, rt.FUSED_MAX_BATCH, NO_TENSOR)
+    for c in (fused, staged):  # single-stream steps too: no cluster path
+        c.set_cluster_step(0)
     return fused, staged
 
 
