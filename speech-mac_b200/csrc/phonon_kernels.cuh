@@ -69,15 +69,12 @@ __device__ __forceinline__ void flag_nonfinite(int32_t* status, int b) {
 }
 
 // ------------------------------------------------------------------ LayerNorm
-// Merge ADD samples (a_mean, a_m2) into (mean, m2) holding N samples, in the
+// Merge a block (a_mean, a_m2) into (mean, m2) holding n samples, in the
 // reference's unfused order: mean += c*delta; m2 += a_m2 + delta*delta*c*n
-// with c = ADD / (N + ADD) (src/phonon_transformer.c:90-98). N and ADD are
-// template constants, so c is a compile-time constant (the reference's
-// cascade only ever divides by these counts).
-template <int N, int ADD>
-__device__ __forceinline__ void ln_merge(float a_mean, float a_m2, float& mean, float& m2) {
-    constexpr float n = static_cast<float>(N);
-    constexpr float c = (N + ADD) != 0 ? static_cast<float>(ADD) / static_cast<float>(N + ADD) : 0.0f;
+// with c = added / (n + added) (src/phonon_transformer.c:90-98). The cascade
+// below only ever merges equal halves or into an empty level, so c is 1, 1/2
+// or 0 (nothing into nothing) and exact.
+__device__ __forceinline__ void ln_merge(float a_mean, float a_m2, float& mean, float& m2, float c, float n) {
     const float delta = __fsub_rn(a_mean, mean);
     mean = __fadd_rn(mean, __fmul_rn(c, delta));
     m2 = __fadd_rn(m2, __fadd_rn(a_m2, __fmul_rn(__fmul_rn(__fmul_rn(delta, delta), c), n)));
@@ -88,8 +85,12 @@ __device__ __forceinline__ void ln_merge(float a_mean, float a_m2, float& mean, 
 // (src/phonon_transformer.c:99-151): a 16-step Welford per lane; then every
 // lane replays, for each of the four lanes l of a chunk, the cascade that
 // folds the 8 chunk results (16 samples each) through three levels of a
-// binary counter, and finally merges the four lanes. The schedule below is
-// that cascade unrolled. Returns the mean and 1/sqrt(var + eps).
+// binary counter (after chunk ch, level 0 carries into level 1 when bit 0 of
+// ch + 1 is clear, level 1 into level 2 when bits 0-1 are), and finally
+// merges the four lanes. The cascade is a loop over chunks, not unrolled:
+// its straight-line form was ~640 instructions, and inside large kernels
+// (the cluster step) fetching them cold cost several microseconds per
+// LayerNorm. Returns the mean and 1/sqrt(var + eps).
 __device__ __forceinline__ void ln_moments512(const float (&v)[16], float eps, float& mu_out, float& scale_out) {
     constexpr float kRecip[16] = {1.0f / 1,  1.0f / 2,  1.0f / 3,  1.0f / 4,  1.0f / 5,  1.0f / 6,
                                   1.0f / 7,  1.0f / 8,  1.0f / 9,  1.0f / 10, 1.0f / 11, 1.0f / 12,
@@ -104,55 +105,38 @@ __device__ __forceinline__ void ln_moments512(const float (&v)[16], float eps, f
     float l0m[4], l0q[4], l1m[4], l1q[4], l2m[4], l2q[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) l0m[k] = l0q[k] = l1m[k] = l1q[k] = l2m[k] = l2q[k] = 0.0f;
-    auto chunk_into_l0 = [&](int ch, auto first) {
+#pragma unroll 1
+    for (int ch = 0; ch < 8; ++ch) {
+        // chunk ch (16 samples) into level 0: onto nothing (even ch) or onto 16
+        const float c0 = (ch & 1) ? 0.5f : 1.0f, n0 = (ch & 1) ? 16.0f : 0.0f;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const float fm = __shfl_sync(kFull, mean, ch * 4 + k);
             const float fq = __shfl_sync(kFull, m2, ch * 4 + k);
-            if constexpr (decltype(first)::value) ln_merge<0, 16>(fm, fq, l0m[k], l0q[k]);
-            else ln_merge<16, 16>(fm, fq, l0m[k], l0q[k]);
+            ln_merge(fm, fq, l0m[k], l0q[k], c0, n0);
         }
-    };
-    using First = std::true_type;
-    using Second = std::false_type;
-    // chunks 0, 1 -> level 1 (32 samples)
-    chunk_into_l0(0, First{});
-    chunk_into_l0(1, Second{});
+        if (ch & 1) {  // level 0 (32) carries into level 1: onto nothing or onto 32
+            const float c1 = (ch & 2) ? 0.5f : 1.0f, n1 = (ch & 2) ? 32.0f : 0.0f;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        ln_merge<0, 32>(l0m[k], l0q[k], l1m[k], l1q[k]);
-        l0m[k] = l0q[k] = 0.0f;
+            for (int k = 0; k < 4; ++k) {
+                ln_merge(l0m[k], l0q[k], l1m[k], l1q[k], c1, n1);
+                l0m[k] = l0q[k] = 0.0f;
+            }
+            if (ch & 2) {  // level 1 (64) carries into level 2: onto nothing or onto 64
+                const float c2 = (ch & 4) ? 0.5f : 1.0f, n2 = (ch & 4) ? 64.0f : 0.0f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    ln_merge(l1m[k], l1q[k], l2m[k], l2q[k], c2, n2);
+                    l1m[k] = l1q[k] = 0.0f;
+                }
+            }
+        }
     }
-    // chunks 2, 3 -> level 1 (64) -> level 2
-    chunk_into_l0(2, First{});
-    chunk_into_l0(3, Second{});
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        ln_merge<32, 32>(l0m[k], l0q[k], l1m[k], l1q[k]);
-        l0m[k] = l0q[k] = 0.0f;
-        ln_merge<0, 64>(l1m[k], l1q[k], l2m[k], l2q[k]);
-        l1m[k] = l1q[k] = 0.0f;
-    }
-    // chunks 4, 5 -> level 1 (32)
-    chunk_into_l0(4, First{});
-    chunk_into_l0(5, Second{});
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        ln_merge<0, 32>(l0m[k], l0q[k], l1m[k], l1q[k]);
-        l0m[k] = l0q[k] = 0.0f;
-    }
-    // chunks 6, 7 -> level 1 (64) -> level 2 (128)
-    chunk_into_l0(6, First{});
-    chunk_into_l0(7, Second{});
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        ln_merge<32, 32>(l0m[k], l0q[k], l1m[k], l1q[k]);
-        l0m[k] = l0q[k] = 0.0f;
-        ln_merge<64, 64>(l1m[k], l1q[k], l2m[k], l2q[k]);
-        l1m[k] = l1q[k] = 0.0f;
-        // final fold of the (now empty) levels into level 0
-        ln_merge<0, 0>(l1m[k], l1q[k], l0m[k], l0q[k]);
-        ln_merge<0, 128>(l2m[k], l2q[k], l0m[k], l0q[k]);
+        // final fold of the (now empty) level 1 and of level 2 into level 0
+        ln_merge(l1m[k], l1q[k], l0m[k], l0q[k], 0.0f, 0.0f);
+        ln_merge(l2m[k], l2q[k], l0m[k], l0q[k], 1.0f, 0.0f);
     }
     // four-lane merge, 128 samples each: c = 1, 1/2, 1/3, 1/4
     float mu = 0.0f, q = 0.0f;
