@@ -311,8 +311,8 @@ __global__ void __launch_bounds__(kClThreads, 1)
         sincos(static_cast<double>(phase), &sd, &cd);
         rope_s[threadIdx.x] = make_float2(__double2float_rn(cd), __double2float_rn(sd));
     }
-    if (threadIdx.x < kWidth / 4)
-        reinterpret_cast<float4*>(x_s)[threadIdx.x] = reinterpret_cast<const float4*>(p.in)[threadIdx.x];
+    // scalar loads: the caller's row need only be float-aligned, as on the other step paths
+    for (int i = threadIdx.x; i < kWidth; i += kClThreads) x_s[i] = p.in[i];
     if (rank == 0 && threadIdx.x < p.n_updates) {
         const int* u = p.updates + 3 * threadIdx.x;
         const_cast<int32_t*>(p.kv.table)[static_cast<size_t>(u[0]) * p.kv.max_pages + u[1]] = u[2];
