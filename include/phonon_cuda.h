@@ -160,7 +160,9 @@ void phonon_cuda_linear_destroy(PhononCudaLinear *linear);
  * (src/phonon_transformer.c:253-313, src/phonon_q8.c:64-92). */
 int phonon_cuda_linear_apply(PhononCudaLinear *linear, const float *x, size_t batch,
                              const float *bias, float *y);
-/* Same on device buffers, enqueued on `cuda_stream` (a cudaStream_t, may be 0). */
+/* Same on device buffers, enqueued on `cuda_stream` (a cudaStream_t, may be 0).
+ * x_dev must be 16-byte aligned (rows are read four floats at a time; cudaMalloc
+ * memory and whole-row offsets of it are), else PHONON_CUDA_INVALID_ARGUMENT. */
 int phonon_cuda_linear_apply_device(PhononCudaLinear *linear, const float *x_dev, size_t batch,
                                     const float *bias_dev, float *y_dev, int32_t *status_dev,
                                     void *cuda_stream);
@@ -178,7 +180,8 @@ int phonon_cuda_linear_apply_device(PhononCudaLinear *linear, const float *x_dev
  * by the int8 tcgen05 kernel. No cudaMalloc, cudaFree or other allocating
  * routine is called. Requirements: the linear has Q8_0 weights whose
  * 32-blocks share one scale per row and 512 or 2048 columns; batch <=
- * PHONON_CUDA_NOALLOC_MAX_BATCH (else PHONON_CUDA_CAPACITY). The first call
+ * PHONON_CUDA_NOALLOC_MAX_BATCH (else PHONON_CUDA_CAPACITY); x_dev 16-byte
+ * aligned, as for phonon_cuda_linear_apply_device. The first call
  * on a device looks up the scratch address on that device; make that first
  * call before any stream capture. Every call shares the one scratch array:
  * calls that overlap on the GPU (different streams or threads without

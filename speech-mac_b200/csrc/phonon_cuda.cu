@@ -2355,6 +2355,7 @@ int phonon_cuda_linear_apply_device_noalloc(PhononCudaLinear* l, const float* x_
                                             const float* bias_dev, float* y_dev, int32_t* status_dev,
                                             void* cuda_stream) {
     if (!l || !x_dev || !y_dev || batch == 0) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(x_dev) % 16) return PHONON_CUDA_INVALID_ARGUMENT;  // read as float4
     if (batch > PHONON_CUDA_NOALLOC_MAX_BATCH) {
         std::fprintf(stderr, "phonon_cuda_linear_apply_device_noalloc: batch %zu exceeds the scratch limit of %d\n",
                      batch, PHONON_CUDA_NOALLOC_MAX_BATCH);
@@ -2392,6 +2393,7 @@ int phonon_cuda_linear_apply_device_noalloc(PhononCudaLinear* l, const float* x_
 int phonon_cuda_linear_apply_device(PhononCudaLinear* l, const float* x_dev, size_t batch, const float* bias_dev,
                                     float* y_dev, int32_t* status_dev, void* cuda_stream) {
     if (!l || !x_dev || !y_dev || batch == 0 || batch > 65536) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(x_dev) % 16) return PHONON_CUDA_INVALID_ARGUMENT;  // rows are read as float4
     int st = set_device(l->device);
     if (st) return st;
     CUDA_TRY(launch_linear(l->lin, x_dev, static_cast<int>(batch), bias_dev, y_dev, status_dev,
