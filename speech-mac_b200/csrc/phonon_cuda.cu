@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -246,16 +247,18 @@ cudaError_t launch_gemv_t(const GemvParams& p, cudaStream_t s) {
     auto kern = gemv_kernel<kQ8, kChunks, kBT, kSrc, kEpi>;
     constexpr int smem = kBT * kChunks * 512 * 4;
     if constexpr (smem > 48 * 1024) {
-        // The opt-in shared memory size is a per-device function attribute.
-        static bool configured[kMaxDevices] = {};
+        // The opt-in shared memory size is a per-device function attribute:
+        // one bit per device that has it set.
+        static std::atomic<uint64_t> configured{0};
         int dev = 0;
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
-        if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
-        if (!configured[dev]) {
+        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+        const uint64_t bit = uint64_t{1} << dev;
+        if (!(configured.load(std::memory_order_acquire) & bit)) {
             e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (e != cudaSuccess) return e;
-            configured[dev] = true;
+            configured.fetch_or(bit, std::memory_order_release);
         }
     }
     const int rows_per_cta = kGemvWarps * kRowsPerWarp;
@@ -1349,7 +1352,8 @@ int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::v
     if ((st = upload_batch(c, s0, p0, updates, &b0, true, &c->lanes[0], c->d_status, grid))) return st;
     CUDA_TRY(cudaEventRecord(c->fork, c->stream));  // page updates and everything before this step
     CUDA_TRY(cudaStreamWaitEvent(L1.stream, c->fork, 0));
-    if ((st = upload_batch(c, s1, p1, {}, &b1, true, &L1, c->d_status + n0, grid))) return st;
+    st = upload_batch(c, s1, p1, {}, &b1, true, &L1, c->d_status + n0, grid);
+    if (st) return st;
     b0.split = b1.split = true;
     // The halves' launches are issued layer by layer, alternating, so that
     // the second half starts as soon as the first (issuing all of one half
