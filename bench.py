@@ -54,6 +54,39 @@ def measured_hbm_gbs():
         return HBM_FALLBACK_GBS, "fallback"
 
 
+# Useful int8 multiply-adds of the four projections per decoded frame, counted
+# as 2 ops each: 12 layers x (1536 + 512 + 2048) x 512 + 512 x 2048 weights.
+PROJ_OPS_PER_FRAME = 2 * N_LAYERS * (1536 * 512 + 512 * 512 + 2048 * 512 + 512 * 2048)
+BF16_FALLBACK_TFLOPS = 1590.0
+
+
+def measured_int8_tops():
+    """Dense int8 tensor peak: twice the measured dense bf16 GEMM rate (the
+    B200 tensor cores run int8 at twice the bf16 rate); the fallback figure
+    when no measurement exists."""
+    try:
+        return 2.0 * float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]), \
+            "2 x measured bf16 dense"
+    except Exception:
+        return 2.0 * BF16_FALLBACK_TFLOPS, "2 x fallback bf16 dense"
+
+
+def projection_roofline(prof, frames):
+    """The four projection stages of the profiled steps against the int8
+    tensor peak: useful ops (PROJ_OPS_PER_FRAME per frame, digit slicing not
+    counted) over the time of the qkv, out, up and down classes (on the
+    tensor-core path these include the LayerNorm/digit-slicing launches that
+    feed the GEMMs). None when the profile has no projection time."""
+    ms = sum(prof.get(k, {}).get("ms", 0.0) for k in ("qkv", "out", "up", "down"))
+    if ms <= 0.0 or frames <= 0:
+        return None
+    peak, kind = measured_int8_tops()
+    tops = PROJ_OPS_PER_FRAME * frames / (ms * 1e-3) / 1e12
+    return {"bound": "tensor", "achieved": round(tops, 1), "peak": round(peak, 1), "unit": "TOPS",
+            "frac": round(tops / peak, 4), "peak_source": kind, "ms": round(ms, 3),
+            "ops": "useful int8 ops, 2 per multiply-add of the four projections"}
+
+
 # ------------------------------------------------------------------ workload
 class ServingSim:
     """configs[3] arrival process, identical on every rank.
@@ -311,7 +344,7 @@ def run_ours(args):
     # the other half's launches, and its events would time both.
     prof_steps = min(args.steps, 60)
     ctx.set_batch_paths(split_min_batch=1 << 30)
-    _, prof_ms, _, prof, _ = timed(device_step, prof_steps, profile=True)
+    prof_frames, prof_ms, _, prof, _ = timed(device_step, prof_steps, profile=True)
     ctx.set_batch_paths()
     for _ in range(args.warmup):
         host_step()
@@ -360,6 +393,7 @@ def run_ours(args):
                          "kernels": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
                                          "gbs": round(v["bytes"] / max(v["ms"], 1e-9) * 1e-6, 1)}
                                      for k, v in prof.items() if v["launches"]}},
+            "projections": projection_roofline(prof, prof_frames),
             "e2e": {"value": round(e_tot / (e_max * 1e-3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": int(h2d / args.steps),
                     "d2h_bytes_per_step": int(d2h / args.steps)},
