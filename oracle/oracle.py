@@ -56,6 +56,58 @@ class OracleCache(C.Structure):
                 ("kv_bf16", C.c_int)]
 
 
+class OracleAffine(C.Structure):
+    _fields_ = [("w", OracleLinear), ("b", C.c_void_p)]
+
+
+HEAD_BLOCKS = 6
+
+
+class OracleFlowHead(C.Structure):
+    _fields_ = [("input", OracleAffine), ("cond", OracleAffine), ("time", (OracleAffine * 2) * 2),
+                ("time_freqs", C.c_void_p * 2), ("time_alpha", C.c_void_p * 2),
+                ("block_ada", OracleAffine * HEAD_BLOCKS), ("block_norm_w", C.c_void_p * HEAD_BLOCKS),
+                ("block_norm_b", C.c_void_p * HEAD_BLOCKS), ("block_mlp", (OracleAffine * 2) * HEAD_BLOCKS),
+                ("final_ada", OracleAffine), ("final_out", OracleAffine)]
+
+
+def flow_head_struct(head):
+    """OracleFlowHead over a flow head given as bf16 (uint16) arrays:
+    {"input", "cond", "final_ada", "final_out": (W [rows, cols], b [rows]),
+     "time": [[(W, b)] * 2] * 2, "time_freqs": [128] * 2, "time_alpha": [512] * 2,
+     "block_ada": [(W, b)] * 6, "block_norm_w"/"block_norm_b": [512] * 6,
+     "block_mlp": [[(W, b)] * 2] * 6}. The arrays must outlive the struct
+    (the caller keeps `head`)."""
+    def aff(wb):
+        w, b = wb
+        assert w.dtype == np.uint16 and b.dtype == np.uint16 and w.flags.c_contiguous
+        return OracleAffine(OracleLinear(2, w.shape[0], w.shape[1], w.ctypes.data), b.ctypes.data)
+
+    h = OracleFlowHead()
+    h.input, h.cond = aff(head["input"]), aff(head["cond"])
+    for i in range(2):
+        for j in range(2):
+            h.time[i][j] = aff(head["time"][i][j])
+        h.time_freqs[i] = head["time_freqs"][i].ctypes.data
+        h.time_alpha[i] = head["time_alpha"][i].ctypes.data
+    for k in range(HEAD_BLOCKS):
+        h.block_ada[k] = aff(head["block_ada"][k])
+        h.block_norm_w[k] = head["block_norm_w"][k].ctypes.data
+        h.block_norm_b[k] = head["block_norm_b"][k].ctypes.data
+        for j in range(2):
+            h.block_mlp[k][j] = aff(head["block_mlp"][k][j])
+    h.final_ada, h.final_out = aff(head["final_ada"]), aff(head["final_out"])
+    return h
+
+
+def _head_call(fn, head, condition, state, *scalars):
+    out = np.zeros(32, np.float32)
+    h = flow_head_struct(head)
+    ok = fn(C.byref(h), _ptr(np.ascontiguousarray(condition, np.float32)),
+            _ptr(np.ascontiguousarray(state, np.float32)), *[C.c_float(v) for v in scalars], _ptr(out))
+    return bool(ok), out
+
+
 class Oracle:
     """The C restatement."""
 
@@ -88,6 +140,20 @@ class Oracle:
                                         C.c_size_t, C.c_void_p, C.c_float, C.c_void_p]
         L.oracle_stack_step.argtypes = [C.POINTER(OracleLayer), C.c_size_t, C.POINTER(OracleCache),
                                         C.c_size_t, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p]
+        L.oracle_flow_head_forward.restype = C.c_int
+        L.oracle_flow_head_forward.argtypes = [C.POINTER(OracleFlowHead), C.c_void_p, C.c_void_p,
+                                               C.c_float, C.c_float, C.c_void_p]
+        L.oracle_flow_lsd_one_step.restype = C.c_int
+        L.oracle_flow_lsd_one_step.argtypes = [C.POINTER(OracleFlowHead), C.c_void_p, C.c_void_p,
+                                               C.c_float, C.c_void_p]
+
+    # flow head ---------------------------------------------------------------
+    def flow_head_forward(self, head, condition, state, s, t):
+        """(ok, velocity[32]) of the flow head (see flow_head_struct)."""
+        return _head_call(self.lib.oracle_flow_head_forward, head, condition, state, s, t)
+
+    def flow_lsd_one_step(self, head, condition, raw_noise, temperature):
+        return _head_call(self.lib.oracle_flow_lsd_one_step, head, condition, raw_noise, temperature)
 
     # primitives -------------------------------------------------------------
     def half_to_float(self, bits):
@@ -230,6 +296,12 @@ class Reference:
         L.ref_stream_fill.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_void_p]
         L.ref_stream_length.restype = C.c_size_t
         L.ref_stream_length.argtypes = [C.c_void_p]
+        L.ref_flow_head_forward.restype = C.c_int
+        L.ref_flow_head_forward.argtypes = [C.POINTER(OracleFlowHead), C.c_void_p, C.c_void_p,
+                                            C.c_float, C.c_float, C.c_void_p]
+        L.ref_flow_lsd_one_step.restype = C.c_int
+        L.ref_flow_lsd_one_step.argtypes = [C.POINTER(OracleFlowHead), C.c_void_p, C.c_void_p,
+                                            C.c_float, C.c_void_p]
         L.phonon_q8_dot.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
         L.phonon_q8_matvec.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p]
         L.phonon_layer_norm.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_float,
@@ -302,6 +374,14 @@ class Reference:
             raise RuntimeError("ref_model_prepare failed")
         return m
 
+
+    # flow head ---------------------------------------------------------------
+    def flow_head_forward(self, head, condition, state, s, t):
+        """(ok, velocity[32]) of the reference's phonon_flow_head_forward."""
+        return _head_call(self.lib.ref_flow_head_forward, head, condition, state, s, t)
+
+    def flow_lsd_one_step(self, head, condition, raw_noise, temperature):
+        return _head_call(self.lib.ref_flow_lsd_one_step, head, condition, raw_noise, temperature)
 
 class RefModel:
     def __init__(self, ref, weights, dtype=1):

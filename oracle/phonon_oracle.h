@@ -68,4 +68,34 @@ int oracle_stack_step(const OracleLayer *layers, size_t n_layers, OracleCache *c
                       size_t position, const float *input, float theta, float *output,
                       float *layer_outputs);
 
+/* ---- flow head (src/phonon_sampler.h:48-75): bf16 linears with bf16 biases ---- */
+#define ORACLE_HEAD_BLOCKS 6
+
+typedef struct {
+    OracleLinear w;     /* ORACLE_BF16 [rows, cols] */
+    const uint16_t *b;  /* bf16 [rows] */
+} OracleAffine;
+
+typedef struct {
+    OracleAffine input;                   /* [512, 32] latent state in */
+    OracleAffine cond;                    /* [512, 512] condition in */
+    OracleAffine time[2][2];              /* per flow time: [512, 256], [512, 512] */
+    const uint16_t *time_freqs[2];        /* bf16 [128] */
+    const uint16_t *time_alpha[2];        /* bf16 [512] */
+    OracleAffine block_ada[ORACLE_HEAD_BLOCKS];      /* [1536, 512]: shift, scale, gate */
+    const uint16_t *block_norm_w[ORACLE_HEAD_BLOCKS];  /* bf16 [512] */
+    const uint16_t *block_norm_b[ORACLE_HEAD_BLOCKS];
+    OracleAffine block_mlp[ORACLE_HEAD_BLOCKS][2];   /* [512, 512] x 2 */
+    OracleAffine final_ada;               /* [1024, 512]: shift, scale */
+    OracleAffine final_out;               /* [32, 512] velocity out */
+} OracleFlowHead;
+
+/* phonon_flow_head_forward (src/phonon_sampler.c:307-364): velocity of the
+ * flow at state for times s, t, conditioned on a transformer output row. */
+int oracle_flow_head_forward(const OracleFlowHead *head, const float condition[512],
+                             const float state[32], float s, float t, float velocity[32]);
+/* phonon_flow_lsd_one_step (src/phonon_sampler.c:366-393). */
+int oracle_flow_lsd_one_step(const OracleFlowHead *head, const float condition[512],
+                             const float raw_noise[32], float temperature, float output[32]);
+
 #endif

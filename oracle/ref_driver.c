@@ -227,3 +227,59 @@ int ref_stream_fill(RefStream *s, size_t n_layers, size_t length, const float *k
         s->caches[c].length = length;
     return 1;
 }
+
+/* ---- flow head (src/phonon_sampler.c) ----
+ * The head's bf16 arrays arrive in the oracle's OracleFlowHead layout and are
+ * wrapped in the reference's PhononTensorView contract (bf16 rank-2 linears,
+ * rank-1 vectors), then run through the reference's own functions. */
+#include "phonon_oracle.h"
+#include "phonon_sampler.h"
+
+static void set_vector(PhononTensorView *v, const uint16_t *data, size_t count) {
+    memset(v, 0, sizeof(*v));
+    v->dtype = PHONON_PACK_BF16;
+    v->rank = 1;
+    v->shape[0] = count;
+    v->data = data;
+    v->byte_count = count * 2;
+}
+
+static void set_affine(PhononTensorView *w, PhononTensorView *b, const OracleAffine *a) {
+    set_linear(w, 2, a->w.data, a->w.rows, a->w.cols);
+    set_vector(b, a->b, a->w.rows);
+}
+
+static void build_head(const OracleFlowHead *in, PhononFlowHead *h) {
+    memset(h, 0, sizeof(*h));
+    set_affine(&h->input_weight, &h->input_bias, &in->input);
+    set_affine(&h->cond_weight, &h->cond_bias, &in->cond);
+    for (size_t i = 0; i < 2; i++) {
+        for (size_t j = 0; j < 2; j++)
+            set_affine(&h->time_weight[i][j], &h->time_bias[i][j], &in->time[i][j]);
+        set_vector(&h->time_freqs[i], in->time_freqs[i], 128);
+        set_vector(&h->time_alpha[i], in->time_alpha[i], 512);
+    }
+    for (size_t b = 0; b < PHONON_FLOW_HEAD_BLOCKS; b++) {
+        set_affine(&h->block_ada_weight[b], &h->block_ada_bias[b], &in->block_ada[b]);
+        set_vector(&h->block_norm_weight[b], in->block_norm_w[b], 512);
+        set_vector(&h->block_norm_bias[b], in->block_norm_b[b], 512);
+        for (size_t j = 0; j < 2; j++)
+            set_affine(&h->block_mlp_weight[b][j], &h->block_mlp_bias[b][j], &in->block_mlp[b][j]);
+    }
+    set_affine(&h->final_ada_weight, &h->final_ada_bias, &in->final_ada);
+    set_affine(&h->final_weight, &h->final_bias, &in->final_out);
+}
+
+int ref_flow_head_forward(const OracleFlowHead *in, const float condition[512], const float state[32],
+                          float s, float t, float velocity[32]) {
+    PhononFlowHead h;
+    build_head(in, &h);
+    return phonon_flow_head_forward(&h, condition, state, s, t, velocity);
+}
+
+int ref_flow_lsd_one_step(const OracleFlowHead *in, const float condition[512], const float raw_noise[32],
+                          float temperature, float output[32]) {
+    PhononFlowHead h;
+    build_head(in, &h);
+    return phonon_flow_lsd_one_step(&h, condition, raw_noise, temperature, output);
+}

@@ -143,6 +143,18 @@ def main():
         "capacity": 2, "layer": 8, "position": 1, "key": "k[i]=i", "value": "v[i]=-i",
         "flat_index": (8 * 2 + 1) * 512 + 7, "expected": 7.0,
     }
+    # --- flow head (tests/test_phonon_sampler.c): a nonzero synthetic head whose
+    # weights, condition and state follow formulas in the test; the expected
+    # velocity comes from an independent PyTorch evaluation quoted there.
+    t = (ref / "tests/test_phonon_sampler.c").read_text()
+    exp, a, b = block(t, "const float expected[32] = {")
+    lo = t.index("static void test_nonzero_flow_head_against_independent_reference(void) {")
+    pins["flow_head_synthetic"] = {
+        "source": f"tests/test_phonon_sampler.c:{t[:lo].count(chr(10)) + 1}-{b + 7}",
+        "expected": parse_floats(exp),
+        "atol": 2e-4,
+        "s": 0.0, "t": 1.0,
+    }
     out = Path(__file__).with_name("pins.json")
     out.write_text(json.dumps(pins, indent=1, sort_keys=True) + "\n")
     print(f"wrote {out} ({out.stat().st_size} bytes)")
