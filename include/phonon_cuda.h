@@ -168,10 +168,11 @@ int phonon_cuda_linear_apply_device(PhononCudaLinear *linear, const float *x_dev
                                     void *cuda_stream);
 /* Allocation-free variant of phonon_cuda_linear_apply_device, for callers
  * that may not allocate device memory once they are running: a host thread
- * inside a real-time audio callback, code that runs while a CUDA graph is
- * being captured, or an engine whose device memory budget was fixed at start
- * up. It has no counterpart in the reference (the reference's linears are
- * host SGEMMs, src/phonon_transformer.c:253-313).
+ * inside a real-time audio callback (cudaMalloc can block for milliseconds
+ * and take driver locks an audio deadline cannot wait for), or an engine
+ * whose device memory budget was fixed at start-up and must not grow. It has
+ * no counterpart in the reference (the reference's linears are host SGEMMs,
+ * src/phonon_transformer.c:253-313).
  *
  * It runs the tensor-core path: the batch is digit-sliced into a scratch
  * array that the library owns as a file-scope device array (sized for
@@ -185,7 +186,11 @@ int phonon_cuda_linear_apply_device(PhononCudaLinear *linear, const float *x_dev
  * on a device looks up the scratch address on that device; make that first
  * call before any stream capture. Every call shares the one scratch array:
  * calls that overlap on the GPU (different streams or threads without
- * ordering) race and corrupt each other's results. */
+ * ordering) race and corrupt each other's results. When a bounded wait inside
+ * the tensor-core kernel expires (about two seconds; see
+ * phonon_cuda_wait_expiry_probe), the rows of y_dev are not written and every
+ * status_dev[b], b < batch, is set to PHONON_CUDA_DEVICE_ERROR (pass
+ * status_dev to learn of it: the call itself returns before the GPU runs). */
 #define PHONON_CUDA_NOALLOC_MAX_BATCH 64
 int phonon_cuda_linear_apply_device_noalloc(PhononCudaLinear *linear, const float *x_dev,
                                             size_t batch, const float *bias_dev, float *y_dev,
@@ -219,9 +224,12 @@ int phonon_cuda_i8_gemm(int device, const int8_t *a, const int8_t *b, size_t m, 
  * the kernel finish; the call then returns PHONON_CUDA_DEVICE_ERROR and the
  * context stays usable. This entry point runs those wait routines with a
  * budget of budget_us microseconds on something nothing completes: kind 0,
- * an mbarrier; kind 1, a grid barrier that one CTA never reaches. It returns
+ * an mbarrier; kind 1, a grid barrier that one CTA never reaches; kind 2,
+ * an mbarrier whose expiry is reported through the error flag of the
+ * allocation-free entry point's scratch, which must then reach all four
+ * status words of a call as PHONON_CUDA_DEVICE_ERROR. It returns
  * PHONON_CUDA_DEVICE_ERROR when the wait expired and reported it (the
- * expected outcome), and the wall time of the kernel in *elapsed_ns. */
+ * expected outcome), and the wall time of the wait kernel in *elapsed_ns. */
 int phonon_cuda_wait_expiry_probe(int device, int kind, uint32_t budget_us, uint64_t *elapsed_ns);
 
 /* ---- live kernel profiling (CUDA events on the context's stream) ---- */
@@ -285,6 +293,20 @@ int phonon_cuda_set_batch_paths(PhononCuda *ctx, uint32_t fused_min_batch, uint3
  * Projections and appended K/V rows equal the other paths' bit for bit; the
  * attention merges its partial sums in another order (within rounding). */
 int phonon_cuda_set_cluster_step(PhononCuda *ctx, uint32_t max_position, int *available);
+
+/* ---- per-layer output trace (test instrumentation) ----
+ * trace_dev: device memory of [n_layers][max_rows][512] fp32, or NULL to
+ * switch the trace off. While it is set, every decode step
+ * (phonon_cuda_step, phonon_cuda_step_device) also writes each layer's output
+ * rows there: row i of the batch after layer l at
+ * trace_dev[(l * max_rows + i) * 512]. A step takes the same path as without
+ * the trace (the per-stage path launches its kernels directly instead of
+ * replaying a graph and adds one device copy per layer; the persistent and
+ * cluster kernels store the rows themselves). A step of more than max_rows
+ * streams is PHONON_CUDA_INVALID_ARGUMENT; max_rows must be 1..max_batch.
+ * No counterpart in the reference: it lets tests compare every layer of a
+ * batched step with a CPU layer step given the same input and K/V rows. */
+int phonon_cuda_set_layer_trace(PhononCuda *ctx, float *trace_dev, uint32_t max_rows);
 
 const char *phonon_cuda_status_string(int status);
 

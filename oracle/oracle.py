@@ -26,6 +26,14 @@ Q8_BYTES_PER_32 = 34
 LINEAR_SHAPES = {"qkv": (1536, 512), "out": (512, 512), "up": (2048, 512), "down": (512, 2048)}
 
 
+def reference_root():
+    """The speech-mac source tree: $PHONON_REFERENCE_ROOT, else a `reference`
+    directory beside the repository checkout (it exists only where the oracle
+    is built, never on the GPU box)."""
+    env = os.environ.get("PHONON_REFERENCE_ROOT")
+    return Path(env) if env else HERE.parent.parent / "reference"
+
+
 def build(ref_root=None):
     """Compile liboracle.so and, when the reference tree exists, _ref/."""
     cmd = f"make -s -C {HERE}"
@@ -120,7 +128,7 @@ class Oracle:
         for name in ["oracle_q8_dot", "oracle_q8_matvec", "oracle_linear_batch",
                      "oracle_layer_norm", "oracle_rms_norm", "oracle_erf_gelu",
                      "oracle_rope_interleaved", "oracle_attention", "oracle_cache_init",
-                     "oracle_layer_step", "oracle_stack_step"]:
+                     "oracle_layer_step", "oracle_layer_step_forced", "oracle_stack_step"]:
             getattr(L, name).restype = C.c_int
         L.oracle_q8_dot.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]
         L.oracle_q8_matvec.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p]
@@ -138,6 +146,9 @@ class Oracle:
         L.oracle_cache_destroy.argtypes = [C.POINTER(OracleCache)]
         L.oracle_layer_step.argtypes = [C.POINTER(OracleLayer), C.POINTER(OracleCache), C.c_size_t,
                                         C.c_size_t, C.c_void_p, C.c_float, C.c_void_p]
+        L.oracle_layer_step_forced.argtypes = [C.POINTER(OracleLayer), C.POINTER(OracleCache),
+                                               C.c_size_t, C.c_size_t, C.c_void_p, C.c_float,
+                                               C.c_void_p, C.c_void_p, C.c_void_p]
         L.oracle_stack_step.argtypes = [C.POINTER(OracleLayer), C.c_size_t, C.POINTER(OracleCache),
                                         C.c_size_t, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p]
         L.oracle_flow_head_forward.restype = C.c_int
@@ -254,6 +265,29 @@ class OracleModel:
                                           position, _ptr(np.ascontiguousarray(x, np.float32)),
                                           theta, _ptr(out))
         return ok, out
+
+    def layer_step_forced(self, cache, layer, position, x, theta=10000.0):
+        """Layer step whose K/V row at `position` is the one already in the
+        cache (teacher-forced append); returns (ok, y, k, v) with the rows the
+        oracle itself computes. Sets cache.length = position first."""
+        out = np.zeros(512, np.float32)
+        k = np.zeros(512, np.float32)
+        v = np.zeros(512, np.float32)
+        cache.length = position
+        ok = self.o.lib.oracle_layer_step_forced(C.byref(self.layers[layer]), C.byref(cache), layer,
+                                                 position, _ptr(np.ascontiguousarray(x, np.float32)),
+                                                 theta, _ptr(out), _ptr(k), _ptr(v))
+        return ok, out, k, v
+
+    def load_kv(self, cache, keys, values):
+        """Rows [0, count) of every layer from keys/values [n_layers][count][512]."""
+        n_layers, count = keys.shape[0], keys.shape[1]
+        assert n_layers == cache.n_layers and count <= cache.capacity
+        shape = (cache.n_layers, cache.capacity, 512)
+        ck = np.ctypeslib.as_array(cache.keys, shape=(cache.n_layers * cache.capacity * 512,)).reshape(shape)
+        cv = np.ctypeslib.as_array(cache.values, shape=(cache.n_layers * cache.capacity * 512,)).reshape(shape)
+        ck[:, :count] = keys
+        cv[:, :count] = values
 
     def kv(self, cache, layer, position):
         n = cache.capacity * 512

@@ -499,8 +499,9 @@ void oracle_cache_destroy(OracleCache *cache) {
 /* Pre-LN block: LN1 -> QKV -> RoPE(q,k) -> append -> 8-head attention over
  * position+1 keys -> out proj -> +x -> LN2 -> up -> GELU -> down -> +residual
  * (src/phonon_transformer.c:406-453). */
-int oracle_layer_step(const OracleLayer *w, OracleCache *cache, size_t layer, size_t position,
-                      const float *input, float theta, float *output) {
+static int layer_step(const OracleLayer *w, OracleCache *cache, size_t layer, size_t position,
+                      const float *input, float theta, float *output, int keep_row, float *k_out,
+                      float *v_out) {
     if (!w || !cache || !input || !output || layer >= cache->n_layers ||
         position >= cache->capacity || position >= ORACLE_MAX_POSITIONS ||
         cache->length != position)
@@ -519,14 +520,20 @@ int oracle_layer_step(const OracleLayer *w, OracleCache *cache, size_t layer, si
     for (size_t i = 0; i < 512; i++)
         if (!isfinite(k[i]) || !isfinite(v[i]))
             return 0;
-    size_t base = layer * cache->capacity * 512;
-    memcpy(cache->keys + base + position * 512, k, 512 * sizeof(float));
-    memcpy(cache->values + base + position * 512, v, 512 * sizeof(float));
     if (cache->kv_bf16) /* bf16 KV pages (benchmark configs[3]): one rounding on append */
         for (size_t i = 0; i < 512; i++) {
-            cache->keys[base + position * 512 + i] = round_bf16(k[i]);
-            cache->values[base + position * 512 + i] = round_bf16(v[i]);
+            k[i] = round_bf16(k[i]);
+            v[i] = round_bf16(v[i]);
         }
+    if (k_out)
+        memcpy(k_out, k, 512 * sizeof(float));
+    if (v_out)
+        memcpy(v_out, v, 512 * sizeof(float));
+    size_t base = layer * cache->capacity * 512;
+    if (!keep_row) {
+        memcpy(cache->keys + base + position * 512, k, 512 * sizeof(float));
+        memcpy(cache->values + base + position * 512, v, 512 * sizeof(float));
+    }
     for (size_t h = 0; h < 8; h++)
         if (!oracle_attention(q + h * 64, cache->keys + base + h * 64,
                               cache->values + base + h * 64, position + 1, 512,
@@ -546,6 +553,21 @@ int oracle_layer_step(const OracleLayer *w, OracleCache *cache, size_t layer, si
             return 0;
     }
     return 1;
+}
+
+int oracle_layer_step(const OracleLayer *w, OracleCache *cache, size_t layer, size_t position,
+                      const float *input, float theta, float *output) {
+    return layer_step(w, cache, layer, position, input, theta, output, 0, NULL, NULL);
+}
+
+/* Test hook (teacher forcing of the K/V append): the same layer step, but
+ * the row at `position` is the one the caller left in the cache (a device's
+ * appended row) instead of the row this step computes; the computed rows
+ * (bf16-rounded in a bf16 cache) go to k_out / v_out. */
+int oracle_layer_step_forced(const OracleLayer *w, OracleCache *cache, size_t layer,
+                             size_t position, const float *input, float theta, float *output,
+                             float *k_out, float *v_out) {
+    return layer_step(w, cache, layer, position, input, theta, output, 1, k_out, v_out);
 }
 
 /* All layers in order, then one commit of the position

@@ -63,6 +63,11 @@ int oracle_cache_init(OracleCache *cache, size_t n_layers, size_t capacity);
 void oracle_cache_destroy(OracleCache *cache);
 int oracle_layer_step(const OracleLayer *w, OracleCache *cache, size_t layer, size_t position,
                       const float *input, float theta, float *output);
+/* The layer step with the K/V row at `position` taken from the cache as the
+ * caller left it; the rows the step computes go to k_out / v_out (test hook). */
+int oracle_layer_step_forced(const OracleLayer *w, OracleCache *cache, size_t layer,
+                             size_t position, const float *input, float theta, float *output,
+                             float *k_out, float *v_out);
 /* Full step over n_layers; layer_outputs (optional) receives [n_layers][512]. */
 int oracle_stack_step(const OracleLayer *layers, size_t n_layers, OracleCache *cache,
                       size_t position, const float *input, float theta, float *output,

@@ -118,6 +118,8 @@ struct ClusterParams {
     int updates[3 * kClMaxUpdates];
     const float* freq;           // [32] RoPE inverse frequencies
     KvView kv;
+    float* trace;                // optional: layer l's output row at trace[l * trace_stride]
+    int trace_stride;
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -632,6 +634,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 const int rr = lane & 3, r = 32 * rank + 4 * warp + rr;
                 const float v = __fadd_rn(h_s[r], pick4(s, rr));
                 if (lane < 4 && !isfinite(v)) flag_nonfinite(p.status, 0);
+                if (p.trace && lane < 4) p.trace[static_cast<size_t>(l) * p.trace_stride + r] = v;
                 if (last_layer) {
                     if (lane < 4) p.out[r] = v;
                 } else {

@@ -242,24 +242,37 @@ int upload_linear(int kind, const void* host, size_t rows, size_t cols, DevLinea
 }
 
 // ------------------------------------------------------------- GEMV launcher
+// The opt-in shared memory size is a per-device function attribute: one bit
+// per device of `configured` records that it is set (host threads may race
+// here; setting the attribute twice is harmless).
+cudaError_t opt_in_smem(const void* kern, int smem, std::atomic<uint64_t>& configured) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    const uint64_t bit = uint64_t{1} << dev;
+    if (!(configured.load(std::memory_order_acquire) & bit)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        configured.fetch_or(bit, std::memory_order_release);
+    }
+    return cudaSuccess;
+}
+
+template <int kEpi>
+std::atomic<uint64_t>& gemm_configured() {
+    static std::atomic<uint64_t> configured{0};
+    return configured;
+}
+
 template <bool kQ8, int kChunks, int kBT, int kSrc, int kEpi>
 cudaError_t launch_gemv_t(const GemvParams& p, cudaStream_t s) {
     auto kern = gemv_kernel<kQ8, kChunks, kBT, kSrc, kEpi>;
     constexpr int smem = kBT * kChunks * 512 * 4;
     if constexpr (smem > 48 * 1024) {
-        // The opt-in shared memory size is a per-device function attribute:
-        // one bit per device that has it set.
         static std::atomic<uint64_t> configured{0};
-        int dev = 0;
-        cudaError_t e = cudaGetDevice(&dev);
+        const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(kern), smem, configured);
         if (e != cudaSuccess) return e;
-        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-        const uint64_t bit = uint64_t{1} << dev;
-        if (!(configured.load(std::memory_order_acquire) & bit)) {
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            if (e != cudaSuccess) return e;
-            configured.fetch_or(bit, std::memory_order_release);
-        }
     }
     const int rows_per_cta = kGemvWarps * kRowsPerWarp;
     return launch_pdl(kern, dim3((p.rows + rows_per_cta - 1) / rows_per_cta), dim3(kGemvWarps * 32), smem, s, p);
@@ -309,33 +322,17 @@ cudaError_t launch_linear(const DevLinear& l, const float* x, int B, const float
 template <int kEpi>
 cudaError_t launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, int rows, int n_digit_rows, const GemmParams& p,
                         cudaStream_t s) {
-    static bool configured[kMaxDevices] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(i8_gemm_kernel<kEpi>), kGemmSmem, gemm_configured<kEpi>());
     if (e != cudaSuccess) return e;
-    if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
-        e = cudaFuncSetAttribute(i8_gemm_kernel<kEpi>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
-        if (e != cudaSuccess) return e;
-        configured[dev] = true;
-    }
     dim3 grid((rows + kGemmM - 1) / kGemmM, (n_digit_rows + kGemmN - 1) / kGemmN);
     return launch_pdl(i8_gemm_kernel<kEpi>, grid, dim3(kGemmThreads), kGemmSmem, s, tw, tx, p);
 }
 
 template <bool kBf16>
 cudaError_t launch_attn_tma(const CUtensorMap& tm, const AttnParams& p, int32_t* err, int n_ctas, cudaStream_t s) {
-    static bool configured[kMaxDevices] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static std::atomic<uint64_t> configured{0};
+    cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(attn_tma_kernel<kBf16>), AttnTma<kBf16>::kSmem, configured);
     if (e != cudaSuccess) return e;
-    if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
-    if (!configured[dev]) {
-        e = cudaFuncSetAttribute(attn_tma_kernel<kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 AttnTma<kBf16>::kSmem);
-        if (e != cudaSuccess) return e;
-        configured[dev] = true;
-    }
     return launch_pdl(attn_tma_kernel<kBf16>, dim3(n_ctas), dim3(kAttnTmaThreads), AttnTma<kBf16>::kSmem, s, tm, p, err);
 }
 
@@ -463,6 +460,10 @@ struct PhononCuda {
     double prof_ms[PHONON_CUDA_K_COUNT] = {};
     double prof_bytes[PHONON_CUDA_K_COUNT] = {};
     uint64_t prof_launches[PHONON_CUDA_K_COUNT] = {};
+    // per-layer output trace of decode steps (phonon_cuda_set_layer_trace)
+    float* trace = nullptr;
+    uint32_t trace_rows = 0;
+    bool tracing = false;  // inside a traced decode step
     // pending phonon_cuda_step_device
     bool pending = false;
     std::vector<uint32_t> pending_streams;
@@ -587,6 +588,7 @@ struct Batch {
     int R = 0, S = 0, U = 0;
     bool persist = false;  // whole step in step_persist_kernel
     bool split = false;    // one lane's share of a step split over two lanes
+    int row0 = 0;          // first row of this batch within the step (the second lane's half)
     Lane* lane = nullptr;
     int32_t* d_status = nullptr;  // status words of this batch's entries
     double keys = 0;  // sum over entries of (position + 1)
@@ -1087,12 +1089,22 @@ void drop_graph(PhononCuda* c) {
     c->last_shape = PhononCuda::StepShape{};
 }
 
+// Test instrumentation (phonon_cuda_set_layer_trace): layer l's output rows
+// of batch b into the trace, on the batch's stream.
+int trace_layer(PhononCuda* c, const Batch& b, int l, const float* out) {
+    if (!c->tracing) return PHONON_CUDA_OK;
+    CUDA_TRY(cudaMemcpyAsync(c->trace + (static_cast<size_t>(l) * c->trace_rows + b.row0) * kWidth, out,
+                             static_cast<size_t>(b.R) * kWidth * 4, cudaMemcpyDeviceToDevice, b.lane->stream));
+    return PHONON_CUDA_OK;
+}
+
 int enqueue_layers_direct(PhononCuda* c, const Batch& b, const float* in, float* final_out) {
     const int L = static_cast<int>(c->cfg.n_layers);
     const float* cur = in;
     for (int l = 0; l < L; ++l) {
         float* out = (l == L - 1) ? final_out : ((cur == b.lane->x0) ? b.lane->x1 : b.lane->x0);
-        const int st = enqueue_layer(c, b, l, cur, out);
+        int st = enqueue_layer(c, b, l, cur, out);
+        if (st == PHONON_CUDA_OK) st = trace_layer(c, b, l, out);
         if (st != PHONON_CUDA_OK) return st;
         cur = out;
     }
@@ -1201,6 +1213,8 @@ int enqueue_persist(PhononCuda* c, const Batch& b, const float* in, float* final
     pp.off_norm = sh.off_norm;
     pp.off_bar = sh.off_bar;
     pp.ring = sh.ring;
+    pp.trace = c->tracing ? c->trace : nullptr;
+    pp.trace_rows = static_cast<int>(c->trace_rows);
     double weights = 0.0;
     for (const DevLayer& D : c->layers)
         weights += linear_bytes(D.qkv) + linear_bytes(D.out) + linear_bytes(D.up) + linear_bytes(D.down);
@@ -1274,6 +1288,8 @@ int enqueue_cluster(PhononCuda* c, int32_t slot, int32_t pos, const std::vector<
     for (size_t i = 0; i < updates.size(); ++i) cp.updates[i] = updates[i];
     cp.freq = c->d_freq;
     cp.kv = kv_view(c);
+    cp.trace = c->tracing ? c->trace : nullptr;
+    cp.trace_stride = static_cast<int>(c->trace_rows) * kWidth;
     double weights = 0.0;
     for (const DevLayer& D : c->layers)
         weights += linear_bytes(D.qkv) + linear_bytes(D.out) + linear_bytes(D.up) + linear_bytes(D.down);
@@ -1295,7 +1311,7 @@ int enqueue_stack(PhononCuda* c, const Batch& b, const float* in, float* final_o
                   PhononCudaCancelPoll cancel, void* cctx, const std::vector<int>* polls_per_layer,
                   bool* cancelled) {
     if (b.persist) return enqueue_persist(c, b, in, final_out);
-    if (!cancel && !c->prof_on && !b.split) return enqueue_layers_graphed(c, b, in, final_out);
+    if (!cancel && !c->prof_on && !b.split && !c->tracing) return enqueue_layers_graphed(c, b, in, final_out);
     if (!cancel) return enqueue_layers_direct(c, b, in, final_out);
     const int L = static_cast<int>(c->cfg.n_layers);
     const float* cur = in;
@@ -1309,7 +1325,8 @@ int enqueue_stack(PhononCuda* c, const Batch& b, const float* in, float* final_o
                 }
         }
         float* out = (l == L - 1) ? final_out : ((cur == b.lane->x0) ? b.lane->x1 : b.lane->x0);
-        const int st = enqueue_layer(c, b, l, cur, out);
+        int st = enqueue_layer(c, b, l, cur, out);
+        if (st == PHONON_CUDA_OK) st = trace_layer(c, b, l, out);
         if (st != PHONON_CUDA_OK) return st;
         cur = out;
     }
@@ -1331,9 +1348,9 @@ int set_device(int device) {
 // lanes, so that one half's attention (HBM-bound) overlaps the other half's
 // projections (latency-bound); everything else runs one launch per stage.
 // Page-table updates are applied by the first lane before the second starts.
-int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::vector<int32_t>& pos,
-                   const std::vector<int32_t>& updates, const float* in, float* out, PhononCudaCancelPoll cancel,
-                   void* cctx, bool* cancelled) {
+int enqueue_decode_paths(PhononCuda* c, const std::vector<int32_t>& slot, const std::vector<int32_t>& pos,
+                         const std::vector<int32_t>& updates, const float* in, float* out,
+                         PhononCudaCancelPoll cancel, void* cctx, bool* cancelled) {
     const int n = static_cast<int>(slot.size());
     if (use_cluster(c, n, pos, updates, cancel != nullptr)) return enqueue_cluster(c, slot[0], pos[0], updates, in, out);
     const bool persist = use_persist(c, n, cancel != nullptr);
@@ -1355,6 +1372,7 @@ int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::v
     st = upload_batch(c, s1, p1, {}, &b1, true, &L1, c->d_status + n0, grid);
     if (st) return st;
     b0.split = b1.split = true;
+    b1.row0 = n0;
     // The halves' launches are issued layer by layer, alternating, so that
     // the second half starts as soon as the first (issuing all of one half
     // first delays the other by the host time of ~100 launches).
@@ -1368,12 +1386,25 @@ int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::v
                 const Batch& b = *bs[k];
                 float* o = (l == L - 1) ? fin[k] : ((cur[k] == b.lane->x0) ? b.lane->x1 : b.lane->x0);
                 if ((st = enqueue_layer(c, b, l, cur[k], o))) return st;
+                if ((st = trace_layer(c, b, l, o))) return st;
                 cur[k] = o;
             }
     }
     CUDA_TRY(cudaEventRecord(c->join, L1.stream));
     CUDA_TRY(cudaStreamWaitEvent(c->stream, c->join, 0));
     return PHONON_CUDA_OK;
+}
+
+// A decode step on the paths above; with a layer trace set, every layer's
+// output rows are copied into it as well.
+int enqueue_decode(PhononCuda* c, const std::vector<int32_t>& slot, const std::vector<int32_t>& pos,
+                   const std::vector<int32_t>& updates, const float* in, float* out, PhononCudaCancelPoll cancel,
+                   void* cctx, bool* cancelled) {
+    if (c->trace && slot.size() > c->trace_rows) return PHONON_CUDA_INVALID_ARGUMENT;
+    c->tracing = c->trace != nullptr;
+    const int st = enqueue_decode_paths(c, slot, pos, updates, in, out, cancel, cctx, cancelled);
+    c->tracing = false;
+    return st;
 }
 
 // Upload the per-layer weight pointers of step_persist_kernel and decide
@@ -1477,6 +1508,10 @@ int prefill_polls_per_layer(size_t length) {
     }
     return static_cast<int>(3 + 8 * attn);
 }
+
+// Kind 2 of phonon_cuda_wait_expiry_probe (defined with the allocation-free
+// entry point, whose scratch it uses).
+int noalloc_expiry_probe(int device, uint32_t budget_us, uint64_t* elapsed_ns);
 
 }  // namespace
 
@@ -1752,9 +1787,10 @@ uint64_t phonon_cuda_launch_count(PhononCuda* c) {
 }
 
 int phonon_cuda_wait_expiry_probe(int device, int kind, uint32_t budget_us, uint64_t* elapsed_ns) {
-    if ((kind != 0 && kind != 1) || budget_us == 0 || budget_us > 1000000) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (kind < 0 || kind > 2 || budget_us == 0 || budget_us > 1000000) return PHONON_CUDA_INVALID_ARGUMENT;
     int st = set_device(device);
     if (st) return st;
+    if (kind == 2) return noalloc_expiry_probe(device, budget_us, elapsed_ns);
     int32_t* d_err = nullptr;
     unsigned* d_ctr = nullptr;
     cudaEvent_t a = nullptr, b = nullptr;
@@ -1808,6 +1844,15 @@ int phonon_cuda_debug_cluster_trace(unsigned long long* out) {
                                                                                              : PHONON_CUDA_DEVICE_ERROR;
 }
 #endif
+
+int phonon_cuda_set_layer_trace(PhononCuda* c, float* trace_dev, uint32_t max_rows) {
+    if (!c || (trace_dev && (max_rows == 0 || max_rows > c->cfg.max_batch))) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    c->trace = trace_dev;
+    c->trace_rows = trace_dev ? max_rows : 0;
+    return PHONON_CUDA_OK;
+}
 
 int phonon_cuda_set_cluster_step(PhononCuda* c, uint32_t max_position, int* available) {
     if (!c) return PHONON_CUDA_INVALID_ARGUMENT;
@@ -2315,6 +2360,15 @@ static __device__ __align__(256) int32_t g_noalloc_error[1];
 
 namespace {
 
+// After the tensor-core kernel of an allocation-free call: when one of its
+// bounded waits expired (the flag in the scratch), the rows of y were not
+// written, and every status word of the call says so.
+__global__ void noalloc_report_kernel(const int32_t* error, int32_t* status, int B) {
+    pdl_wait();
+    if (*error)
+        for (int b = threadIdx.x; b < B; b += blockDim.x) status[b] = PHONON_CUDA_DEVICE_ERROR;
+}
+
 struct NoallocScratch {
     bool ready = false;
     int8_t* digits = nullptr;
@@ -2349,6 +2403,47 @@ int noalloc_scratch(int device, NoallocScratch** out) {
     }
     *out = &t;
     return PHONON_CUDA_OK;
+}
+
+// An mbarrier wait that nothing completes expires against the scratch's error
+// flag, then the report kernel marks the status words of a 4-row call: the
+// path by which an expired wait inside the tensor-core kernel reaches the
+// caller of phonon_cuda_linear_apply_device_noalloc. DEVICE_ERROR when every
+// status word reads PHONON_CUDA_DEVICE_ERROR (the expected outcome).
+int noalloc_expiry_probe(int device, uint32_t budget_us, uint64_t* elapsed_ns) {
+    NoallocScratch* sc = nullptr;
+    int st = noalloc_scratch(device, &sc);
+    if (st) return st;
+    constexpr int kRows = 4;
+    int32_t* d_status = nullptr;
+    cudaEvent_t a = nullptr, b = nullptr;
+    int clock_khz = 0;
+    int result = PHONON_CUDA_DEVICE_ERROR;
+    if (cudaMalloc(&d_status, kRows * 4) == cudaSuccess && cudaMemset(d_status, 0, kRows * 4) == cudaSuccess &&
+        cudaMemset(sc->error, 0, 4) == cudaSuccess && cudaEventCreate(&a) == cudaSuccess &&
+        cudaEventCreate(&b) == cudaSuccess &&
+        cudaDeviceGetAttribute(&clock_khz, cudaDevAttrClockRate, device) == cudaSuccess) {
+        const long long budget = static_cast<long long>(budget_us) * clock_khz / 1000;
+        cudaEventRecord(a);
+        wait_expiry_kernel<<<2, 32>>>(0, budget, sc->error, nullptr);
+        cudaEventRecord(b);
+        noalloc_report_kernel<<<1, 64>>>(sc->error, d_status, kRows);
+        int32_t status[kRows] = {};
+        float ms = 0.0f;
+        if (cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+            cudaMemcpy(status, d_status, sizeof(status), cudaMemcpyDeviceToHost) == cudaSuccess &&
+            cudaEventElapsedTime(&ms, a, b) == cudaSuccess) {
+            if (elapsed_ns) *elapsed_ns = static_cast<uint64_t>(ms * 1e6);
+            bool all = true;
+            for (int i = 0; i < kRows; ++i) all &= status[i] == PHONON_CUDA_DEVICE_ERROR;
+            result = all ? PHONON_CUDA_DEVICE_ERROR : PHONON_CUDA_OK;
+        }
+        cudaMemset(sc->error, 0, 4);
+    }
+    if (a) cudaEventDestroy(a);
+    if (b) cudaEventDestroy(b);
+    if (d_status) cudaFree(d_status);
+    return result;
 }
 
 }  // namespace
@@ -2391,6 +2486,7 @@ int phonon_cuda_linear_apply_device_noalloc(PhononCudaLinear* l, const float* x_
     p.error = sc->error;
     p.bias = bias_dev;
     CUDA_TRY(launch_gemm<GEPI_STORE>(w.tmap, w.cols == 512 ? sc->map512 : sc->map2048, w.rows, kDigits * Bpad, p, s));
+    if (status_dev) CUDA_TRY(launch_pdl(noalloc_report_kernel, dim3(1), dim3(64), 0, s, sc->error, status_dev, B));
     return PHONON_CUDA_OK;
 }
 

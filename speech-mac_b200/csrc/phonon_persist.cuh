@@ -110,6 +110,8 @@ struct PersistParams {
     KvView kv;                 // kv.table is written in stage 0 (page updates)
     int off_x, off_w0, off_w1, off_norm, off_bar;  // shared-memory offsets from the 1024-aligned base
     int ring;                  // stage-B ring stages (2..kPersistMaxRing)
+    float* trace;              // optional [n_layers][trace_rows][512]: every layer's output rows
+    int trace_rows;
 };
 
 struct RowSlice {
@@ -643,6 +645,11 @@ __global__ void __launch_bounds__(kPersistThreads, 1)
         PERSIST_MARK(l, 13);
         grid_sync(p, epoch, failed);
         PERSIST_MARK(l, 14);
+        if (p.trace) {  // test instrumentation: this layer's output rows (written by other CTAs: via L2)
+            float* dst = p.trace + static_cast<size_t>(l) * p.trace_rows * kWidth;
+            for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.R * kWidth; i += gridDim.x * blockDim.x)
+                dst[i] = __ldcg(next + i);
+        }
     }
 
     // Copies still in flight (only after a failure) land before the CTA exits.

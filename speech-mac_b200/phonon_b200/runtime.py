@@ -79,6 +79,7 @@ def lib():
         "phonon_cuda_profile_read": [P, P, P, P],
         "phonon_cuda_set_batch_paths": [P, U32, U32, U32, U32],
         "phonon_cuda_set_cluster_step": [P, U32, C.POINTER(C.c_int)],
+        "phonon_cuda_set_layer_trace": [P, P, U32],
         "phonon_cuda_wait_expiry_probe": [C.c_int, C.c_int, U32, C.POINTER(C.c_uint64)],
     }
     for name, args in sig.items():
@@ -260,6 +261,13 @@ class Context:
         available = C.c_int(0)
         check(self.L.phonon_cuda_set_cluster_step(self.h, max_position, C.byref(available)), "set_cluster_step")
         return bool(available.value)
+
+    def set_layer_trace(self, trace_ptr, max_rows):
+        """Every later decode step also writes each layer's output rows into
+        device memory at trace_ptr ([n_layers][max_rows][512] fp32); a null
+        pointer (0 / None) switches the trace off."""
+        check(self.L.phonon_cuda_set_layer_trace(self.h, C.c_void_p(trace_ptr or None),
+                                                 max_rows if trace_ptr else 0), "set_layer_trace")
 
     def layer_step(self, s, layer, position, x):
         x = np.ascontiguousarray(x, np.float32)

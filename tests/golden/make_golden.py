@@ -1,6 +1,7 @@
 """Extract the speech-mac model-free pins into tests/golden/pins.json.
 
-Run in a checkout that has the reference tree (default /root/reference):
+Run in a checkout that has the reference tree ($PHONON_REFERENCE_ROOT, else a
+`reference` directory beside the repository):
 
     python tests/golden/make_golden.py [REF_ROOT]
 
@@ -38,7 +39,9 @@ def block(text, start_pat, end_pat="};"):
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+    from oracle.oracle import reference_root
+    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_root()
     pins = {}
 
     # --- GELU (tests/test_phonon_transformer.c) ---

@@ -58,7 +58,8 @@ def test_tensor_view_layout():
 def test_reference_test_compiles_against_dropin(tmp_path, test):
     """Where the speech-mac tree exists, its own Q8 test links unchanged
     against the drop-in headers and library (linked, not run: no GPU)."""
-    src = Path("/root/reference/tests") / test
+    from oracle.oracle import reference_root
+    src = reference_root() / "tests" / test
     if not src.exists():
         pytest.skip("speech-mac tree not present")
     exe = tmp_path / "t"

@@ -12,8 +12,10 @@ from phonon_b200 import runtime as rt
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("kind", [0, 1, 2])
 def test_wait_expires_and_reports(cuda_ok, kind):
+    """kind 2: the expiry reaches the status words of an allocation-free
+    linear call (phonon_cuda_linear_apply_device_noalloc) as DEVICE_ERROR."""
     st, secs = rt.wait_expiry_probe(kind, 2000)  # 2 ms budget
     assert st == rt.DEVICE_ERROR
     assert 0.001 < secs < 0.5, secs

@@ -1,12 +1,14 @@
 """phonon_cuda_linear_apply_device_noalloc: the allocation-free entry point.
 
-Callers such as a real-time audio thread, code running while a CUDA graph is
-being captured, or an engine whose device memory was fixed at start-up cannot
+Callers such as a real-time audio thread (where cudaMalloc may block past the
+audio deadline) or an engine whose device memory was fixed at start-up cannot
 call cudaMalloc mid-run. This entry point serves them: it keeps its scratch in
 a device array that the library owns, and allocates nothing. Its output must
 match the allocating entry point phonon_cuda_linear_apply_device on the same
 inputs, within the per-layer tolerance of the parity tests, on two calls in a
-row. The second call reuses the scratch the first one left behind."""
+row. The second call reuses the scratch the first one left behind. A row
+with a non-finite value is flagged in its own status word only, and free
+device memory is the same before and after a call."""
 import ctypes as C
 
 import numpy as np
@@ -28,7 +30,7 @@ def noalloc_fn():
     return fn
 
 
-@pytest.mark.parametrize("rows,cols,batch", [(1536, 512, 64), (512, 2048, 40), (2048, 512, 7)])
+@pytest.mark.parametrize("rows,cols,batch", [(1536, 512, 64), (512, 2048, 40), (2048, 512, 7), (512, 512, 1)])
 def test_noalloc_matches_allocating_entry_point(cuda_ok, rows, cols, batch):
     import torch
     g = synth.Generator(1000 + rows + cols)
@@ -67,3 +69,37 @@ def test_noalloc_limits(cuda_ok):
     assert rc == rt.INVALID  # only Q8_0 with one scale per row runs on this path
     lin.close()
     bf.close()
+
+
+def test_noalloc_nonfinite_row_and_no_allocation(cuda_ok):
+    """Row 3 of 9 holds a NaN: only its status word is flagged (the other
+    rows match the allocating entry point), and a call leaves the device's
+    free memory unchanged."""
+    import torch
+    g = synth.Generator(99)
+    rows, cols, batch, bad = 512, 2048, 9, 3
+    lin = rt.Linear(g.q8_linear(rows, cols, synth.SCALE_PER_ROW), rows, cols)
+    stream = torch.cuda.current_stream().cuda_stream
+    fn = noalloc_fn()
+    x = torch.tensor(g.normal(batch * cols).reshape(batch, cols), device="cuda")
+    x[bad, 17] = float("nan")
+    y_ref = torch.empty(batch, rows, device="cuda")
+    y_new = torch.empty(batch, rows, device="cuda")
+    st_ref = torch.zeros(batch, dtype=torch.int32, device="cuda")
+    st_new = torch.zeros(batch, dtype=torch.int32, device="cuda")
+    lin.apply_device(x.data_ptr(), batch, y_ref.data_ptr(), stream, None, st_ref.data_ptr())
+    assert fn(lin.h, x.data_ptr(), batch, None, y_new.data_ptr(), st_new.data_ptr(), stream) == rt.OK
+    torch.cuda.synchronize()
+    flagged = st_new.cpu().numpy()
+    assert flagged[bad] == rt.NON_FINITE and np.count_nonzero(flagged) == 1, flagged
+    assert st_ref.cpu().numpy()[bad] == rt.NON_FINITE
+    ok = [i for i in range(batch) if i != bad]
+    a, b = y_new.cpu().numpy()[ok], y_ref.cpu().numpy()[ok]
+    assert rt.rel_err(a.ravel(), b.ravel()) < 1e-4
+    st_new.zero_()
+    torch.cuda.synchronize()
+    free_before = torch.cuda.mem_get_info()[0]
+    assert fn(lin.h, x.data_ptr(), batch, None, y_new.data_ptr(), st_new.data_ptr(), stream) == rt.OK
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free_before
+    lin.close()
