@@ -42,9 +42,11 @@ UNIT = "frames/s"
 L2_BYTES = 126 * 2**20
 HBM_FALLBACK_GBS = 6650.0
 # DRAM bytes (read + write) per algorithmic byte of the attention kernel, from
-# one ncu capture of the same kernel on the configs[3] shape at 128 streams;
-# scaled by each launch's algorithmic bytes to give `traffic`.
-ATTN_DRAM_PER_ALGO_BYTE = 1.024
+# one ncu capture of the same kernel on the configs[3] shape at 128 streams
+# (profiles/attn_tma_kernel_configs3_128streams.md: 293.07 MB of DRAM traffic
+# for 286.35 MB of K/V); scaled by each launch's algorithmic bytes to give
+# `traffic`.
+ATTN_DRAM_PER_ALGO_BYTE = 1.0235
 
 
 def measured_hbm_gbs():
@@ -183,63 +185,88 @@ class RankServer:
 
 # -------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during a region
-    (a reader thread collects lines while the region runs)."""
+    """SM clock and throttle reasons sampled during a region.
 
+    NVML (nvidia_ml_py) is polled every 2 ms from a thread, so that even a
+    region of a few tens of milliseconds gets samples; without NVML it falls
+    back to `nvidia-smi -lms 100`. Only samples taken between __enter__ and
+    __exit__ count."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device):
+    def __init__(self, device, period_s=0.002):
         self.device = device
+        self.period = period_s
+        self.samples = []  # (sm_mhz, max_mhz, reasons set)
         self.proc = None
-        self.lines = []
-        self.first = threading.Event()
+        self.thread = None
+        self.stop = threading.Event()
 
-    def _read(self):
+    def _nvml_loop(self, nv, h):
+        reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = reasons_fn(h)
+                self.samples.append((float(sm), float(mx),
+                                     {k for k, b in self.REASONS.items() if bits & b}))
+            except Exception:
+                pass
+            self.stop.wait(self.period)
+
+    def _smi_loop(self):
         for line in self.proc.stdout:
-            if line.strip():
-                self.lines.append(line)
-                self.first.set()
+            f = [x.strip() for x in line.split(",")]
+            try:
+                sm, mx = float(f[0]), float(f[1])
+            except (ValueError, IndexError):
+                continue
+            names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+            self.samples.append((sm, mx, {n for n, v in zip(names, f[3:7]) if v.lower().startswith("active")}))
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.reader = threading.Thread(target=self._read, daemon=True)
-            self.reader.start()
-            self.first.wait(timeout=10)
-            self.skip = len(self.lines)  # samples taken before the region starts
-        except OSError:
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.device)
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+        except Exception:
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                     "--format=csv,noheader,nounits", "-lms", "100"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.thread = threading.Thread(target=self._smi_loop, daemon=True)
+            except OSError:
+                self.thread = None
+        if self.thread:
+            self.thread.start()
         return self
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=10)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-            self.reader.join(timeout=10)
+        if self.thread:
+            self.thread.join(timeout=10)
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines[getattr(self, "skip", 0):]:
-            f = [x.strip() for x in line.split(",")]
-            try:
-                sm.append(float(f[0]))
-                mx = max(mx, float(f[1]))
-            except (ValueError, IndexError):
-                continue
-            for name, val in zip(names, f[3:7]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [x[0] for x in self.samples]
+        reasons = set().union(*[x[2] for x in self.samples]) if self.samples else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(x[1] for x in self.samples) if self.samples else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml, 2 ms" if self.proc is None else "nvidia-smi, 100 ms"}
 
 
 # --------------------------------------------------------------- GPU arm

@@ -1,6 +1,6 @@
 /* Flow-transformer API of speech-mac, served on a B200 (drop-in header).
  *
- * Prototypes match speech-mac src/phonon_transformer.h:10-81 so that speech.c,
+ * Prototypes match speech-mac src/phonon_transformer.h:10-103 so that speech.c,
  * phonon_sampler.c and the reference tests link against
  * libphonon_transformer_cuda instead of src/phonon_transformer.c +
  * src/phonon_q8.c. Every function returns 1 on success and 0 on failure. The
@@ -11,6 +11,7 @@
 
 #include "phonon_pack.h"
 #include <stddef.h>
+#include <stdint.h>
 
 /* Return nonzero to stop; cancel-aware calls then reset the cache and return 0. */
 typedef int (*PhononCancelPoll)(void *context);
@@ -73,6 +74,34 @@ int phonon_flow_stack_prefill_cancel(const PhononFlowLayerWeights weights[PHONON
 int phonon_flow_stack_prefill(const PhononFlowLayerWeights weights[PHONON_FLOW_LAYERS],
                               PhononKvCache *cache, const float *input, size_t length, float theta,
                               float output[512]);
+
+/* Conditioning and embedding helpers of src/phonon_transformer.h:66-103
+ * (defined at src/phonon_transformer.c:711-914). Host C17 with their matrix
+ * products and the output LayerNorm on the device. The pack-backed ones look
+ * tensors up through the engine's pack reader (src/phonon_pack.c,
+ * phonon_pack_tensor); where no pack reader is linked they return 0. */
+int phonon_flow_condition(const PhononTensorView *speaker_embeddings,
+                          const PhononTensorView *speaker_projection,
+                          const PhononTensorView *duration_projection, size_t speaker_count,
+                          float duration_delta, float output[PHONON_FLOW_WIDTH]);
+int phonon_voice_project(const float *voice_latents, size_t frames,
+                         const PhononTensorView *projection, float *projected);
+int phonon_flow_prepare_prefix(const int32_t *ids, size_t tokens, const float *token_embeddings,
+                               size_t prompt_id, size_t bos_id, const float *projected_voice,
+                               size_t voice_frames, const float *bos_latent_projection,
+                               float *prefix_embeddings);
+int phonon_flow_load_layers(const PhononPack *pack, PhononTensorView storage[PHONON_FLOW_LAYERS][8],
+                            PhononFlowLayerWeights weights[PHONON_FLOW_LAYERS]);
+int phonon_flow_embed_tokens(const PhononPack *pack, const int32_t *ids, size_t count,
+                             float *embeddings);
+int phonon_flow_embed_bos(const PhononPack *pack, const float condition[PHONON_FLOW_WIDTH],
+                          float output[PHONON_FLOW_WIDTH]);
+int phonon_flow_embed_latent(const PhononPack *pack, const float latent[32],
+                             const float condition[PHONON_FLOW_WIDTH],
+                             float output[PHONON_FLOW_WIDTH]);
+int phonon_flow_normalize_latent(const PhononPack *pack, const float denormalized[32],
+                                 float normalized[32]);
+int phonon_flow_output_norm(const PhononPack *pack, float values[PHONON_FLOW_WIDTH]);
 
 /* Drop-in extension: CUDA device used by this library (default 0). Call
  * before the first transformer call. */

@@ -562,7 +562,14 @@ __global__ void linear_generic_kernel(const void* __restrict__ w, const __half* 
         }
         acc = fmaf(xr[c], wv, acc);
     }
-    acc = warp_sum(acc);
+    // Lane sums combine in an adjacent-pair tree (lanes 2i and 2i+1 first,
+    // then pairs of pairs), i.e. columns in a balanced tree over their
+    // natural order. On the reference's pinned cancellation row
+    // ([1e8, 1, -1e8, 1] x 8 against unit weights,
+    // tests/test_phonon_transformer.c:617-652) that order gives its SGEMM's
+    // 0 (+bias); the reverse butterfly would give 16.
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) acc += __shfl_xor_sync(kFull, acc, o);
     if (lane == 0) {
         if (bias) acc = __fadd_rn(acc, bias[r]);
         if (!isfinite(acc)) flag_nonfinite(status, b);

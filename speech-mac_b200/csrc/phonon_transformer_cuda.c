@@ -1,7 +1,8 @@
 /* libphonon_transformer_cuda: C17 drop-in for speech-mac's
- * src/phonon_transformer.c (Flow-LM step, KV cache, primitives) and
- * src/phonon_q8.c, running every numerical call on a B200 through
- * libphonon_cuda (include/phonon_cuda.h).
+ * src/phonon_transformer.c (Flow-LM step, KV cache, primitives, conditioning
+ * and embedding helpers) and src/phonon_q8.c, running every numerical call
+ * on a B200 through libphonon_cuda (include/phonon_cuda.h). An engine links
+ * it in place of those two files; its pack reader (src/phonon_pack.c) stays.
  *
  * Contracts kept from the reference (src/phonon_transformer.h:7-9, :33-81):
  *  - 1 on success, 0 on failure; argument checks in the reference's order;
@@ -27,6 +28,7 @@
 #include <math.h>
 #include <pthread.h>
 #include <stdint.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -563,4 +565,240 @@ int phonon_flow_stack_prefill(const PhononFlowLayerWeights weights[PHONON_FLOW_L
                               float output[512]) {
     return phonon_flow_stack_prefill_cancel(weights, cache, input, length, theta, output, NULL,
                                             NULL);
+}
+
+/* ---------------------------------------------- conditioning and embeddings
+ * The helpers around the stack (src/phonon_transformer.c:711-914): speaker
+ * and duration conditioning, voice projection, prefix assembly, and the
+ * pack-backed embeddings and output norm. They run once per request or once
+ * per frame on a few hundred values, so the glue stays on the host; their
+ * matrix products go through phonon_linear / phonon_linear_batch and the
+ * output norm through phonon_layer_norm, i.e. onto the device. Argument
+ * checks come in the reference's order; tensor names are the pack's. */
+
+/* The engine's pack reader (src/phonon_pack.c) owns the pack; it is
+ * referenced weakly so that this library also loads where no pack reader is
+ * linked (every pack-backed helper then returns 0). */
+#pragma weak phonon_pack_tensor
+
+static int pack_lookup(const PhononPack *pack, const char *name, PhononTensorView *view) {
+    return phonon_pack_tensor != NULL && phonon_pack_tensor(pack, name, view);
+}
+
+/* bf16 bits -> fp32; 0 if any value is non-finite (phonon_bf16_to_float,
+ * src/phonon_pack.c:321-340, without the overlap check: callers here never
+ * alias). */
+static int widen_bf16(const uint16_t *bits, size_t count, float *out) {
+    for (size_t i = 0; i < count; i++) {
+        uint32_t u = (uint32_t)bits[i] << 16;
+        memcpy(&out[i], &u, sizeof(float));
+        if (!isfinite(out[i]))
+            return 0;
+    }
+    return 1;
+}
+
+/* A rank-1 bf16 vector of `count` values, exactly sized. */
+static int bf16_vector_view(const PhononTensorView *v, size_t count, float *out) {
+    return v && v->data && v->rank == 1 && v->shape[0] == count && v->dtype == PHONON_PACK_BF16 &&
+           v->byte_count == count * sizeof(uint16_t) && widen_bf16(v->data, count, out);
+}
+
+int phonon_voice_project(const float *voice_latents, size_t frames,
+                         const PhononTensorView *projection, float *projected) {
+    if (!voice_latents || !projection || !projected || frames == 0 || frames > 8192)
+        return 0;
+    return phonon_linear_batch(projection, voice_latents, PHONON_FLOW_WIDTH, PHONON_FLOW_WIDTH,
+                               NULL, projected, frames);
+}
+
+int phonon_flow_condition(const PhononTensorView *speaker_embeddings,
+                          const PhononTensorView *speaker_projection,
+                          const PhononTensorView *duration_projection, size_t speaker_count,
+                          float duration_delta, float output[PHONON_FLOW_WIDTH]) {
+    enum { SPEAKER_DIM = 16, DURATION_DIM = 128 };
+    const PhononTensorView *table = speaker_embeddings;
+    if (!table || !table->data || !speaker_projection || !duration_projection || !output ||
+        table->rank != 2 || table->shape[1] != SPEAKER_DIM || speaker_count >= table->shape[0] ||
+        !isfinite(duration_delta))
+        return 0;
+    if (table->dtype != PHONON_PACK_BF16 ||
+        table->byte_count != table->shape[0] * SPEAKER_DIM * sizeof(uint16_t))
+        return 0;
+    /* speaker row (bf16 widened; a non-finite entry fails in the projection) */
+    float speaker_row[SPEAKER_DIM], speaker[PHONON_FLOW_WIDTH];
+    const uint16_t *row = (const uint16_t *)table->data + speaker_count * SPEAKER_DIM;
+    for (size_t i = 0; i < SPEAKER_DIM; i++) {
+        uint32_t u = (uint32_t)row[i] << 16;
+        memcpy(&speaker_row[i], &u, sizeof(float));
+    }
+    if (!phonon_linear(speaker_projection, speaker_row, PHONON_FLOW_WIDTH, SPEAKER_DIM, NULL,
+                       speaker))
+        return 0;
+    /* duration: 64 cosines then 64 sines of 1000*delta / 10000^(i/63), in double */
+    float duration[DURATION_DIM], duration_out[PHONON_FLOW_WIDTH];
+    const double amplitude = 1000.0 * (double)duration_delta;
+    for (size_t i = 0; i < DURATION_DIM / 2; i++) {
+        const double angle = amplitude / pow(10000.0, (double)i / 63.0);
+        duration[i] = (float)cos(angle);
+        duration[DURATION_DIM / 2 + i] = (float)sin(angle);
+    }
+    if (!phonon_linear(duration_projection, duration, PHONON_FLOW_WIDTH, DURATION_DIM, NULL,
+                       duration_out))
+        return 0;
+    for (size_t i = 0; i < PHONON_FLOW_WIDTH; i++) {
+        output[i] = speaker[i] + duration_out[i];
+        if (!isfinite(output[i]))
+            return 0;
+    }
+    return 1;
+}
+
+int phonon_flow_prepare_prefix(const int32_t *ids, size_t tokens, const float *token_embeddings,
+                               size_t prompt_id, size_t bos_id, const float *projected_voice,
+                               size_t voice_frames, const float *bos_latent_projection,
+                               float *prefix_embeddings) {
+    if (!ids || !tokens || !token_embeddings || !projected_voice || !voice_frames ||
+        !bos_latent_projection || !prefix_embeddings || tokens > 8192 || voice_frames > tokens ||
+        prompt_id > INT32_MAX || bos_id > INT32_MAX)
+        return 0;
+    const int32_t prompt = (int32_t)prompt_id, bos = (int32_t)bos_id;
+    size_t n_prompt = 0, n_bos = 0;
+    for (size_t i = 0; i < tokens; i++) {
+        n_prompt += ids[i] == prompt;
+        n_bos += ids[i] == bos;
+    }
+    if (n_prompt != voice_frames || n_bos != 1)
+        return 0;
+    /* prompt slots take the voice frames in order, the BOS slot its latent
+     * projection, every other slot its own token embedding */
+    const float *next_voice = projected_voice;
+    for (size_t i = 0; i < tokens; i++) {
+        const float *src;
+        if (ids[i] == prompt) {
+            src = next_voice;
+            next_voice += PHONON_FLOW_WIDTH;
+        } else if (ids[i] == bos) {
+            src = bos_latent_projection;
+        } else {
+            src = token_embeddings + i * PHONON_FLOW_WIDTH;
+        }
+        float *dst = prefix_embeddings + i * PHONON_FLOW_WIDTH;
+        memcpy(dst, src, PHONON_FLOW_WIDTH * sizeof(float));
+        for (size_t j = 0; j < PHONON_FLOW_WIDTH; j++)
+            if (!isfinite(dst[j]))
+                return 0;
+    }
+    return 1;
+}
+
+int phonon_flow_load_layers(const PhononPack *pack, PhononTensorView storage[PHONON_FLOW_LAYERS][8],
+                            PhononFlowLayerWeights weights[PHONON_FLOW_LAYERS]) {
+    /* Per layer, the pack's eight tensors in the order of PhononFlowLayerWeights. */
+    static const char *const suffix[8] = {"self_attn.in_proj.weight", "self_attn.out_proj.weight",
+                                          "linear1.weight",           "linear2.weight",
+                                          "norm1.weight",             "norm1.bias",
+                                          "norm2.weight",             "norm2.bias"};
+    if (!pack || !storage || !weights)
+        return 0;
+    for (size_t layer = 0; layer < PHONON_FLOW_LAYERS; layer++) {
+        const PhononTensorView **field[8] = {
+            &weights[layer].qkv,          &weights[layer].attention_out, &weights[layer].mlp_in,
+            &weights[layer].mlp_out,      &weights[layer].norm1_weight,  &weights[layer].norm1_bias,
+            &weights[layer].norm2_weight, &weights[layer].norm2_bias};
+        for (size_t k = 0; k < 8; k++) {
+            char name[160];
+            (void)snprintf(name, sizeof(name), "flow_lm.transformer.layers.%zu.%s", layer, suffix[k]);
+            if (!pack_lookup(pack, name, &storage[layer][k]))
+                return 0;
+            *field[k] = &storage[layer][k];
+        }
+    }
+    return 1;
+}
+
+int phonon_flow_embed_tokens(const PhononPack *pack, const int32_t *ids, size_t count,
+                             float *embeddings) {
+    PhononTensorView table;
+    if (!pack || !ids || !count || !embeddings || count > 8192 ||
+        !pack_lookup(pack,
+                     "flow_lm.condition_provider.conditioners.transcript_in_segment.embed.weight",
+                     &table) ||
+        table.rank != 2 || table.shape[1] != PHONON_FLOW_WIDTH || table.dtype != PHONON_PACK_BF16 ||
+        table.byte_count != table.shape[0] * PHONON_FLOW_WIDTH * sizeof(uint16_t))
+        return 0;
+    for (size_t i = 0; i < count; i++) {
+        if (ids[i] < 0 || (uint64_t)ids[i] >= table.shape[0] ||
+            !widen_bf16((const uint16_t *)table.data + (size_t)ids[i] * PHONON_FLOW_WIDTH,
+                        PHONON_FLOW_WIDTH, embeddings + i * PHONON_FLOW_WIDTH))
+            return 0;
+    }
+    return 1;
+}
+
+/* output = input_linear(latent[32]) + condition, finite. */
+static int project_latent(const PhononPack *pack, const float latent[32],
+                          const float condition[PHONON_FLOW_WIDTH],
+                          float output[PHONON_FLOW_WIDTH]) {
+    PhononTensorView projection;
+    if (!pack_lookup(pack, "flow_lm.input_linear.weight", &projection) ||
+        !phonon_linear(&projection, latent, PHONON_FLOW_WIDTH, 32, NULL, output))
+        return 0;
+    for (size_t i = 0; i < PHONON_FLOW_WIDTH; i++) {
+        output[i] += condition[i];
+        if (!isfinite(output[i]))
+            return 0;
+    }
+    return 1;
+}
+
+int phonon_flow_embed_bos(const PhononPack *pack, const float condition[PHONON_FLOW_WIDTH],
+                          float output[PHONON_FLOW_WIDTH]) {
+    PhononTensorView bos;
+    float latent[32];
+    if (!pack || !condition || !output || !pack_lookup(pack, "flow_lm.bos_emb", &bos) ||
+        bos.rank != 1 || bos.shape[0] != 32 || bos.dtype != PHONON_PACK_BF16 || !bos.data ||
+        !widen_bf16((const uint16_t *)bos.data, 32, latent))
+        return 0;
+    return project_latent(pack, latent, condition, output);
+}
+
+int phonon_flow_embed_latent(const PhononPack *pack, const float latent[32],
+                             const float condition[PHONON_FLOW_WIDTH],
+                             float output[PHONON_FLOW_WIDTH]) {
+    if (!pack || !latent || !condition || !output)
+        return 0;
+    return project_latent(pack, latent, condition, output);
+}
+
+int phonon_flow_normalize_latent(const PhononPack *pack, const float denormalized[32],
+                                 float normalized[32]) {
+    PhononTensorView mean_view, std_view;
+    float mean[32], std_dev[32];
+    if (!pack || !denormalized || !normalized ||
+        !pack_lookup(pack, "flow_lm.emb_mean", &mean_view) ||
+        !pack_lookup(pack, "flow_lm.emb_std", &std_view) ||
+        !bf16_vector_view(&mean_view, 32, mean) || !bf16_vector_view(&std_view, 32, std_dev))
+        return 0;
+    for (size_t i = 0; i < 32; i++) {
+        if (!isfinite(denormalized[i]) || !(std_dev[i] > 0.0f))
+            return 0;
+        normalized[i] = (denormalized[i] - mean[i]) / std_dev[i];
+        if (!isfinite(normalized[i]))
+            return 0;
+    }
+    return 1;
+}
+
+int phonon_flow_output_norm(const PhononPack *pack, float values[PHONON_FLOW_WIDTH]) {
+    PhononTensorView weight_view, bias_view;
+    float weight[PHONON_FLOW_WIDTH], bias[PHONON_FLOW_WIDTH], result[PHONON_FLOW_WIDTH];
+    if (!pack || !values || !pack_lookup(pack, "flow_lm.out_norm.weight", &weight_view) ||
+        !pack_lookup(pack, "flow_lm.out_norm.bias", &bias_view) ||
+        !bf16_vector_view(&weight_view, PHONON_FLOW_WIDTH, weight) ||
+        !bf16_vector_view(&bias_view, PHONON_FLOW_WIDTH, bias) ||
+        !phonon_layer_norm(values, weight, bias, PHONON_FLOW_WIDTH, 1e-5f, result))
+        return 0;
+    memcpy(values, result, sizeof(result));
+    return 1;
 }

@@ -54,6 +54,49 @@ def test_tensor_view_layout():
     assert PhononTensorView.data.offset == 72
 
 
+# Engine sources that build on Linux (audio_queue_playback.c needs AudioToolbox,
+# speech_stream.c the playback header, phonon_math.c NEON and sha256.c
+# CommonCrypto; the first two reference nothing of the path).
+ENGINE = ["english_normalize", "phonon_conv", "phonon_mimi", "phonon_pack", "phonon_pcm",
+          "phonon_prompt_plan", "phonon_sampler", "phonon_tokenizer", "phonon_voice", "speech",
+          "speech_cli", "speech_error", "speech_main", "utf8", "wav_writer"]
+
+
+def test_engine_links_against_dropin(tmp_path):
+    """Every symbol that speech-mac's engine sources take from
+    src/phonon_transformer.c or src/phonon_q8.c is exported by
+    libphonon_transformer_cuda.so, so the engine links with those two files
+    replaced by the drop-in (nm over objects compiled here; no GPU)."""
+    from oracle.oracle import reference_root
+    src = reference_root() / "src"
+    if not (src / "phonon_transformer.c").exists():
+        pytest.skip("speech-mac tree not present")
+    shim = ROOT / "oracle" / "shim"
+
+    def obj(name):
+        out = tmp_path / f"{name}.o"
+        subprocess.run(["gcc", "-std=c17", "-O1", "-c", f"-I{shim}", f"-I{src}", "-DPHONON_PACK_TEST_API",
+                        str(src / f"{name}.c"), "-o", str(out)], check=True)
+        return out
+
+    def syms(path, *flags):
+        r = subprocess.run(["nm", *flags, str(path)], capture_output=True, text=True, check=True)
+        return {ln.split()[-1] for ln in r.stdout.splitlines() if ln.strip()}
+
+    path_defs = set()
+    for name in ("phonon_transformer", "phonon_q8"):
+        r = subprocess.run(["nm", "--defined-only", "--extern-only", str(obj(name))], capture_output=True,
+                           text=True, check=True)
+        path_defs |= {ln.split()[-1] for ln in r.stdout.splitlines() if ln.split()[1] == "T"}
+    needed = set()
+    for name in ENGINE:
+        needed |= syms(obj(name), "-u") & path_defs
+    exported = syms(PKG / "libphonon_transformer_cuda.so", "-D", "--defined-only")
+    assert needed, "no engine symbol taken from the path?"
+    assert not needed - exported, sorted(needed - exported)
+    assert {"phonon_flow_condition", "phonon_flow_output_norm", "phonon_flow_embed_latent"} <= needed
+
+
 @pytest.mark.parametrize("test", ["test_phonon_q8.c"])
 def test_reference_test_compiles_against_dropin(tmp_path, test):
     """Where the speech-mac tree exists, its own Q8 test links unchanged
