@@ -3,62 +3,87 @@
 // A decode step of one stream is a chain of ~60 dependent stages whose work
 // is small (a 512-wide LayerNorm, a few hundred GEMV rows, attention over a
 // few hundred keys per head): its time is the latency of the chain, not the
-// ~50 MB of traffic. Kernel boundaries and grid-wide barriers each cost
-// microseconds per stage. Here one cluster of 16 CTAs (one per SM) runs
-// every layer of the step (the loop of phonon_flow_stack_step, speech-mac
-// src/phonon_transformer.c:455-489). CTAs exchange activations through
-// distributed shared memory and meet at hardware cluster barriers; every CTA
-// keeps the full rows it reads. CTA `rank` serves head rank / 2, half
-// rank % 2:
+// ~50 MB of traffic. Here one cluster of 16 CTAs (one per SM) runs every
+// layer of the step (the loop of phonon_flow_stack_step, speech-mac
+// src/phonon_transformer.c:455-489) without kernel boundaries, grid barriers
+// or cluster barriers between stages. CTA `rank` serves head rank / 2,
+// half rank % 2:
 //
-//   A  LN1 of x (each CTA) -> QKV rows of dims [32*half, +32) of its head;
-//      RoPE; q to both CTAs of the head, k and v appended to the stream's
-//      KV page (src/phonon_transformer.c:414-431)
-//   B  attention of its head over its half of the stream's pages, one page
-//      per warp at a time (TMA page staging, the page math of the other
-//      paths); the CTA's partial goes to every CTA (flow_attention, :340-404)
-//   C  every CTA merges the two partials of each head into the attention
-//      row; out rows [32*rank, +32) + residual -> h to every CTA (:432-443)
-//   D  LN2 (each CTA) -> up rows [128*rank, +128) + GELU -> to every CTA
-//      (:444-447)
-//   E  down rows [32*rank, +32) + residual -> x' to every CTA (:448-452)
+//   A  LN1 of x (each CTA) -> the head's 64 q rows and the k and v rows of
+//      dims [32*half, +32); RoPE; k and v appended to the stream's KV page
+//      (src/phonon_transformer.c:414-431)
+//   B  attention of q over the keys of this CTA's half of the stream's
+//      earlier pages (TMA page staging, the page math of the other paths);
+//      the current position's key is not read back from the page: each CTA
+//      contributes its half of q.k and its half of v, and the key joins the
+//      softmax as one more term of the merge (flow_attention, :340-404)
+//   C  every CTA merges, per head, the two CTA partials and the current key
+//      into the attention row; out rows [32*rank, +32) + residual -> h
+//      (:432-443)
+//   D  LN2 (each CTA) -> up rows [128*rank, +128) + GELU -> g (:444-447)
+//   E  down rows [32*rank, +32) + residual -> x' (:448-452)
 //
-// Warp 8 is the copy warp. It streams the CTA's weight rows through a ring
-// of shared-memory slots (bulk copies; a unit is 17 KB: 32 rows of a
-// 512-column matrix or 8 rows of the 2048-column one, with their Q8_0
-// scales), the LayerNorm vectors through a two-slot ring, and its head's
-// K/V blocks of the stream's pages through a third ring (TMA, 16-row
-// SWIZZLE_128B boxes), each unit as soon as its slot is released. Only the
-// page this step appends to waits for phase A.
+// Exchanges: every stage output a CTA produces (its attention message, and
+// its slices of h, g and x') is pushed into the same buffer of all 16 CTAs
+// with st.async, which completes the bytes on that buffer's mbarrier in the
+// receiving CTA; a CTA waits on its own mbarrier for exactly the bytes its
+// next stage reads. One DSMEM hop per exchange, four per layer, and no
+// release fences: the stores complete on the receiver's barrier. Every
+// exchange buffer is single-buffered: a CTA can only produce layer l+1's data
+// for a buffer after it received data that every other CTA sends after it
+// has finished reading that buffer for layer l (the chain is A..E in order),
+// and each buffer's barrier completes exactly one phase per layer.
 //
-// Numerics: the LayerNorm, the row dot products (gemv_kernel's per-lane
-// fp32 accumulation and butterfly sum), RoPE, GELU, residuals and the page
-// math of the attention are those of the other step paths, so projections
-// and appended K/V rows are bit-identical to them; the attention partials
-// are merged in another order (pages are split between two CTAs and eight
-// warps), which changes sums within rounding.
+// Warp 8 is the copy warp. At launch it asks L2 to prefetch the CTA's weight
+// rows for the whole step and its head's K/V blocks of every layer
+// (cp.async.bulk.prefetch.L2). Then it streams, in the order the compute
+// warps consume them, the CTA's weight rows through a ring of 17 KB slots
+// (32 rows of a 512-column matrix or 8 rows of the 2048-column one, with
+// their Q8_0 scales), the LayerNorm vectors through a two-slot ring and its
+// head's K/V blocks of the stream's earlier pages through an eight-slot page
+// ring (TMA, 16-row SWIZZLE_128B boxes), each as soon as the slot it refills
+// is released. No page read waits for this step's append.
+//
+// Code size: the LayerNorm, the row dot products and the attention page are
+// each one non-inlined routine, so the ~60 stages of a step run through a
+// small, hot instruction footprint.
+//
+// Numerics: the LayerNorm, the row dot products (gemv_kernel's per-lane fp32
+// accumulation and butterfly sum), RoPE, GELU and residuals are those of the
+// other step paths, so projections and appended K/V rows are bit-identical
+// to them; the attention partials merge in another order (pages split
+// between two CTAs and eight warps, the current key last), which changes
+// sums within rounding.
 //
 // Every mbarrier wait is bounded: on expiry the CTA raises the context's
-// error flag and skips the rest of its work, but every thread still takes
-// every cluster barrier, so the launch ends; the copy warp waits (bounded)
-// for its copies in flight before the CTA exits. No multicast.
+// error flag and skips the rest of its work (its waits return at once); it
+// still takes the final cluster barrier, so no CTA exits while another could
+// still store into its shared memory, and the copy warp waits (bounded) for
+// its copies in flight first. No multicast.
 #pragma once
 
 #include "phonon_persist.cuh"
 
 namespace phonon {
 
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
 // Phase timestamps for profiling builds (-DPHONON_CLUSTER_TRACE): thread 0
 // of every CTA writes %globaltimer at marked points into
-// g_cluster_trace[(rank * 64 + layer) * 32 + slot] (layer 63: set-up).
-// Empty otherwise.
+// g_cluster_trace[(rank * 64 + layer) * 32 + slot] (layer 63: set-up). Marks
+// sit right after waits and named barriers, which order them against the
+// work before them. Empty otherwise.
 #ifdef PHONON_CLUSTER_TRACE
 __device__ unsigned long long g_cluster_trace[16 * 64 * 32];
 #define CL_MARK(layer, slot)                                                                       \
     do {                                                                                           \
         if (threadIdx.x == 0) {                                                                    \
             unsigned long long t_;                                                                 \
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                                 \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)::"memory");                      \
             g_cluster_trace[(static_cast<size_t>(cluster_ctarank()) * 64 + (layer)) * 32 + (slot)] = t_; \
         }                                                                                          \
     } while (0)
@@ -73,11 +98,23 @@ constexpr int kClWarps = 8;                       // compute warps
 constexpr int kClThreads = 32 * (kClWarps + 1);   // + copy warp
 constexpr int kClUnitPlane = 16384;               // int8 bytes of a weight unit
 constexpr int kClUnitBytes = kClUnitPlane + 1024; // + binary16 block scales
-constexpr int kClUnitsPerLayer = 12;              // q, k, v, out, 4 x up, 4 x down
-constexpr int kClKvSlots = 8;                     // page ring: one page per compute warp
-constexpr int kClPartStride = 68;                 // floats: max, sum, acc[64], pad
+// Weight units of a layer, in consumption order: q rows [0, 32) and [32, 64)
+// of the head, k rows and v rows of the CTA's 32 dims, out, 4 x up, 4 x down.
+constexpr int kClUnitsPerLayer = 13;
+constexpr int kClUnitOut = 4, kClUnitUp = 5, kClUnitDown = 9;
+constexpr int kClKvSlots = 8;                     // page ring
+constexpr int kClPartStride = 68;                 // warp partials: max, sum, acc[64], pad
+// A CTA's attention message: max, sum, its half of the current key's q.k,
+// pad, acc[64], its half of the current key's v [32].
+constexpr int kClMsgFloats = 100;
 constexpr int kClNormBytes = 2 * kWidth * 4;      // one LayerNorm's weight + bias (fp32)
 constexpr int kClMaxUpdates = 2;                  // page-table updates carried in the parameters
+// Exchange buffers with one mbarrier each, completing once per layer.
+enum ClExchange : int { CLX_PART = 0, CLX_H = 1, CLX_G = 2, CLX_X = 3 };
+constexpr uint32_t kClBytesPart = kClusterCtas * kClMsgFloats * 4;  // 16 messages
+constexpr uint32_t kClBytesH = kWidth * 4;                          // 16 slices of 32 rows
+constexpr uint32_t kClBytesG = kFfn * 4;                            // 16 slices of 128 rows
+constexpr uint32_t kClBytesX = kWidth * 4;
 
 template <bool kBf16>
 struct ClShape {
@@ -95,14 +132,19 @@ struct ClShape {
     static constexpr int kOffA = kOffH + kWidth * 4;                // attention row [512]
     static constexpr int kOffG = kOffA + kWidth * 4;                // GELU row [2048]
     static constexpr int kOffQ = kOffG + kFfn * 4;                  // q of the head [64]
-    static constexpr int kOffPart = kOffQ + kHeadDim * 4;           // CTA partials [16][68]
-    static constexpr int kOffWPart = kOffPart + kClusterCtas * kClPartStride * 4;  // warp partials [8][68]
-    static constexpr int kOffRope = kOffWPart + kClWarps * kClPartStride * 4;      // (cos, sin) [32]
+    static constexpr int kOffSelf = kOffQ + kHeadDim * 4;           // this CTA's k, v of the current key [2][32]
+    static constexpr int kOffMsg = kOffSelf + 64 * 4;               // messages of the 16 CTAs [16][100]
+    static constexpr int kOffMine = kOffMsg + kClusterCtas * kClMsgFloats * 4;  // this CTA's message [100]
+    static constexpr int kOffWPart = kOffMine + kClMsgFloats * 4;   // warp partials [8][68]
+    static constexpr int kOffRope = kOffWPart + kClWarps * kClPartStride * 4;  // (cos, sin) [32]
     static constexpr int kOffBar = kOffRope + 32 * 8;
-    static constexpr int kBars = 2 * kWSlots + 4 + 2 * kClKvSlots;
+    static constexpr int kBars = 2 * kWSlots + 4 + 2 * kClKvSlots + 4;
     static constexpr int kOffFlag = kOffBar + kBars * 8;
     static constexpr int kSmem = kOffFlag + 16 + 1024;  // + alignment slack
     static_assert(kKvSlot % 1024 == 0 && kOffW % 16 == 0 && kClUnitBytes % 16 == 0, "slot alignment");
+    static_assert(kOffMsg % 16 == 0 && kOffH % 16 == 0 && kOffG % 16 == 0 && kOffX % 16 == 0 &&
+                      kOffMine % 16 == 0 && kOffQ % 16 == 0 && kOffSelf % 16 == 0 && kOffBar % 8 == 0,
+                  "vector and st.async alignment");
     static_assert(kSmem <= 232448, "shared memory of one CTA");
 };
 
@@ -114,19 +156,14 @@ struct ClusterParams {
     int32_t* status;             // [1]
     int32_t* error;              // context error flag (bounded waits)
     int slot, pos;               // the stream's slot and the position decoded
-    int n_updates;               // page-table updates (slot, index, page), applied first
+    int last_page;               // page holding position pos
+    int n_updates;               // page-table updates (slot, index, page), for later steps
     int updates[3 * kClMaxUpdates];
     const float* freq;           // [32] RoPE inverse frequencies
     KvView kv;
     float* trace;                // optional: layer l's output row at trace[l * trace_stride]
     int trace_stride;
 };
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
 
 // Address of the same shared-memory location in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
@@ -135,22 +172,54 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
     return r;
 }
 
-__device__ __forceinline__ void st_cluster(uint32_t addr, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+// 16 bytes into CTA `rank`'s shared memory at (its copy of) saddr; the bytes
+// complete on its copy of the mbarrier bar.
+__device__ __forceinline__ void st_async4(uint32_t saddr, uint32_t bar, uint32_t rank, float4 v) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(cluster_map(saddr, rank)), "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)),
+                   "r"(__float_as_uint(v.z)), "r"(__float_as_uint(v.w)), "r"(cluster_map(bar, rank))
+                 : "memory");
 }
 
-__device__ __forceinline__ void st_cluster2(uint32_t addr, float a, float b) {
-    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+// Bounded wait on an exchange barrier (completions come from other CTAs:
+// acquire at cluster scope).
+__device__ __forceinline__ bool cl_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
 }
 
-// All threads of all CTAs of the cluster; release/acquire at cluster scope
-// (shared memory of every CTA and global memory).
+__device__ __noinline__ bool cl_exchange_wait(uint32_t bar, uint32_t parity, int32_t* error, volatile int* failed) {
+    if (cl_try_wait_cluster(bar, parity)) return true;
+    const long long start = clock64();
+    while (!cl_try_wait_cluster(bar, parity)) {
+        if (*failed) return false;
+        if (clock64() - start > kWaitBudgetCycles) {
+            *failed = 1;
+            if (error) atomicExch(error, 1);
+            return false;
+        }
+    }
+    return true;
+}
+
+// All threads of all CTAs of the cluster; release/acquire at cluster scope.
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 // The 256 compute threads (named barrier 1; the copy warp never takes it).
 __device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 // A consumer lane's offsets into one head's K and V blocks of a page, each a
 // 16-row SWIZZLE_128B box (fp32: two boxes of 32 dims, 2 KB apart): the
@@ -173,18 +242,17 @@ __device__ __forceinline__ AttnLane<kBf16> cl_attn_lane(int lane) {
     return a;
 }
 
-// Four rows (local rows 4q .. 4q+3 of a weight unit in shared memory)
-// against one activation row xs[kChunks * 512]: gemv_kernel's per-lane
-// arithmetic (int8 widened exactly, fp32 dot per 4 columns, scaled fma per
-// 32-block) and butterfly sum. Every lane returns the four row sums.
-template <int kChunks>
-__device__ __forceinline__ void cl_rows4(const uint8_t* unit, int q, const float* xs, float (&sum)[4]) {
-    constexpr int cols = kChunks * 512;
+// Four rows (local rows 4q .. 4q+3 of a weight unit in shared memory) of a
+// chunks*512-column matrix against one activation row xs: gemv_kernel's
+// per-lane arithmetic (int8 widened exactly, fp32 dot per 4 columns, scaled
+// fma per 32-block) and butterfly sum. Every lane returns the four row sums.
+__device__ __noinline__ float4 cl_rows4(const uint8_t* unit, int q, const float* xs, int chunks) {
+    const int cols = chunks * 512;
     const __half* wsc = reinterpret_cast<const __half*>(unit + kClUnitPlane);
     const int lane = threadIdx.x & 31;
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll 1
-    for (int c = 0; c < kChunks; ++c) {
+    for (int c = 0; c < chunks; ++c) {
         float wf[4][16], sc[4][4];
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
@@ -219,32 +287,63 @@ __device__ __forceinline__ void cl_rows4(const uint8_t* unit, int q, const float
             }
         }
     }
+    return make_float4(warp_sum(acc[0]), warp_sum(acc[1]), warp_sum(acc[2]), warp_sum(acc[3]));
+}
+
+// warp_layernorm512 as one routine (one copy of its code in the kernel).
+__device__ __noinline__ bool cl_layernorm(const float* src, const float* w, const float* b, float* dst) {
+    return warp_layernorm512(src, w, b, dst);
+}
+
+// Online-softmax state of a warp (max, sum, the lane's two accumulated
+// dims) and its finite flag, passed by value so that it stays in registers.
+struct ClAttnState {
+    float m, l, a0, a1;
+    int ok;
+};
+
+// One page of the warp's head into its online-softmax state.
+template <bool kBf16>
+__device__ __noinline__ ClAttnState cl_attn_page(const uint8_t* sK, const float* q, int key0, int n_keys,
+                                                 ClAttnState st) {
+    const int lane = threadIdx.x & 31;
+    const AttnLane<kBf16> ad = cl_attn_lane<kBf16>(lane);
+    float qh[32];
 #pragma unroll
-    for (int rr = 0; rr < 4; ++rr) sum[rr] = warp_sum(acc[rr]);
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = reinterpret_cast<const float4*>(q + (lane >> 4) * 32)[i];
+        qh[4 * i] = v.x;
+        qh[4 * i + 1] = v.y;
+        qh[4 * i + 2] = v.z;
+        qh[4 * i + 3] = v.w;
+    }
+    bool ok = st.ok != 0;
+    attn_page<kBf16>(sK, sK + ClShape<kBf16>::kKvBlock, ad, qh, key0, n_keys, st.m, st.l, st.a0, st.a1, ok);
+    st.ok = ok;
+    return st;
 }
 
-__device__ __forceinline__ float pick4(const float (&v)[4], int i) {
-    return i == 0 ? v[0] : (i == 1 ? v[1] : (i == 2 ? v[2] : v[3]));
-}
-
-// Source rows of weight unit u (layer u / 12) for CTA `rank`.
+// Source rows of weight unit u (layer u / 13) for CTA `rank`.
 __device__ __forceinline__ void cl_unit_src(const ClusterParams& p, int u, int rank, const uint8_t*& plane,
                                             const uint8_t*& scales) {
     const int l = u / kClUnitsPerLayer, k = u % kClUnitsPerLayer;
     const int head = rank >> 1, half = rank & 1;
     int m, row0;
-    if (k < 3) {
+    if (k < 2) {
         m = PM_QKV;
-        row0 = k * kWidth + head * kHeadDim + half * 32;
-    } else if (k == 3) {
+        row0 = head * kHeadDim + 32 * k;
+    } else if (k < kClUnitOut) {
+        m = PM_QKV;
+        row0 = (k - 1) * kWidth + head * kHeadDim + half * 32;
+    } else if (k == kClUnitOut) {
         m = PM_OUT;
         row0 = 32 * rank;
-    } else if (k < 8) {
+    } else if (k < kClUnitDown) {
         m = PM_UP;
-        row0 = 128 * rank + 32 * (k - 4);
+        row0 = 128 * rank + 32 * (k - kClUnitUp);
     } else {
         m = PM_DOWN;
-        row0 = 32 * rank + 8 * (k - 8);
+        row0 = 32 * rank + 8 * (k - kClUnitDown);
     }
     const int cols = persist_cols(m);
     const PersistLayer& L = p.layers[l];
@@ -268,12 +367,14 @@ __global__ void __launch_bounds__(kClThreads, 1)
     float* a_s = reinterpret_cast<float*>(smem + Sh::kOffA);
     float* g_s = reinterpret_cast<float*>(smem + Sh::kOffG);
     float* q_s = reinterpret_cast<float*>(smem + Sh::kOffQ);
-    float* part_s = reinterpret_cast<float*>(smem + Sh::kOffPart);
+    float* self_s = reinterpret_cast<float*>(smem + Sh::kOffSelf);
+    float* msg_s = reinterpret_cast<float*>(smem + Sh::kOffMsg);
+    float* mine_s = reinterpret_cast<float*>(smem + Sh::kOffMine);
     float* wpart_s = reinterpret_cast<float*>(smem + Sh::kOffWPart);
     float2* rope_s = reinterpret_cast<float2*>(smem + Sh::kOffRope);
     const uint32_t bar0 = smem_addr(smem + Sh::kOffBar);
     const uint32_t wfull0 = bar0, wempty0 = bar0 + 8 * kW, nfull0 = bar0 + 16 * kW, nempty0 = nfull0 + 16,
-                   kfull0 = nfull0 + 32, kempty0 = kfull0 + 8 * kClKvSlots;
+                   kfull0 = nfull0 + 32, kempty0 = kfull0 + 8 * kClKvSlots, xbar0 = kempty0 + 8 * kClKvSlots;
     volatile int* failed = reinterpret_cast<volatile int*>(smem + Sh::kOffFlag);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -281,13 +382,12 @@ __global__ void __launch_bounds__(kClThreads, 1)
     const int head = rank >> 1, half = rank & 1;
     const int L = p.n_layers;
     const int n_units = kClUnitsPerLayer * L;
-    const int n_keys = p.pos + 1;
-    const int n_pages = p.pos / kPage + 1;
-    // Pages of the stream split between the head's two CTAs: [pg0, pg0 + npc).
-    const int n_first = (n_pages + 1) / 2;
+    // Earlier keys [0, pos) live on pages [0, n_old); the head's two CTAs
+    // take [0, n_first) and [n_first, n_old); this CTA's: [pg0, pg0 + npc).
+    const int n_old = (p.pos + kPage - 1) / kPage;
+    const int n_first = (n_old + 1) / 2;
     const int pg0 = half ? n_first : 0;
-    const int npc = half ? n_pages - n_first : n_first;
-    const bool holds_last = npc > 0 && pg0 + npc == n_pages;  // the page this step appends to
+    const int npc = half ? n_old - n_first : n_first;
     const int32_t* table = p.kv.table + static_cast<size_t>(p.slot) * p.kv.max_pages;
 
     CL_MARK(63, 0);
@@ -304,6 +404,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
             mbar_init(kfull0 + 8 * s, 1);
             mbar_init(kempty0 + 8 * s, 1);
         }
+        for (int x = 0; x < 4; ++x) mbar_init(xbar0 + 8 * x, 1);
         *failed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -315,67 +416,66 @@ __global__ void __launch_bounds__(kClThreads, 1)
     }
     // scalar loads: the caller's row need only be float-aligned, as on the other step paths
     for (int i = threadIdx.x; i < kWidth; i += kClThreads) x_s[i] = p.in[i];
-    if (rank == 0 && threadIdx.x < p.n_updates) {
+    if (rank == 0 && threadIdx.x < p.n_updates) {  // for later steps; this one reads only earlier pages
         const int* u = p.updates + 3 * threadIdx.x;
         const_cast<int32_t*>(p.kv.table)[static_cast<size_t>(u[0]) * p.kv.max_pages + u[1]] = u[2];
     }
-    cluster_sync();  // barriers initialised, page table updated, every CTA running
+    cluster_sync();  // barriers initialised in every CTA before any st.async reaches them
     CL_MARK(63, 1);
-    const int last_page = __ldcg(table + (n_pages - 1));
 
     if (warp == kClWarps) {
         // ------------------------------------------------------ copy warp
-        const bool issuer = lane == 0;
-        int w_last[kW], k_last[kClKvSlots], n_last[2];
-#pragma unroll
-        for (int s = 0; s < kW; ++s) w_last[s] = -1;
-#pragma unroll
-        for (int s = 0; s < kClKvSlots; ++s) k_last[s] = -1;
-        n_last[0] = n_last[1] = -1;
-        int kv_next = 0, kv_last_ok = -1;  // next page-ring index; layer whose appended page may be read
-
-        auto issue_unit = [&](int u) {
-            const int s = u % kW;
-            const uint32_t bar = wfull0 + 8 * s;
+        // L2 prefetch of the whole step: the CTA's weight units, then its
+        // head's K/V blocks of every layer (spread over the lanes).
+        for (int u = lane; u < n_units; u += 32) {
             const uint8_t *plane, *scales;
             cl_unit_src(p, u, rank, plane, scales);
-            uint8_t* dst = w_ring + s * kClUnitBytes;
-            mbar_expect_tx(bar, kClUnitBytes);
-            bulk_load(smem_addr(dst), plane, kClUnitPlane, bar);
-            bulk_load(smem_addr(dst + kClUnitPlane), scales, kClUnitBytes - kClUnitPlane, bar);
-            w_last[s] = u;
-        };
-        // Unit u has been consumed: refill its slot with unit u + kW.
-        auto refill_after = [&](int u) {
-            if (!issuer || *failed || u + kW >= n_units) return;
-            if (!mbar_wait(wempty0 + 8 * (u % kW), (u / kW) & 1, p.error, failed)) return;
-            issue_unit(u + kW);
-        };
-        auto issue_norm = [&](int n) {  // norm n: layer n / 2, LN1 (even) or LN2 (odd)
-            const int s = n & 1;
-            const uint32_t bar = nfull0 + 8 * s;
-            mbar_expect_tx(bar, kClNormBytes);
-            bulk_load(smem_addr(n_ring + s * kClNormBytes), p.layers[n >> 1].norms + (n & 1) * 2 * kWidth,
-                      kClNormBytes, bar);
-            n_last[s] = n;
-        };
-        auto renorm_after = [&](int n) {
-            if (!issuer || *failed || n + 2 >= 2 * L) return;
-            if (!mbar_wait(nempty0 + 8 * (n & 1), (n >> 1) & 1, p.error, failed)) return;
-            issue_norm(n + 2);
-        };
-        // K/V blocks of this CTA's pages, ring index n = layer * npc + i,
-        // up to `limit`; the appended page of a layer waits for its phase A.
-        auto issue_kv = [&](int limit) {
-            if (!issuer) return;
-            for (; kv_next < limit && !*failed; ++kv_next) {
-                const int layer = kv_next / npc, i = kv_next % npc;
-                if (holds_last && i == npc - 1 && layer > kv_last_ok) break;
-                const int s = kv_next % kClKvSlots;
-                if (kv_next >= kClKvSlots &&
-                    !mbar_wait(kempty0 + 8 * s, ((kv_next / kClKvSlots) - 1) & 1, p.error, failed))
-                    break;
-                const int page = i == npc - 1 && holds_last ? last_page : __ldcg(table + pg0 + i);
+            prefetch_l2(plane, kClUnitPlane);
+            prefetch_l2(scales, kClUnitBytes - kClUnitPlane);
+        }
+        for (int n = lane; n < L * npc; n += 32) {
+            const int layer = n / npc, page = __ldcg(table + pg0 + n % npc);
+            for (int which = 0; which < 2; ++which) {
+                const long long off = kv_offset(p.kv, page, layer, which, head, 0);
+                prefetch_l2(static_cast<const uint8_t*>(p.kv.pool) + off * (kBf16 ? 2 : 4), Sh::kKvBlock);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            int w_last[kW], k_last[kClKvSlots], n_last[2];
+            for (int s = 0; s < kW; ++s) w_last[s] = -1;
+            for (int s = 0; s < kClKvSlots; ++s) k_last[s] = -1;
+            n_last[0] = n_last[1] = -1;
+            int w_next = 0, k_next = 0;
+            // Each issue waits (bounded) until the slot it refills has been
+            // released by every consumer of its previous contents.
+            auto issue_unit = [&]() {
+                const int u = w_next++, s = u % kW;
+                if (*failed) return;
+                if (u >= kW && !mbar_wait(wempty0 + 8 * s, ((u / kW) - 1) & 1, p.error, failed)) return;
+                const uint8_t *plane, *scales;
+                cl_unit_src(p, u, rank, plane, scales);
+                uint8_t* dst = w_ring + s * kClUnitBytes;
+                mbar_expect_tx(wfull0 + 8 * s, kClUnitBytes);
+                bulk_load(smem_addr(dst), plane, kClUnitPlane, wfull0 + 8 * s);
+                bulk_load(smem_addr(dst + kClUnitPlane), scales, kClUnitBytes - kClUnitPlane, wfull0 + 8 * s);
+                w_last[s] = u;
+            };
+            auto issue_norm = [&](int n) {  // norm n: layer n / 2, LN1 (even) or LN2 (odd)
+                const int s = n & 1;
+                if (*failed) return;
+                if (n >= 2 && !mbar_wait(nempty0 + 8 * s, ((n >> 1) - 1) & 1, p.error, failed)) return;
+                mbar_expect_tx(nfull0 + 8 * s, kClNormBytes);
+                bulk_load(smem_addr(n_ring + s * kClNormBytes), p.layers[n >> 1].norms + (n & 1) * 2 * kWidth,
+                          kClNormBytes, nfull0 + 8 * s);
+                n_last[s] = n;
+            };
+            auto issue_page = [&](int layer, int i) {  // page ring index k_next = layer * npc + i
+                const int n = k_next++, s = n % kClKvSlots;
+                if (*failed) return;
+                if (n >= kClKvSlots && !mbar_wait(kempty0 + 8 * s, ((n / kClKvSlots) - 1) & 1, p.error, failed))
+                    return;
+                const int page = __ldcg(table + pg0 + i);
                 const int row = (layer * p.kv.pool_pages + page) * 256 + head * kPage;  // K rows; V 128 rows on
                 uint8_t* dst = kv_ring + s * Sh::kKvSlot;
                 const uint32_t bar = kfull0 + 8 * s;
@@ -385,45 +485,18 @@ __global__ void __launch_bounds__(kClThreads, 1)
                     tma_load_2d(smem_addr(dst + bx * Sh::kBox), &tm_kv16, bx * 32, row, bar);
                     tma_load_2d(smem_addr(dst + Sh::kKvBlock + bx * Sh::kBox), &tm_kv16, bx * 32, row + 128, bar);
                 }
-                k_last[s] = kv_next;
+                k_last[s] = n;
+            };
+            // The compute warps' consumption order, layer by layer.
+            for (int l = 0; l < L; ++l) {
+                issue_norm(2 * l);
+                for (int k = 0; k < kClUnitOut; ++k) issue_unit();
+                for (int i = 0; i < npc; ++i) issue_page(l, i);
+                issue_unit();  // out
+                issue_norm(2 * l + 1);
+                for (int k = kClUnitUp; k < kClUnitsPerLayer; ++k) issue_unit();
             }
-        };
-
-        if (issuer) {
-            for (int u = 0; u < kW && u < n_units; ++u) issue_unit(u);
-            for (int n = 0; n < 2 && n < 2 * L; ++n) issue_norm(n);
-        }
-        issue_kv(min(npc, kClKvSlots));
-        __syncwarp();
-        for (int l = 0; l < L; ++l) {
-            const int u0 = kClUnitsPerLayer * l;
-            // A
-            for (int k = 0; k < 3; ++k) refill_after(u0 + k);
-            renorm_after(2 * l);
-            __syncwarp();
-            cluster_sync();
-            // B: the appended page is in global memory now
-            if (issuer) fence_proxy_async_global();
-            kv_last_ok = l;
-            issue_kv(min(min((l + 1) * npc + kClKvSlots, (l + 2) * npc), L * npc));
-            __syncwarp();
-            cluster_sync();
-            // C
-            refill_after(u0 + 3);
-            __syncwarp();
-            cluster_sync();
-            // D
-            for (int k = 4; k < 8; ++k) refill_after(u0 + k);
-            renorm_after(2 * l + 1);
-            __syncwarp();
-            cluster_sync();
-            // E
-            for (int k = 8; k < 12; ++k) refill_after(u0 + k);
-            __syncwarp();
-            cluster_sync();
-        }
-        // Copies still in flight (only after a failure) land before the CTA exits.
-        if (issuer) {
+            // Copies still in flight (only after a failure) land before the CTA exits.
             for (int s = 0; s < kW; ++s)
                 if (w_last[s] >= 0) mbar_drain(wfull0 + 8 * s, (w_last[s] / kW) & 1);
             for (int s = 0; s < kClKvSlots; ++s)
@@ -431,223 +504,232 @@ __global__ void __launch_bounds__(kClThreads, 1)
             for (int s = 0; s < 2; ++s)
                 if (n_last[s] >= 0) mbar_drain(nfull0 + 8 * s, (n_last[s] >> 1) & 1);
         }
-        return;
-    }
-
-    // ---------------------------------------------------------- compute warps
-    const AttnLane<kBf16> ad = cl_attn_lane<kBf16>(lane);
-    const uint32_t q_addr = smem_addr(q_s), part_addr = smem_addr(part_s), h_addr = smem_addr(h_s),
-                   g_addr = smem_addr(g_s), x_addr = smem_addr(x_s);
-    auto wait_unit = [&](int u) { return mbar_wait(wfull0 + 8 * (u % kW), (u / kW) & 1, p.error, failed); };
-    auto release_unit = [&](int u) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(wempty0 + 8 * (u % kW));
-    };
-    auto unit_ptr = [&](int u) { return w_ring + (u % kW) * kClUnitBytes; };
-    // LayerNorm of a 512-wide row (norm n of the ring) into xn_s, by warp 0.
-    auto layer_norm = [&](int n, const float* src) {
-        if (warp != 0) return;
-        const int s = n & 1;
-        const bool got = mbar_wait(nfull0 + 8 * s, (n >> 1) & 1, p.error, failed);
-        CL_MARK(n >> 1, 28 + 2 * (n & 1));
-        if (got) {
-            const float* nw = reinterpret_cast<const float*>(n_ring + s * kClNormBytes);
-            const bool ok = warp_layernorm512(src, nw, nw + kWidth, xn_s);
-            if (!ok && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
-        }
-        CL_MARK(n >> 1, 29 + 2 * (n & 1));
-        __syncwarp();
-        if (lane == 0) mbar_arrive(nempty0 + 8 * s);
-    };
+    } else {
+        // ---------------------------------------------------- compute warps
+        const uint32_t msg_addr = smem_addr(msg_s), h_addr = smem_addr(h_s), g_addr = smem_addr(g_s),
+                       x_addr = smem_addr(x_s);
+        auto wait_unit = [&](int u) { return mbar_wait(wfull0 + 8 * (u % kW), (u / kW) & 1, p.error, failed); };
+        auto release_unit = [&](int u) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(wempty0 + 8 * (u % kW));
+        };
+        auto unit_ptr = [&](int u) { return w_ring + (u % kW) * kClUnitBytes; };
+        // Exchange x of layer `use`: arm its barrier with the bytes it
+        // expects (before or after they arrive), then wait for the phase.
+        auto exchange_wait = [&](int x, uint32_t bytes, int use) {
+            if (threadIdx.x == 0) mbar_expect_tx(xbar0 + 8 * x, bytes);
+            return cl_exchange_wait(xbar0 + 8 * x, use & 1, p.error, failed);
+        };
+        // LayerNorm of a 512-wide row (norm n of the ring) into xn_s, by warp 0.
+        auto layer_norm = [&](int n, const float* src) {
+            if (warp != 0) return;
+            const int s = n & 1;
+            if (mbar_wait(nfull0 + 8 * s, (n >> 1) & 1, p.error, failed)) {
+                const float* nw = reinterpret_cast<const float*>(n_ring + s * kClNormBytes);
+                if (!cl_layernorm(src, nw, nw + kWidth, xn_s) && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(nempty0 + 8 * s);
+        };
 
-    for (int l = 0; l < L; ++l) {
-        const int u0 = kClUnitsPerLayer * l;
-        const bool last_layer = l == L - 1;
+        for (int l = 0; l < L; ++l) {
+            const int u0 = kClUnitsPerLayer * l;
+            const bool last_layer = l == L - 1;
 
-        // ---- A: LN1 -> q, k, v dims [32*half, +32) of the head
-        CL_MARK(l, 0);
-        layer_norm(2 * l, x_s);
-        compute_sync();
-        CL_MARK(l, 1);
-        for (int region = 0; region < 3; ++region) {
-            const int u = u0 + region;
-            const bool got_u = wait_unit(u);
-            CL_MARK(l, 16 + region);
-            if (got_u) {
-                float s[4];
-                cl_rows4<1>(unit_ptr(u), warp, xn_s, s);
-                if (lane < 2) {
-                    const int d = half * 32 + 4 * warp + 2 * lane;  // dim within the head (even)
-                    float v0 = lane ? s[2] : s[0], v1 = lane ? s[3] : s[1];
-                    if (region < 2) rope_apply(v0, v1, rope_s[d >> 1]);
-                    if (!isfinite(v0) || !isfinite(v1)) flag_nonfinite(p.status, 0);
-                    if (region == 0) {
-                        const uint32_t a = q_addr + d * 4;
-                        st_cluster2(cluster_map(a, rank), v0, v1);
-                        st_cluster2(cluster_map(a, rank ^ 1), v0, v1);
-                    } else {
-                        const long long off =
-                            kv_offset(p.kv, last_page, l, region - 1, head, p.pos % kPage) + d;
-                        kv_store2(p.kv, off, v0, v1);
+            // ---- A: LN1 -> q (64), k, v (the CTA's 32 dims) of the head
+            if (l > 0) exchange_wait(CLX_X, kClBytesX, l - 1);
+            CL_MARK(l, 0);
+            layer_norm(2 * l, x_s);
+            compute_sync();
+            CL_MARK(l, 1);
+            for (int k = 0; k < kClUnitOut; ++k) {
+                const int u = u0 + k;
+                if (wait_unit(u)) {
+                    const float4 s = cl_rows4(unit_ptr(u), warp, xn_s, 1);
+                    if (lane == 0) {
+                        // rows 4w .. 4w+3 of the unit: two RoPE pairs (q, k) or plain (v)
+                        float v[4] = {s.x, s.y, s.z, s.w};
+                        const int d = (k < 2 ? 32 * k : 32 * half) + 4 * warp;  // dim within the head
+                        if (k < 3) {
+                            rope_apply(v[0], v[1], rope_s[d >> 1]);
+                            rope_apply(v[2], v[3], rope_s[(d >> 1) + 1]);
+                        }
+                        bool ok = true;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) ok &= isfinite(v[e]);
+                        if (!ok) flag_nonfinite(p.status, 0);
+                        if (k < 2) {
+                            *reinterpret_cast<float4*>(q_s + d) = make_float4(v[0], v[1], v[2], v[3]);
+                        } else {
+                            const long long off = kv_offset(p.kv, p.last_page, l, k - 2, head, p.pos % kPage) + d;
+                            kv_store2(p.kv, off, v[0], v[1]);
+                            kv_store2(p.kv, off + 2, v[2], v[3]);
+                            if (kBf16) {  // the current key joins the softmax as the cache holds it
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) v[e] = bf16_to_f32(f32_to_bf16(v[e]));
+                            }
+                            *reinterpret_cast<float4*>(self_s + 32 * (k - 2) + (d - 32 * half)) =
+                                make_float4(v[0], v[1], v[2], v[3]);
+                        }
                     }
                 }
+                release_unit(u);
             }
-            release_unit(u);
-        }
-        fence_proxy_async_global();  // K/V appends before phase B's TMA reads
-        CL_MARK(l, 2);
-        cluster_sync();
-        CL_MARK(l, 3);
+            compute_sync();
+            CL_MARK(l, 2);
 
-        // ---- B: attention of the head over this CTA's pages
-        {
-            float qh[32];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float4 v = reinterpret_cast<const float4*>(q_s + (lane >> 4) * 32)[i];
-                qh[4 * i] = v.x;
-                qh[4 * i + 1] = v.y;
-                qh[4 * i + 2] = v.z;
-                qh[4 * i + 3] = v.w;
-            }
-            float m = -INFINITY, lsum = 0.0f, a0 = 0.0f, a1 = 0.0f;
-            bool finite_ok = true;
-            for (int i = warp; i < npc; i += kClWarps) {
-                const int n = l * npc + i, s = n % kClKvSlots;
-                const bool got =
-                    __all_sync(kFull, mbar_wait(kfull0 + 8 * s, (n / kClKvSlots) & 1, p.error, failed));
-                if (got) {
-                    const uint8_t* sK = kv_ring + s * Sh::kKvSlot;
-                    attn_page<kBf16>(sK, sK + Sh::kKvBlock, ad, qh, (pg0 + i) * kPage, n_keys, m, lsum, a0, a1,
-                                     finite_ok);
+            // ---- B: attention of the head over this CTA's earlier pages
+            {
+                ClAttnState st{-INFINITY, 0.0f, 0.0f, 0.0f, 1};
+                for (int i = warp; i < npc; i += kClWarps) {
+                    const int n = l * npc + i, s = n % kClKvSlots;
+                    if (__all_sync(kFull, mbar_wait(kfull0 + 8 * s, (n / kClKvSlots) & 1, p.error, failed)))
+                        st = cl_attn_page<kBf16>(kv_ring + s * Sh::kKvSlot, q_s, (pg0 + i) * kPage, p.pos, st);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(kempty0 + 8 * s);
                 }
+                if (!__all_sync(kFull, st.ok != 0) && lane == 0) flag_nonfinite(p.status, 0);
+                float* wp = wpart_s + warp * kClPartStride;
+                *reinterpret_cast<float2*>(wp + 2 + 2 * lane) = make_float2(st.a0, st.a1);
+                if (lane == 0) {
+                    wp[0] = st.m;
+                    wp[1] = st.l;
+                }
+            }
+            compute_sync();
+            if (warp == 0) {  // the CTA's message: warps merged in page order, the current key's halves
+                float M = -INFINITY, S = 0.0f, A0 = 0.0f, A1 = 0.0f;
+                for (int w = 0; w < kClWarps && w < npc; ++w) {
+                    const float* wp = wpart_s + w * kClPartStride;
+                    const MergeWeights mw = merge_weights(M, wp[0]);
+                    S = merge_fold(S, mw, wp[1]);
+                    const float2 pa = *reinterpret_cast<const float2*>(wp + 2 + 2 * lane);
+                    A0 = merge_fold(A0, mw, pa.x);
+                    A1 = merge_fold(A1, mw, pa.y);
+                }
+                // this CTA's half of q.k of the current key (dims [32*half, +32))
+                const float qk = warp_sum(q_s[32 * half + lane] * self_s[lane]);
+                *reinterpret_cast<float2*>(mine_s + 4 + 2 * lane) = make_float2(A0, A1);
+                mine_s[68 + lane] = self_s[32 + lane];
+                if (lane == 0) *reinterpret_cast<float4*>(mine_s) = make_float4(M, S, qk, 0.0f);
+            }
+            compute_sync();
+            // to every CTA: warp w sends the 25 16-byte pieces to CTAs 2w, 2w+1
+            if (lane < kClMsgFloats / 4 && !*failed) {
+                const float4 v = reinterpret_cast<const float4*>(mine_s)[lane];
+                const uint32_t dst = msg_addr + (rank * kClMsgFloats + 4 * lane) * 4;
+                st_async4(dst, xbar0 + 8 * CLX_PART, 2 * warp, v);
+                st_async4(dst, xbar0 + 8 * CLX_PART, 2 * warp + 1, v);
+            }
+            CL_MARK(l, 3);
+
+            // ---- C: merge each head's two CTA partials and the current key;
+            //      h = x + attn Wout^T, slices to every CTA
+            exchange_wait(CLX_PART, kClBytesPart, l);
+            CL_MARK(l, 4);
+            {
+                const int hh = warp;  // warp w merges head w; lane j owns dims 2j, 2j+1
+                float M = -INFINITY, S = 0.0f, A0 = 0.0f, A1 = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const float* pp = msg_s + (2 * hh + k) * kClMsgFloats;
+                    const MergeWeights mw = merge_weights(M, pp[0]);
+                    S = merge_fold(S, mw, pp[1]);
+                    const float2 pa = *reinterpret_cast<const float2*>(pp + 4 + 2 * lane);
+                    A0 = merge_fold(A0, mw, pa.x);
+                    A1 = merge_fold(A1, mw, pa.y);
+                }
+                // the current key: q.k from both halves, v dims 2j, 2j+1 from half j / 16
+                const float* m0 = msg_s + (2 * hh) * kClMsgFloats;
+                const float* m1 = m0 + kClMsgFloats;
+                const float score = __fmul_rn(__fadd_rn(m0[2], m1[2]), 0.125f);
+                const float2 vs = *reinterpret_cast<const float2*>((lane < 16 ? m0 : m1) + 68 + 2 * (lane & 15));
+                bool ok = isfinite(score);
+                const MergeWeights mw = merge_weights(M, score);
+                S = merge_fold(S, mw, 1.0f);
+                A0 = merge_fold(A0, mw, vs.x);
+                A1 = merge_fold(A1, mw, vs.y);
+                ok &= S > 0.0f && isfinite(S);
+                const float inv = __fdiv_rn(1.0f, S);
+                const float o0 = __fmul_rn(A0, inv), o1 = __fmul_rn(A1, inv);
+                ok &= isfinite(o0) && isfinite(o1);
+                *reinterpret_cast<float2*>(a_s + hh * kHeadDim + 2 * lane) = make_float2(o0, o1);
+                if (!__all_sync(kFull, ok) && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
+            }
+            compute_sync();
+            {
+                const int u = u0 + kClUnitOut;
+                if (wait_unit(u)) {
+                    const float4 s = cl_rows4(unit_ptr(u), warp, a_s, 1);
+                    const int r = 32 * rank + 4 * warp;
+                    const float4 h = make_float4(__fadd_rn(x_s[r], s.x), __fadd_rn(x_s[r + 1], s.y),
+                                                 __fadd_rn(x_s[r + 2], s.z), __fadd_rn(x_s[r + 3], s.w));
+                    if (lane == 0 && !(isfinite(h.x) && isfinite(h.y) && isfinite(h.z) && isfinite(h.w)))
+                        flag_nonfinite(p.status, 0);
+                    if (lane < kClusterCtas) st_async4(h_addr + r * 4, xbar0 + 8 * CLX_H, lane, h);
+                }
+                release_unit(u);
+            }
+            CL_MARK(l, 5);
+
+            // ---- D: g = GELU(LN2(h) Wup^T), slices to every CTA
+            exchange_wait(CLX_H, kClBytesH, l);
+            CL_MARK(l, 6);
+            layer_norm(2 * l + 1, h_s);
+            compute_sync();
+            CL_MARK(l, 7);
+            for (int k = 0; k < 4; ++k) {
+                const int u = u0 + kClUnitUp + k;
+                if (wait_unit(u)) {
+                    const float4 s = cl_rows4(unit_ptr(u), warp, xn_s, 1);
+                    const int r = 128 * rank + 32 * k + 4 * warp;
+                    const float4 g = make_float4(gelu_erf(s.x), gelu_erf(s.y), gelu_erf(s.z), gelu_erf(s.w));
+                    if (lane == 0 && !(isfinite(s.x) && isfinite(s.y) && isfinite(s.z) && isfinite(s.w) &&
+                                       isfinite(g.x) && isfinite(g.y) && isfinite(g.z) && isfinite(g.w)))
+                        flag_nonfinite(p.status, 0);
+                    if (lane < kClusterCtas) st_async4(g_addr + r * 4, xbar0 + 8 * CLX_G, lane, g);
+                }
+                release_unit(u);
+            }
+            CL_MARK(l, 8);
+
+            // ---- E: x' = h + g Wdown^T, slices to every CTA (the last layer: to `out`)
+            exchange_wait(CLX_G, kClBytesG, l);
+            CL_MARK(l, 9);
+            {
+                const int u = u0 + kClUnitDown + (warp >> 1);
+                if (wait_unit(u)) {
+                    const float4 s = cl_rows4(unit_ptr(u), warp & 1, g_s, 4);
+                    const int r = 32 * rank + 8 * (warp >> 1) + 4 * (warp & 1);
+                    const float4 x = make_float4(__fadd_rn(h_s[r], s.x), __fadd_rn(h_s[r + 1], s.y),
+                                                 __fadd_rn(h_s[r + 2], s.z), __fadd_rn(h_s[r + 3], s.w));
+                    if (lane == 0 && !(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w)))
+                        flag_nonfinite(p.status, 0);
+                    if (p.trace && lane == 0)
+                        *reinterpret_cast<float4*>(p.trace + static_cast<size_t>(l) * p.trace_stride + r) = x;
+                    if (last_layer) {
+                        if (lane == 0) {  // float-aligned caller rows: scalar stores
+                            p.out[r] = x.x;
+                            p.out[r + 1] = x.y;
+                            p.out[r + 2] = x.z;
+                            p.out[r + 3] = x.w;
+                        }
+                    } else if (lane < kClusterCtas) {
+                        st_async4(x_addr + r * 4, xbar0 + 8 * CLX_X, lane, x);
+                    }
+                }
+                // every warp releases all four down units (each is read by two
+                // warps); the units before them in the ring are released
+                // already, so these arrivals count for this layer's units
                 __syncwarp();
-                if (lane == 0) mbar_arrive(kempty0 + 8 * s);
+                if (lane < 4) mbar_arrive(wempty0 + 8 * ((u0 + kClUnitDown + lane) % kW));
             }
-            if (!__all_sync(kFull, finite_ok) && lane == 0) flag_nonfinite(p.status, 0);
-            float* wp = wpart_s + warp * kClPartStride;
-            *reinterpret_cast<float2*>(wp + 2 + 2 * lane) = make_float2(a0, a1);
-            if (lane == 0) {
-                wp[0] = m;
-                wp[1] = lsum;
-            }
+            CL_MARK(l, 10);
         }
-        CL_MARK(l, 4);
-        compute_sync();
-        CL_MARK(l, 5);
-        if (warp == 0) {  // the CTA's partial: warps in page order, then to every CTA
-            float M = -INFINITY, S = 0.0f, A0 = 0.0f, A1 = 0.0f;
-            for (int w = 0; w < kClWarps && w < npc; ++w) {
-                const float* wp = wpart_s + w * kClPartStride;
-                const MergeWeights mw = merge_weights(M, wp[0]);
-                S = merge_fold(S, mw, wp[1]);
-                const float2 pa = *reinterpret_cast<const float2*>(wp + 2 + 2 * lane);
-                A0 = merge_fold(A0, mw, pa.x);
-                A1 = merge_fold(A1, mw, pa.y);
-            }
-            const uint32_t dst = part_addr + rank * kClPartStride * 4;
-#pragma unroll 4
-            for (int r = 0; r < kClusterCtas; ++r) {
-                const uint32_t a = cluster_map(dst, r);
-                st_cluster2(a + 8 + 8 * lane, A0, A1);
-                if (lane == 0) st_cluster2(a, M, S);
-            }
-        }
-        CL_MARK(l, 6);
-        cluster_sync();
-        CL_MARK(l, 7);
-
-        // ---- C: merge the heads' partials; h = x + attn Wout^T, to every CTA
-        {
-            const int hh = warp;  // warp w merges head w; lane j owns dims 2j, 2j+1
-            float M = -INFINITY, S = 0.0f, A0 = 0.0f, A1 = 0.0f;
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-                const float* pp = part_s + (2 * hh + k) * kClPartStride;
-                const MergeWeights mw = merge_weights(M, pp[0]);
-                S = merge_fold(S, mw, pp[1]);
-                const float2 pa = *reinterpret_cast<const float2*>(pp + 2 + 2 * lane);
-                A0 = merge_fold(A0, mw, pa.x);
-                A1 = merge_fold(A1, mw, pa.y);
-            }
-            bool ok = S > 0.0f && isfinite(S);
-            const float inv = __fdiv_rn(1.0f, S);
-            const float o0 = __fmul_rn(A0, inv), o1 = __fmul_rn(A1, inv);
-            ok &= isfinite(o0) && isfinite(o1);
-            *reinterpret_cast<float2*>(a_s + hh * kHeadDim + 2 * lane) = make_float2(o0, o1);
-            if (!__all_sync(kFull, ok) && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
-        }
-        compute_sync();
-        {
-            const int u = u0 + 3;
-            const bool got_u = wait_unit(u);
-            CL_MARK(l, 19);
-            if (got_u) {
-                float s[4];
-                cl_rows4<1>(unit_ptr(u), warp, a_s, s);
-                const int rr = lane & 3, r = 32 * rank + 4 * warp + rr;
-                const float v = __fadd_rn(x_s[r], pick4(s, rr));
-                if (lane < 4 && !isfinite(v)) flag_nonfinite(p.status, 0);
-                st_cluster(cluster_map(h_addr + r * 4, lane >> 2), v);
-                st_cluster(cluster_map(h_addr + r * 4, (lane >> 2) + 8), v);
-            }
-            release_unit(u);
-        }
-        CL_MARK(l, 8);
-        cluster_sync();
-        CL_MARK(l, 9);
-
-        // ---- D: g = GELU(LN2(h) Wup^T), to every CTA
-        layer_norm(2 * l + 1, h_s);
-        compute_sync();
-        CL_MARK(l, 10);
-        for (int k = 0; k < 4; ++k) {
-            const int u = u0 + 4 + k;
-            const bool got_u = wait_unit(u);
-            CL_MARK(l, 20 + k);
-            if (got_u) {
-                float s[4];
-                cl_rows4<1>(unit_ptr(u), warp, xn_s, s);
-                const int rr = lane & 3, r = 128 * rank + 32 * k + 4 * warp + rr;
-                float v = pick4(s, rr);
-                bool ok = isfinite(v);
-                v = gelu_erf(v);
-                ok &= isfinite(v);
-                if (lane < 4 && !ok) flag_nonfinite(p.status, 0);
-                st_cluster(cluster_map(g_addr + r * 4, lane >> 2), v);
-                st_cluster(cluster_map(g_addr + r * 4, (lane >> 2) + 8), v);
-            }
-            release_unit(u);
-        }
-        CL_MARK(l, 11);
-        cluster_sync();
-        CL_MARK(l, 12);
-
-        // ---- E: x' = h + g Wdown^T, to every CTA (the last layer: to `out`)
-        for (int k = 0; k < 4; ++k) {
-            const int u = u0 + 8 + k;
-            const bool got = wait_unit(u);
-            CL_MARK(l, 24 + k);
-            if (got && (warp >> 1) == k) {
-                float s[4];
-                cl_rows4<4>(unit_ptr(u), warp & 1, g_s, s);
-                const int rr = lane & 3, r = 32 * rank + 4 * warp + rr;
-                const float v = __fadd_rn(h_s[r], pick4(s, rr));
-                if (lane < 4 && !isfinite(v)) flag_nonfinite(p.status, 0);
-                if (p.trace && lane < 4) p.trace[static_cast<size_t>(l) * p.trace_stride + r] = v;
-                if (last_layer) {
-                    if (lane < 4) p.out[r] = v;
-                } else {
-                    st_cluster(cluster_map(x_addr + r * 4, lane >> 2), v);
-                    st_cluster(cluster_map(x_addr + r * 4, (lane >> 2) + 8), v);
-                }
-            }
-            release_unit(u);
-        }
-        CL_MARK(l, 13);
-        cluster_sync();
-        CL_MARK(l, 14);
     }
+    // No CTA exits while another may still store into its shared memory.
+    cluster_sync();
 }
 
 }  // namespace phonon

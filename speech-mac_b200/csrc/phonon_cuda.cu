@@ -1284,6 +1284,7 @@ int enqueue_cluster(PhononCuda* c, int32_t slot, int32_t pos, const std::vector<
     cp.error = c->d_err;
     cp.slot = slot;
     cp.pos = pos;
+    cp.last_page = c->streams[slot].pages[pos / kPage];
     cp.n_updates = static_cast<int>(updates.size() / 3);
     for (size_t i = 0; i < updates.size(); ++i) cp.updates[i] = updates[i];
     cp.freq = c->d_freq;
