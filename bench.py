@@ -286,13 +286,13 @@ def run_ours(args):
     if world > 1:
         import datetime
 
-        os.environ["NCCL_DEBUG"] = "WARN"  # rank 0 prints exactly one line on stdout
-
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        # The data path has no collective: a host-side gloo group only lines
+        # the ranks up around the timed regions and reduces their timings.
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
 
     def barrier():
+        torch.cuda.synchronize()
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
@@ -300,7 +300,7 @@ def run_ours(args):
     def reduce(x, op):
         if not dist:
             return x
-        t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+        t = torch.tensor([float(x)], dtype=torch.float64)
         dist.all_reduce(t, op=op)
         return float(t.item())
 
@@ -380,6 +380,24 @@ def run_ours(args):
     e_tot = reduce(e_frames, dist.ReduceOp.SUM if dist else None)
     e_max = reduce(e_ms, dist.ReduceOp.MAX if dist else None)
 
+    strong = None
+    if world > 1:
+        # configs[3] as specified: 512 streams in total, sharded by request
+        # over the N GPUs (the per-GPU batch shrinks as N grows).
+        ctx.close()
+        server = RankServer(rt, weights, rank, world, local, total_steps, args.streams, args.prefix_max)
+        ctx = server.ctx
+        stream = torch.cuda.ExternalStream(ctx.cuda_stream())
+        for _ in range(args.warmup):
+            device_step()
+        s_frames, s_ms, _, _, _ = timed(device_step, args.steps)
+        s_tot = reduce(s_frames, dist.ReduceOp.SUM)
+        s_max = reduce(s_ms, dist.ReduceOp.MAX)
+        strong = {"value": round(s_tot / (s_max * 1e-3), 1), "unit": UNIT, "scaling": "strong",
+                  "streams_total": args.streams, "streams_per_gpu": round(args.streams / world, 1),
+                  "ms_per_step": round(s_max / args.steps, 4),
+                  "note": "configs[3] as specified: 512 streams in total sharded over the GPUs"}
+
     extras = {}
     if world == 1 and not args.quick:
         extras["single_stream"] = bench_single_stream(rt, synth, weights, torch)
@@ -427,9 +445,17 @@ def run_ours(args):
             "gpu_launches": int(launches),
             "clocks": clocks,
         }
+        if strong:
+            line["strong"] = strong
         line.update(extras)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+            if not args.quick:
+                cpu = cpu_extras()
+                line["single_stream"]["cpu_baseline"] = cpu["config0"]
+                line["q8_matvec"]["cpu_baseline"] = cpu["q8_matvec"]
+                line["config2"]["cpu_baseline"] = cpu["config2"]
+                line["config4"]["cpu_baseline"] = cpu["config4"]
         print(json.dumps(line), flush=True)
     ctx.close()
     if dist:
@@ -644,22 +670,51 @@ def bench_q8_matvec(rt, synth, torch, reps):
 
 
 # --------------------------------------------------------------- CPU baseline
-class RefRunner:
-    """The reference (oracle/_ref) on the configs[3] shape: one host thread
-    per stream, contexts U[64,2048] (seed 2) filled with seeded K/V rows,
-    prepared fp32 linears, OpenBLAS single-threaded per call."""
+def numpy_flow_weights(n_layers, seed=0):
+    """Weights of the configs' architecture for the CPU reference runs, drawn
+    with numpy (PCG64) in the same distributions as the shared generator:
+    Q8_0 blocks with one binary16 scale U(0.5,1.5)/(127*sqrt(cols)) per
+    linear and int8 values uniform in [-127, 127]; LayerNorm gamma ~
+    N(1, 0.02), beta ~ N(0, 0.02) as bf16. The reference's step time does not
+    depend on the values, and this keeps the reference arm free of this
+    repository's native code."""
+    rng = np.random.default_rng(seed)
+    shapes = {"qkv": (1536, 512), "out": (512, 512), "up": (2048, 512), "down": (512, 2048)}
 
-    def __init__(self, threads):
+    def bf16(x):
+        u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+    layers = []
+    for _ in range(n_layers):
+        w = {}
+        for name, (rows, cols) in shapes.items():
+            scale = np.float16(rng.uniform(0.5, 1.5) / (127.0 * np.sqrt(cols)))
+            blocks = np.empty((rows * cols // 32, 34), np.uint8)
+            blocks[:, 0:2] = np.frombuffer(scale.tobytes(), np.uint8)
+            blocks[:, 2:] = rng.integers(-127, 128, (rows * cols // 32, 32), dtype=np.int8).view(np.uint8)
+            w[name] = blocks.ravel()
+        for name, mean in (("norm1_w", 1.0), ("norm1_b", 0.0), ("norm2_w", 1.0), ("norm2_b", 0.0)):
+            w[name] = bf16(mean + 0.02 * rng.standard_normal(512))
+        layers.append(w)
+    return layers
+
+
+class RefRunner:
+    """The reference (oracle/_ref) decoding one stream per host thread:
+    contexts filled with seeded K/V rows through the public PhononKvCache,
+    prepared fp32 linears, OpenBLAS single-threaded per call. Default
+    contexts: the configs[3] draw U[64,2048] (seed 2)."""
+
+    def __init__(self, threads, lens=None):
         from oracle.oracle import REF_SO, Reference
-        from phonon_b200 import synth
         if not REF_SO.exists():
             raise FileNotFoundError("oracle/_ref/libphonon_ref.so is not built")
-        self.synth = synth
         self.threads = threads
         ref = Reference(blas_threads=1)
-        self.model = ref.model(synth.flow_weights(N_LAYERS, seed=0), prepare=True)
+        self.model = ref.model(numpy_flow_weights(N_LAYERS, seed=0), prepare=True)
         rng = np.random.default_rng(2)
-        self.lens = [int(x) for x in rng.integers(64, 2049, threads)]
+        self.lens = [int(x) for x in rng.integers(64, 2049, threads)] if lens is None else list(lens)
         self.cap = max(self.lens) + 2048
         kv = rng.standard_normal((N_LAYERS, max(self.lens), 512), dtype=np.float32)
         self.streams = []
@@ -669,7 +724,7 @@ class RefRunner:
             self.model.fill(s, self.lens[t], keys, keys)
             self.streams.append(s)
         self.pos = list(self.lens)
-        self.x = [synth.stream_generator(5, t).normal(512) for t in range(threads)]
+        self.x = [np.random.default_rng(5 + t).standard_normal(512).astype(np.float32) for t in range(threads)]
 
     def run(self, seconds):
         frames = [0] * self.threads
@@ -696,6 +751,50 @@ class RefRunner:
     def close(self):
         for s in self.streams:
             self.model.free_stream(s)
+
+
+def cpu_extras(seconds=3.0):
+    """The reference's CPU path on the other configs, on the box's host cores
+    (bounded samples, a few seconds each): configs[0] on one thread,
+    configs[1] through phonon_q8_matvec on one thread, configs[2] and
+    configs[4] with one stream per host thread."""
+    out = {}
+    threads = cpu_threads()
+    r = RefRunner(1, lens=[128])
+    r.run(0.5)
+    f, dt = r.run(seconds)
+    r.close()
+    out["config0"] = {"value": round(f / dt, 1), "unit": "frames/s", "cores": 1, "kind": "reference",
+                      "sample": f"1 stream, 12 layers, fp32 KV, contexts from 128 on, {f} frames in {dt:.1f} s"}
+    from oracle.oracle import Reference
+    ref = Reference(blas_threads=1)
+    rng = np.random.default_rng(1)
+    mv = {}
+    for name, (rows, cols) in {"qkv": (1536, 512), "out": (512, 512), "up": (2048, 512),
+                               "down": (512, 2048)}.items():
+        blocks = np.empty((rows * cols // 32, 34), np.uint8)
+        blocks[:, 0:2] = np.frombuffer(np.float16(1.0 / 127).tobytes(), np.uint8)
+        blocks[:, 2:] = rng.integers(-127, 128, (rows * cols // 32, 32), dtype=np.int8).view(np.uint8)
+        x = rng.standard_normal(cols).astype(np.float32)
+        y = np.zeros(rows, np.float32)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / 4:
+            ref.q8_matvec(blocks, x, rows, cols, y)
+            n += 1
+        dt = time.perf_counter() - t0
+        mv[name] = round(blocks.nbytes * n / dt / 1e9, 2)
+    out["q8_matvec"] = {"gbs": mv, "unit": "GB/s of weight bytes", "cores": 1, "kind": "reference",
+                        "sample": f"phonon_q8_matvec, batch 1, {seconds / 4:.2f} s per shape"}
+    lens2 = [int(x) for x in np.random.default_rng(1).integers(32, 513, threads)]
+    for key, lens, what in (("config2", lens2, "prefixes U[32,512] seed 1"),
+                            ("config4", [2304] * min(threads, 8), "contexts 2304 (mid-run of 256..4352)")):
+        r = RefRunner(len(lens), lens=lens)
+        r.run(0.5)
+        f, dt = r.run(seconds)
+        r.close()
+        out[key] = {"value": round(f / dt, 1), "unit": "frames/s", "cores": len(lens), "kind": "reference",
+                    "sample": f"{len(lens)} streams, one per host thread, {what}, fp32 KV, {f} frames in {dt:.1f} s"}
+    return out
 
 
 def cpu_threads():
