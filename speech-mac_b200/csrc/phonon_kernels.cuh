@@ -80,17 +80,34 @@ __device__ __forceinline__ void ln_merge(float a_mean, float a_m2, float& mean, 
     m2 = __fadd_rn(m2, __fadd_rn(a_m2, __fmul_rn(__fmul_rn(__fmul_rn(delta, delta), c), n)));
 }
 
+// One level of the chunk tree: lanes whose chunk index differs in the bit
+// `mask` (a lane bit: chunk = lane >> 2) merge their blocks; the lower
+// chunk is the accumulator holding n samples, the higher one is added with
+// c = 1/2 (equal halves), i.e. ln_merge(higher, lower, 1/2, n). Both lanes
+// of a pair compute the same operation on the same operands.
+__device__ __forceinline__ void ln_tree_level(float& mean, float& m2, int mask, float n) {
+    const int lane = threadIdx.x & 31;
+    const float om = __shfl_xor_sync(kFull, mean, mask), oq = __shfl_xor_sync(kFull, m2, mask);
+    const bool low = (lane & mask) == 0;
+    float lm = low ? mean : om, lq = low ? m2 : oq;
+    ln_merge(low ? om : mean, low ? oq : m2, lm, lq, 0.5f, n);
+    mean = lm;
+    m2 = lq;
+}
+
 // Moments of one 512-wide row held by a warp, lane (chunk*4 + l) holding
 // elements chunk*64 + j*4 + l (j = 0..15), as the reference's moments_512
-// (src/phonon_transformer.c:99-151): a 16-step Welford per lane; then every
-// lane replays, for each of the four lanes l of a chunk, the cascade that
-// folds the 8 chunk results (16 samples each) through three levels of a
-// binary counter (after chunk ch, level 0 carries into level 1 when bit 0 of
-// ch + 1 is clear, level 1 into level 2 when bits 0-1 are), and finally
-// merges the four lanes. The cascade is a loop over chunks, not unrolled:
-// its straight-line form was ~640 instructions, and inside large kernels
-// (the cluster step) fetching them cold cost several microseconds per
-// LayerNorm. Returns the mean and 1/sqrt(var + eps).
+// (src/phonon_transformer.c:99-151): a 16-step Welford per lane; then, for
+// each l, the reference folds the 8 chunk results (16 samples each) through
+// the three levels of a binary counter (after chunk ch, level 0 carries into
+// level 1 when bit 0 of ch + 1 is clear, level 1 into level 2 when bits 0-1
+// are; a block carried onto an empty level is copied exactly, and the final
+// folds of the empty levels 0 and 1 are exact too), which is a balanced
+// tree: ((c0 c1)(c2 c3))((c4 c5)(c6 c7)), every node the merge of two equal
+// halves with the earlier one as accumulator. Here the tree runs across
+// lanes, one shuffle level per tree level, with the reference's operations
+// at every node; then the four lanes l are merged in order. Returns the
+// mean and 1/sqrt(var + eps).
 __device__ __forceinline__ void ln_moments512(const float (&v)[16], float eps, float& mu_out, float& scale_out) {
     constexpr float kRecip[16] = {1.0f / 1,  1.0f / 2,  1.0f / 3,  1.0f / 4,  1.0f / 5,  1.0f / 6,
                                   1.0f / 7,  1.0f / 8,  1.0f / 9,  1.0f / 10, 1.0f / 11, 1.0f / 12,
@@ -102,51 +119,19 @@ __device__ __forceinline__ void ln_moments512(const float (&v)[16], float eps, f
         mean = __fadd_rn(mean, __fmul_rn(delta, kRecip[j]));
         m2 = __fadd_rn(m2, __fmul_rn(delta, __fsub_rn(v[j], mean)));
     }
-    float l0m[4], l0q[4], l1m[4], l1q[4], l2m[4], l2q[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) l0m[k] = l0q[k] = l1m[k] = l1q[k] = l2m[k] = l2q[k] = 0.0f;
-#pragma unroll 1
-    for (int ch = 0; ch < 8; ++ch) {
-        // chunk ch (16 samples) into level 0: onto nothing (even ch) or onto 16
-        const float c0 = (ch & 1) ? 0.5f : 1.0f, n0 = (ch & 1) ? 16.0f : 0.0f;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float fm = __shfl_sync(kFull, mean, ch * 4 + k);
-            const float fq = __shfl_sync(kFull, m2, ch * 4 + k);
-            ln_merge(fm, fq, l0m[k], l0q[k], c0, n0);
-        }
-        if (ch & 1) {  // level 0 (32) carries into level 1: onto nothing or onto 32
-            const float c1 = (ch & 2) ? 0.5f : 1.0f, n1 = (ch & 2) ? 32.0f : 0.0f;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                ln_merge(l0m[k], l0q[k], l1m[k], l1q[k], c1, n1);
-                l0m[k] = l0q[k] = 0.0f;
-            }
-            if (ch & 2) {  // level 1 (64) carries into level 2: onto nothing or onto 64
-                const float c2 = (ch & 4) ? 0.5f : 1.0f, n2 = (ch & 4) ? 64.0f : 0.0f;
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    ln_merge(l1m[k], l1q[k], l2m[k], l2q[k], c2, n2);
-                    l1m[k] = l1q[k] = 0.0f;
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        // final fold of the (now empty) level 1 and of level 2 into level 0
-        ln_merge(l1m[k], l1q[k], l0m[k], l0q[k], 0.0f, 0.0f);
-        ln_merge(l2m[k], l2q[k], l0m[k], l0q[k], 1.0f, 0.0f);
-    }
+    ln_tree_level(mean, m2, 4, 16.0f);   // chunk pairs (16 + 16)
+    ln_tree_level(mean, m2, 8, 32.0f);   // pairs of pairs (32 + 32)
+    ln_tree_level(mean, m2, 16, 64.0f);  // halves (64 + 64)
     // four-lane merge, 128 samples each: c = 1, 1/2, 1/3, 1/4
     float mu = 0.0f, q = 0.0f;
     constexpr float kC[4] = {128.0f / 128.0f, 128.0f / 256.0f, 128.0f / 384.0f, 128.0f / 512.0f};
     constexpr float kN[4] = {0.0f, 128.0f, 256.0f, 384.0f};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const float delta = __fsub_rn(l0m[k], mu);
+        const float lm = __shfl_sync(kFull, mean, k), lq = __shfl_sync(kFull, m2, k);
+        const float delta = __fsub_rn(lm, mu);
         mu = __fmaf_rn(kC[k], delta, mu);
-        q = __fadd_rn(q, __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), kC[k]), kN[k], l0q[k]));
+        q = __fadd_rn(q, __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), kC[k]), kN[k], lq));
     }
     const float var = __fmul_rn(q, 1.0f / 512.0f);  // == q / 512 exactly (power of two)
     mu_out = mu;
