@@ -115,6 +115,14 @@ constexpr uint32_t kClBytesPart = kClusterCtas * kClMsgFloats * 4;  // 16 messag
 constexpr uint32_t kClBytesH = kWidth * 4;                          // 16 slices of 32 rows
 constexpr uint32_t kClBytesG = kFfn * 4;                            // 16 slices of 128 rows
 constexpr uint32_t kClBytesX = kWidth * 4;
+// Activation rows in shared memory are padded: 4 floats after every 64, so
+// that the LayerNorm lanes' stride-4 accesses (lane = chunk * 4 + l) fall into
+// 32 banks; element e lives at cl_pad(e).
+constexpr int kClChunk = 68;
+constexpr int kClRowPad = kWidth / 64 * kClChunk;  // 544 floats
+constexpr int kClFfnPad = kFfn / 64 * kClChunk;    // 2176 floats
+__host__ __device__ constexpr int cl_pad(int e) { return e + 4 * (e >> 6); }
+constexpr int kClNormPadBytes = 2 * kClRowPad * 4;  // a LayerNorm's padded weight + bias
 
 template <bool kBf16>
 struct ClShape {
@@ -126,12 +134,12 @@ struct ClShape {
     static constexpr int kOffKv = 0;
     static constexpr int kOffW = kOffKv + kClKvSlots * kKvSlot;
     static constexpr int kOffNorm = kOffW + kWSlots * kClUnitBytes;
-    static constexpr int kOffX = kOffNorm + 2 * kClNormBytes;      // layer input x [512]
-    static constexpr int kOffXn = kOffX + kWidth * 4;               // LayerNorm output [512]
-    static constexpr int kOffH = kOffXn + kWidth * 4;               // h = x + attn Wout [512]
-    static constexpr int kOffA = kOffH + kWidth * 4;                // attention row [512]
-    static constexpr int kOffG = kOffA + kWidth * 4;                // GELU row [2048]
-    static constexpr int kOffQ = kOffG + kFfn * 4;                  // q of the head [64]
+    static constexpr int kOffX = kOffNorm + 2 * kClNormPadBytes;   // layer input x [512], padded
+    static constexpr int kOffXn = kOffX + kClRowPad * 4;            // LayerNorm output, padded
+    static constexpr int kOffH = kOffXn + kClRowPad * 4;            // h = x + attn Wout, padded
+    static constexpr int kOffA = kOffH + kClRowPad * 4;             // attention row, padded
+    static constexpr int kOffG = kOffA + kClRowPad * 4;             // GELU row [2048], padded
+    static constexpr int kOffQ = kOffG + kClFfnPad * 4;             // q of the head [64]
     static constexpr int kOffSelf = kOffQ + kHeadDim * 4;           // this CTA's k, v of the current key [2][32]
     static constexpr int kOffMsg = kOffSelf + 64 * 4;               // messages of the 16 CTAs [16][100]
     static constexpr int kOffMine = kOffMsg + kClusterCtas * kClMsgFloats * 4;  // this CTA's message [100]
@@ -209,6 +217,10 @@ __device__ __noinline__ bool cl_exchange_wait(uint32_t bar, uint32_t parity, int
     return true;
 }
 
+__device__ __forceinline__ void mbar_arrive_count(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
 // All threads of all CTAs of the cluster; release/acquire at cluster scope.
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
@@ -243,7 +255,7 @@ __device__ __forceinline__ AttnLane<kBf16> cl_attn_lane(int lane) {
 }
 
 // Four rows (local rows 4q .. 4q+3 of a weight unit in shared memory) of a
-// chunks*512-column matrix against one activation row xs: gemv_kernel's
+// chunks*512-column matrix against one padded activation row xs: gemv_kernel's
 // per-lane arithmetic (int8 widened exactly, fp32 dot per 4 columns, scaled
 // fma per 32-block) and butterfly sum. Every lane returns the four row sums.
 __device__ __noinline__ float4 cl_rows4(const uint8_t* unit, int q, const float* xs, int chunks) {
@@ -271,10 +283,11 @@ __device__ __noinline__ float4 cl_rows4(const uint8_t* unit, int q, const float*
             i8x4_to_float(wq.z, wf[rr] + 8);
             i8x4_to_float(wq.w, wf[rr] + 12);
         }
-        const float* xr = xs + c * 512 + lane * 4;
+        // x[c*512 + lane*4 + j*128 .. +3] in the padded row
+        const float* xr = xs + c * (512 / 64 * kClChunk) + lane * 4 + 4 * (lane >> 4);
         float4 xv[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) xv[j] = *reinterpret_cast<const float4*>(xr + j * 128);
+        for (int j = 0; j < 4; ++j) xv[j] = *reinterpret_cast<const float4*>(xr + j * (2 * kClChunk));
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
 #pragma unroll
@@ -290,9 +303,9 @@ __device__ __noinline__ float4 cl_rows4(const uint8_t* unit, int q, const float*
     return make_float4(warp_sum(acc[0]), warp_sum(acc[1]), warp_sum(acc[2]), warp_sum(acc[3]));
 }
 
-// warp_layernorm512 as one routine (one copy of its code in the kernel).
+// warp_layernorm512 on padded rows, as one routine (one copy of its code).
 __device__ __noinline__ bool cl_layernorm(const float* src, const float* w, const float* b, float* dst) {
-    return warp_layernorm512(src, w, b, dst);
+    return warp_layernorm512<false, kClChunk>(src, w, b, dst);
 }
 
 // Online-softmax state of a warp (max, sum, the lane's two accumulated
@@ -415,7 +428,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
         rope_s[threadIdx.x] = make_float2(__double2float_rn(cd), __double2float_rn(sd));
     }
     // scalar loads: the caller's row need only be float-aligned, as on the other step paths
-    for (int i = threadIdx.x; i < kWidth; i += kClThreads) x_s[i] = p.in[i];
+    for (int i = threadIdx.x; i < kWidth; i += kClThreads) x_s[cl_pad(i)] = p.in[i];
     if (rank == 0 && threadIdx.x < p.n_updates) {  // for later steps; this one reads only earlier pages
         const int* u = p.updates + 3 * threadIdx.x;
         const_cast<int32_t*>(p.kv.table)[static_cast<size_t>(u[0]) * p.kv.max_pages + u[1]] = u[2];
@@ -466,8 +479,12 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 if (*failed) return;
                 if (n >= 2 && !mbar_wait(nempty0 + 8 * s, ((n >> 1) - 1) & 1, p.error, failed)) return;
                 mbar_expect_tx(nfull0 + 8 * s, kClNormBytes);
-                bulk_load(smem_addr(n_ring + s * kClNormBytes), p.layers[n >> 1].norms + (n & 1) * 2 * kWidth,
-                          kClNormBytes, nfull0 + 8 * s);
+                // weight and bias, each as 8 chunks of 64 floats into padded rows
+                const float* src = p.layers[n >> 1].norms + (n & 1) * 2 * kWidth;
+                uint8_t* dst = n_ring + s * kClNormPadBytes;
+                for (int k = 0; k < 16; ++k)
+                    bulk_load(smem_addr(dst + ((k >> 3) * kClRowPad + (k & 7) * kClChunk) * 4), src + 64 * k, 256,
+                              nfull0 + 8 * s);
                 n_last[s] = n;
             };
             auto issue_page = [&](int layer, int i) {  // page ring index k_next = layer * npc + i
@@ -509,7 +526,13 @@ __global__ void __launch_bounds__(kClThreads, 1)
         // ---------------------------------------------------- compute warps
         const uint32_t msg_addr = smem_addr(msg_s), h_addr = smem_addr(h_s), g_addr = smem_addr(g_s),
                        x_addr = smem_addr(x_s);
-        auto wait_unit = [&](int u) { return mbar_wait(wfull0 + 8 * (u % kW), (u / kW) & 1, p.error, failed); };
+        // Every wait of a compute warp ends warp-uniform (__all_sync): the
+        // lanes leave a spin loop at different iterations, and a warp that
+        // enters the row dot products or the LayerNorm split into groups of
+        // lanes runs them several times over.
+        auto wait_unit = [&](int u) {
+            return __all_sync(kFull, mbar_wait(wfull0 + 8 * (u % kW), (u / kW) & 1, p.error, failed));
+        };
         auto release_unit = [&](int u) {
             __syncwarp();
             if (lane == 0) mbar_arrive(wempty0 + 8 * (u % kW));
@@ -519,15 +542,15 @@ __global__ void __launch_bounds__(kClThreads, 1)
         // expects (before or after they arrive), then wait for the phase.
         auto exchange_wait = [&](int x, uint32_t bytes, int use) {
             if (threadIdx.x == 0) mbar_expect_tx(xbar0 + 8 * x, bytes);
-            return cl_exchange_wait(xbar0 + 8 * x, use & 1, p.error, failed);
+            return __all_sync(kFull, cl_exchange_wait(xbar0 + 8 * x, use & 1, p.error, failed));
         };
         // LayerNorm of a 512-wide row (norm n of the ring) into xn_s, by warp 0.
         auto layer_norm = [&](int n, const float* src) {
             if (warp != 0) return;
             const int s = n & 1;
-            if (mbar_wait(nfull0 + 8 * s, (n >> 1) & 1, p.error, failed)) {
-                const float* nw = reinterpret_cast<const float*>(n_ring + s * kClNormBytes);
-                if (!cl_layernorm(src, nw, nw + kWidth, xn_s) && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
+            if (__all_sync(kFull, mbar_wait(nfull0 + 8 * s, (n >> 1) & 1, p.error, failed))) {
+                const float* nw = reinterpret_cast<const float*>(n_ring + s * kClNormPadBytes);
+                if (!cl_layernorm(src, nw, nw + kClRowPad, xn_s) && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(nempty0 + 8 * s);
@@ -654,7 +677,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 const float inv = __fdiv_rn(1.0f, S);
                 const float o0 = __fmul_rn(A0, inv), o1 = __fmul_rn(A1, inv);
                 ok &= isfinite(o0) && isfinite(o1);
-                *reinterpret_cast<float2*>(a_s + hh * kHeadDim + 2 * lane) = make_float2(o0, o1);
+                *reinterpret_cast<float2*>(a_s + hh * kClChunk + 2 * lane) = make_float2(o0, o1);  // head hh = chunk hh
                 if (!__all_sync(kFull, ok) && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
             }
             compute_sync();
@@ -663,11 +686,12 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 if (wait_unit(u)) {
                     const float4 s = cl_rows4(unit_ptr(u), warp, a_s, 1);
                     const int r = 32 * rank + 4 * warp;
-                    const float4 h = make_float4(__fadd_rn(x_s[r], s.x), __fadd_rn(x_s[r + 1], s.y),
-                                                 __fadd_rn(x_s[r + 2], s.z), __fadd_rn(x_s[r + 3], s.w));
+                    const float4 xr = *reinterpret_cast<const float4*>(x_s + cl_pad(r));
+                    const float4 h = make_float4(__fadd_rn(xr.x, s.x), __fadd_rn(xr.y, s.y), __fadd_rn(xr.z, s.z),
+                                                 __fadd_rn(xr.w, s.w));
                     if (lane == 0 && !(isfinite(h.x) && isfinite(h.y) && isfinite(h.z) && isfinite(h.w)))
                         flag_nonfinite(p.status, 0);
-                    if (lane < kClusterCtas) st_async4(h_addr + r * 4, xbar0 + 8 * CLX_H, lane, h);
+                    if (lane < kClusterCtas) st_async4(h_addr + cl_pad(r) * 4, xbar0 + 8 * CLX_H, lane, h);
                 }
                 release_unit(u);
             }
@@ -688,7 +712,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
                     if (lane == 0 && !(isfinite(s.x) && isfinite(s.y) && isfinite(s.z) && isfinite(s.w) &&
                                        isfinite(g.x) && isfinite(g.y) && isfinite(g.z) && isfinite(g.w)))
                         flag_nonfinite(p.status, 0);
-                    if (lane < kClusterCtas) st_async4(g_addr + r * 4, xbar0 + 8 * CLX_G, lane, g);
+                    if (lane < kClusterCtas) st_async4(g_addr + cl_pad(r) * 4, xbar0 + 8 * CLX_G, lane, g);
                 }
                 release_unit(u);
             }
@@ -702,8 +726,9 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 if (wait_unit(u)) {
                     const float4 s = cl_rows4(unit_ptr(u), warp & 1, g_s, 4);
                     const int r = 32 * rank + 8 * (warp >> 1) + 4 * (warp & 1);
-                    const float4 x = make_float4(__fadd_rn(h_s[r], s.x), __fadd_rn(h_s[r + 1], s.y),
-                                                 __fadd_rn(h_s[r + 2], s.z), __fadd_rn(h_s[r + 3], s.w));
+                    const float4 hr = *reinterpret_cast<const float4*>(h_s + cl_pad(r));
+                    const float4 x = make_float4(__fadd_rn(hr.x, s.x), __fadd_rn(hr.y, s.y), __fadd_rn(hr.z, s.z),
+                                                 __fadd_rn(hr.w, s.w));
                     if (lane == 0 && !(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w)))
                         flag_nonfinite(p.status, 0);
                     if (p.trace && lane == 0)
@@ -716,14 +741,14 @@ __global__ void __launch_bounds__(kClThreads, 1)
                             p.out[r + 3] = x.w;
                         }
                     } else if (lane < kClusterCtas) {
-                        st_async4(x_addr + r * 4, xbar0 + 8 * CLX_X, lane, x);
+                        st_async4(x_addr + cl_pad(r) * 4, xbar0 + 8 * CLX_X, lane, x);
                     }
                 }
-                // every warp releases all four down units (each is read by two
-                // warps); the units before them in the ring are released
-                // already, so these arrivals count for this layer's units
+                // a down unit is read by two warps: each counts for four of
+                // the slot's eight arrivals, so the slot refills (the next
+                // layer's q/k/v/out/up units) while the other warps still work
                 __syncwarp();
-                if (lane < 4) mbar_arrive(wempty0 + 8 * ((u0 + kClUnitDown + lane) % kW));
+                if (lane == 0) mbar_arrive_count(wempty0 + 8 * (u % kW), kClWarps / 2);
             }
             CL_MARK(l, 10);
         }

@@ -143,21 +143,24 @@ __device__ __forceinline__ void ln_moments512(const float (&v)[16], float eps, f
 // (src/phonon_transformer.c:178-183). x is read once; each lane applies the
 // affine step to the elements it holds. Returns false (on every lane) if an
 // input, weight, bias or output is non-finite. kL2: read x through L2 only
-// (rows that other CTAs of a running kernel wrote).
+// (rows that other CTAs of a running kernel wrote). kChunk: floats from one
+// 64-element chunk of x, w, b and out to the next (64: plain rows; 68: the
+// padded shared-memory rows of the cluster step, where the lanes' strided
+// accesses fall into 32 different banks).
 template <bool kL2 = false>
 __device__ __forceinline__ float ln_load(const float* p) {
     if constexpr (kL2) return __ldcg(p);
     return *p;
 }
 
-template <bool kL2 = false>
+template <bool kL2 = false, int kChunk = 64>
 __device__ __forceinline__ bool warp_layernorm512(const float* __restrict__ x,
                                                   const float* __restrict__ w,
                                                   const float* __restrict__ b,
                                                   float* __restrict__ out,
                                                   float eps = 1e-5f) {
     const int lane = threadIdx.x & 31;
-    const int base = (lane >> 2) * 64 + (lane & 3);
+    const int base = (lane >> 2) * kChunk + (lane & 3);
     float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = ln_load<kL2>(x + base + j * 4);
