@@ -303,6 +303,106 @@ __device__ __noinline__ float4 cl_rows4(const uint8_t* unit, int q, const float*
     return make_float4(warp_sum(acc[0]), warp_sum(acc[1]), warp_sum(acc[2]), warp_sum(acc[3]));
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): each element is computed
+// exactly as the scalar operation would, two rows per instruction.
+__device__ __forceinline__ uint64_t cl_pk(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float2 cl_upk(uint64_t v) {
+    float a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+    return make_float2(a, b);
+}
+__device__ __forceinline__ uint64_t cl_fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t cl_mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t cl_sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+struct ClRows8 {
+    float4 a, b;  // rows 4qa .. 4qa+3 of unit ua, rows 4qb .. 4qb+3 of unit ub
+};
+
+// Eight rows against one padded 512-wide activation row: four rows of unit
+// ua and four of unit ub, computed as four row pairs with packed fp32
+// arithmetic. Per row, every operation and its order are cl_rows4's
+// (gemv_kernel's per-lane arithmetic), so the sums are bit-identical; the
+// pairs halve the instructions and the eight independent chains hide each
+// other's latency.
+__device__ __noinline__ ClRows8 cl_rows8(const uint8_t* ua, int qa, const uint8_t* ub, int qb, const float* xs) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t magic = cl_pk(8388736.0f, 8388736.0f);
+    uint4 wq[8];
+    float sc[8][4];
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) {
+        const uint8_t* unit = rr < 4 ? ua : ub;
+        const int lr = 4 * (rr < 4 ? qa : qb) + (rr & 3);
+        wq[rr] = *reinterpret_cast<const uint4*>(unit + static_cast<size_t>(lr) * 512 + lane * 16);
+        const uint2 raw = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(unit + kClUnitPlane) +
+                                                          static_cast<size_t>(lr) * 16 + (lane >> 3) * 4);
+        const __half2 h01 = *reinterpret_cast<const __half2*>(&raw.x);
+        const __half2 h23 = *reinterpret_cast<const __half2*>(&raw.y);
+        sc[rr][0] = __low2float(h01);
+        sc[rr][1] = __high2float(h01);
+        sc[rr][2] = __low2float(h23);
+        sc[rr][3] = __high2float(h23);
+    }
+    const float* xr = xs + lane * 4 + 4 * (lane >> 4);
+    float4 xv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xv[j] = *reinterpret_cast<const float4*>(xr + j * (2 * kClChunk));
+    uint64_t acc[4];
+#pragma unroll
+    for (int pr = 0; pr < 4; ++pr) acc[pr] = cl_pk(0.0f, 0.0f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float xe[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+        uint64_t x2[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x2[e] = cl_pk(xe[e], xe[e]);
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) {
+            const int r0 = 2 * pr, r1 = 2 * pr + 1;
+            const uint32_t w0 = (j == 0 ? wq[r0].x : j == 1 ? wq[r0].y : j == 2 ? wq[r0].z : wq[r0].w) ^ 0x80808080u;
+            const uint32_t w1 = (j == 0 ? wq[r1].x : j == 1 ? wq[r1].y : j == 2 ? wq[r1].z : wq[r1].w) ^ 0x80808080u;
+            uint64_t wf[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t sel = e | (4 << 4) | (5 << 8) | (7 << 12);
+                wf[e] = cl_sub2(cl_pk(__uint_as_float(__byte_perm(w0, 0x4B000000u, sel)),
+                                      __uint_as_float(__byte_perm(w1, 0x4B000000u, sel))),
+                                magic);
+            }
+            uint64_t part = cl_mul2(wf[0], x2[0]);
+            part = cl_fma2(wf[1], x2[1], part);
+            part = cl_fma2(wf[2], x2[2], part);
+            part = cl_fma2(wf[3], x2[3], part);
+            acc[pr] = cl_fma2(cl_pk(sc[r0][j], sc[r1][j]), part, acc[pr]);
+        }
+    }
+    float sum[8];
+#pragma unroll
+    for (int pr = 0; pr < 4; ++pr) {
+        const float2 v = cl_upk(acc[pr]);
+        sum[2 * pr] = warp_sum(v.x);
+        sum[2 * pr + 1] = warp_sum(v.y);
+    }
+    return ClRows8{make_float4(sum[0], sum[1], sum[2], sum[3]), make_float4(sum[4], sum[5], sum[6], sum[7])};
+}
+
 // warp_layernorm512 on padded rows, as one routine (one copy of its code).
 __device__ __noinline__ bool cl_layernorm(const float* src, const float* w, const float* b, float* dst) {
     return warp_layernorm512<false, kClChunk>(src, w, b, dst);
@@ -566,38 +666,44 @@ __global__ void __launch_bounds__(kClThreads, 1)
             layer_norm(2 * l, x_s);
             compute_sync();
             CL_MARK(l, 1);
-            for (int k = 0; k < kClUnitOut; ++k) {
-                const int u = u0 + k;
-                if (wait_unit(u)) {
-                    const float4 s = cl_rows4(unit_ptr(u), warp, xn_s, 1);
+            for (int k0 = 0; k0 < kClUnitOut; k0 += 2) {
+                const bool got = wait_unit(u0 + k0) & wait_unit(u0 + k0 + 1);
+                if (got) {
+                    const ClRows8 s8 = cl_rows8(unit_ptr(u0 + k0), warp, unit_ptr(u0 + k0 + 1), warp, xn_s);
                     if (lane == 0) {
-                        // rows 4w .. 4w+3 of the unit: two RoPE pairs (q, k) or plain (v)
-                        float v[4] = {s.x, s.y, s.z, s.w};
-                        const int d = (k < 2 ? 32 * k : 32 * half) + 4 * warp;  // dim within the head
-                        if (k < 3) {
-                            rope_apply(v[0], v[1], rope_s[d >> 1]);
-                            rope_apply(v[2], v[3], rope_s[(d >> 1) + 1]);
-                        }
-                        bool ok = true;
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) ok &= isfinite(v[e]);
-                        if (!ok) flag_nonfinite(p.status, 0);
-                        if (k < 2) {
-                            *reinterpret_cast<float4*>(q_s + d) = make_float4(v[0], v[1], v[2], v[3]);
-                        } else {
-                            const long long off = kv_offset(p.kv, p.last_page, l, k - 2, head, p.pos % kPage) + d;
-                            kv_store2(p.kv, off, v[0], v[1]);
-                            kv_store2(p.kv, off + 2, v[2], v[3]);
-                            if (kBf16) {  // the current key joins the softmax as the cache holds it
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) v[e] = bf16_to_f32(f32_to_bf16(v[e]));
+                        for (int kk = 0; kk < 2; ++kk) {
+                            const int k = k0 + kk;
+                            const float4 s = kk ? s8.b : s8.a;
+                            // rows 4w .. 4w+3 of unit k: two RoPE pairs (q, k) or plain (v)
+                            float v[4] = {s.x, s.y, s.z, s.w};
+                            const int d = (k < 2 ? 32 * k : 32 * half) + 4 * warp;  // dim within the head
+                            if (k < 3) {
+                                rope_apply(v[0], v[1], rope_s[d >> 1]);
+                                rope_apply(v[2], v[3], rope_s[(d >> 1) + 1]);
                             }
-                            *reinterpret_cast<float4*>(self_s + 32 * (k - 2) + (d - 32 * half)) =
-                                make_float4(v[0], v[1], v[2], v[3]);
+                            bool ok = true;
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) ok &= isfinite(v[e]);
+                            if (!ok) flag_nonfinite(p.status, 0);
+                            if (k < 2) {
+                                *reinterpret_cast<float4*>(q_s + d) = make_float4(v[0], v[1], v[2], v[3]);
+                            } else {
+                                const long long off = kv_offset(p.kv, p.last_page, l, k - 2, head, p.pos % kPage) + d;
+                                kv_store2(p.kv, off, v[0], v[1]);
+                                kv_store2(p.kv, off + 2, v[2], v[3]);
+                                if (kBf16) {  // the current key joins the softmax as the cache holds it
+#pragma unroll
+                                    for (int e = 0; e < 4; ++e) v[e] = bf16_to_f32(f32_to_bf16(v[e]));
+                                }
+                                *reinterpret_cast<float4*>(self_s + 32 * (k - 2) + (d - 32 * half)) =
+                                    make_float4(v[0], v[1], v[2], v[3]);
+                            }
                         }
                     }
                 }
-                release_unit(u);
+                release_unit(u0 + k0);
+                release_unit(u0 + k0 + 1);
             }
             compute_sync();
             CL_MARK(l, 2);
@@ -703,18 +809,24 @@ __global__ void __launch_bounds__(kClThreads, 1)
             layer_norm(2 * l + 1, h_s);
             compute_sync();
             CL_MARK(l, 7);
-            for (int k = 0; k < 4; ++k) {
-                const int u = u0 + kClUnitUp + k;
-                if (wait_unit(u)) {
-                    const float4 s = cl_rows4(unit_ptr(u), warp, xn_s, 1);
-                    const int r = 128 * rank + 32 * k + 4 * warp;
-                    const float4 g = make_float4(gelu_erf(s.x), gelu_erf(s.y), gelu_erf(s.z), gelu_erf(s.w));
-                    if (lane == 0 && !(isfinite(s.x) && isfinite(s.y) && isfinite(s.z) && isfinite(s.w) &&
-                                       isfinite(g.x) && isfinite(g.y) && isfinite(g.z) && isfinite(g.w)))
-                        flag_nonfinite(p.status, 0);
-                    if (lane < kClusterCtas) st_async4(g_addr + cl_pad(r) * 4, xbar0 + 8 * CLX_G, lane, g);
+            for (int k0 = 0; k0 < 4; k0 += 2) {
+                const int ua = u0 + kClUnitUp + k0;
+                const bool got = wait_unit(ua) & wait_unit(ua + 1);
+                if (got) {
+                    const ClRows8 s8 = cl_rows8(unit_ptr(ua), warp, unit_ptr(ua + 1), warp, xn_s);
+#pragma unroll
+                    for (int kk = 0; kk < 2; ++kk) {
+                        const float4 s = kk ? s8.b : s8.a;
+                        const int r = 128 * rank + 32 * (k0 + kk) + 4 * warp;
+                        const float4 g = make_float4(gelu_erf(s.x), gelu_erf(s.y), gelu_erf(s.z), gelu_erf(s.w));
+                        if (lane == 0 && !(isfinite(s.x) && isfinite(s.y) && isfinite(s.z) && isfinite(s.w) &&
+                                           isfinite(g.x) && isfinite(g.y) && isfinite(g.z) && isfinite(g.w)))
+                            flag_nonfinite(p.status, 0);
+                        if (lane < kClusterCtas) st_async4(g_addr + cl_pad(r) * 4, xbar0 + 8 * CLX_G, lane, g);
+                    }
                 }
-                release_unit(u);
+                release_unit(ua);
+                release_unit(ua + 1);
             }
             CL_MARK(l, 8);
 

@@ -3,25 +3,30 @@
 step_cluster_kernel (speech-mac_b200/csrc/phonon_cluster.cuh) has one copy
 warp that fills three rings of shared-memory slots (weight units, LayerNorm
 vectors, K/V pages) and eight compute warps that consume them; full and
-empty mbarriers pair them up, and all warps of the CTA meet at five cluster
-barriers per layer. A wrong refill schedule would not give wrong numbers, it
-would hang (bounded by the kernel's 2 s wait budget) or silently reuse a slot.
-This model replays, in the kernel's order, every wait, arrival, copy issue
-and barrier of one CTA (the copy warp's per-phase refills, phonon_cluster.cuh
-copy-warp loop; the compute warps' waits and releases per phase), under
-random interleavings, and checks that
+empty mbarriers pair them up. The copy warp issues every unit, norm and page
+in the order the compute warps consume them, each after a bounded wait for
+the release of its slot's previous contents; the compute warps meet at
+named barriers between stages and at the exchanges with the other CTAs. A
+wrong protocol would not give wrong numbers, it would hang (bounded by the
+kernel's 2 s wait budget) or silently reuse a slot. This model replays, in
+the kernel's order, every wait, arrival and copy issue of one CTA (the copy
+warp's issue sequence; the compute warps' waits and releases per stage: QKV
+and up units in pairs, one out unit, down units read by two warps that each
+count for four arrivals), under random interleavings, and checks that
 
-- every wait is eventually satisfied (no deadlock at any barrier),
+- every wait is eventually satisfied (no deadlock),
 - no waiter ever lags two phases behind an mbarrier (the parity would alias),
 - no slot is refilled before every consumer of its previous unit released it.
 
 Mbarriers are modelled by their completed-phase count; a copy completes its
-full barrier when issued (the latency does not change the protocol)."""
+full barrier when issued (the latency does not change the protocol); an
+exchange with the other CTAs is a meeting point of the compute warps."""
 import random
 
 import pytest
 
-UNITS_PER_LAYER = 12  # q, k, v, out, 4 x up, 4 x down
+UNITS_PER_LAYER = 13  # q0, q1, k, v, out, 4 x up, 4 x down
+UNIT_OUT, UNIT_UP, UNIT_DOWN = 4, 5, 9
 KV_SLOTS = 8
 WARPS = 8
 
@@ -30,17 +35,16 @@ class Bar:
     def __init__(self, count):
         self.count, self.pending, self.phase = count, count, 0
 
-    def arrive(self):
-        self.pending -= 1
+    def arrive(self, n=1):
+        self.pending -= n
         assert self.pending >= 0
         if self.pending == 0:
             self.phase += 1
             self.pending = self.count
 
 
-def run(L, npc, w_slots, holds_last, seed, wait_release=True):
+def run(L, npc, w_slots, seed, wait_release=True):
     rnd = random.Random(seed)
-    n_units = UNITS_PER_LAYER * L
     wfull = [Bar(1) for _ in range(w_slots)]
     wempty = [Bar(WARPS) for _ in range(w_slots)]
     nfull, nempty = [Bar(1), Bar(1)], [Bar(1), Bar(1)]
@@ -55,96 +59,84 @@ def run(L, npc, w_slots, holds_last, seed, wait_release=True):
         loaded[key] = idx
         full[idx % nslots].arrive()
 
-    def release(ring, idx, nslots, empty, consumers):
-        releases[(ring, idx)] = releases.get((ring, idx), 0) + 1
+    def release(ring, idx, nslots, empty, consumers, weight=1):
+        releases[(ring, idx)] = releases.get((ring, idx), 0) + weight
         if releases[(ring, idx)] == consumers:
             assert loaded.pop((ring, idx % nslots)) == idx
-        empty[idx % nslots].arrive()
+        empty[idx % nslots].arrive(weight)
 
-    state = {"kv_next": 0, "kv_last_ok": -1}
+    def copy_warp():
+        state = {"u": 0, "k": 0}
 
-    def refill_after(u):  # copy warp: unit u consumed -> unit u + w_slots into its slot
-        if u + w_slots >= n_units:
-            return
-        if wait_release:
-            yield ("wait", wempty[u % w_slots], u // w_slots)
-        issue("w", u + w_slots, w_slots, wfull)
+        def unit():
+            u = state["u"]
+            state["u"] += 1
+            if u >= w_slots and wait_release:
+                yield ("wait", wempty[u % w_slots], u // w_slots - 1)
+            issue("w", u, w_slots, wfull)
 
-    def renorm_after(n):
-        if n + 2 >= 2 * L:
-            return
-        yield ("wait", nempty[n & 1], n >> 1)
-        issue("n", n + 2, 2, nfull)
+        def norm(n):
+            if n >= 2:
+                yield ("wait", nempty[n & 1], (n >> 1) - 1)
+            issue("n", n, 2, nfull)
 
-    def issue_kv(limit):
-        while state["kv_next"] < limit:
-            n = state["kv_next"]
-            layer, i = divmod(n, npc)
-            if holds_last and i == npc - 1 and layer > state["kv_last_ok"]:
-                break  # the appended page waits for its layer's phase A
+        def page():
+            n = state["k"]
+            state["k"] += 1
             if n >= KV_SLOTS:
                 yield ("wait", kempty[n % KV_SLOTS], n // KV_SLOTS - 1)
             issue("k", n, KV_SLOTS, kfull)
-            state["kv_next"] += 1
 
-    def copy_warp():
-        for u in range(min(w_slots, n_units)):
-            issue("w", u, w_slots, wfull)
-        for n in range(min(2, 2 * L)):
-            issue("n", n, 2, nfull)
-        yield from issue_kv(min(npc, KV_SLOTS))
-        for l in range(L):
-            u0 = UNITS_PER_LAYER * l
-            for k in range(3):  # A
-                yield from refill_after(u0 + k)
-            yield from renorm_after(2 * l)
-            yield ("cluster",)
-            state["kv_last_ok"] = l  # B
-            yield from issue_kv(min((l + 1) * npc + KV_SLOTS, (l + 2) * npc, L * npc))
-            yield ("cluster",)
-            yield from refill_after(u0 + 3)  # C
-            yield ("cluster",)
-            for k in range(4, 8):  # D
-                yield from refill_after(u0 + k)
-            yield from renorm_after(2 * l + 1)
-            yield ("cluster",)
-            for k in range(8, 12):  # E
-                yield from refill_after(u0 + k)
-            yield ("cluster",)
+        for _ in range(L):  # the compute warps' consumption order
+            yield from norm(2 * _)
+            for _k in range(UNIT_OUT):
+                yield from unit()
+            for _i in range(npc):
+                yield from page()
+            yield from unit()  # out
+            yield from norm(2 * _ + 1)
+            for _k in range(UNIT_UP, UNITS_PER_LAYER):
+                yield from unit()
 
-    def use_unit(u):
+    def wait_unit(u):
         yield ("wait", wfull[u % w_slots], u // w_slots)
-        release("w", u, w_slots, wempty, WARPS)
 
     def compute_warp(w):
         for l in range(L):
             u0 = UNITS_PER_LAYER * l
+            yield ("meet",)  # exchange of x (layer l > 0)
             if w == 0:  # LN1
                 yield ("wait", nfull[(2 * l) & 1], l)
                 release("n", 2 * l, 2, nempty, 1)
-            yield ("csync",)
-            for k in range(3):
-                yield from use_unit(u0 + k)
-            yield ("cluster",)
-            for i in range(w, npc, KV_SLOTS):  # B: pages w, w + 8, ...
+            yield ("meet",)
+            for k0 in (0, 2):  # QKV units in pairs
+                yield from wait_unit(u0 + k0)
+                yield from wait_unit(u0 + k0 + 1)
+                release("w", u0 + k0, w_slots, wempty, WARPS)
+                release("w", u0 + k0 + 1, w_slots, wempty, WARPS)
+            yield ("meet",)
+            for i in range(w, npc, WARPS):  # B: pages w, w + 8, ...
                 n = l * npc + i
                 yield ("wait", kfull[n % KV_SLOTS], n // KV_SLOTS)
                 release("k", n, KV_SLOTS, kempty, 1)
-            yield ("csync",)
-            yield ("cluster",)
-            yield ("csync",)  # C
-            yield from use_unit(u0 + 3)
-            yield ("cluster",)
+            yield ("meet",)  # warp partials merged, message sent
+            yield ("meet",)  # exchange of the messages, merge of the heads
+            yield from wait_unit(u0 + UNIT_OUT)
+            release("w", u0 + UNIT_OUT, w_slots, wempty, WARPS)
+            yield ("meet",)  # exchange of h
             if w == 0:  # LN2
                 yield ("wait", nfull[(2 * l + 1) & 1], l)
                 release("n", 2 * l + 1, 2, nempty, 1)
-            yield ("csync",)
-            for k in range(4, 8):
-                yield from use_unit(u0 + k)
-            yield ("cluster",)
-            for k in range(8, 12):  # E: every warp waits for and releases all four down units
-                yield from use_unit(u0 + k)
-            yield ("cluster",)
+            yield ("meet",)
+            for k0 in (0, 2):  # up units in pairs
+                yield from wait_unit(u0 + UNIT_UP + k0)
+                yield from wait_unit(u0 + UNIT_UP + k0 + 1)
+                release("w", u0 + UNIT_UP + k0, w_slots, wempty, WARPS)
+                release("w", u0 + UNIT_UP + k0 + 1, w_slots, wempty, WARPS)
+            yield ("meet",)  # exchange of g
+            u = u0 + UNIT_DOWN + (w >> 1)  # E: a down unit is read by two warps, four arrivals each
+            yield from wait_unit(u)
+            release("w", u, w_slots, wempty, WARPS, weight=WARPS // 2)
 
     actors = {"copy": copy_warp(), **{f"w{w}": compute_warp(w) for w in range(WARPS)}}
     blocked = {a: None for a in actors}
@@ -163,16 +155,10 @@ def run(L, npc, w_slots, holds_last, seed, wait_release=True):
                 if bar.phase > phase:
                     runnable.append(a)
         if not runnable:
-            live = [a for a in actors if a not in done]
-            at_cluster = [a for a in live if blocked[a] and blocked[a][0] == "cluster"]
-            at_csync = [a for a in live if blocked[a] and blocked[a][0] == "csync"]
-            compute = [a for a in live if a != "copy"]
-            if at_cluster and len(at_cluster) == len(live):
-                for a in at_cluster:
-                    blocked[a] = None
-                continue
-            if at_csync and sorted(at_csync) == sorted(compute):
-                for a in at_csync:
+            compute = [a for a in actors if a != "copy" and a not in done]
+            meeting = [a for a in compute if blocked[a] and blocked[a][0] == "meet"]
+            if meeting and sorted(meeting) == sorted(compute):
+                for a in meeting:
                     blocked[a] = None
                 continue
             raise AssertionError(f"deadlock: {blocked}")
@@ -188,9 +174,8 @@ def run(L, npc, w_slots, holds_last, seed, wait_release=True):
 @pytest.mark.parametrize("L", [1, 2, 12])
 @pytest.mark.parametrize("npc", [0, 1, 5, 8, 9, 17, 64])
 def test_cluster_rings_never_deadlock_or_alias(L, npc, w_slots):
-    for holds_last in ((False, True) if npc else (False,)):
-        for seed in range(3):
-            run(L, npc, w_slots, holds_last, seed)
+    for seed in range(3):
+        run(L, npc, w_slots, seed)
 
 
 def test_model_catches_a_refill_before_release():
@@ -198,4 +183,4 @@ def test_model_catches_a_refill_before_release():
     waiting for its consumers' release is rejected."""
     with pytest.raises(AssertionError):
         for seed in range(10):
-            run(2, 4, 7, False, seed, wait_release=False)
+            run(2, 4, 7, seed, wait_release=False)
