@@ -644,9 +644,12 @@ __global__ void __launch_bounds__(kClThreads, 1)
             if (threadIdx.x == 0) mbar_expect_tx(xbar0 + 8 * x, bytes);
             return __all_sync(kFull, cl_exchange_wait(xbar0 + 8 * x, use & 1, p.error, failed));
         };
-        // LayerNorm of a 512-wide row (norm n of the ring) into xn_s, by warp 0.
+        // LayerNorm of a 512-wide row (norm n of the ring) into xn_s, by one
+        // warp: LN1 by warp 1, LN2 by warp 0 (measured: LN1 on warp 0, which
+        // shares its scheduler with the copy warp while that warp issues the
+        // next layer's copies, took ~6,000 cycles instead of ~1,800).
         auto layer_norm = [&](int n, const float* src) {
-            if (warp != 0) return;
+            if (warp != ((n & 1) ? 0 : 1)) return;
             const int s = n & 1;
             if (__all_sync(kFull, mbar_wait(nfull0 + 8 * s, (n >> 1) & 1, p.error, failed))) {
                 const float* nw = reinterpret_cast<const float*>(n_ring + s * kClNormPadBytes);
@@ -814,14 +817,21 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 const bool got = wait_unit(ua) & wait_unit(ua + 1);
                 if (got) {
                     const ClRows8 s8 = cl_rows8(unit_ptr(ua), warp, unit_ptr(ua + 1), warp, xn_s);
+                    // lane i < 8 takes the GELU of row sum i (one erf chain per lane
+                    // instead of eight), then every lane gathers the eight
+                    const float sv[8] = {s8.a.x, s8.a.y, s8.a.z, s8.a.w, s8.b.x, s8.b.y, s8.b.z, s8.b.w};
+                    float mine = sv[0];
+#pragma unroll
+                    for (int i = 1; i < 8; ++i) mine = (lane & 7) == i ? sv[i] : mine;
+                    const float gm = gelu_erf(mine);
+                    if (lane < 8 && !(isfinite(mine) && isfinite(gm))) flag_nonfinite(p.status, 0);
+                    float gv[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) gv[i] = __shfl_sync(kFull, gm, i);
 #pragma unroll
                     for (int kk = 0; kk < 2; ++kk) {
-                        const float4 s = kk ? s8.b : s8.a;
                         const int r = 128 * rank + 32 * (k0 + kk) + 4 * warp;
-                        const float4 g = make_float4(gelu_erf(s.x), gelu_erf(s.y), gelu_erf(s.z), gelu_erf(s.w));
-                        if (lane == 0 && !(isfinite(s.x) && isfinite(s.y) && isfinite(s.z) && isfinite(s.w) &&
-                                           isfinite(g.x) && isfinite(g.y) && isfinite(g.z) && isfinite(g.w)))
-                            flag_nonfinite(p.status, 0);
+                        const float4 g = make_float4(gv[4 * kk], gv[4 * kk + 1], gv[4 * kk + 2], gv[4 * kk + 3]);
                         if (lane < kClusterCtas) st_async4(g_addr + cl_pad(r) * 4, xbar0 + 8 * CLX_G, lane, g);
                     }
                 }
