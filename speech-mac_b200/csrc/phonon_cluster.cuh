@@ -254,55 +254,6 @@ __device__ __forceinline__ AttnLane<kBf16> cl_attn_lane(int lane) {
     return a;
 }
 
-// Four rows (local rows 4q .. 4q+3 of a weight unit in shared memory) of a
-// chunks*512-column matrix against one padded activation row xs: gemv_kernel's
-// per-lane arithmetic (int8 widened exactly, fp32 dot per 4 columns, scaled
-// fma per 32-block) and butterfly sum. Every lane returns the four row sums.
-__device__ __noinline__ float4 cl_rows4(const uint8_t* unit, int q, const float* xs, int chunks) {
-    const int cols = chunks * 512;
-    const __half* wsc = reinterpret_cast<const __half*>(unit + kClUnitPlane);
-    const int lane = threadIdx.x & 31;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 1
-    for (int c = 0; c < chunks; ++c) {
-        float wf[4][16], sc[4][4];
-#pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-            const int lr = 4 * q + rr;
-            const uint4 wq = *reinterpret_cast<const uint4*>(unit + static_cast<size_t>(lr) * cols + c * 512 + lane * 16);
-            const uint2 raw =
-                *reinterpret_cast<const uint2*>(wsc + static_cast<size_t>(lr) * (cols / 32) + c * 16 + (lane >> 3) * 4);
-            const __half2 h01 = *reinterpret_cast<const __half2*>(&raw.x);
-            const __half2 h23 = *reinterpret_cast<const __half2*>(&raw.y);
-            sc[rr][0] = __low2float(h01);
-            sc[rr][1] = __high2float(h01);
-            sc[rr][2] = __low2float(h23);
-            sc[rr][3] = __high2float(h23);
-            i8x4_to_float(wq.x, wf[rr] + 0);
-            i8x4_to_float(wq.y, wf[rr] + 4);
-            i8x4_to_float(wq.z, wf[rr] + 8);
-            i8x4_to_float(wq.w, wf[rr] + 12);
-        }
-        // x[c*512 + lane*4 + j*128 .. +3] in the padded row
-        const float* xr = xs + c * (512 / 64 * kClChunk) + lane * 4 + 4 * (lane >> 4);
-        float4 xv[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) xv[j] = *reinterpret_cast<const float4*>(xr + j * (2 * kClChunk));
-#pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float part = wf[rr][j * 4 + 0] * xv[j].x;
-                part = fmaf(wf[rr][j * 4 + 1], xv[j].y, part);
-                part = fmaf(wf[rr][j * 4 + 2], xv[j].z, part);
-                part = fmaf(wf[rr][j * 4 + 3], xv[j].w, part);
-                acc[rr] = fmaf(sc[rr][j], part, acc[rr]);
-            }
-        }
-    }
-    return make_float4(warp_sum(acc[0]), warp_sum(acc[1]), warp_sum(acc[2]), warp_sum(acc[3]));
-}
-
 // Packed fp32 pairs (sm_100 f32x2 arithmetic): each element is computed
 // exactly as the scalar operation would, two rows per instruction.
 __device__ __forceinline__ uint64_t cl_pk(float a, float b) {
@@ -329,6 +280,65 @@ __device__ __forceinline__ uint64_t cl_sub2(uint64_t a, uint64_t b) {
     uint64_t r;
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
+}
+
+// Four rows (local rows 4q .. 4q+3 of a weight unit in shared memory) of a
+// chunks*512-column matrix against one padded activation row xs: gemv_kernel's
+// per-lane arithmetic (int8 widened exactly, fp32 dot per 4 columns, scaled
+// fma per 32-block, in that order per row; two rows per packed f32x2
+// instruction) and butterfly sum. Every lane returns the four row sums.
+__device__ __noinline__ float4 cl_rows4(const uint8_t* unit, int q, const float* xs, int chunks) {
+    const int cols = chunks * 512;
+    const __half* wsc = reinterpret_cast<const __half*>(unit + kClUnitPlane);
+    const int lane = threadIdx.x & 31;
+    const uint64_t magic = cl_pk(8388736.0f, 8388736.0f);
+    uint64_t acc[2] = {cl_pk(0.0f, 0.0f), cl_pk(0.0f, 0.0f)};  // row pairs (0, 1), (2, 3)
+#pragma unroll 1
+    for (int c = 0; c < chunks; ++c) {
+        uint4 wq[4];
+        float sc[4][4];
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+            const int lr = 4 * q + rr;
+            wq[rr] = *reinterpret_cast<const uint4*>(unit + static_cast<size_t>(lr) * cols + c * 512 + lane * 16);
+            const uint2 raw =
+                *reinterpret_cast<const uint2*>(wsc + static_cast<size_t>(lr) * (cols / 32) + c * 16 + (lane >> 3) * 4);
+            const __half2 h01 = *reinterpret_cast<const __half2*>(&raw.x);
+            const __half2 h23 = *reinterpret_cast<const __half2*>(&raw.y);
+            sc[rr][0] = __low2float(h01);
+            sc[rr][1] = __high2float(h01);
+            sc[rr][2] = __low2float(h23);
+            sc[rr][3] = __high2float(h23);
+        }
+        // x[c*512 + lane*4 + j*128 .. +3] in the padded row
+        const float* xr = xs + c * (512 / 64 * kClChunk) + lane * 4 + 4 * (lane >> 4);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 xv = *reinterpret_cast<const float4*>(xr + j * (2 * kClChunk));
+            const uint64_t x2[4] = {cl_pk(xv.x, xv.x), cl_pk(xv.y, xv.y), cl_pk(xv.z, xv.z), cl_pk(xv.w, xv.w)};
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr) {
+                const int r0 = 2 * pr, r1 = 2 * pr + 1;
+                const uint32_t w0 = (j == 0 ? wq[r0].x : j == 1 ? wq[r0].y : j == 2 ? wq[r0].z : wq[r0].w) ^ 0x80808080u;
+                const uint32_t w1 = (j == 0 ? wq[r1].x : j == 1 ? wq[r1].y : j == 2 ? wq[r1].z : wq[r1].w) ^ 0x80808080u;
+                uint64_t wf[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t sel = e | (4 << 4) | (5 << 8) | (7 << 12);
+                    wf[e] = cl_sub2(cl_pk(__uint_as_float(__byte_perm(w0, 0x4B000000u, sel)),
+                                          __uint_as_float(__byte_perm(w1, 0x4B000000u, sel))),
+                                    magic);
+                }
+                uint64_t part = cl_mul2(wf[0], x2[0]);
+                part = cl_fma2(wf[1], x2[1], part);
+                part = cl_fma2(wf[2], x2[2], part);
+                part = cl_fma2(wf[3], x2[3], part);
+                acc[pr] = cl_fma2(cl_pk(sc[r0][j], sc[r1][j]), part, acc[pr]);
+            }
+        }
+    }
+    const float2 a01 = cl_upk(acc[0]), a23 = cl_upk(acc[1]);
+    return make_float4(warp_sum(a01.x), warp_sum(a01.y), warp_sum(a23.x), warp_sum(a23.y));
 }
 
 struct ClRows8 {
@@ -645,9 +655,9 @@ __global__ void __launch_bounds__(kClThreads, 1)
             return __all_sync(kFull, cl_exchange_wait(xbar0 + 8 * x, use & 1, p.error, failed));
         };
         // LayerNorm of a 512-wide row (norm n of the ring) into xn_s, by one
-        // warp: LN1 by warp 1, LN2 by warp 0 (measured: LN1 on warp 0, which
-        // shares its scheduler with the copy warp while that warp issues the
-        // next layer's copies, took ~6,000 cycles instead of ~1,800).
+        // warp: LN1 by warp 1, LN2 by warp 0 (measured with clock64 on B200:
+        // LN1 on warp 0 took ~6,000 cycles from the second layer on, on warp 1
+        // ~1,800; LN2 on warp 0 ~1,700).
         auto layer_norm = [&](int n, const float* src) {
             if (warp != ((n & 1) ? 0 : 1)) return;
             const int s = n & 1;
