@@ -401,6 +401,12 @@ def run_ours(args):
     extras = {}
     if world == 1 and not args.quick:
         extras["single_stream"] = bench_single_stream(rt, synth, weights, torch)
+        extras["prefill"] = bench_prefill(rt, synth, weights, torch)
+        lens3 = [int(x) for x in np.random.default_rng(2).integers(64, 2049, 512)]
+        extras["frame_loop"] = {
+            "configs3": bench_frame_loop(rt, synth, weights, torch, lens3, rt.KV_BF16, 10),
+            "configs0": bench_frame_loop(rt, synth, weights, torch, [128], rt.KV_F32, 100),
+        }
         extras["q8_matvec"] = bench_q8_matvec(rt, synth, torch, args.matvec_reps)
         extras["config2"] = bench_config2(rt, weights, torch)
         extras["config4"] = bench_config4(rt, weights, torch)
@@ -456,6 +462,7 @@ def run_ours(args):
                 line["q8_matvec"]["cpu_baseline"] = cpu["q8_matvec"]
                 line["config2"]["cpu_baseline"] = cpu["config2"]
                 line["config4"]["cpu_baseline"] = cpu["config4"]
+                line["frame_loop"]["cpu_baseline_head"] = cpu["flow_head"]
         print(json.dumps(line), flush=True)
     ctx.close()
     if dist:
@@ -506,6 +513,37 @@ def bench_single_stream(rt, synth, weights, torch):
 
 
 WEIGHT_BYTES_PER_LAYER = 3_342_336  # Q8_0 qkv + out + up + down (34-byte blocks of 32)
+
+
+def bench_prefill(rt, synth, weights, torch, lengths=(128, 2048)):
+    """Prefill (phonon_cuda_append, the batched GPU path of
+    phonon_flow_stack_prefill_cancel) of one stream: rows [len][512] from
+    host memory through all 12 layers into an empty fp32-K/V stream, timed
+    end to end on the host (median of 5 after a warm-up). Positions/s, and
+    the causal attention's fp32 arithmetic rate (2 flops per multiply-add,
+    q.k and p.v over 8 heads x 64 dims for every key a position attends to),
+    the work that dominates a long prefill."""
+    out = {}
+    g = synth.stream_generator(3, 0)
+    for n in lengths:
+        ctx = rt.Context(weights, max_streams=2, max_batch=1, pool_pages=n // 16 + 8, kv_type=rt.KV_F32)
+        rows = np.stack([g.normal(512) for _ in range(n)])
+        times = []
+        for rep in range(6):
+            s = ctx.stream_alloc(n + 1)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            ctx.append(s, rows)
+            times.append(time.perf_counter() - t0)
+            ctx.stream_free(s)
+        ctx.close()
+        t = statistics.median(times[1:])
+        flops = N_LAYERS * 2 * 2 * 512 * (n * (n + 1) / 2)
+        out[f"len{n}"] = {"positions_per_s": round(n / t, 1), "ms": round(t * 1e3, 3),
+                          "attention_tflops": round(flops / t / 1e12, 2)}
+    return {"workload": "prefill of one stream (configs[0] prefix and a configs[3]-length context)",
+            "timing": "host wall clock around phonon_cuda_append (H2D of the rows and D2H of the last output included)",
+            **out}
 
 
 def decode_run(rt, weights, torch, lengths, steps, kv_type, profile_every=0):
@@ -563,6 +601,63 @@ def attention_gbs(rt, weights, torch, lengths, steps, kv_type):
     ctx.close()
     att = prof["attention"]
     return round(att["bytes"] / (att["ms"] * 1e-3) / 1e9, 1)
+
+
+def bench_frame_loop(rt, synth, weights, torch, lengths, kv_type, frames, warmup=3):
+    """The whole frame loop on the device (phonon_cuda_frame_step: EOS logit,
+    flow head LSD step, embedding, 12-layer decode step, output norm) for
+    len(lengths) streams, synthetic K/V prefixes and a random head: stream
+    frames per second over `frames` frames (host clock around the
+    synchronous call, so the H2D of the noise and the D2H of latents and
+    logits are inside), and the head's share of the device time from a
+    second, profiled run."""
+    R = len(lengths)
+    total = warmup + frames
+    pages = sum((int(n) + 2 * total + 15) // 16 + 1 for n in lengths)
+    ctx = rt.Context(weights, max_streams=R + 1, max_batch=R, pool_pages=pages + 8, kv_type=kv_type)
+    head = rt.Head(ctx, synth.flow_head(0), synth.frame_tensors(0))
+    try:
+        ss = [ctx.stream_alloc(int(n) + 2 * total + 1) for n in lengths]
+        for i, (s, n) in enumerate(zip(ss, lengths)):
+            ctx.fill_synthetic(s, int(n), 500 + i)
+        g = torch.Generator(device="cuda").manual_seed(9)
+        x = torch.randn(R, 512, device="cuda", generator=g)
+        state = torch.empty(R, 512, device="cuda")
+        head.output_norm_device(R, x.data_ptr(), state.data_ptr())
+        cond = 0.5 * torch.randn(R, 512, device="cuda", generator=g)
+        rng = np.random.default_rng(9)
+        noise = rng.standard_normal((total, R, 32)).astype(np.float32)
+        pos = [int(n) for n in lengths]
+
+        def frame(k):
+            _, _, status = head.frame_step(ss, pos, state.data_ptr(), cond.data_ptr(), noise[k], 0.8)
+            if status.any():
+                raise RuntimeError("frame failed")
+            for i in range(R):
+                pos[i] += 1
+
+        for k in range(warmup):
+            frame(k)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for k in range(warmup, total):
+            frame(k)
+        dt = time.perf_counter() - t0
+        ctx.profile(True)
+        for k in range(frames):
+            frame(k % total)
+        prof = ctx.profile_read()
+        ctx.profile(False)
+        dev_ms = sum(v["ms"] for v in prof.values())
+        return {"streams": R, "frames": frames, "frames_per_s": round(R * frames / dt, 1),
+                "ms_per_frame": round(dt / frames * 1e3, 4),
+                "head_ms_per_frame": round(prof["head"]["ms"] / frames, 4),
+                "head_share_of_device_time": round(prof["head"]["ms"] / dev_ms, 3),
+                "head_launches_per_frame": round(prof["head"]["launches"] / frames, 1),
+                "timing": "host clock around the synchronous frame call; head share from per-launch CUDA events"}
+    finally:
+        head.close()
+        ctx.close()
 
 
 def bench_config2(rt, weights, torch):
@@ -785,6 +880,18 @@ def cpu_extras(seconds=3.0):
         mv[name] = round(blocks.nbytes * n / dt / 1e9, 2)
     out["q8_matvec"] = {"gbs": mv, "unit": "GB/s of weight bytes", "cores": 1, "kind": "reference",
                         "sample": f"phonon_q8_matvec, batch 1, {seconds / 4:.2f} s per shape"}
+    from phonon_b200 import synth
+    head = synth.flow_head(0)
+    cond = rng.standard_normal(512).astype(np.float32)
+    noise = rng.standard_normal(32).astype(np.float32)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds / 4:
+        ok, _ = ref.flow_lsd_one_step(head, cond, noise, 0.8)
+        assert ok
+        n += 1
+    dt = time.perf_counter() - t0
+    out["flow_head"] = {"value": round(n / dt, 1), "unit": "head steps/s", "cores": 1, "kind": "reference",
+                        "sample": f"phonon_flow_lsd_one_step, one row, {n} calls in {dt:.2f} s"}
     lens2 = [int(x) for x in np.random.default_rng(1).integers(32, 513, threads)]
     for key, lens, what in (("config2", lens2, "prefixes U[32,512] seed 1"),
                             ("config4", [2304] * min(threads, 8), "contexts 2304 (mid-run of 256..4352)")):

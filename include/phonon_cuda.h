@@ -242,7 +242,8 @@ typedef enum {
     PHONON_CUDA_K_DOWN = 5,      /* FFN down + residual */
     PHONON_CUDA_K_OTHER = 6,     /* page-table updates, KV fills */
     PHONON_CUDA_K_FUSED = 7,     /* whole step in one persistent launch (small batches) */
-    PHONON_CUDA_K_COUNT = 8
+    PHONON_CUDA_K_HEAD = 8,      /* frame loop: flow head, EOS, embedding, output norm */
+    PHONON_CUDA_K_COUNT = 9
 } PhononCudaKernelClass;
 /* Enable (1) or disable (0) per-launch event timing; enabling clears the
  * totals. While enabled, every step accumulates per class: device time (ms),
@@ -307,6 +308,73 @@ int phonon_cuda_set_cluster_step(PhononCuda *ctx, uint32_t max_position, int *av
  * No counterpart in the reference: it lets tests compare every layer of a
  * batched step with a CPU layer step given the same input and K/V rows. */
 int phonon_cuda_set_layer_trace(PhononCuda *ctx, float *trace_dev, uint32_t max_rows);
+
+/* ---- the frame loop around the step: flow head, EOS logit, embedding,
+ * output norm (src/phonon_sampler.c:280-402, src/phonon_transformer.c:860-914) ----
+ * Weights are bf16 bits, host memory, borrowed only during
+ * phonon_cuda_head_create. Matrices are row-major [rows][cols], biases
+ * [rows]; the names are the pack tensors phonon_flow_head_load
+ * (src/phonon_sampler.c:160-212) and the frame loop read. */
+typedef struct {
+    const uint16_t *weight, *bias;
+} PhononCudaAffine;
+
+#define PHONON_CUDA_HEAD_BLOCKS 6 /* PHONON_FLOW_HEAD_BLOCKS */
+#define PHONON_CUDA_LATENT 32     /* PHONON_LATENT_WIDTH */
+
+typedef struct {
+    PhononCudaAffine input;                 /* flow_net.input_proj [512][32] */
+    PhononCudaAffine cond;                  /* flow_net.cond_embed [512][512] */
+    PhononCudaAffine time[2][2];            /* time_embed.{0,1}.mlp.{0,2}: [512][256], [512][512] */
+    const uint16_t *time_freqs[2];          /* time_embed.{0,1}.freqs [128] */
+    const uint16_t *time_alpha[2];          /* time_embed.{0,1}.mlp.3.alpha [512] */
+    PhononCudaAffine block_ada[PHONON_CUDA_HEAD_BLOCKS];     /* res_blocks.i.adaLN_modulation.1 [1536][512] */
+    const uint16_t *block_norm_w[PHONON_CUDA_HEAD_BLOCKS];   /* res_blocks.i.in_ln.weight [512] */
+    const uint16_t *block_norm_b[PHONON_CUDA_HEAD_BLOCKS];   /* res_blocks.i.in_ln.bias [512] */
+    PhononCudaAffine block_mlp[PHONON_CUDA_HEAD_BLOCKS][2];  /* res_blocks.i.mlp.{0,2} [512][512] */
+    PhononCudaAffine final_ada;             /* final_layer.adaLN_modulation.1 [1024][512] */
+    PhononCudaAffine final_out;             /* final_layer.linear [32][512] */
+    /* The frame loop's neighbours (flow_lm.*); NULL pointers leave the head
+     * usable on its own but phonon_cuda_frame_step / _output_norm refuse. */
+    PhononCudaAffine eos;                   /* out_eos [1][512] */
+    const uint16_t *embed;                  /* input_linear.weight [512][32], no bias */
+    const uint16_t *out_norm_w, *out_norm_b;  /* out_norm.{weight,bias} [512] */
+} PhononCudaHeadWeights;
+
+typedef struct PhononCudaHead PhononCudaHead;
+/* Upload a head for batches of up to the context's max_batch rows; calls
+ * run on the context's stream under its lock. A non-finite weight is
+ * PHONON_CUDA_NON_FINITE. Free before the context. */
+int phonon_cuda_head_create(PhononCuda *ctx, const PhononCudaHeadWeights *weights, PhononCudaHead **out);
+void phonon_cuda_head_free(PhononCudaHead *head);
+/* phonon_flow_head_forward for `batch` rows (host buffers: condition
+ * [batch][512], state [batch][32], velocity [batch][32]); s and t are shared.
+ * PHONON_CUDA_NON_FINITE when any row fails the reference's checks (no row
+ * is then written). */
+int phonon_cuda_head_forward(PhononCudaHead *head, uint32_t batch, const float *condition, const float *state,
+                             float s, float t, float *velocity);
+/* phonon_flow_lsd_one_step for `batch` rows: output = noise*sqrt(T) +
+ * head(condition, noise*sqrt(T), 0, 1), raw_noise [batch][32]. */
+int phonon_cuda_lsd_one_step(PhononCudaHead *head, uint32_t batch, const float *condition, const float *raw_noise,
+                             float temperature, float *output);
+/* phonon_flow_eos_logit for `batch` rows of state [batch][512]. */
+int phonon_cuda_eos_logit(PhononCudaHead *head, uint32_t batch, const float *state, float *logit);
+/* phonon_flow_output_norm of `batch` device rows (in place allowed). */
+int phonon_cuda_output_norm_device(PhononCudaHead *head, uint32_t batch, const float *x_dev, float *out_dev);
+/* One frame of src/speech.c:127-172 for `batch` streams, all on the device:
+ *   logit = eos(state), latent = lsd_one_step(state, raw_noise, temperature),
+ *   x = input_linear(latent) + condition          (phonon_flow_embed_latent)
+ *   y = decode step of x at positions[i]          (phonon_cuda_step)
+ *   state = output_norm(y)                        (phonon_flow_output_norm)
+ * state_dev [batch][512] (read, then overwritten with the new state) and
+ * condition_dev [batch][512] are device rows; raw_noise [batch][32] is host
+ * memory; eos_logit [batch] and latent [batch][32] are host outputs (the
+ * frame's logit and normalized latent). status[i] as phonon_cuda_step; a row
+ * whose head or embedding is non-finite gets PHONON_CUDA_NON_FINITE and its
+ * stream does not advance. */
+int phonon_cuda_frame_step(PhononCudaHead *head, uint32_t batch, const uint32_t *streams, const uint32_t *positions,
+                           float *state_dev, const float *condition_dev, const float *raw_noise, float temperature,
+                           float *eos_logit, float *latent, int32_t *status);
 
 const char *phonon_cuda_status_string(int status);
 

@@ -6,6 +6,7 @@
 #include "phonon_kernels.cuh"
 #include "phonon_cluster.cuh"
 #include "phonon_persist.cuh"
+#include "phonon_head.cuh"
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -35,6 +36,7 @@ constexpr int kPrefillChunk = 256;  // rows per prefill pass
 // 16: 1683 / 624 / 730, 64: 4741 / 885 / 1106.
 constexpr int kTensorMinBatch = 4;   // streams from which projections run on tcgen05
 constexpr int kMaxSms = 1024;        // bound on the SM count (persistent split table)
+constexpr int kSmCount = 148;        // B200 SMs (launch-shape heuristics only)
 constexpr int kFusedMinBatch = 2;    // default window of the persistent step
 constexpr int kFusedMaxBatch = 3;
 constexpr int kPlanHeader = 8;       // ints of the step plan header in the metadata
@@ -275,7 +277,22 @@ cudaError_t launch_gemv_t(const GemvParams& p, cudaStream_t s) {
         if (e != cudaSuccess) return e;
     }
     const int rows_per_cta = kGemvWarps * kRowsPerWarp;
-    return launch_pdl(kern, dim3((p.rows + rows_per_cta - 1) / rows_per_cta), dim3(kGemvWarps * 32), smem, s, p);
+    const int gx = (p.rows + rows_per_cta - 1) / rows_per_cta;
+    // Large batches of a matrix with few row blocks: split the streams over
+    // grid.y so that about two CTAs per SM run (each re-reads its rows'
+    // weights, a few KB from L2).
+    GemvParams q = p;
+    int gy = 1;
+    const int tiles = (p.B + kBT - 1) / kBT;
+    const int want = (2 * kSmCount + gx - 1) / gx;
+    if (want > 1 && tiles > 1) {
+        gy = std::min(want, tiles);
+        q.b_per_cta = ((tiles + gy - 1) / gy) * kBT;
+        gy = (p.B + q.b_per_cta - 1) / q.b_per_cta;
+    } else {
+        q.b_per_cta = 0;
+    }
+    return launch_pdl(kern, dim3(gx, gy), dim3(kGemvWarps * 32), smem, s, q);
 }
 
 template <bool kQ8, int kChunks, int kSrc, int kEpi>
@@ -2730,6 +2747,515 @@ int phonon_cuda_rope_interleaved(int device, float* values, size_t width, size_t
         e->d_a, static_cast<int>(width), static_cast<int>(heads), static_cast<int>(position), e->d_b, e->d_status);
     if ((st = prim_finish(e))) return st;
     CUDA_TRY(cudaMemcpy(values, e->d_a, width * 4, cudaMemcpyDeviceToHost));
+    return PHONON_CUDA_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ frame loop
+// The flow head, EOS logit, embedding and output norm (phonon_head.cuh) on a
+// context's stream and lock. Matrices fed to gemv_kernel use its
+// lane-interleaved bf16 layout (upload_linear); the small ones the head's own
+// kernels read stay natural row-major bf16.
+struct PhononCudaHead {
+    PhononCuda* c = nullptr;
+    DevLinear cond;                    // [513][512]: cond_embed rows, then the EOS row
+    DevLinear ada;                     // [kAdaRows][512]: every block's adaLN rows, the final layer's last
+    DevLinear mlp[phonon::kHeadBlocks][2];
+    uint16_t* w16 = nullptr;           // natural bf16 matrices (offsets below)
+    const uint16_t *in_w = nullptr, *fin_w = nullptr, *embed_w = nullptr;
+    const uint16_t* time_w[2][2] = {};
+    float* f = nullptr;                // fp32 copies of the vectors (offsets below)
+    float *cond_b = nullptr, *ada_b = nullptr, *mlp_b = nullptr, *in_b = nullptr, *norm_w = nullptr,
+          *norm_b = nullptr, *fin_b = nullptr, *time_b = nullptr, *freqs = nullptr, *alpha = nullptr,
+          *onorm_w = nullptr, *onorm_b = nullptr, *temb = nullptr;
+    bool has_eos = false, has_embed = false, has_onorm = false;
+    bool temb_ok = false;              // temb holds the embeddings of (temb_s, temb_t)
+    float temb_s = 0.0f, temb_t = 0.0f;
+    // scratch for max_batch rows
+    uint32_t cap = 0;
+    float *d_cond = nullptr, *d_y = nullptr, *d_x = nullptr, *d_sy = nullptr, *d_mod = nullptr, *d_h = nullptr,
+          *d_first = nullptr, *d_noise = nullptr, *d_out = nullptr;
+    int32_t* d_status = nullptr;       // [cap + 1]: per row, then the time embeddings'
+    float *h_in = nullptr, *h_out = nullptr;
+    int32_t* h_status = nullptr;
+};
+
+namespace {
+
+void head_release(PhononCudaHead* h) {
+    free_linear(h->cond);
+    free_linear(h->ada);
+    for (auto& m : h->mlp) {
+        free_linear(m[0]);
+        free_linear(m[1]);
+    }
+    for (void* p : {static_cast<void*>(h->w16), static_cast<void*>(h->f), static_cast<void*>(h->d_cond),
+                    static_cast<void*>(h->d_y), static_cast<void*>(h->d_x), static_cast<void*>(h->d_sy),
+                    static_cast<void*>(h->d_mod), static_cast<void*>(h->d_h), static_cast<void*>(h->d_first),
+                    static_cast<void*>(h->d_noise), static_cast<void*>(h->d_out), static_cast<void*>(h->d_status)})
+        if (p) cudaFree(p);
+    if (h->h_in) cudaFreeHost(h->h_in);
+    if (h->h_out) cudaFreeHost(h->h_out);
+    if (h->h_status) cudaFreeHost(h->h_status);
+}
+
+// bf16 bits -> float, false on a non-finite value or a missing vector.
+bool head_vec(const uint16_t* bits, size_t n, float* out) {
+    if (!bits) return false;
+    for (size_t i = 0; i < n; ++i) {
+        if (!bf16_is_finite(bits[i])) return false;
+        const uint32_t u = static_cast<uint32_t>(bits[i]) << 16;
+        std::memcpy(out + i, &u, 4);
+    }
+    return true;
+}
+
+bool head_mat(const uint16_t* bits, size_t n) {
+    if (!bits) return false;
+    for (size_t i = 0; i < n; ++i)
+        if (!bf16_is_finite(bits[i])) return false;
+    return true;
+}
+
+int head_upload(PhononCudaHead* h, const PhononCudaHeadWeights& w) {
+    using namespace phonon;
+    constexpr size_t W = kWidth;
+    // fp32 vectors
+    const size_t n_cond_b = kHeadCondLd, n_ada_b = kAdaRows, n_mlp_b = kHeadBlocks * 2 * W, n_in_b = W,
+                 n_norm = kHeadBlocks * W, n_fin_b = kLatent, n_time_b = 4 * W, n_freqs = 2 * 128,
+                 n_alpha = 2 * W, n_onorm = W, n_temb = 2 * W;
+    std::vector<float> f(n_cond_b + n_ada_b + n_mlp_b + n_in_b + 2 * n_norm + n_fin_b + n_time_b + n_freqs +
+                         n_alpha + 2 * n_onorm + n_temb, 0.0f);
+    size_t o = 0;
+    auto take = [&](size_t n) {
+        const size_t at = o;
+        o += n;
+        return at;
+    };
+    const size_t o_cond_b = take(n_cond_b), o_ada_b = take(n_ada_b), o_mlp_b = take(n_mlp_b), o_in_b = take(n_in_b),
+                 o_norm_w = take(n_norm), o_norm_b = take(n_norm), o_fin_b = take(n_fin_b), o_time_b = take(n_time_b),
+                 o_freqs = take(n_freqs), o_alpha = take(n_alpha), o_onorm_w = take(n_onorm),
+                 o_onorm_b = take(n_onorm), o_temb = take(n_temb);
+    bool ok = head_vec(w.cond.bias, W, &f[o_cond_b]) && head_vec(w.input.bias, W, &f[o_in_b]) &&
+              head_vec(w.final_out.bias, kLatent, &f[o_fin_b]) && head_vec(w.final_ada.bias, 2 * W,
+                                                                           &f[o_ada_b + kHeadBlocks * kAdaBlockRows]);
+    for (int b = 0; b < kHeadBlocks && ok; ++b)
+        ok = head_vec(w.block_ada[b].bias, kAdaBlockRows, &f[o_ada_b + b * kAdaBlockRows]) &&
+             head_vec(w.block_norm_w[b], W, &f[o_norm_w + b * W]) && head_vec(w.block_norm_b[b], W, &f[o_norm_b + b * W]) &&
+             head_vec(w.block_mlp[b][0].bias, W, &f[o_mlp_b + (2 * b) * W]) &&
+             head_vec(w.block_mlp[b][1].bias, W, &f[o_mlp_b + (2 * b + 1) * W]);
+    for (int t = 0; t < 2 && ok; ++t)
+        ok = head_vec(w.time[t][0].bias, W, &f[o_time_b + (2 * t) * W]) &&
+             head_vec(w.time[t][1].bias, W, &f[o_time_b + (2 * t + 1) * W]) &&
+             head_vec(w.time_freqs[t], 128, &f[o_freqs + t * 128]) && head_vec(w.time_alpha[t], W, &f[o_alpha + t * W]);
+    if (!ok) return PHONON_CUDA_NON_FINITE;
+    h->has_eos = w.eos.weight && w.eos.bias;
+    if (h->has_eos && !head_vec(w.eos.bias, 1, &f[o_cond_b + W])) return PHONON_CUDA_NON_FINITE;
+    h->has_onorm = w.out_norm_w && w.out_norm_b;
+    if (h->has_onorm &&
+        !(head_vec(w.out_norm_w, W, &f[o_onorm_w]) && head_vec(w.out_norm_b, W, &f[o_onorm_b])))
+        return PHONON_CUDA_NON_FINITE;
+    h->has_embed = w.embed != nullptr;
+    // natural bf16 matrices: input [512][32], time mlp.0 [512][256] x2, time mlp.2 [512][512] x2,
+    // final [32][512], embed [512][32]
+    const size_t n_in = W * kLatent, n_t0 = W * 256, n_t1 = W * W, n_fin = kLatent * W, n_emb = W * kLatent;
+    std::vector<uint16_t> m16(n_in + 2 * n_t0 + 2 * n_t1 + n_fin + n_emb, 0);
+    if (!head_mat(w.input.weight, n_in) || !head_mat(w.final_out.weight, n_fin)) return PHONON_CUDA_NON_FINITE;
+    std::memcpy(&m16[0], w.input.weight, n_in * 2);
+    for (int t = 0; t < 2; ++t) {
+        if (!head_mat(w.time[t][0].weight, n_t0) || !head_mat(w.time[t][1].weight, n_t1)) return PHONON_CUDA_NON_FINITE;
+        std::memcpy(&m16[n_in + t * n_t0], w.time[t][0].weight, n_t0 * 2);
+        std::memcpy(&m16[n_in + 2 * n_t0 + t * n_t1], w.time[t][1].weight, n_t1 * 2);
+    }
+    std::memcpy(&m16[n_in + 2 * n_t0 + 2 * n_t1], w.final_out.weight, n_fin * 2);
+    if (h->has_embed) {
+        if (!head_mat(w.embed, n_emb)) return PHONON_CUDA_NON_FINITE;
+        std::memcpy(&m16[n_in + 2 * n_t0 + 2 * n_t1 + n_fin], w.embed, n_emb * 2);
+    }
+    // GEMV matrices: cond (+ EOS row), all modulation rows, the MLPs
+    std::vector<uint16_t> cond((W + 1) * W, 0);
+    if (!w.cond.weight) return PHONON_CUDA_NON_FINITE;
+    std::memcpy(cond.data(), w.cond.weight, W * W * 2);
+    if (h->has_eos) std::memcpy(&cond[W * W], w.eos.weight, W * 2);
+    std::vector<uint16_t> ada(static_cast<size_t>(kAdaRows) * W);
+    for (int b = 0; b < kHeadBlocks; ++b) {
+        if (!w.block_ada[b].weight) return PHONON_CUDA_NON_FINITE;
+        std::memcpy(&ada[static_cast<size_t>(b) * kAdaBlockRows * W], w.block_ada[b].weight, kAdaBlockRows * W * 2);
+    }
+    if (!w.final_ada.weight) return PHONON_CUDA_NON_FINITE;
+    std::memcpy(&ada[static_cast<size_t>(kHeadBlocks) * kAdaBlockRows * W], w.final_ada.weight, 2 * W * W * 2);
+    int st;
+    if ((st = upload_linear(PHONON_CUDA_LINEAR_BF16, cond.data(), W + 1, W, &h->cond)) ||
+        (st = upload_linear(PHONON_CUDA_LINEAR_BF16, ada.data(), kAdaRows, W, &h->ada)))
+        return st;
+    for (int b = 0; b < kHeadBlocks; ++b)
+        for (int j = 0; j < 2; ++j) {
+            if (!w.block_mlp[b][j].weight) return PHONON_CUDA_NON_FINITE;
+            if ((st = upload_linear(PHONON_CUDA_LINEAR_BF16, w.block_mlp[b][j].weight, W, W, &h->mlp[b][j]))) return st;
+        }
+    if (cudaMalloc(&h->w16, m16.size() * 2) != cudaSuccess || cudaMalloc(&h->f, f.size() * 4) != cudaSuccess)
+        return PHONON_CUDA_OUT_OF_MEMORY;
+    CUDA_TRY(cudaMemcpy(h->w16, m16.data(), m16.size() * 2, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(h->f, f.data(), f.size() * 4, cudaMemcpyHostToDevice));
+    h->in_w = h->w16;
+    for (int t = 0; t < 2; ++t) {
+        h->time_w[t][0] = h->w16 + n_in + t * n_t0;
+        h->time_w[t][1] = h->w16 + n_in + 2 * n_t0 + t * n_t1;
+    }
+    h->fin_w = h->w16 + n_in + 2 * n_t0 + 2 * n_t1;
+    h->embed_w = h->has_embed ? h->fin_w + n_fin : nullptr;
+    h->cond_b = h->f + o_cond_b;
+    h->ada_b = h->f + o_ada_b;
+    h->mlp_b = h->f + o_mlp_b;
+    h->in_b = h->f + o_in_b;
+    h->norm_w = h->f + o_norm_w;
+    h->norm_b = h->f + o_norm_b;
+    h->fin_b = h->f + o_fin_b;
+    h->time_b = h->f + o_time_b;
+    h->freqs = h->f + o_freqs;
+    h->alpha = h->f + o_alpha;
+    h->onorm_w = h->f + o_onorm_w;
+    h->onorm_b = h->f + o_onorm_b;
+    h->temb = h->f + o_temb;
+    return PHONON_CUDA_OK;
+}
+
+int head_alloc(PhononCudaHead* h, uint32_t cap) {
+    using namespace phonon;
+    const size_t B = cap;
+    h->cap = cap;
+    if (cudaMalloc(&h->d_cond, B * kWidth * 4) != cudaSuccess || cudaMalloc(&h->d_y, B * kHeadCondLd * 4) != cudaSuccess ||
+        cudaMalloc(&h->d_x, B * kWidth * 4) != cudaSuccess || cudaMalloc(&h->d_sy, B * kWidth * 4) != cudaSuccess ||
+        cudaMalloc(&h->d_mod, B * kAdaRows * 4) != cudaSuccess || cudaMalloc(&h->d_h, B * kWidth * 4) != cudaSuccess ||
+        cudaMalloc(&h->d_first, B * kWidth * 4) != cudaSuccess || cudaMalloc(&h->d_noise, B * kLatent * 4) != cudaSuccess ||
+        cudaMalloc(&h->d_out, B * kLatent * 4) != cudaSuccess || cudaMalloc(&h->d_status, (B + 1) * 4) != cudaSuccess ||
+        cudaMallocHost(&h->h_in, B * (kWidth + kLatent) * 4) != cudaSuccess ||
+        cudaMallocHost(&h->h_out, B * (kLatent + 1) * 4) != cudaSuccess ||
+        cudaMallocHost(&h->h_status, (B + 1) * 4) != cudaSuccess)
+        return PHONON_CUDA_OUT_OF_MEMORY;
+    return PHONON_CUDA_OK;
+}
+
+// cond_embed (and the EOS row) of B condition rows at x_dev: h->d_y [B][520].
+int enqueue_head_cond(PhononCudaHead* h, int B, const float* x_dev) {
+    using namespace phonon;
+    PhononCuda* c = h->c;
+    GemvParams p{};
+    p.w = h->cond.plane;
+    p.rows = kWidth + 1;
+    p.cols = kWidth;
+    p.x = x_dev;
+    p.ldx = kWidth;
+    p.B = B;
+    p.bias = h->cond_b;
+    p.y = h->d_y;
+    p.ldy = kHeadCondLd;
+    p.status = h->d_status;
+    LaunchScope ls(c, PHONON_CUDA_K_HEAD, (kWidth + 1) * kWidth * 2.0 + B * (kWidth + kWidth + 1) * 4.0);
+    CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_STORE>(p, c->stream)));
+    return PHONON_CUDA_OK;
+}
+
+// The head for B rows: conditions at x_dev (the cond GEMV's input, already
+// enqueued by the caller through enqueue_head_cond), latents or raw noise
+// in h->d_noise; the result goes to h->d_out. With embed_out, also the
+// next input rows input_linear(result) + condition_rows.
+int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float t, float* embed_out,
+                 const float* condition_rows) {
+    using namespace phonon;
+    PhononCuda* c = h->c;
+    cudaStream_t st = c->stream;
+    if (!h->temb_ok || h->temb_s != s || h->temb_t != t) {
+        for (int k = 0; k < 2; ++k) {
+            LaunchScope ls(c, PHONON_CUDA_K_HEAD, (kWidth * 256 + kWidth * kWidth) * 2.0);
+            head_time_kernel<<<1, 512, 0, st>>>(k == 0 ? s : t, h->freqs + k * 128, h->time_w[k][0],
+                                                h->time_b + (2 * k) * kWidth, h->time_w[k][1],
+                                                h->time_b + (2 * k + 1) * kWidth, h->alpha + k * kWidth,
+                                                h->temb + k * kWidth, h->d_status + h->cap);
+            CUDA_TRY(cudaGetLastError());
+        }
+        h->temb_ok = true;  // withdrawn by the caller if the status word reports a non-finite embedding
+        h->temb_s = s;
+        h->temb_t = t;
+    }
+    {
+        HeadInParams q{};
+        q.noise = h->d_noise;
+        q.noise_scale = scale;
+        q.scaled = lsd ? 1 : 0;
+        q.in_w = h->in_w;
+        q.in_b = h->in_b;
+        q.cond = h->d_y;
+        q.ldc = kHeadCondLd;
+        q.temb = h->temb;
+        q.x = h->d_x;
+        q.silu_y = h->d_sy;
+        q.B = B;
+        q.status = h->d_status;
+        LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kLatent * 2.0 + B * kWidth * 12.0);
+        CUDA_TRY(launch_pdl(head_in_kernel, dim3(B), dim3(512), 0, st, q));
+    }
+    {
+        GemvParams p{};
+        p.w = h->ada.plane;
+        p.rows = kAdaRows;
+        p.cols = kWidth;
+        p.x = h->d_sy;
+        p.ldx = kWidth;
+        p.B = B;
+        p.bias = h->ada_b;
+        p.y = h->d_mod;
+        p.ldy = kAdaRows;
+        p.status = h->d_status;
+        LaunchScope ls(c, PHONON_CUDA_K_HEAD, kAdaRows * kWidth * 2.0 + B * (kWidth + kAdaRows) * 4.0);
+        CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_STORE>(p, st)));
+    }
+    for (int blk = 0; blk < kHeadBlocks; ++blk) {
+        {
+            LaunchScope ls(c, PHONON_CUDA_K_HEAD, B * kWidth * 16.0);
+            CUDA_TRY(launch_pdl(head_block_kernel, dim3((B + 7) / 8), dim3(256), 0, st, static_cast<const float*>(h->d_x),
+                                static_cast<const float*>(h->d_mod), blk,
+                                static_cast<const float*>(h->norm_w + blk * kWidth),
+                                static_cast<const float*>(h->norm_b + blk * kWidth), h->d_h, B, h->d_status));
+        }
+        GemvParams p{};
+        p.rows = kWidth;
+        p.cols = kWidth;
+        p.ldx = kWidth;
+        p.B = B;
+        p.ldy = kWidth;
+        p.status = h->d_status;
+        p.w = h->mlp[blk][0].plane;
+        p.x = h->d_h;
+        p.bias = h->mlp_b + (2 * blk) * kWidth;
+        p.y = h->d_first;
+        {
+            LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kWidth * 2.0 + B * kWidth * 8.0);
+            CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_SILU>(p, st)));
+        }
+        p.w = h->mlp[blk][1].plane;
+        p.x = h->d_first;
+        p.bias = h->mlp_b + (2 * blk + 1) * kWidth;
+        p.y = h->d_x;
+        p.res = h->d_x;
+        p.ldres = kWidth;
+        p.gate = h->d_mod + static_cast<size_t>(blk) * kAdaBlockRows + 2 * kWidth;
+        p.ldgate = kAdaRows;
+        {
+            LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kWidth * 2.0 + B * kWidth * 16.0);
+            CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_GATE>(p, st)));
+        }
+    }
+    HeadFinalParams f{};
+    f.x = h->d_x;
+    f.mod = h->d_mod;
+    f.fin_w = h->fin_w;
+    f.fin_b = h->fin_b;
+    f.noise = h->d_noise;
+    f.noise_scale = scale;
+    f.scaled = lsd ? 1 : 0;
+    f.out = h->d_out;
+    f.embed_w = embed_out ? h->embed_w : nullptr;
+    f.condition = condition_rows;
+    f.embed_out = embed_out;
+    f.B = B;
+    f.status = h->d_status;
+    LaunchScope ls(c, PHONON_CUDA_K_HEAD, kLatent * kWidth * 2.0 + B * kWidth * 12.0);
+    CUDA_TRY(launch_pdl(head_final_kernel, dim3(B), dim3(256), 0, st, f));
+    return PHONON_CUDA_OK;
+}
+
+// Wait for the head's work, read its row statuses (and the time embeddings'
+// word, which fails every row); false if any row failed.
+int head_finish(PhononCudaHead* h, uint32_t B, bool* any_bad) {
+    PhononCuda* c = h->c;
+    CUDA_TRY(cudaMemcpyAsync(h->h_status, h->d_status, B * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(h->h_status + h->cap, h->d_status + h->cap, 4, cudaMemcpyDeviceToHost, c->stream));
+    int st = finish_sync(c, 0);
+    if (st) return st;
+    if (h->h_status[h->cap]) {
+        h->temb_ok = false;
+        cudaMemsetAsync(h->d_status + h->cap, 0, 4, c->stream);
+        for (uint32_t i = 0; i < B; ++i) h->h_status[i] |= PHONON_CUDA_NON_FINITE;
+    }
+    *any_bad = false;
+    for (uint32_t i = 0; i < B; ++i)
+        if (h->h_status[i]) *any_bad = true;
+    return PHONON_CUDA_OK;
+}
+
+int head_begin(PhononCudaHead* h, uint32_t batch) {
+    if (!h || batch < 1 || batch > h->cap) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (h->c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(h->c->cfg.device);
+    if (st) return st;
+    CUDA_TRY(cudaMemsetAsync(h->d_status, 0, batch * 4, h->c->stream));
+    return PHONON_CUDA_OK;
+}
+
+// Host rows -> device through the pinned staging buffer (at float offset
+// `at`: condition rows at 0, latent rows after max_batch condition rows).
+int head_upload_rows(PhononCudaHead* h, float* dst, const float* src, size_t floats, size_t at = 0) {
+    std::memcpy(h->h_in + at, src, floats * 4);
+    CUDA_TRY(cudaMemcpyAsync(dst, h->h_in + at, floats * 4, cudaMemcpyHostToDevice, h->c->stream));
+    return PHONON_CUDA_OK;
+}
+
+int head_run_host(PhononCudaHead* h, uint32_t batch, const float* condition, const float* latent, bool lsd, float scale,
+                  float s, float t, float* out) {
+    std::lock_guard<std::mutex> g(h->c->mu);
+    int st = head_begin(h, batch);
+    if (st) return st;
+    const int B = static_cast<int>(batch);
+    if ((st = head_upload_rows(h, h->d_cond, condition, static_cast<size_t>(B) * phonon::kWidth)) ||
+        (st = head_upload_rows(h, h->d_noise, latent, static_cast<size_t>(B) * phonon::kLatent,
+                               static_cast<size_t>(h->cap) * phonon::kWidth)))
+        return st;
+    if ((st = enqueue_head_cond(h, B, h->d_cond))) return st;
+    if ((st = enqueue_head(h, B, lsd, scale, s, t, nullptr, nullptr))) return st;
+    CUDA_TRY(cudaMemcpyAsync(h->h_out, h->d_out, static_cast<size_t>(B) * phonon::kLatent * 4, cudaMemcpyDeviceToHost,
+                             h->c->stream));
+    bool bad = false;
+    if ((st = head_finish(h, batch, &bad))) return st;
+    if (bad) return PHONON_CUDA_NON_FINITE;
+    std::memcpy(out, h->h_out, static_cast<size_t>(B) * phonon::kLatent * 4);
+    return PHONON_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int phonon_cuda_head_create(PhononCuda* c, const PhononCudaHeadWeights* w, PhononCudaHead** out) {
+    if (!c || !w || !out) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(c->mu);
+    int st = set_device(c->cfg.device);
+    if (st) return st;
+    PhononCudaHead* h = new (std::nothrow) PhononCudaHead;
+    if (!h) return PHONON_CUDA_OUT_OF_MEMORY;
+    h->c = c;
+    if ((st = head_upload(h, *w)) || (st = head_alloc(h, c->cfg.max_batch))) {
+        head_release(h);
+        delete h;
+        return st;
+    }
+    CUDA_TRY(cudaMemset(h->d_status, 0, (h->cap + 1) * 4));
+    *out = h;
+    return PHONON_CUDA_OK;
+}
+
+void phonon_cuda_head_free(PhononCudaHead* h) {
+    if (!h) return;
+    {
+        std::lock_guard<std::mutex> g(h->c->mu);
+        set_device(h->c->cfg.device);
+        cudaStreamSynchronize(h->c->stream);
+        head_release(h);
+    }
+    delete h;
+}
+
+int phonon_cuda_head_forward(PhononCudaHead* h, uint32_t batch, const float* condition, const float* state, float s,
+                             float t, float* velocity) {
+    if (!h || !condition || !state || !velocity) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (!std::isfinite(s) || !std::isfinite(t)) return PHONON_CUDA_NON_FINITE;
+    return head_run_host(h, batch, condition, state, false, 1.0f, s, t, velocity);
+}
+
+int phonon_cuda_lsd_one_step(PhononCudaHead* h, uint32_t batch, const float* condition, const float* raw_noise,
+                             float temperature, float* output) {
+    if (!h || !condition || !raw_noise || !output) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (!std::isfinite(temperature) || !(temperature > 0.0f)) return PHONON_CUDA_INVALID_ARGUMENT;
+    return head_run_host(h, batch, condition, raw_noise, true, std::sqrt(temperature), 0.0f, 1.0f, output);
+}
+
+int phonon_cuda_eos_logit(PhononCudaHead* h, uint32_t batch, const float* state, float* logit) {
+    if (!h || !state || !logit) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (!h->has_eos) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(h->c->mu);
+    int st = head_begin(h, batch);
+    if (st) return st;
+    if ((st = head_upload_rows(h, h->d_cond, state, static_cast<size_t>(batch) * phonon::kWidth))) return st;
+    if ((st = enqueue_head_cond(h, static_cast<int>(batch), h->d_cond))) return st;
+    CUDA_TRY(cudaMemcpy2DAsync(h->h_out, 4, h->d_y + phonon::kWidth, phonon::kHeadCondLd * 4, 4, batch,
+                               cudaMemcpyDeviceToHost, h->c->stream));
+    bool bad = false;
+    if ((st = head_finish(h, batch, &bad))) return st;
+    if (bad) return PHONON_CUDA_NON_FINITE;
+    std::memcpy(logit, h->h_out, batch * 4);
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_output_norm_device(PhononCudaHead* h, uint32_t batch, const float* x_dev, float* out_dev) {
+    if (!h || !x_dev || !out_dev || !h->has_onorm) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(h->c->mu);
+    int st = head_begin(h, batch);
+    if (st) return st;
+    {
+        LaunchScope ls(h->c, PHONON_CUDA_K_HEAD, batch * phonon::kWidth * 8.0);
+        CUDA_TRY(launch_pdl(output_norm_kernel, dim3((batch + 7) / 8), dim3(256), 0, h->c->stream, x_dev,
+                            static_cast<const float*>(h->onorm_w), static_cast<const float*>(h->onorm_b), out_dev,
+                            static_cast<int>(batch), h->d_status));
+    }
+    bool bad = false;
+    if ((st = head_finish(h, batch, &bad))) return st;
+    return bad ? PHONON_CUDA_NON_FINITE : PHONON_CUDA_OK;
+}
+
+int phonon_cuda_frame_step(PhononCudaHead* h, uint32_t batch, const uint32_t* streams, const uint32_t* positions,
+                           float* state_dev, const float* condition_dev, const float* raw_noise, float temperature,
+                           float* eos_logit, float* latent, int32_t* status) {
+    if (!h || !state_dev || !condition_dev || !raw_noise || !eos_logit || !latent || !status)
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    if (!h->has_eos || !h->has_embed || !h->has_onorm) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (!std::isfinite(temperature) || !(temperature > 0.0f)) return PHONON_CUDA_INVALID_ARGUMENT;
+    PhononCuda* c = h->c;
+    std::lock_guard<std::mutex> g(c->mu);
+    int st = head_begin(h, batch);
+    if (st) return st;
+    std::vector<int32_t> slot, pos, updates;
+    PageUndo undo{c, {}};
+    if ((st = prepare_decode(c, batch, streams, positions, slot, pos, updates, undo, true))) return st;
+    const int B = static_cast<int>(batch);
+    if ((st = head_upload_rows(h, h->d_noise, raw_noise, static_cast<size_t>(B) * phonon::kLatent))) return st;
+    bool cancelled = false;
+    if ((st = enqueue_head_cond(h, B, state_dev)) ||
+        (st = enqueue_head(h, B, true, std::sqrt(temperature), 0.0f, 1.0f, c->d_x0, condition_dev))) {
+        undo.rollback();
+        return st;
+    }
+    // A memset between the head and the step: the step's first kernels were
+    // written to follow a copy, and this ordering point keeps any of them
+    // that read their input before griddepcontrol.wait after the head's end.
+    CUDA_TRY(cudaMemsetAsync(c->d_status, 0, batch * 4, c->stream));
+    if ((st = enqueue_decode(c, slot, pos, updates, c->d_x0, c->d_y, nullptr, nullptr, &cancelled))) {
+        undo.rollback();
+        return st;
+    }
+    {
+        LaunchScope ls(c, PHONON_CUDA_K_HEAD, B * phonon::kWidth * 8.0);
+        CUDA_TRY(launch_pdl(output_norm_kernel, dim3((B + 7) / 8), dim3(256), 0, c->stream,
+                            static_cast<const float*>(c->d_y), static_cast<const float*>(h->onorm_w),
+                            static_cast<const float*>(h->onorm_b), state_dev, B, h->d_status));
+    }
+    CUDA_TRY(cudaMemcpyAsync(h->h_out, h->d_out, static_cast<size_t>(B) * phonon::kLatent * 4, cudaMemcpyDeviceToHost,
+                             c->stream));
+    CUDA_TRY(cudaMemcpy2DAsync(h->h_out + static_cast<size_t>(B) * phonon::kLatent, 4, h->d_y + phonon::kWidth,
+                               phonon::kHeadCondLd * 4, 4, batch, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(c->h_status, c->d_status, batch * 4, cudaMemcpyDeviceToHost, c->stream));
+    bool bad = false;
+    if ((st = head_finish(h, batch, &bad))) return st;
+    for (uint32_t i = 0; i < batch; ++i) {
+        int32_t s = c->h_status[i] ? c->h_status[i] : PHONON_CUDA_OK;
+        if (h->h_status[i]) s = PHONON_CUDA_NON_FINITE;
+        status[i] = s;
+        if (s != PHONON_CUDA_OK) continue;
+        c->streams[streams[i]].length++;
+        std::memcpy(latent + static_cast<size_t>(i) * phonon::kLatent,
+                    h->h_out + static_cast<size_t>(i) * phonon::kLatent, phonon::kLatent * 4);
+        eos_logit[i] = h->h_out[static_cast<size_t>(B) * phonon::kLatent + i];
+    }
     return PHONON_CUDA_OK;
 }
 

@@ -1,0 +1,288 @@
+// The frame loop around the decode step, on the device: the flow head (the
+// MLP that turns a transformer output row into the next 32-wide latent,
+// speech-mac src/phonon_sampler.c:280-393), the EOS logit
+// (src/phonon_sampler.c:395-402), phonon_flow_embed_latent and
+// phonon_flow_output_norm (src/phonon_transformer.c:860-914).
+//
+// The head's linears are bf16 matrices applied with gemv_kernel (fp32
+// arithmetic, bias added after the sum); everything between them runs here,
+// one warp or one CTA per stream row:
+//
+//   head_time_kernel     time embedding of one flow time (sin/cos, MLP, RMS
+//                        normalisation with a learned gain), stream-independent
+//   head_in_kernel       x = input_proj(noise), silu(cond_embed(c) + time terms)
+//   head_block_kernel    LayerNorm(x) modulated by the block's shift/scale
+//   (gemv EPI_SILU)      silu(mlp.0(h))
+//   (gemv EPI_GATE)      x += gate * mlp.2(...)
+//   head_final_kernel    final LayerNorm + modulation, final linear, the Euler
+//                        step noise + velocity, and the embedding of that
+//                        latent as the next step's input row
+//
+// Sums that the reference evaluates in a fixed order outside BLAS (the
+// 512-element means, the double variance) follow that order; the linears
+// sum in the GEMV's order, as the reference's SGEMM calls do in theirs.
+#pragma once
+
+#include "phonon_kernels.cuh"
+
+namespace phonon {
+
+constexpr int kHeadBlocks = 6;                          // PHONON_FLOW_HEAD_BLOCKS
+constexpr int kLatent = 32;                             // PHONON_LATENT_WIDTH
+constexpr int kAdaBlockRows = 3 * kWidth;               // shift, scale, gate
+constexpr int kAdaRows = kHeadBlocks * kAdaBlockRows + 2 * kWidth;  // every modulation row, final layer last
+constexpr int kHeadCondLd = 520;                        // cond_embed rows, then the EOS row, padded
+
+// Mean of a 512-wide row in the order of src/phonon_sampler.c:229-248 (the
+// reference's restatement of PyTorch's SumKernel): element
+// e = chunk*256 + group*16 + v*4 + l; each (chunk, v, l) sums its 16 groups
+// from zero in order, the two chunks are added into a zeroed accumulator,
+// the vectors v = 1..3 are added to v = 0 in order, and the four lanes are
+// summed from zero. Lane (chunk*16 + v*4 + l) owns one chain; every lane
+// returns the mean. `row` may be shared or global memory.
+__device__ __forceinline__ float head_mean512(const float* row) {
+    const int lane = threadIdx.x & 31;
+    float p = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) p = __fadd_rn(p, row[(lane >> 4) * 256 + g * 16 + (lane & 15)]);
+    const float p1 = __shfl_down_sync(kFull, p, 16);          // chunk 1 of the same (v, l)
+    const float s = __fadd_rn(__fadd_rn(0.0f, p), p1);        // sums[v][l], lanes 0..15
+    const int l = lane & 3;
+    const float s1 = __shfl_sync(kFull, s, 4 + l), s2 = __shfl_sync(kFull, s, 8 + l),
+                s3 = __shfl_sync(kFull, s, 12 + l);
+    const float f = __fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3);  // sums[0][l], lanes 0..3
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) sum = __fadd_rn(sum, __shfl_sync(kFull, f, k));
+    return __fmul_rn(sum, 1.0f / 512.0f);  // == sum / 512 (power of two)
+}
+
+// The head's LayerNorm (src/phonon_sampler.c:250-278) of a 512-wide row in
+// shared memory, by one warp: float mean (head_mean512), variance from the
+// double sum of centred squares rounded once to float, eps 1e-6, optional
+// affine, then the adaLN modulation out = h * (1 + scale) + shift. Lane i
+// writes elements i + 32k. Returns false on every lane if an input, weight,
+// bias or result is non-finite.
+__device__ __forceinline__ bool head_ln_modulate(const float* x, const float* w, const float* b, const float* shift,
+                                                 const float* scale, float* out) {
+    const int lane = threadIdx.x & 31;
+    bool ok = true;
+    for (int k = 0; k < 16; ++k) {
+        const int i = lane + 32 * k;
+        ok &= isfinite(x[i]) && (!w || isfinite(w[i])) && (!b || isfinite(b[i]));
+    }
+    ok = __all_sync(kFull, ok);
+    const float mean = head_mean512(x);
+    double sq = 0.0;
+    for (int k = 0; k < 16; ++k) {
+        const double c = __dsub_rn(static_cast<double>(x[lane + 32 * k]), static_cast<double>(mean));
+        sq = __dadd_rn(sq, __dmul_rn(c, c));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
+    const float variance = static_cast<float>(sq / 512.0);
+    const float inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, 1e-6f)));
+    for (int k = 0; k < 16; ++k) {
+        const int i = lane + 32 * k;
+        float n = __fmul_rn(__fsub_rn(x[i], mean), inverse);
+        if (w) n = __fmul_rn(n, w[i]);
+        if (b) n = __fadd_rn(n, b[i]);
+        ok &= isfinite(n);
+        const float v = __fadd_rn(__fmul_rn(n, __fadd_rn(1.0f, scale[i])), shift[i]);
+        out[i] = v;
+    }
+    return __all_sync(kFull, ok);
+}
+
+// Row r of a natural row-major bf16 matrix [rows][cols] times v (shared
+// memory), summed by one warp (cols a multiple of 32): lane-strided partial
+// sums, then the warp tree.
+__device__ __forceinline__ float head_row_dot(const uint16_t* __restrict__ w, int cols, int r, const float* v) {
+    const int lane = threadIdx.x & 31;
+    const uint16_t* row = w + static_cast<size_t>(r) * cols;
+    float acc = 0.0f;
+    for (int k = lane; k < cols; k += 32) acc = fmaf(bf16_to_f32(__ldg(row + k)), v[k], acc);
+    return warp_sum(acc);
+}
+
+// Time embedding of one flow time (src/phonon_sampler.c:280-305), one CTA
+// of 512 threads: phase_i = t * freq_i, [cos | sin] of the 128 phases,
+// hidden = silu(W0 e + b0) (512 x 256), o = W1 hidden + b1 (512 x 512),
+// out_i = (alpha_i * o_i) / sqrt(mean(o^2) + 1e-5). W0 and W1 are natural
+// row-major bf16; bias, freqs and alpha are fp32 copies of bf16 vectors.
+__global__ void __launch_bounds__(512) head_time_kernel(float value, const float* __restrict__ freqs,
+                                                        const uint16_t* __restrict__ w0, const float* __restrict__ b0,
+                                                        const uint16_t* __restrict__ w1, const float* __restrict__ b1,
+                                                        const float* __restrict__ alpha, float* __restrict__ out,
+                                                        int32_t* status) {
+    __shared__ float e[256], hidden[kWidth], o[kWidth], sq[kWidth];
+    __shared__ float inverse;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    if (t < 128) {
+        float s, c;
+        sincosf(__fmul_rn(value, freqs[t]), &s, &c);
+        e[t] = c;
+        e[128 + t] = s;
+    }
+    __syncthreads();
+    for (int r = warp; r < kWidth; r += 16) {
+        const float d = head_row_dot(w0, 256, r, e);
+        if (lane == 0) hidden[r] = silu_f(__fadd_rn(d, b0[r]));
+    }
+    __syncthreads();
+    for (int r = warp; r < kWidth; r += 16) {
+        const float d = head_row_dot(w1, kWidth, r, hidden);
+        if (lane == 0) o[r] = __fadd_rn(d, b1[r]);
+    }
+    __syncthreads();
+    sq[t] = __fmul_rn(o[t], o[t]);
+    __syncthreads();
+    if (warp == 0) {
+        const float m = head_mean512(sq);
+        if (lane == 0) inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(m, 1e-5f)));
+    }
+    __syncthreads();
+    const float v = __fmul_rn(__fmul_rn(alpha[t], o[t]), inverse);
+    if (!isfinite(v)) flag_nonfinite(status, 0);
+    out[t] = v;
+}
+
+struct HeadInParams {
+    const float* noise;      // [B][32] raw noise (lsd) or the latent state (forward)
+    float noise_scale;       // sqrt(temperature) (lsd) or 1 with scaled = false
+    int scaled;
+    const uint16_t* in_w;    // input_proj [512][32] bf16
+    const float* in_b;       // [512]
+    const float* cond;       // cond_embed(condition) + bias, [B][ldc]
+    int ldc;
+    const float* temb;       // [2][512] time embeddings of s and t
+    float* x;                // [B][512]
+    float* silu_y;           // [B][512]
+    int B;
+    int32_t* status;
+};
+
+// One CTA of 512 threads per stream (src/phonon_sampler.c:310-318):
+// x = input_proj(noise) + b, y = cond + 0.5 * (time_s + time_t), silu(y)
+// (the same silu(y) feeds every block's and the final modulation).
+__global__ void __launch_bounds__(512) head_in_kernel(HeadInParams p) {
+    __shared__ float nz[kLatent];
+    const int b = blockIdx.x, t = threadIdx.x;
+    pdl_wait();
+    pdl_trigger();
+    if (t < kLatent) {
+        const float r = p.noise[static_cast<size_t>(b) * kLatent + t];
+        if (!isfinite(r)) flag_nonfinite(p.status, b);
+        nz[t] = p.scaled ? __fmul_rn(r, p.noise_scale) : r;
+    }
+    __syncthreads();
+    const uint16_t* row = p.in_w + static_cast<size_t>(t) * kLatent;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int k = 0; k < kLatent; ++k) acc = fmaf(bf16_to_f32(__ldg(row + k)), nz[k], acc);
+    const float x = __fadd_rn(acc, p.in_b[t]);
+    const float y = __fadd_rn(p.cond[static_cast<size_t>(b) * p.ldc + t],
+                              __fmul_rn(0.5f, __fadd_rn(p.temb[t], p.temb[kWidth + t])));
+    const float sy = silu_f(y);
+    if (!isfinite(x) || !isfinite(sy)) flag_nonfinite(p.status, b);
+    p.x[static_cast<size_t>(b) * kWidth + t] = x;
+    p.silu_y[static_cast<size_t>(b) * kWidth + t] = sy;
+}
+
+// Residual block LayerNorm (src/phonon_sampler.c:319-332): h = LN(x; w, b)
+// * (1 + scale) + shift, shift/scale the block's first two modulation
+// thirds. One warp per stream, the row staged in shared memory.
+__global__ void __launch_bounds__(256) head_block_kernel(const float* __restrict__ x, const float* __restrict__ mod,
+                                                         int block, const float* __restrict__ norm_w,
+                                                         const float* __restrict__ norm_b, float* __restrict__ h, int B,
+                                                         int32_t* status) {
+    __shared__ float row[8][kWidth];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x * 8 + warp;
+    pdl_wait();
+    pdl_trigger();
+    if (b >= B) return;
+    for (int k = 0; k < 16; ++k) row[warp][lane + 32 * k] = x[static_cast<size_t>(b) * kWidth + lane + 32 * k];
+    __syncwarp();
+    const float* m = mod + static_cast<size_t>(b) * kAdaRows + block * kAdaBlockRows;
+    if (!head_ln_modulate(row[warp], norm_w, norm_b, m, m + kWidth, h + static_cast<size_t>(b) * kWidth) && lane == 0)
+        flag_nonfinite(status, b);
+}
+
+struct HeadFinalParams {
+    const float* x;          // [B][512]
+    const float* mod;        // [B][kAdaRows]: the final shift/scale are its last 1024
+    const uint16_t* fin_w;   // final_layer.linear [32][512] bf16
+    const float* fin_b;      // [32]
+    const float* noise;      // as HeadInParams
+    float noise_scale;
+    int scaled;              // 1: out = noise * scale + velocity (lsd); 0: out = velocity
+    float* out;              // [B][32]
+    const uint16_t* embed_w; // optional: input_linear [512][32] bf16 ...
+    const float* condition;  // ... [B][512] ...
+    float* embed_out;        // ... -> [B][512] = input_linear(out) + condition
+    int B;
+    int32_t* status;
+};
+
+// Final layer and Euler step (src/phonon_sampler.c:349-393), then the
+// embedding of the new latent (phonon_flow_embed_latent,
+// src/phonon_transformer.c:860-875) when the frame loop asks for it: one
+// CTA of 256 threads per stream.
+__global__ void __launch_bounds__(256) head_final_kernel(HeadFinalParams p) {
+    __shared__ float xr[kWidth], h[kWidth], lat[kLatent];
+    __shared__ int bad;
+    const int b = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    pdl_wait();
+    pdl_trigger();
+    if (t == 0) bad = 0;
+    for (int i = t; i < kWidth; i += 256) xr[i] = p.x[static_cast<size_t>(b) * kWidth + i];
+    __syncthreads();
+    if (warp == 0) {
+        const float* m = p.mod + static_cast<size_t>(b) * kAdaRows + kHeadBlocks * kAdaBlockRows;
+        if (!head_ln_modulate(xr, nullptr, nullptr, m, m + kWidth, h) && lane == 0) bad = 1;
+    }
+    __syncthreads();
+    for (int j = warp; j < kLatent; j += 8) {
+        const float v = __fadd_rn(head_row_dot(p.fin_w, kWidth, j, h), p.fin_b[j]);
+        if (lane == 0) {
+            float o = v;
+            if (p.scaled) o = __fadd_rn(__fmul_rn(p.noise[static_cast<size_t>(b) * kLatent + j], p.noise_scale), v);
+            if (!isfinite(o)) bad = 1;
+            lat[j] = o;
+            p.out[static_cast<size_t>(b) * kLatent + j] = o;
+        }
+    }
+    __syncthreads();
+    if (p.embed_out) {
+        for (int i = t; i < kWidth; i += 256) {
+            const uint16_t* row = p.embed_w + static_cast<size_t>(i) * kLatent;
+            float acc = 0.0f;
+#pragma unroll 8
+            for (int k = 0; k < kLatent; ++k) acc = fmaf(bf16_to_f32(__ldg(row + k)), lat[k], acc);
+            const float v = __fadd_rn(acc, p.condition[static_cast<size_t>(b) * kWidth + i]);
+            if (!isfinite(v)) bad = 1;
+            p.embed_out[static_cast<size_t>(b) * kWidth + i] = v;
+        }
+        __syncthreads();
+    }
+    if (t == 0 && bad) flag_nonfinite(p.status, b);
+}
+
+// phonon_flow_output_norm of B rows (src/phonon_transformer.c:904-914): the
+// transformer's LayerNorm (eps 1e-5) with the out_norm weight and bias, one
+// warp per row; non-finite rows are flagged per stream.
+__global__ void __launch_bounds__(256) output_norm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                          const float* __restrict__ b, float* __restrict__ out, int B,
+                                                          int32_t* status) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
+    pdl_wait();
+    pdl_trigger();
+    if (r >= B) return;
+    if (!warp_layernorm512(x + static_cast<size_t>(r) * kWidth, w, b, out + static_cast<size_t>(r) * kWidth) &&
+        lane == 0)
+        flag_nonfinite(status, r);
+}
+
+}  // namespace phonon

@@ -34,7 +34,9 @@ constexpr int kAttnWarps = 4;      // warps per attention CTA
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kStatusNonFinite = 2;  // PHONON_CUDA_NON_FINITE
 
-enum Epilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_GELU = 2, EPI_QKV = 3 };
+// EPI_SILU: y = silu(acc + bias); EPI_GATE: y = res + gate * (acc + bias)
+// (the flow head's MLP, src/phonon_sampler.c:333-345).
+enum Epilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_GELU = 2, EPI_QKV = 3, EPI_SILU = 4, EPI_GATE = 5 };
 // Where a GEMV's activation rows come from: x as is, LayerNorm(x), or the
 // merge of the step's attention split partials (the attention output).
 enum GemvSource : int { SRC_X = 0, SRC_LN = 1, SRC_MERGE = 2 };
@@ -63,6 +65,10 @@ __device__ __forceinline__ float warp_sum(float v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
     return v;
 }
+
+// x / (1 + e^-x) (src/phonon_math.c:18-28; CUDA's expf where the reference
+// calls SLEEF's u10 exp: both within ~1 ulp of e^-x).
+__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
 
 __device__ __forceinline__ void flag_nonfinite(int32_t* status, int b) {
     if (status) atomicOr(status + b, kStatusNonFinite);
@@ -315,7 +321,9 @@ struct GemvParams {
     const float* part;        // SRC_MERGE: split partials [S][8][66] ...
     const int32_t* first;     // ... and each stream's first split and split count
     const int32_t* count;
-    const float* bias;        // EPI_STORE, optional
+    const float* bias;        // EPI_STORE (optional), EPI_SILU, EPI_GATE
+    const float* gate;        // EPI_GATE: [B][ldgate]
+    int ldgate;
     float* y;                 // output [B][ldy]
     int ldy;
     const float* res;         // EPI_RESID residual [B][ldres]
@@ -328,6 +336,7 @@ struct GemvParams {
     KvView kv;
     int layer;
     int32_t* status;          // [B]
+    int b_per_cta;            // streams per CTA along grid.y (a multiple of the tile), 0: all
 };
 
 template <bool kQ8, int kChunks, int kBT, int kSrc, int kEpi>
@@ -375,8 +384,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
     }
 
     pdl_wait();  // weights above are independent of the previous kernel
-    for (int b0 = 0; b0 < p.B; b0 += kBT) {
-        const int nb = min(kBT, p.B - b0);
+    // Streams [b_begin, b_end) of this CTA: blockIdx.y picks a slice of the
+    // batch when the launch splits it (p.b_per_cta > 0) so that a matrix of
+    // few rows still spreads over the SMs at large batches.
+    const int b_begin = p.b_per_cta > 0 ? static_cast<int>(blockIdx.y) * p.b_per_cta : 0;
+    const int b_end = p.b_per_cta > 0 ? min(p.B, b_begin + p.b_per_cta) : p.B;
+    for (int b0 = b_begin; b0 < b_end; b0 += kBT) {
+        const int nb = min(kBT, b_end - b0);
         __syncthreads();
         if constexpr (kLN) {
             for (int r = warp; r < nb; r += kGemvWarps) {
@@ -478,7 +492,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
 #pragma unroll
             for (int bb = 0; bb < kBT; ++bb) acc[rr][bb] = warp_sum(acc[rr][bb]);
 
-        if (b0 + kBT >= p.B) pdl_trigger();
+        if (b0 + kBT >= b_end) pdl_trigger();
         // Lane bb finishes stream b0+bb for both rows of the pair.
 #pragma unroll
         for (int bb = 0; bb < kBT; ++bb) {
@@ -517,6 +531,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
                     if constexpr (kEpi == EPI_STORE) {
                         if (p.bias) v = __fadd_rn(v, p.bias[r]);
                     }
+                    if constexpr (kEpi == EPI_SILU) v = silu_f(__fadd_rn(v, p.bias[r]));
+                    if constexpr (kEpi == EPI_GATE)
+                        v = __fadd_rn(p.res[static_cast<size_t>(b) * p.ldres + r],
+                                      __fmul_rn(p.gate[static_cast<size_t>(b) * p.ldgate + r], __fadd_rn(v, p.bias[r])));
                     if (!isfinite(v)) flag_nonfinite(p.status, b);
                     p.y[static_cast<size_t>(b) * p.ldy + r] = v;
                 }

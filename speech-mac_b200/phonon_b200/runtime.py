@@ -10,7 +10,7 @@ import numpy as np
 
 from ._libs import load_cuda
 
-KERNEL_CLASSES = ("qkv", "attention", "combine", "out", "up", "down", "other", "fused")
+KERNEL_CLASSES = ("qkv", "attention", "combine", "out", "up", "down", "other", "fused", "head")
 OK, INVALID, NON_FINITE, OOM, POOL_EXHAUSTED, CAPACITY, BAD_POSITION, CANCELLED, DEVICE_ERROR = range(9)
 Q8_0, BF16 = 1, 2
 KV_F32, KV_BF16 = 0, 1
@@ -33,6 +33,23 @@ class Layer(C.Structure):
                 ("mlp_out", C.c_void_p), ("norm1_weight", C.c_void_p), ("norm1_bias", C.c_void_p),
                 ("norm2_weight", C.c_void_p), ("norm2_bias", C.c_void_p),
                 ("linear_kind", C.c_uint32)]
+
+
+HEAD_BLOCKS = 6  # PHONON_CUDA_HEAD_BLOCKS
+LATENT = 32  # PHONON_CUDA_LATENT
+
+
+class Affine(C.Structure):
+    _fields_ = [("weight", C.c_void_p), ("bias", C.c_void_p)]
+
+
+class HeadWeights(C.Structure):
+    _fields_ = [("input", Affine), ("cond", Affine), ("time", (Affine * 2) * 2),
+                ("time_freqs", C.c_void_p * 2), ("time_alpha", C.c_void_p * 2),
+                ("block_ada", Affine * HEAD_BLOCKS), ("block_norm_w", C.c_void_p * HEAD_BLOCKS),
+                ("block_norm_b", C.c_void_p * HEAD_BLOCKS), ("block_mlp", (Affine * 2) * HEAD_BLOCKS),
+                ("final_ada", Affine), ("final_out", Affine), ("eos", Affine), ("embed", C.c_void_p),
+                ("out_norm_w", C.c_void_p), ("out_norm_b", C.c_void_p)]
 
 
 class CudaError(RuntimeError):
@@ -81,11 +98,19 @@ def lib():
         "phonon_cuda_set_cluster_step": [P, U32, C.POINTER(C.c_int)],
         "phonon_cuda_set_layer_trace": [P, P, U32],
         "phonon_cuda_wait_expiry_probe": [C.c_int, C.c_int, U32, C.POINTER(C.c_uint64)],
+        "phonon_cuda_head_create": [P, C.POINTER(HeadWeights), C.POINTER(P)],
+        "phonon_cuda_head_forward": [P, U32, P, P, F, F, P],
+        "phonon_cuda_lsd_one_step": [P, U32, P, P, F, P],
+        "phonon_cuda_eos_logit": [P, U32, P, P],
+        "phonon_cuda_output_norm_device": [P, U32, P, P],
+        "phonon_cuda_frame_step": [P, U32, P, P, P, P, P, F, P, P, P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
         fn.argtypes = args
         fn.restype = C.c_int
+    L.phonon_cuda_head_free.argtypes = [P]
+    L.phonon_cuda_head_free.restype = None
     L.phonon_cuda_destroy.argtypes = [P]
     L.phonon_cuda_destroy.restype = None
     L.phonon_cuda_linear_destroy.argtypes = [P]
@@ -371,3 +396,96 @@ def i8_gemm(a, b, device=0):
     L.phonon_cuda_i8_gemm.restype = C.c_int
     check(L.phonon_cuda_i8_gemm(device, _p(a), _p(b), m, n, k, _p(d)), "i8_gemm")
     return d
+
+
+def head_struct(head, frame=None):
+    """PhononCudaHeadWeights over a head dict of bf16 arrays (the layout of
+    the flow-head tests: (weight, bias) pairs per linear) and, optionally,
+    the frame loop's tensors: frame = {"eos": (w [1][512], b [1]),
+    "embed": w [512][32], "out_norm": (w, b)}. The arrays must outlive the
+    create call."""
+    def ptr(a):
+        return None if a is None else a.ctypes.data
+
+    def aff(wb):
+        return Affine(ptr(wb[0]), ptr(wb[1]))
+
+    w = HeadWeights()
+    w.input = aff(head["input"])
+    w.cond = aff(head["cond"])
+    for t in range(2):
+        for j in range(2):
+            w.time[t][j] = aff(head["time"][t][j])
+        w.time_freqs[t] = ptr(head["time_freqs"][t])
+        w.time_alpha[t] = ptr(head["time_alpha"][t])
+    for b in range(HEAD_BLOCKS):
+        w.block_ada[b] = aff(head["block_ada"][b])
+        w.block_norm_w[b] = ptr(head["block_norm_w"][b])
+        w.block_norm_b[b] = ptr(head["block_norm_b"][b])
+        for j in range(2):
+            w.block_mlp[b][j] = aff(head["block_mlp"][b][j])
+    w.final_ada = aff(head["final_ada"])
+    w.final_out = aff(head["final_out"])
+    if frame:
+        w.eos = aff(frame["eos"])
+        w.embed = ptr(frame["embed"])
+        w.out_norm_w = ptr(frame["out_norm"][0])
+        w.out_norm_b = ptr(frame["out_norm"][1])
+    return w
+
+
+class Head:
+    """A flow head (and the frame loop's tensors) on a context's device."""
+
+    def __init__(self, ctx, head, frame=None):
+        self.ctx = ctx
+        self.L = lib()
+        self._keep = (head, frame)
+        w = head_struct(head, frame)
+        h = C.c_void_p()
+        check(self.L.phonon_cuda_head_create(ctx.h, C.byref(w), C.byref(h)), "head_create")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.L.phonon_cuda_head_free(self.h)
+            self.h = None
+
+    def forward(self, condition, state, s, t):
+        condition = np.ascontiguousarray(condition, np.float32).reshape(-1, WIDTH)
+        state = np.ascontiguousarray(state, np.float32).reshape(-1, LATENT)
+        out = np.zeros((condition.shape[0], LATENT), np.float32)
+        check(self.L.phonon_cuda_head_forward(self.h, condition.shape[0], _p(condition), _p(state), s, t, _p(out)),
+              "head_forward")
+        return out
+
+    def lsd_one_step(self, condition, raw_noise, temperature):
+        condition = np.ascontiguousarray(condition, np.float32).reshape(-1, WIDTH)
+        raw_noise = np.ascontiguousarray(raw_noise, np.float32).reshape(-1, LATENT)
+        out = np.zeros((condition.shape[0], LATENT), np.float32)
+        check(self.L.phonon_cuda_lsd_one_step(self.h, condition.shape[0], _p(condition), _p(raw_noise), temperature,
+                                              _p(out)), "lsd_one_step")
+        return out
+
+    def eos_logit(self, state):
+        state = np.ascontiguousarray(state, np.float32).reshape(-1, WIDTH)
+        out = np.zeros(state.shape[0], np.float32)
+        check(self.L.phonon_cuda_eos_logit(self.h, state.shape[0], _p(state), _p(out)), "eos_logit")
+        return out
+
+    def output_norm_device(self, batch, x_ptr, out_ptr):
+        check(self.L.phonon_cuda_output_norm_device(self.h, batch, x_ptr, out_ptr), "output_norm_device")
+
+    def frame_step(self, streams, positions, state_ptr, condition_ptr, raw_noise, temperature):
+        """One on-device frame; returns (eos logits [n], latents [n][32],
+        status [n])."""
+        n = len(streams)
+        st = np.ascontiguousarray(streams, np.uint32)
+        po = np.ascontiguousarray(positions, np.uint32)
+        raw_noise = np.ascontiguousarray(raw_noise, np.float32).reshape(n, LATENT)
+        logit = np.zeros(n, np.float32)
+        latent = np.zeros((n, LATENT), np.float32)
+        status = np.zeros(n, np.int32)
+        check(self.L.phonon_cuda_frame_step(self.h, n, _p(st), _p(po), state_ptr, condition_ptr, _p(raw_noise),
+                                            temperature, _p(logit), _p(latent), _p(status)), "frame_step")
+        return logit, latent, status

@@ -107,3 +107,45 @@ def float_to_bf16(x):
 
 def bf16_to_float(bits):
     return (np.asarray(bits, np.uint32) << 16).view(np.float32)
+
+
+HEAD_BLOCKS = 6  # PHONON_FLOW_HEAD_BLOCKS
+
+
+def flow_head(seed=0):
+    """A random flow head (src/phonon_sampler.c:160-212 shapes) as bf16 bits:
+    {"input", "cond", "final_ada", "final_out": (W [rows][cols], b [rows]),
+    "time": [[(W, b)] * 2] * 2, "time_freqs": [128] * 2, "time_alpha": [512] * 2,
+    "block_ada": [(W, b)] * 6, "block_norm_w"/"block_norm_b": [512] * 6,
+    "block_mlp": [[(W, b)] * 2] * 6}. Weights N(0, 1/cols), biases N(0, 0.05^2),
+    gains N(1, 0.1^2), time frequencies exp(-9 k / 127)."""
+    g = Generator(seed ^ 0x68656164)
+
+    def lin(rows, cols):
+        w = g.bf16_normal(0.0, 1.0 / np.sqrt(cols), rows * cols).reshape(rows, cols)
+        return np.ascontiguousarray(w), g.bf16_normal(0.0, 0.05, rows)
+
+    freqs = np.array([float_to_bf16(float(np.exp(-9.0 * k / 127))) for k in range(128)], np.uint16)
+    return {
+        "input": lin(512, 32), "cond": lin(512, 512),
+        "time": [[lin(512, 256), lin(512, 512)] for _ in range(2)],
+        "time_freqs": [freqs, freqs.copy()],
+        "time_alpha": [g.bf16_normal(1.0, 0.1, 512) for _ in range(2)],
+        "block_ada": [lin(1536, 512) for _ in range(HEAD_BLOCKS)],
+        "block_norm_w": [g.bf16_normal(1.0, 0.1, 512) for _ in range(HEAD_BLOCKS)],
+        "block_norm_b": [g.bf16_normal(0.0, 0.1, 512) for _ in range(HEAD_BLOCKS)],
+        "block_mlp": [[lin(512, 512), lin(512, 512)] for _ in range(HEAD_BLOCKS)],
+        "final_ada": lin(1024, 512), "final_out": lin(32, 512),
+    }
+
+
+def frame_tensors(seed=0):
+    """The frame loop's pack tensors next to the head, as bf16 bits:
+    flow_lm.out_eos (w [1][512], b [1]), flow_lm.input_linear.weight
+    [512][32], flow_lm.out_norm (w, b [512])."""
+    g = Generator(seed ^ 0x6672616d)
+    return {
+        "eos": (g.bf16_normal(0.0, 1.0 / np.sqrt(512), 512).reshape(1, 512), g.bf16_normal(0.0, 0.1, 1)),
+        "embed": np.ascontiguousarray(g.bf16_normal(0.0, 1.0 / np.sqrt(32), 512 * 32).reshape(512, 32)),
+        "out_norm": (g.bf16_normal(1.0, 0.05, 512), g.bf16_normal(0.0, 0.05, 512)),
+    }
