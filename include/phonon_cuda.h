@@ -347,6 +347,11 @@ typedef struct PhononCudaHead PhononCudaHead;
  * PHONON_CUDA_NON_FINITE. Free before the context. */
 int phonon_cuda_head_create(PhononCuda *ctx, const PhononCudaHeadWeights *weights, PhononCudaHead **out);
 void phonon_cuda_head_free(PhononCudaHead *head);
+/* Batches of at least min_batch rows (default 32) run the head's linears on
+ * the tensor cores (bf16 weights times three bf16 slices of the fp32
+ * activations, fp32 accumulation); smaller ones on the GEMV. *available: 1
+ * when the tensor-core path could be set up. */
+int phonon_cuda_head_set_tensor_min(PhononCudaHead *head, uint32_t min_batch, int *available);
 /* phonon_flow_head_forward for `batch` rows (host buffers: condition
  * [batch][512], state [batch][32], velocity [batch][32]); s and t are shared.
  * PHONON_CUDA_NON_FINITE when any row fails the reference's checks (no row

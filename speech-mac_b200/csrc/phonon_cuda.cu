@@ -2779,6 +2779,13 @@ struct PhononCudaHead {
     int32_t* d_status = nullptr;       // [cap + 1]: per row, then the time embeddings'
     float *h_in = nullptr, *h_out = nullptr;
     int32_t* h_status = nullptr;
+    // tensor-core path (head_gemm_kernel) for batches of at least tensor_min rows
+    uint16_t* wn = nullptr;            // natural bf16 rows: cond + EOS (513), every adaLN row, the MLPs
+    CUtensorMap tm_cond, tm_ada, tm_mlp[phonon::kHeadBlocks][2];
+    uint16_t *sl_a = nullptr, *sl_h = nullptr, *sl_f = nullptr;  // [3 * cap_pad][512] bf16 slice rows
+    CUtensorMap tm_sl_a, tm_sl_h, tm_sl_f;
+    bool tensor_ok = false;
+    uint32_t tensor_min = 32;
 };
 
 namespace {
@@ -2790,6 +2797,9 @@ void head_release(PhononCudaHead* h) {
         free_linear(m[0]);
         free_linear(m[1]);
     }
+    for (void* p : {static_cast<void*>(h->wn), static_cast<void*>(h->sl_a), static_cast<void*>(h->sl_h),
+                    static_cast<void*>(h->sl_f)})
+        if (p) cudaFree(p);
     for (void* p : {static_cast<void*>(h->w16), static_cast<void*>(h->f), static_cast<void*>(h->d_cond),
                     static_cast<void*>(h->d_y), static_cast<void*>(h->d_x), static_cast<void*>(h->d_sy),
                     static_cast<void*>(h->d_mod), static_cast<void*>(h->d_h), static_cast<void*>(h->d_first),
@@ -2894,6 +2904,24 @@ int head_upload(PhononCudaHead* h, const PhononCudaHeadWeights& w) {
             if (!w.block_mlp[b][j].weight) return PHONON_CUDA_NON_FINITE;
             if ((st = upload_linear(PHONON_CUDA_LINEAR_BF16, w.block_mlp[b][j].weight, W, W, &h->mlp[b][j]))) return st;
         }
+    // natural bf16 copies for the tensor-core path: [cond + EOS | adaLN rows | MLPs], 128-row TMA boxes
+    const size_t rows_n = (W + 1) + static_cast<size_t>(kAdaRows) + kHeadBlocks * 2 * W;
+    if (cudaMalloc(&h->wn, rows_n * W * 2) != cudaSuccess) return PHONON_CUDA_OUT_OF_MEMORY;
+    CUDA_TRY(cudaMemcpy(h->wn, cond.data(), (W + 1) * W * 2, cudaMemcpyHostToDevice));
+    uint16_t* wn_ada = h->wn + (W + 1) * W;
+    CUDA_TRY(cudaMemcpy(wn_ada, ada.data(), ada.size() * 2, cudaMemcpyHostToDevice));
+    uint16_t* wn_mlp = wn_ada + static_cast<size_t>(kAdaRows) * W;
+    for (int b = 0; b < kHeadBlocks; ++b)
+        for (int j = 0; j < 2; ++j)
+            CUDA_TRY(cudaMemcpy(wn_mlp + (2 * b + j) * W * W, w.block_mlp[b][j].weight, W * W * 2, cudaMemcpyHostToDevice));
+    // (the TMA alignment rules hold by construction: 1 KB rows, 16-byte aligned bases)
+    bool maps = make_map_2d(&h->tm_cond, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, h->wn, W + 1, W, W * 2, kHgKTile, kHgM) &&
+                make_map_2d(&h->tm_ada, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, wn_ada, kAdaRows, W, W * 2, kHgKTile, kHgM);
+    for (int b = 0; b < kHeadBlocks && maps; ++b)
+        for (int j = 0; j < 2 && maps; ++j)
+            maps = make_map_2d(&h->tm_mlp[b][j], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, wn_mlp + (2 * b + j) * W * W, W, W,
+                               W * 2, kHgKTile, kHgM);
+    h->tensor_ok = maps;
     if (cudaMalloc(&h->w16, m16.size() * 2) != cudaSuccess || cudaMalloc(&h->f, f.size() * 4) != cudaSuccess)
         return PHONON_CUDA_OUT_OF_MEMORY;
     CUDA_TRY(cudaMemcpy(h->w16, m16.data(), m16.size() * 2, cudaMemcpyHostToDevice));
@@ -2934,7 +2962,37 @@ int head_alloc(PhononCudaHead* h, uint32_t cap) {
         cudaMallocHost(&h->h_out, B * (kLatent + 1) * 4) != cudaSuccess ||
         cudaMallocHost(&h->h_status, (B + 1) * 4) != cudaSuccess)
         return PHONON_CUDA_OUT_OF_MEMORY;
+    const size_t slice_rows = 3 * ((B + kHgStreams - 1) / kHgStreams * kHgStreams);
+    for (uint16_t** sl : {&h->sl_a, &h->sl_h, &h->sl_f}) {
+        if (cudaMalloc(sl, slice_rows * kWidth * 2) != cudaSuccess) return PHONON_CUDA_OUT_OF_MEMORY;
+        CUDA_TRY(cudaMemset(*sl, 0, slice_rows * kWidth * 2));
+    }
+    h->tensor_ok = h->tensor_ok &&
+                   make_map_2d(&h->tm_sl_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, h->sl_a, slice_rows, kWidth, kWidth * 2,
+                               kHgKTile, kHgN) &&
+                   make_map_2d(&h->tm_sl_h, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, h->sl_h, slice_rows, kWidth, kWidth * 2,
+                               kHgKTile, kHgN) &&
+                   make_map_2d(&h->tm_sl_f, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, h->sl_f, slice_rows, kWidth, kWidth * 2,
+                               kHgKTile, kHgN);
     return PHONON_CUDA_OK;
+}
+
+template <int kEpi>
+cudaError_t launch_head_gemm(PhononCudaHead* h, const CUtensorMap& tw, const CUtensorMap& tx, int rows, int B,
+                             HeadGemmParams p) {
+    static std::atomic<uint64_t> configured{0};
+    const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(head_gemm_kernel<kEpi>), kHgSmem, configured);
+    if (e != cudaSuccess) return e;
+    p.rows = rows;
+    p.B = B;
+    p.status = h->d_status;
+    p.error = h->c->d_err;
+    const dim3 grid((rows + kHgM - 1) / kHgM, (B + kHgStreams - 1) / kHgStreams);
+    return launch_pdl(head_gemm_kernel<kEpi>, grid, dim3(kHgThreads), kHgSmem, h->c->stream, tw, tx, p);
+}
+
+bool head_tensor(const PhononCudaHead* h, int B) {
+    return h->tensor_ok && static_cast<uint32_t>(B) >= h->tensor_min;
 }
 
 // cond_embed (and the EOS row) of B condition rows at x_dev: h->d_y [B][520].
@@ -2952,6 +3010,20 @@ int enqueue_head_cond(PhononCudaHead* h, int B, const float* x_dev) {
     p.y = h->d_y;
     p.ldy = kHeadCondLd;
     p.status = h->d_status;
+    if (head_tensor(h, B)) {
+        {
+            LaunchScope ls(c, PHONON_CUDA_K_HEAD, B * kWidth * 10.0);
+            CUDA_TRY(launch_pdl(slice_rows_kernel, dim3(B), dim3(128), 0, c->stream, x_dev, static_cast<int>(kWidth), B,
+                                h->sl_a));
+        }
+        HeadGemmParams g{};
+        g.bias = h->cond_b;
+        g.y = h->d_y;
+        g.ldy = kHeadCondLd;
+        LaunchScope ls(c, PHONON_CUDA_K_HEAD, (kWidth + 1) * kWidth * 2.0 + B * (3 * kWidth * 2.0 + (kWidth + 1) * 4.0));
+        CUDA_TRY(launch_head_gemm<HG_STORE>(h, h->tm_cond, h->tm_sl_a, kWidth + 1, B, g));
+        return PHONON_CUDA_OK;
+    }
     LaunchScope ls(c, PHONON_CUDA_K_HEAD, (kWidth + 1) * kWidth * 2.0 + B * (kWidth + kWidth + 1) * 4.0);
     CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_STORE>(p, c->stream)));
     return PHONON_CUDA_OK;
@@ -2966,6 +3038,7 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
     using namespace phonon;
     PhononCuda* c = h->c;
     cudaStream_t st = c->stream;
+    const bool tensor = head_tensor(h, B);
     if (!h->temb_ok || h->temb_s != s || h->temb_t != t) {
         for (int k = 0; k < 2; ++k) {
             LaunchScope ls(c, PHONON_CUDA_K_HEAD, (kWidth * 256 + kWidth * kWidth) * 2.0);
@@ -2991,12 +3064,20 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
         q.temb = h->temb;
         q.x = h->d_x;
         q.silu_y = h->d_sy;
+        q.sy_slices = tensor ? h->sl_a : nullptr;
         q.B = B;
         q.status = h->d_status;
         LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kLatent * 2.0 + B * kWidth * 12.0);
         CUDA_TRY(launch_pdl(head_in_kernel, dim3(B), dim3(512), 0, st, q));
     }
-    {
+    if (tensor) {
+        HeadGemmParams g{};
+        g.bias = h->ada_b;
+        g.y = h->d_mod;
+        g.ldy = kAdaRows;
+        LaunchScope ls(c, PHONON_CUDA_K_HEAD, kAdaRows * kWidth * 2.0 + B * (3 * kWidth * 2.0 + kAdaRows * 4.0));
+        CUDA_TRY(launch_head_gemm<HG_STORE>(h, h->tm_ada, h->tm_sl_a, kAdaRows, B, g));
+    } else {
         GemvParams p{};
         p.w = h->ada.plane;
         p.rows = kAdaRows;
@@ -3017,7 +3098,26 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
             CUDA_TRY(launch_pdl(head_block_kernel, dim3((B + 7) / 8), dim3(256), 0, st, static_cast<const float*>(h->d_x),
                                 static_cast<const float*>(h->d_mod), blk,
                                 static_cast<const float*>(h->norm_w + blk * kWidth),
-                                static_cast<const float*>(h->norm_b + blk * kWidth), h->d_h, B, h->d_status));
+                                static_cast<const float*>(h->norm_b + blk * kWidth), h->d_h, B, h->d_status,
+                                tensor ? h->sl_h : nullptr));
+        }
+        if (tensor) {
+            HeadGemmParams g{};
+            g.bias = h->mlp_b + (2 * blk) * kWidth;
+            g.slices = h->sl_f;
+            {
+                LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kWidth * 2.0 + B * 12.0 * kWidth);
+                CUDA_TRY(launch_head_gemm<HG_SILU>(h, h->tm_mlp[blk][0], h->tm_sl_h, kWidth, B, g));
+            }
+            g = HeadGemmParams{};
+            g.bias = h->mlp_b + (2 * blk + 1) * kWidth;
+            g.y = h->d_x;
+            g.ldy = kWidth;
+            g.gate = h->d_mod + static_cast<size_t>(blk) * kAdaBlockRows + 2 * kWidth;
+            g.ldgate = kAdaRows;
+            LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kWidth * 2.0 + B * 18.0 * kWidth);
+            CUDA_TRY(launch_head_gemm<HG_GATE>(h, h->tm_mlp[blk][1], h->tm_sl_f, kWidth, B, g));
+            continue;
         }
         GemvParams p{};
         p.rows = kWidth;
@@ -3154,6 +3254,14 @@ void phonon_cuda_head_free(PhononCudaHead* h) {
         head_release(h);
     }
     delete h;
+}
+
+int phonon_cuda_head_set_tensor_min(PhononCudaHead* h, uint32_t min_batch, int* available) {
+    if (!h) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(h->c->mu);
+    h->tensor_min = min_batch;
+    if (available) *available = h->tensor_ok ? 1 : 0;
+    return PHONON_CUDA_OK;
 }
 
 int phonon_cuda_head_forward(PhononCudaHead* h, uint32_t batch, const float* condition, const float* state, float s,

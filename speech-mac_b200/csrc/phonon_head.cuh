@@ -23,7 +23,7 @@
 // sum in the GEMV's order, as the reference's SGEMM calls do in theirs.
 #pragma once
 
-#include "phonon_kernels.cuh"
+#include "phonon_head_gemm.cuh"
 
 namespace phonon {
 
@@ -158,6 +158,7 @@ struct HeadInParams {
     const float* temb;       // [2][512] time embeddings of s and t
     float* x;                // [B][512]
     float* silu_y;           // [B][512]
+    uint16_t* sy_slices;     // optional: silu(y) as bf16 slice rows (tensor-core path)
     int B;
     int32_t* status;
 };
@@ -186,7 +187,16 @@ __global__ void __launch_bounds__(512) head_in_kernel(HeadInParams p) {
     const float sy = silu_f(y);
     if (!isfinite(x) || !isfinite(sy)) flag_nonfinite(p.status, b);
     p.x[static_cast<size_t>(b) * kWidth + t] = x;
-    p.silu_y[static_cast<size_t>(b) * kWidth + t] = sy;
+    if (p.sy_slices) {
+        uint16_t s0, s1, s2;
+        bf16x3_split(sy, s0, s1, s2);
+        uint16_t* row = p.sy_slices + static_cast<size_t>(3 * b) * kWidth + t;
+        row[0] = s0;
+        row[kWidth] = s1;
+        row[2 * kWidth] = s2;
+    } else {
+        p.silu_y[static_cast<size_t>(b) * kWidth + t] = sy;
+    }
 }
 
 // Residual block LayerNorm (src/phonon_sampler.c:319-332): h = LN(x; w, b)
@@ -195,8 +205,9 @@ __global__ void __launch_bounds__(512) head_in_kernel(HeadInParams p) {
 __global__ void __launch_bounds__(256) head_block_kernel(const float* __restrict__ x, const float* __restrict__ mod,
                                                          int block, const float* __restrict__ norm_w,
                                                          const float* __restrict__ norm_b, float* __restrict__ h, int B,
-                                                         int32_t* status) {
+                                                         int32_t* status, uint16_t* __restrict__ h_slices) {
     __shared__ float row[8][kWidth];
+    __shared__ float hr[8][kWidth];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.x * 8 + warp;
     pdl_wait();
@@ -205,8 +216,20 @@ __global__ void __launch_bounds__(256) head_block_kernel(const float* __restrict
     for (int k = 0; k < 16; ++k) row[warp][lane + 32 * k] = x[static_cast<size_t>(b) * kWidth + lane + 32 * k];
     __syncwarp();
     const float* m = mod + static_cast<size_t>(b) * kAdaRows + block * kAdaBlockRows;
-    if (!head_ln_modulate(row[warp], norm_w, norm_b, m, m + kWidth, h + static_cast<size_t>(b) * kWidth) && lane == 0)
-        flag_nonfinite(status, b);
+    float* out = h_slices ? hr[warp] : h + static_cast<size_t>(b) * kWidth;
+    if (!head_ln_modulate(row[warp], norm_w, norm_b, m, m + kWidth, out) && lane == 0) flag_nonfinite(status, b);
+    if (h_slices) {  // the next linear's operand: three bf16 slice rows
+        __syncwarp();
+        for (int k = 0; k < 16; ++k) {
+            const int i = lane + 32 * k;
+            uint16_t s0, s1, s2;
+            bf16x3_split(hr[warp][i], s0, s1, s2);
+            uint16_t* dst = h_slices + static_cast<size_t>(3 * b) * kWidth + i;
+            dst[0] = s0;
+            dst[kWidth] = s1;
+            dst[2 * kWidth] = s2;
+        }
+    }
 }
 
 struct HeadFinalParams {

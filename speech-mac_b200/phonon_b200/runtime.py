@@ -100,6 +100,7 @@ def lib():
         "phonon_cuda_wait_expiry_probe": [C.c_int, C.c_int, U32, C.POINTER(C.c_uint64)],
         "phonon_cuda_head_create": [P, C.POINTER(HeadWeights), C.POINTER(P)],
         "phonon_cuda_head_forward": [P, U32, P, P, F, F, P],
+        "phonon_cuda_head_set_tensor_min": [P, U32, C.POINTER(C.c_int)],
         "phonon_cuda_lsd_one_step": [P, U32, P, P, F, P],
         "phonon_cuda_eos_logit": [P, U32, P, P],
         "phonon_cuda_output_norm_device": [P, U32, P, P],
@@ -450,6 +451,13 @@ class Head:
         if self.h:
             self.L.phonon_cuda_head_free(self.h)
             self.h = None
+
+    def set_tensor_min(self, min_batch):
+        """Batches of at least min_batch rows take the tensor-core linears;
+        returns whether that path is available."""
+        ok = C.c_int(0)
+        check(self.L.phonon_cuda_head_set_tensor_min(self.h, min_batch, C.byref(ok)), "head_set_tensor_min")
+        return bool(ok.value)
 
     def forward(self, condition, state, s, t):
         condition = np.ascontiguousarray(condition, np.float32).reshape(-1, WIDTH)
