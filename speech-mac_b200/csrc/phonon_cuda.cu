@@ -3068,7 +3068,7 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
         q.B = B;
         q.status = h->d_status;
         LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kLatent * 2.0 + B * kWidth * 12.0);
-        CUDA_TRY(launch_pdl(head_in_kernel, dim3(B), dim3(512), 0, st, q));
+        CUDA_TRY(launch_pdl(head_in_kernel, dim3((B + kHeadInStreams - 1) / kHeadInStreams), dim3(512), 0, st, q));
     }
     if (tensor) {
         HeadGemmParams g{};

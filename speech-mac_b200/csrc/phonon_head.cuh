@@ -66,30 +66,41 @@ __device__ __forceinline__ float head_mean512(const float* row) {
 __device__ __forceinline__ bool head_ln_modulate(const float* x, const float* w, const float* b, const float* shift,
                                                  const float* scale, float* out) {
     const int lane = threadIdx.x & 31;
-    bool ok = true;
+    // every operand loaded up front (independent loads, no load behind a
+    // branch on an earlier one)
+    float xv[16], wv[16], bv[16], sc[16], sh[16];
+    const bool hw = w != nullptr, hb = b != nullptr;
+#pragma unroll
     for (int k = 0; k < 16; ++k) {
         const int i = lane + 32 * k;
-        ok &= isfinite(x[i]) && (!w || isfinite(w[i])) && (!b || isfinite(b[i]));
+        xv[k] = x[i];
+        wv[k] = hw ? w[i] : 1.0f;
+        bv[k] = hb ? b[i] : 0.0f;
+        sc[k] = scale[i];
+        sh[k] = shift[i];
     }
+    bool ok = true;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) ok &= isfinite(xv[k]) & isfinite(wv[k]) & isfinite(bv[k]);
     ok = __all_sync(kFull, ok);
     const float mean = head_mean512(x);
     double sq = 0.0;
+#pragma unroll
     for (int k = 0; k < 16; ++k) {
-        const double c = __dsub_rn(static_cast<double>(x[lane + 32 * k]), static_cast<double>(mean));
+        const double c = __dsub_rn(static_cast<double>(xv[k]), static_cast<double>(mean));
         sq = __dadd_rn(sq, __dmul_rn(c, c));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
     const float variance = static_cast<float>(sq / 512.0);
     const float inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, 1e-6f)));
+#pragma unroll
     for (int k = 0; k < 16; ++k) {
-        const int i = lane + 32 * k;
-        float n = __fmul_rn(__fsub_rn(x[i], mean), inverse);
-        if (w) n = __fmul_rn(n, w[i]);
-        if (b) n = __fadd_rn(n, b[i]);
+        float n = __fmul_rn(__fsub_rn(xv[k], mean), inverse);
+        if (hw) n = __fmul_rn(n, wv[k]);
+        if (hb) n = __fadd_rn(n, bv[k]);
         ok &= isfinite(n);
-        const float v = __fadd_rn(__fmul_rn(n, __fadd_rn(1.0f, scale[i])), shift[i]);
-        out[i] = v;
+        out[lane + 32 * k] = __fadd_rn(__fmul_rn(n, __fadd_rn(1.0f, sc[k])), sh[k]);
     }
     return __all_sync(kFull, ok);
 }
@@ -163,39 +174,64 @@ struct HeadInParams {
     int32_t* status;
 };
 
-// One CTA of 512 threads per stream (src/phonon_sampler.c:310-318):
+// Streams [8 * blockIdx.x, +8) per CTA of 512 threads, thread t = output
+// row t with its input_proj row in registers (src/phonon_sampler.c:310-318):
 // x = input_proj(noise) + b, y = cond + 0.5 * (time_s + time_t), silu(y)
 // (the same silu(y) feeds every block's and the final modulation).
+constexpr int kHeadInStreams = 8;
 __global__ void __launch_bounds__(512) head_in_kernel(HeadInParams p) {
-    __shared__ float nz[kLatent];
-    const int b = blockIdx.x, t = threadIdx.x;
-    pdl_wait();
+    __shared__ float nz[kHeadInStreams][kLatent];
+    const int t = threadIdx.x;
+    const int b_first = blockIdx.x * kHeadInStreams;
+    float wr[kLatent];
+    {
+        const uint4* row = reinterpret_cast<const uint4*>(p.in_w + static_cast<size_t>(t) * kLatent);
+#pragma unroll
+        for (int q = 0; q < kLatent / 8; ++q) {
+            const uint4 u = __ldg(row + q);
+            const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                wr[8 * q + 2 * e] = __uint_as_float(wd[e] << 16);
+                wr[8 * q + 2 * e + 1] = __uint_as_float(wd[e] & 0xffff0000u);
+            }
+        }
+    }
+    const float in_b = p.in_b[t];
+    pdl_wait();  // the time embeddings, conditions and noise come from earlier work
     pdl_trigger();
-    if (t < kLatent) {
-        const float r = p.noise[static_cast<size_t>(b) * kLatent + t];
-        if (!isfinite(r)) flag_nonfinite(p.status, b);
-        nz[t] = p.scaled ? __fmul_rn(r, p.noise_scale) : r;
+    const float half_t = __fmul_rn(0.5f, __fadd_rn(p.temb[t], p.temb[kWidth + t]));
+    if (t < kHeadInStreams * kLatent) {
+        const int bb = t / kLatent, k = t % kLatent, b = b_first + bb;
+        float r = 0.0f;
+        if (b < p.B) {
+            r = p.noise[static_cast<size_t>(b) * kLatent + k];
+            if (!isfinite(r)) flag_nonfinite(p.status, b);
+        }
+        nz[bb][k] = p.scaled ? __fmul_rn(r, p.noise_scale) : r;
     }
     __syncthreads();
-    const uint16_t* row = p.in_w + static_cast<size_t>(t) * kLatent;
-    float acc = 0.0f;
-#pragma unroll 8
-    for (int k = 0; k < kLatent; ++k) acc = fmaf(bf16_to_f32(__ldg(row + k)), nz[k], acc);
-    const float x = __fadd_rn(acc, p.in_b[t]);
-    const float y = __fadd_rn(p.cond[static_cast<size_t>(b) * p.ldc + t],
-                              __fmul_rn(0.5f, __fadd_rn(p.temb[t], p.temb[kWidth + t])));
-    const float sy = silu_f(y);
-    if (!isfinite(x) || !isfinite(sy)) flag_nonfinite(p.status, b);
-    p.x[static_cast<size_t>(b) * kWidth + t] = x;
-    if (p.sy_slices) {
-        uint16_t s0, s1, s2;
-        bf16x3_split(sy, s0, s1, s2);
-        uint16_t* row = p.sy_slices + static_cast<size_t>(3 * b) * kWidth + t;
-        row[0] = s0;
-        row[kWidth] = s1;
-        row[2 * kWidth] = s2;
-    } else {
-        p.silu_y[static_cast<size_t>(b) * kWidth + t] = sy;
+    for (int bb = 0; bb < kHeadInStreams; ++bb) {
+        const int b = b_first + bb;
+        if (b >= p.B) break;
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kLatent; ++k) acc = fmaf(wr[k], nz[bb][k], acc);
+        const float x = __fadd_rn(acc, in_b);
+        const float y = __fadd_rn(p.cond[static_cast<size_t>(b) * p.ldc + t], half_t);
+        const float sy = silu_f(y);
+        if (!isfinite(x) || !isfinite(sy)) flag_nonfinite(p.status, b);
+        p.x[static_cast<size_t>(b) * kWidth + t] = x;
+        if (p.sy_slices) {
+            uint16_t s0, s1, s2;
+            bf16x3_split(sy, s0, s1, s2);
+            uint16_t* row = p.sy_slices + static_cast<size_t>(3 * b) * kWidth + t;
+            row[0] = s0;
+            row[kWidth] = s1;
+            row[2 * kWidth] = s2;
+        } else {
+            p.silu_y[static_cast<size_t>(b) * kWidth + t] = sy;
+        }
     }
 }
 
