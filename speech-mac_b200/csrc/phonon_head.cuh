@@ -105,15 +105,59 @@ __device__ __forceinline__ bool head_ln_modulate(const float* x, const float* w,
     return __all_sync(kFull, ok);
 }
 
-// Row r of a natural row-major bf16 matrix [rows][cols] times v (shared
-// memory), summed by one warp (cols a multiple of 32): lane-strided partial
-// sums, then the warp tree.
-__device__ __forceinline__ float head_row_dot(const uint16_t* __restrict__ w, int cols, int r, const float* v) {
+// bf16 pair of a 32-bit word -> two floats (element 2i in the low half).
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Rows r0 .. r0+3 of a natural row-major bf16 matrix [rows][cols] times v
+// (shared memory), summed by one warp (cols a multiple of 256, rows 16-byte
+// aligned): lane l takes columns [8l + 256s, +8); every 16-byte load of the
+// four rows is issued before the arithmetic; then the warp tree.
+__device__ __forceinline__ float4 head_rows4_dot(const uint16_t* __restrict__ w, int cols, int r0, const float* v) {
     const int lane = threadIdx.x & 31;
-    const uint16_t* row = w + static_cast<size_t>(r) * cols;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int c0 = lane * 8; c0 < cols; c0 += 256) {
+        uint4 u[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            u[q] = __ldg(reinterpret_cast<const uint4*>(w + static_cast<size_t>(r0 + q) * cols + c0));
+        const float4 va = *reinterpret_cast<const float4*>(v + c0);
+        const float4 vb = *reinterpret_cast<const float4*>(v + c0 + 4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float a = acc[q];
+            a = fmaf(bf16_lo(u[q].x), va.x, a);
+            a = fmaf(bf16_hi(u[q].x), va.y, a);
+            a = fmaf(bf16_lo(u[q].y), va.z, a);
+            a = fmaf(bf16_hi(u[q].y), va.w, a);
+            a = fmaf(bf16_lo(u[q].z), vb.x, a);
+            a = fmaf(bf16_hi(u[q].z), vb.y, a);
+            a = fmaf(bf16_lo(u[q].w), vb.z, a);
+            a = fmaf(bf16_hi(u[q].w), vb.w, a);
+            acc[q] = a;
+        }
+    }
+    return make_float4(warp_sum(acc[0]), warp_sum(acc[1]), warp_sum(acc[2]), warp_sum(acc[3]));
+}
+
+// Row i of a natural row-major bf16 [rows][32] matrix times lat[32]
+// (shared memory), one thread: four 16-byte loads, then the products.
+__device__ __forceinline__ float head_row32_dot(const uint16_t* __restrict__ w, int i, const float* lat) {
+    const uint4* row = reinterpret_cast<const uint4*>(w + static_cast<size_t>(i) * kLatent);
+    uint4 u[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) u[q] = __ldg(row + q);
     float acc = 0.0f;
-    for (int k = lane; k < cols; k += 32) acc = fmaf(bf16_to_f32(__ldg(row + k)), v[k], acc);
-    return warp_sum(acc);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t wd[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            acc = fmaf(bf16_lo(wd[e]), lat[8 * q + 2 * e], acc);
+            acc = fmaf(bf16_hi(wd[e]), lat[8 * q + 2 * e + 1], acc);
+        }
+    }
+    return acc;
 }
 
 // Time embedding of one flow time (src/phonon_sampler.c:280-305), one CTA
@@ -126,7 +170,10 @@ __global__ void __launch_bounds__(512) head_time_kernel(float value, const float
                                                         const uint16_t* __restrict__ w1, const float* __restrict__ b1,
                                                         const float* __restrict__ alpha, float* __restrict__ out,
                                                         int32_t* status) {
-    __shared__ float e[256], hidden[kWidth], o[kWidth], sq[kWidth];
+    __shared__ __align__(16) float e[256];
+    __shared__ __align__(16) float hidden[kWidth];
+    __shared__ __align__(16) float o[kWidth];
+    __shared__ __align__(16) float sq[kWidth];
     __shared__ float inverse;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     if (t < 128) {
@@ -136,14 +183,15 @@ __global__ void __launch_bounds__(512) head_time_kernel(float value, const float
         e[128 + t] = s;
     }
     __syncthreads();
-    for (int r = warp; r < kWidth; r += 16) {
-        const float d = head_row_dot(w0, 256, r, e);
-        if (lane == 0) hidden[r] = silu_f(__fadd_rn(d, b0[r]));
+    for (int r = 4 * warp; r < kWidth; r += 64) {
+        const float4 d = head_rows4_dot(w0, 256, r, e);
+        if (lane < 4) hidden[r + lane] = silu_f(__fadd_rn(lane == 0 ? d.x : lane == 1 ? d.y : lane == 2 ? d.z : d.w,
+                                                          b0[r + lane]));
     }
     __syncthreads();
-    for (int r = warp; r < kWidth; r += 16) {
-        const float d = head_row_dot(w1, kWidth, r, hidden);
-        if (lane == 0) o[r] = __fadd_rn(d, b1[r]);
+    for (int r = 4 * warp; r < kWidth; r += 64) {
+        const float4 d = head_rows4_dot(w1, kWidth, r, hidden);
+        if (lane < 4) o[r + lane] = __fadd_rn(lane == 0 ? d.x : lane == 1 ? d.y : lane == 2 ? d.z : d.w, b1[r + lane]);
     }
     __syncthreads();
     sq[t] = __fmul_rn(o[t], o[t]);
@@ -289,7 +337,9 @@ struct HeadFinalParams {
 // src/phonon_transformer.c:860-875) when the frame loop asks for it: one
 // CTA of 256 threads per stream.
 __global__ void __launch_bounds__(256) head_final_kernel(HeadFinalParams p) {
-    __shared__ float xr[kWidth], h[kWidth], lat[kLatent];
+    __shared__ __align__(16) float xr[kWidth];
+    __shared__ __align__(16) float h[kWidth];
+    __shared__ __align__(16) float lat[kLatent];
     __shared__ int bad;
     const int b = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
     pdl_wait();
@@ -302,9 +352,12 @@ __global__ void __launch_bounds__(256) head_final_kernel(HeadFinalParams p) {
         if (!head_ln_modulate(xr, nullptr, nullptr, m, m + kWidth, h) && lane == 0) bad = 1;
     }
     __syncthreads();
-    for (int j = warp; j < kLatent; j += 8) {
-        const float v = __fadd_rn(head_row_dot(p.fin_w, kWidth, j, h), p.fin_b[j]);
-        if (lane == 0) {
+    {  // warp w: final rows 4w .. 4w+3
+        const int j0 = 4 * warp;
+        const float4 d = head_rows4_dot(p.fin_w, kWidth, j0, h);
+        if (lane < 4) {
+            const int j = j0 + lane;
+            const float v = __fadd_rn(lane == 0 ? d.x : lane == 1 ? d.y : lane == 2 ? d.z : d.w, p.fin_b[j]);
             float o = v;
             if (p.scaled) o = __fadd_rn(__fmul_rn(p.noise[static_cast<size_t>(b) * kLatent + j], p.noise_scale), v);
             if (!isfinite(o)) bad = 1;
@@ -314,15 +367,13 @@ __global__ void __launch_bounds__(256) head_final_kernel(HeadFinalParams p) {
     }
     __syncthreads();
     if (p.embed_out) {
-        for (int i = t; i < kWidth; i += 256) {
-            const uint16_t* row = p.embed_w + static_cast<size_t>(i) * kLatent;
-            float acc = 0.0f;
-#pragma unroll 8
-            for (int k = 0; k < kLatent; ++k) acc = fmaf(bf16_to_f32(__ldg(row + k)), lat[k], acc);
-            const float v = __fadd_rn(acc, p.condition[static_cast<size_t>(b) * kWidth + i]);
-            if (!isfinite(v)) bad = 1;
-            p.embed_out[static_cast<size_t>(b) * kWidth + i] = v;
-        }
+        const float c0 = p.condition[static_cast<size_t>(b) * kWidth + t];
+        const float c1 = p.condition[static_cast<size_t>(b) * kWidth + t + 256];
+        const float v0 = __fadd_rn(head_row32_dot(p.embed_w, t, lat), c0);
+        const float v1 = __fadd_rn(head_row32_dot(p.embed_w, t + 256, lat), c1);
+        if (!isfinite(v0) || !isfinite(v1)) bad = 1;
+        p.embed_out[static_cast<size_t>(b) * kWidth + t] = v0;
+        p.embed_out[static_cast<size_t>(b) * kWidth + t + 256] = v1;
         __syncthreads();
     }
     if (t == 0 && bad) flag_nonfinite(p.status, b);
