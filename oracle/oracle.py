@@ -108,6 +108,41 @@ def flow_head_struct(head):
     return h
 
 
+class OracleMimi(C.Structure):
+    _fields_ = [("projection", OracleLinear), ("upsample", C.c_void_p), ("in_proj", OracleLinear * 2),
+                ("out_proj", OracleLinear * 2), ("linear1", OracleLinear * 2), ("linear2", OracleLinear * 2),
+                ("norm1_w", C.c_void_p * 2), ("norm1_b", C.c_void_p * 2), ("norm2_w", C.c_void_p * 2),
+                ("norm2_b", C.c_void_p * 2), ("scale1", C.c_void_p * 2), ("scale2", C.c_void_p * 2),
+                ("rope_theta", C.c_float)]
+
+
+class OracleMimiState(C.Structure):
+    _fields_ = [("position", C.c_size_t), ("failed", C.c_int), ("previous", C.c_float * 512),
+                ("keys", C.POINTER(C.c_float)), ("values", C.POINTER(C.c_float))]
+
+
+MIMI_FIELDS = ("in_proj", "out_proj", "linear1", "linear2", "norm1_w", "norm1_b", "norm2_w", "norm2_b",
+               "scale1", "scale2")  # the reference's per-layer tensor order (src/phonon_mimi.c:57-66)
+MIMI_SHAPES = {"in_proj": (1536, 512), "out_proj": (512, 512), "linear1": (2048, 512), "linear2": (512, 2048)}
+
+
+def mimi_struct(model):
+    """OracleMimi over a Mimi model given as bf16 (uint16) arrays:
+    {"projection": [512, 32], "upsample": [512, 32], "layers": [{field: array}] * 2}
+    with the fields of MIMI_FIELDS (matrices [rows, cols], vectors [512])."""
+    m = OracleMimi()
+    m.projection = OracleLinear(2, 512, 32, model["projection"].ctypes.data)
+    m.upsample = model["upsample"].ctypes.data
+    for i, layer in enumerate(model["layers"]):
+        for f, (rows, cols) in MIMI_SHAPES.items():
+            assert layer[f].shape == (rows, cols) and layer[f].dtype == np.uint16
+            getattr(m, f)[i] = OracleLinear(2, rows, cols, layer[f].ctypes.data)
+        for f in MIMI_FIELDS[4:]:
+            getattr(m, f)[i] = layer[f].ctypes.data
+    m.rope_theta = 10000.0
+    return m
+
+
 def _head_call(fn, head, condition, state, *scalars):
     out = np.zeros(32, np.float32)
     h = flow_head_struct(head)
@@ -157,6 +192,16 @@ class Oracle:
         L.oracle_flow_lsd_one_step.restype = C.c_int
         L.oracle_flow_lsd_one_step.argtypes = [C.POINTER(OracleFlowHead), C.c_void_p, C.c_void_p,
                                                C.c_float, C.c_void_p]
+        L.oracle_mimi_state_init.restype = C.c_int
+        L.oracle_mimi_state_init.argtypes = [C.POINTER(OracleMimiState)]
+        L.oracle_mimi_state_free.argtypes = [C.POINTER(OracleMimiState)]
+        L.oracle_mimi_state_reset.argtypes = [C.POINTER(OracleMimiState)]
+        L.oracle_mimi_upsample_frame.restype = C.c_int
+        L.oracle_mimi_upsample_frame.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t,
+                                                 C.c_void_p]
+        L.oracle_mimi_process.restype = C.c_int
+        L.oracle_mimi_process.argtypes = [C.POINTER(OracleMimi), C.POINTER(OracleMimiState), C.c_void_p,
+                                          C.c_size_t, C.c_void_p]
 
     # flow head ---------------------------------------------------------------
     def flow_head_forward(self, head, condition, state, s, t):
@@ -165,6 +210,17 @@ class Oracle:
 
     def flow_lsd_one_step(self, head, condition, raw_noise, temperature):
         return _head_call(self.lib.oracle_flow_lsd_one_step, head, condition, raw_noise, temperature)
+
+    # Mimi --------------------------------------------------------------------
+    def mimi(self, model):
+        return OracleMimiRunner(self, model)
+
+    def mimi_upsample(self, weight, x, previous, channels, stride):
+        out = np.zeros(channels * stride, np.float32)
+        ok = self.lib.oracle_mimi_upsample_frame(_ptr(weight), _ptr(np.ascontiguousarray(x, np.float32)),
+                                                 _ptr(np.ascontiguousarray(previous, np.float32)), channels,
+                                                 stride, _ptr(out))
+        return bool(ok), out
 
     # primitives -------------------------------------------------------------
     def half_to_float(self, bits):
@@ -297,10 +353,100 @@ class OracleModel:
         return keys[base:base + 512].copy(), vals[base:base + 512].copy()
 
 
+class OracleMimiRunner:
+    """One request state of the restated Mimi transformer."""
+
+    def __init__(self, oracle, model):
+        self.o = oracle
+        self.model = model
+        self.struct = mimi_struct(model)
+        self.state = OracleMimiState()
+        if not oracle.lib.oracle_mimi_state_init(C.byref(self.state)):
+            raise MemoryError("oracle mimi state")
+
+    def reset(self):
+        self.o.lib.oracle_mimi_state_reset(C.byref(self.state))
+
+    def process(self, latents):
+        """(ok, features [frames * 16][512]) for latents [frames][32]."""
+        latents = np.ascontiguousarray(latents, np.float32).reshape(-1, 32)
+        out = np.zeros((latents.shape[0] * 16, 512), np.float32)
+        ok = self.o.lib.oracle_mimi_process(C.byref(self.struct), C.byref(self.state), _ptr(latents),
+                                            latents.shape[0], _ptr(out))
+        return bool(ok), out
+
+    @property
+    def position(self):
+        return self.state.position
+
+    def close(self):
+        self.o.lib.oracle_mimi_state_free(C.byref(self.state))
+
+
+class PhononMimiConfig(C.Structure):
+    """src/phonon_mimi.h:10-16 layout."""
+    _fields_ = [("sample_rate", C.c_uint), ("frame_rate", C.c_float), ("ratios", C.c_uint * 3),
+                ("context", C.c_size_t), ("rope_theta", C.c_float)]
+
+
 class PhononTensorView(C.Structure):
     """src/phonon_pack.h:10-19 layout."""
     _fields_ = [("dtype", C.c_int), ("rank", C.c_uint), ("shape", C.c_uint64 * 8),
                 ("data", C.c_void_p), ("byte_count", C.c_size_t), ("linear_data", C.c_void_p)]
+
+
+class PhononMimiModel(C.Structure):
+    """src/phonon_mimi.h:19-24 layout."""
+    _fields_ = [("config", PhononMimiConfig), ("stride", C.c_size_t), ("projection", PhononTensorView),
+                ("upsample", PhononTensorView), ("layers", (PhononTensorView * 10) * 2)]
+
+
+def _bf16_view(a, shape):
+    v = PhononTensorView()
+    v.dtype, v.rank = 2, len(shape)
+    for i, n in enumerate(shape):
+        v.shape[i] = n
+    v.data = a.ctypes.data
+    v.byte_count = a.size * 2
+    return v
+
+
+class RefMimiRunner:
+    """One request state of the reference's own phonon_mimi_process."""
+
+    def __init__(self, ref, model):
+        self.r = ref
+        self.model = model
+        m = self.struct = PhononMimiModel()
+        m.config = ref.lib.phonon_mimi_config()
+        m.stride = 16
+        m.projection = _bf16_view(model["projection"], (512, 32, 1))
+        m.upsample = _bf16_view(model["upsample"], (512, 1, 32))
+        for i, layer in enumerate(model["layers"]):
+            for f_i, f in enumerate(MIMI_FIELDS):
+                shape = MIMI_SHAPES[f] if f in MIMI_SHAPES else (512,)
+                m.layers[i][f_i] = _bf16_view(layer[f], shape)
+        self.state = C.c_void_p()
+        if not ref.lib.phonon_mimi_state_create(C.byref(m), C.byref(self.state)):
+            raise RuntimeError("phonon_mimi_state_create failed")
+
+    def reset(self):
+        self.r.lib.phonon_mimi_state_reset(self.state)
+
+    def process(self, latents):
+        latents = np.ascontiguousarray(latents, np.float32).reshape(-1, 32)
+        out = np.zeros((latents.shape[0] * 16, 512), np.float32)
+        ok = self.r.lib.phonon_mimi_process(self.state, _ptr(latents), latents.shape[0], _ptr(out), out.shape[0])
+        return bool(ok), out
+
+    @property
+    def position(self):
+        return self.r.lib.phonon_mimi_positions(self.state)
+
+    def close(self):
+        if self.state:
+            self.r.lib.phonon_mimi_state_destroy(self.state)
+            self.state = C.c_void_p()
 
 
 class Reference:
@@ -353,6 +499,18 @@ class Reference:
         L.phonon_math_sincos.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]
         L.phonon_math_exp4.argtypes = [C.c_void_p]
         L.phonon_math_silu.argtypes = [C.c_void_p, C.c_size_t]
+        L.phonon_mimi_config.restype = PhononMimiConfig
+        L.phonon_mimi_state_create.restype = C.c_int
+        L.phonon_mimi_state_create.argtypes = [C.POINTER(PhononMimiModel), C.POINTER(C.c_void_p)]
+        L.phonon_mimi_state_reset.argtypes = [C.c_void_p]
+        L.phonon_mimi_state_destroy.argtypes = [C.c_void_p]
+        L.phonon_mimi_positions.restype = C.c_size_t
+        L.phonon_mimi_positions.argtypes = [C.c_void_p]
+        L.phonon_mimi_process.restype = C.c_int
+        L.phonon_mimi_process.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]
+        L.phonon_mimi_upsample_frame.restype = C.c_int
+        L.phonon_mimi_upsample_frame.argtypes = [C.POINTER(PhononTensorView), C.c_void_p, C.c_void_p, C.c_size_t,
+                                                 C.c_size_t, C.c_void_p]
 
     def q8_dot(self, blocks, x):
         out = C.c_float()
@@ -416,6 +574,18 @@ class Reference:
 
     def flow_lsd_one_step(self, head, condition, raw_noise, temperature):
         return _head_call(self.lib.ref_flow_lsd_one_step, head, condition, raw_noise, temperature)
+
+    # Mimi --------------------------------------------------------------------
+    def mimi(self, model):
+        return RefMimiRunner(self, model)
+
+    def mimi_upsample(self, weight, x, previous, channels, stride):
+        out = np.zeros(channels * stride, np.float32)
+        v = _bf16_view(weight, (channels, 1, 2 * stride))
+        ok = self.lib.phonon_mimi_upsample_frame(C.byref(v), _ptr(np.ascontiguousarray(x, np.float32)),
+                                                 _ptr(np.ascontiguousarray(previous, np.float32)), channels,
+                                                 stride, _ptr(out))
+        return bool(ok), out
 
 class RefModel:
     def __init__(self, ref, weights, dtype=1):

@@ -103,4 +103,31 @@ int oracle_flow_head_forward(const OracleFlowHead *head, const float condition[5
 int oracle_flow_lsd_one_step(const OracleFlowHead *head, const float condition[512],
                              const float raw_noise[32], float temperature, float output[32]);
 
+/* ---- Mimi latent transformer (src/phonon_mimi.c): bf16 weights, no biases ---- */
+typedef struct {
+    OracleLinear projection;                 /* [512, 32] mimi.quantizer.output_proj */
+    const uint16_t *upsample;                /* [512][32] depthwise transposed-conv kernel */
+    OracleLinear in_proj[2], out_proj[2];    /* [1536, 512], [512, 512] */
+    OracleLinear linear1[2], linear2[2];     /* [2048, 512], [512, 2048] */
+    const uint16_t *norm1_w[2], *norm1_b[2], *norm2_w[2], *norm2_b[2];  /* bf16 [512] */
+    const uint16_t *scale1[2], *scale2[2];   /* layer scales, bf16 [512] */
+    float rope_theta;
+} OracleMimi;
+
+typedef struct {
+    size_t position;
+    int failed;
+    float previous[512];
+    float *keys, *values; /* [2][250][512] ring */
+} OracleMimiState;
+
+int oracle_mimi_state_init(OracleMimiState *state);
+void oracle_mimi_state_free(OracleMimiState *state);
+void oracle_mimi_state_reset(OracleMimiState *state);
+int oracle_mimi_upsample_frame(const uint16_t *weight, const float *input, const float *previous,
+                               size_t channels, size_t stride, float *output);
+/* latents [frames][32] -> features [frames * 16][512] (src/phonon_mimi.c:246-283). */
+int oracle_mimi_process(const OracleMimi *model, OracleMimiState *state, const float *latents,
+                        size_t frames, float *features);
+
 #endif
