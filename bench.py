@@ -403,6 +403,7 @@ def run_ours(args):
         extras["single_stream"] = bench_single_stream(rt, synth, weights, torch)
         extras["prefill"] = bench_prefill(rt, synth, weights, torch)
         lens3 = [int(x) for x in np.random.default_rng(2).integers(64, 2049, 512)]
+        extras["mimi"] = bench_mimi(rt, synth, torch)
         extras["frame_loop"] = {
             "configs3": bench_frame_loop(rt, synth, weights, torch, lens3, rt.KV_BF16, 10),
             "configs0": bench_frame_loop(rt, synth, weights, torch, [128], rt.KV_F32, 100),
@@ -463,6 +464,7 @@ def run_ours(args):
                 line["config2"]["cpu_baseline"] = cpu["config2"]
                 line["config4"]["cpu_baseline"] = cpu["config4"]
                 line["frame_loop"]["cpu_baseline_head"] = cpu["flow_head"]
+                line["mimi"]["cpu_baseline"] = cpu["mimi"]
         print(json.dumps(line), flush=True)
     ctx.close()
     if dist:
@@ -658,6 +660,36 @@ def bench_frame_loop(rt, synth, weights, torch, lengths, kv_type, frames, warmup
     finally:
         head.close()
         ctx.close()
+
+
+def bench_mimi(rt, synth, torch, batches=(1, 64), frames=40, warmup=3):
+    """The Mimi latent transformer (phonon_cuda_mimi_step): one latent frame
+    -> 16 feature rows for each of n request states per call, host buffers
+    (H2D of the latents and D2H of the features inside), host clock around
+    the synchronous call; the states' rings fill past the 250-key window."""
+    out = {}
+    model = synth.mimi_model(0)
+    rng = np.random.default_rng(5)
+    for n in batches:
+        m = rt.Mimi(model, max_states=n, max_batch=n)
+        try:
+            states = [m.alloc() for _ in range(n)]
+            lat = rng.standard_normal((warmup + frames + 16, n, 32)).astype(np.float32)
+            for k in range(16 + warmup):  # past the first 250 positions
+                m.step(states, lat[k])
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for k in range(frames):
+                _, status = m.step(states, lat[16 + warmup + k])
+                if status.any():
+                    raise RuntimeError("mimi step failed")
+            dt = time.perf_counter() - t0
+        finally:
+            m.close()
+        out[f"states{n}"] = {"frames_per_s": round(n * frames / dt, 1), "ms_per_step": round(dt / frames * 1e3, 4),
+                             "feature_rows_per_s": round(16 * n * frames / dt, 1)}
+    return {"workload": "Mimi latent transformer, random bf16 model, rings past the 250-key window",
+            "timing": "host clock around phonon_cuda_mimi_step (latents up, features down)", **out}
 
 
 def bench_config2(rt, weights, torch):
@@ -892,6 +924,18 @@ def cpu_extras(seconds=3.0):
     dt = time.perf_counter() - t0
     out["flow_head"] = {"value": round(n / dt, 1), "unit": "head steps/s", "cores": 1, "kind": "reference",
                         "sample": f"phonon_flow_lsd_one_step, one row, {n} calls in {dt:.2f} s"}
+    mimi = ref.mimi(synth.mimi_model(0))
+    lat = rng.standard_normal((4096, 32)).astype(np.float32)
+    mimi.process(lat[:16])  # past the first 250 positions
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds / 4 and n < 4000:
+        ok, _ = mimi.process(lat[16 + n:17 + n])
+        assert ok
+        n += 1
+    dt = time.perf_counter() - t0
+    mimi.close()
+    out["mimi"] = {"value": round(n / dt, 1), "unit": "frames/s", "cores": 1, "kind": "reference",
+                   "sample": f"phonon_mimi_process, one state, one frame per call, {n} frames in {dt:.2f} s"}
     lens2 = [int(x) for x in np.random.default_rng(1).integers(32, 513, threads)]
     for key, lens, what in (("config2", lens2, "prefixes U[32,512] seed 1"),
                             ("config4", [2304] * min(threads, 8), "contexts 2304 (mid-run of 256..4352)")):

@@ -381,6 +381,46 @@ int phonon_cuda_frame_step(PhononCudaHead *head, uint32_t batch, const uint32_t 
                            float *state_dev, const float *condition_dev, const float *raw_noise, float temperature,
                            float *eos_logit, float *latent, int32_t *status);
 
+/* ---- Mimi latent transformer (src/phonon_mimi.c:108-283) ----
+ * Each latent frame [32] of a request becomes 16 feature rows [512]: the
+ * projection, the depthwise transposed-convolution upsample and two
+ * transformer layers whose queries attend over at most 250 earlier rows.
+ * Weights are bf16 bits, host memory, borrowed only during create; matrices
+ * row-major: in_proj [1536][512], out_proj [512][512], linear1 [2048][512],
+ * linear2 [512][2048], vectors [512]; the pack tensors
+ * mimi.quantizer.output_proj.weight [512][32][1], mimi.upsample.convtr.convtr.weight
+ * [512][1][32] and mimi.decoder_transformer.transformer.layers.{0,1}.* that
+ * phonon_mimi_model_load reads. */
+#define PHONON_CUDA_MIMI_MAX_FRAMES 8192 /* PHONON_MIMI_MAX_FRAMES */
+typedef struct {
+    const uint16_t *projection, *upsample;
+    const uint16_t *in_proj[2], *out_proj[2], *linear1[2], *linear2[2];
+    const uint16_t *norm1_w[2], *norm1_b[2], *norm2_w[2], *norm2_b[2];
+    const uint16_t *scale1[2], *scale2[2]; /* layer_scale_1, layer_scale_2 */
+} PhononCudaMimiWeights;
+
+typedef struct PhononCudaMimi PhononCudaMimi;
+/* max_states request states resident on `device`; steps of up to max_batch states. */
+int phonon_cuda_mimi_create(int device, const PhononCudaMimiWeights *weights, uint32_t max_states,
+                            uint32_t max_batch, PhononCudaMimi **out);
+void phonon_cuda_mimi_destroy(PhononCudaMimi *mimi);
+/* A request state (phonon_mimi_state_create / _reset / _destroy / _positions). */
+int phonon_cuda_mimi_state_alloc(PhononCudaMimi *mimi, uint32_t *state);
+int phonon_cuda_mimi_state_reset(PhononCudaMimi *mimi, uint32_t state);
+int phonon_cuda_mimi_state_free(PhononCudaMimi *mimi, uint32_t state);
+int phonon_cuda_mimi_positions(PhononCudaMimi *mimi, uint32_t state, uint64_t *positions);
+/* One frame of each of n distinct states at once: latents [n][32] (host) ->
+ * features [n][16][512] (host). status[i] is OK, or NON_FINITE when the
+ * state's frame produced a non-finite value: that state is then unusable
+ * until reset (calls with it return INVALID_ARGUMENT), as in the reference.
+ * A non-finite latent rejects the whole call before any work. */
+int phonon_cuda_mimi_step(PhononCudaMimi *mimi, uint32_t n, const uint32_t *states, const float *latents,
+                          float *features, int32_t *status);
+/* phonon_mimi_process for one state: frames latents [frames][32] ->
+ * features [frames * 16][512], capacity in feature rows. */
+int phonon_cuda_mimi_process(PhononCudaMimi *mimi, uint32_t state, const float *latents, size_t frames,
+                             float *features, size_t capacity);
+
 const char *phonon_cuda_status_string(int status);
 
 #ifdef __cplusplus

@@ -7,6 +7,7 @@
 #include "phonon_cluster.cuh"
 #include "phonon_persist.cuh"
 #include "phonon_head.cuh"
+#include "phonon_mimi.cuh"
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -3363,6 +3364,339 @@ int phonon_cuda_frame_step(PhononCudaHead* h, uint32_t batch, const uint32_t* st
         std::memcpy(latent + static_cast<size_t>(i) * phonon::kLatent,
                     h->h_out + static_cast<size_t>(i) * phonon::kLatent, phonon::kLatent * 4);
         eos_logit[i] = h->h_out[static_cast<size_t>(B) * phonon::kLatent + i];
+    }
+    return PHONON_CUDA_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ Mimi
+// The Mimi latent transformer (phonon_mimi.cuh): weights, per-request ring
+// states and a step of one frame for a batch of states, on its own stream.
+struct PhononCudaMimi {
+    int device = 0;
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    uint32_t max_states = 0, max_batch = 0;
+    DevLinear in_proj[phonon::kMimiLayers], out_proj[phonon::kMimiLayers], linear1[phonon::kMimiLayers],
+        linear2[phonon::kMimiLayers];
+    uint16_t* w16 = nullptr;   // projection [512][32], upsample [512][32]
+    float* vec = nullptr;      // per layer: norm1 w, b, norm2 w, b, scale1, scale2 [512]; zeros [512]; freq [32]
+    float* rings = nullptr;    // [state][layer][k|v][272][512]
+    float* previous = nullptr; // [state][512]
+    // scratch for max_batch states (16 rows each)
+    float *d_lat = nullptr, *d_hidden = nullptr, *d_norm = nullptr, *d_qkv = nullptr, *d_att = nullptr,
+          *d_mlp = nullptr;
+    int32_t *d_meta = nullptr, *d_status = nullptr;  // meta: slots [max_batch], positions [max_batch]
+    float *h_lat = nullptr, *h_out = nullptr;
+    int32_t *h_meta = nullptr, *h_status = nullptr;
+    struct State {
+        bool used = false, failed = false;
+        uint64_t position = 0;
+    };
+    std::vector<State> states;
+};
+
+namespace {
+
+constexpr int kMimiVecPerLayer = 6;
+
+void mimi_release(PhononCudaMimi* m) {
+    for (int l = 0; l < phonon::kMimiLayers; ++l) {
+        free_linear(m->in_proj[l]);
+        free_linear(m->out_proj[l]);
+        free_linear(m->linear1[l]);
+        free_linear(m->linear2[l]);
+    }
+    for (void* p : {static_cast<void*>(m->w16), static_cast<void*>(m->vec), static_cast<void*>(m->rings),
+                    static_cast<void*>(m->previous), static_cast<void*>(m->d_lat), static_cast<void*>(m->d_hidden),
+                    static_cast<void*>(m->d_norm), static_cast<void*>(m->d_qkv), static_cast<void*>(m->d_att),
+                    static_cast<void*>(m->d_mlp), static_cast<void*>(m->d_meta), static_cast<void*>(m->d_status)})
+        if (p) cudaFree(p);
+    for (void* p : {static_cast<void*>(m->h_lat), static_cast<void*>(m->h_out), static_cast<void*>(m->h_meta),
+                    static_cast<void*>(m->h_status)})
+        if (p) cudaFreeHost(p);
+    if (m->stream) cudaStreamDestroy(m->stream);
+}
+
+int mimi_setup(PhononCudaMimi* m, const PhononCudaMimiWeights& w) {
+    using namespace phonon;
+    constexpr size_t W = kWidth;
+    // vectors
+    std::vector<float> v(kMimiLayers * kMimiVecPerLayer * W + W + 32, 0.0f);
+    for (int l = 0; l < kMimiLayers; ++l) {
+        const uint16_t* src[kMimiVecPerLayer] = {w.norm1_w[l], w.norm1_b[l], w.norm2_w[l],
+                                                 w.norm2_b[l], w.scale1[l],  w.scale2[l]};
+        for (int k = 0; k < kMimiVecPerLayer; ++k)
+            if (!head_vec(src[k], W, &v[(l * kMimiVecPerLayer + k) * W])) return PHONON_CUDA_NON_FINITE;
+    }
+    rope_frequencies(10000.0f, kHeadDim, &v[kMimiLayers * kMimiVecPerLayer * W + W]);
+    // natural bf16 projection and upsample kernel
+    if (!head_mat(w.projection, W * 32) || !head_mat(w.upsample, W * 32)) return PHONON_CUDA_NON_FINITE;
+    CUDA_TRY(cudaMalloc(&m->w16, 2 * W * 32 * 2));
+    CUDA_TRY(cudaMemcpy(m->w16, w.projection, W * 32 * 2, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(m->w16 + W * 32, w.upsample, W * 32 * 2, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMalloc(&m->vec, v.size() * 4));
+    CUDA_TRY(cudaMemcpy(m->vec, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+    int st;
+    for (int l = 0; l < kMimiLayers; ++l) {
+        if (!w.in_proj[l] || !w.out_proj[l] || !w.linear1[l] || !w.linear2[l]) return PHONON_CUDA_INVALID_ARGUMENT;
+        if ((st = upload_linear(PHONON_CUDA_LINEAR_BF16, w.in_proj[l], 3 * W, W, &m->in_proj[l])) ||
+            (st = upload_linear(PHONON_CUDA_LINEAR_BF16, w.out_proj[l], W, W, &m->out_proj[l])) ||
+            (st = upload_linear(PHONON_CUDA_LINEAR_BF16, w.linear1[l], kFfn, W, &m->linear1[l])) ||
+            (st = upload_linear(PHONON_CUDA_LINEAR_BF16, w.linear2[l], W, kFfn, &m->linear2[l])))
+            return st;
+    }
+    const size_t S = m->max_states, rows = static_cast<size_t>(m->max_batch) * kMimiRows;
+    if (cudaMalloc(&m->rings, S * kMimiLayers * 2 * kMimiRing * W * 4) != cudaSuccess ||
+        cudaMalloc(&m->previous, S * W * 4) != cudaSuccess ||
+        cudaMalloc(&m->d_lat, m->max_batch * 32 * 4) != cudaSuccess ||
+        cudaMalloc(&m->d_hidden, rows * W * 4) != cudaSuccess || cudaMalloc(&m->d_norm, rows * W * 4) != cudaSuccess ||
+        cudaMalloc(&m->d_qkv, rows * 3 * W * 4) != cudaSuccess || cudaMalloc(&m->d_att, rows * W * 4) != cudaSuccess ||
+        cudaMalloc(&m->d_mlp, rows * kFfn * 4) != cudaSuccess ||
+        cudaMalloc(&m->d_meta, 2 * m->max_batch * 4) != cudaSuccess ||
+        cudaMalloc(&m->d_status, rows * 4) != cudaSuccess ||
+        cudaMallocHost(&m->h_lat, m->max_batch * 32 * 4) != cudaSuccess ||
+        cudaMallocHost(&m->h_out, rows * W * 4) != cudaSuccess ||
+        cudaMallocHost(&m->h_meta, 2 * m->max_batch * 4) != cudaSuccess ||
+        cudaMallocHost(&m->h_status, rows * 4) != cudaSuccess)
+        return PHONON_CUDA_OUT_OF_MEMORY;
+    CUDA_TRY(cudaMemset(m->previous, 0, S * W * 4));
+    CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    m->states.assign(S, PhononCudaMimi::State{});
+    return PHONON_CUDA_OK;
+}
+
+// One frame of n states whose latents are in m->d_lat and slot/position
+// metadata in m->d_meta: features in m->d_hidden, per-row status.
+int mimi_enqueue(PhononCudaMimi* m, int n) {
+    using namespace phonon;
+    cudaStream_t s = m->stream;
+    const int rows = n * kMimiRows;
+    const int32_t* slots = m->d_meta;
+    const int32_t* pos = m->d_meta + m->max_batch;
+    const float* zeros = m->vec + kMimiLayers * kMimiVecPerLayer * kWidth;
+    const float* freq = zeros + kWidth;
+    CUDA_TRY(launch_pdl(mimi_in_kernel, dim3(n), dim3(512), 0, s, static_cast<const float*>(m->d_lat), slots,
+                        static_cast<const uint16_t*>(m->w16), static_cast<const uint16_t*>(m->w16 + kWidth * 32),
+                        m->previous, m->d_hidden, m->d_status));
+    for (int l = 0; l < kMimiLayers; ++l) {
+        const float* v = m->vec + l * kMimiVecPerLayer * kWidth;
+        CUDA_TRY(launch_pdl(mimi_ln_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, static_cast<const float*>(m->d_hidden),
+                            v, v + kWidth, m->d_norm, rows, m->d_status));
+        GemvParams p{};
+        p.rows = 3 * kWidth;
+        p.cols = kWidth;
+        p.w = m->in_proj[l].plane;
+        p.x = m->d_norm;
+        p.ldx = kWidth;
+        p.B = rows;
+        p.y = m->d_qkv;
+        p.ldy = 3 * kWidth;
+        p.status = m->d_status;
+        CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_STORE>(p, s)));
+        CUDA_TRY(launch_pdl(mimi_rope_kv_kernel, dim3(rows), dim3(256), 0, s, m->d_qkv, slots, pos, freq, m->rings, l));
+        CUDA_TRY(launch_pdl(mimi_attn_kernel, dim3(rows), dim3(256), 0, s, static_cast<const float*>(m->d_qkv), slots, pos,
+                            static_cast<const float*>(m->rings), l, m->d_att, m->d_status));
+        p = GemvParams{};
+        p.rows = kWidth;
+        p.cols = kWidth;
+        p.w = m->out_proj[l].plane;
+        p.x = m->d_att;
+        p.ldx = kWidth;
+        p.B = rows;
+        p.bias = zeros;
+        p.y = m->d_hidden;
+        p.ldy = kWidth;
+        p.res = m->d_hidden;
+        p.ldres = kWidth;
+        p.gate = v + 4 * kWidth;  // layer_scale_1, the same for every row
+        p.ldgate = 0;
+        p.status = m->d_status;
+        CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_GATE>(p, s)));
+        CUDA_TRY(launch_pdl(mimi_ln_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, static_cast<const float*>(m->d_hidden),
+                            v + 2 * kWidth, v + 3 * kWidth, m->d_norm, rows, m->d_status));
+        p = GemvParams{};
+        p.rows = kFfn;
+        p.cols = kWidth;
+        p.w = m->linear1[l].plane;
+        p.x = m->d_norm;
+        p.ldx = kWidth;
+        p.B = rows;
+        p.y = m->d_mlp;
+        p.ldy = kFfn;
+        p.status = m->d_status;
+        CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_GELU>(p, s)));
+        p = GemvParams{};
+        p.rows = kWidth;
+        p.cols = kFfn;
+        p.w = m->linear2[l].plane;
+        p.x = m->d_mlp;
+        p.ldx = kFfn;
+        p.B = rows;
+        p.bias = zeros;
+        p.y = m->d_hidden;
+        p.ldy = kWidth;
+        p.res = m->d_hidden;
+        p.ldres = kWidth;
+        p.gate = v + 5 * kWidth;  // layer_scale_2
+        p.ldgate = 0;
+        p.status = m->d_status;
+        CUDA_TRY((launch_gemv_bt<false, 4, SRC_X, EPI_GATE>(p, s)));
+    }
+    return PHONON_CUDA_OK;
+}
+
+// One frame for n distinct live states (host latents [n][32] -> host
+// features [n][16][512]); per-state status.
+int mimi_step_locked(PhononCudaMimi* m, uint32_t n, const uint32_t* states, const float* latents, float* features,
+                     int32_t* status) {
+    using namespace phonon;
+    if (n < 1 || n > m->max_batch || !states || !latents || !features || !status) return PHONON_CUDA_INVALID_ARGUMENT;
+    for (uint32_t i = 0; i < n; ++i) {
+        if (states[i] >= m->max_states || !m->states[states[i]].used) return PHONON_CUDA_INVALID_ARGUMENT;
+        for (uint32_t j = 0; j < i; ++j)
+            if (states[j] == states[i]) return PHONON_CUDA_INVALID_ARGUMENT;
+        if (m->states[states[i]].failed) return PHONON_CUDA_INVALID_ARGUMENT;
+        if (m->states[states[i]].position / kMimiRows >= PHONON_CUDA_MIMI_MAX_FRAMES) return PHONON_CUDA_CAPACITY;
+        if (m->states[states[i]].position + kMimiRows > static_cast<uint64_t>(INT32_MAX)) return PHONON_CUDA_CAPACITY;
+    }
+    for (size_t i = 0; i < static_cast<size_t>(n) * 32; ++i)
+        if (!std::isfinite(latents[i])) return PHONON_CUDA_NON_FINITE;
+    int st = set_device(m->device);
+    if (st) return st;
+    for (uint32_t i = 0; i < n; ++i) {
+        m->h_meta[i] = static_cast<int32_t>(states[i]);
+        m->h_meta[m->max_batch + i] = static_cast<int32_t>(m->states[states[i]].position);
+    }
+    std::memcpy(m->h_lat, latents, static_cast<size_t>(n) * 32 * 4);
+    const size_t rows = static_cast<size_t>(n) * kMimiRows;
+    CUDA_TRY(cudaMemcpyAsync(m->d_meta, m->h_meta, 2 * m->max_batch * 4, cudaMemcpyHostToDevice, m->stream));
+    CUDA_TRY(cudaMemcpyAsync(m->d_lat, m->h_lat, static_cast<size_t>(n) * 32 * 4, cudaMemcpyHostToDevice, m->stream));
+    CUDA_TRY(cudaMemsetAsync(m->d_status, 0, rows * 4, m->stream));
+    if ((st = mimi_enqueue(m, static_cast<int>(n)))) return st;
+    CUDA_TRY(cudaMemcpyAsync(m->h_out, m->d_hidden, rows * kWidth * 4, cudaMemcpyDeviceToHost, m->stream));
+    CUDA_TRY(cudaMemcpyAsync(m->h_status, m->d_status, rows * 4, cudaMemcpyDeviceToHost, m->stream));
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    for (uint32_t i = 0; i < n; ++i) {
+        bool bad = false;
+        for (int r = 0; r < kMimiRows; ++r) bad |= m->h_status[i * kMimiRows + r] != 0;
+        PhononCudaMimi::State& s = m->states[states[i]];
+        if (bad) {
+            s.failed = true;  // the reference marks the state unusable until reset
+            status[i] = PHONON_CUDA_NON_FINITE;
+            continue;
+        }
+        status[i] = PHONON_CUDA_OK;
+        s.position += kMimiRows;
+        std::memcpy(features + static_cast<size_t>(i) * kMimiRows * kWidth,
+                    m->h_out + static_cast<size_t>(i) * kMimiRows * kWidth, kMimiRows * kWidth * 4);
+    }
+    return PHONON_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int phonon_cuda_mimi_create(int device, const PhononCudaMimiWeights* w, uint32_t max_states, uint32_t max_batch,
+                            PhononCudaMimi** out) {
+    if (!w || !out || !max_states || !max_batch || max_batch > max_states || max_states > 65536)
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(device);
+    if (st) return st;
+    PhononCudaMimi* m = new (std::nothrow) PhononCudaMimi;
+    if (!m) return PHONON_CUDA_OUT_OF_MEMORY;
+    m->device = device;
+    m->max_states = max_states;
+    m->max_batch = max_batch;
+    if ((st = mimi_setup(m, *w))) {
+        mimi_release(m);
+        delete m;
+        return st;
+    }
+    *out = m;
+    return PHONON_CUDA_OK;
+}
+
+void phonon_cuda_mimi_destroy(PhononCudaMimi* m) {
+    if (!m) return;
+    set_device(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    mimi_release(m);
+    delete m;
+}
+
+int phonon_cuda_mimi_state_alloc(PhononCudaMimi* m, uint32_t* state) {
+    if (!m || !state) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(m->mu);
+    for (uint32_t i = 0; i < m->max_states; ++i)
+        if (!m->states[i].used) {
+            int st = set_device(m->device);
+            if (st) return st;
+            CUDA_TRY(cudaMemsetAsync(m->previous + static_cast<size_t>(i) * phonon::kWidth, 0, phonon::kWidth * 4,
+                                     m->stream));
+            CUDA_TRY(cudaStreamSynchronize(m->stream));
+            m->states[i] = PhononCudaMimi::State{true, false, 0};
+            *state = i;
+            return PHONON_CUDA_OK;
+        }
+    return PHONON_CUDA_CAPACITY;
+}
+
+int phonon_cuda_mimi_state_reset(PhononCudaMimi* m, uint32_t state) {
+    if (!m || state >= m->max_states) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(m->mu);
+    if (!m->states[state].used) return PHONON_CUDA_INVALID_ARGUMENT;
+    int st = set_device(m->device);
+    if (st) return st;
+    CUDA_TRY(cudaMemsetAsync(m->previous + static_cast<size_t>(state) * phonon::kWidth, 0, phonon::kWidth * 4,
+                             m->stream));
+    CUDA_TRY(cudaStreamSynchronize(m->stream));
+    m->states[state] = PhononCudaMimi::State{true, false, 0};
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_mimi_state_free(PhononCudaMimi* m, uint32_t state) {
+    if (!m || state >= m->max_states) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(m->mu);
+    if (!m->states[state].used) return PHONON_CUDA_INVALID_ARGUMENT;
+    m->states[state] = PhononCudaMimi::State{};
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_mimi_positions(PhononCudaMimi* m, uint32_t state, uint64_t* positions) {
+    if (!m || !positions || state >= m->max_states) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(m->mu);
+    if (!m->states[state].used) return PHONON_CUDA_INVALID_ARGUMENT;
+    *positions = m->states[state].position;
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_mimi_step(PhononCudaMimi* m, uint32_t n, const uint32_t* states, const float* latents,
+                          float* features, int32_t* status) {
+    if (!m) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(m->mu);
+    return mimi_step_locked(m, n, states, latents, features, status);
+}
+
+int phonon_cuda_mimi_process(PhononCudaMimi* m, uint32_t state, const float* latents, size_t frames, float* features,
+                             size_t capacity) {
+    if (!m || !latents || !features || !frames || frames > PHONON_CUDA_MIMI_MAX_FRAMES ||
+        capacity < frames * phonon::kMimiRows)
+        return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(m->mu);
+    if (state >= m->max_states || !m->states[state].used || m->states[state].failed) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (m->states[state].position / phonon::kMimiRows > PHONON_CUDA_MIMI_MAX_FRAMES - frames)
+        return PHONON_CUDA_CAPACITY;
+    for (size_t i = 0; i < frames * 32; ++i)
+        if (!std::isfinite(latents[i])) return PHONON_CUDA_NON_FINITE;
+    for (size_t f = 0; f < frames; ++f) {
+        int32_t st_row = 0;
+        const int st = mimi_step_locked(m, 1, &state, latents + f * 32,
+                                        features + f * phonon::kMimiRows * phonon::kWidth, &st_row);
+        if (st) return st;
+        if (st_row) return st_row;
     }
     return PHONON_CUDA_OK;
 }

@@ -1,0 +1,221 @@
+// The Mimi latent transformer on the device (speech-mac src/phonon_mimi.c:
+// 108-283): every latent frame of a request becomes 16 feature rows of 512
+// through a linear projection (512 x 32), a depthwise transposed-convolution
+// upsample, and two pre-LayerNorm transformer layers whose 16 queries per
+// frame attend causally over at most 250 keys.
+//
+// A step runs one frame of each of B request states at once (16 B rows):
+//
+//   mimi_in_kernel       projection + upsample -> hidden rows, keeps the
+//                        projection as the next frame's `previous`
+//   per layer:
+//     mimi_ln_kernel     LayerNorm 1 (the transformer's LayerNorm, eps 1e-5)
+//     gemv (bf16)        in_proj -> q | k | v
+//     mimi_rope_kv_kernel RoPE of q and k at each row's position; k and v
+//                        of all 16 rows into the state's ring
+//     mimi_attn_kernel   softmax(q k / 8) v over the row's window
+//     gemv EPI_GATE      hidden += layer_scale_1 * out_proj(att)
+//     mimi_ln_kernel     LayerNorm 2
+//     gemv EPI_GELU      erf-GELU(linear1)
+//     gemv EPI_GATE      hidden += layer_scale_2 * linear2(.)
+//
+// The ring: the reference keeps 250 slots and inserts a frame's keys query by
+// query, so that a later row's write never evicts a key an earlier row still
+// reads. Here the 16 rows' keys are written first and then every row attends,
+// so the ring holds kMimiRing = 272 >= 250 + 15 slots: position p lives in
+// slot p % 272, and each query still sees exactly the positions
+// [max(0, p - 249), p] of the reference.
+#pragma once
+
+#include "phonon_kernels.cuh"
+
+namespace phonon {
+
+constexpr int kMimiRows = 16;      // feature rows per latent frame (PHONON_MIMI_STRIDE)
+constexpr int kMimiContext = 250;  // keys a query attends to at most (PHONON_MIMI_CONTEXT)
+constexpr int kMimiRing = 272;     // ring slots per layer
+constexpr int kMimiLayers = 2;
+
+// Ring of one state: [layer][k | v][slot][512] fp32.
+__device__ __forceinline__ float* mimi_ring(float* rings, int slot, int layer, int which) {
+    return rings + ((static_cast<size_t>(slot) * kMimiLayers + layer) * 2 + which) * kMimiRing * kWidth;
+}
+
+// One CTA of 512 threads per state (src/phonon_mimi.c:270-279, :108-131):
+// channel c: projected = W[c] . latent (bias-free linear), then for tap o
+// hidden[o][c] = previous[c] * k[c][16 + o] + projected[c] * k[c][o] (two
+// products, one sum, no contraction), previous[c] = projected.
+__global__ void __launch_bounds__(512) mimi_in_kernel(const float* __restrict__ latents, const int32_t* __restrict__ slots,
+                                                      const uint16_t* __restrict__ proj_w,
+                                                      const uint16_t* __restrict__ up_w, float* __restrict__ previous,
+                                                      float* __restrict__ hidden, int32_t* status) {
+    __shared__ float lat[32];
+    const int b = blockIdx.x, c = threadIdx.x;
+    const uint4* wrow = reinterpret_cast<const uint4*>(proj_w + static_cast<size_t>(c) * 32);
+    const uint4* krow = reinterpret_cast<const uint4*>(up_w + static_cast<size_t>(c) * 32);
+    uint4 wq[4], kq[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        wq[q] = __ldg(wrow + q);
+        kq[q] = __ldg(krow + q);
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (c < 32) lat[c] = latents[static_cast<size_t>(b) * 32 + c];
+    __syncthreads();
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t wd[4] = {wq[q].x, wq[q].y, wq[q].z, wq[q].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            acc = fmaf(__uint_as_float(wd[e] << 16), lat[8 * q + 2 * e], acc);
+            acc = fmaf(__uint_as_float(wd[e] & 0xffff0000u), lat[8 * q + 2 * e + 1], acc);
+        }
+    }
+    float k[32];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t kd[4] = {kq[q].x, kq[q].y, kq[q].z, kq[q].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            k[8 * q + 2 * e] = __uint_as_float(kd[e] << 16);
+            k[8 * q + 2 * e + 1] = __uint_as_float(kd[e] & 0xffff0000u);
+        }
+    }
+    float* prev = previous + static_cast<size_t>(slots[b]) * kWidth + c;
+    const float old_in = *prev;
+    bool ok = isfinite(acc) && isfinite(old_in);
+#pragma unroll
+    for (int o = 0; o < kMimiRows; ++o) {
+        const float v = __fadd_rn(__fmul_rn(old_in, k[kMimiRows + o]), __fmul_rn(acc, k[o]));
+        ok &= isfinite(v);
+        hidden[(static_cast<size_t>(b) * kMimiRows + o) * kWidth + c] = v;
+    }
+    *prev = acc;
+    if (!ok) flag_nonfinite(status, b * kMimiRows);
+}
+
+// LayerNorm of rows (eps 1e-5, the reference's Welford cascade), one warp per
+// row; a non-finite row flags its status word.
+__global__ void __launch_bounds__(256) mimi_ln_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                      const float* __restrict__ b, float* __restrict__ out, int rows,
+                                                      int32_t* status) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+    pdl_wait();
+    pdl_trigger();
+    if (r >= rows) return;
+    if (!warp_layernorm512(x + static_cast<size_t>(r) * kWidth, w, b, out + static_cast<size_t>(r) * kWidth) &&
+        (threadIdx.x & 31) == 0)
+        flag_nonfinite(status, r);
+}
+
+// One CTA of 256 threads per row: RoPE of q and k (interleaved pairs, eight
+// 64-wide heads, the phase of pair i of a head at position p is p * freq[i]
+// in fp32, cos and sin rounded from double; src/phonon_transformer.c:222-251),
+// q rotated in place, k and v of the row written into ring slot p % 272.
+__global__ void __launch_bounds__(256) mimi_rope_kv_kernel(float* __restrict__ qkv, const int32_t* __restrict__ slots,
+                                                           const int32_t* __restrict__ pos0, const float* __restrict__ freq,
+                                                           float* __restrict__ rings, int layer) {
+    const int row = blockIdx.x, t = threadIdx.x;
+    const int b = row / kMimiRows;
+    pdl_wait();
+    pdl_trigger();
+    const int position = pos0[b] + row % kMimiRows;
+    const int ring_slot = position % kMimiRing;
+    float* q = qkv + static_cast<size_t>(row) * 3 * kWidth;
+    float2 cs;
+    {
+        const float phase = __fmul_rn(static_cast<float>(position), freq[t & 31]);
+        double sd, cd;
+        sincos(static_cast<double>(phase), &sd, &cd);
+        cs = make_float2(__double2float_rn(cd), __double2float_rn(sd));
+    }
+    // pair t of q (dims 2t, 2t+1), pair t of k
+    float2 qp = *reinterpret_cast<float2*>(q + 2 * t);
+    float2 kp = *reinterpret_cast<float2*>(q + kWidth + 2 * t);
+    rope_apply(qp.x, qp.y, cs);
+    rope_apply(kp.x, kp.y, cs);
+    *reinterpret_cast<float2*>(q + 2 * t) = qp;
+    const int slot = slots[b];
+    float* kr = mimi_ring(rings, slot, layer, 0) + static_cast<size_t>(ring_slot) * kWidth;
+    float* vr = mimi_ring(rings, slot, layer, 1) + static_cast<size_t>(ring_slot) * kWidth;
+    *reinterpret_cast<float2*>(kr + 2 * t) = kp;
+    *reinterpret_cast<float2*>(vr + 2 * t) = *reinterpret_cast<const float2*>(q + 2 * kWidth + 2 * t);
+}
+
+// One CTA per row, warp h = head h (src/phonon_mimi.c:136-193): scores of the
+// row's query against the keys of positions [first, p] (lane j takes keys j,
+// j + 32, ...; each dot over the head's [even | odd] component order, as the
+// reference's permuted GEMM operands), scale 1/8, max, e^(s - max) and their
+// sum over the warp, then P.V with lane l owning dims 2l, 2l+1, and the
+// output scaled by 1 / sum.
+__global__ void __launch_bounds__(256) mimi_attn_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ slots,
+                                                        const int32_t* __restrict__ pos0, const float* __restrict__ rings,
+                                                        int layer, float* __restrict__ att, int32_t* status) {
+    __shared__ __align__(16) float qs[kHeads][kHeadDim];
+    __shared__ float ps[kHeads][kMimiContext + 2];
+    const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = row / kMimiRows;
+    pdl_wait();
+    pdl_trigger();
+    const int position = pos0[b] + row % kMimiRows;
+    const int count = position < kMimiContext - 1 ? position + 1 : kMimiContext;
+    const int first = position + 1 - count;
+    const float* q = qkv + static_cast<size_t>(row) * 3 * kWidth + warp * kHeadDim;
+    qs[warp][lane] = q[lane];
+    qs[warp][lane + 32] = q[lane + 32];
+    __syncwarp();
+    const float* keys = mimi_ring(const_cast<float*>(rings), slots[b], layer, 0) + warp * kHeadDim;
+    const float* values = mimi_ring(const_cast<float*>(rings), slots[b], layer, 1) + warp * kHeadDim;
+    float mx = -INFINITY;
+    bool ok = true;
+    for (int j = lane; j < count; j += 32) {
+        const float* kr = keys + static_cast<size_t>((first + j) % kMimiRing) * kWidth;
+        float kv[kHeadDim];
+#pragma unroll
+        for (int i = 0; i < kHeadDim / 4; ++i) {
+            const float4 f = *reinterpret_cast<const float4*>(kr + 4 * i);
+            kv[4 * i] = f.x;
+            kv[4 * i + 1] = f.y;
+            kv[4 * i + 2] = f.z;
+            kv[4 * i + 3] = f.w;
+        }
+        float dot = 0.0f;
+#pragma unroll
+        for (int parity = 0; parity < 2; ++parity)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) dot = fmaf(qs[warp][2 * i + parity], kv[2 * i + parity], dot);
+        const float s = __fmul_rn(dot, 0.125f);
+        ok &= isfinite(s);
+        ps[warp][j] = s;
+        mx = fmaxf(mx, s);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    __syncwarp();
+    float total = 0.0f;
+    for (int j = lane; j < count; j += 32) {
+        const float e = expf(__fsub_rn(ps[warp][j], mx));
+        ps[warp][j] = e;
+        total = __fadd_rn(total, e);
+    }
+    total = warp_sum(total);
+    __syncwarp();
+    float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll 4
+    for (int j = 0; j < count; ++j) {
+        const float2 v = *reinterpret_cast<const float2*>(values + static_cast<size_t>((first + j) % kMimiRing) * kWidth +
+                                                          2 * lane);
+        const float p = ps[warp][j];
+        a0 = fmaf(p, v.x, a0);
+        a1 = fmaf(p, v.y, a1);
+    }
+    const float inv = __fdiv_rn(1.0f, total);
+    const float o0 = __fmul_rn(a0, inv), o1 = __fmul_rn(a1, inv);
+    ok &= total > 0.0f && isfinite(total) && isfinite(o0) && isfinite(o1);
+    *reinterpret_cast<float2*>(att + static_cast<size_t>(row) * kWidth + warp * kHeadDim + 2 * lane) = make_float2(o0, o1);
+    if (!__all_sync(kFull, ok) && lane == 0) flag_nonfinite(status, row);
+}
+
+}  // namespace phonon

@@ -52,6 +52,13 @@ class HeadWeights(C.Structure):
                 ("out_norm_w", C.c_void_p), ("out_norm_b", C.c_void_p)]
 
 
+class MimiWeights(C.Structure):
+    _fields_ = [("projection", C.c_void_p), ("upsample", C.c_void_p), ("in_proj", C.c_void_p * 2),
+                ("out_proj", C.c_void_p * 2), ("linear1", C.c_void_p * 2), ("linear2", C.c_void_p * 2),
+                ("norm1_w", C.c_void_p * 2), ("norm1_b", C.c_void_p * 2), ("norm2_w", C.c_void_p * 2),
+                ("norm2_b", C.c_void_p * 2), ("scale1", C.c_void_p * 2), ("scale2", C.c_void_p * 2)]
+
+
 class CudaError(RuntimeError):
     def __init__(self, status, what):
         self.status = status
@@ -105,11 +112,20 @@ def lib():
         "phonon_cuda_eos_logit": [P, U32, P, P],
         "phonon_cuda_output_norm_device": [P, U32, P, P],
         "phonon_cuda_frame_step": [P, U32, P, P, P, P, P, F, P, P, P],
+        "phonon_cuda_mimi_create": [C.c_int, C.POINTER(MimiWeights), U32, U32, C.POINTER(P)],
+        "phonon_cuda_mimi_state_alloc": [P, C.POINTER(U32)],
+        "phonon_cuda_mimi_state_reset": [P, U32],
+        "phonon_cuda_mimi_state_free": [P, U32],
+        "phonon_cuda_mimi_positions": [P, U32, C.POINTER(C.c_uint64)],
+        "phonon_cuda_mimi_step": [P, U32, P, P, P, P],
+        "phonon_cuda_mimi_process": [P, U32, P, SZ, P, SZ],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
         fn.argtypes = args
         fn.restype = C.c_int
+    L.phonon_cuda_mimi_destroy.argtypes = [P]
+    L.phonon_cuda_mimi_destroy.restype = None
     L.phonon_cuda_head_free.argtypes = [P]
     L.phonon_cuda_head_free.restype = None
     L.phonon_cuda_destroy.argtypes = [P]
@@ -497,3 +513,65 @@ class Head:
         check(self.L.phonon_cuda_frame_step(self.h, n, _p(st), _p(po), state_ptr, condition_ptr, _p(raw_noise),
                                             temperature, _p(logit), _p(latent), _p(status)), "frame_step")
         return logit, latent, status
+
+
+class Mimi:
+    """The Mimi latent transformer on a device: model = {"projection": [512][32],
+    "upsample": [512][32], "layers": [{in_proj, out_proj, linear1, linear2,
+    norm1_w, norm1_b, norm2_w, norm2_b, scale1, scale2}] * 2} as bf16 arrays."""
+
+    FIELDS = ("in_proj", "out_proj", "linear1", "linear2", "norm1_w", "norm1_b", "norm2_w", "norm2_b",
+              "scale1", "scale2")
+
+    def __init__(self, model, device=0, max_states=8, max_batch=8):
+        self.L = lib()
+        w = MimiWeights()
+        w.projection = np.ascontiguousarray(model["projection"]).ctypes.data
+        w.upsample = np.ascontiguousarray(model["upsample"]).ctypes.data
+        keep = [model]
+        for i, layer in enumerate(model["layers"]):
+            for f in self.FIELDS:
+                a = np.ascontiguousarray(layer[f])
+                keep.append(a)
+                getattr(w, f)[i] = a.ctypes.data
+        h = C.c_void_p()
+        check(self.L.phonon_cuda_mimi_create(device, C.byref(w), max_states, max_batch, C.byref(h)), "mimi_create")
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.L.phonon_cuda_mimi_destroy(self.h)
+            self.h = None
+
+    def alloc(self):
+        s = C.c_uint32()
+        check(self.L.phonon_cuda_mimi_state_alloc(self.h, C.byref(s)), "mimi_state_alloc")
+        return s.value
+
+    def reset(self, s):
+        check(self.L.phonon_cuda_mimi_state_reset(self.h, s), "mimi_state_reset")
+
+    def free(self, s):
+        check(self.L.phonon_cuda_mimi_state_free(self.h, s), "mimi_state_free")
+
+    def positions(self, s):
+        n = C.c_uint64()
+        check(self.L.phonon_cuda_mimi_positions(self.h, s, C.byref(n)), "mimi_positions")
+        return n.value
+
+    def step(self, states, latents):
+        """One frame per state: latents [n][32] -> (features [n][16][512], status [n])."""
+        n = len(states)
+        st = np.ascontiguousarray(states, np.uint32)
+        latents = np.ascontiguousarray(latents, np.float32).reshape(n, 32)
+        feats = np.zeros((n, 16, WIDTH), np.float32)
+        status = np.zeros(n, np.int32)
+        check(self.L.phonon_cuda_mimi_step(self.h, n, _p(st), _p(latents), _p(feats), _p(status)), "mimi_step")
+        return feats, status
+
+    def process(self, s, latents):
+        latents = np.ascontiguousarray(latents, np.float32).reshape(-1, 32)
+        feats = np.zeros((latents.shape[0] * 16, WIDTH), np.float32)
+        check(self.L.phonon_cuda_mimi_process(self.h, s, _p(latents), latents.shape[0], _p(feats), feats.shape[0]),
+              "mimi_process")
+        return feats

@@ -149,3 +149,29 @@ def frame_tensors(seed=0):
         "embed": np.ascontiguousarray(g.bf16_normal(0.0, 1.0 / np.sqrt(32), 512 * 32).reshape(512, 32)),
         "out_norm": (g.bf16_normal(1.0, 0.05, 512), g.bf16_normal(0.0, 0.05, 512)),
     }
+
+
+def mimi_model(seed=0):
+    """A random Mimi latent transformer (src/phonon_mimi.c:47-82 shapes) as
+    bf16 bits: {"projection": [512][32], "upsample": [512][32], "layers":
+    [{in_proj [1536][512], out_proj [512][512], linear1 [2048][512],
+    linear2 [512][2048], norm1_w/b, norm2_w/b, scale1, scale2 [512]}] * 2}.
+    Weights N(0, 1/cols), gains N(1, 0.1^2), biases N(0, 0.1^2), layer
+    scales N(0.2, 0.05^2)."""
+    g = Generator(seed ^ 0x6d696d69)
+
+    def mat(rows, cols):
+        return np.ascontiguousarray(g.bf16_normal(0.0, 1.0 / np.sqrt(cols), rows * cols).reshape(rows, cols))
+
+    layers = []
+    for _ in range(2):
+        layers.append({
+            "in_proj": mat(1536, 512), "out_proj": mat(512, 512), "linear1": mat(2048, 512),
+            "linear2": mat(512, 2048),
+            "norm1_w": g.bf16_normal(1.0, 0.1, 512), "norm1_b": g.bf16_normal(0.0, 0.1, 512),
+            "norm2_w": g.bf16_normal(1.0, 0.1, 512), "norm2_b": g.bf16_normal(0.0, 0.1, 512),
+            "scale1": g.bf16_normal(0.2, 0.05, 512), "scale2": g.bf16_normal(0.2, 0.05, 512),
+        })
+    return {"projection": mat(512, 32),
+            "upsample": np.ascontiguousarray(g.bf16_normal(0.0, 0.3, 512 * 32).reshape(512, 32)),
+            "layers": layers}
