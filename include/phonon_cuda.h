@@ -102,8 +102,9 @@ uint32_t phonon_cuda_free_pages(PhononCuda *ctx);
  * when status[i] == OK. cancel (optional) is polled before every layer and
  * once after the last one; a nonzero poll resets every stream of the call and
  * returns PHONON_CUDA_CANCELLED without writing y. x in page-locked memory
- * (cudaHostAlloc / cudaHostRegister) is copied to the device directly;
- * other host memory is staged through the context's page-locked buffer. */
+ * (cudaHostAlloc / cudaHostRegister) is copied to the device directly, and so
+ * are the rows of y (for the streams that succeeded) when y is page-locked;
+ * other host memory is staged through the context's page-locked buffers. */
 int phonon_cuda_step(PhononCuda *ctx, uint32_t n, const uint32_t *streams,
                      const uint32_t *positions, const float *x, float *y, int32_t *status,
                      PhononCudaCancelPoll cancel, void *cancel_context);

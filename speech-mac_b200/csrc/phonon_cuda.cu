@@ -1969,7 +1969,11 @@ int phonon_cuda_step(PhononCuda* c, uint32_t n, const uint32_t* streams, const u
     bool cancelled = false;
     st = enqueue_decode(c, slot, pos, updates, c->d_x0, c->d_y, cancel, cctx, &cancelled);
     if (st && st != PHONON_CUDA_CANCELLED && !cancelled) undo.rollback();
-    if (st == PHONON_CUDA_OK)
+    // Page-locked y: read the status words first, then DMA the rows of the
+    // streams that succeeded straight into y (runs of consecutive rows), so
+    // no host copy of the outputs is made. Other y: through the staging rows.
+    const bool direct_y = is_pinned_host(y);
+    if (st == PHONON_CUDA_OK && !direct_y)
         cudaMemcpyAsync(c->h_y, c->d_y, static_cast<size_t>(n) * kWidth * 4, cudaMemcpyDeviceToHost, c->stream);
     const int sync = finish_sync(c, n);
     if (cancelled) {
@@ -1978,12 +1982,26 @@ int phonon_cuda_step(PhononCuda* c, uint32_t n, const uint32_t* streams, const u
     }
     if (st) return st;
     if (sync) return sync;
-    for (uint32_t i = 0; i < n; ++i) {
-        status[i] = c->h_status[i] ? c->h_status[i] : PHONON_CUDA_OK;
-        if (status[i] == PHONON_CUDA_OK) {
-            c->streams[streams[i]].length++;
-            std::memcpy(y + static_cast<size_t>(i) * kWidth, c->h_y + static_cast<size_t>(i) * kWidth, kWidth * 4);
+    for (uint32_t i = 0; i < n; ++i) status[i] = c->h_status[i] ? c->h_status[i] : PHONON_CUDA_OK;
+    if (direct_y) {
+        for (uint32_t i = 0; i < n;) {
+            if (status[i] != PHONON_CUDA_OK) {
+                ++i;
+                continue;
+            }
+            uint32_t j = i;
+            while (j < n && status[j] == PHONON_CUDA_OK) ++j;
+            CUDA_TRY(cudaMemcpyAsync(y + static_cast<size_t>(i) * kWidth, c->d_y + static_cast<size_t>(i) * kWidth,
+                                     static_cast<size_t>(j - i) * kWidth * 4, cudaMemcpyDeviceToHost, c->stream));
+            i = j;
         }
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+    }
+    for (uint32_t i = 0; i < n; ++i) {
+        if (status[i] != PHONON_CUDA_OK) continue;
+        c->streams[streams[i]].length++;
+        if (!direct_y)
+            std::memcpy(y + static_cast<size_t>(i) * kWidth, c->h_y + static_cast<size_t>(i) * kWidth, kWidth * 4);
     }
     return PHONON_CUDA_OK;
 }
