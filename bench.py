@@ -404,6 +404,11 @@ def run_ours(args):
         extras["prefill"] = bench_prefill(rt, synth, weights, torch)
         lens3 = [int(x) for x in np.random.default_rng(2).integers(64, 2049, 512)]
         extras["mimi"] = bench_mimi(rt, synth, torch)
+        # configs[3]'s streams with per-block-scale Q8_0 (real packs' layout): the three-plane tensor-core path
+        lens3b = [int(x) for x in np.random.default_rng(2).integers(64, 2049, 512)]
+        extras["per_block_scales"] = {
+            "workload": "configs[3] streams (512, U[64,2048] seed 2, bf16 K/V, no churn), per-block fp16 scales",
+            **decode_run(rt, synth.per_block_scales(weights, 5), torch, lens3b, 20, rt.KV_BF16)}
         extras["frame_loop"] = {
             "configs3": bench_frame_loop(rt, synth, weights, torch, lens3, rt.KV_BF16, 10),
             "configs0": bench_frame_loop(rt, synth, weights, torch, [128], rt.KV_F32, 100),

@@ -81,9 +81,13 @@ struct DevLinear {
     void* plane = nullptr;
     __half* scales = nullptr;
     size_t bytes = 0;
-    // Tensor-core copy: Q8_0 whose 32-blocks share one scale per row.
+    // Tensor-core copy of a Q8_0 linear: one natural row-major int8 plane
+    // [rows][cols] when every 32-block of a row shares one scale (wd = 1),
+    // else three weight digit planes [3][rows][cols] of the per-block-scaled
+    // integers (wd = 3, phonon_gemm.cuh), and the fp32 row scales.
     bool tensor = false;
-    int8_t* nat = nullptr;       // natural row-major int8 [rows][cols]
+    int wd = 1;
+    int8_t* nat = nullptr;       // [wd * rows][cols]
     float* row_scale = nullptr;  // [rows]
     CUtensorMap tmap;            // 128-byte x 128-row SWIZZLE_128B boxes over `nat`
 };
@@ -217,6 +221,50 @@ int upload_linear(int kind, const void* host, size_t rows, size_t cols, DevLinea
                 return PHONON_CUDA_DEVICE_ERROR;
             }
             l.tensor = make_i8_map(&l.tmap, l.nat, rows, cols);
+        } else if (cols % kGemmKTile == 0 && rows % kGemmM == 0) {
+            // Per-block scales: three weight digit planes (phonon_gemm.cuh).
+            std::vector<int8_t> planes(3 * n);
+            rs.assign(rows, 1.0f);
+            for (size_t r = 0; r < rows; ++r) {
+                const uint8_t* row = blocks + r * (cols / 32) * 34;
+                int emax = INT32_MIN;
+                for (size_t b = 0; b < cols / 32; ++b) {
+                    const uint16_t h = static_cast<uint16_t>(row[b * 34] | (row[b * 34 + 1] << 8));
+                    const int e5 = (h >> 10) & 0x1f, m = (e5 ? 1024 : 0) + (h & 0x3ff);
+                    if (m) emax = std::max(emax, (e5 ? e5 : 1) - 25);
+                }
+                if (emax == INT32_MIN) continue;  // an all-zero row: zero planes
+                rs[r] = std::ldexp(1.0f, emax - 2);
+                for (size_t b = 0; b < cols / 32; ++b) {
+                    const uint16_t h = static_cast<uint16_t>(row[b * 34] | (row[b * 34 + 1] << 8));
+                    const int e5 = (h >> 10) & 0x1f, m = (e5 ? 1024 : 0) + (h & 0x3ff);
+                    const int sign = (h & 0x8000) ? -1 : 1;
+                    const int shift = (e5 ? e5 : 1) - 25 - emax + 2;  // <= 2
+                    for (size_t i = 0; i < 32; ++i) {
+                        const long long qm = static_cast<long long>(static_cast<int8_t>(row[b * 34 + 2 + i])) * m * sign;
+                        const long long W = shift >= 0 ? qm << shift : std::llround(std::ldexp(static_cast<double>(qm), shift));
+                        const long long w2 = ((W + 64) % 128 + 128) % 128 - 64;
+                        const long long W1 = (W - w2) / 128;
+                        const long long w1 = ((W1 + 64) % 128 + 128) % 128 - 64;
+                        const long long w0 = (W1 - w1) / 128;
+                        const size_t at = r * cols + b * 32 + i;
+                        planes[at] = static_cast<int8_t>(w0);
+                        planes[n + at] = static_cast<int8_t>(w1);
+                        planes[2 * n + at] = static_cast<int8_t>(w2);
+                    }
+                }
+            }
+            if (cudaMalloc(&l.nat, 3 * n) != cudaSuccess || cudaMalloc(&l.row_scale, rows * 4) != cudaSuccess) {
+                free_linear(l);
+                return PHONON_CUDA_OUT_OF_MEMORY;
+            }
+            if (cudaMemcpy(l.nat, planes.data(), 3 * n, cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemcpy(l.row_scale, rs.data(), rows * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+                free_linear(l);
+                return PHONON_CUDA_DEVICE_ERROR;
+            }
+            l.wd = 3;
+            l.tensor = make_i8_map(&l.tmap, l.nat, 3 * rows, cols);
         }
         if (cudaMemcpy(l.plane, q.data(), n, cudaMemcpyHostToDevice) != cudaSuccess ||
             cudaMemcpy(l.scales, s.data(), s.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
@@ -260,12 +308,6 @@ cudaError_t opt_in_smem(const void* kern, int smem, std::atomic<uint64_t>& confi
         configured.fetch_or(bit, std::memory_order_release);
     }
     return cudaSuccess;
-}
-
-template <int kEpi>
-std::atomic<uint64_t>& gemm_configured() {
-    static std::atomic<uint64_t> configured{0};
-    return configured;
 }
 
 template <bool kQ8, int kChunks, int kBT, int kSrc, int kEpi>
@@ -337,13 +379,23 @@ cudaError_t launch_linear(const DevLinear& l, const float* x, int B, const float
     return cudaGetLastError();
 }
 
-template <int kEpi>
+template <int kEpi, int kWD = 1>
 cudaError_t launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, int rows, int n_digit_rows, const GemmParams& p,
                         cudaStream_t s) {
-    cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(i8_gemm_kernel<kEpi>), kGemmSmem, gemm_configured<kEpi>());
+    static std::atomic<uint64_t> configured{0};
+    constexpr int smem = gemm_smem(kWD);
+    cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(i8_gemm_kernel<kEpi, kWD>), smem, configured);
     if (e != cudaSuccess) return e;
     dim3 grid((rows + kGemmM - 1) / kGemmM, (n_digit_rows + kGemmN - 1) / kGemmN);
-    return launch_pdl(i8_gemm_kernel<kEpi>, grid, dim3(kGemmThreads), kGemmSmem, s, tw, tx, p);
+    return launch_pdl(i8_gemm_kernel<kEpi, kWD>, grid, dim3(kGemmThreads), smem, s, tw, tx, p);
+}
+
+// A projection of a linear on the tensor cores: one or three weight planes.
+template <int kEpi>
+cudaError_t launch_linear_gemm(const DevLinear& w, const CUtensorMap& tx, int n_digit_rows, const GemmParams& p,
+                               cudaStream_t s) {
+    return w.wd == 3 ? launch_gemm<kEpi, 3>(w.tmap, tx, w.rows, n_digit_rows, p, s)
+                     : launch_gemm<kEpi, 1>(w.tmap, tx, w.rows, n_digit_rows, p, s);
 }
 
 template <bool kBf16>
@@ -947,7 +999,7 @@ int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, 
     g.layer = l;
     {
         LaunchScope ls(c, PHONON_CUDA_K_QKV, 1536.0 * 512 + dig * 512 + act * kWidth + B * 2.0 * kWidth * esize, b.lane->stream);
-        CUDA_TRY(launch_gemm<GEPI_QKV>(L.qkv.tmap, b.lane->tm_dig512, 1536, nd, g, s));
+        CUDA_TRY(launch_linear_gemm<GEPI_QKV>(L.qkv, b.lane->tm_dig512, nd, g, s));
     }
     // 2. attention; the combine writes the digit rows of the attention output
     int st = enqueue_attention(c, b, l, true);
@@ -963,7 +1015,7 @@ int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, 
     go.ldy = kWidth;
     {
         LaunchScope ls(c, PHONON_CUDA_K_OUT, 512.0 * 512 + dig * 512 + act * 2 * kWidth, b.lane->stream);
-        CUDA_TRY(launch_gemm<GEPI_RESID>(L.out.tmap, b.lane->tm_dig512, 512, nd, go, s));
+        CUDA_TRY(launch_linear_gemm<GEPI_RESID>(L.out, b.lane->tm_dig512, nd, go, s));
     }
     // 4. g = GELU(LN2(h) Wup^T)
     {
@@ -979,7 +1031,7 @@ int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, 
     gu.ldy = kFfn;
     {
         LaunchScope ls(c, PHONON_CUDA_K_UP, 2048.0 * 512 + dig * 512 + act * kFfn, b.lane->stream);
-        CUDA_TRY(launch_gemm<GEPI_GELU>(L.up.tmap, b.lane->tm_dig512, kFfn, nd, gu, s));
+        CUDA_TRY(launch_linear_gemm<GEPI_GELU>(L.up, b.lane->tm_dig512, nd, gu, s));
     }
     // 5. out = h + g Wdown^T
     {
@@ -997,7 +1049,7 @@ int enqueue_layer_tensor(PhononCuda* c, const Batch& b, int l, const float* in, 
     gd.ldy = kWidth;
     {
         LaunchScope ls(c, PHONON_CUDA_K_DOWN, 512.0 * 2048 + dig * 2048 + act * 2 * kWidth, b.lane->stream);
-        CUDA_TRY(launch_gemm<GEPI_RESID>(L.down.tmap, b.lane->tm_dig2048, 512, nd, gd, s));
+        CUDA_TRY(launch_linear_gemm<GEPI_RESID>(L.down, b.lane->tm_dig2048, nd, gd, s));
     }
     return PHONON_CUDA_OK;
 }
@@ -2498,7 +2550,7 @@ int phonon_cuda_linear_apply_device_noalloc(PhononCudaLinear* l, const float* x_
         return PHONON_CUDA_CAPACITY;
     }
     const DevLinear& w = l->lin;
-    if (!w.tensor || (w.cols != 512 && w.cols != 2048)) return PHONON_CUDA_INVALID_ARGUMENT;
+    if (!w.tensor || w.wd != 1 || (w.cols != 512 && w.cols != 2048)) return PHONON_CUDA_INVALID_ARGUMENT;
     int st = set_device(l->device);
     if (st) return st;
     NoallocScratch* sc = nullptr;

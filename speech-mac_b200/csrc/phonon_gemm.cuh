@@ -11,6 +11,19 @@
 // (|D| <= 2048 * 64 * 127 < 2^24, so it is also exact in fp32), and the
 // epilogue recombines y = s_r * sum_j D[r][4b+j] * 2^(e_b - 7(j+1)).
 //
+// Per-block-scale Q8_0 (one fp16 scale per 32 weights, as real packs carry):
+// with d_b = M_b 2^E_b (M_b the 11-bit integer significand) and E the row's
+// largest E_b, the weights become integers W = q M_b 2^(E_b - E + 2) (exact
+// for blocks within a factor 4 of the row's largest scale exponent, rounded
+// to the nearest integer below that: an error below 2^-21 of the row's
+// largest weight), |W| < 2^20, and the row scale is 2^(E - 2). W is split into
+// three balanced base-128 digit planes w_0..w_2 (W = w_0 2^14 + w_1 2^7 + w_2,
+// |w_i| <= 64), stacked as rows [i * rows, (i + 1) * rows) of operand A; the
+// CTA runs one MMA chain per plane into its own 128 accumulator columns
+// (kWD = 3, 512 TMEM columns), and the epilogue forms
+// T_j = D_0j 2^14 + D_1j 2^7 + D_2j exactly in 64-bit integers before the
+// recombination with the activation digits.
+//
 // Kernel shape: one CTA per 128-row x 32-stream tile (M = 128, N = 128 digit
 // rows), 10 warps: warp 0 issues TMA tile loads (no multicast), warp 1 owns
 // the TMEM accumulator and issues tcgen05.mma, warps 2-9 drain TMEM in the
@@ -42,7 +55,11 @@ struct GemmTileMeta {
     int32_t page[kGemmN / 4];
     float2 cs[kGemmN / 4][32];
 };
-constexpr int kGemmSmem = 1024 + kGemmStages * (kGemmM + kGemmN) * kGemmKTile + 256 + static_cast<int>(sizeof(GemmTileMeta));
+// Shared memory of a launch with kWD weight digit planes per tile (see below).
+__host__ __device__ constexpr int gemm_smem(int wd) {
+    return 1024 + kGemmStages * (wd * kGemmM + kGemmN) * kGemmKTile + 256 + static_cast<int>(sizeof(GemmTileMeta));
+}
+constexpr int kGemmSmem = gemm_smem(1);
 constexpr long long kWaitBudgetCycles = 4ll << 30;  // ~2 s at 1.9 GHz
 
 enum GemmEpilogue : int { GEPI_RAW = 0, GEPI_RESID = 1, GEPI_GELU = 2, GEPI_QKV = 3, GEPI_STORE = 4 };
@@ -215,18 +232,22 @@ __device__ __forceinline__ float pow2f(int e) {  // exact 2^e for normal exponen
     return __int_as_float((127 + e) << 23);
 }
 
-template <int kEpi>
-__global__ void __launch_bounds__(kGemmThreads, 2)
+template <int kEpi, int kWD = 1>
+__global__ void __launch_bounds__(kGemmThreads, kWD == 1 ? 2 : 1)
     i8_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    GemmParams p) {
+    static_assert(kWD == 1 || kWD == 3, "one or three weight digit planes");
+    constexpr int kStageA = kWD * kGemmM * kGemmKTile;            // bytes of the A planes of one stage
+    constexpr uint32_t kTmemCols = kWD == 1 ? kGemmN : 512;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sA = smem;                                           // [stages][128 rows][128 B]
-    uint8_t* sB = smem + kGemmStages * kGemmM * kGemmKTile;       // [stages][128 rows][128 B]
+    uint8_t* sA = smem;                                           // [stages][kWD planes][128 rows][128 B]
+    uint8_t* sB = smem + kGemmStages * kStageA;                   // [stages][128 rows][128 B]
     uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kGemmStages * kGemmN * kGemmKTile);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kGemmStages + 1);
     volatile int* failed = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    GemmTileMeta* meta = reinterpret_cast<GemmTileMeta*>(smem + kGemmStages * (kGemmM + kGemmN) * kGemmKTile + 256);
+    GemmTileMeta* meta =
+        reinterpret_cast<GemmTileMeta*>(smem + kGemmStages * (kStageA + kGemmN * kGemmKTile) + 256);
     const uint32_t full0 = smem_addr(bars), empty0 = full0 + 8 * kGemmStages, accum = full0 + 16 * kGemmStages;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -244,7 +265,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
-                     "r"(kGemmN)
+                     "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -257,11 +278,13 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
         // TMA producer: weight tile rows [m_tile*128, +128), digit rows [n_tile*128, +128).
         // Weight tiles of the first stages do not depend on the previous
         // kernel: issue them before waiting for it.
+        // Plane i of the weights is rows [i * p.rows, (i + 1) * p.rows) of tm_w.
         const int pre = nk < kGemmStages ? nk : kGemmStages;
         for (int kt = 0; kt < pre; ++kt) {
-            mbar_expect_tx(full0 + 8 * kt, (kGemmM + kGemmN) * kGemmKTile);
-            tma_load_2d(smem_addr(sA + kt * kGemmM * kGemmKTile), &tm_w, kt * kGemmKTile, m_tile * kGemmM,
-                        full0 + 8 * kt);
+            mbar_expect_tx(full0 + 8 * kt, kStageA + kGemmN * kGemmKTile);
+            for (int i = 0; i < kWD; ++i)
+                tma_load_2d(smem_addr(sA + kt * kStageA + i * kGemmM * kGemmKTile), &tm_w, kt * kGemmKTile,
+                            i * p.rows + m_tile * kGemmM, full0 + 8 * kt);
         }
         pdl_wait();
         GEMM_MARK(1);  // previous launch complete
@@ -269,9 +292,10 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
             const int s = kt % kGemmStages;
             if (kt >= pre) {
                 if (!mbar_wait(empty0 + 8 * s, ((kt / kGemmStages) - 1) & 1, p.error, failed)) break;
-                mbar_expect_tx(full0 + 8 * s, (kGemmM + kGemmN) * kGemmKTile);
-                tma_load_2d(smem_addr(sA + s * kGemmM * kGemmKTile), &tm_w, kt * kGemmKTile, m_tile * kGemmM,
-                            full0 + 8 * s);
+                mbar_expect_tx(full0 + 8 * s, kStageA + kGemmN * kGemmKTile);
+                for (int i = 0; i < kWD; ++i)
+                    tma_load_2d(smem_addr(sA + s * kStageA + i * kGemmM * kGemmKTile), &tm_w, kt * kGemmKTile,
+                                i * p.rows + m_tile * kGemmM, full0 + 8 * s);
             }
             tma_load_2d(smem_addr(sB + s * kGemmN * kGemmKTile), &tm_x, kt * kGemmKTile, n_tile * kGemmN,
                         full0 + 8 * s);
@@ -288,12 +312,14 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
             }
             if (kt == 0) GEMM_MARK(2);  // first stage landed
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t a0 = smem_addr(sA + s * kGemmM * kGemmKTile);
+            const uint32_t a0 = smem_addr(sA + s * kStageA);
             const uint32_t b0 = smem_addr(sB + s * kGemmN * kGemmKTile);
 #pragma unroll
-            for (int kk = 0; kk < kGemmKTile / 32; ++kk)
-                umma_i8(tmem, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
-                        (kt | kk) != 0);
+            for (int i = 0; i < kWD; ++i)
+#pragma unroll
+                for (int kk = 0; kk < kGemmKTile / 32; ++kk)
+                    umma_i8(tmem + i * kGemmN, umma_desc_sw128(a0 + i * kGemmM * kGemmKTile + kk * 32),
+                            umma_desc_sw128(b0 + kk * 32), idesc, (kt | kk) != 0);
             umma_commit(empty0 + 8 * s);
         }
         if (ok) umma_commit(accum);
@@ -360,6 +386,11 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
                 const int c0 = half * (kGemmN / 2) + h * 32;
                 uint32_t d[32];
                 tmem_load32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c0, d);
+                uint32_t d1[kWD == 3 ? 32 : 1], d2[kWD == 3 ? 32 : 1];
+                if constexpr (kWD == 3) {
+                    tmem_load32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + kGemmN + c0, d1);
+                    tmem_load32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + 2 * kGemmN + c0, d2);
+                }
                 if constexpr (kEpi == GEPI_RAW) {
                     if (r < p.rows)
                         for (int i = 0; i < 32; ++i) {
@@ -376,8 +407,18 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
                         const int e = meta->exp[(c0 >> 2) + t];
                         float acc = 0.0f;
 #pragma unroll
-                        for (int j = 0; j < kDigits; ++j)
-                            acc = fmaf(static_cast<float>(static_cast<int32_t>(d[4 * t + j])), pow2f(e - 7 * (j + 1)), acc);
+                        for (int j = 0; j < kDigits; ++j) {
+                            float dj;
+                            if constexpr (kWD == 3) {
+                                const long long T = (static_cast<long long>(static_cast<int32_t>(d[4 * t + j])) << 14) +
+                                                    (static_cast<long long>(static_cast<int32_t>(d1[4 * t + j])) << 7) +
+                                                    static_cast<long long>(static_cast<int32_t>(d2[4 * t + j]));
+                                dj = __ll2float_rn(T);
+                            } else {
+                                dj = static_cast<float>(static_cast<int32_t>(d[4 * t + j]));
+                            }
+                            acc = fmaf(dj, pow2f(e - 7 * (j + 1)), acc);
+                        }
                         v[t] = acc * scale;
                     }
                     if constexpr (kEpi == GEPI_QKV) {
@@ -437,7 +478,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
     }
     if (threadIdx.x == 0) GEMM_MARK(7);  // CTA end
 }

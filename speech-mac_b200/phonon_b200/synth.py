@@ -175,3 +175,23 @@ def mimi_model(seed=0):
     return {"projection": mat(512, 32),
             "upsample": np.ascontiguousarray(g.bf16_normal(0.0, 0.3, 512 * 32).reshape(512, 32)),
             "layers": layers}
+
+
+def per_block_scales(weights, seed):
+    """Copies of Q8_0 layers (flow_weights) whose 32-blocks carry their own
+    fp16 scales, as real packs do: each block's scale is the linear's scale
+    times U(0.1, 1) (up to 10x apart within a row), and eight blocks per
+    linear are zero."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for w in weights:
+        w2 = dict(w)
+        for k in ("qkv", "out", "up", "down"):
+            blob = w[k].copy().reshape(-1, 34)
+            base = blob[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+            scale = (base * rng.uniform(0.1, 1.0, blob.shape[0])).astype(np.float16)
+            scale[rng.integers(0, blob.shape[0], 8)] = 0.0
+            blob[:, 0:2] = scale.view(np.uint8).reshape(-1, 2)
+            w2[k] = np.ascontiguousarray(blob.reshape(-1))
+        out.append(w2)
+    return out

@@ -79,3 +79,51 @@ def test_tensor_path_vs_oracle(ctx12t, oracle, weights12):
         om.free_stream(c)
     print(f"tensor path vs oracle, 40 streams x 20 steps: max rel err {worst:.2e}")
     assert worst < 1e-3, worst
+
+
+def test_per_block_scales_on_the_tensor_cores(cuda_ok, oracle, weights12):
+    """Per-block-scale Q8_0 linears take the three-digit-plane tcgen05 path
+    (a batch of 40 streams): every layer teacher-forced against the oracle,
+    which applies each block's scale itself, within the per-layer bound; and
+    the step against the CUDA-core GEMV path of the same weights."""
+    import parity
+    weights = synth.per_block_scales(weights12, 5)
+    n = 40
+    ctx = rt.Context(weights, max_streams=n + 4, max_batch=n, pool_pages=1024, kv_type=rt.KV_F32)
+    gemv = rt.Context(weights, max_streams=n + 4, max_batch=n, pool_pages=1024, kv_type=rt.KV_F32)
+    gemv.set_batch_paths(rt.FUSED_MAX_BATCH + 1, rt.FUSED_MAX_BATCH, 1 << 20)
+    trace = parity.Trace(ctx, n)
+    try:
+        lens = [20 + 7 * i for i in range(n)]
+        ss = [ctx.stream_alloc(600) for _ in range(n)]
+        sg = [gemv.stream_alloc(600) for _ in range(n)]
+        for i in range(n):
+            ctx.fill_synthetic(ss[i], lens[i], 300 + i)
+            gemv.fill_synthetic(sg[i], lens[i], 300 + i)
+        g = synth.Generator(17)
+        xs, traces, worst_gemv = [], [], 0.0
+        for t in range(2):
+            x = g.normal(n * 512).reshape(n, 512)
+            pos = [ln + t for ln in lens]
+            l0 = ctx.launch_count()
+            y = ctx.step(ss, pos, x)
+            launches = ctx.launch_count() - l0
+            traces.append(trace.read(n))
+            xs.append(x)
+            l0 = gemv.launch_count()
+            yg = gemv.step(sg, pos, x)
+            # the tensor path runs nine launches per layer (digit slicing + GEMMs), the GEMV path fewer
+            assert launches > gemv.launch_count() - l0, (launches, gemv.launch_count() - l0)
+            worst_gemv = max(worst_gemv, rt.rel_err(y, yg))
+        om = oracle.model(weights)
+        stats = parity.Stats()
+        for i in (0, 13, 27, 39):
+            parity.check_stream_oracle(ctx, om, ss[i], [lens[i], lens[i] + 1], [x[i] for x in xs], traces, i, stats,
+                                       kv_bf16=False, label=f"stream {i}")
+        print(f"per-block scales, tensor path: {stats}; vs GEMV path {worst_gemv:.2e}")
+        assert stats.rel < parity.PER_LAYER_TOL, str(stats)
+        assert worst_gemv < 1e-3
+    finally:
+        trace.close()
+        ctx.close()
+        gemv.close()
