@@ -417,6 +417,10 @@ int phonon_cuda_mimi_positions(PhononCudaMimi *mimi, uint32_t state, uint64_t *p
  * A non-finite latent rejects the whole call before any work. */
 int phonon_cuda_mimi_step(PhononCudaMimi *mimi, uint32_t n, const uint32_t *states, const float *latents,
                           float *features, int32_t *status);
+/* Steps of at least min_states states (default 4) run the four linears on
+ * the tensor cores (bf16 weights times three bf16 slices of the fp32
+ * activations); *available: 1 when that path could be set up. */
+int phonon_cuda_mimi_set_tensor_min(PhononCudaMimi *mimi, uint32_t min_states, int *available);
 /* phonon_mimi_process for one state: frames latents [frames][32] ->
  * features [frames * 16][512], capacity in feature rows. */
 int phonon_cuda_mimi_process(PhononCudaMimi *mimi, uint32_t state, const float *latents, size_t frames,

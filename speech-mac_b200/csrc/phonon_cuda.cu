@@ -3053,18 +3053,26 @@ int head_alloc(PhononCudaHead* h, uint32_t cap) {
     return PHONON_CUDA_OK;
 }
 
-template <int kEpi>
-cudaError_t launch_head_gemm(PhononCudaHead* h, const CUtensorMap& tw, const CUtensorMap& tx, int rows, int B,
-                             HeadGemmParams p) {
+// A bf16 x three-slice linear (head_gemm_kernel) of `rows` outputs for B
+// activation rows, on stream s; status and error words in p.
+template <int kEpi, int kK = kHgK>
+cudaError_t launch_bf16x3_gemm(const CUtensorMap& tw, const CUtensorMap& tx, int rows, int B, HeadGemmParams p,
+                               cudaStream_t s) {
     static std::atomic<uint64_t> configured{0};
-    const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(head_gemm_kernel<kEpi>), kHgSmem, configured);
+    const cudaError_t e = opt_in_smem(reinterpret_cast<const void*>(head_gemm_kernel<kEpi, kK>), kHgSmem, configured);
     if (e != cudaSuccess) return e;
     p.rows = rows;
     p.B = B;
+    const dim3 grid((rows + kHgM - 1) / kHgM, (B + kHgStreams - 1) / kHgStreams);
+    return launch_pdl(head_gemm_kernel<kEpi, kK>, grid, dim3(kHgThreads), kHgSmem, s, tw, tx, p);
+}
+
+template <int kEpi>
+cudaError_t launch_head_gemm(PhononCudaHead* h, const CUtensorMap& tw, const CUtensorMap& tx, int rows, int B,
+                             HeadGemmParams p) {
     p.status = h->d_status;
     p.error = h->c->d_err;
-    const dim3 grid((rows + kHgM - 1) / kHgM, (B + kHgStreams - 1) / kHgStreams);
-    return launch_pdl(head_gemm_kernel<kEpi>, grid, dim3(kHgThreads), kHgSmem, h->c->stream, tw, tx, p);
+    return launch_bf16x3_gemm<kEpi>(tw, tx, rows, B, p, h->c->stream);
 }
 
 bool head_tensor(const PhononCudaHead* h, int B) {
@@ -3181,6 +3189,7 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
             HeadGemmParams g{};
             g.bias = h->mlp_b + (2 * blk) * kWidth;
             g.slices = h->sl_f;
+            g.slice_ld = kWidth;
             {
                 LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kWidth * 2.0 + B * 12.0 * kWidth);
                 CUDA_TRY(launch_head_gemm<HG_SILU>(h, h->tm_mlp[blk][0], h->tm_sl_h, kWidth, B, g));
@@ -3465,6 +3474,14 @@ struct PhononCudaMimi {
     int32_t *d_meta = nullptr, *d_status = nullptr;  // meta: slots [max_batch], positions [max_batch]
     float *h_lat = nullptr, *h_out = nullptr;
     int32_t *h_meta = nullptr, *h_status = nullptr;
+    // tensor-core linears (head_gemm_kernel) for steps of at least tensor_min states
+    uint16_t* wn = nullptr;                       // natural bf16 copies of the eight matrices
+    CUtensorMap tm_w[phonon::kMimiLayers][4];     // in_proj, out_proj, linear1, linear2
+    uint16_t *sl_a = nullptr, *sl_g = nullptr;    // slice rows [3 * rows_pad][512], [3 * rows_pad][2048]
+    CUtensorMap tm_sl_a, tm_sl_g;
+    int32_t* d_err = nullptr;                     // bounded-wait expiry of the tensor-core linears
+    bool tensor_ok = false;
+    uint32_t tensor_min = 4;
     struct State {
         bool used = false, failed = false;
         uint64_t position = 0;
@@ -3483,6 +3500,9 @@ void mimi_release(PhononCudaMimi* m) {
         free_linear(m->linear1[l]);
         free_linear(m->linear2[l]);
     }
+    for (void* p : {static_cast<void*>(m->wn), static_cast<void*>(m->sl_a), static_cast<void*>(m->sl_g),
+                    static_cast<void*>(m->d_err)})
+        if (p) cudaFree(p);
     for (void* p : {static_cast<void*>(m->w16), static_cast<void*>(m->vec), static_cast<void*>(m->rings),
                     static_cast<void*>(m->previous), static_cast<void*>(m->d_lat), static_cast<void*>(m->d_hidden),
                     static_cast<void*>(m->d_norm), static_cast<void*>(m->d_qkv), static_cast<void*>(m->d_att),
@@ -3498,14 +3518,14 @@ int mimi_setup(PhononCudaMimi* m, const PhononCudaMimiWeights& w) {
     using namespace phonon;
     constexpr size_t W = kWidth;
     // vectors
-    std::vector<float> v(kMimiLayers * kMimiVecPerLayer * W + W + 32, 0.0f);
+    std::vector<float> v(kMimiLayers * kMimiVecPerLayer * W + kFfn + 32, 0.0f);  // vectors, zeros [2048], freq [32]
     for (int l = 0; l < kMimiLayers; ++l) {
         const uint16_t* src[kMimiVecPerLayer] = {w.norm1_w[l], w.norm1_b[l], w.norm2_w[l],
                                                  w.norm2_b[l], w.scale1[l],  w.scale2[l]};
         for (int k = 0; k < kMimiVecPerLayer; ++k)
             if (!head_vec(src[k], W, &v[(l * kMimiVecPerLayer + k) * W])) return PHONON_CUDA_NON_FINITE;
     }
-    rope_frequencies(10000.0f, kHeadDim, &v[kMimiLayers * kMimiVecPerLayer * W + W]);
+    rope_frequencies(10000.0f, kHeadDim, &v[kMimiLayers * kMimiVecPerLayer * W + kFfn]);
     // natural bf16 projection and upsample kernel
     if (!head_mat(w.projection, W * 32) || !head_mat(w.upsample, W * 32)) return PHONON_CUDA_NON_FINITE;
     CUDA_TRY(cudaMalloc(&m->w16, 2 * W * 32 * 2));
@@ -3539,6 +3559,32 @@ int mimi_setup(PhononCudaMimi* m, const PhononCudaMimiWeights& w) {
     CUDA_TRY(cudaMemset(m->previous, 0, S * W * 4));
     CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     m->states.assign(S, PhononCudaMimi::State{});
+    // tensor-core copies: natural bf16 rows in 128-row TMA boxes, slice rows in 96-row boxes
+    const size_t mats = static_cast<size_t>(kMimiLayers) * (3 * W * W + W * W + kFfn * W + W * kFfn);
+    const size_t rows_pad = (rows + kHgStreams - 1) / kHgStreams * kHgStreams;
+    if (cudaMalloc(&m->wn, mats * 2) != cudaSuccess || cudaMalloc(&m->sl_a, 3 * rows_pad * W * 2) != cudaSuccess ||
+        cudaMalloc(&m->sl_g, 3 * rows_pad * kFfn * 2) != cudaSuccess || cudaMalloc(&m->d_err, 4) != cudaSuccess)
+        return PHONON_CUDA_OUT_OF_MEMORY;
+    CUDA_TRY(cudaMemset(m->d_err, 0, 4));
+    CUDA_TRY(cudaMemset(m->sl_a, 0, 3 * rows_pad * W * 2));
+    CUDA_TRY(cudaMemset(m->sl_g, 0, 3 * rows_pad * kFfn * 2));
+    bool maps = true;
+    uint16_t* at = m->wn;
+    for (int l = 0; l < kMimiLayers; ++l) {
+        const uint16_t* src[4] = {w.in_proj[l], w.out_proj[l], w.linear1[l], w.linear2[l]};
+        const size_t rws[4] = {3 * W, W, static_cast<size_t>(kFfn), W}, cls[4] = {W, W, W, static_cast<size_t>(kFfn)};
+        for (int k = 0; k < 4; ++k) {
+            CUDA_TRY(cudaMemcpy(at, src[k], rws[k] * cls[k] * 2, cudaMemcpyHostToDevice));
+            maps = maps && make_map_2d(&m->tm_w[l][k], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, at, rws[k], cls[k], cls[k] * 2,
+                                       kHgKTile, kHgM);
+            at += rws[k] * cls[k];
+        }
+    }
+    m->tensor_ok = maps &&
+                   make_map_2d(&m->tm_sl_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, m->sl_a, 3 * rows_pad, W, W * 2, kHgKTile,
+                               kHgN) &&
+                   make_map_2d(&m->tm_sl_g, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, m->sl_g, 3 * rows_pad, kFfn, kFfn * 2,
+                               kHgKTile, kHgN);
     return PHONON_CUDA_OK;
 }
 
@@ -3551,47 +3597,82 @@ int mimi_enqueue(PhononCudaMimi* m, int n) {
     const int32_t* slots = m->d_meta;
     const int32_t* pos = m->d_meta + m->max_batch;
     const float* zeros = m->vec + kMimiLayers * kMimiVecPerLayer * kWidth;
-    const float* freq = zeros + kWidth;
+    const float* freq = zeros + kFfn;
+    const bool tensor = m->tensor_ok && static_cast<uint32_t>(n) >= m->tensor_min;
+    uint16_t* sl = tensor ? m->sl_a : nullptr;
     CUDA_TRY(launch_pdl(mimi_in_kernel, dim3(n), dim3(512), 0, s, static_cast<const float*>(m->d_lat), slots,
                         static_cast<const uint16_t*>(m->w16), static_cast<const uint16_t*>(m->w16 + kWidth * 32),
                         m->previous, m->d_hidden, m->d_status));
     for (int l = 0; l < kMimiLayers; ++l) {
         const float* v = m->vec + l * kMimiVecPerLayer * kWidth;
+        HeadGemmParams g{};
+        g.bias = zeros;
+        g.status = m->d_status;
+        g.error = m->d_err;
         CUDA_TRY(launch_pdl(mimi_ln_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, static_cast<const float*>(m->d_hidden),
-                            v, v + kWidth, m->d_norm, rows, m->d_status));
-        GemvParams p{};
-        p.rows = 3 * kWidth;
-        p.cols = kWidth;
-        p.w = m->in_proj[l].plane;
-        p.x = m->d_norm;
-        p.ldx = kWidth;
-        p.B = rows;
-        p.y = m->d_qkv;
-        p.ldy = 3 * kWidth;
-        p.status = m->d_status;
-        CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_STORE>(p, s)));
+                            v, v + kWidth, m->d_norm, rows, m->d_status, sl));
+        if (tensor) {
+            HeadGemmParams q = g;
+            q.y = m->d_qkv;
+            q.ldy = 3 * kWidth;
+            CUDA_TRY((launch_bf16x3_gemm<HG_STORE>(m->tm_w[l][0], m->tm_sl_a, 3 * kWidth, rows, q, s)));
+        } else {
+            GemvParams p{};
+            p.rows = 3 * kWidth;
+            p.cols = kWidth;
+            p.w = m->in_proj[l].plane;
+            p.x = m->d_norm;
+            p.ldx = kWidth;
+            p.B = rows;
+            p.y = m->d_qkv;
+            p.ldy = 3 * kWidth;
+            p.status = m->d_status;
+            CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_STORE>(p, s)));
+        }
         CUDA_TRY(launch_pdl(mimi_rope_kv_kernel, dim3(rows), dim3(256), 0, s, m->d_qkv, slots, pos, freq, m->rings, l));
         CUDA_TRY(launch_pdl(mimi_attn_kernel, dim3(rows), dim3(256), 0, s, static_cast<const float*>(m->d_qkv), slots, pos,
-                            static_cast<const float*>(m->rings), l, m->d_att, m->d_status));
-        p = GemvParams{};
-        p.rows = kWidth;
-        p.cols = kWidth;
-        p.w = m->out_proj[l].plane;
-        p.x = m->d_att;
-        p.ldx = kWidth;
-        p.B = rows;
-        p.bias = zeros;
-        p.y = m->d_hidden;
-        p.ldy = kWidth;
-        p.res = m->d_hidden;
-        p.ldres = kWidth;
-        p.gate = v + 4 * kWidth;  // layer_scale_1, the same for every row
-        p.ldgate = 0;
-        p.status = m->d_status;
-        CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_GATE>(p, s)));
+                            static_cast<const float*>(m->rings), l, m->d_att, m->d_status, sl));
+        if (tensor) {
+            HeadGemmParams o = g;
+            o.y = m->d_hidden;
+            o.ldy = kWidth;
+            o.gate = v + 4 * kWidth;  // layer_scale_1, the same for every row
+            o.ldgate = 0;
+            CUDA_TRY((launch_bf16x3_gemm<HG_GATE>(m->tm_w[l][1], m->tm_sl_a, kWidth, rows, o, s)));
+        } else {
+            GemvParams p{};
+            p.rows = kWidth;
+            p.cols = kWidth;
+            p.w = m->out_proj[l].plane;
+            p.x = m->d_att;
+            p.ldx = kWidth;
+            p.B = rows;
+            p.bias = zeros;
+            p.y = m->d_hidden;
+            p.ldy = kWidth;
+            p.res = m->d_hidden;
+            p.ldres = kWidth;
+            p.gate = v + 4 * kWidth;  // layer_scale_1, the same for every row
+            p.ldgate = 0;
+            p.status = m->d_status;
+            CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_GATE>(p, s)));
+        }
         CUDA_TRY(launch_pdl(mimi_ln_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, static_cast<const float*>(m->d_hidden),
-                            v + 2 * kWidth, v + 3 * kWidth, m->d_norm, rows, m->d_status));
-        p = GemvParams{};
+                            v + 2 * kWidth, v + 3 * kWidth, m->d_norm, rows, m->d_status, sl));
+        if (tensor) {
+            HeadGemmParams u = g;
+            u.slices = m->sl_g;
+            u.slice_ld = kFfn;
+            CUDA_TRY((launch_bf16x3_gemm<HG_GELU>(m->tm_w[l][2], m->tm_sl_a, kFfn, rows, u, s)));
+            HeadGemmParams d = g;
+            d.y = m->d_hidden;
+            d.ldy = kWidth;
+            d.gate = v + 5 * kWidth;  // layer_scale_2
+            d.ldgate = 0;
+            CUDA_TRY((launch_bf16x3_gemm<HG_GATE, kFfn>(m->tm_w[l][3], m->tm_sl_g, kWidth, rows, d, s)));
+            continue;
+        }
+        GemvParams p{};
         p.rows = kFfn;
         p.cols = kWidth;
         p.w = m->linear1[l].plane;
@@ -3652,7 +3733,13 @@ int mimi_step_locked(PhononCudaMimi* m, uint32_t n, const uint32_t* states, cons
     if ((st = mimi_enqueue(m, static_cast<int>(n)))) return st;
     CUDA_TRY(cudaMemcpyAsync(m->h_out, m->d_hidden, rows * kWidth * 4, cudaMemcpyDeviceToHost, m->stream));
     CUDA_TRY(cudaMemcpyAsync(m->h_status, m->d_status, rows * 4, cudaMemcpyDeviceToHost, m->stream));
+    int32_t err = 0;
+    CUDA_TRY(cudaMemcpyAsync(&err, m->d_err, 4, cudaMemcpyDeviceToHost, m->stream));
     CUDA_TRY(cudaStreamSynchronize(m->stream));
+    if (err) {  // a bounded device wait expired: report, clear for the next call
+        CUDA_TRY(cudaMemset(m->d_err, 0, 4));
+        return PHONON_CUDA_DEVICE_ERROR;
+    }
     for (uint32_t i = 0; i < n; ++i) {
         bool bad = false;
         for (int r = 0; r < kMimiRows; ++r) bad |= m->h_status[i * kMimiRows + r] != 0;
@@ -3745,6 +3832,14 @@ int phonon_cuda_mimi_positions(PhononCudaMimi* m, uint32_t state, uint64_t* posi
     std::lock_guard<std::mutex> g(m->mu);
     if (!m->states[state].used) return PHONON_CUDA_INVALID_ARGUMENT;
     *positions = m->states[state].position;
+    return PHONON_CUDA_OK;
+}
+
+int phonon_cuda_mimi_set_tensor_min(PhononCudaMimi* m, uint32_t min_states, int* available) {
+    if (!m) return PHONON_CUDA_INVALID_ARGUMENT;
+    std::lock_guard<std::mutex> g(m->mu);
+    m->tensor_min = min_states;
+    if (available) *available = m->tensor_ok ? 1 : 0;
     return PHONON_CUDA_OK;
 }
 

@@ -17,9 +17,10 @@
 // raises the error flag, skips its stores and still frees its TMEM.
 //
 // Epilogues: HG_STORE y = acc + bias (fp32 rows); HG_GATE y = res + gate *
-// (acc + bias) in place (the residual update of a head block); HG_SILU
-// silu(acc + bias) written as the three slice rows of the next linear's
-// operand B.
+// (acc + bias) in place (the residual update of a head block, or a layer
+// scale with a gate stride of 0); HG_SILU silu(acc + bias) and HG_GELU
+// erf-GELU(acc + bias) written as the three slice rows of the next linear's
+// operand B. K is 512 or 2048 (kK).
 #pragma once
 
 #include "phonon_gemm.cuh"
@@ -37,7 +38,7 @@ constexpr int kHgTmemCols = 128;
 constexpr int kHgStageBytes = (kHgM + kHgN) * kHgKTile * 2;
 constexpr int kHgSmem = 1024 + kHgStages * kHgStageBytes + 256;
 
-enum HeadGemmEpilogue : int { HG_STORE = 0, HG_GATE = 1, HG_SILU = 2 };
+enum HeadGemmEpilogue : int { HG_STORE = 0, HG_GATE = 1, HG_SILU = 2, HG_GELU = 3 };
 
 struct HeadGemmParams {
     int rows;               // weight rows (M)
@@ -47,7 +48,8 @@ struct HeadGemmParams {
     int ldy;
     const float* gate;      // HG_GATE: [B][ldgate]
     int ldgate;
-    uint16_t* slices;       // HG_SILU: [3 * Bpad][512] bf16
+    uint16_t* slices;       // HG_SILU, HG_GELU: [3 * Bpad][slice_ld] bf16 (the next linear's operand B)
+    int slice_ld;
     int32_t* status;        // [B]
     int32_t* error;         // set when a bounded wait expires
 };
@@ -89,7 +91,7 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[N], int o
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-template <int kEpi>
+template <int kEpi, int kK = kHgK>
 __global__ void __launch_bounds__(kHgThreads, 2)
     head_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                      HeadGemmParams p) {
@@ -104,7 +106,7 @@ __global__ void __launch_bounds__(kHgThreads, 2)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_tile = blockIdx.x, n_tile = blockIdx.y;
-    constexpr int nk = kHgK / kHgKTile;
+    constexpr int nk = kK / kHgKTile;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kHgStages; ++s) {
@@ -205,15 +207,16 @@ __global__ void __launch_bounds__(kHgThreads, 2)
                     v = __fadd_rn(v, bias);
                     if constexpr (kEpi == HG_GATE) v = __fadd_rn(res[t], __fmul_rn(gate[t], v));
                     if constexpr (kEpi == HG_SILU) v = silu_f(v);
+                    if constexpr (kEpi == HG_GELU) v = gelu_erf(v);
                     if (!row_ok || b >= p.B) continue;
                     if (!isfinite(v)) flag_nonfinite(p.status, b);
-                    if constexpr (kEpi == HG_SILU) {
+                    if constexpr (kEpi == HG_SILU || kEpi == HG_GELU) {
                         uint16_t s0, s1, s2;
                         bf16x3_split(v, s0, s1, s2);
-                        uint16_t* row = p.slices + static_cast<size_t>(3 * b) * kHgK + r;
+                        uint16_t* row = p.slices + static_cast<size_t>(3 * b) * p.slice_ld + r;
                         row[0] = s0;
-                        row[kHgK] = s1;
-                        row[2 * kHgK] = s2;
+                        row[p.slice_ld] = s1;
+                        row[2 * p.slice_ld] = s2;
                     } else {
                         p.y[static_cast<size_t>(b) * p.ldy + r] = v;
                     }

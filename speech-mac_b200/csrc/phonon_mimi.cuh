@@ -8,16 +8,18 @@
 //
 //   mimi_in_kernel       projection + upsample -> hidden rows, keeps the
 //                        projection as the next frame's `previous`
-//   per layer:
+//   per layer (the linears on gemv_kernel, or from 4 states on the tensor
+//   cores: head_gemm_kernel, bf16 weights x three bf16 slices of the
+//   activations, whose producers then write slice rows):
 //     mimi_ln_kernel     LayerNorm 1 (the transformer's LayerNorm, eps 1e-5)
-//     gemv (bf16)        in_proj -> q | k | v
+//     linear             in_proj -> q | k | v
 //     mimi_rope_kv_kernel RoPE of q and k at each row's position; k and v
 //                        of all 16 rows into the state's ring
 //     mimi_attn_kernel   softmax(q k / 8) v over the row's window
-//     gemv EPI_GATE      hidden += layer_scale_1 * out_proj(att)
+//     linear, gated     hidden += layer_scale_1 * out_proj(att)
 //     mimi_ln_kernel     LayerNorm 2
-//     gemv EPI_GELU      erf-GELU(linear1)
-//     gemv EPI_GATE      hidden += layer_scale_2 * linear2(.)
+//     linear, GELU       erf-GELU(linear1)
+//     linear, gated     hidden += layer_scale_2 * linear2(.)
 //
 // The ring: the reference keeps 250 slots and inserts a frame's keys query by
 // query, so that a later row's write never evicts a key an earlier row still
@@ -27,7 +29,7 @@
 // [max(0, p - 249), p] of the reference.
 #pragma once
 
-#include "phonon_kernels.cuh"
+#include "phonon_head_gemm.cuh"
 
 namespace phonon {
 
@@ -97,17 +99,29 @@ __global__ void __launch_bounds__(512) mimi_in_kernel(const float* __restrict__ 
 }
 
 // LayerNorm of rows (eps 1e-5, the reference's Welford cascade), one warp per
-// row; a non-finite row flags its status word.
+// row; a non-finite row flags its status word. With `slices`, the row also
+// goes out as its three bf16 slice rows (the tensor-core linears' operand).
 __global__ void __launch_bounds__(256) mimi_ln_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                       const float* __restrict__ b, float* __restrict__ out, int rows,
-                                                      int32_t* status) {
-    const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+                                                      int32_t* status, uint16_t* __restrict__ slices) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     pdl_wait();
     pdl_trigger();
     if (r >= rows) return;
-    if (!warp_layernorm512(x + static_cast<size_t>(r) * kWidth, w, b, out + static_cast<size_t>(r) * kWidth) &&
-        (threadIdx.x & 31) == 0)
-        flag_nonfinite(status, r);
+    float* o = out + static_cast<size_t>(r) * kWidth;
+    if (!warp_layernorm512(x + static_cast<size_t>(r) * kWidth, w, b, o) && lane == 0) flag_nonfinite(status, r);
+    if (slices) {
+        __syncwarp();
+        for (int k = 0; k < kWidth / 32; ++k) {
+            const int i = lane + 32 * k;
+            uint16_t s0, s1, s2;
+            bf16x3_split(o[i], s0, s1, s2);
+            uint16_t* dst = slices + static_cast<size_t>(3 * r) * kWidth + i;
+            dst[0] = s0;
+            dst[kWidth] = s1;
+            dst[2 * kWidth] = s2;
+        }
+    }
 }
 
 // One CTA of 256 threads per row: RoPE of q and k (interleaved pairs, eight
@@ -152,7 +166,8 @@ __global__ void __launch_bounds__(256) mimi_rope_kv_kernel(float* __restrict__ q
 // output scaled by 1 / sum.
 __global__ void __launch_bounds__(256) mimi_attn_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ slots,
                                                         const int32_t* __restrict__ pos0, const float* __restrict__ rings,
-                                                        int layer, float* __restrict__ att, int32_t* status) {
+                                                        int layer, float* __restrict__ att, int32_t* status,
+                                                        uint16_t* __restrict__ slices) {
     __shared__ __align__(16) float qs[kHeads][kHeadDim];
     __shared__ float ps[kHeads][kMimiContext + 2];
     const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -214,7 +229,18 @@ __global__ void __launch_bounds__(256) mimi_attn_kernel(const float* __restrict_
     const float inv = __fdiv_rn(1.0f, total);
     const float o0 = __fmul_rn(a0, inv), o1 = __fmul_rn(a1, inv);
     ok &= total > 0.0f && isfinite(total) && isfinite(o0) && isfinite(o1);
-    *reinterpret_cast<float2*>(att + static_cast<size_t>(row) * kWidth + warp * kHeadDim + 2 * lane) = make_float2(o0, o1);
+    const int col = warp * kHeadDim + 2 * lane;
+    if (slices) {  // operand of the tensor-core out projection
+        uint16_t a0s, a1s, a2s, b0s, b1s, b2s;
+        bf16x3_split(o0, a0s, a1s, a2s);
+        bf16x3_split(o1, b0s, b1s, b2s);
+        uint16_t* dst = slices + static_cast<size_t>(3 * row) * kWidth + col;
+        *reinterpret_cast<uint32_t*>(dst) = a0s | (static_cast<uint32_t>(b0s) << 16);
+        *reinterpret_cast<uint32_t*>(dst + kWidth) = a1s | (static_cast<uint32_t>(b1s) << 16);
+        *reinterpret_cast<uint32_t*>(dst + 2 * kWidth) = a2s | (static_cast<uint32_t>(b2s) << 16);
+    } else {
+        *reinterpret_cast<float2*>(att + static_cast<size_t>(row) * kWidth + col) = make_float2(o0, o1);
+    }
     if (!__all_sync(kFull, ok) && lane == 0) flag_nonfinite(status, row);
 }
 

@@ -118,6 +118,7 @@ def lib():
         "phonon_cuda_mimi_state_free": [P, U32],
         "phonon_cuda_mimi_positions": [P, U32, C.POINTER(C.c_uint64)],
         "phonon_cuda_mimi_step": [P, U32, P, P, P, P],
+        "phonon_cuda_mimi_set_tensor_min": [P, U32, C.POINTER(C.c_int)],
         "phonon_cuda_mimi_process": [P, U32, P, SZ, P, SZ],
     }
     for name, args in sig.items():
@@ -542,6 +543,11 @@ class Mimi:
         if self.h:
             self.L.phonon_cuda_mimi_destroy(self.h)
             self.h = None
+
+    def set_tensor_min(self, min_states):
+        ok = C.c_int(0)
+        check(self.L.phonon_cuda_mimi_set_tensor_min(self.h, min_states, C.byref(ok)), "mimi_set_tensor_min")
+        return bool(ok.value)
 
     def alloc(self):
         s = C.c_uint32()

@@ -40,13 +40,16 @@ def test_synthetic_closed_form(cuda_ok):
         m.close()
 
 
-@pytest.mark.parametrize("seed", [0, 1])
-def test_random_vs_oracle_and_reference(cuda_ok, oracle, reference, seed):
+@pytest.mark.parametrize("seed,tensor", [(0, False), (1, False), (0, True)])
+def test_random_vs_oracle_and_reference(cuda_ok, oracle, reference, seed, tensor):
+    """tensor: the four linears on the tensor cores (head_gemm_kernel, bf16
+    weights x three bf16 slices), forced for this small batch."""
     model = mimi_models.random_model(seed)
     rng = np.random.default_rng(40 + seed)
     n, frames = 3, 18  # 288 positions: the ring wraps
     latents = rng.standard_normal((n, frames, 32)).astype(np.float32)
     m = rt.Mimi(model, max_states=4, max_batch=4)
+    assert m.set_tensor_min(1 if tensor else 1 << 20), "tensor-core Mimi path unavailable"
     try:
         states = [m.alloc() for _ in range(n)]
         feats = np.zeros((n, frames * 16, 512), np.float32)
@@ -66,7 +69,7 @@ def test_random_vs_oracle_and_reference(cuda_ok, oracle, reference, seed):
         r.close()
         assert ok
         worst_r = rel_err(feats[0], fr)
-        print(f"mimi seed {seed}: vs oracle {worst_o:.2e}, vs reference build {worst_r:.2e}")
+        print(f"mimi seed {seed}{' tensor' if tensor else ''}: vs oracle {worst_o:.2e}, vs reference build {worst_r:.2e}")
         assert worst_o < CHAIN_TOL and worst_r < CHAIN_TOL
         # one state alone gives the same rows as in the batch
         s = m.alloc()
