@@ -3630,8 +3630,13 @@ int mimi_enqueue(PhononCudaMimi* m, int n) {
             CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_STORE>(p, s)));
         }
         CUDA_TRY(launch_pdl(mimi_rope_kv_kernel, dim3(rows), dim3(256), 0, s, m->d_qkv, slots, pos, freq, m->rings, l));
-        CUDA_TRY(launch_pdl(mimi_attn_kernel, dim3(rows), dim3(256), 0, s, static_cast<const float*>(m->d_qkv), slots, pos,
-                            static_cast<const float*>(m->rings), l, m->d_att, m->d_status, sl));
+        {
+            static std::atomic<uint64_t> configured{0};
+            CUDA_TRY(opt_in_smem(reinterpret_cast<const void*>(mimi_attn_kernel), kMimiAttnSmem, configured));
+        }
+        CUDA_TRY(launch_pdl(mimi_attn_kernel, dim3(n * kHeads), dim3(kMimiRows * 32), kMimiAttnSmem, s,
+                            static_cast<const float*>(m->d_qkv), slots, pos, static_cast<const float*>(m->rings), l,
+                            m->d_att, m->d_status, sl));
         if (tensor) {
             HeadGemmParams o = g;
             o.y = m->d_hidden;

@@ -15,7 +15,8 @@
 //     linear             in_proj -> q | k | v
 //     mimi_rope_kv_kernel RoPE of q and k at each row's position; k and v
 //                        of all 16 rows into the state's ring
-//     mimi_attn_kernel   softmax(q k / 8) v over the row's window
+//     mimi_attn_kernel   softmax(q k / 8) v over each row's window, one CTA
+//                        per (state, head) with the window staged once
 //     linear, gated     hidden += layer_scale_1 * out_proj(att)
 //     mimi_ln_kernel     LayerNorm 2
 //     linear, GELU       erf-GELU(linear1)
@@ -158,35 +159,58 @@ __global__ void __launch_bounds__(256) mimi_rope_kv_kernel(float* __restrict__ q
     *reinterpret_cast<float2*>(vr + 2 * t) = *reinterpret_cast<const float2*>(q + 2 * kWidth + 2 * t);
 }
 
-// One CTA per row, warp h = head h (src/phonon_mimi.c:136-193): scores of the
-// row's query against the keys of positions [first, p] (lane j takes keys j,
-// j + 32, ...; each dot over the head's [even | odd] component order, as the
-// reference's permuted GEMM operands), scale 1/8, max, e^(s - max) and their
-// sum over the warp, then P.V with lane l owning dims 2l, 2l+1, and the
+// Keys of a frame's window staged per (state, head): at most 250 + 15
+// positions, rows padded to 68 floats (lanes reading different rows at the
+// same column fall into different banks).
+constexpr int kMimiWin = kMimiContext + kMimiRows - 1;
+constexpr int kMimiKvStride = kHeadDim + 4;
+constexpr int kMimiAttnSmem = (2 * kMimiWin * kMimiKvStride + kMimiRows * (kMimiContext + 2)) * 4;
+
+// One CTA per (state, head), warp r = the frame's query row r
+// (src/phonon_mimi.c:136-193): the head's K and V rows of every position the
+// frame's 16 queries see are staged in shared memory once; then each warp
+// scores its query against the keys of its window [first, p] (lane j takes
+// keys j, j + 32, ...; each dot over the head's [even | odd] component order,
+// as the reference's permuted GEMM operands), scale 1/8, max, e^(s - max) and
+// their sum over the warp, then P.V with lane l owning dims 2l, 2l+1, and the
 // output scaled by 1 / sum.
-__global__ void __launch_bounds__(256) mimi_attn_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ slots,
-                                                        const int32_t* __restrict__ pos0, const float* __restrict__ rings,
-                                                        int layer, float* __restrict__ att, int32_t* status,
-                                                        uint16_t* __restrict__ slices) {
-    __shared__ __align__(16) float qs[kHeads][kHeadDim];
-    __shared__ float ps[kHeads][kMimiContext + 2];
-    const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b = row / kMimiRows;
+__global__ void __launch_bounds__(512, 1) mimi_attn_kernel(const float* __restrict__ qkv, const int32_t* __restrict__ slots,
+                                                           const int32_t* __restrict__ pos0, const float* __restrict__ rings,
+                                                           int layer, float* __restrict__ att, int32_t* status,
+                                                           uint16_t* __restrict__ slices) {
+    extern __shared__ __align__(16) float mimi_smem[];
+    float* ks = mimi_smem;                                   // [kMimiWin][68]
+    float* vs = ks + kMimiWin * kMimiKvStride;                // [kMimiWin][68]
+    float* ps_all = vs + kMimiWin * kMimiKvStride;            // [16][252]
+    __shared__ __align__(16) float qs[kMimiRows][kHeadDim];
+    const int b = blockIdx.x / kHeads, head = blockIdx.x % kHeads;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
     pdl_trigger();
-    const int position = pos0[b] + row % kMimiRows;
-    const int count = position < kMimiContext - 1 ? position + 1 : kMimiContext;
-    const int first = position + 1 - count;
-    const float* q = qkv + static_cast<size_t>(row) * 3 * kWidth + warp * kHeadDim;
+    const int p0 = pos0[b];
+    const int win_first = p0 > kMimiContext - 1 ? p0 - (kMimiContext - 1) : 0;  // the first row's first key
+    const int win_count = p0 + kMimiRows - win_first;                              // through the last row's key
+    const float* kg = mimi_ring(const_cast<float*>(rings), slots[b], layer, 0) + head * kHeadDim;
+    const float* vg = mimi_ring(const_cast<float*>(rings), slots[b], layer, 1) + head * kHeadDim;
+    for (int i = threadIdx.x; i < win_count * (kHeadDim / 4); i += blockDim.x) {
+        const int key = i / (kHeadDim / 4), c4 = i % (kHeadDim / 4);
+        const size_t src = static_cast<size_t>((win_first + key) % kMimiRing) * kWidth + 4 * c4;
+        *reinterpret_cast<float4*>(ks + key * kMimiKvStride + 4 * c4) = *reinterpret_cast<const float4*>(kg + src);
+        *reinterpret_cast<float4*>(vs + key * kMimiKvStride + 4 * c4) = *reinterpret_cast<const float4*>(vg + src);
+    }
+    const int row = b * kMimiRows + warp;
+    const float* q = qkv + static_cast<size_t>(row) * 3 * kWidth + head * kHeadDim;
     qs[warp][lane] = q[lane];
     qs[warp][lane + 32] = q[lane + 32];
-    __syncwarp();
-    const float* keys = mimi_ring(const_cast<float*>(rings), slots[b], layer, 0) + warp * kHeadDim;
-    const float* values = mimi_ring(const_cast<float*>(rings), slots[b], layer, 1) + warp * kHeadDim;
+    __syncthreads();
+    const int position = p0 + warp;
+    const int count = position < kMimiContext - 1 ? position + 1 : kMimiContext;
+    const int first = position + 1 - count - win_first;  // the row's first key in the staged window
+    float* ps = ps_all + warp * (kMimiContext + 2);
     float mx = -INFINITY;
     bool ok = true;
     for (int j = lane; j < count; j += 32) {
-        const float* kr = keys + static_cast<size_t>((first + j) % kMimiRing) * kWidth;
+        const float* kr = ks + (first + j) * kMimiKvStride;
         float kv[kHeadDim];
 #pragma unroll
         for (int i = 0; i < kHeadDim / 4; ++i) {
@@ -203,7 +227,7 @@ __global__ void __launch_bounds__(256) mimi_attn_kernel(const float* __restrict_
             for (int i = 0; i < 32; ++i) dot = fmaf(qs[warp][2 * i + parity], kv[2 * i + parity], dot);
         const float s = __fmul_rn(dot, 0.125f);
         ok &= isfinite(s);
-        ps[warp][j] = s;
+        ps[j] = s;
         mx = fmaxf(mx, s);
     }
 #pragma unroll
@@ -211,8 +235,8 @@ __global__ void __launch_bounds__(256) mimi_attn_kernel(const float* __restrict_
     __syncwarp();
     float total = 0.0f;
     for (int j = lane; j < count; j += 32) {
-        const float e = expf(__fsub_rn(ps[warp][j], mx));
-        ps[warp][j] = e;
+        const float e = expf(__fsub_rn(ps[j], mx));
+        ps[j] = e;
         total = __fadd_rn(total, e);
     }
     total = warp_sum(total);
@@ -220,16 +244,15 @@ __global__ void __launch_bounds__(256) mimi_attn_kernel(const float* __restrict_
     float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll 4
     for (int j = 0; j < count; ++j) {
-        const float2 v = *reinterpret_cast<const float2*>(values + static_cast<size_t>((first + j) % kMimiRing) * kWidth +
-                                                          2 * lane);
-        const float p = ps[warp][j];
+        const float2 v = *reinterpret_cast<const float2*>(vs + (first + j) * kMimiKvStride + 2 * lane);
+        const float p = ps[j];
         a0 = fmaf(p, v.x, a0);
         a1 = fmaf(p, v.y, a1);
     }
     const float inv = __fdiv_rn(1.0f, total);
     const float o0 = __fmul_rn(a0, inv), o1 = __fmul_rn(a1, inv);
     ok &= total > 0.0f && isfinite(total) && isfinite(o0) && isfinite(o1);
-    const int col = warp * kHeadDim + 2 * lane;
+    const int col = head * kHeadDim + 2 * lane;
     if (slices) {  // operand of the tensor-core out projection
         uint16_t a0s, a1s, a2s, b0s, b1s, b2s;
         bf16x3_split(o0, a0s, a1s, a2s);
