@@ -262,10 +262,10 @@ uint64_t phonon_cuda_launch_count(PhononCuda *ctx);
  * launch per stage, with the projections on the tensor cores from
  * tensor_min_batch streams up, and from split_min_batch streams up as two
  * half batches on two CUDA streams, so that one half's attention overlaps
- * the other half's projections. Defaults: 2, 3, 4, 320 (measured on B200:
+ * the other half's projections. Defaults: 2, 3, 4, 96 (measured on B200:
  * one stream is fastest on the per-stage GEMVs, two and three in the
  * persistent step, from four on the tensor-core projections win; halves gain
- * from a few hundred streams; the second lane exists when max_batch >= 96). A step
+ * from about a hundred streams; the second lane exists when max_batch >= 96). A step
  * on two lanes gives the results of one lane up to rounding: each half
  * plans its attention splits on its own, so partial sums merge in another
  * order. fused_min_batch > fused_max_batch disables the

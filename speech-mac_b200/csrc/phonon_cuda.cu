@@ -44,7 +44,7 @@ constexpr int kPlanHeader = 8;       // ints of the step plan header in the meta
 constexpr int kGuide = 2;            // guided chunks: remaining pages / (kGuide * attention CTAs)
 constexpr int kTicketMinChunk = 8;   // pages per guided chunk, at least
 constexpr int kMaxChunks = 8192;     // chunks per plan, at most
-constexpr int kSplitMinBatch = 320;  // from here a step runs as two concurrent half batches
+constexpr int kSplitMinBatch = 96;   // from here a step runs as two concurrent half batches
 
 #define CUDA_TRY(expr)                                                                       \
     do {                                                                                     \

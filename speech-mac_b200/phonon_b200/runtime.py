@@ -289,7 +289,7 @@ class Context:
         return int(self.L.phonon_cuda_launch_count(self.h))
 
     def set_batch_paths(self, fused_min_batch=2, fused_max_batch=3, tensor_min_batch=4,
-                        split_min_batch=320):
+                        split_min_batch=96):
         """Batch sizes routed to the persistent whole-step launch
         (fused_min_batch..fused_max_batch; a minimum above the maximum
         disables it), to the tensor-core projections (>= tensor_min_batch) and

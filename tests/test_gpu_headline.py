@@ -47,6 +47,8 @@ def test_headline_step_teacher_forced(cuda_ok, oracle, weights12, n, n_pick):
     lens = _contexts(n)
     pages = sum((ln + STEPS) // 16 + 1 for ln in lens) + 64
     ctx = rt.Context(weights12, max_streams=n + 8, max_batch=n, pool_pages=pages, kv_type=rt.KV_BF16)
+    if n < 512:  # one lane, so that attention hands out its chunks by ticket
+        ctx.set_batch_paths(split_min_batch=1 << 20)
     trace = parity.Trace(ctx, n)
     try:
         streams = [ctx.stream_alloc(2048 + STEPS + 16) for _ in range(n)]
