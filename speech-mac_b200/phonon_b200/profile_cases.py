@@ -16,6 +16,10 @@ cases:
   head512   the flow head at 512 rows on the tensor cores (head_gemm_kernel
             and the head's small kernels), three LSD steps
   frame1    three frames of one stream through phonon_cuda_frame_step
+  mimi64    the Mimi latent transformer, 64 states (tensor-core linears),
+            rings past the 250-key window, three steps
+  perblock512  step512 with per-block-scale Q8_0 weights (three weight
+            digit planes on the tensor cores)
 Each case runs three steps (or calls) after its set-up and prints "ok".
 """
 import sys
@@ -26,8 +30,10 @@ from . import runtime as rt
 from . import synth
 
 
-def _decode(n, lens, kv, steps=3):
+def _decode(n, lens, kv, steps=3, per_block=False):
     w = synth.flow_weights(12, seed=0)
+    if per_block:
+        w = synth.per_block_scales(w, 5)
     pages = sum((ln + 8) // 16 + 1 for ln in lens) + 16
     ctx = rt.Context(w, max_streams=n + 2, max_batch=n, pool_pages=pages, kv_type=kv)
     ss = [ctx.stream_alloc(max(lens) + 64) for _ in range(n)]
@@ -96,6 +102,16 @@ def frame1():
     ctx.close()
 
 
+def mimi64():
+    m = rt.Mimi(synth.mimi_model(0), max_states=64, max_batch=64)
+    states = [m.alloc() for _ in range(64)]
+    rng = np.random.default_rng(5)
+    for _ in range(16 + 3):  # 304 positions: past the window
+        _, st = m.step(states, rng.standard_normal((64, 32)).astype(np.float32))
+        assert not st.any()
+    m.close()
+
+
 CASES = {
     "cluster": cluster,
     "gemv": gemv,
@@ -104,6 +120,9 @@ CASES = {
     "persist": lambda: _decode(3, [1000, 1500, 2000], rt.KV_BF16),
     "head512": head512,
     "frame1": frame1,
+    "mimi64": mimi64,
+    "perblock512": lambda: _decode(512, [int(x) for x in np.random.default_rng(2).integers(64, 129, 512)], rt.KV_BF16,
+                                   per_block=True),
 }
 
 if __name__ == "__main__":
