@@ -515,7 +515,8 @@ def bench_single_stream(rt, synth, weights, torch):
     return {"workload": "configs[0]", "frames_per_s": round(125 / (total * 1e-3), 1),
             "ms_per_step_median": round(statistics.median(times), 4),
             "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 4), "peak_source": peak_kind,
-            "path": "16-CTA cluster step" if cluster else "per-stage GEMV step",
+            "path": {2: "16-CTA cluster step, projections on the tensor cores",
+                     1: "16-CTA cluster step"}.get(cluster, "per-stage GEMV step"),
             "l2": "flushed before each step"}
 
 

@@ -290,10 +290,14 @@ int phonon_cuda_set_batch_paths(PhononCuda *ctx, uint32_t fused_min_batch, uint3
  * reference engine's one-request-per-thread decode loop (src/speech.c:170).
  * max_position 0 sends every batch through the paths of
  * phonon_cuda_set_batch_paths; the default is PHONON_CUDA_MAX_POSITIONS.
- * *available (optional) receives 1 when the context can run the path (Q8_0
- * weights, TMA K/V staging, a 16-CTA cluster resident on the device).
- * Projections and appended K/V rows equal the other paths' bit for bit; the
- * attention merges its partial sums in another order (within rounding). */
+ * *available (optional) receives 0 when the context cannot run the path, 1
+ * when it runs it with every projection on the CUDA cores (Q8_0 weights, TMA
+ * K/V staging, a 16-CTA cluster resident on the device), 2 when it runs the
+ * four projections on the tensor cores (every layer's weights carry one scale
+ * per row). Projections and appended K/V rows equal those of the per-stage
+ * path with the same arithmetic bit for bit: the GEMV path's in form 1, the
+ * tensor-core path's (digit-sliced activations) in form 2. The attention
+ * merges its partial sums in another order (within rounding). */
 int phonon_cuda_set_cluster_step(PhononCuda *ctx, uint32_t max_position, int *available);
 
 /* ---- per-layer output trace (test instrumentation) ----

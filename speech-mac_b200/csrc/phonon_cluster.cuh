@@ -34,15 +34,20 @@
 // has finished reading that buffer for layer l (the chain is A..E in order),
 // and each buffer's barrier completes exactly one phase per layer.
 //
-// Warp 8 is the copy warp. At launch it asks L2 to prefetch the CTA's weight
-// rows for the whole step and its head's K/V blocks of every layer
-// (cp.async.bulk.prefetch.L2). Then it streams, in the order the compute
+// Warp 8 is the copy warp. It streams, in the order the compute
 // warps consume them, the CTA's weight rows through a ring of 17 KB slots
 // (32 rows of a 512-column matrix or 8 rows of the 2048-column one, with
 // their Q8_0 scales), the LayerNorm vectors through a two-slot ring and its
 // head's K/V blocks of the stream's earlier pages through an eight-slot page
 // ring (TMA, 16-row SWIZZLE_128B boxes), each as soon as the slot it refills
-// is released. No page read waits for this step's append.
+// is released. No page read waits for this step's append. Most copies are
+// issued several microseconds before their data is read; the two that are
+// not (the next layer's v unit, whose slot frees at the end of a layer, and
+// the last down unit, whose slot frees in stage D) are prefetched into L2 a
+// layer ahead (cp.async.bulk.prefetch.L2). Prefetching more costs more than
+// it saves: prefetches queue in the SM's bulk-copy unit ahead of the ring's
+// copies (the whole step's weights prefetched at launch, ~3 MB per CTA, held
+// the first layer back ~20 us; a layer ahead, the attention pages ~3 us).
 //
 // Code size: the LayerNorm, the row dot products and the attention page are
 // each one non-inlined routine, so the ~60 stages of a step run through a
@@ -73,24 +78,26 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 }
 
 // Phase timestamps for profiling builds (-DPHONON_CLUSTER_TRACE): thread 0
-// of every CTA writes %globaltimer at marked points into
+// (CL_MARK_T: the given thread) of every CTA writes %globaltimer at marked points into
 // g_cluster_trace[(rank * 64 + layer) * 32 + slot] (layer 63: set-up). Marks
 // sit right after waits and named barriers, which order them against the
 // work before them. Empty otherwise.
 #ifdef PHONON_CLUSTER_TRACE
 __device__ unsigned long long g_cluster_trace[16 * 64 * 32];
-#define CL_MARK(layer, slot)                                                                       \
+#define CL_MARK_T(thread, layer, slot)                                                             \
     do {                                                                                           \
-        if (threadIdx.x == 0) {                                                                    \
+        if (threadIdx.x == (thread)) {                                                             \
             unsigned long long t_;                                                                 \
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_)::"memory");                      \
             g_cluster_trace[(static_cast<size_t>(cluster_ctarank()) * 64 + (layer)) * 32 + (slot)] = t_; \
         }                                                                                          \
     } while (0)
+#define CL_MARK(layer, slot) CL_MARK_T(0, layer, slot)
 #else
-#define CL_MARK(layer, slot) \
-    do {                     \
+#define CL_MARK_T(thread, layer, slot) \
+    do {                               \
     } while (0)
+#define CL_MARK(layer, slot) CL_MARK_T(0, layer, slot)
 #endif
 
 constexpr int kClusterCtas = 16;
@@ -110,11 +117,15 @@ constexpr int kClMsgFloats = 100;
 constexpr int kClNormBytes = 2 * kWidth * 4;      // one LayerNorm's weight + bias (fp32)
 constexpr int kClMaxUpdates = 2;                  // page-table updates carried in the parameters
 // Exchange buffers with one mbarrier each, completing once per layer.
-enum ClExchange : int { CLX_PART = 0, CLX_H = 1, CLX_G = 2, CLX_X = 3 };
+// CLX_R (kTc): the down projection's int32 partial sums, reduced by the
+// CTA that owns the rows.
+enum ClExchange : int { CLX_PART = 0, CLX_H = 1, CLX_G = 2, CLX_X = 3, CLX_R = 4 };
+constexpr int kClExchanges = 5;
 constexpr uint32_t kClBytesPart = kClusterCtas * kClMsgFloats * 4;  // 16 messages
 constexpr uint32_t kClBytesH = kWidth * 4;                          // 16 slices of 32 rows
 constexpr uint32_t kClBytesG = kFfn * 4;                            // 16 slices of 128 rows
 constexpr uint32_t kClBytesX = kWidth * 4;
+constexpr uint32_t kClBytesR = 4 * 32 * 4 * 4;  // four senders x 32 rows x 4 digit sums
 // Activation rows in shared memory are padded: 4 floats after every 64, so
 // that the LayerNorm lanes' stride-4 accesses (lane = chunk * 4 + l) fall into
 // 32 banks; element e lives at cl_pad(e).
@@ -124,17 +135,35 @@ constexpr int kClFfnPad = kFfn / 64 * kClChunk;    // 2176 floats
 __host__ __device__ constexpr int cl_pad(int e) { return e + 4 * (e >> 6); }
 constexpr int kClNormPadBytes = 2 * kClRowPad * 4;  // a LayerNorm's padded weight + bias
 
-template <bool kBf16>
+// Tensor-core units (kTc): with one scale per weight row (every Q8_0 block of
+// a row shares it), a CTA's 128 q/k/v rows and its 128 up rows are each one
+// M = 128 tile of a tcgen05 int8 MMA. The out and down projections are split
+// over K: CTA rank computes rows [128 (rank / 4), +128) over columns
+// [128 (rank % 4), +128) (out) or [512 (rank % 4), +512) (down), and the four
+// CTAs of a row group send their int32 partial sums of rows [32 r, +32) to
+// CTA r, which adds them (exactly) and finishes those rows. The weight units
+// of the four projections are K
+// slices: unit k holds 128 columns of the 128 rows as a SWIZZLE_128B tile
+// (16 KB) followed by the 128 fp32 row scales. Activations enter as four
+// base-128 digit rows (operand B, N = 16: rows 4-15 stay zero), sliced with
+// the exponent of the whole row exactly as the batched tensor path slices
+// its rows (ln_digits_kernel, digits_kernel<2048>).
+constexpr int kClTcDigRowBytes = 16 * 128;         // B tile of one K slice: 16 rows x 128 bytes
+constexpr int kClTcDigBytes = 4 * kClTcDigRowBytes;  // K = 512
+constexpr int kClTcUnits = kClUnitsPerLayer;       // per layer and CTA: 4 q/k/v, out, 4 up, 4 down slices
+
+template <bool kBf16, bool kTc = false>
 struct ClShape {
-    static constexpr int kWSlots = kBf16 ? 9 : 7;                    // weight ring slots
+    static constexpr int kWSlots = kBf16 ? (kTc ? 8 : 9) : 7;        // weight ring slots
     static constexpr int kBox = kPage * 128;                          // 16 rows x 128 bytes
     static constexpr int kKvBlock = kPage * kHeadDim * (kBf16 ? 2 : 4);  // K (or V) of one head, one page
     static constexpr int kKvSlot = 2 * kKvBlock;
     // Offsets from the 1024-aligned base (SWIZZLE_128B boxes first).
     static constexpr int kOffKv = 0;
     static constexpr int kOffW = kOffKv + kClKvSlots * kKvSlot;
-    static constexpr int kOffNorm = kOffW + kWSlots * kClUnitBytes;
-    static constexpr int kOffX = kOffNorm + 2 * kClNormPadBytes;   // layer input x [512], padded
+    static constexpr int kOffDig = kOffW + kWSlots * kClUnitBytes;   // digit rows (kTc), 1024-aligned
+    static constexpr int kOffNorm = kOffDig + (kTc ? kClTcDigBytes : 0);
+    static constexpr int kOffX = kOffNorm + kClNormPadBytes;        // layer input x [512], padded
     static constexpr int kOffXn = kOffX + kClRowPad * 4;            // LayerNorm output, padded
     static constexpr int kOffH = kOffXn + kClRowPad * 4;            // h = x + attn Wout, padded
     static constexpr int kOffA = kOffH + kClRowPad * 4;             // attention row, padded
@@ -145,19 +174,25 @@ struct ClShape {
     static constexpr int kOffMine = kOffMsg + kClusterCtas * kClMsgFloats * 4;  // this CTA's message [100]
     static constexpr int kOffWPart = kOffMine + kClMsgFloats * 4;   // warp partials [8][68]
     static constexpr int kOffRope = kOffWPart + kClWarps * kClPartStride * 4;  // (cos, sin) [32]
-    static constexpr int kOffBar = kOffRope + 32 * 8;
-    static constexpr int kBars = 2 * kWSlots + 4 + 2 * kClKvSlots + 4;
-    static constexpr int kOffFlag = kOffBar + kBars * 8;
+    static constexpr int kOffRed = kOffRope + 32 * 8;               // kTc: down partial sums [4][32][4] int32
+    static constexpr int kOffBar = kOffRed + (kTc ? static_cast<int>(kClBytesR) : 0);
+    // weight ring full/empty, LayerNorm vectors full/empty, page ring
+    // full/empty, the exchanges, the MMA accumulator
+    static constexpr int kBars = 2 * kWSlots + 2 + 2 * kClKvSlots + kClExchanges + 1;
+    static constexpr int kOffFlag = kOffBar + kBars * 8;            // failed flag, TMEM base, digit exponent
     static constexpr int kSmem = kOffFlag + 16 + 1024;  // + alignment slack
-    static_assert(kKvSlot % 1024 == 0 && kOffW % 16 == 0 && kClUnitBytes % 16 == 0, "slot alignment");
+    static_assert(kKvSlot % 1024 == 0 && kOffW % 1024 == 0 && kClUnitBytes % 1024 == 0 && kOffDig % 1024 == 0,
+                  "slot alignment (SWIZZLE_128B operand tiles)");
     static_assert(kOffMsg % 16 == 0 && kOffH % 16 == 0 && kOffG % 16 == 0 && kOffX % 16 == 0 &&
-                      kOffMine % 16 == 0 && kOffQ % 16 == 0 && kOffSelf % 16 == 0 && kOffBar % 8 == 0,
+                      kOffMine % 16 == 0 && kOffQ % 16 == 0 && kOffSelf % 16 == 0 && kOffRed % 16 == 0 &&
+                      kOffBar % 8 == 0,
                   "vector and st.async alignment");
     static_assert(kSmem <= 232448, "shared memory of one CTA");
 };
 
 struct ClusterParams {
     const PersistLayer* layers;  // per layer: lane-interleaved Q8_0 planes, scales, fp32 norms
+    const uint8_t* tc;           // kTc: [layer][16 CTAs][8 units][kClUnitBytes] tensor-core units
     int n_layers;
     const float* in;             // [512]
     float* out;                  // [512]
@@ -213,6 +248,26 @@ __device__ __noinline__ bool cl_exchange_wait(uint32_t bar, uint32_t parity, int
             if (error) atomicExch(error, 1);
             return false;
         }
+    }
+    return true;
+}
+
+// The copy warp's bounded wait for a slot release. The copy warp is warp 8
+// and shares a scheduler with compute warps 0 and 4 (warps are assigned to
+// the SM's four schedulers by warp index mod 4); polling without a pause took
+// issue slots from them (a LayerNorm on warp 0 ran ~4x longer than the same
+// routine on warp 1), so it sleeps between polls.
+__device__ __noinline__ bool cl_copy_wait(uint32_t bar, uint32_t parity, int32_t* error, volatile int* failed) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long start = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*failed) return false;
+        if (clock64() - start > kWaitBudgetCycles) {
+            *failed = 1;
+            if (error) atomicExch(error, 1);
+            return false;
+        }
+        __nanosleep(64);
     }
     return true;
 }
@@ -446,10 +501,17 @@ __device__ __noinline__ ClAttnState cl_attn_page(const uint8_t* sK, const float*
     return st;
 }
 
-// Source rows of weight unit u (layer u / 13) for CTA `rank`.
+// Source rows of weight unit u (layer u / 13) for CTA `rank`. With kTc the
+// q/k/v and up units are the K slices of the tensor-core pack.
+template <bool kTc = false>
 __device__ __forceinline__ void cl_unit_src(const ClusterParams& p, int u, int rank, const uint8_t*& plane,
                                             const uint8_t*& scales) {
     const int l = u / kClUnitsPerLayer, k = u % kClUnitsPerLayer;
+    if (kTc) {
+        plane = p.tc + (static_cast<size_t>(l * kClusterCtas + rank) * kClTcUnits + k) * kClUnitBytes;
+        scales = plane + kClUnitPlane;
+        return;
+    }
     const int head = rank >> 1, half = rank & 1;
     int m, row0;
     if (k < 2) {
@@ -474,10 +536,10 @@ __device__ __forceinline__ void cl_unit_src(const ClusterParams& p, int u, int r
     scales = reinterpret_cast<const uint8_t*>(L.scales[m] + static_cast<size_t>(row0) * (cols / 32));
 }
 
-template <bool kBf16>
+template <bool kBf16, bool kTc>
 __global__ void __launch_bounds__(kClThreads, 1)
     step_cluster_kernel(const __grid_constant__ CUtensorMap tm_kv16, const __grid_constant__ ClusterParams p) {
-    using Sh = ClShape<kBf16>;
+    using Sh = ClShape<kBf16, kTc>;
     constexpr int kW = Sh::kWSlots;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -495,16 +557,20 @@ __global__ void __launch_bounds__(kClThreads, 1)
     float* mine_s = reinterpret_cast<float*>(smem + Sh::kOffMine);
     float* wpart_s = reinterpret_cast<float*>(smem + Sh::kOffWPart);
     float2* rope_s = reinterpret_cast<float2*>(smem + Sh::kOffRope);
+    int32_t* red_s = reinterpret_cast<int32_t*>(smem + Sh::kOffRed);
     const uint32_t bar0 = smem_addr(smem + Sh::kOffBar);
-    const uint32_t wfull0 = bar0, wempty0 = bar0 + 8 * kW, nfull0 = bar0 + 16 * kW, nempty0 = nfull0 + 16,
-                   kfull0 = nfull0 + 32, kempty0 = kfull0 + 8 * kClKvSlots, xbar0 = kempty0 + 8 * kClKvSlots;
+    const uint32_t wfull0 = bar0, wempty0 = bar0 + 8 * kW, nfull = bar0 + 16 * kW, nempty = nfull + 8,
+                   kfull0 = nfull + 16, kempty0 = kfull0 + 8 * kClKvSlots, xbar0 = kempty0 + 8 * kClKvSlots,
+                   accum = xbar0 + 8 * kClExchanges;
     volatile int* failed = reinterpret_cast<volatile int*>(smem + Sh::kOffFlag);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Sh::kOffFlag + 4);
+    int* dig_e = reinterpret_cast<int*>(smem + Sh::kOffFlag + 8);
+    uint8_t* dig = smem + Sh::kOffDig;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rank = static_cast<int>(cluster_ctarank());
     const int head = rank >> 1, half = rank & 1;
     const int L = p.n_layers;
-    const int n_units = kClUnitsPerLayer * L;
     // Earlier keys [0, pos) live on pages [0, n_old); the head's two CTAs
     // take [0, n_first) and [n_first, n_old); this CTA's: [pg0, pg0 + npc).
     const int n_old = (p.pos + kPage - 1) / kPage;
@@ -519,15 +585,14 @@ __global__ void __launch_bounds__(kClThreads, 1)
             mbar_init(wfull0 + 8 * s, 1);
             mbar_init(wempty0 + 8 * s, kClWarps);
         }
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(nfull0 + 8 * s, 1);
-            mbar_init(nempty0 + 8 * s, 1);
-        }
+        mbar_init(nfull, 1);
+        mbar_init(nempty, 1);
         for (int s = 0; s < kClKvSlots; ++s) {
             mbar_init(kfull0 + 8 * s, 1);
             mbar_init(kempty0 + 8 * s, 1);
         }
-        for (int x = 0; x < 4; ++x) mbar_init(xbar0 + 8 * x, 1);
+        for (int x = 0; x < kClExchanges; ++x) mbar_init(xbar0 + 8 * x, 1);
+        mbar_init(accum, 4);  // kTc: the four issuing warps' commits
         *failed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -543,64 +608,59 @@ __global__ void __launch_bounds__(kClThreads, 1)
         const int* u = p.updates + 3 * threadIdx.x;
         const_cast<int32_t*>(p.kv.table)[static_cast<size_t>(u[0]) * p.kv.max_pages + u[1]] = u[2];
     }
+    if constexpr (kTc) {
+        // digit rows 4-15 of the B tiles stay zero; four 16-column TMEM accumulator blocks
+        for (int i = threadIdx.x; i < kClTcDigBytes / 16; i += kClThreads)
+            reinterpret_cast<uint4*>(dig)[i] = make_uint4(0u, 0u, 0u, 0u);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (warp == 1) {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 64;" ::"r"(smem_addr(tmem_slot))
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
+    }
     cluster_sync();  // barriers initialised in every CTA before any st.async reaches them
     CL_MARK(63, 1);
+    if constexpr (kTc) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
     if (warp == kClWarps) {
         // ------------------------------------------------------ copy warp
-        // L2 prefetch of the whole step: the CTA's weight units, then its
-        // head's K/V blocks of every layer (spread over the lanes).
-        for (int u = lane; u < n_units; u += 32) {
-            const uint8_t *plane, *scales;
-            cl_unit_src(p, u, rank, plane, scales);
-            prefetch_l2(plane, kClUnitPlane);
-            prefetch_l2(scales, kClUnitBytes - kClUnitPlane);
-        }
-        for (int n = lane; n < L * npc; n += 32) {
-            const int layer = n / npc, page = __ldcg(table + pg0 + n % npc);
-            for (int which = 0; which < 2; ++which) {
-                const long long off = kv_offset(p.kv, page, layer, which, head, 0);
-                prefetch_l2(static_cast<const uint8_t*>(p.kv.pool) + off * (kBf16 ? 2 : 4), Sh::kKvBlock);
-            }
-        }
-        __syncwarp();
         if (lane == 0) {
-            int w_last[kW], k_last[kClKvSlots], n_last[2];
+            int w_last[kW], k_last[kClKvSlots], n_last = -1;
             for (int s = 0; s < kW; ++s) w_last[s] = -1;
             for (int s = 0; s < kClKvSlots; ++s) k_last[s] = -1;
-            n_last[0] = n_last[1] = -1;
             int w_next = 0, k_next = 0;
             // Each issue waits (bounded) until the slot it refills has been
             // released by every consumer of its previous contents.
             auto issue_unit = [&]() {
                 const int u = w_next++, s = u % kW;
                 if (*failed) return;
-                if (u >= kW && !mbar_wait(wempty0 + 8 * s, ((u / kW) - 1) & 1, p.error, failed)) return;
+                if (u >= kW && !cl_copy_wait(wempty0 + 8 * s, ((u / kW) - 1) & 1, p.error, failed)) return;
                 const uint8_t *plane, *scales;
-                cl_unit_src(p, u, rank, plane, scales);
+                cl_unit_src<kTc>(p, u, rank, plane, scales);
                 uint8_t* dst = w_ring + s * kClUnitBytes;
                 mbar_expect_tx(wfull0 + 8 * s, kClUnitBytes);
                 bulk_load(smem_addr(dst), plane, kClUnitPlane, wfull0 + 8 * s);
                 bulk_load(smem_addr(dst + kClUnitPlane), scales, kClUnitBytes - kClUnitPlane, wfull0 + 8 * s);
                 w_last[s] = u;
             };
-            auto issue_norm = [&](int n) {  // norm n: layer n / 2, LN1 (even) or LN2 (odd)
-                const int s = n & 1;
+            // norm n: layer n / 2, LN1 (even) or LN2 (odd), through one slot
+            // (a layer's LN2 vectors are read ~5 us after its LN1 vectors)
+            auto issue_norm = [&](int n) {
                 if (*failed) return;
-                if (n >= 2 && !mbar_wait(nempty0 + 8 * s, ((n >> 1) - 1) & 1, p.error, failed)) return;
-                mbar_expect_tx(nfull0 + 8 * s, kClNormBytes);
+                if (n >= 1 && !cl_copy_wait(nempty, (n - 1) & 1, p.error, failed)) return;
+                mbar_expect_tx(nfull, kClNormBytes);
                 // weight and bias, each as 8 chunks of 64 floats into padded rows
                 const float* src = p.layers[n >> 1].norms + (n & 1) * 2 * kWidth;
-                uint8_t* dst = n_ring + s * kClNormPadBytes;
                 for (int k = 0; k < 16; ++k)
-                    bulk_load(smem_addr(dst + ((k >> 3) * kClRowPad + (k & 7) * kClChunk) * 4), src + 64 * k, 256,
-                              nfull0 + 8 * s);
-                n_last[s] = n;
+                    bulk_load(smem_addr(n_ring + ((k >> 3) * kClRowPad + (k & 7) * kClChunk) * 4), src + 64 * k, 256,
+                              nfull);
+                n_last = n;
             };
             auto issue_page = [&](int layer, int i) {  // page ring index k_next = layer * npc + i
                 const int n = k_next++, s = n % kClKvSlots;
                 if (*failed) return;
-                if (n >= kClKvSlots && !mbar_wait(kempty0 + 8 * s, ((n / kClKvSlots) - 1) & 1, p.error, failed))
+                if (n >= kClKvSlots && !cl_copy_wait(kempty0 + 8 * s, ((n / kClKvSlots) - 1) & 1, p.error, failed))
                     return;
                 const int page = __ldcg(table + pg0 + i);
                 const int row = (layer * p.kv.pool_pages + page) * 256 + head * kPage;  // K rows; V 128 rows on
@@ -615,9 +675,20 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 k_last[s] = n;
             };
             // The compute warps' consumption order, layer by layer.
+            auto prefetch_unit = [&](int u) {
+                const uint8_t *plane, *scales;
+                cl_unit_src<kTc>(p, u, rank, plane, scales);
+                prefetch_l2(plane, kClUnitPlane);
+                prefetch_l2(scales, kClUnitBytes - kClUnitPlane);
+            };
             for (int l = 0; l < L; ++l) {
                 issue_norm(2 * l);
                 for (int k = 0; k < kClUnitOut; ++k) issue_unit();
+                if (l == 0) prefetch_unit(kClUnitsPerLayer - 1);
+                if (l + 1 < L) {
+                    prefetch_unit(kClUnitsPerLayer * (l + 1) + kClUnitOut - 1);  // v
+                    prefetch_unit(kClUnitsPerLayer * (l + 2) - 1);                // last down unit
+                }
                 for (int i = 0; i < npc; ++i) issue_page(l, i);
                 issue_unit();  // out
                 issue_norm(2 * l + 1);
@@ -628,8 +699,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 if (w_last[s] >= 0) mbar_drain(wfull0 + 8 * s, (w_last[s] / kW) & 1);
             for (int s = 0; s < kClKvSlots; ++s)
                 if (k_last[s] >= 0) mbar_drain(kfull0 + 8 * s, (k_last[s] / kClKvSlots) & 1);
-            for (int s = 0; s < 2; ++s)
-                if (n_last[s] >= 0) mbar_drain(nfull0 + 8 * s, (n_last[s] >> 1) & 1);
+            if (n_last >= 0) mbar_drain(nfull, n_last & 1);
         }
         __syncwarp();
     } else {
@@ -654,29 +724,204 @@ __global__ void __launch_bounds__(kClThreads, 1)
             if (threadIdx.x == 0) mbar_expect_tx(xbar0 + 8 * x, bytes);
             return __all_sync(kFull, cl_exchange_wait(xbar0 + 8 * x, use & 1, p.error, failed));
         };
-        // LayerNorm of a 512-wide row (norm n of the ring) into xn_s, by one
-        // warp: LN1 by warp 1, LN2 by warp 0 (measured with clock64 on B200:
-        // LN1 on warp 0 took ~6,000 cycles from the second layer on, on warp 1
-        // ~1,800; LN2 on warp 0 ~1,700).
+        // LayerNorm of a 512-wide row (norm n of the ring) into xn_s, by warp
+        // 1, which shares its scheduler with no copy-warp polling (measured on
+        // B200: LN2 on warp 0 took 3.9 us per layer, LN1 on warp 1 1.0 us).
         auto layer_norm = [&](int n, const float* src) {
-            if (warp != ((n & 1) ? 0 : 1)) return;
-            const int s = n & 1;
-            if (__all_sync(kFull, mbar_wait(nfull0 + 8 * s, (n >> 1) & 1, p.error, failed))) {
-                const float* nw = reinterpret_cast<const float*>(n_ring + s * kClNormPadBytes);
+            if (warp != 1) return;
+            if (__all_sync(kFull, mbar_wait(nfull, n & 1, p.error, failed))) {
+                const float* nw = reinterpret_cast<const float*>(n_ring);
                 if (!cl_layernorm(src, nw, nw + kClRowPad, xn_s) && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(nempty0 + 8 * s);
+            if (lane == 0) mbar_arrive(nempty);
+        };
+        int cur_l = 0;  // the layer, for trace marks
+        // kTc, all compute warps: columns [k0, k0 + ncs) of the padded row
+        // `row` (ncols wide) as four base-128 digit rows into the B tiles,
+        // with the exponent of the whole row (every warp finds the row
+        // maximum; a row holding a non-finite value gives zero digits), as the
+        // batched tensor path slices its rows. Warp w, lane l: columns
+        // k0 + 64 w + 2 l and the next. Ends with the proxy fence that makes
+        // the digits visible to the MMA; a compute_sync follows.
+        auto tc_slice = [&](const float* row, int ncols, int k0, int ncs) {
+            float mx = 0.0f;
+            bool fin = true;
+            for (int i = 0; i < ncols / 128; ++i) {  // columns 128 i + 4 lane .. +3
+                const float4 f = *reinterpret_cast<const float4*>(row + cl_pad(128 * i + 4 * lane));
+                fin &= isfinite(f.x) && isfinite(f.y) && isfinite(f.z) && isfinite(f.w);
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+            const bool ok = __all_sync(kFull, fin);
+            bool zero;
+            const int e = digit_exponent(ok ? mx : 0.0f, zero);
+            const int c = 64 * warp + 2 * lane;  // column within [k0, k0 + ncs)
+            if (c < ncs) {
+                const float2 f = *reinterpret_cast<const float2*>(row + cl_pad(k0 + c));
+                const float down = pow2f(-e);
+                const uint32_t d0 = (ok && !zero) ? slice_digits(f.x * down) : 0u;
+                const uint32_t d1 = (ok && !zero) ? slice_digits(f.y * down) : 0u;
+                uint8_t* tile = dig + (c >> 7) * kClTcDigRowBytes + (c & 15);
+                const int chunk = (c & 127) >> 4;
+#pragma unroll
+                for (int j = 0; j < kDigits; ++j)  // SWIZZLE_128B: chunk q of row j at q ^ j
+                    *reinterpret_cast<uint16_t*>(tile + j * 128 + ((chunk ^ j) << 4)) =
+                        static_cast<uint16_t>(((d0 >> (8 * j)) & 0xffu) | (((d1 >> (8 * j)) & 0xffu) << 8));
+            }
+            if (threadIdx.x == 0) *dig_e = e;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        };
+        // kTc, warps 0-3: the MMAs of one projection (weights A, M = 128;
+        // digits B, N = 16), issued in parallel: with n = 4 units warp k
+        // issues unit k's four K = 32 steps, with n = 1 (out) step k of the
+        // one unit, into accumulator block k (TMEM columns [16 k, +16)), and
+        // commits to `accum` (four arrivals a phase). One thread issued them
+        // all at ~0.35 us per unit. Every unit but the last (whose tail holds
+        // the row scales the epilogue reads) is released by a commit that
+        // follows its MMAs plus seven arrivals, so its slot refills as soon as
+        // the tensor core has read it; the last is released by all eight warps.
+        auto tc_mma = [&](int u_first, int n, int mark) {
+            const uint32_t tmem = *tmem_slot + 16 * warp;
+            constexpr uint32_t idesc = umma_idesc_i8(kGemmM, 16);
+            const int u = u_first + (n == 4 ? warp : 0);
+            if (wait_unit(u)) {
+                if (warp == 1) CL_MARK_T(32, cur_l, mark);
+                if (lane == 0) {
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t a0 = smem_addr(unit_ptr(u)), b0 = smem_addr(dig + (n == 4 ? warp : 0) * kClTcDigRowBytes);
+                    if (n == 4) {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)  // K = 32 bytes per MMA
+                            umma_i8(tmem, umma_desc_sw128(a0 + 32 * kk), umma_desc_sw128(b0 + 32 * kk), idesc, kk != 0);
+                        if (warp < 3) {
+                            umma_commit(wempty0 + 8 * (u % kW));
+                            mbar_arrive_count(wempty0 + 8 * (u % kW), kClWarps - 1);
+                        }
+                    } else {
+                        umma_i8(tmem, umma_desc_sw128(a0 + 32 * warp), umma_desc_sw128(b0 + 32 * warp), idesc, 0u);
+                    }
+                }
+            }
+            if (lane == 0) umma_commit(accum);
+            __syncwarp();
+            if (warp == 1) CL_MARK_T(32, cur_l, mark + 1);
+        };
+        // kTc, warps 0-3: the four digit sums of row 32 warp + lane of the
+        // projection's 128 rows (TMEM lane quarter `warp`): the four
+        // accumulator blocks added (exact in int32), once `accum` completes the
+        // phase of this parity.
+        auto tc_sums = [&](int parity, uint32_t (&d)[4], int mark) {
+            if (!__all_sync(kFull, mbar_wait(accum, parity, p.error, failed))) return false;
+            CL_MARK_T(0, cur_l, mark);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t t0 = *tmem_slot + (static_cast<uint32_t>(32 * warp) << 16);
+            uint32_t r[4][4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(r[k][0]), "=r"(r[k][1]), "=r"(r[k][2]), "=r"(r[k][3])
+                             : "r"(t0 + 16 * k));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d[j] = r[0][j] + r[1][j] + r[2][j] + r[3][j];
+            return true;
+        };
+        // Digit sums recombined as i8_gemm_kernel's epilogue does, times the
+        // row scale: row i of the 128 rows of unit u's tail.
+        auto tc_finish = [&](const uint32_t (&d)[4], int u, int i) {
+            const int e = *dig_e;
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kDigits; ++j)
+                acc = fmaf(static_cast<float>(static_cast<int32_t>(d[j])), pow2f(e - 7 * (j + 1)), acc);
+            return acc * reinterpret_cast<const float*>(unit_ptr(u) + kClUnitPlane)[i];
+        };
+        // kTc, split over K (out, down): warps 0-3 send the digit sums of rows
+        // [32 w, +32) of the row group to CTA (rank & ~3) + w; warp 0 of the
+        // owner adds the four senders' sums (exact in int32) and returns its
+        // row 32 rank + lane, scaled with the holder unit u's row scales.
+        auto tc_reduce = [&](int parity, int use, int u, float& y, int mark) {
+            uint32_t d[4];
+            if (warp < 4 && tc_sums(parity, d, mark) && !*failed) {
+                const uint32_t dst = smem_addr(red_s) + (((rank & 3) * 32 + lane) * 4) * 4;
+                st_async4(dst, xbar0 + 8 * CLX_R, (rank & ~3) + warp,
+                          make_float4(__uint_as_float(d[0]), __uint_as_float(d[1]), __uint_as_float(d[2]),
+                                      __uint_as_float(d[3])));
+            }
+            if (warp != 0 || !exchange_wait(CLX_R, kClBytesR, use)) return false;
+            CL_MARK(cur_l, mark + 1);
+            uint32_t t[4];
+#pragma unroll
+            for (int j = 0; j < kDigits; ++j) {
+                int32_t sum = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) sum += red_s[(q * 32 + lane) * 4 + j];
+                t[j] = static_cast<uint32_t>(sum);
+            }
+            y = tc_finish(t, u, 32 * (rank & 3) + lane);
+            return true;
+        };
+        // One row per lane (rows r0 + lane) of a warp into exchange x of every
+        // CTA: rows 4m .. 4m+3 (m = lane % 8) gathered from lanes 4m .. 4m+3
+        // and pushed by lane l to CTAs l / 8 + 4i.
+        auto push_rows = [&](uint32_t buf, int x, int r0, float v) {
+            const int m = lane & 7;
+            const float4 v4 = make_float4(__shfl_sync(kFull, v, 4 * m), __shfl_sync(kFull, v, 4 * m + 1),
+                                          __shfl_sync(kFull, v, 4 * m + 2), __shfl_sync(kFull, v, 4 * m + 3));
+            if (*failed) return;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) st_async4(buf + cl_pad(r0 + 4 * m) * 4, xbar0 + 8 * x, (lane >> 3) + 4 * i, v4);
         };
 
         for (int l = 0; l < L; ++l) {
             const int u0 = kClUnitsPerLayer * l;
             const bool last_layer = l == L - 1;
+            cur_l = l;
+            (void)cur_l;
 
             // ---- A: LN1 -> q (64), k, v (the CTA's 32 dims) of the head
             if (l > 0) exchange_wait(CLX_X, kClBytesX, l - 1);
             CL_MARK(l, 0);
             layer_norm(2 * l, x_s);
+            if constexpr (kTc) {
+                compute_sync();
+                CL_MARK_T(32, l, 12);
+                tc_slice(xn_s, kWidth, 0, kWidth);
+                compute_sync();
+                CL_MARK_T(32, l, 13);
+                if (warp < 4) tc_mma(u0, 4, 14);
+                CL_MARK(l, 1);
+                uint32_t d[4];
+                if (warp < 4 && tc_sums(0, d, 11)) {
+                    float y = tc_finish(d, u0 + 3, 32 * warp + lane);
+                    // warps 0, 1: q dims [32 warp, +32); 2: k, 3: v, dims [32 half, +32)
+                    const int d = (warp < 2 ? 32 * warp : 32 * half) + lane;
+                    if (warp < 3) {  // RoPE pairs (2i, 2i+1) in adjacent lanes
+                        const float other = __shfl_xor_sync(kFull, y, 1);
+                        float a = (lane & 1) ? other : y, b = (lane & 1) ? y : other;
+                        rope_apply(a, b, rope_s[d >> 1]);
+                        y = (lane & 1) ? b : a;
+                    }
+                    if (!__all_sync(kFull, isfinite(y)) && lane == 0) flag_nonfinite(p.status, 0);
+                    if (warp < 2) {
+                        q_s[d] = y;
+                    } else {
+                        const int which = warp - 2;
+                        const long long off = kv_offset(p.kv, p.last_page, l, which, head, p.pos % kPage) + d;
+                        if (kBf16) {  // the current key joins the softmax as the cache holds it
+                            const uint16_t hb = f32_to_bf16(y);
+                            static_cast<uint16_t*>(p.kv.pool)[off] = hb;
+                            y = bf16_to_f32(hb);
+                        } else {
+                            static_cast<float*>(p.kv.pool)[off] = y;
+                        }
+                        self_s[32 * which + lane] = y;
+                    }
+                }
+                release_unit(u0 + 3);  // the scale holder: warps 0-3 after their reads
+            } else {
             compute_sync();
             CL_MARK(l, 1);
             for (int k0 = 0; k0 < kClUnitOut; k0 += 2) {
@@ -718,6 +963,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 release_unit(u0 + k0);
                 release_unit(u0 + k0 + 1);
             }
+            }
             compute_sync();
             CL_MARK(l, 2);
 
@@ -740,7 +986,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 }
             }
             compute_sync();
-            if (warp == 0) {  // the CTA's message: warps merged in page order, the current key's halves
+            if (warp == 1) {  // the CTA's message: warps merged in page order, the current key's halves
                 float M = -INFINITY, S = 0.0f, A0 = 0.0f, A1 = 0.0f;
                 for (int w = 0; w < kClWarps && w < npc; ++w) {
                     const float* wp = wpart_s + w * kClPartStride;
@@ -800,7 +1046,20 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 if (!__all_sync(kFull, ok) && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
             }
             compute_sync();
-            {
+            if constexpr (kTc) {
+                // rows [128 (rank / 4), +128) over columns [128 (rank % 4), +128)
+                tc_slice(a_s, kWidth, 128 * (rank & 3), 128);
+                compute_sync();
+                if (warp < 4) tc_mma(u0 + kClUnitOut, 1, 27);
+                float y;
+                if (tc_reduce(1, 2 * l, u0 + kClUnitOut, y, 29)) {
+                    const int r = 32 * rank + lane;
+                    const float h = __fadd_rn(x_s[cl_pad(r)], y);
+                    if (!__all_sync(kFull, isfinite(h)) && lane == 0) flag_nonfinite(p.status, 0);
+                    push_rows(h_addr, CLX_H, 32 * rank, h);
+                }
+                release_unit(u0 + kClUnitOut);
+            } else {
                 const int u = u0 + kClUnitOut;
                 if (wait_unit(u)) {
                     const float4 s = cl_rows4(unit_ptr(u), warp, a_s, 1);
@@ -820,6 +1079,23 @@ __global__ void __launch_bounds__(kClThreads, 1)
             exchange_wait(CLX_H, kClBytesH, l);
             CL_MARK(l, 6);
             layer_norm(2 * l + 1, h_s);
+            if constexpr (kTc) {
+                compute_sync();
+                CL_MARK_T(32, l, 16);
+                tc_slice(xn_s, kWidth, 0, kWidth);
+                compute_sync();
+                CL_MARK_T(32, l, 17);
+                if (warp < 4) tc_mma(u0 + kClUnitUp, 4, 18);
+                CL_MARK(l, 7);
+                uint32_t d[4];
+                if (warp < 4 && tc_sums(0, d, 22)) {
+                    const float y = tc_finish(d, u0 + kClUnitUp + 3, 32 * warp + lane);
+                    const float gm = gelu_erf(y);
+                    if (!__all_sync(kFull, isfinite(y) && isfinite(gm)) && lane == 0) flag_nonfinite(p.status, 0);
+                    push_rows(g_addr, CLX_G, 128 * rank + 32 * warp, gm);
+                }
+                release_unit(u0 + kClUnitUp + 3);
+            } else {
             compute_sync();
             CL_MARK(l, 7);
             for (int k0 = 0; k0 < 4; k0 += 2) {
@@ -848,12 +1124,29 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 release_unit(ua);
                 release_unit(ua + 1);
             }
+            }
             CL_MARK(l, 8);
 
             // ---- E: x' = h + g Wdown^T, slices to every CTA (the last layer: to `out`)
             exchange_wait(CLX_G, kClBytesG, l);
             CL_MARK(l, 9);
-            {
+            if constexpr (kTc) {
+                // rows [128 (rank / 4), +128) over columns [512 (rank % 4), +512)
+                tc_slice(g_s, kFfn, 512 * (rank & 3), 512);
+                compute_sync();
+                CL_MARK_T(32, l, 20);
+                if (warp < 4) tc_mma(u0 + kClUnitDown, 4, 23);
+                float y;
+                if (tc_reduce(1, 2 * l + 1, u0 + kClUnitDown + 3, y, 25)) {
+                    const int r = 32 * rank + lane;
+                    const float x = __fadd_rn(h_s[cl_pad(r)], y);
+                    if (!__all_sync(kFull, isfinite(x)) && lane == 0) flag_nonfinite(p.status, 0);
+                    if (p.trace) p.trace[static_cast<size_t>(l) * p.trace_stride + r] = x;
+                    if (last_layer) p.out[r] = x;
+                    else push_rows(x_addr, CLX_X, 32 * rank, x);
+                }
+                release_unit(u0 + kClUnitDown + 3);
+            } else {
                 const int u = u0 + kClUnitDown + (warp >> 1);
                 if (wait_unit(u)) {
                     const float4 s = cl_rows4(unit_ptr(u), warp & 1, g_s, 4);
@@ -886,7 +1179,59 @@ __global__ void __launch_bounds__(kClThreads, 1)
         }
     }
     // No CTA exits while another may still store into its shared memory.
+    if constexpr (kTc) asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     cluster_sync();
+    if constexpr (kTc) {
+        if (warp == 1) {
+            // the last accumulator phase before the columns are
+            // freed; bounded, for MMAs left running after a failure
+            if (lane == 0) mbar_drain(accum, 1);  // 4 L commits: the last phase is odd
+            __syncwarp();
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 64;" ::"r"(*tmem_slot) : "memory");
+        }
+    }
+}
+
+// Tensor-core units of one layer for step_cluster_kernel<kBf16, true>, in the
+// order the step consumes them (unit k of CTA rank at (rank * 13 + k) *
+// kClUnitBytes): k < 4: K slice k of the CTA's 128 q/k/v rows (q rows
+// [64 head, +64), k and v rows of dims [32 half, +32) of the head); k = 4:
+// columns [128 (rank % 4), +128) of out rows [128 (rank / 4), +128);
+// 5 <= k < 9: K slice k - 5 of up rows [128 rank, +128); k >= 9: columns
+// [512 (rank % 4) + 128 (k - 9), +128) of down rows [128 (rank / 4), +128).
+// Each unit: a 128-row x 128-byte SWIZZLE_128B tile (row i at
+// (i / 8) * 1024 + (i % 8) * 128, 16-byte chunk c at position c ^ (i % 8))
+// from the natural int8 planes, then the 128 fp32 row scales, then zeros to
+// kClUnitBytes. One CTA per unit, 256 threads.
+struct ClTcSource {
+    const int8_t* w[4];     // natural int8 planes: qkv, out, up, down
+    const float* scale[4];  // their row scales
+};
+
+__global__ void cluster_tc_pack_kernel(const ClTcSource src, uint8_t* __restrict__ dst) {
+    const int rank = blockIdx.x / kClTcUnits, k = blockIdx.x % kClTcUnits;
+    const int head = rank >> 1, half = rank & 1, group = rank >> 2, quarter = rank & 3;
+    uint8_t* out = dst + static_cast<size_t>(blockIdx.x) * kClUnitBytes;
+    const int m = k < kClUnitOut ? PM_QKV : k == kClUnitOut ? PM_OUT : k < kClUnitDown ? PM_UP : PM_DOWN;
+    const int cols = m == PM_DOWN ? kFfn : kWidth;
+    const int col0 = m == PM_QKV ? 128 * k
+                   : m == PM_OUT ? 128 * quarter
+                   : m == PM_UP  ? 128 * (k - kClUnitUp)
+                                 : 512 * quarter + 128 * (k - kClUnitDown);
+    auto src_row = [&](int i) {
+        if (m == PM_OUT || m == PM_DOWN) return 128 * group + i;
+        if (m == PM_UP) return 128 * rank + i;
+        if (i < 64) return head * kHeadDim + i;
+        return (i < 96 ? kWidth : 2 * kWidth) + head * kHeadDim + half * 32 + (i & 31);
+    };
+    for (int q = threadIdx.x; q < 128 * 8; q += blockDim.x) {
+        const int i = q >> 3, c = q & 7;
+        const uint4 v = *reinterpret_cast<const uint4*>(src.w[m] + static_cast<size_t>(src_row(i)) * cols + col0 + 16 * c);
+        *reinterpret_cast<uint4*>(out + (i >> 3) * 1024 + (i & 7) * 128 + ((c ^ (i & 7)) << 4)) = v;
+    }
+    for (int i = threadIdx.x; i < (kClUnitBytes - kClUnitPlane) / 4; i += blockDim.x)
+        reinterpret_cast<float*>(out + kClUnitPlane)[i] = i < 128 ? src.scale[m][src_row(i)] : 0.0f;
 }
 
 }  // namespace phonon

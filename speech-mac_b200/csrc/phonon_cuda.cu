@@ -483,6 +483,11 @@ struct PhononCuda {
     // position below cluster_max_pos take that path when cluster_ok.
     CUtensorMap tm_kv16;
     bool cluster_ok = false;
+    // ... with every projection on the tensor cores when every layer's
+    // weights have one scale per row (d_cltc: their K-slice units,
+    // cluster_tc_pack_kernel)
+    bool cluster_tc = false;
+    uint8_t* d_cltc = nullptr;
     uint32_t cluster_max_pos = PHONON_CUDA_MAX_POSITIONS;
     Lane lanes[2];
     bool lane1_ok = false;  // second lane allocated
@@ -1298,12 +1303,12 @@ int enqueue_persist(PhononCuda* c, const Batch& b, const float* in, float* final
     return PHONON_CUDA_OK;
 }
 
-template <bool kBf16>
+template <bool kBf16, bool kTc>
 cudaLaunchConfig_t cluster_config(cudaStream_t s, cudaLaunchAttribute* at) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(kClusterCtas);
     cfg.blockDim = dim3(kClThreads);
-    cfg.dynamicSmemBytes = static_cast<size_t>(ClShape<kBf16>::kSmem);
+    cfg.dynamicSmemBytes = static_cast<size_t>(ClShape<kBf16, kTc>::kSmem);
     cfg.stream = s;
     at[0].id = cudaLaunchAttributeClusterDimension;  // the whole grid is one cluster
     at[0].val.clusterDim.x = kClusterCtas;
@@ -1316,18 +1321,18 @@ cudaLaunchConfig_t cluster_config(cudaStream_t s, cudaLaunchAttribute* at) {
 
 // Opt the cluster kernel into its shared memory and a 16-CTA cluster, and
 // check that such a cluster can be resident on this device.
-template <bool kBf16>
+template <bool kBf16, bool kTc>
 bool cluster_launchable() {
-    const void* fn = reinterpret_cast<const void*>(step_cluster_kernel<kBf16>);
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ClShape<kBf16>::kSmem) != cudaSuccess ||
+    const void* fn = reinterpret_cast<const void*>(step_cluster_kernel<kBf16, kTc>);
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ClShape<kBf16, kTc>::kSmem) != cudaSuccess ||
         cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
     cudaLaunchAttribute at[1];
-    cudaLaunchConfig_t cfg = cluster_config<kBf16>(nullptr, at);
+    cudaLaunchConfig_t cfg = cluster_config<kBf16, kTc>(nullptr, at);
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, step_cluster_kernel<kBf16>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, step_cluster_kernel<kBf16, kTc>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
@@ -1347,6 +1352,7 @@ int enqueue_cluster(PhononCuda* c, int32_t slot, int32_t pos, const std::vector<
     const bool bf16 = c->cfg.kv_type == PHONON_CUDA_KV_BF16;
     ClusterParams cp{};
     cp.layers = c->d_players;
+    cp.tc = c->d_cltc;
     cp.n_layers = static_cast<int>(c->cfg.n_layers);
     cp.in = in;
     cp.out = out;
@@ -1368,12 +1374,18 @@ int enqueue_cluster(PhononCuda* c, int32_t slot, int32_t pos, const std::vector<
     const double bytes = weights + cp.n_layers * (pos + 2.0) * 2.0 * kWidth * esize + 2.0 * kWidth * 4.0;
     LaunchScope ls(c, PHONON_CUDA_K_FUSED, bytes, c->stream);
     cudaLaunchAttribute at[1];
-    if (bf16) {
-        cudaLaunchConfig_t cfg = cluster_config<true>(c->stream, at);
-        CUDA_TRY(cudaLaunchKernelEx(&cfg, step_cluster_kernel<true>, c->tm_kv16, cp));
+    if (bf16 && c->cluster_tc) {
+        cudaLaunchConfig_t cfg = cluster_config<true, true>(c->stream, at);
+        CUDA_TRY(cudaLaunchKernelEx(&cfg, step_cluster_kernel<true, true>, c->tm_kv16, cp));
+    } else if (bf16) {
+        cudaLaunchConfig_t cfg = cluster_config<true, false>(c->stream, at);
+        CUDA_TRY(cudaLaunchKernelEx(&cfg, step_cluster_kernel<true, false>, c->tm_kv16, cp));
+    } else if (c->cluster_tc) {
+        cudaLaunchConfig_t cfg = cluster_config<false, true>(c->stream, at);
+        CUDA_TRY(cudaLaunchKernelEx(&cfg, step_cluster_kernel<false, true>, c->tm_kv16, cp));
     } else {
-        cudaLaunchConfig_t cfg = cluster_config<false>(c->stream, at);
-        CUDA_TRY(cudaLaunchKernelEx(&cfg, step_cluster_kernel<false>, c->tm_kv16, cp));
+        cudaLaunchConfig_t cfg = cluster_config<false, false>(c->stream, at);
+        CUDA_TRY(cudaLaunchKernelEx(&cfg, step_cluster_kernel<false, false>, c->tm_kv16, cp));
     }
     return PHONON_CUDA_OK;
 }
@@ -1521,8 +1533,37 @@ int refresh_persist(PhononCuda* c) {
         const DevLinear* lin[4] = {&D.qkv, &D.out, &D.up, &D.down};
         for (int m = 0; m < 4; ++m) cl = cl && D.q8 && lin[m]->fast && lin[m]->plane && lin[m]->scales;
     }
-    if (cl) cl = c->cfg.kv_type == PHONON_CUDA_KV_BF16 ? cluster_launchable<true>() : cluster_launchable<false>();
+    const bool bf16 = c->cfg.kv_type == PHONON_CUDA_KV_BF16;
+    if (cl) cl = bf16 ? cluster_launchable<true, false>() : cluster_launchable<false, false>();
     c->cluster_ok = cl;
+    // Its tensor-core form: one scale per row in every layer's four linears.
+    bool tc = cl && c->tensor_ok;
+    for (const DevLayer& D : c->layers)
+        tc = tc && D.qkv.tensor && D.qkv.wd == 1 && D.qkv.rows == 3 * kWidth && D.qkv.cols == kWidth && D.out.tensor &&
+             D.out.wd == 1 && D.out.rows == kWidth && D.out.cols == kWidth && D.up.tensor && D.up.wd == 1 &&
+             D.up.rows == kFfn && D.up.cols == kWidth && D.down.tensor && D.down.wd == 1 && D.down.rows == kWidth &&
+             D.down.cols == kFfn;
+    if (tc) tc = bf16 ? cluster_launchable<true, true>() : cluster_launchable<false, true>();
+    if (tc && !c->d_cltc) {
+        const size_t bytes = c->layers.size() * kClusterCtas * kClTcUnits * static_cast<size_t>(kClUnitBytes);
+        if (cudaMalloc(&c->d_cltc, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            c->d_cltc = nullptr;
+            tc = false;
+        }
+    }
+    if (tc) {
+        for (size_t l = 0; l < c->layers.size(); ++l) {
+            const DevLayer& D = c->layers[l];
+            const ClTcSource src{{D.qkv.nat, D.out.nat, D.up.nat, D.down.nat},
+                                 {D.qkv.row_scale, D.out.row_scale, D.up.row_scale, D.down.row_scale}};
+            cluster_tc_pack_kernel<<<kClusterCtas * kClTcUnits, 256, 0, c->stream>>>(
+                src, c->d_cltc + l * kClusterCtas * kClTcUnits * static_cast<size_t>(kClUnitBytes));
+            CUDA_TRY(cudaGetLastError());
+        }
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+    }
+    c->cluster_tc = tc;
     return PHONON_CUDA_OK;
 }
 
@@ -1540,7 +1581,7 @@ void destroy_context(PhononCuda* c) {
     void* dev[] = {c->kv_pool, c->d_table, c->d_freq, c->d_x0, c->d_x1, c->d_y, c->d_q, c->d_a,
                    c->d_h, c->d_g, c->d_part, c->d_stage, c->d_meta, c->d_status,
                    c->d_dig512, c->d_dig2048, c->d_exps, c->d_err, c->d_rope,
-                   c->d_players, c->d_bar};
+                   c->d_players, c->d_bar, c->d_cltc};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {c->h_meta, c->h_x, c->h_y, c->h_stage, c->h_status};
@@ -1935,7 +1976,7 @@ int phonon_cuda_set_cluster_step(PhononCuda* c, uint32_t max_position, int* avai
     std::lock_guard<std::mutex> g(c->mu);
     if (c->pending) return PHONON_CUDA_INVALID_ARGUMENT;
     c->cluster_max_pos = max_position;
-    if (available) *available = c->cluster_ok ? 1 : 0;
+    if (available) *available = c->cluster_ok ? (c->cluster_tc ? 2 : 1) : 0;
     drop_graph(c);
     return PHONON_CUDA_OK;
 }

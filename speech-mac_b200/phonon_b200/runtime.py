@@ -299,11 +299,13 @@ class Context:
 
     def set_cluster_step(self, max_position=8192):
         """Single-stream steps at positions below max_position run on one
-        16-CTA cluster (0 disables it). Returns whether the context can run
-        that path at all."""
+        16-CTA cluster (0 disables it). Returns 0 when the context cannot run
+        that path, 1 when it runs it with every projection on the CUDA cores,
+        2 when its projections run on the tensor cores (weights with one
+        scale per row)."""
         available = C.c_int(0)
         check(self.L.phonon_cuda_set_cluster_step(self.h, max_position, C.byref(available)), "set_cluster_step")
-        return bool(available.value)
+        return available.value
 
     def set_layer_trace(self, trace_ptr, max_rows):
         """Every later decode step also writes each layer's output rows into

@@ -20,7 +20,15 @@ count for four arrivals), under random interleavings, and checks that
 
 Mbarriers are modelled by their completed-phase count; a copy completes its
 full barrier when issued (the latency does not change the protocol); an
-exchange with the other CTAs is a meeting point of the compute warps."""
+exchange with the other CTAs is a meeting point of the compute warps.
+
+In the tensor-core form (tc) every projection is an MMA issued by warps
+0-3: for the four-unit projections (q/k/v, up, down) warp k waits for unit
+k, issues its MMAs and commits them to an accumulator barrier (four arrivals
+a phase); units 0-2 are released by a commit after their MMAs (modelled as
+all eight arrivals at issue); for out, all four warps wait for the one unit.
+The last unit (the row scales' holder) is released by all eight warps, warps
+0-3 after they waited for the accumulator."""
 import random
 
 import pytest
@@ -43,11 +51,12 @@ class Bar:
             self.pending = self.count
 
 
-def run(L, npc, w_slots, seed, wait_release=True):
+def run(L, npc, w_slots, seed, wait_release=True, tc=False):
     rnd = random.Random(seed)
     wfull = [Bar(1) for _ in range(w_slots)]
     wempty = [Bar(WARPS) for _ in range(w_slots)]
-    nfull, nempty = [Bar(1), Bar(1)], [Bar(1), Bar(1)]
+    nfull, nempty = Bar(1), Bar(1)  # one LayerNorm slot
+    accum = Bar(4)
     kfull = [Bar(1) for _ in range(KV_SLOTS)]
     kempty = [Bar(1) for _ in range(KV_SLOTS)]
     loaded = {}  # (ring, slot) -> index held and not yet released
@@ -76,9 +85,9 @@ def run(L, npc, w_slots, seed, wait_release=True):
             issue("w", u, w_slots, wfull)
 
         def norm(n):
-            if n >= 2:
-                yield ("wait", nempty[n & 1], (n >> 1) - 1)
-            issue("n", n, 2, nfull)
+            if n >= 1:
+                yield ("wait", nempty, n - 1)
+            issue("n", n, 1, [nfull])
 
         def page():
             n = state["k"]
@@ -101,19 +110,33 @@ def run(L, npc, w_slots, seed, wait_release=True):
     def wait_unit(u):
         yield ("wait", wfull[u % w_slots], u // w_slots)
 
+    def projection(w, l, first, use, n=4):
+        if tc:
+            yield ("meet",)  # the digit rows sliced by all warps
+            if w < 4:  # warp w's MMAs, their commit
+                u = first + (w if n == 4 else 0)
+                yield from wait_unit(u)
+                if n == 4 and w < 3:
+                    release("w", u, w_slots, wempty, WARPS, weight=WARPS)
+                accum.arrive()
+                yield ("wait", accum, use)
+            release("w", first + n - 1, w_slots, wempty, WARPS)
+        else:
+            yield ("meet",)
+            for k0 in (0, 2):  # units in pairs
+                yield from wait_unit(first + k0)
+                yield from wait_unit(first + k0 + 1)
+                release("w", first + k0, w_slots, wempty, WARPS)
+                release("w", first + k0 + 1, w_slots, wempty, WARPS)
+
     def compute_warp(w):
         for l in range(L):
             u0 = UNITS_PER_LAYER * l
             yield ("meet",)  # exchange of x (layer l > 0)
-            if w == 0:  # LN1
-                yield ("wait", nfull[(2 * l) & 1], l)
-                release("n", 2 * l, 2, nempty, 1)
-            yield ("meet",)
-            for k0 in (0, 2):  # QKV units in pairs
-                yield from wait_unit(u0 + k0)
-                yield from wait_unit(u0 + k0 + 1)
-                release("w", u0 + k0, w_slots, wempty, WARPS)
-                release("w", u0 + k0 + 1, w_slots, wempty, WARPS)
+            if w == 1:  # LN1
+                yield ("wait", nfull, 2 * l)
+                release("n", 2 * l, 1, [nempty], 1)
+            yield from projection(w, l, u0, 4 * l)  # q/k/v
             yield ("meet",)
             for i in range(w, npc, WARPS):  # B: pages w, w + 8, ...
                 n = l * npc + i
@@ -121,22 +144,23 @@ def run(L, npc, w_slots, seed, wait_release=True):
                 release("k", n, KV_SLOTS, kempty, 1)
             yield ("meet",)  # warp partials merged, message sent
             yield ("meet",)  # exchange of the messages, merge of the heads
-            yield from wait_unit(u0 + UNIT_OUT)
-            release("w", u0 + UNIT_OUT, w_slots, wempty, WARPS)
+            if tc:
+                yield from projection(w, l, u0 + UNIT_OUT, 4 * l + 1, n=1)
+            else:
+                yield from wait_unit(u0 + UNIT_OUT)
+                release("w", u0 + UNIT_OUT, w_slots, wempty, WARPS)
             yield ("meet",)  # exchange of h
-            if w == 0:  # LN2
-                yield ("wait", nfull[(2 * l + 1) & 1], l)
-                release("n", 2 * l + 1, 2, nempty, 1)
-            yield ("meet",)
-            for k0 in (0, 2):  # up units in pairs
-                yield from wait_unit(u0 + UNIT_UP + k0)
-                yield from wait_unit(u0 + UNIT_UP + k0 + 1)
-                release("w", u0 + UNIT_UP + k0, w_slots, wempty, WARPS)
-                release("w", u0 + UNIT_UP + k0 + 1, w_slots, wempty, WARPS)
+            if w == 1:  # LN2
+                yield ("wait", nfull, 2 * l + 1)
+                release("n", 2 * l + 1, 1, [nempty], 1)
+            yield from projection(w, l, u0 + UNIT_UP, 4 * l + 2)  # up
             yield ("meet",)  # exchange of g
-            u = u0 + UNIT_DOWN + (w >> 1)  # E: a down unit is read by two warps, four arrivals each
-            yield from wait_unit(u)
-            release("w", u, w_slots, wempty, WARPS, weight=WARPS // 2)
+            if tc:
+                yield from projection(w, l, u0 + UNIT_DOWN, 4 * l + 3)
+            else:
+                u = u0 + UNIT_DOWN + (w >> 1)  # E: a down unit is read by two warps, four arrivals each
+                yield from wait_unit(u)
+                release("w", u, w_slots, wempty, WARPS, weight=WARPS // 2)
 
     actors = {"copy": copy_warp(), **{f"w{w}": compute_warp(w) for w in range(WARPS)}}
     blocked = {a: None for a in actors}
@@ -170,17 +194,19 @@ def run(L, npc, w_slots, seed, wait_release=True):
             blocked[a] = None
 
 
-@pytest.mark.parametrize("w_slots", [7, 9])  # fp32 and bf16 K/V
+@pytest.mark.parametrize("tc", [False, True])  # CUDA-core rows, tensor-core q/k/v and up
+@pytest.mark.parametrize("w_slots", [7, 8, 9])  # fp32 K/V, bf16 K/V (tensor-core form: 8)
 @pytest.mark.parametrize("L", [1, 2, 12])
 @pytest.mark.parametrize("npc", [0, 1, 5, 8, 9, 17, 64])
-def test_cluster_rings_never_deadlock_or_alias(L, npc, w_slots):
+def test_cluster_rings_never_deadlock_or_alias(L, npc, w_slots, tc):
     for seed in range(3):
-        run(L, npc, w_slots, seed)
+        run(L, npc, w_slots, seed, tc=tc)
 
 
 def test_model_catches_a_refill_before_release():
     """The checker itself: a copy warp that refills a weight slot without
     waiting for its consumers' release is rejected."""
-    with pytest.raises(AssertionError):
-        for seed in range(10):
-            run(2, 4, 7, seed, wait_release=False)
+    for tc in (False, True):
+        with pytest.raises(AssertionError):
+            for seed in range(10):
+                run(2, 4, 7, seed, wait_release=False, tc=tc)
