@@ -739,22 +739,41 @@ __global__ void __launch_bounds__(kClThreads, 1)
         int cur_l = 0;  // the layer, for trace marks
         // kTc, all compute warps: columns [k0, k0 + ncs) of the padded row
         // `row` (ncols wide) as four base-128 digit rows into the B tiles,
-        // with the exponent of the whole row (every warp finds the row
-        // maximum; a row holding a non-finite value gives zero digits), as the
-        // batched tensor path slices its rows. Warp w, lane l: columns
-        // k0 + 64 w + 2 l and the next. Ends with the proxy fence that makes
-        // the digits visible to the MMA; a compute_sync follows.
+        // with the exponent of the whole row (a row holding a non-finite value
+        // gives zero digits), as the batched tensor path slices its rows. The
+        // row maximum of a 512-wide row: every warp over the whole row; of the
+        // 2048-wide row: warp w over columns [256 w, +256), combined through
+        // the warp-partial buffer (free outside the attention stage) -- one
+        // named barrier more, which costs a 512-wide row more than it saves.
+        // The slicing: warp w, lane l, columns k0 + 64 w + 2 l and the next.
+        // Ends with the proxy fence that makes the digits visible to the MMA;
+        // a compute_sync follows.
         auto tc_slice = [&](const float* row, int ncols, int k0, int ncs) {
+            const bool split = ncols > kWidth;
+            const int span = split ? ncols / kClWarps : ncols;  // columns of this warp's maximum
+            const int c0 = split ? span * warp : 0;
             float mx = 0.0f;
             bool fin = true;
-            for (int i = 0; i < ncols / 128; ++i) {  // columns 128 i + 4 lane .. +3
-                const float4 f = *reinterpret_cast<const float4*>(row + cl_pad(128 * i + 4 * lane));
+            for (int i = 0; i < span / 128; ++i) {  // columns c0 + 128 i + 4 lane .. +3
+                const float4 f = *reinterpret_cast<const float4*>(row + cl_pad(c0 + 128 * i + 4 * lane));
                 fin &= isfinite(f.x) && isfinite(f.y) && isfinite(f.z) && isfinite(f.w);
                 mx = fmaxf(mx, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
-            const bool ok = __all_sync(kFull, fin);
+            bool ok = __all_sync(kFull, fin);
+            if (split) {
+                if (lane == 0) {
+                    wpart_s[warp * kClPartStride] = mx;
+                    wpart_s[warp * kClPartStride + 1] = ok ? 1.0f : 0.0f;
+                }
+                compute_sync();
+#pragma unroll
+                for (int w = 0; w < kClWarps; ++w) {
+                    mx = fmaxf(mx, wpart_s[w * kClPartStride]);
+                    ok &= wpart_s[w * kClPartStride + 1] != 0.0f;
+                }
+            }
             bool zero;
             const int e = digit_exponent(ok ? mx : 0.0f, zero);
             const int c = 64 * warp + 2 * lane;  // column within [k0, k0 + ncs)
