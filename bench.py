@@ -204,21 +204,29 @@ class ClockSampler:
         self.samples = []  # (sm_mhz, max_mhz, reasons set)
         self.proc = None
         self.thread = None
+        self.nvml = None
         self.stop = threading.Event()
 
-    def _nvml_loop(self, nv, h):
-        reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
-        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+    def _nvml_sample(self):
+        nv, h = self.nvml
+        try:
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            bits = self.reasons_fn(h)
+            self.samples.append((float(sm), float(self.max_mhz), {k for k, b in self.REASONS.items() if bits & b}))
+        except Exception:
+            pass
+
+    def _nvml_loop(self):
         while not self.stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                bits = reasons_fn(h)
-                self.samples.append((float(sm), float(mx),
-                                     {k for k, b in self.REASONS.items() if bits & b}))
-            except Exception:
-                pass
+            self._nvml_sample()
             self.stop.wait(self.period)
+
+    def poll(self):
+        """One sample taken by the caller's thread (the timed loop calls it
+        after each step it enqueues, while the GPU runs): a short timed
+        region leaves the sampling thread little interpreter time."""
+        if self.nvml is not None:
+            self._nvml_sample()
 
     def _smi_loop(self):
         for line in self.proc.stdout:
@@ -235,8 +243,13 @@ class ClockSampler:
             import pynvml as nv
             nv.nvmlInit()
             h = nv.nvmlDeviceGetHandleByIndex(self.device)
-            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h), daemon=True)
+            self.reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.nvml = (nv, h)
+            self.thread = threading.Thread(target=self._nvml_loop, daemon=True)
         except Exception:
+            self.nvml = None
             try:
                 self.proc = subprocess.Popen(
                     ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
@@ -266,7 +279,8 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(x[1] for x in self.samples) if self.samples else None,
                 "reasons": sorted(reasons), "samples": len(sm),
-                "source": "nvml, 2 ms" if self.proc is None else "nvidia-smi, 100 ms"}
+                "source": "nvml: a thread every 2 ms and one sample per enqueued step" if self.proc is None
+                else "nvidia-smi, 100 ms"}
 
 
 # --------------------------------------------------------------- GPU arm
@@ -340,7 +354,7 @@ def run_ours(args):
         server.sim.advance()
         return n
 
-    def timed(fn, steps, profile=False):
+    def timed(fn, steps, profile=False, poll=False):
         barrier()
         if profile:
             ctx.profile(True)
@@ -351,6 +365,8 @@ def run_ours(args):
             start.record(stream)
             for _ in range(steps):
                 frames += fn()
+                if poll:
+                    clocks.poll()
             end.record(stream)
             end.synchronize()
         barrier()
@@ -362,7 +378,7 @@ def run_ours(args):
 
     for _ in range(args.warmup):
         device_step()
-    frames, ms, launches, _, clocks = timed(device_step, args.steps)
+    frames, ms, launches, _, clocks = timed(device_step, args.steps, poll=True)
     tot_frames = reduce(frames, dist.ReduceOp.SUM if dist else None)
     max_ms = reduce(ms, dist.ReduceOp.MAX if dist else None)
     # Per-kernel roofline: a second pass of the same workload with CUDA events
