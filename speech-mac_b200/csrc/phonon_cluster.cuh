@@ -592,7 +592,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
             mbar_init(kempty0 + 8 * s, 1);
         }
         for (int x = 0; x < kClExchanges; ++x) mbar_init(xbar0 + 8 * x, 1);
-        mbar_init(accum, 4);  // kTc: the four issuing warps' commits
+        mbar_init(accum, kClWarps);  // kTc: the eight issuing warps' commits
         *failed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -609,12 +609,12 @@ __global__ void __launch_bounds__(kClThreads, 1)
         const_cast<int32_t*>(p.kv.table)[static_cast<size_t>(u[0]) * p.kv.max_pages + u[1]] = u[2];
     }
     if constexpr (kTc) {
-        // digit rows 4-15 of the B tiles stay zero; four 16-column TMEM accumulator blocks
+        // digit rows 4-15 of the B tiles stay zero; eight 16-column TMEM accumulator blocks
         for (int i = threadIdx.x; i < kClTcDigBytes / 16; i += kClThreads)
             reinterpret_cast<uint4*>(dig)[i] = make_uint4(0u, 0u, 0u, 0u);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         if (warp == 1) {
-            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 64;" ::"r"(smem_addr(tmem_slot))
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 128;" ::"r"(smem_addr(tmem_slot))
                          : "memory");
             asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
         }
@@ -792,31 +792,36 @@ __global__ void __launch_bounds__(kClThreads, 1)
             if (threadIdx.x == 0) *dig_e = e;
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         };
-        // kTc, warps 0-3: the MMAs of one projection (weights A, M = 128;
-        // digits B, N = 16), issued in parallel: with n = 4 units warp k
-        // issues unit k's four K = 32 steps, with n = 1 (out) step k of the
-        // one unit, into accumulator block k (TMEM columns [16 k, +16)), and
-        // commits to `accum` (four arrivals a phase). One thread issued them
-        // all at ~0.35 us per unit. Every unit but the last (whose tail holds
-        // the row scales the epilogue reads) is released by a commit that
-        // follows its MMAs plus seven arrivals, so its slot refills as soon as
-        // the tensor core has read it; the last is released by all eight warps.
+        // kTc, all compute warps: the MMAs of one projection (weights A,
+        // M = 128; digits B, N = 16), issued in parallel into accumulator
+        // block w (TMEM columns [16 w, +16)) of warp w, each warp committing
+        // to `accum` (eight arrivals a phase). With n = 4 units warps 2k and
+        // 2k+1 issue unit k's K = 32 steps {0, 1} and {2, 3}; with n = 1 (out)
+        // warp w < 4 issues step w of the one unit. Issuing four MMAs and a
+        // commit takes a warp ~0.4 us: one warp issuing a projection's 16
+        // took 1.5 us. Every unit but the last (whose tail holds the row
+        // scales the epilogue reads) is released by its two warps' commits
+        // plus six arrivals, so its slot refills as soon as the tensor core
+        // has read it; the last is released by all eight warps.
         auto tc_mma = [&](int u_first, int n, int mark) {
             const uint32_t tmem = *tmem_slot + 16 * warp;
             constexpr uint32_t idesc = umma_idesc_i8(kGemmM, 16);
-            const int u = u_first + (n == 4 ? warp : 0);
-            if (wait_unit(u)) {
+            const int k = n == 4 ? warp >> 1 : 0;  // the unit (K slice) of this warp
+            const int u = u_first + k;
+            if ((n == 4 || warp < 4) && wait_unit(u)) {
                 if (warp == 1) CL_MARK_T(32, cur_l, mark);
                 if (lane == 0) {
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t a0 = smem_addr(unit_ptr(u)), b0 = smem_addr(dig + (n == 4 ? warp : 0) * kClTcDigRowBytes);
+                    const uint32_t a0 = smem_addr(unit_ptr(u)), b0 = smem_addr(dig + k * kClTcDigRowBytes);
                     if (n == 4) {
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk)  // K = 32 bytes per MMA
-                            umma_i8(tmem, umma_desc_sw128(a0 + 32 * kk), umma_desc_sw128(b0 + 32 * kk), idesc, kk != 0);
-                        if (warp < 3) {
+                        for (int kk = 0; kk < 2; ++kk) {  // K = 32 bytes per MMA
+                            const uint32_t off = 32 * (2 * (warp & 1) + kk);
+                            umma_i8(tmem, umma_desc_sw128(a0 + off), umma_desc_sw128(b0 + off), idesc, kk);
+                        }
+                        if (k < 3) {
                             umma_commit(wempty0 + 8 * (u % kW));
-                            mbar_arrive_count(wempty0 + 8 * (u % kW), kClWarps - 1);
+                            mbar_arrive_count(wempty0 + 8 * (u % kW), kClWarps / 2 - 1);
                         }
                     } else {
                         umma_i8(tmem, umma_desc_sw128(a0 + 32 * warp), umma_desc_sw128(b0 + 32 * warp), idesc, 0u);
@@ -828,23 +833,26 @@ __global__ void __launch_bounds__(kClThreads, 1)
             if (warp == 1) CL_MARK_T(32, cur_l, mark + 1);
         };
         // kTc, warps 0-3: the four digit sums of row 32 warp + lane of the
-        // projection's 128 rows (TMEM lane quarter `warp`): the four
-        // accumulator blocks added (exact in int32), once `accum` completes the
-        // phase of this parity.
-        auto tc_sums = [&](int parity, uint32_t (&d)[4], int mark) {
+        // projection's 128 rows (TMEM lane quarter `warp`): the accumulator
+        // blocks the projection wrote (8, or 4 for out) added, exact in int32,
+        // once `accum` completes the phase of this parity.
+        auto tc_sums = [&](int parity, uint32_t (&d)[4], int mark, int blocks) {
             if (!__all_sync(kFull, mbar_wait(accum, parity, p.error, failed))) return false;
             CL_MARK_T(0, cur_l, mark);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t t0 = *tmem_slot + (static_cast<uint32_t>(32 * warp) << 16);
-            uint32_t r[4][4];
+            uint32_t r[8][4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
+            for (int b = 0; b < 8; ++b)
                 asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
-                             : "=r"(r[k][0]), "=r"(r[k][1]), "=r"(r[k][2]), "=r"(r[k][3])
-                             : "r"(t0 + 16 * k));
+                             : "=r"(r[b][0]), "=r"(r[b][1]), "=r"(r[b][2]), "=r"(r[b][3])
+                             : "r"(t0 + 16 * b));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-            for (int j = 0; j < 4; ++j) d[j] = r[0][j] + r[1][j] + r[2][j] + r[3][j];
+            for (int j = 0; j < 4; ++j) {
+                d[j] = r[0][j] + r[1][j] + r[2][j] + r[3][j];
+                if (blocks == 8) d[j] += r[4][j] + r[5][j] + r[6][j] + r[7][j];
+            }
             return true;
         };
         // Digit sums recombined as i8_gemm_kernel's epilogue does, times the
@@ -861,9 +869,9 @@ __global__ void __launch_bounds__(kClThreads, 1)
         // [32 w, +32) of the row group to CTA (rank & ~3) + w; warp 0 of the
         // owner adds the four senders' sums (exact in int32) and returns its
         // row 32 rank + lane, scaled with the holder unit u's row scales.
-        auto tc_reduce = [&](int parity, int use, int u, float& y, int mark) {
+        auto tc_reduce = [&](int parity, int use, int u, float& y, int mark, int blocks) {
             uint32_t d[4];
-            if (warp < 4 && tc_sums(parity, d, mark) && !*failed) {
+            if (warp < 4 && tc_sums(parity, d, mark, blocks) && !*failed) {
                 const uint32_t dst = smem_addr(red_s) + (((rank & 3) * 32 + lane) * 4) * 4;
                 st_async4(dst, xbar0 + 8 * CLX_R, (rank & ~3) + warp,
                           make_float4(__uint_as_float(d[0]), __uint_as_float(d[1]), __uint_as_float(d[2]),
@@ -910,10 +918,10 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 tc_slice(xn_s, kWidth, 0, kWidth);
                 compute_sync();
                 CL_MARK_T(32, l, 13);
-                if (warp < 4) tc_mma(u0, 4, 14);
+                tc_mma(u0, 4, 14);
                 CL_MARK(l, 1);
                 uint32_t d[4];
-                if (warp < 4 && tc_sums(0, d, 11)) {
+                if (warp < 4 && tc_sums(0, d, 11, 8)) {
                     float y = tc_finish(d, u0 + 3, 32 * warp + lane);
                     // warps 0, 1: q dims [32 warp, +32); 2: k, 3: v, dims [32 half, +32)
                     const int d = (warp < 2 ? 32 * warp : 32 * half) + lane;
@@ -1069,9 +1077,9 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 // rows [128 (rank / 4), +128) over columns [128 (rank % 4), +128)
                 tc_slice(a_s, kWidth, 128 * (rank & 3), 128);
                 compute_sync();
-                if (warp < 4) tc_mma(u0 + kClUnitOut, 1, 27);
+                tc_mma(u0 + kClUnitOut, 1, 27);
                 float y;
-                if (tc_reduce(1, 2 * l, u0 + kClUnitOut, y, 29)) {
+                if (tc_reduce(1, 2 * l, u0 + kClUnitOut, y, 29, 4)) {
                     const int r = 32 * rank + lane;
                     const float h = __fadd_rn(x_s[cl_pad(r)], y);
                     if (!__all_sync(kFull, isfinite(h)) && lane == 0) flag_nonfinite(p.status, 0);
@@ -1104,10 +1112,10 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 tc_slice(xn_s, kWidth, 0, kWidth);
                 compute_sync();
                 CL_MARK_T(32, l, 17);
-                if (warp < 4) tc_mma(u0 + kClUnitUp, 4, 18);
+                tc_mma(u0 + kClUnitUp, 4, 18);
                 CL_MARK(l, 7);
                 uint32_t d[4];
-                if (warp < 4 && tc_sums(0, d, 22)) {
+                if (warp < 4 && tc_sums(0, d, 22, 8)) {
                     const float y = tc_finish(d, u0 + kClUnitUp + 3, 32 * warp + lane);
                     const float gm = gelu_erf(y);
                     if (!__all_sync(kFull, isfinite(y) && isfinite(gm)) && lane == 0) flag_nonfinite(p.status, 0);
@@ -1154,9 +1162,9 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 tc_slice(g_s, kFfn, 512 * (rank & 3), 512);
                 compute_sync();
                 CL_MARK_T(32, l, 20);
-                if (warp < 4) tc_mma(u0 + kClUnitDown, 4, 23);
+                tc_mma(u0 + kClUnitDown, 4, 23);
                 float y;
-                if (tc_reduce(1, 2 * l + 1, u0 + kClUnitDown + 3, y, 25)) {
+                if (tc_reduce(1, 2 * l + 1, u0 + kClUnitDown + 3, y, 25, 8)) {
                     const int r = 32 * rank + lane;
                     const float x = __fadd_rn(h_s[cl_pad(r)], y);
                     if (!__all_sync(kFull, isfinite(x)) && lane == 0) flag_nonfinite(p.status, 0);
@@ -1207,7 +1215,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
             if (lane == 0) mbar_drain(accum, 1);  // 4 L commits: the last phase is odd
             __syncwarp();
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 64;" ::"r"(*tmem_slot) : "memory");
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 128;" ::"r"(*tmem_slot) : "memory");
         }
     }
 }
