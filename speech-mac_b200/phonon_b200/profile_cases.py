@@ -12,6 +12,8 @@ cases:
             i8_gemm x4, attn_combine_digits, digits<2048>) with short
             contexts (64..128 positions) so the K/V pool stays under 1 GB
   step128   128 streams, contexts U[64, 2048] (seed 2), bf16 K/V
+  long8     configs[4]'s late steps: 8 streams at contexts 4000, fp32 K/V,
+            per-stage launches (attn_tma_kernel at ~131 MB per launch)
   persist   3 streams at contexts 1000..2000 (step_persist_kernel)
   head512   the flow head at 512 rows on the tensor cores (head_gemm_kernel
             and the head's small kernels), three LSD steps
@@ -118,6 +120,7 @@ CASES = {
     "step512": lambda: _decode(512, [int(x) for x in np.random.default_rng(2).integers(64, 129, 512)], rt.KV_BF16),
     "step128": lambda: _decode(128, [int(x) for x in np.random.default_rng(2).integers(64, 2049, 128)], rt.KV_BF16),
     "persist": lambda: _decode(3, [1000, 1500, 2000], rt.KV_BF16),
+    "long8": lambda: _decode(8, [4000] * 8, rt.KV_F32),
     "head512": head512,
     "frame1": frame1,
     "mimi64": mimi64,
