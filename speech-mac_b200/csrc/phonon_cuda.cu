@@ -2903,11 +2903,29 @@ struct PhononCudaHead {
     CUtensorMap tm_sl_a, tm_sl_h, tm_sl_f;
     bool tensor_ok = false;
     uint32_t tensor_min = 32;
+    // The frame step's head launches, captured into a CUDA graph once a frame
+    // repeats the previous frame's shape (rows, path, caller buffers, noise
+    // scale, scratch), and replayed from then on.
+    struct FrameShape {
+        int B = -1;
+        bool tensor = false;
+        const float *state = nullptr, *cond = nullptr, *x = nullptr, *x0 = nullptr;
+        uint32_t scale_bits = 0;
+        bool operator==(const FrameShape& o) const {
+            return B == o.B && tensor == o.tensor && state == o.state && cond == o.cond && x == o.x && x0 == o.x0 &&
+                   scale_bits == o.scale_bits;
+        }
+    };
+    cudaGraphExec_t frame_graph = nullptr;
+    FrameShape frame_shape, frame_last;
+    uint64_t frame_graph_kernels = 0;
 };
 
 namespace {
 
 void head_release(PhononCudaHead* h) {
+    if (h->frame_graph) cudaGraphExecDestroy(h->frame_graph);
+    h->frame_graph = nullptr;
     free_linear(h->cond);
     free_linear(h->ada);
     for (auto& m : h->mlp) {
@@ -3154,6 +3172,25 @@ int enqueue_head_cond(PhononCudaHead* h, int B, const float* x_dev) {
     return PHONON_CUDA_OK;
 }
 
+// The time embeddings of (s, t), unless temb holds them already.
+int enqueue_head_time(PhononCudaHead* h, float s, float t) {
+    using namespace phonon;
+    if (h->temb_ok && h->temb_s == s && h->temb_t == t) return PHONON_CUDA_OK;
+    PhononCuda* c = h->c;
+    for (int k = 0; k < 2; ++k) {
+        LaunchScope ls(c, PHONON_CUDA_K_HEAD, (kWidth * 256 + kWidth * kWidth) * 2.0);
+        head_time_kernel<<<1, 512, 0, c->stream>>>(k == 0 ? s : t, h->freqs + k * 128, h->time_w[k][0],
+                                                   h->time_b + (2 * k) * kWidth, h->time_w[k][1],
+                                                   h->time_b + (2 * k + 1) * kWidth, h->alpha + k * kWidth,
+                                                   h->temb + k * kWidth, h->d_status + h->cap);
+        CUDA_TRY(cudaGetLastError());
+    }
+    h->temb_ok = true;  // withdrawn by the caller if the status word reports a non-finite embedding
+    h->temb_s = s;
+    h->temb_t = t;
+    return PHONON_CUDA_OK;
+}
+
 // The head for B rows: conditions at x_dev (the cond GEMV's input, already
 // enqueued by the caller through enqueue_head_cond), latents or raw noise
 // in h->d_noise; the result goes to h->d_out. With embed_out, also the
@@ -3164,19 +3201,7 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
     PhononCuda* c = h->c;
     cudaStream_t st = c->stream;
     const bool tensor = head_tensor(h, B);
-    if (!h->temb_ok || h->temb_s != s || h->temb_t != t) {
-        for (int k = 0; k < 2; ++k) {
-            LaunchScope ls(c, PHONON_CUDA_K_HEAD, (kWidth * 256 + kWidth * kWidth) * 2.0);
-            head_time_kernel<<<1, 512, 0, st>>>(k == 0 ? s : t, h->freqs + k * 128, h->time_w[k][0],
-                                                h->time_b + (2 * k) * kWidth, h->time_w[k][1],
-                                                h->time_b + (2 * k + 1) * kWidth, h->alpha + k * kWidth,
-                                                h->temb + k * kWidth, h->d_status + h->cap);
-            CUDA_TRY(cudaGetLastError());
-        }
-        h->temb_ok = true;  // withdrawn by the caller if the status word reports a non-finite embedding
-        h->temb_s = s;
-        h->temb_t = t;
-    }
+    if (int e = enqueue_head_time(h, s, t)) return e;
     {
         HeadInParams q{};
         q.noise = h->d_noise;
@@ -3289,6 +3314,65 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
     f.status = h->d_status;
     LaunchScope ls(c, PHONON_CUDA_K_HEAD, kLatent * kWidth * 2.0 + B * kWidth * 12.0);
     CUDA_TRY(launch_pdl(head_final_kernel, dim3(B), dim3(256), 0, st, f));
+    return PHONON_CUDA_OK;
+}
+
+// The frame step's head: the cond GEMV from the state rows, then the LSD
+// step (s, t) = (0, 1) with the embedding of the new latent into c->d_x0.
+// From the second frame of a repeated shape on, one captured graph (the
+// head is ~23 dependent launches at one stream, launch-bound); the time
+// embeddings are computed before, outside the graph (they change only with
+// (s, t)). Profiling and layer tracing launch directly.
+int enqueue_head_frame(PhononCudaHead* h, int B, const float* state_dev, float scale, const float* cond_dev) {
+    PhononCuda* c = h->c;
+    if (int e = enqueue_head_time(h, 0.0f, 1.0f)) return e;
+    auto direct = [&]() {
+        int e = enqueue_head_cond(h, B, state_dev);
+        return e ? e : enqueue_head(h, B, true, scale, 0.0f, 1.0f, c->d_x0, cond_dev);
+    };
+    if (c->prof_on || c->tracing) return direct();
+    uint32_t bits = 0;
+    std::memcpy(&bits, &scale, 4);
+    PhononCudaHead::FrameShape shape;
+    shape.B = B;
+    shape.tensor = head_tensor(h, B);
+    shape.state = state_dev;
+    shape.cond = cond_dev;
+    shape.x = h->d_x;
+    shape.x0 = c->d_x0;
+    shape.scale_bits = bits;
+    if (h->frame_graph && h->frame_shape == shape) {
+        CUDA_TRY(cudaGraphLaunch(h->frame_graph, c->stream));
+        c->launches += h->frame_graph_kernels;
+        return PHONON_CUDA_OK;
+    }
+    if (!(h->frame_last == shape)) {
+        h->frame_last = shape;
+        return direct();
+    }
+    cudaGraph_t g = nullptr;
+    const uint64_t before = c->launches;
+    if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return direct();
+    }
+    const int st = direct();
+    const cudaError_t end = cudaStreamEndCapture(c->stream, &g);
+    cudaGraphExec_t exec = nullptr;
+    if (st != PHONON_CUDA_OK || end != cudaSuccess || !g || cudaGraphInstantiate(&exec, g, 0) != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        c->launches = before;
+        return direct();
+    }
+    cudaGraphDestroy(g);
+    if (h->frame_graph) cudaGraphExecDestroy(h->frame_graph);
+    h->frame_graph = exec;
+    h->frame_shape = shape;
+    h->frame_graph_kernels = c->launches - before;
+    c->launches = before;
+    CUDA_TRY(cudaGraphLaunch(h->frame_graph, c->stream));
+    c->launches += h->frame_graph_kernels;
     return PHONON_CUDA_OK;
 }
 
@@ -3454,8 +3538,7 @@ int phonon_cuda_frame_step(PhononCudaHead* h, uint32_t batch, const uint32_t* st
     const int B = static_cast<int>(batch);
     if ((st = head_upload_rows(h, h->d_noise, raw_noise, static_cast<size_t>(B) * phonon::kLatent))) return st;
     bool cancelled = false;
-    if ((st = enqueue_head_cond(h, B, state_dev)) ||
-        (st = enqueue_head(h, B, true, std::sqrt(temperature), 0.0f, 1.0f, c->d_x0, condition_dev))) {
+    if ((st = enqueue_head_frame(h, B, state_dev, std::sqrt(temperature), condition_dev))) {
         undo.rollback();
         return st;
     }
