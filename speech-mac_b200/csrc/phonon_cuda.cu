@@ -3611,6 +3611,12 @@ struct PhononCudaMimi {
         uint64_t position = 0;
     };
     std::vector<State> states;
+    // A step's launches depend on the batch size and the path alone: once a
+    // step repeats the previous one's (n, path) they are captured into a CUDA
+    // graph and replayed (one state: ~20 dependent launches per frame).
+    cudaGraphExec_t graph = nullptr;
+    int graph_n = -1, last_n = -1;
+    bool graph_tensor = false, last_tensor = false;
 };
 
 namespace {
@@ -3618,6 +3624,8 @@ namespace {
 constexpr int kMimiVecPerLayer = 6;
 
 void mimi_release(PhononCudaMimi* m) {
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
     for (int l = 0; l < phonon::kMimiLayers; ++l) {
         free_linear(m->in_proj[l]);
         free_linear(m->out_proj[l]);
@@ -3834,6 +3842,39 @@ int mimi_enqueue(PhononCudaMimi* m, int n) {
 
 // One frame for n distinct live states (host latents [n][32] -> host
 // features [n][16][512]); per-state status.
+int mimi_enqueue_graphed(PhononCudaMimi* m, int n) {
+    const bool tensor = m->tensor_ok && static_cast<uint32_t>(n) >= m->tensor_min;
+    if (m->graph && m->graph_n == n && m->graph_tensor == tensor) {
+        CUDA_TRY(cudaGraphLaunch(m->graph, m->stream));
+        return PHONON_CUDA_OK;
+    }
+    if (m->last_n != n || m->last_tensor != tensor) {
+        m->last_n = n;
+        m->last_tensor = tensor;
+        return mimi_enqueue(m, n);
+    }
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return mimi_enqueue(m, n);
+    }
+    const int st = mimi_enqueue(m, n);
+    const cudaError_t end = cudaStreamEndCapture(m->stream, &g);
+    cudaGraphExec_t exec = nullptr;
+    if (st != PHONON_CUDA_OK || end != cudaSuccess || !g || cudaGraphInstantiate(&exec, g, 0) != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return mimi_enqueue(m, n);
+    }
+    cudaGraphDestroy(g);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    m->graph = exec;
+    m->graph_n = n;
+    m->graph_tensor = tensor;
+    CUDA_TRY(cudaGraphLaunch(m->graph, m->stream));
+    return PHONON_CUDA_OK;
+}
+
 int mimi_step_locked(PhononCudaMimi* m, uint32_t n, const uint32_t* states, const float* latents, float* features,
                      int32_t* status) {
     using namespace phonon;
@@ -3859,7 +3900,7 @@ int mimi_step_locked(PhononCudaMimi* m, uint32_t n, const uint32_t* states, cons
     CUDA_TRY(cudaMemcpyAsync(m->d_meta, m->h_meta, 2 * m->max_batch * 4, cudaMemcpyHostToDevice, m->stream));
     CUDA_TRY(cudaMemcpyAsync(m->d_lat, m->h_lat, static_cast<size_t>(n) * 32 * 4, cudaMemcpyHostToDevice, m->stream));
     CUDA_TRY(cudaMemsetAsync(m->d_status, 0, rows * 4, m->stream));
-    if ((st = mimi_enqueue(m, static_cast<int>(n)))) return st;
+    if ((st = mimi_enqueue_graphed(m, static_cast<int>(n)))) return st;
     CUDA_TRY(cudaMemcpyAsync(m->h_out, m->d_hidden, rows * kWidth * 4, cudaMemcpyDeviceToHost, m->stream));
     CUDA_TRY(cudaMemcpyAsync(m->h_status, m->d_status, rows * 4, cudaMemcpyDeviceToHost, m->stream));
     int32_t err = 0;
