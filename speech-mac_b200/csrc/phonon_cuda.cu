@@ -42,6 +42,8 @@ constexpr int kFusedMinBatch = 2;    // default window of the persistent step
 constexpr int kFusedMaxBatch = 3;
 constexpr int kPlanHeader = 8;       // ints of the step plan header in the metadata
 constexpr int kGuide = 2;            // guided chunks: remaining pages / (kGuide * attention CTAs)
+constexpr uint32_t kClusterMaxPosF32 = 1216;   // default cluster-step window (positions below), fp32 K/V
+constexpr uint32_t kClusterMaxPosBf16 = 1408;  // ... bf16 K/V
 constexpr int kTicketMinChunk = 8;   // pages per guided chunk, at least
 constexpr int kMaxChunks = 8192;     // chunks per plan, at most
 constexpr int kSplitMinBatch = 96;   // from here a step runs as two concurrent half batches
@@ -488,7 +490,7 @@ struct PhononCuda {
     // cluster_tc_pack_kernel)
     bool cluster_tc = false;
     uint8_t* d_cltc = nullptr;
-    uint32_t cluster_max_pos = PHONON_CUDA_MAX_POSITIONS;
+    uint32_t cluster_max_pos = PHONON_CUDA_MAX_POSITIONS;  // set at creation from the K/V type
     Lane lanes[2];
     bool lane1_ok = false;  // second lane allocated
     // Whole-step persistent kernel (batches up to fused_max streams)
@@ -1663,6 +1665,11 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
     PhononCuda* c = new (std::nothrow) PhononCuda();
     if (!c) return PHONON_CUDA_OUT_OF_MEMORY;
     c->cfg = cfg;
+    // The cluster step reads a stream's K/V on its 16 SMs, the per-stage path on
+    // all of them: measured on B200 (one stream, L2 flushed), the per-stage path
+    // is faster from ~1,220 positions with fp32 K/V (2,048: 0.60 vs 0.47 ms per
+    // step) and from ~1,430 with bf16 K/V.
+    c->cluster_max_pos = cfg.kv_type == PHONON_CUDA_KV_BF16 ? kClusterMaxPosBf16 : kClusterMaxPosF32;
     auto fail = [&](int code) {
         destroy_context(c);
         return code;
