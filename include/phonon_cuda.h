@@ -289,7 +289,7 @@ int phonon_cuda_set_batch_paths(PhononCuda *ctx, uint32_t fused_min_batch, uint3
  * phonon_flow_stack_step_cancel (src/phonon_transformer.c:455-482) for the
  * reference engine's one-request-per-thread decode loop (src/speech.c:170).
  * max_position 0 sends every batch through the paths of
- * phonon_cuda_set_batch_paths; the default is 1216 with fp32 K/V and 1408
+ * phonon_cuda_set_batch_paths; the default is 1152 with fp32 K/V and 1248
  * with bf16 K/V: the cluster reads the stream's K/V on its 16 SMs, and past
  * those positions the per-stage path, whose attention runs on every SM, is
  * faster (measured on B200).

@@ -42,8 +42,8 @@ constexpr int kFusedMinBatch = 2;    // default window of the persistent step
 constexpr int kFusedMaxBatch = 3;
 constexpr int kPlanHeader = 8;       // ints of the step plan header in the metadata
 constexpr int kGuide = 2;            // guided chunks: remaining pages / (kGuide * attention CTAs)
-constexpr uint32_t kClusterMaxPosF32 = 1216;   // default cluster-step window (positions below), fp32 K/V
-constexpr uint32_t kClusterMaxPosBf16 = 1408;  // ... bf16 K/V
+constexpr uint32_t kClusterMaxPosF32 = 1152;   // default cluster-step window (positions below), fp32 K/V
+constexpr uint32_t kClusterMaxPosBf16 = 1248;  // ... bf16 K/V
 constexpr int kTicketMinChunk = 8;   // pages per guided chunk, at least
 constexpr int kMaxChunks = 8192;     // chunks per plan, at most
 constexpr int kSplitMinBatch = 96;   // from here a step runs as two concurrent half batches
@@ -786,7 +786,13 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     // steps merge the same splits), and each half of a batch split over two
     // lanes (plan_grid: a static chunk per CTA leaves the SMs a CTA finishes
     // early with to the other lane's projections): at most `grid` balanced
-    // chunks of at least kPersistMinChunk pages, chunk k run by CTA k. Other
+    // chunks of at least kPersistMinChunk pages, chunk k run by CTA k, and at
+    // most ~sqrt(2 x pages per stream) splits per stream: every split is one
+    // more partial the merge folds in, one after the other (one stream at
+    // 8000 positions in 125 four-page splits spent 0.64 ms of its 0.98 ms step
+    // merging; in ~32 splits the step takes 0.57 ms, at 2048 positions in ~16
+    // 0.41 ms against 0.46), while a longer chunk only costs when few
+    // streams leave SMs idle. Other
     // batches: guided self-scheduling over two attention CTAs per SM, chunk
     // sizes ceil(remaining / (kGuide * grid)) pages, at least
     // kTicketMinChunk, the first `grid` chunks run by CTA k and the rest
@@ -797,7 +803,11 @@ int upload_batch(PhononCuda* c, const std::vector<int32_t>& slot, const std::vec
     cuts.clear();
     cuts.push_back(0);
     if (!guided) {
-        const long long chunks = std::max<long long>(1, std::min<long long>(grid, total_pages / kPersistMinChunk));
+        const long long per_stream = std::max<long long>(
+            1, std::llround(std::sqrt(2.0 * static_cast<double>(total_pages) / static_cast<double>(R))));
+        const long long min_chunk =
+            std::max<long long>(kPersistMinChunk, (total_pages + R * per_stream - 1) / (R * per_stream));
+        const long long chunks = std::max<long long>(1, std::min<long long>(grid, total_pages / min_chunk));
         for (long long k = 1; k <= chunks; ++k) cuts.push_back(k * total_pages / chunks);
     } else {
         long long done = 0;
@@ -1667,8 +1677,8 @@ int phonon_cuda_create(const PhononCudaConfig* config, const PhononCudaLayer* la
     c->cfg = cfg;
     // The cluster step reads a stream's K/V on its 16 SMs, the per-stage path on
     // all of them: measured on B200 (one stream, L2 flushed), the per-stage path
-    // is faster from ~1,220 positions with fp32 K/V (2,048: 0.60 vs 0.47 ms per
-    // step) and from ~1,430 with bf16 K/V.
+    // is faster from ~1,150 positions with fp32 K/V (2,048: 0.60 vs 0.42 ms per
+    // step) and from ~1,250 with bf16 K/V.
     c->cluster_max_pos = cfg.kv_type == PHONON_CUDA_KV_BF16 ? kClusterMaxPosBf16 : kClusterMaxPosF32;
     auto fail = [&](int code) {
         destroy_context(c);

@@ -151,19 +151,19 @@ def test_cluster_nonfinite_input(cuda_ok, weights12):
 
 
 def test_cluster_default_window(cuda_ok, weights12):
-    """By default one stream's step runs on the cluster below 1216 positions
+    """By default one stream's step runs on the cluster below 1152 positions
     (fp32 K/V) and per stage from there on, where the attention over all SMs
     is faster than over the cluster's 16."""
     ctx = rt.Context(weights12, max_streams=2, max_batch=2, pool_pages=160, kv_type=rt.KV_F32)
     try:
         s = ctx.stream_alloc(2048)
-        ctx.fill_synthetic(s, 1215, 3)
+        ctx.fill_synthetic(s, 1151, 3)
         x = synth.Generator(9).normal(512)[None]
         l0 = ctx.launch_count()
-        ctx.step([s], [1215], x)
+        ctx.step([s], [1151], x)
         assert ctx.launch_count() - l0 == 1  # one cluster launch
         l0 = ctx.launch_count()
-        ctx.step([s], [1216], x)
+        ctx.step([s], [1152], x)
         assert ctx.launch_count() - l0 > 1  # the per-stage launches
     finally:
         ctx.close()
