@@ -40,7 +40,8 @@
 // their Q8_0 scales), the LayerNorm vectors through a two-slot ring and its
 // head's K/V blocks of the stream's earlier pages through an eight-slot page
 // ring (TMA, 16-row SWIZZLE_128B boxes), each as soon as the slot it refills
-// is released. No page read waits for this step's append. Most copies are
+// is released; the first eight pages of a layer go out right after the
+// previous layer's out unit. No page read waits for this step's append. Most copies are
 // issued several microseconds before their data is read; the two that are
 // not (the next layer's v unit, whose slot frees at the end of a layer, and
 // the last down unit, whose slot frees in stage D) are prefetched into L2 a
@@ -681,6 +682,10 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 prefetch_l2(plane, kClUnitPlane);
                 prefetch_l2(scales, kClUnitBytes - kClUnitPlane);
             };
+            // The first pages of layer l + 1 go out right after layer l's out
+            // unit: their ring slots free as soon as layer l's attention has
+            // read its pages, so they land while stages C-E run.
+            const int early = npc < kClKvSlots ? npc : kClKvSlots;
             for (int l = 0; l < L; ++l) {
                 issue_norm(2 * l);
                 for (int k = 0; k < kClUnitOut; ++k) issue_unit();
@@ -689,8 +694,10 @@ __global__ void __launch_bounds__(kClThreads, 1)
                     prefetch_unit(kClUnitsPerLayer * (l + 1) + kClUnitOut - 1);  // v
                     prefetch_unit(kClUnitsPerLayer * (l + 2) - 1);                // last down unit
                 }
-                for (int i = 0; i < npc; ++i) issue_page(l, i);
+                for (int i = l == 0 ? 0 : early; i < npc; ++i) issue_page(l, i);
                 issue_unit();  // out
+                if (l + 1 < L)
+                    for (int i = 0; i < early; ++i) issue_page(l + 1, i);
                 issue_norm(2 * l + 1);
                 for (int k = kClUnitUp; k < kClUnitsPerLayer; ++k) issue_unit();
             }

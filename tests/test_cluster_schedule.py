@@ -6,7 +6,9 @@ vectors, K/V pages) and eight compute warps that consume them; full and
 empty mbarriers pair them up. The copy warp issues every unit, norm and page
 in the order the compute warps consume them, each after a bounded wait for
 the release of its slot's previous contents; the compute warps meet at
-named barriers between stages and at the exchanges with the other CTAs. A
+named barriers between stages and at the exchanges with the other CTAs.
+The first eight K/V pages of layer l + 1 are issued right after layer l's
+out unit (their slots free once layer l's attention has read them). A
 wrong protocol would not give wrong numbers, it would hang (bounded by the
 kernel's 2 s wait budget) or silently reuse a slot. This model replays, in
 the kernel's order, every wait, arrival and copy issue of one CTA (the copy
@@ -96,14 +98,18 @@ def run(L, npc, w_slots, seed, wait_release=True, tc=False):
                 yield ("wait", kempty[n % KV_SLOTS], n // KV_SLOTS - 1)
             issue("k", n, KV_SLOTS, kfull)
 
-        for _ in range(L):  # the compute warps' consumption order
-            yield from norm(2 * _)
+        early = min(npc, KV_SLOTS)  # pages of the next layer issued after this layer's out unit
+        for l in range(L):  # the compute warps' consumption order
+            yield from norm(2 * l)
             for _k in range(UNIT_OUT):
                 yield from unit()
-            for _i in range(npc):
+            for _i in range(0 if l == 0 else early, npc):
                 yield from page()
             yield from unit()  # out
-            yield from norm(2 * _ + 1)
+            if l + 1 < L:
+                for _i in range(early):
+                    yield from page()
+            yield from norm(2 * l + 1)
             for _k in range(UNIT_UP, UNITS_PER_LAYER):
                 yield from unit()
 
