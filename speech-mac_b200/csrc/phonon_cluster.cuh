@@ -587,7 +587,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
             mbar_init(wempty0 + 8 * s, kClWarps);
         }
         mbar_init(nfull, 1);
-        mbar_init(nempty, 1);
+        mbar_init(nempty, kTc ? kClWarps : 1);  // kTc: every compute warp reads the LayerNorm vectors
         for (int s = 0; s < kClKvSlots; ++s) {
             mbar_init(kfull0 + 8 * s, 1);
             mbar_init(kempty0 + 8 * s, 1);
@@ -799,6 +799,62 @@ __global__ void __launch_bounds__(kClThreads, 1)
             if (threadIdx.x == 0) *dig_e = e;
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         };
+        // kTc, all compute warps: LayerNorm n of the padded row src and its
+        // digit rows in one pass, without a shared-memory row in between.
+        // Every warp computes the row's moments (ln_moments512, the cascade of
+        // warp_layernorm512) and the affine outputs of its lanes' 16 elements
+        // for the row maximum; then it recomputes the outputs of its columns
+        // 64 w + 2 l and the next with the same operations and slices them
+        // into the B tiles as tc_slice does. Every warp releases the vectors.
+        auto tc_ln_slice = [&](int n, const float* src) {
+            const bool got = __all_sync(kFull, mbar_wait(nfull, n & 1, p.error, failed));
+            const float* nw = reinterpret_cast<const float*>(n_ring);
+            const float* nb = nw + kClRowPad;
+            const int base = (lane >> 2) * kClChunk + (lane & 3);
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = src[base + j * 4];
+            bool ok = got;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) ok &= isfinite(v[j]);
+            float mu, scale;
+            ln_moments512(v, 1e-5f, mu, scale);
+            float mx = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int i = base + j * 4;
+                const float wi = nw[i], bi = nb[i];
+                ok &= isfinite(wi) && isfinite(bi);
+                const float y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[j], mu), scale), wi), bi);
+                ok &= isfinite(y);
+                mx = fmaxf(mx, fabsf(y));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+            ok = __all_sync(kFull, ok);
+            if (got && !ok && warp == 1 && lane == 0 && rank == 0) flag_nonfinite(p.status, 0);
+            bool zero;
+            const int e = digit_exponent(ok ? mx : 0.0f, zero);
+            const int c = 64 * warp + 2 * lane;  // this lane's two columns
+            const float down = pow2f(-e);
+            uint32_t d[2];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const int i = cl_pad(c + t);
+                const float y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(src[i], mu), scale), nw[i]), nb[i]);
+                d[t] = (ok && !zero) ? slice_digits(y * down) : 0u;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(nempty);
+            uint8_t* tile = dig + (c >> 7) * kClTcDigRowBytes + (c & 15);
+            const int chunk = (c & 127) >> 4;
+#pragma unroll
+            for (int j = 0; j < kDigits; ++j)  // SWIZZLE_128B: chunk q of row j at q ^ j
+                *reinterpret_cast<uint16_t*>(tile + j * 128 + ((chunk ^ j) << 4)) =
+                    static_cast<uint16_t>(((d[0] >> (8 * j)) & 0xffu) | (((d[1] >> (8 * j)) & 0xffu) << 8));
+            if (threadIdx.x == 0) *dig_e = e;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        };
         // kTc, all compute warps: the MMAs of one projection (weights A,
         // M = 128; digits B, N = 16), issued in parallel into accumulator
         // block w (TMEM columns [16 w, +16)) of warp w, each warp committing
@@ -918,11 +974,8 @@ __global__ void __launch_bounds__(kClThreads, 1)
             // ---- A: LN1 -> q (64), k, v (the CTA's 32 dims) of the head
             if (l > 0) exchange_wait(CLX_X, kClBytesX, l - 1);
             CL_MARK(l, 0);
-            layer_norm(2 * l, x_s);
             if constexpr (kTc) {
-                compute_sync();
-                CL_MARK_T(32, l, 12);
-                tc_slice(xn_s, kWidth, 0, kWidth);
+                tc_ln_slice(2 * l, x_s);
                 compute_sync();
                 CL_MARK_T(32, l, 13);
                 tc_mma(u0, 4, 14);
@@ -956,6 +1009,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 }
                 release_unit(u0 + 3);  // the scale holder: warps 0-3 after their reads
             } else {
+            layer_norm(2 * l, x_s);
             compute_sync();
             CL_MARK(l, 1);
             for (int k0 = 0; k0 < kClUnitOut; k0 += 2) {
@@ -1112,11 +1166,8 @@ __global__ void __launch_bounds__(kClThreads, 1)
             // ---- D: g = GELU(LN2(h) Wup^T), slices to every CTA
             exchange_wait(CLX_H, kClBytesH, l);
             CL_MARK(l, 6);
-            layer_norm(2 * l + 1, h_s);
             if constexpr (kTc) {
-                compute_sync();
-                CL_MARK_T(32, l, 16);
-                tc_slice(xn_s, kWidth, 0, kWidth);
+                tc_ln_slice(2 * l + 1, h_s);
                 compute_sync();
                 CL_MARK_T(32, l, 17);
                 tc_mma(u0 + kClUnitUp, 4, 18);
@@ -1130,6 +1181,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
                 }
                 release_unit(u0 + kClUnitUp + 3);
             } else {
+            layer_norm(2 * l + 1, h_s);
             compute_sync();
             CL_MARK(l, 7);
             for (int k0 = 0; k0 < 4; k0 += 2) {

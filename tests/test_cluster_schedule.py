@@ -24,7 +24,8 @@ Mbarriers are modelled by their completed-phase count; a copy completes its
 full barrier when issued (the latency does not change the protocol); an
 exchange with the other CTAs is a meeting point of the compute warps.
 
-In the tensor-core form (tc) every projection is an MMA issued by warps
+In the tensor-core form (tc) every warp runs the LayerNorms (fused with the
+digit slicing) and every projection is an MMA issued by warps
 0-3: for the four-unit projections (q/k/v, up, down) warp k waits for unit
 k, issues its MMAs and commits them to an accumulator barrier (four arrivals
 a phase); units 0-2 are released by a commit after their MMAs (modelled as
@@ -57,7 +58,7 @@ def run(L, npc, w_slots, seed, wait_release=True, tc=False):
     rnd = random.Random(seed)
     wfull = [Bar(1) for _ in range(w_slots)]
     wempty = [Bar(WARPS) for _ in range(w_slots)]
-    nfull, nempty = Bar(1), Bar(1)  # one LayerNorm slot
+    nfull, nempty = Bar(1), Bar(WARPS if tc else 1)  # one LayerNorm slot; tc: every warp reads it
     accum = Bar(4)
     kfull = [Bar(1) for _ in range(KV_SLOTS)]
     kempty = [Bar(1) for _ in range(KV_SLOTS)]
@@ -139,9 +140,9 @@ def run(L, npc, w_slots, seed, wait_release=True, tc=False):
         for l in range(L):
             u0 = UNITS_PER_LAYER * l
             yield ("meet",)  # exchange of x (layer l > 0)
-            if w == 1:  # LN1
+            if w == 1 or tc:  # LN1 (tc: every warp, fused with the digit slicing)
                 yield ("wait", nfull, 2 * l)
-                release("n", 2 * l, 1, [nempty], 1)
+                release("n", 2 * l, 1, [nempty], WARPS if tc else 1)
             yield from projection(w, l, u0, 4 * l)  # q/k/v
             yield ("meet",)
             for i in range(w, npc, WARPS):  # B: pages w, w + 8, ...
@@ -156,9 +157,9 @@ def run(L, npc, w_slots, seed, wait_release=True, tc=False):
                 yield from wait_unit(u0 + UNIT_OUT)
                 release("w", u0 + UNIT_OUT, w_slots, wempty, WARPS)
             yield ("meet",)  # exchange of h
-            if w == 1:  # LN2
+            if w == 1 or tc:  # LN2
                 yield ("wait", nfull, 2 * l + 1)
-                release("n", 2 * l + 1, 1, [nempty], 1)
+                release("n", 2 * l + 1, 1, [nempty], WARPS if tc else 1)
             yield from projection(w, l, u0 + UNIT_UP, 4 * l + 2)  # up
             yield ("meet",)  # exchange of g
             if tc:
