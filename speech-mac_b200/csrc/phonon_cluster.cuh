@@ -127,6 +127,10 @@ constexpr uint32_t kClBytesH = kWidth * 4;                          // 16 slices
 constexpr uint32_t kClBytesG = kFfn * 4;                            // 16 slices of 128 rows
 constexpr uint32_t kClBytesX = kWidth * 4;
 constexpr uint32_t kClBytesR = 4 * 32 * 4 * 4;  // four senders x 32 rows x 4 digit sums
+// kTc: with its slice of g every CTA pushes, per up epilogue warp, the largest
+// |g| of the warp's 32 rows (+inf if any is not finite) to every CTA: the down
+// projection's digit exponent without a pass over the 2048-wide row.
+constexpr uint32_t kClBytesGmax = kClusterCtas * 4 * 16;  // 16 CTAs x 4 warps, one float4 each
 // Activation rows in shared memory are padded: 4 floats after every 64, so
 // that the LayerNorm lanes' stride-4 accesses (lane = chunk * 4 + l) fall into
 // 32 banks; element e lives at cl_pad(e).
@@ -176,7 +180,8 @@ struct ClShape {
     static constexpr int kOffWPart = kOffMine + kClMsgFloats * 4;   // warp partials [8][68]
     static constexpr int kOffRope = kOffWPart + kClWarps * kClPartStride * 4;  // (cos, sin) [32]
     static constexpr int kOffRed = kOffRope + 32 * 8;               // kTc: down partial sums [4][32][4] int32
-    static constexpr int kOffBar = kOffRed + (kTc ? static_cast<int>(kClBytesR) : 0);
+    static constexpr int kOffGmax = kOffRed + (kTc ? static_cast<int>(kClBytesR) : 0);  // kTc: [64] float4
+    static constexpr int kOffBar = kOffGmax + (kTc ? static_cast<int>(kClBytesGmax) : 0);
     // weight ring full/empty, LayerNorm vectors full/empty, page ring
     // full/empty, the exchanges, the MMA accumulator
     static constexpr int kBars = 2 * kWSlots + 2 + 2 * kClKvSlots + kClExchanges + 1;
@@ -559,6 +564,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
     float* wpart_s = reinterpret_cast<float*>(smem + Sh::kOffWPart);
     float2* rope_s = reinterpret_cast<float2*>(smem + Sh::kOffRope);
     int32_t* red_s = reinterpret_cast<int32_t*>(smem + Sh::kOffRed);
+    float4* gmax_s = reinterpret_cast<float4*>(smem + Sh::kOffGmax);
     const uint32_t bar0 = smem_addr(smem + Sh::kOffBar);
     const uint32_t wfull0 = bar0, wempty0 = bar0 + 8 * kW, nfull = bar0 + 16 * kW, nempty = nfull + 8,
                    kfull0 = nfull + 16, kempty0 = kfull0 + 8 * kClKvSlots, xbar0 = kempty0 + 8 * kClKvSlots,
@@ -744,6 +750,30 @@ __global__ void __launch_bounds__(kClThreads, 1)
             if (lane == 0) mbar_arrive(nempty);
         };
         int cur_l = 0;  // the layer, for trace marks
+        // kTc, all compute warps: columns [k0, k0 + ncs) of the padded row as
+        // digit rows in the B tiles, given the row maximum mx and whether the
+        // row is finite (else zero digits). Warp w, lane l: columns
+        // k0 + 64 w + 2 l and the next. Ends with the proxy fence that makes
+        // the digits visible to the MMA; a compute_sync follows.
+        auto tc_slice_cols = [&](const float* row, int k0, int ncs, float mx, bool ok) {
+            bool zero;
+            const int e = digit_exponent(ok ? mx : 0.0f, zero);
+            const int c = 64 * warp + 2 * lane;  // column within [k0, k0 + ncs)
+            if (c < ncs) {
+                const float2 f = *reinterpret_cast<const float2*>(row + cl_pad(k0 + c));
+                const float down = pow2f(-e);
+                const uint32_t d0 = (ok && !zero) ? slice_digits(f.x * down) : 0u;
+                const uint32_t d1 = (ok && !zero) ? slice_digits(f.y * down) : 0u;
+                uint8_t* tile = dig + (c >> 7) * kClTcDigRowBytes + (c & 15);
+                const int chunk = (c & 127) >> 4;
+#pragma unroll
+                for (int j = 0; j < kDigits; ++j)  // SWIZZLE_128B: chunk q of row j at q ^ j
+                    *reinterpret_cast<uint16_t*>(tile + j * 128 + ((chunk ^ j) << 4)) =
+                        static_cast<uint16_t>(((d0 >> (8 * j)) & 0xffu) | (((d1 >> (8 * j)) & 0xffu) << 8));
+            }
+            if (threadIdx.x == 0) *dig_e = e;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        };
         // kTc, all compute warps: columns [k0, k0 + ncs) of the padded row
         // `row` (ncols wide) as four base-128 digit rows into the B tiles,
         // with the exponent of the whole row (a row holding a non-finite value
@@ -755,7 +785,14 @@ __global__ void __launch_bounds__(kClThreads, 1)
         // The slicing: warp w, lane l, columns k0 + 64 w + 2 l and the next.
         // Ends with the proxy fence that makes the digits visible to the MMA;
         // a compute_sync follows.
-        auto tc_slice = [&](const float* row, int ncols, int k0, int ncs) {
+        auto tc_slice = [&](const float* row, int ncols, int k0, int ncs, const float4* maxima = nullptr) {
+            if (maxima) {  // the row maximum from the 64 pushed per-warp maxima
+                float mx = fmaxf(maxima[lane].x, maxima[32 + lane].x);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+                tc_slice_cols(row, k0, ncs, mx, isfinite(mx));
+                return;
+            }
             const bool split = ncols > kWidth;
             const int span = split ? ncols / kClWarps : ncols;  // columns of this warp's maximum
             const int c0 = split ? span * warp : 0;
@@ -781,23 +818,7 @@ __global__ void __launch_bounds__(kClThreads, 1)
                     ok &= wpart_s[w * kClPartStride + 1] != 0.0f;
                 }
             }
-            bool zero;
-            const int e = digit_exponent(ok ? mx : 0.0f, zero);
-            const int c = 64 * warp + 2 * lane;  // column within [k0, k0 + ncs)
-            if (c < ncs) {
-                const float2 f = *reinterpret_cast<const float2*>(row + cl_pad(k0 + c));
-                const float down = pow2f(-e);
-                const uint32_t d0 = (ok && !zero) ? slice_digits(f.x * down) : 0u;
-                const uint32_t d1 = (ok && !zero) ? slice_digits(f.y * down) : 0u;
-                uint8_t* tile = dig + (c >> 7) * kClTcDigRowBytes + (c & 15);
-                const int chunk = (c & 127) >> 4;
-#pragma unroll
-                for (int j = 0; j < kDigits; ++j)  // SWIZZLE_128B: chunk q of row j at q ^ j
-                    *reinterpret_cast<uint16_t*>(tile + j * 128 + ((chunk ^ j) << 4)) =
-                        static_cast<uint16_t>(((d0 >> (8 * j)) & 0xffu) | (((d1 >> (8 * j)) & 0xffu) << 8));
-            }
-            if (threadIdx.x == 0) *dig_e = e;
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_slice_cols(row, k0, ncs, mx, ok);
         };
         // kTc, all compute warps: LayerNorm n of the padded row src and its
         // digit rows in one pass, without a shared-memory row in between.
@@ -1178,6 +1199,11 @@ __global__ void __launch_bounds__(kClThreads, 1)
                     const float gm = gelu_erf(y);
                     if (!__all_sync(kFull, isfinite(y) && isfinite(gm)) && lane == 0) flag_nonfinite(p.status, 0);
                     push_rows(g_addr, CLX_G, 128 * rank + 32 * warp, gm);
+                    float m = isfinite(y) && isfinite(gm) ? fabsf(gm) : INFINITY;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, o));
+                    if (lane < kClusterCtas && !*failed)
+                        st_async4(smem_addr(gmax_s + rank * 4 + warp), xbar0 + 8 * CLX_G, lane, make_float4(m, 0.0f, 0.0f, 0.0f));
                 }
                 release_unit(u0 + kClUnitUp + 3);
             } else {
@@ -1214,11 +1240,11 @@ __global__ void __launch_bounds__(kClThreads, 1)
             CL_MARK(l, 8);
 
             // ---- E: x' = h + g Wdown^T, slices to every CTA (the last layer: to `out`)
-            exchange_wait(CLX_G, kClBytesG, l);
+            exchange_wait(CLX_G, kTc ? kClBytesG + kClBytesGmax : kClBytesG, l);
             CL_MARK(l, 9);
             if constexpr (kTc) {
                 // rows [128 (rank / 4), +128) over columns [512 (rank % 4), +512)
-                tc_slice(g_s, kFfn, 512 * (rank & 3), 512);
+                tc_slice(g_s, kFfn, 512 * (rank & 3), 512, gmax_s);
                 compute_sync();
                 CL_MARK_T(32, l, 20);
                 tc_mma(u0 + kClUnitDown, 4, 23);
