@@ -3260,15 +3260,15 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
         CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_STORE>(p, st)));
     }
     for (int blk = 0; blk < kHeadBlocks; ++blk) {
-        {
-            LaunchScope ls(c, PHONON_CUDA_K_HEAD, B * kWidth * 16.0);
-            CUDA_TRY(launch_pdl(head_block_kernel, dim3((B + 7) / 8), dim3(256), 0, st, static_cast<const float*>(h->d_x),
-                                static_cast<const float*>(h->d_mod), blk,
-                                static_cast<const float*>(h->norm_w + blk * kWidth),
-                                static_cast<const float*>(h->norm_b + blk * kWidth), h->d_h, B, h->d_status,
-                                tensor ? h->sl_h : nullptr));
-        }
         if (tensor) {
+            {
+                LaunchScope ls(c, PHONON_CUDA_K_HEAD, B * kWidth * 16.0);
+                CUDA_TRY(launch_pdl(head_block_kernel, dim3((B + 7) / 8), dim3(256), 0, st,
+                                    static_cast<const float*>(h->d_x), static_cast<const float*>(h->d_mod), blk,
+                                    static_cast<const float*>(h->norm_w + blk * kWidth),
+                                    static_cast<const float*>(h->norm_b + blk * kWidth), h->d_h, B, h->d_status,
+                                    h->sl_h));
+            }
             HeadGemmParams g{};
             g.bias = h->mlp_b + (2 * blk) * kWidth;
             g.slices = h->sl_f;
@@ -3287,6 +3287,8 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
             CUDA_TRY(launch_head_gemm<HG_GATE>(h, h->tm_mlp[blk][1], h->tm_sl_f, kWidth, B, g));
             continue;
         }
+        // the block LayerNorm + modulation in the first MLP GEMV's prologue
+        // (SRC_HEADLN), in place of a head_block_kernel launch
         GemvParams p{};
         p.rows = kWidth;
         p.cols = kWidth;
@@ -3295,12 +3297,16 @@ int enqueue_head(PhononCudaHead* h, int B, bool lsd, float scale, float s, float
         p.ldy = kWidth;
         p.status = h->d_status;
         p.w = h->mlp[blk][0].plane;
-        p.x = h->d_h;
+        p.x = h->d_x;
+        p.ln_w = h->norm_w + blk * kWidth;
+        p.ln_b = h->norm_b + blk * kWidth;
+        p.mod = h->d_mod + static_cast<size_t>(blk) * kAdaBlockRows;
+        p.ldmod = kAdaRows;
         p.bias = h->mlp_b + (2 * blk) * kWidth;
         p.y = h->d_first;
         {
-            LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kWidth * 2.0 + B * kWidth * 8.0);
-            CUDA_TRY((launch_gemv_bt<false, 1, SRC_X, EPI_SILU>(p, st)));
+            LaunchScope ls(c, PHONON_CUDA_K_HEAD, kWidth * kWidth * 2.0 + B * kWidth * 24.0);
+            CUDA_TRY((launch_gemv_bt<false, 1, SRC_HEADLN, EPI_SILU>(p, st)));
         }
         p.w = h->mlp[blk][1].plane;
         p.x = h->d_first;

@@ -11,7 +11,10 @@
 //   head_time_kernel     time embedding of one flow time (sin/cos, MLP, RMS
 //                        normalisation with a learned gain), stream-independent
 //   head_in_kernel       x = input_proj(noise), silu(cond_embed(c) + time terms)
-//   head_block_kernel    LayerNorm(x) modulated by the block's shift/scale
+//   head_block_kernel    LayerNorm(x) modulated by the block's shift/scale,
+//                        written as bf16 slices for the tensor-core linears
+//                        (below 32 streams the same head_ln_modulate runs in
+//                        the first MLP GEMV's prologue, SRC_HEADLN)
 //   (gemv EPI_SILU)      silu(mlp.0(h))
 //   (gemv EPI_GATE)      x += gate * mlp.2(...)
 //   head_final_kernel    final LayerNorm + modulation, final linear, the Euler
@@ -33,77 +36,6 @@ constexpr int kAdaBlockRows = 3 * kWidth;               // shift, scale, gate
 constexpr int kAdaRows = kHeadBlocks * kAdaBlockRows + 2 * kWidth;  // every modulation row, final layer last
 constexpr int kHeadCondLd = 520;                        // cond_embed rows, then the EOS row, padded
 
-// Mean of a 512-wide row in the order of src/phonon_sampler.c:229-248 (the
-// reference's restatement of PyTorch's SumKernel): element
-// e = chunk*256 + group*16 + v*4 + l; each (chunk, v, l) sums its 16 groups
-// from zero in order, the two chunks are added into a zeroed accumulator,
-// the vectors v = 1..3 are added to v = 0 in order, and the four lanes are
-// summed from zero. Lane (chunk*16 + v*4 + l) owns one chain; every lane
-// returns the mean. `row` may be shared or global memory.
-__device__ __forceinline__ float head_mean512(const float* row) {
-    const int lane = threadIdx.x & 31;
-    float p = 0.0f;
-#pragma unroll
-    for (int g = 0; g < 16; ++g) p = __fadd_rn(p, row[(lane >> 4) * 256 + g * 16 + (lane & 15)]);
-    const float p1 = __shfl_down_sync(kFull, p, 16);          // chunk 1 of the same (v, l)
-    const float s = __fadd_rn(__fadd_rn(0.0f, p), p1);        // sums[v][l], lanes 0..15
-    const int l = lane & 3;
-    const float s1 = __shfl_sync(kFull, s, 4 + l), s2 = __shfl_sync(kFull, s, 8 + l),
-                s3 = __shfl_sync(kFull, s, 12 + l);
-    const float f = __fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3);  // sums[0][l], lanes 0..3
-    float sum = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) sum = __fadd_rn(sum, __shfl_sync(kFull, f, k));
-    return __fmul_rn(sum, 1.0f / 512.0f);  // == sum / 512 (power of two)
-}
-
-// The head's LayerNorm (src/phonon_sampler.c:250-278) of a 512-wide row in
-// shared memory, by one warp: float mean (head_mean512), variance from the
-// double sum of centred squares rounded once to float, eps 1e-6, optional
-// affine, then the adaLN modulation out = h * (1 + scale) + shift. Lane i
-// writes elements i + 32k. Returns false on every lane if an input, weight,
-// bias or result is non-finite.
-__device__ __forceinline__ bool head_ln_modulate(const float* x, const float* w, const float* b, const float* shift,
-                                                 const float* scale, float* out) {
-    const int lane = threadIdx.x & 31;
-    // every operand loaded up front (independent loads, no load behind a
-    // branch on an earlier one)
-    float xv[16], wv[16], bv[16], sc[16], sh[16];
-    const bool hw = w != nullptr, hb = b != nullptr;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-        const int i = lane + 32 * k;
-        xv[k] = x[i];
-        wv[k] = hw ? w[i] : 1.0f;
-        bv[k] = hb ? b[i] : 0.0f;
-        sc[k] = scale[i];
-        sh[k] = shift[i];
-    }
-    bool ok = true;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) ok &= isfinite(xv[k]) & isfinite(wv[k]) & isfinite(bv[k]);
-    ok = __all_sync(kFull, ok);
-    const float mean = head_mean512(x);
-    double sq = 0.0;
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-        const double c = __dsub_rn(static_cast<double>(xv[k]), static_cast<double>(mean));
-        sq = __dadd_rn(sq, __dmul_rn(c, c));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
-    const float variance = static_cast<float>(sq / 512.0);
-    const float inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, 1e-6f)));
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-        float n = __fmul_rn(__fsub_rn(xv[k], mean), inverse);
-        if (hw) n = __fmul_rn(n, wv[k]);
-        if (hb) n = __fadd_rn(n, bv[k]);
-        ok &= isfinite(n);
-        out[lane + 32 * k] = __fadd_rn(__fmul_rn(n, __fadd_rn(1.0f, sc[k])), sh[k]);
-    }
-    return __all_sync(kFull, ok);
-}
 
 // bf16 pair of a 32-bit word -> two floats (element 2i in the low half).
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }

@@ -39,7 +39,9 @@ constexpr int kStatusNonFinite = 2;  // PHONON_CUDA_NON_FINITE
 enum Epilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_GELU = 2, EPI_QKV = 3, EPI_SILU = 4, EPI_GATE = 5 };
 // Where a GEMV's activation rows come from: x as is, LayerNorm(x), or the
 // merge of the step's attention split partials (the attention output).
-enum GemvSource : int { SRC_X = 0, SRC_LN = 1, SRC_MERGE = 2 };
+// SRC_HEADLN: the flow head's block LayerNorm with its modulation
+// (head_ln_modulate) of each x row, in place of a head_block_kernel launch.
+enum GemvSource : int { SRC_X = 0, SRC_LN = 1, SRC_MERGE = 2, SRC_HEADLN = 3 };
 
 // Programmatic dependent launch: kernels of a step are launched so that the
 // next one may start while this one drains. pdl_wait() blocks until the
@@ -310,14 +312,88 @@ __device__ __forceinline__ float merge_fold(float acc, MergeWeights w, float v) 
 // conflicts. Q8_0 scales: r*(cols/32) + c*16 + g*4 + j holds the binary16
 // scale of block c*16 + j*4 + g, so lane l reads its four scales
 // (g = l/8) as one 8-byte load. bf16 weights use the same column order.
+// Mean of a 512-wide row in the order of src/phonon_sampler.c:229-248 (the
+// reference's restatement of PyTorch's SumKernel): element
+// e = chunk*256 + group*16 + v*4 + l; each (chunk, v, l) sums its 16 groups
+// from zero in order, the two chunks are added into a zeroed accumulator,
+// the vectors v = 1..3 are added to v = 0 in order, and the four lanes are
+// summed from zero. Lane (chunk*16 + v*4 + l) owns one chain; every lane
+// returns the mean. `row` may be shared or global memory.
+__device__ __forceinline__ float head_mean512(const float* row) {
+    const int lane = threadIdx.x & 31;
+    float p = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) p = __fadd_rn(p, row[(lane >> 4) * 256 + g * 16 + (lane & 15)]);
+    const float p1 = __shfl_down_sync(kFull, p, 16);          // chunk 1 of the same (v, l)
+    const float s = __fadd_rn(__fadd_rn(0.0f, p), p1);        // sums[v][l], lanes 0..15
+    const int l = lane & 3;
+    const float s1 = __shfl_sync(kFull, s, 4 + l), s2 = __shfl_sync(kFull, s, 8 + l),
+                s3 = __shfl_sync(kFull, s, 12 + l);
+    const float f = __fadd_rn(__fadd_rn(__fadd_rn(s, s1), s2), s3);  // sums[0][l], lanes 0..3
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) sum = __fadd_rn(sum, __shfl_sync(kFull, f, k));
+    return __fmul_rn(sum, 1.0f / 512.0f);  // == sum / 512 (power of two)
+}
+
+// The head's LayerNorm (src/phonon_sampler.c:250-278) of a 512-wide row in
+// shared memory, by one warp: float mean (head_mean512), variance from the
+// double sum of centred squares rounded once to float, eps 1e-6, optional
+// affine, then the adaLN modulation out = h * (1 + scale) + shift. Lane i
+// writes elements i + 32k. Returns false on every lane if an input, weight,
+// bias or result is non-finite.
+__device__ __forceinline__ bool head_ln_modulate(const float* x, const float* w, const float* b, const float* shift,
+                                                 const float* scale, float* out) {
+    const int lane = threadIdx.x & 31;
+    // every operand loaded up front (independent loads, no load behind a
+    // branch on an earlier one)
+    float xv[16], wv[16], bv[16], sc[16], sh[16];
+    const bool hw = w != nullptr, hb = b != nullptr;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const int i = lane + 32 * k;
+        xv[k] = x[i];
+        wv[k] = hw ? w[i] : 1.0f;
+        bv[k] = hb ? b[i] : 0.0f;
+        sc[k] = scale[i];
+        sh[k] = shift[i];
+    }
+    bool ok = true;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) ok &= isfinite(xv[k]) & isfinite(wv[k]) & isfinite(bv[k]);
+    ok = __all_sync(kFull, ok);
+    const float mean = head_mean512(x);
+    double sq = 0.0;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const double c = __dsub_rn(static_cast<double>(xv[k]), static_cast<double>(mean));
+        sq = __dadd_rn(sq, __dmul_rn(c, c));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
+    const float variance = static_cast<float>(sq / 512.0);
+    const float inverse = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, 1e-6f)));
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        float n = __fmul_rn(__fsub_rn(xv[k], mean), inverse);
+        if (hw) n = __fmul_rn(n, wv[k]);
+        if (hb) n = __fadd_rn(n, bv[k]);
+        ok &= isfinite(n);
+        out[lane + 32 * k] = __fadd_rn(__fmul_rn(n, __fadd_rn(1.0f, sc[k])), sh[k]);
+    }
+    return __all_sync(kFull, ok);
+}
+
 struct GemvParams {
     const void* w;            // int8 plane (Q8_0) or bf16 plane
     const __half* scales;     // Q8_0 only
     int rows, cols;
     const float* x;           // [B][ldx]
     int ldx, B;
-    const float* ln_w;        // SRC_LN: LayerNorm weight and bias (fp32 [512])
+    const float* ln_w;        // SRC_LN, SRC_HEADLN: LayerNorm weight and bias (fp32 [512])
     const float* ln_b;
+    const float* mod;         // SRC_HEADLN: row b's shift at mod + b * ldmod, its scale 512 floats on
+    int ldmod;
     const float* part;        // SRC_MERGE: split partials [S][8][66] ...
     const int32_t* first;     // ... and each stream's first split and split count
     const int32_t* count;
@@ -398,6 +474,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
                                             p.ln_b, xs + r * cols);
                 if (lane == 0) ln_bad[r] = ok ? 0 : 1;
             }
+        } else if constexpr (kSrc == SRC_HEADLN) {
+            for (int r = warp; r < nb; r += kGemvWarps) {
+                const float* shift = p.mod + static_cast<size_t>(b0 + r) * p.ldmod;
+                const bool ok = head_ln_modulate(p.x + static_cast<size_t>(b0 + r) * p.ldx, p.ln_w, p.ln_b, shift,
+                                                 shift + kWidth, xs + r * cols);
+                if (lane == 0) ln_bad[r] = ok ? 0 : 1;
+            }
         } else if constexpr (kSrc == SRC_MERGE) {
             // Warp h merges head h of every stream of the tile (the
             // arithmetic of attn_combine_kernel).
@@ -429,7 +512,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(GemvParams p) {
             }
         }
         __syncthreads();
-        if constexpr (kLN) {
+        if constexpr (kLN || kSrc == SRC_HEADLN) {
             if (blockIdx.x == 0 && threadIdx.x < nb && ln_bad[threadIdx.x])
                 flag_nonfinite(p.status, b0 + threadIdx.x);
         }
