@@ -184,13 +184,46 @@ class RankServer:
 
 
 # -------------------------------------------------------------------- clocks
+def nvml_sample_loop(nv, device, period_s, out, keep_going):
+    """Body of the clock sampler process: the SM clock and the throttle
+    reason bits every period_s, one line "monotonic_s sm_mhz bits" each (the
+    first line "max <sm max MHz>" says the sampler is ready)."""
+    nv.nvmlInit()
+    h = nv.nvmlDeviceGetHandleByIndex(device)
+    reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+        getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+    out.write(f"max {nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)}\n")
+    out.flush()
+    while keep_going():
+        try:
+            out.write(f"{time.monotonic():.6f} {nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)} {reasons(h)}\n")
+            out.flush()
+        except Exception:
+            pass
+        time.sleep(period_s)
+
+
+def clock_sampler_main(argv):
+    """Entry of the sampler process (device, period_s, output file): it
+    samples until it is terminated, its parent exits, or 15 minutes pass."""
+    import pynvml
+
+    device, period, path = int(argv[0]), float(argv[1]), argv[2]
+    parent, t_end = os.getppid(), time.monotonic() + 900.0
+    with open(path, "w") as out:
+        nvml_sample_loop(pynvml, device, period, out,
+                         lambda: os.getppid() == parent and time.monotonic() < t_end)
+
+
 class ClockSampler:
     """SM clock and throttle reasons sampled during a region.
 
-    NVML (nvidia_ml_py) is polled every 2 ms from a thread, so that even a
-    region of a few tens of milliseconds gets samples; without NVML it falls
-    back to `nvidia-smi -lms 100`. Only samples taken between __enter__ and
-    __exit__ count."""
+    NVML (nvidia_ml_py) is sampled every 2 ms by a separate process that
+    stamps each sample with the monotonic clock, so that even a region of a
+    few tens of milliseconds gets samples and the timed loop neither waits
+    for an NVML call nor shares the interpreter with a sampling thread;
+    without NVML it falls back to `nvidia-smi -lms 100`. Only samples taken
+    between __enter__ and __exit__ count."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
                "sw_power_cap": 0x4}
@@ -198,35 +231,58 @@ class ClockSampler:
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device, period_s=0.002):
+    def __init__(self, device, period_s=0.002, extra_path=None):
         self.device = device
         self.period = period_s
+        self.extra_path = extra_path  # prepended to the sampler's sys.path (tests: a fake pynvml)
         self.samples = []  # (sm_mhz, max_mhz, reasons set)
         self.proc = None
+        self.sampler = None
+        self.path = None
         self.thread = None
-        self.nvml = None
-        self.stop = threading.Event()
+        self.t0 = self.t1 = 0.0
 
-    def _nvml_sample(self):
-        nv, h = self.nvml
-        try:
-            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-            bits = self.reasons_fn(h)
-            self.samples.append((float(sm), float(self.max_mhz), {k for k, b in self.REASONS.items() if bits & b}))
-        except Exception:
-            pass
+    def _start_sampler(self):
+        import tempfile
 
-    def _nvml_loop(self):
-        while not self.stop.is_set():
-            self._nvml_sample()
-            self.stop.wait(self.period)
+        fd, self.path = tempfile.mkstemp(suffix=".clocks")
+        os.close(fd)
+        paths = [str(ROOT)] + ([str(self.extra_path)] if self.extra_path else [])
+        code = ("import sys; sys.path[:0] = sys.argv[1].split(':'); import bench; "
+                "bench.clock_sampler_main(sys.argv[2:])")
+        self.sampler = subprocess.Popen(
+            [sys.executable, "-c", code, ":".join(reversed(paths)), str(self.device), str(self.period), self.path],
+            stdin=subprocess.DEVNULL, stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        deadline = time.monotonic() + 30.0
+        while time.monotonic() < deadline and self.sampler.poll() is None:
+            with open(self.path) as f:
+                if f.readline().startswith("max "):
+                    return True
+            time.sleep(0.01)
+        self._stop_sampler()
+        return False
 
-    def poll(self):
-        """One sample taken by the caller's thread (the timed loop calls it
-        after each step it enqueues, while the GPU runs): a short timed
-        region leaves the sampling thread little interpreter time."""
-        if self.nvml is not None:
-            self._nvml_sample()
+    def _stop_sampler(self):
+        if self.sampler is not None:
+            self.sampler.terminate()
+            try:
+                self.sampler.wait(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.sampler.kill()
+                self.sampler.wait()
+
+    def _read_samples(self):
+        with open(self.path) as f:
+            lines = f.read().splitlines()
+        os.unlink(self.path)
+        max_mhz = float(lines[0].split()[1])
+        for line in lines[1:]:
+            f = line.split()
+            if len(f) != 3:
+                continue
+            t, sm, bits = float(f[0]), float(f[1]), int(f[2])
+            if self.t0 <= t <= self.t1:
+                self.samples.append((sm, max_mhz, {k for k, b in self.REASONS.items() if bits & b}))
 
     def _smi_loop(self):
         for line in self.proc.stdout:
@@ -239,31 +295,27 @@ class ClockSampler:
             self.samples.append((sm, mx, {n for n, v in zip(names, f[3:7]) if v.lower().startswith("active")}))
 
     def __enter__(self):
-        try:
-            import pynvml as nv
-            nv.nvmlInit()
-            h = nv.nvmlDeviceGetHandleByIndex(self.device)
-            self.reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-                getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
-            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
-            self.nvml = (nv, h)
-            self.thread = threading.Thread(target=self._nvml_loop, daemon=True)
-        except Exception:
-            self.nvml = None
+        if not self._start_sampler():
+            self.sampler = None
             try:
                 self.proc = subprocess.Popen(
                     ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
                      "--format=csv,noheader,nounits", "-lms", "100"],
                     stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
                 self.thread = threading.Thread(target=self._smi_loop, daemon=True)
+                self.thread.start()
             except OSError:
                 self.thread = None
-        if self.thread:
-            self.thread.start()
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
-        self.stop.set()
+        self.t1 = time.monotonic()
+        if self.sampler is not None:
+            time.sleep(2 * self.period)  # the sample that closes the region
+            self.t1 = time.monotonic()
+            self._stop_sampler()
+            self._read_samples()
         if self.proc:
             self.proc.terminate()
             try:
@@ -279,8 +331,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(x[1] for x in self.samples) if self.samples else None,
                 "reasons": sorted(reasons), "samples": len(sm),
-                "source": "nvml: a thread every 2 ms and one sample per enqueued step" if self.proc is None
-                else "nvidia-smi, 100 ms"}
+                "source": "nvml, a sampler process every 2 ms" if self.proc is None else "nvidia-smi, 100 ms"}
 
 
 # --------------------------------------------------------------- GPU arm
@@ -354,7 +405,7 @@ def run_ours(args):
         server.sim.advance()
         return n
 
-    def timed(fn, steps, profile=False, poll=False):
+    def timed(fn, steps, profile=False):
         barrier()
         if profile:
             ctx.profile(True)
@@ -365,8 +416,6 @@ def run_ours(args):
             start.record(stream)
             for _ in range(steps):
                 frames += fn()
-                if poll:
-                    clocks.poll()
             end.record(stream)
             end.synchronize()
         barrier()
@@ -378,7 +427,7 @@ def run_ours(args):
 
     for _ in range(args.warmup):
         device_step()
-    frames, ms, launches, _, clocks = timed(device_step, args.steps, poll=True)
+    frames, ms, launches, _, clocks = timed(device_step, args.steps)
     tot_frames = reduce(frames, dist.ReduceOp.SUM if dist else None)
     max_ms = reduce(ms, dist.ReduceOp.MAX if dist else None)
     # Per-kernel roofline: a second pass of the same workload with CUDA events

@@ -1,8 +1,7 @@
-"""bench.py's roofline helpers, on CPU: the int8 projection figure the bench
-adds to its line must be computed from the profile it is given, and be
-absent (not an exception) when a profile has no projection time."""
-import sys
-
+"""bench.py's roofline helpers and clock sampler, on CPU: the int8
+projection figure the bench adds to its line must be computed from the
+profile it is given, and be absent (not an exception) when a profile has no
+projection time; the clock record comes from a sampler process."""
 import bench
 
 
@@ -24,19 +23,47 @@ def test_projection_roofline_without_projection_time():
     assert bench.projection_roofline({"qkv": {"ms": 1.0}}, 0) is None
 
 
-def test_clock_sampler_samples_each_step(monkeypatch):
-    """The timed loop's per-step poll records clocks even when the sampling
-    thread gets no interpreter time (a fake NVML: 1900 of 1965 MHz, power cap)."""
+FAKE_NVML = """
+NVML_CLOCK_SM = 0
+def nvmlInit(): pass
+def nvmlDeviceGetHandleByIndex(i): return i
+def nvmlDeviceGetMaxClockInfo(h, c): return 1965
+def nvmlDeviceGetClockInfo(h, c): return 1900
+def nvmlDeviceGetCurrentClocksEventReasons(h): return 0x4
+"""
+
+
+def test_nvml_sample_loop_lines():
+    """The sampler process's loop: a ready line with the max clock, then one
+    stamped line per sample (a fake NVML: 1900 of 1965 MHz, power cap)."""
+    import io
     import types
 
-    fake = types.SimpleNamespace(
-        NVML_CLOCK_SM=0, nvmlInit=lambda: None, nvmlDeviceGetHandleByIndex=lambda i: i,
-        nvmlDeviceGetMaxClockInfo=lambda h, c: 1965, nvmlDeviceGetClockInfo=lambda h, c: 1900,
-        nvmlDeviceGetCurrentClocksEventReasons=lambda h: 0x4)
-    monkeypatch.setitem(sys.modules, "pynvml", fake)
-    with bench.ClockSampler(0, period_s=3600.0) as clocks:
-        for _ in range(3):
-            clocks.poll()
+    ns = {}
+    exec(FAKE_NVML, ns)
+    fake = types.SimpleNamespace(**{k: v for k, v in ns.items() if not k.startswith("__")})
+    out, left = io.StringIO(), [3]
+
+    def keep_going():
+        left[0] -= 1
+        return left[0] >= 0
+
+    bench.nvml_sample_loop(fake, 0, 0.0, out, keep_going)
+    lines = out.getvalue().splitlines()
+    assert lines[0] == "max 1965" and len(lines) == 4
+    assert all(line.split()[1:] == ["1900", "4"] for line in lines[1:])
+
+
+def test_clock_sampler_process_records_the_region(tmp_path):
+    """The sampler runs as its own process (the timed loop never waits on an
+    NVML call): samples inside the region are kept, with the reasons decoded."""
+    import time
+
+    (tmp_path / "pynvml.py").write_text(FAKE_NVML)
+    with bench.ClockSampler(0, period_s=0.002, extra_path=tmp_path) as clocks:
+        assert clocks.sampler is not None and clocks.sampler.poll() is None
+        time.sleep(0.05)
     s = clocks.summary()
     assert s["samples"] >= 3 and s["sm_mhz"] == 1900.0 and s["sm_max_mhz"] == 1965.0
-    assert s["reasons"] == ["sw_power_cap"]
+    assert s["reasons"] == ["sw_power_cap"] and s["source"].startswith("nvml")
+    assert clocks.sampler.returncode is not None  # stopped
