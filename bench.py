@@ -259,7 +259,8 @@ class ClockSampler:
                 if f.readline().startswith("max "):
                     return True
             time.sleep(0.01)
-        self._stop_sampler()
+        self._stop_sampler()  # no NVML (or it failed): no samples from this process
+        os.unlink(self.path)
         return False
 
     def _stop_sampler(self):
@@ -331,7 +332,8 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(x[1] for x in self.samples) if self.samples else None,
                 "reasons": sorted(reasons), "samples": len(sm),
-                "source": "nvml, a sampler process every 2 ms" if self.proc is None else "nvidia-smi, 100 ms"}
+                "source": "nvml, a sampler process every 2 ms" if self.sampler is not None
+                else "nvidia-smi, 100 ms" if self.proc is not None else "none (neither NVML nor nvidia-smi)"}
 
 
 # --------------------------------------------------------------- GPU arm

@@ -67,3 +67,22 @@ def test_clock_sampler_process_records_the_region(tmp_path):
     assert s["samples"] >= 3 and s["sm_mhz"] == 1900.0 and s["sm_max_mhz"] == 1965.0
     assert s["reasons"] == ["sw_power_cap"] and s["source"].startswith("nvml")
     assert clocks.sampler.returncode is not None  # stopped
+
+
+def test_clock_sampler_without_nvml(tmp_path, monkeypatch):
+    """An NVML that fails to initialise: the sampler process ends at once,
+    its file is removed, and the record says where its samples came from
+    (nvidia-smi, or none) instead of claiming NVML."""
+    import os
+    import tempfile
+
+    (tmp_path / "pynvml.py").write_text("def nvmlInit():\n    raise RuntimeError('no NVML')\n")
+    scratch = tmp_path / "tmp"
+    scratch.mkdir()
+    monkeypatch.setattr(tempfile, "tempdir", str(scratch))  # where the sampler's file goes
+    monkeypatch.setenv("PATH", str(tmp_path))  # no nvidia-smi either
+    with bench.ClockSampler(0, period_s=0.002, extra_path=tmp_path) as clocks:
+        assert clocks.sampler is None
+    s = clocks.summary()
+    assert s["samples"] == 0 and s["sm_mhz"] is None and s["source"].startswith("none")
+    assert os.listdir(scratch) == []
